@@ -1,0 +1,415 @@
+"""Benchmark of the B200 Shannon-Prime KV-cache hot path.
+
+Headline workload: fused decompress-KQ/V decode attention
+in Llama-3-8B shape — 32 layers, 32 query heads / 8 KV heads (GQA 4),
+head_dim 128, batch 1, 32768 cached positions compressed on the ship path
+(K bands 5,5,4,3; V 3-bit).  One step = one decode token: attention of every
+layer's 32 queries over the whole compressed cache (one sp_cuda_attn_decode
+call over all 32 layers).  The compressed cache (1.06 GB) is larger than L2
+(126 MB), so no flush is needed between steps.  Also measured: ship-path
+compression throughput on one full layer (32768 positions x 8 KV heads, fp32
+in, 268 MB > L2).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 (torchrun, one rank per GPU): KV heads are partitioned across ranks
+(rank r owns heads h with h % N == r, all layers), each rank attends over its
+own shard, then one NCCL all-gather of the per-head fp16 outputs
+(torch.distributed) completes the step; the time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "shannon-prime-llama_b200"
+for _p in (ROOT, PKG, ROOT / "oracle"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+# Workload (config 1).
+N_LAYERS, N_Q, N_KV, HD, CTX = 32, 32, 8, 128, 32768
+KB, VB = [5, 5, 4, 3], [3]
+K_ROW, V_ROW = 76, 50
+SEED = 1
+METRIC = ("fused decompress-KQ/V decode latency per token @32K ctx "
+          "(Llama-3-8B shape: 32 layers, 32 Q / 8 KV heads, hd 128, ship K 5/5/4/3 + V 3-bit)")
+UNIT = "us/token"
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, burst copy)"
+    return 6650.0, "fallback 6.65 TB/s"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except OSError:
+            self.p = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.p:
+            time.sleep(0.2)
+            self.p.terminate()
+            self.p.wait()
+
+    def summary(self):
+        self.f.flush()
+        rows = []
+        for line in Path(self.f.name).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ----------------------------------------------------------------- helpers --
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def local_heads(rank: int, world: int):
+    """KV heads owned by a rank: h % world == rank (balanced for world | 8)."""
+    return [h for h in range(N_KV) if h % world == rank]
+
+
+def cpu_decode_sample(n_threads: int, layers: int = 1):
+    """The oracle's decode attention (the reference's fused decompress-KQ
+    algorithm plus softmax and V) on `layers` layers of the workload, cache
+    built by the oracle itself.  Returns (seconds per layer, threads used)."""
+    import numpy as np
+    import oracle as O
+    from spb200 import synth
+    kp = np.zeros((N_KV, CTX, K_ROW), np.uint8)
+    vp = np.zeros((N_KV, CTX, V_ROW), np.uint8)
+    for h in range(N_KV):
+        k, v = synth.kv_slot_np(SEED, 0, h, CTX, HD)
+        kp[h] = O.ship_write(k, KB, True, n_threads)
+        vp[h] = O.ship_write(v, VB, False, n_threads)
+    q = synth.q_np(SEED, 1, N_Q, HD, 1.0 / 128 ** 0.5)[0]
+    t0 = time.perf_counter()
+    for _ in range(layers):
+        O.attn_decode(kp, vp, HD, KB, VB, True, q, CTX, 1.0, n_threads)
+    dt = (time.perf_counter() - t0) / layers
+    return dt, min(n_threads, N_KV)
+
+
+def cpu_compress_sample(n_threads: int, n_pos: int = 8192):
+    """Oracle ship-path compression of n_pos positions x 8 heads (K and V)."""
+    import numpy as np
+    import oracle as O
+    from spb200 import synth
+    ks, vs = [], []
+    for h in range(N_KV):
+        k, v = synth.kv_slot_np(0, 0, h, n_pos, HD)
+        ks.append(k)
+        vs.append(v)
+    k = np.concatenate(ks)
+    v = np.concatenate(vs)
+    t0 = time.perf_counter()
+    O.ship_write(k, KB, True, n_threads)
+    O.ship_write(v, VB, False, n_threads)
+    dt = time.perf_counter() - t0
+    return k.shape[0] / dt, n_threads
+
+
+def run_reference(args):
+    """--impl reference: the oracle port of the reference CPU path (the
+    reference's own CPU core is an empty submodule and cannot be built),
+    timed on this box's host cores.  Each step = one layer of the decode
+    step, scaled x32 to a full token."""
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    n_threads = os.cpu_count() or 1
+    import numpy as np
+    import oracle as O
+    from spb200 import synth
+    kp = np.zeros((N_KV, CTX, K_ROW), np.uint8)
+    vp = np.zeros((N_KV, CTX, V_ROW), np.uint8)
+    for h in range(N_KV):
+        k, v = synth.kv_slot_np(SEED, 0, h, CTX, HD)
+        kp[h] = O.ship_write(k, KB, True, n_threads)
+        vp[h] = O.ship_write(v, VB, False, n_threads)
+    q = synth.q_np(SEED, 1, N_Q, HD, 1.0 / 128 ** 0.5)[0]
+    for _ in range(args.warmup):
+        O.attn_decode(kp, vp, HD, KB, VB, True, q, CTX, 1.0, n_threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.attn_decode(kp, vp, HD, KB, VB, True, q, CTX, 1.0, n_threads)
+    per_layer = (time.perf_counter() - t0) / args.steps
+    us_tok = per_layer * N_LAYERS * 1e6
+    cores = min(n_threads, N_KV)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": us_tok, "unit": UNIT,
+        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": us_tok / 1e3, "higher_is_better": False, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config-1 distributions)",
+        "config": {"workload": "config 1: 32L x 32Q/8KV x hd128, ctx 32768, batch 1, ship 5/5/4/3 + V3",
+                   "sample": "1 of 32 layers per step, scaled x32"},
+        "cpu_baseline": {"value": us_tok, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": "one layer (8 KV heads x 32768 positions) per step, x32"},
+        "e2e": {"value": us_tok, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference CPU core (lib/shannon-prime) is absent from the reference checkout; "
+                "this is the CPU restatement of its algorithm (oracle/sp_oracle.c), OpenMP over KV heads",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import ctypes as C
+
+    import torch
+    import torch.distributed as dist
+
+    import spb200
+    from spb200 import synth
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    L = spb200.lib()
+    # A dedicated stream: the legacy default stream's handle is NULL, which the
+    # bridge would read as "make a private stream".
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    heads = local_heads(rank, ws)
+    H = len(heads)
+    G = N_Q // N_KV
+    nq_local = H * G
+
+    # The bridge context (the reference-facing API) owns the cache; the device
+    # entry points run on its sp_cuda_cache_t.
+    os.environ["SHANNON_PRIME_ENABLED"] = "1"
+    params = spb200.SpLlamaParams(HD, N_LAYERS, H, CTX, 1, stream.cuda_stream, None)
+    ctx = L.sp_llama_init(C.byref(params))
+    if not ctx:
+        raise RuntimeError("sp_llama_init failed")
+    cc = C.cast(L.sp_llama_get_cuda_cache(ctx), C.POINTER(spb200.SpCudaCache))
+
+    # Fill the cache: per layer, synthetic K/V for this rank's heads.
+    gen = torch.Generator(device=dev)
+    t_fill = time.perf_counter()
+    for layer in range(N_LAYERS):
+        gen.manual_seed(SEED * 1000003 + layer)
+        k, v = synth.kv_layer_torch(gen, CTX, N_KV, HD, device=dev)
+        k = k[:, heads].contiguous()
+        v = v[:, heads].contiguous()
+        rc = L.sp_cuda_write_kv_tokens(cc, layer, 0, CTX, k.data_ptr(), v.data_ptr(), 0)
+        spb200.check(rc, "write_kv_tokens")
+        if layer == 0:
+            k0, v0 = k, v
+    torch.cuda.synchronize()
+    t_fill = time.perf_counter() - t_fill
+
+    gq = torch.Generator(device=dev)
+    gq.manual_seed(SEED)
+    q_all = (torch.randn(N_LAYERS, N_Q, HD, device=dev, generator=gq) / HD ** 0.5).half()
+    qidx = torch.tensor([h * G + g for h in heads for g in range(G)], device=dev)
+    q = q_all[:, qidx].contiguous()
+    out = torch.empty(N_LAYERS, nq_local, HD, dtype=torch.float16, device=dev)
+    gathered = [torch.empty_like(out) for _ in range(ws)] if ws > 1 else None
+
+    def step():
+        rc = L.sp_cuda_attn_decode(cc, 0, N_LAYERS, q.data_ptr(), nq_local, CTX, 1.0,
+                                   out.data_ptr(), -1, stream.cuda_stream)
+        if rc:
+            spb200.check(rc, "attn_decode")
+        if ws > 1:
+            dist.all_gather(gathered, out)
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if ws == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    clocks = clk.summary()
+
+    # Main-kernel duration (roofline), measured with events inside the call.
+    L.sp_cuda_attn_profile(1)
+    kms = []
+    for _ in range(max(3, min(args.steps, 20))):
+        L.sp_cuda_attn_decode(cc, 0, N_LAYERS, q.data_ptr(), nq_local, CTX, 1.0,
+                              out.data_ptr(), -1, stream.cuda_stream)
+        kms.append(L.sp_cuda_attn_last_kernel_ms())
+    L.sp_cuda_attn_profile(0)
+    splits = L.sp_cuda_attn_last_splits()
+    kernel_ms = max_over_ranks(statistics.mean(kms))
+    cache_bytes = N_LAYERS * H * CTX * (K_ROW + V_ROW)
+    q_bytes = N_LAYERS * nq_local * HD * 2
+    alg_bytes = cache_bytes + q_bytes
+    peak, peak_src = peaks()
+    achieved = alg_bytes / (kernel_ms * 1e-3) / 1e9
+
+    # End to end through the bridge with host buffers.
+    hq = q.cpu().pin_memory()
+    hout = torch.empty(out.shape, dtype=torch.float16).pin_memory()
+    hgat = [torch.empty(out.shape, dtype=torch.float16) for _ in range(ws)]
+
+    def e2e_step():
+        rc = L.sp_llama_attn_decode(ctx, 0, N_LAYERS, hq.data_ptr(), nq_local, CTX, 1.0,
+                                    hout.data_ptr(), -1)
+        if rc:
+            raise RuntimeError(f"sp_llama_attn_decode {rc}")
+        if ws > 1:
+            d = hout.to(dev, non_blocking=True)
+            dist.all_gather(gathered, d)
+            for i in range(ws):
+                hgat[i].copy_(gathered[i])
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    barrier()
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) / args.steps * 1e3)
+    h2d = hq.numel() * 2 + (out.numel() * 2 if ws > 1 else 0)
+    d2h = hout.numel() * 2 * (ws if ws > 1 else 1)
+
+    # Ship-path compression throughput on one full layer (K and V, fp32).
+    for _ in range(3):
+        L.sp_cuda_write_kv_tokens(cc, 0, 0, CTX, k0.data_ptr(), v0.data_ptr(), 0)
+    barrier()
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    c0.record(stream)
+    for _ in range(reps):
+        L.sp_cuda_write_kv_tokens(cc, 0, 0, CTX, k0.data_ptr(), v0.data_ptr(), 0)
+    c1.record(stream)
+    barrier()
+    cms = max_over_ranks(c0.elapsed_time(c1) / reps)
+    pairs = CTX * H
+    comp_mpairs = pairs * ws / (cms * 1e-3) / 1e6
+    comp_gbs = pairs * (2 * HD * 4 + K_ROW + V_ROW) / (cms * 1e-3) / 1e9
+
+    # CPU baseline (rank 0, N = 1): the oracle on a bounded sample.
+    cpu = None
+    if ws == 1 and not args.no_cpu:
+        n_threads = os.cpu_count() or 1
+        per_layer, cores = cpu_decode_sample(n_threads, layers=3)
+        cpu = {"value": per_layer * N_LAYERS * 1e6, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": "3 passes over one layer (8 KV heads x 32768 positions), scaled x32 layers",
+               "compress_mpairs_s": None}
+        mp, _ = cpu_compress_sample(n_threads)
+        cpu["compress_mpairs_s"] = mp / 1e6
+        cpu["compress_cores"] = n_threads
+
+    launches_per_step = 2        # fused decode kernel + split combine kernel
+    line = {
+        "metric": METRIC, "value": ms * 1e3, "unit": UNIT, "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+        "dtype": "u8 codes -> f32 accumulate (fp16 q/out)",
+        "data": "synthetic (seeded; K = RoPE(N(0,1) x LogNormal(0,0.5) per dim), V = N(0,1), q = N(0,1/sqrt(128)) fp16)",
+        "config": {"workload": "config 1: fused decode, 32 layers x 32 Q / 8 KV heads x hd 128, ctx 32768, batch 1, "
+                               "ship K 5/5/4/3 + V 3-bit",
+                   "l2": "inputs larger than L2 (compressed cache %.2f GB per GPU)" % (cache_bytes / 1e9),
+                   "parallelism": f"kv-head shards x{ws}" if ws > 1 else "single GPU",
+                   "kv_heads_per_gpu": H, "splits": splits},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
+                     "kernel": "fused decode main kernel", "kernel_ms": kernel_ms,
+                     "algorithmic_bytes": alg_bytes},
+        "e2e": {"value": e2e_ms * 1e3, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "path": "sp_llama_attn_decode (host q in, host out back)"},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+        "compress": {"metric": "ship-path compress throughput (K+V pairs)", "value": comp_mpairs,
+                     "unit": "Mpairs/s", "model_tokens_per_s_M": comp_mpairs / (N_KV * 1.0),
+                     "achieved_gbs": comp_gbs, "frac": comp_gbs / peak,
+                     "workload": "one layer: 32768 positions x %d KV heads, fp32 in" % H,
+                     "ms": cms},
+        "cache_fill_s": t_fill,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    L.sp_llama_free(ctx)
+    if ws > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

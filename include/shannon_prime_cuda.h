@@ -1,0 +1,191 @@
+/*
+ * shannon_prime_cuda.h — C-ABI of the B200 (sm_100a) Shannon-Prime KV-cache
+ * hot path.
+ *
+ * Drop-in for the reference's CUDA C-ABI src/backends/cuda/shannon_prime_cuda.h
+ * (names, argument meaning and the caller-visible struct fields are kept:
+ * k_bands.total_bytes, stream, d_k_cache, d_v_cache, d_mobius_order,
+ * max_seq_len are read by the reference engine at src/engine/kv_cache.cpp:
+ * 638, 1034, 1378-1383, 1457-1459).  The reference functions return void and
+ * fail silently; here every void entry point records its status, readable
+ * with sp_cuda_last_error(), and every new entry point returns it (0 = ok).
+ *
+ * All device pointers are plain CUDA device addresses; "stream" is a
+ * cudaStream_t passed as void*.  Work is stream-ordered; no entry point
+ * below allocates device memory after sp_cuda_cache_init, and none
+ * synchronises the stream unless it says so.
+ *
+ * Cache layout (as the reference, shannon_prime_cuda.cu:494-497): slot-major
+ * [n_layers * n_heads_kv][max_seq_len][total_bytes], slot = layer*H + head.
+ * sp_cuda_cache_init rounds max_seq_len up to a multiple of 16 and stores the
+ * rounded value, so every 16-position tile of every slot starts on a 16-byte
+ * boundary (the fused decode kernels stage tiles with bulk copies).
+ */
+#ifndef SHANNON_PRIME_CUDA_H
+#define SHANNON_PRIME_CUDA_H
+
+#include "shannon_prime.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes returned by the int entry points / sp_cuda_last_error(). */
+#define SP_OK              0
+#define SP_ERR_ARG        -1   /* invalid argument, shape or range */
+#define SP_ERR_CUDA       -2   /* a CUDA runtime call failed */
+#define SP_ERR_UNSUPPORTED -3  /* configuration this build does not implement */
+#define SP_ERR_TIMEOUT    -4   /* a bounded device-side wait gave up */
+
+/* Element types for the token-major write entry point. */
+#define SP_DTYPE_F32  0
+#define SP_DTYPE_F16  1
+#define SP_DTYPE_BF16 2
+
+typedef struct {
+    /* --- fields of the reference struct (shannon_prime_cuda.h:29-46) --- */
+    sp_config_t      config;
+    sp_band_config_t k_bands;
+    sp_band_config_t v_bands;
+    void            *d_k_cache;      /* [n_slots][max_seq_len][k_bands.total_bytes] */
+    void            *d_v_cache;      /* [n_slots][max_seq_len][v_bands.total_bytes] */
+    int              max_seq_len;
+    int             *d_mobius_order; /* [head_dim] forward permutation (NULL: Möbius off) */
+    int             *d_mobius_inv;   /* [head_dim] inverse permutation */
+    float           *d_scratch;      /* [head_dim] kept for layout compatibility; unused */
+    void            *stream;
+
+    /* --- B200 build additions --- */
+    int              n_slots;        /* n_layers * n_heads_kv */
+    int              device;         /* CUDA device the cache lives on */
+    void            *d_attn_ws;      /* split-K partials of the fused decode */
+    size_t           attn_ws_bytes;
+    int              attn_max_q_heads; /* q heads per layer the workspace is sized for */
+    int              attn_ws_layers;   /* layers per call the workspace is sized for */
+    unsigned int    *d_status;       /* device-side error word (bounded waits) */
+} sp_cuda_cache_t;
+
+/* ------------------------------------------------------------ lifecycle -- */
+
+/* Replaces reference sp_cuda_cache_init (shannon_prime_cuda.h:50-51,
+ * shannon_prime_cuda.cu:407-463).  Allocates the cache slabs, the Möbius
+ * tables and the fused-decode workspace (sized for up to 8 query heads per
+ * KV head and all layers).  Returns 0 or an SP_ERR_* code. */
+int  sp_cuda_cache_init(sp_cuda_cache_t *cc, const sp_config_t *cfg,
+                        int max_seq_len, void *stream);
+/* Replaces reference sp_cuda_cache_free (shannon_prime_cuda.h:52). */
+void sp_cuda_cache_free(sp_cuda_cache_t *cc);
+
+/* ------------------------------------------------------------ write path -- */
+/* VHT2 -> Möbius reorder (K) -> band quantise -> store.  Packed codes are
+ * bit-identical to the CPU restatement of the core path. */
+
+/* Reference shannon_prime_cuda.h:60-66 (single vector, device pointer). */
+void sp_cuda_write_k(sp_cuda_cache_t *cc, int layer, int head, int pos,
+                     const float *d_k_vec);
+void sp_cuda_write_v(sp_cuda_cache_t *cc, int layer, int head, int pos,
+                     const float *d_v_vec);
+
+/* Reference shannon_prime_cuda.h:89-97: d_vecs is [n_pos][head_dim]. */
+void sp_cuda_write_k_batch(sp_cuda_cache_t *cc, int layer, int head,
+                           int start_pos, int n_pos, const float *d_k_vecs);
+void sp_cuda_write_v_batch(sp_cuda_cache_t *cc, int layer, int head,
+                           int start_pos, int n_pos, const float *d_v_vecs);
+
+/* New: one launch for every head of a layer, K and V together, in the
+ * engine's token-major layout [n_tokens][n_heads_kv][head_dim] (the layout
+ * KvCache::write_gpu walks vector by vector, kv_cache.cpp:1045-1091).
+ * d_k or d_v may be NULL to skip that half.  dtype is SP_DTYPE_*. */
+int  sp_cuda_write_kv_tokens(sp_cuda_cache_t *cc, int layer, int start_pos,
+                             int n_tokens, const void *d_k, const void *d_v,
+                             int dtype);
+
+/* ------------------------------------------------------------- read path -- */
+/* dequantise -> Möbius unreorder (K) -> VHT2 -> fp32. */
+
+/* Reference shannon_prime_cuda.h:75-81. */
+void sp_cuda_read_k(const sp_cuda_cache_t *cc, int layer, int head, int pos,
+                    float *d_k_out);
+void sp_cuda_read_v(const sp_cuda_cache_t *cc, int layer, int head, int pos,
+                    float *d_v_out);
+
+/* Reference shannon_prime_cuda.h:100-108: output [n_pos][head_dim]. */
+void sp_cuda_read_k_batch(const sp_cuda_cache_t *cc, int layer, int head,
+                          int start_pos, int n_pos, float *d_k_out);
+void sp_cuda_read_v_batch(const sp_cuda_cache_t *cc, int layer, int head,
+                          int start_pos, int n_pos, float *d_v_out);
+
+/* New: partial-band read (semantics of sp_llama_read_k_partial,
+ * shannon_prime_llama.h:240-255: bands >= max_bands read as zero;
+ * max_bands < 0 or >= n_bands is a full read).  which: 0 = K, 1 = V. */
+int  sp_cuda_read_batch_partial(const sp_cuda_cache_t *cc, int which,
+                                int layer, int head, int start_pos, int n_pos,
+                                float *d_out, int max_bands);
+
+/* -------------------------------------------------- fused decode attention -- */
+/* New (no reference GPU counterpart; replaces the CPU ggml op
+ * llama_sp_kq_compute, src/engine/llama_sp_fused_kq.cpp:82-165, plus the
+ * softmax and V product that ggml runs after it).
+ *
+ * For layers [layer0, layer0+n_layers) and every query head g (KV head
+ * g / (n_q_heads / n_heads_kv)):
+ *     out[l][g] = softmax(logit_scale * q[l][g] . K_hat[l][h][0:kv_len]) . V_hat[l][h]
+ * where K_hat, V_hat are the decompressed cache rows.  Neither K_hat nor
+ * V_hat is materialised: scores are taken in the VHT2 coefficient domain
+ * against the packed codes and V is accumulated in that domain and
+ * transformed once per head.
+ *   d_q   : fp16 [n_layers][n_q_heads][head_dim]
+ *   d_out : fp16 [n_layers][n_q_heads][head_dim]
+ * n_q_heads must be a multiple of n_heads_kv with at most 8 queries per KV
+ * head.  max_bands limits the K and V bands read (-1 = all; the partial-read
+ * rule above).  kv_len == 0 writes zeros. */
+int  sp_cuda_attn_decode(const sp_cuda_cache_t *cc, int layer0, int n_layers,
+                         const void *d_q, int n_q_heads, int kv_len,
+                         float logit_scale, void *d_out, int max_bands,
+                         void *stream);
+
+/* ----------------------------------------- kernel launchers (for tests) -- */
+
+/* Reference shannon_prime_cuda.h:116-134.  In-place VHT2 of n_vecs
+ * vectors (power-of-two n, 32 <= n <= SP_MAX_HEAD_DIM). */
+void sp_cuda_vht2_forward(float *d_data, int n, int n_vecs, void *stream);
+void sp_cuda_mobius_reorder(float *d_data, const int *d_order, int n,
+                            int n_vecs, void *stream);
+void sp_cuda_mobius_unreorder(float *d_data, const int *d_order, int n,
+                              int n_vecs, void *stream);
+void sp_cuda_band_quantize(const float *d_input, void *d_output,
+                           const sp_band_config_t *bc, int n_vecs, void *stream);
+void sp_cuda_band_dequantize(const void *d_input, float *d_output,
+                             const sp_band_config_t *bc, int n_vecs, void *stream);
+
+/* ----------------------------------------------------------- diagnostics -- */
+
+/* Reference shannon_prime_cuda.h:141. */
+void sp_cuda_print_memory(const sp_cuda_cache_t *cc);
+
+/* New: status of the last call made on this host thread (SP_OK or SP_ERR_*)
+ * and a message for it.  The void reference entry points report only here. */
+int         sp_cuda_last_error(void);
+const char *sp_cuda_last_error_string(void);
+
+/* New: sizeof(sp_config_t) (which=0), sizeof(sp_band_config_t) (1),
+ * sizeof(sp_cuda_cache_t) (2), so bindings can check their struct mirrors. */
+int sp_cuda_abi_struct_size(int which);
+
+/* New, for tests and benchmarks: force the fused-decode kernel family
+ * (0 = automatic, 1 = generic SIMT kernel, 2 = tensor-core ship kernel). */
+void sp_cuda_attn_force_impl(int impl);
+
+/* New, for benchmarks: when enabled, sp_cuda_attn_decode records CUDA events
+ * around its main kernel on the caller's stream; sp_cuda_attn_last_kernel_ms
+ * waits for the last one and returns its duration (-1 if none), and
+ * sp_cuda_attn_last_splits the number of token chunks it used. */
+void  sp_cuda_attn_profile(int enable);
+float sp_cuda_attn_last_kernel_ms(void);
+int   sp_cuda_attn_last_splits(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SHANNON_PRIME_CUDA_H */

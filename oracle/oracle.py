@@ -1,0 +1,175 @@
+"""ctypes binding of the CPU oracle (oracle/sp_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline legs, never by the shipped library.  See
+oracle/sp_oracle.h for what pins the restatement ("partially pinned").
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "lib" / "libsp_oracle.so"
+MAX_BANDS = 16
+
+
+class Bands(C.Structure):
+    _fields_ = [
+        ("n", C.c_int), ("n_bands", C.c_int),
+        ("bits", C.c_int * MAX_BANDS), ("off", C.c_int * MAX_BANDS),
+        ("size", C.c_int * MAX_BANDS), ("byte_off", C.c_int * MAX_BANDS),
+        ("total_bytes", C.c_int),
+    ]
+
+
+_lib = None
+_P = C.c_void_p
+
+
+def build() -> Path:
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return LIB_PATH
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            build()
+        L = C.CDLL(str(LIB_PATH))
+        L.or_f32_to_f16.restype = C.c_uint16
+        L.or_f32_to_f16.argtypes = [C.c_float]
+        L.or_f16_to_f32.restype = C.c_float
+        L.or_f16_to_f32.argtypes = [C.c_uint16]
+        L.or_band_config.restype = C.c_int
+        L.or_band_config.argtypes = [C.POINTER(Bands), C.c_int, C.c_int, C.POINTER(C.c_int)]
+        L.or_vht2.argtypes = [_P, C.c_int]
+        L.or_mobius_order.argtypes = [C.c_int, _P]
+        L.or_band_quantize.argtypes = [_P, _P, C.POINTER(Bands)]
+        L.or_band_dequantize.argtypes = [_P, _P, C.POINTER(Bands), C.c_int]
+        L.or_ship_write_batch.argtypes = [C.c_int, _P, C.c_size_t, _P, C.POINTER(Bands), _P, C.c_int]
+        L.or_ship_read_batch.argtypes = [C.c_int, _P, _P, C.POINTER(Bands), _P, C.c_int, C.c_int]
+        L.or_attn_decode.argtypes = [_P, C.c_size_t, _P, C.c_size_t, C.POINTER(Bands),
+                                     C.POINTER(Bands), _P, C.c_int, C.c_int, C.c_int, _P,
+                                     C.c_float, _P, C.c_int]
+        L.or_correlation.restype = C.c_double
+        L.or_correlation.argtypes = [_P, _P, C.c_int]
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray | None) -> int | None:
+    return None if a is None else a.ctypes.data
+
+
+def bands(n: int, bits) -> Bands:
+    b = Bands()
+    arr = (C.c_int * len(bits))(*bits)
+    if lib().or_band_config(C.byref(b), n, len(bits), arr) != 0:
+        raise ValueError(f"bad band config n={n} bits={bits}")
+    return b
+
+
+def threads() -> int:
+    return int(os.environ.get("SP_ORACLE_THREADS", os.cpu_count() or 1))
+
+
+def f32_to_f16(x: float) -> int:
+    return lib().or_f32_to_f16(x)
+
+
+def vht2(x: np.ndarray) -> np.ndarray:
+    y = np.ascontiguousarray(x, dtype=np.float32).copy()
+    flat = y.reshape(-1, y.shape[-1])
+    for row in flat:
+        lib().or_vht2(row.ctypes.data, row.shape[0])
+    return y
+
+
+def mobius_order(n: int) -> np.ndarray:
+    o = np.zeros(n, dtype=np.int32)
+    lib().or_mobius_order(n, o.ctypes.data)
+    return o
+
+
+def ship_write(vecs: np.ndarray, bits, mobius: bool, n_threads: int | None = None) -> np.ndarray:
+    """vecs [N][n] float32 -> packed uint8 [N][total_bytes]."""
+    v = np.ascontiguousarray(vecs, dtype=np.float32).reshape(-1, vecs.shape[-1])
+    n = v.shape[1]
+    bc = bands(n, bits)
+    out = np.zeros((v.shape[0], bc.total_bytes), dtype=np.uint8)
+    order = mobius_order(n) if mobius else None
+    lib().or_ship_write_batch(v.shape[0], v.ctypes.data, n, out.ctypes.data, C.byref(bc),
+                              _p(order), n_threads or threads())
+    return out
+
+
+def ship_read(packed: np.ndarray, n: int, bits, mobius: bool, max_bands: int = -1,
+              n_threads: int | None = None) -> np.ndarray:
+    p = np.ascontiguousarray(packed, dtype=np.uint8)
+    bc = bands(n, bits)
+    assert p.shape[-1] == bc.total_bytes
+    p2 = p.reshape(-1, bc.total_bytes)
+    out = np.zeros((p2.shape[0], n), dtype=np.float32)
+    order = mobius_order(n) if mobius else None
+    lib().or_ship_read_batch(p2.shape[0], p2.ctypes.data, out.ctypes.data, C.byref(bc),
+                             _p(order), max_bands, n_threads or threads())
+    return out
+
+
+def band_quantize(coeffs: np.ndarray, bits) -> np.ndarray:
+    c = np.ascontiguousarray(coeffs, dtype=np.float32).reshape(-1, coeffs.shape[-1])
+    bc = bands(c.shape[1], bits)
+    out = np.zeros((c.shape[0], bc.total_bytes), dtype=np.uint8)
+    for i in range(c.shape[0]):
+        lib().or_band_quantize(c[i].ctypes.data, out[i].ctypes.data, C.byref(bc))
+    return out
+
+
+def band_dequantize(packed: np.ndarray, n: int, bits, max_bands: int = -1) -> np.ndarray:
+    p = np.ascontiguousarray(packed, dtype=np.uint8)
+    bc = bands(n, bits)
+    p2 = p.reshape(-1, bc.total_bytes)
+    out = np.zeros((p2.shape[0], n), dtype=np.float32)
+    for i in range(p2.shape[0]):
+        lib().or_band_dequantize(p2[i].ctypes.data, out[i].ctypes.data, C.byref(bc), max_bands)
+    return out
+
+
+def attn_decode(k_slots: np.ndarray, v_slots: np.ndarray, n: int, k_bits, v_bits, mobius: bool,
+                q_f16: np.ndarray, kv_len: int, logit_scale: float = 1.0,
+                n_threads: int | None = None) -> np.ndarray:
+    """k_slots [H][>=kv_len][kb] uint8, v_slots likewise, q_f16 [n_q][n] float16
+    -> out [n_q][n] float32 (double-accumulated reference attention)."""
+    kb, vb = bands(n, k_bits), bands(n, v_bits)
+    ks = np.ascontiguousarray(k_slots, dtype=np.uint8)
+    vs = np.ascontiguousarray(v_slots, dtype=np.uint8)
+    H = ks.shape[0]
+    q = np.ascontiguousarray(q_f16, dtype=np.float16).view(np.uint16)
+    nq = q.shape[0]
+    out = np.zeros((nq, n), dtype=np.float32)
+    order = mobius_order(n) if mobius else None
+    lib().or_attn_decode(ks.ctypes.data, ks.shape[1] * ks.shape[2], vs.ctypes.data,
+                         vs.shape[1] * vs.shape[2], C.byref(kb), C.byref(vb), _p(order), H,
+                         nq, kv_len, q.ctypes.data, logit_scale, out.ctypes.data,
+                         n_threads or threads())
+    return out
+
+
+def correlation(a: np.ndarray, b: np.ndarray) -> float:
+    a = np.ascontiguousarray(a, dtype=np.float32).ravel()
+    b = np.ascontiguousarray(b, dtype=np.float32).ravel()
+    return lib().or_correlation(a.ctypes.data, b.ctypes.data, a.shape[0])
+
+
+def mean_vector_correlation(a: np.ndarray, b: np.ndarray) -> float:
+    """Pearson correlation per vector, averaged (the reference's per-vector
+    validation measure, sp_llama_validate_k)."""
+    a2 = a.reshape(-1, a.shape[-1])
+    b2 = b.reshape(-1, b.shape[-1])
+    return float(np.mean([correlation(x, y) for x, y in zip(a2, b2)]))

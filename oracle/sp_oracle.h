@@ -1,0 +1,98 @@
+/*
+ * sp_oracle.h — CPU restatement of the Shannon-Prime KV-cache hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  Nothing in the shipped library links, loads or
+ * calls this code; only tests/, __graft_entry__.smoke() and bench.py's CPU
+ * baseline legs use it, as the checker and as the timed CPU baseline.
+ *
+ * Parity status: PARTIALLY PINNED.  The reference CPU path (sp_shadow_*,
+ * sp_band_*, sp_vht2_forward_f32, sp_mobius_mask_init in the core library
+ * lib/shannon-prime) is an empty git submodule in the reference checkout
+ * (.gitmodules:1-3), so it can be neither built nor run.  What pins it:
+ *   - VHT2 follows the NEON restatement shannon_prime_adreno.c:270-309
+ *     (unnormalised ascending-len butterfly, then x 1.0f/sqrtf(n)), which
+ *     the reference's own test log reports as bit-equal to the core at
+ *     hd 32/64/128 (android_build/test_adreno_phone.log:44-46);
+ *   - band quantise/dequantise follow the reference kernels
+ *     shannon_prime_cuda.cu:131-270 operation by operation;
+ *   - known answers: packed bytes K 76 / V 50 at hd 128, K 42 / V 26 at
+ *     hd 64 (shannon_prime_llama.h:336-338, shannon_prime_vulkan.c:99-105);
+ *     correlation thresholds K > 0.985, V > 0.950 at hd 128
+ *     (test_adreno_phone.log:50-51);
+ *   - the reference's own CUDA quantiser, compiled from its source by
+ *     oracle/build_ref.sh, run on the same coefficients (GPU tests).
+ * Unpinned: the Möbius order table itself (restated as squarefree-first,
+ * ascending) and the core's tie rounding (restated as round-half-even, the
+ * reference CUDA kernel's __float2int_rn).
+ */
+#ifndef SP_ORACLE_H
+#define SP_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OR_MAX_BANDS 16
+
+typedef struct {
+    int n;                     /* vector length */
+    int n_bands;
+    int bits[OR_MAX_BANDS];
+    int off[OR_MAX_BANDS];     /* first coefficient of band b */
+    int size[OR_MAX_BANDS];    /* coefficients in band b */
+    int byte_off[OR_MAX_BANDS];/* byte offset of band b's fp16 scale */
+    int total_bytes;
+} or_bands_t;
+
+uint16_t or_f32_to_f16(float f);
+float    or_f16_to_f32(uint16_t h);
+
+int  or_band_config(or_bands_t *bc, int n, int n_bands, const int *bits);
+void or_vht2(float *x, int n);
+void or_mobius_order(int n, int *order);
+
+void or_band_quantize(const float *coeffs, uint8_t *out, const or_bands_t *bc);
+void or_band_dequantize(const uint8_t *in, float *coeffs, const or_bands_t *bc,
+                        int max_bands);
+
+void or_ship_write(const float *vec, uint8_t *out, const or_bands_t *bc,
+                   const int *order);
+void or_ship_read(const uint8_t *in, float *vec, const or_bands_t *bc,
+                  const int *order, int max_bands);
+
+/* Batched forms (OpenMP over vectors when n_threads > 1).  vec i is read
+ * from vecs + i * vec_stride (floats); packed row i goes to out + i * bytes. */
+void or_ship_write_batch(int n_vecs, const float *vecs, size_t vec_stride,
+                         uint8_t *out, const or_bands_t *bc, const int *order,
+                         int n_threads);
+void or_ship_read_batch(int n_vecs, const uint8_t *in, float *vecs,
+                        const or_bands_t *bc, const int *order, int max_bands,
+                        int n_threads);
+
+/* Decode attention over one compressed (layer) cache, the reference's fused
+ * decompress-KQ algorithm (llama_sp_fused_kq.cpp:82-165: decompress a row,
+ * dot it with every query of the group) extended with softmax and the
+ * decompressed V rows, accumulated in double.
+ *   k_slots: [n_kv_heads][slot_stride_k bytes], token t of head h at
+ *            k_slots + h*slot_stride_k + t*kb.total_bytes (same for V)
+ *   q:       [n_q_heads][n] fp16 bits; q head g uses kv head g / (n_q/n_kv)
+ *   out:     [n_q_heads][n] float
+ */
+void or_attn_decode(const uint8_t *k_slots, size_t slot_stride_k,
+                    const uint8_t *v_slots, size_t slot_stride_v,
+                    const or_bands_t *kb, const or_bands_t *vb,
+                    const int *order, int n_kv_heads, int n_q_heads,
+                    int kv_len, const uint16_t *q, float logit_scale,
+                    float *out, int n_threads);
+
+/* Pearson correlation accumulated in double. */
+double or_correlation(const float *a, const float *b, int n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,370 @@
+// sp_attn.cu — fused decompress-KQ / decompress-V decode attention.
+//
+// Math (no K or V row is ever reconstructed):
+//   K_hat_t = H * unreorder(c_t)          (H = orthonormal, symmetric VHT2)
+//   q . K_hat_t = (H q) . unreorder(c_t) = sum_i q'[i] c_t[i],
+//                 q'[i] = (H q)[order[i]]
+//   sum_t p_t V_hat_t = H (sum_t p_t cv_t)
+// so scores are dot products of the transformed query with the dequantised
+// codes, V is accumulated in the coefficient domain, and one VHT2 per
+// (layer, query head) finishes the output.
+//
+// Work split: flash-decoding.  A CTA owns one (layer, KV head, token chunk)
+// and all query heads of that KV head's GQA group; it writes an unnormalised
+// partial (running max m, denominator l, coefficient accumulator) to the
+// cache's workspace, and a combine kernel merges the chunks with
+// log-sum-exp weights, applies the VHT2 and writes fp16.
+//
+// This file holds the generic SIMT kernel (any power-of-two head_dim, any
+// band layout, 1..8 queries per KV head), the combine kernel and the
+// dispatcher.  sp_attn_mma.cu holds the tensor-core kernel for the ship
+// layout (head_dim 128, K bands 5/5/4/3, V 3-bit).
+#include "sp_internal.cuh"
+#include "sp_attn.cuh"
+
+#include <math.h>
+#include <string.h>
+
+namespace {
+
+constexpr int kAttnWarps = 4;
+
+__device__ __forceinline__ int band_of_i(const SpBandLayout &bl, int i)
+{
+    int b = 0;
+#pragma unroll 1
+    for (int k = 1; k < bl.n_bands; k++)
+        if (i >= bl.off[k]) b = k;
+    return b;
+}
+
+// Dequantised coefficient i of a packed row (partial-band rule applied).
+__device__ __forceinline__ float coeff_at(const SpBandLayout &bl, const uint8_t *row, int i,
+                                          int nb_use)
+{
+    const int b = band_of_i(bl, i);
+    if (b >= nb_use) return 0.0f;
+    const int bits = bl.bits[b];
+    const int max_val = (1 << (bits - 1)) - 1;
+    const uint8_t *p = row + bl.byte_off[b];
+    float scale = __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
+    if (!isfinite(scale)) scale = 0.0f;
+    const int bp = (i - bl.off[b]) * bits;
+    const int byte = 2 + (bp >> 3);
+    uint32_t w = p[byte];
+    if ((bp & 7) + bits > 8) w |= (uint32_t)p[byte + 1] << 8;
+    const int u = (int)((w >> (bp & 7)) & ((1u << bits) - 1u));
+    return (float)(u - max_val) * scale;
+}
+
+}  // namespace
+
+// Transformed, permuted, scaled query of one (layer, q head) into s_out[n]
+// (one warp).  s_tmp is n floats of warp-private shared memory.
+template <int E>
+__device__ void sp_attn_prepare_query(const __half *q, const int *order, float scale_all,
+                                      float *s_tmp, float *s_out, int lane)
+{
+    constexpr int n = 32 * E;
+    float x[E];
+#pragma unroll
+    for (int e = 0; e < E; e++) x[e] = __half2float(q[lane * E + e]);
+    sp_warp_wht<E>(x, lane);
+#pragma unroll
+    for (int e = 0; e < E; e++) s_tmp[lane * E + e] = x[e] * scale_all;
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < E; e++) {
+        const int i = lane * E + e;
+        s_out[i] = order ? s_tmp[order[i]] : s_tmp[i];
+    }
+    __syncwarp();
+    (void)n;
+}
+
+namespace {
+
+template <int E>
+__global__ void __launch_bounds__(kAttnWarps * 32)
+k_attn_generic(SpAttnArgs a)
+{
+    constexpr int n = 32 * E;
+    extern __shared__ __align__(16) float sm[];
+    const int G = a.group;
+    float *s_q = sm;                                   // [G][n]
+    float *s_tmp = s_q + G * n;                        // [warps][n]
+    float *s_acc = s_tmp + kAttnWarps * n;             // [warps][G][n]
+    float *s_ml = s_acc + kAttnWarps * G * n;          // [warps][G][2]
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int split = blockIdx.x;
+    const int h = blockIdx.y;
+    const int li = blockIdx.z;                  // layer index within the call
+    const int layer = a.layer0 + li;
+    const int t_begin = split * a.chunk;
+    const int t_end = min(a.kv_len, t_begin + a.chunk);
+    const long long slot = (long long)layer * a.n_kv_heads + h;
+    const float kLog2e = 1.4426950408889634f;
+
+    for (int g = warp; g < G; g += kAttnWarps) {
+        const __half *qg = a.q + ((long long)li * a.n_q_heads + h * G + g) * n;
+        sp_attn_prepare_query<E>(qg, a.order, a.logit_scale * kLog2e * a.inv_sqrt_n, s_tmp + warp * n,
+                                 s_q + g * n, lane);
+    }
+    float *acc = s_acc + warp * G * n;
+    for (int j = lane; j < G * n; j += 32) acc[j] = 0.0f;
+    __syncthreads();
+
+    float m[8], l[8];
+#pragma unroll
+    for (int g = 0; g < 8; g++) { m[g] = -INFINITY; l[g] = 0.0f; }
+
+    const uint8_t *kbase = a.k_cache + slot * a.k_slot_stride;
+    const uint8_t *vbase = a.v_cache + slot * a.v_slot_stride;
+    for (int t = t_begin + warp; t < t_end; t += kAttnWarps) {
+        const uint8_t *krow = kbase + (long long)t * a.kl.total_bytes;
+        const uint8_t *vrow = vbase + (long long)t * a.vl.total_bytes;
+        float ck[E], cv[E];
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            ck[e] = coeff_at(a.kl, krow, lane * E + e, a.nb_k);
+            cv[e] = coeff_at(a.vl, vrow, lane * E + e, a.nb_v);
+        }
+#pragma unroll 1
+        for (int g = 0; g < G; g++) {
+            float s = 0.0f;
+#pragma unroll
+            for (int e = 0; e < E; e++) s += ck[e] * s_q[g * n + lane * E + e];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            // s is the base-2 logit (log2e folded into the query).
+            float mg = m[0], lg = l[0];
+#pragma unroll
+            for (int k = 1; k < 8; k++) if (k == g) { mg = m[k]; lg = l[k]; }
+            const float mn = fmaxf(mg, s);
+            const float alpha = exp2f(mg - mn);
+            const float p = exp2f(s - mn);
+            lg = lg * alpha + p;
+#pragma unroll
+            for (int k = 0; k < 8; k++) if (k == g) { m[k] = mn; l[k] = lg; }
+            float *ag = acc + g * n;
+#pragma unroll
+            for (int e = 0; e < E; e++) {
+                const int i = lane * E + e;
+                ag[i] = ag[i] * alpha + p * cv[e];
+            }
+        }
+    }
+    if (lane == 0) {
+        for (int g = 0; g < G; g++) {
+            float mg = m[0], lg = l[0];
+            for (int k = 1; k < 8; k++) if (k == g) { mg = m[k]; lg = l[k]; }
+            s_ml[(warp * G + g) * 2] = mg;
+            s_ml[(warp * G + g) * 2 + 1] = lg;
+        }
+    }
+    __syncthreads();
+    // Merge the warps and write the CTA's partial.
+    for (int g = 0; g < G; g++) {
+        float M = -INFINITY;
+        for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, s_ml[(w * G + g) * 2]);
+        float wsc[kAttnWarps], L = 0.0f;
+        for (int w = 0; w < kAttnWarps; w++) {
+            const float mw = s_ml[(w * G + g) * 2];
+            wsc[w] = (mw == -INFINITY) ? 0.0f : exp2f(mw - M);
+            L += wsc[w] * s_ml[(w * G + g) * 2 + 1];
+        }
+        float *part = sp_attn_partial(a, li, h * G + g, split);
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            float v = 0.0f;
+            for (int w = 0; w < kAttnWarps; w++) v += wsc[w] * s_acc[(w * G + g) * n + i];
+            part[4 + i] = v;
+        }
+        if (threadIdx.x == 0) { part[0] = M; part[1] = L; }
+    }
+}
+
+// Merge the split partials of one (layer, q head), transform, write fp16.
+template <int E>
+__global__ void k_attn_combine(SpAttnArgs a)
+{
+    constexpr int n = 32 * E;
+    const int lane = threadIdx.x & 31;
+    const int qh = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (qh >= a.n_q_heads) return;
+    const int li = blockIdx.y;
+    float M = -INFINITY;
+    for (int s = 0; s < a.n_splits; s++) M = fmaxf(M, sp_attn_partial(a, li, qh, s)[0]);
+    float x[E];
+#pragma unroll
+    for (int e = 0; e < E; e++) x[e] = 0.0f;
+    float L = 0.0f;
+    for (int s = 0; s < a.n_splits; s++) {
+        const float *p = sp_attn_partial(a, li, qh, s);
+        if (p[0] == -INFINITY) continue;
+        const float w = exp2f(p[0] - M);
+        L += w * p[1];
+#pragma unroll
+        for (int e = 0; e < E; e++) x[e] += w * p[4 + lane * E + e];
+    }
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+    sp_warp_wht<E>(x, lane);
+    __half *o = a.out + ((long long)li * a.n_q_heads + qh) * n + lane * E;
+#pragma unroll
+    for (int e = 0; e < E; e++) o[e] = __float2half_rn(x[e] * a.inv_sqrt_n * inv);
+}
+
+template <int E>
+int launch_generic(const SpAttnArgs &a, cudaStream_t s)
+{
+    constexpr int n = 32 * E;
+    const size_t sm = sizeof(float) * ((size_t)a.group * n + kAttnWarps * n +
+                                       (size_t)kAttnWarps * a.group * n + kAttnWarps * a.group * 2);
+    auto k = k_attn_generic<E>;
+    if (sm > 48 * 1024)
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    dim3 grid(a.n_splits, a.n_kv_heads, a.n_layers);
+    k<<<grid, kAttnWarps * 32, sm, s>>>(a);
+    return sp_check_cuda(cudaGetLastError(), "attention launch");
+}
+
+template <int E>
+int launch_combine(const SpAttnArgs &a, cudaStream_t s)
+{
+    const int per_block = 4;
+    dim3 grid((a.n_q_heads + per_block - 1) / per_block, a.n_layers);
+    k_attn_combine<E><<<grid, per_block * 32, 0, s>>>(a);
+    return sp_check_cuda(cudaGetLastError(), "attention combine launch");
+}
+
+}  // namespace
+
+// ------------------------------------------------------------ dispatch --
+
+size_t sp_attn_workspace_bytes(const sp_cuda_cache_t *cc)
+{
+    return (size_t)cc->attn_ws_layers * cc->attn_max_q_heads * kAttnMaxSplits *
+           sp_attn_partial_stride(cc->config.head_dim) * sizeof(float);
+}
+
+static int g_force_impl = 0;   // 0 auto, 1 generic SIMT, 2 tensor-core
+
+extern "C" void sp_cuda_attn_force_impl(int impl) { g_force_impl = impl; }
+
+// Optional timing of the main (non-combine) kernel with CUDA events recorded
+// on the caller's stream, for the benchmark's roofline figure.
+static bool g_prof = false;
+static cudaEvent_t g_ev[2] = {nullptr, nullptr};
+static int g_prof_splits = 0;
+
+extern "C" void sp_cuda_attn_profile(int enable)
+{
+    g_prof = enable != 0;
+    if (g_prof && !g_ev[0]) {
+        cudaEventCreate(&g_ev[0]);
+        cudaEventCreate(&g_ev[1]);
+    }
+}
+
+extern "C" float sp_cuda_attn_last_kernel_ms(void)
+{
+    if (!g_ev[0]) return -1.0f;
+    float ms = -1.0f;
+    if (cudaEventSynchronize(g_ev[1]) != cudaSuccess) return -1.0f;
+    cudaEventElapsedTime(&ms, g_ev[0], g_ev[1]);
+    return ms;
+}
+
+extern "C" int sp_cuda_attn_last_splits(void) { return g_prof_splits; }
+
+extern "C" int sp_cuda_attn_decode(const sp_cuda_cache_t *cc, int layer0, int n_layers,
+                                   const void *d_q, int n_q_heads, int kv_len,
+                                   float logit_scale, void *d_out, int max_bands, void *stream)
+{
+    sp_clear_error();
+    if (!cc || !cc->d_k_cache || !d_q || !d_out)
+        return sp_set_error(SP_ERR_ARG, "attn_decode: NULL argument");
+    const int H = cc->config.n_heads_kv;
+    if (layer0 < 0 || n_layers <= 0 || layer0 + n_layers > cc->config.n_layers)
+        return sp_set_error(SP_ERR_ARG, "attn_decode: layers [%d,%d) out of range", layer0, layer0 + n_layers);
+    if (n_q_heads <= 0 || n_q_heads % H || n_q_heads / H > 8)
+        return sp_set_error(SP_ERR_ARG, "attn_decode: n_q_heads %d must be a multiple of %d with <= 8 per KV head", n_q_heads, H);
+    if (n_layers > cc->attn_ws_layers || n_q_heads > cc->attn_max_q_heads)
+        return sp_set_error(SP_ERR_ARG, "attn_decode: workspace too small");
+    if (kv_len < 0 || kv_len > cc->max_seq_len)
+        return sp_set_error(SP_ERR_ARG, "attn_decode: kv_len %d outside [0,%d]", kv_len, cc->max_seq_len);
+    if (cudaSetDevice(cc->device) != cudaSuccess)
+        return sp_set_error(SP_ERR_CUDA, "attn_decode: cudaSetDevice");
+
+    SpAttnArgs a;
+    memset(&a, 0, sizeof(a));
+    a.k_cache = (const uint8_t *)cc->d_k_cache;
+    a.v_cache = (const uint8_t *)cc->d_v_cache;
+    a.k_slot_stride = (long long)cc->max_seq_len * cc->k_bands.total_bytes;
+    a.v_slot_stride = (long long)cc->max_seq_len * cc->v_bands.total_bytes;
+    a.order = cc->config.use_mobius_mask ? cc->d_mobius_order : nullptr;
+    a.q = (const __half *)d_q;
+    a.out = (__half *)d_out;
+    a.ws = (float *)cc->d_attn_ws;
+    a.layer0 = layer0; a.n_layers = n_layers; a.n_kv_heads = H;
+    a.n_q_heads = n_q_heads; a.group = n_q_heads / H;
+    a.kv_len = kv_len;
+    a.kl = sp_layout_from(cc->k_bands);
+    a.vl = sp_layout_from(cc->v_bands);
+    a.nb_k = (max_bands < 0 || max_bands >= a.kl.n_bands) ? a.kl.n_bands : max_bands;
+    a.nb_v = (max_bands < 0 || max_bands >= a.vl.n_bands) ? a.vl.n_bands : max_bands;
+    a.logit_scale = logit_scale;
+    a.inv_sqrt_n = sp_inv_sqrt_n(cc->config.head_dim);
+    a.status = cc->d_status;
+
+    cudaStream_t s = (cudaStream_t)stream;
+    const bool use_mma = g_force_impl != 1 && sp_attn_mma_supported(a) == SP_OK;
+    if (g_force_impl == 2 && !use_mma)
+        return sp_set_error(SP_ERR_UNSUPPORTED, "attn_decode: tensor-core path does not support this layout");
+
+    // Chunking: enough CTAs to fill the 148 SMs several times over, chunks of
+    // at least kAttnMinChunk tokens, at most kAttnMaxSplits chunks.
+    const int units = n_layers * H;
+    const int target_ctas = use_mma ? 148 * 4 : 148 * 8;
+    int splits = (target_ctas + units - 1) / units;
+    const int max_by_len = (kv_len + kAttnMinChunk - 1) / kAttnMinChunk;
+    if (splits > max_by_len) splits = max_by_len;
+    if (splits > kAttnMaxSplits) splits = kAttnMaxSplits;
+    if (splits < 1) splits = 1;
+    int chunk = (kv_len + splits - 1) / splits;
+    chunk = (chunk + 15) & ~15;
+    if (chunk < 16) chunk = 16;
+    a.chunk = chunk;
+    a.n_splits = kv_len == 0 ? 0 : (kv_len + chunk - 1) / chunk;
+    if (a.n_splits > kAttnMaxSplits)
+        return sp_set_error(SP_ERR_ARG, "attn_decode: too many splits");
+
+    int rc = SP_OK;
+    const int n = cc->config.head_dim;
+    g_prof_splits = a.n_splits;
+    if (a.n_splits > 0) {
+        if (g_prof) cudaEventRecord(g_ev[0], s);
+        if (use_mma) {
+            rc = sp_attn_mma_launch(a, s);
+        } else {
+            switch (n) {
+            case 32:  rc = launch_generic<1>(a, s); break;
+            case 64:  rc = launch_generic<2>(a, s); break;
+            case 128: rc = launch_generic<4>(a, s); break;
+            case 256: rc = launch_generic<8>(a, s); break;
+            case 512: rc = launch_generic<16>(a, s); break;
+            default: return sp_set_error(SP_ERR_UNSUPPORTED, "attn_decode: head_dim %d", n);
+            }
+        }
+        if (g_prof) cudaEventRecord(g_ev[1], s);
+        if (rc) return rc;
+    }
+    switch (n) {
+    case 32:  return launch_combine<1>(a, s);
+    case 64:  return launch_combine<2>(a, s);
+    case 128: return launch_combine<4>(a, s);
+    case 256: return launch_combine<8>(a, s);
+    case 512: return launch_combine<16>(a, s);
+    }
+    return sp_set_error(SP_ERR_UNSUPPORTED, "attn_decode: head_dim %d", n);
+}

@@ -1,0 +1,489 @@
+// sp_ship.cu — ship-path codec kernels for sm_100a: the write path
+// (VHT2 -> Möbius reorder -> band quantise -> pack) and the read path
+// (unpack -> dequantise -> Möbius unreorder -> VHT2), plus the
+// reference-named C-ABI launchers of shannon_prime_cuda.h.
+//
+// Design: one warp per vector.  The vector lives in registers (E = n/32
+// floats per lane); the Hartley butterfly runs in registers and warp
+// shuffles (sp_warp_wht) instead of one __syncthreads per stage in shared
+// memory (reference kernel_vht2_p2, shannon_prime_cuda.cu:37-75).  The
+// reorder is one shared-memory gather, the band absmax one redux.sync per
+// band, and packing is output-byte-stationary: each lane assembles whole
+// output bytes from the codes that overlap them, so no serial bit loop
+// (reference kernel_band_quantize_simple packs 128 codes in one thread,
+// shannon_prime_cuda.cu:131-204) and no atomics.  A CTA handles 8
+// consecutive positions of one head, so its packed rows are one contiguous
+// range written by the whole CTA.
+//
+// Bit-exactness: every float step is the single IEEE operation the CPU
+// restatement performs (__fadd_rn/__fsub_rn/__fmul_rn/__fdiv_rn, no
+// contraction), __float2half_rn for the scale, round-half-even for codes.
+#include "sp_internal.cuh"
+
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+namespace {
+
+constexpr int kWarps = 8;   // vectors (positions) per CTA
+
+struct EncodeArgs {
+    const void *in;            // [n_tokens][nh][n] elements
+    uint8_t *out_base;         // slab base
+    long long slot0;           // slot of head 0
+    long long slot_stride;     // bytes per slot
+    int n_tokens;
+    int nh;
+    int start_pos;
+    const int *order;          // Möbius order or nullptr
+    float inv_sqrt_n;
+    SpBandLayout bl;
+};
+
+struct DecodeArgs {
+    const uint8_t *in_base;
+    long long slot;
+    long long slot_stride;
+    int start_pos;
+    int n_pos;
+    float *out;                // [n_pos][n]
+    const int *order;          // Möbius order or nullptr (unreorder)
+    float inv_sqrt_n;
+    int max_bands;
+    SpBandLayout bl;
+};
+
+__device__ __forceinline__ int band_of(const SpBandLayout &bl, int i)
+{
+    int b = 0;
+#pragma unroll 1
+    for (int k = 1; k < bl.n_bands; k++)
+        if (i >= bl.off[k]) b = k;
+    return b;
+}
+
+// Assemble packed byte j of a row from the codes in shared memory.
+__device__ __forceinline__ uint8_t pack_byte(const SpBandLayout &bl, const uint8_t *codes,
+                                             const uint16_t *scale_bits, int j)
+{
+    int b = 0;
+#pragma unroll 1
+    for (int k = 1; k < bl.n_bands; k++)
+        if (j >= bl.byte_off[k]) b = k;
+    int r = j - bl.byte_off[b];
+    if (r == 0) return (uint8_t)(scale_bits[b] & 0xff);
+    if (r == 1) return (uint8_t)(scale_bits[b] >> 8);
+    const int d = r - 2, bits = bl.bits[b], sz = bl.size[b];
+    const uint8_t *c = codes + bl.off[b];
+    int k0 = (8 * d) / bits;
+    int k1 = (8 * d + 7) / bits;
+    if (k1 > sz - 1) k1 = sz - 1;
+    uint32_t v = 0;
+    for (int k = k0; k <= k1; k++) {
+        int sh = k * bits - 8 * d;
+        v |= sh >= 0 ? ((uint32_t)c[k] << sh) : ((uint32_t)c[k] >> (-sh));
+    }
+    return (uint8_t)(v & 0xff);
+}
+
+// Write path.  Grid: x = head-major tiles of kWarps positions, one warp per
+// vector.  Dynamic smem: order[n] ints, per-warp float buf[n] + codes[n],
+// per-warp scale info, and the CTA's packed rows.
+template <int E, typename Tin, bool WHT>
+__global__ void __launch_bounds__(kWarps * 32)
+k_encode(EncodeArgs a)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int n = 32 * E;
+    const SpBandLayout &bl = a.bl;
+    int *s_order = reinterpret_cast<int *>(smem);
+    float *s_buf = reinterpret_cast<float *>(s_order + n);             // [kWarps][n]
+    float *s_inv = s_buf + kWarps * n;                                  // [kWarps][16]
+    uint16_t *s_sbits = reinterpret_cast<uint16_t *>(s_inv + kWarps * SP_MAX_BANDS);
+    uint8_t *s_codes = reinterpret_cast<uint8_t *>(s_sbits + kWarps * SP_MAX_BANDS);
+    uint8_t *s_rows = s_codes + kWarps * n;                             // [kWarps][total]
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_tiles = (a.n_tokens + kWarps - 1) / kWarps;
+    const int h = blockIdx.x % a.nh;
+    const int tile = blockIdx.x / a.nh;
+    if (tile >= n_tiles) return;
+    const int t0 = tile * kWarps;
+    const int t = t0 + warp;
+    const bool active = t < a.n_tokens;
+
+    if (a.order)
+        for (int i = threadIdx.x; i < n; i += blockDim.x) s_order[i] = a.order[i];
+    __syncthreads();
+
+    float *buf = s_buf + warp * n;
+    uint8_t *codes = s_codes + warp * n;
+    float x[E];
+    if (active) {
+        const Tin *src = reinterpret_cast<const Tin *>(a.in) +
+                         ((long long)t * a.nh + h) * n + lane * E;
+        if constexpr (sizeof(Tin) == 4 && E % 4 == 0) {
+#pragma unroll
+            for (int e = 0; e < E; e += 4) {
+                float4 v = __ldg(reinterpret_cast<const float4 *>(src + e));
+                x[e] = v.x; x[e + 1] = v.y; x[e + 2] = v.z; x[e + 3] = v.w;
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < E; e++) x[e] = sp_load_as_float(src, e);
+        }
+        if constexpr (WHT) {
+            sp_warp_wht<E>(x, lane);
+#pragma unroll
+            for (int e = 0; e < E; e++) x[e] = __fmul_rn(x[e], a.inv_sqrt_n);
+        }
+        if (a.order) {
+#pragma unroll
+            for (int e = 0; e < E; e++) buf[lane * E + e] = x[e];
+            __syncwarp();
+#pragma unroll
+            for (int e = 0; e < E; e++) x[e] = buf[s_order[lane * E + e]];
+        }
+        // Per-band absmax: |x| of a non-NaN float orders like its bit pattern.
+        for (int b = 0; b < bl.n_bands; b++) {
+            unsigned m = 0;
+#pragma unroll
+            for (int e = 0; e < E; e++) {
+                int i = lane * E + e;
+                if (i >= bl.off[b] && i < bl.off[b] + bl.size[b]) {
+                    float av = fabsf(x[e]);
+                    unsigned u = __float_as_uint(av);
+                    if (!(av != av) && u > m) m = u;
+                }
+            }
+            m = __reduce_max_sync(0xffffffffu, m);
+            if (lane == b) {
+                float amax = __uint_as_float(m);
+                int max_val = (1 << (bl.bits[b] - 1)) - 1;
+                float scale = amax > 0.0f ? __fdiv_rn(amax, (float)max_val) : 0.0f;
+                __half hs = __float2half_rn(scale);
+                float stored = __half2float(hs);
+                s_sbits[warp * SP_MAX_BANDS + b] = __half_as_ushort(hs);
+                s_inv[warp * SP_MAX_BANDS + b] = stored > 0.0f ? __fdiv_rn(1.0f, stored) : 0.0f;
+            }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            int i = lane * E + e;
+            int b = band_of(bl, i);
+            int max_val = (1 << (bl.bits[b] - 1)) - 1;
+            float p = __fmul_rn(x[e], s_inv[warp * SP_MAX_BANDS + b]);
+            int q = __float2int_rn(p);            // NaN -> 0, saturating
+            q = q > max_val ? max_val : (q < -max_val ? -max_val : q);
+            codes[i] = (uint8_t)(q + max_val);
+        }
+        __syncwarp();
+        uint8_t *row = s_rows + warp * bl.total_bytes;
+        for (int j = lane; j < bl.total_bytes; j += 32)
+            row[j] = pack_byte(bl, codes, s_sbits + warp * SP_MAX_BANDS, j);
+    }
+    __syncthreads();
+    // The CTA's rows are contiguous in the slot: copy them out together.
+    const int n_rows = min(kWarps, a.n_tokens - t0);
+    const long long nbytes = (long long)n_rows * bl.total_bytes;
+    uint8_t *dst = a.out_base + (a.slot0 + h) * a.slot_stride +
+                   (long long)(a.start_pos + t0) * bl.total_bytes;
+    if ((((uintptr_t)dst) & 3) == 0 && (nbytes & 3) == 0) {
+        const uint32_t *s32 = reinterpret_cast<const uint32_t *>(s_rows);
+        uint32_t *d32 = reinterpret_cast<uint32_t *>(dst);
+        for (int j = threadIdx.x; j < nbytes / 4; j += blockDim.x) d32[j] = s32[j];
+    } else {
+        for (int j = threadIdx.x; j < nbytes; j += blockDim.x) dst[j] = s_rows[j];
+    }
+}
+
+// Read path.  One warp per position of one slot; the CTA's packed rows are
+// first copied (coalesced) into shared memory, then each lane unpacks the
+// codes of its E reordered coefficients.
+template <int E, bool WHT>
+__global__ void __launch_bounds__(kWarps * 32)
+k_decode(DecodeArgs a)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int n = 32 * E;
+    const SpBandLayout &bl = a.bl;
+    int *s_order = reinterpret_cast<int *>(smem);
+    float *s_buf = reinterpret_cast<float *>(s_order + n);   // [kWarps][n]
+    uint8_t *s_rows = reinterpret_cast<uint8_t *>(s_buf + kWarps * n);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t0 = blockIdx.x * kWarps;
+    const int n_rows = min(kWarps, a.n_pos - t0);
+    if (n_rows <= 0) return;
+    if (a.order)
+        for (int i = threadIdx.x; i < n; i += blockDim.x) s_order[i] = a.order[i];
+    const uint8_t *src = a.in_base + a.slot * a.slot_stride +
+                         (long long)(a.start_pos + t0) * bl.total_bytes;
+    const int nbytes = n_rows * bl.total_bytes;
+    for (int j = threadIdx.x; j < nbytes; j += blockDim.x) s_rows[j] = __ldg(src + j);
+    __syncthreads();
+
+    const int t = t0 + warp;
+    if (t >= a.n_pos) return;
+    const int nb_use = (a.max_bands < 0 || a.max_bands >= bl.n_bands) ? bl.n_bands : a.max_bands;
+    const uint8_t *row = s_rows + warp * bl.total_bytes;
+    float x[E];
+#pragma unroll
+    for (int e = 0; e < E; e++) {
+        const int i = lane * E + e;
+        const int b = band_of(bl, i);
+        float v = 0.0f;
+        if (b < nb_use) {
+            const int bits = bl.bits[b];
+            const int max_val = (1 << (bits - 1)) - 1;
+            const uint8_t *p = row + bl.byte_off[b];
+            float scale = __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
+            if (!isfinite(scale)) scale = 0.0f;
+            const int bp = (i - bl.off[b]) * bits;
+            const int byte = 2 + (bp >> 3);
+            uint32_t w = p[byte];
+            if ((bp & 7) + bits > 8) w |= (uint32_t)p[byte + 1] << 8;
+            const int u = (int)((w >> (bp & 7)) & ((1u << bits) - 1u));
+            v = __fmul_rn((float)(u - max_val), scale);
+        }
+        x[e] = v;
+    }
+    if (a.order) {
+        float *buf = s_buf + warp * n;
+#pragma unroll
+        for (int e = 0; e < E; e++) buf[s_order[lane * E + e]] = x[e];
+        __syncwarp();
+#pragma unroll
+        for (int e = 0; e < E; e++) x[e] = buf[lane * E + e];
+    }
+    if constexpr (WHT) {
+        sp_warp_wht<E>(x, lane);
+#pragma unroll
+        for (int e = 0; e < E; e++) x[e] = __fmul_rn(x[e], a.inv_sqrt_n);
+    }
+    float *dst = a.out + (long long)t * n + lane * E;
+    if constexpr (E % 4 == 0) {
+#pragma unroll
+        for (int e = 0; e < E; e += 4)
+            *reinterpret_cast<float4 *>(dst + e) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
+    } else {
+#pragma unroll
+        for (int e = 0; e < E; e++) dst[e] = x[e];
+    }
+}
+
+// In-place Möbius (un)reorder of n_vecs vectors of length n (one warp each).
+template <bool INVERSE>
+__global__ void k_permute(float *data, const int *order, int n, int n_vecs)
+{
+    extern __shared__ float pbuf[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long v = (long long)blockIdx.x * kWarps + warp;
+    if (v >= n_vecs) return;
+    float *buf = pbuf + warp * n;
+    float *x = data + v * n;
+    for (int i = lane; i < n; i += 32) buf[i] = x[i];
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) {
+        if (INVERSE) x[order[i]] = buf[i];
+        else x[i] = buf[order[i]];
+    }
+}
+
+size_t encode_smem(int n, int total_bytes)
+{
+    return (size_t)n * 4 + (size_t)kWarps * n * 4 + (size_t)kWarps * SP_MAX_BANDS * 6 +
+           (size_t)kWarps * n + (size_t)kWarps * total_bytes + 16;
+}
+
+size_t decode_smem(int n, int total_bytes)
+{
+    return (size_t)n * 4 + (size_t)kWarps * n * 4 + (size_t)kWarps * total_bytes + 16;
+}
+
+template <int E, typename Tin>
+int launch_encode_t(const EncodeArgs &a, bool wht, cudaStream_t s)
+{
+    const int n_tiles = (a.n_tokens + kWarps - 1) / kWarps;
+    const long long blocks = (long long)n_tiles * a.nh;
+    if (blocks > 0x7fffffffLL) return sp_set_error(SP_ERR_ARG, "encode: too many vectors");
+    const size_t sm = encode_smem(32 * E, a.bl.total_bytes);
+    if (wht) {
+        auto k = k_encode<E, Tin, true>;
+        if (sm > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        k<<<(unsigned)blocks, kWarps * 32, sm, s>>>(a);
+    } else {
+        auto k = k_encode<E, Tin, false>;
+        if (sm > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        k<<<(unsigned)blocks, kWarps * 32, sm, s>>>(a);
+    }
+    return sp_check_cuda(cudaGetLastError(), "encode launch");
+}
+
+template <typename Tin>
+int launch_encode_dt(const EncodeArgs &a, bool wht, cudaStream_t s)
+{
+    switch (a.bl.n) {
+    case 32:  return launch_encode_t<1, Tin>(a, wht, s);
+    case 64:  return launch_encode_t<2, Tin>(a, wht, s);
+    case 128: return launch_encode_t<4, Tin>(a, wht, s);
+    case 256: return launch_encode_t<8, Tin>(a, wht, s);
+    case 512: return launch_encode_t<16, Tin>(a, wht, s);
+    default:
+        return sp_set_error(SP_ERR_UNSUPPORTED, "ship path: head_dim %d is not a power of two in [32,512]", a.bl.n);
+    }
+}
+
+template <int E>
+int launch_decode_t(const DecodeArgs &a, bool wht, cudaStream_t s)
+{
+    const int blocks = (a.n_pos + kWarps - 1) / kWarps;
+    const size_t sm = decode_smem(32 * E, a.bl.total_bytes);
+    if (wht) {
+        auto k = k_decode<E, true>;
+        if (sm > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        k<<<blocks, kWarps * 32, sm, s>>>(a);
+    } else {
+        auto k = k_decode<E, false>;
+        if (sm > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        k<<<blocks, kWarps * 32, sm, s>>>(a);
+    }
+    return sp_check_cuda(cudaGetLastError(), "decode launch");
+}
+
+}  // namespace
+
+// ------------------------------------------------------------ launchers --
+
+int sp_launch_encode(const void *d_in, int dtype, int n_tokens, int nh,
+                     uint8_t *d_out_base, long long slot0, long long slot_stride_bytes,
+                     int start_pos, const int *d_order, bool do_wht,
+                     const SpBandLayout &bl, cudaStream_t s)
+{
+    if (n_tokens == 0) return SP_OK;
+    if (!d_in || !d_out_base || n_tokens < 0 || nh <= 0)
+        return sp_set_error(SP_ERR_ARG, "encode: bad arguments");
+    EncodeArgs a;
+    a.in = d_in; a.out_base = d_out_base; a.slot0 = slot0; a.slot_stride = slot_stride_bytes;
+    a.n_tokens = n_tokens; a.nh = nh; a.start_pos = start_pos; a.order = d_order;
+    a.inv_sqrt_n = sp_inv_sqrt_n(bl.n); a.bl = bl;
+    switch (dtype) {
+    case SP_DTYPE_F32:  return launch_encode_dt<float>(a, do_wht, s);
+    case SP_DTYPE_F16:  return launch_encode_dt<__half>(a, do_wht, s);
+    case SP_DTYPE_BF16: return launch_encode_dt<__nv_bfloat16>(a, do_wht, s);
+    default: return sp_set_error(SP_ERR_ARG, "encode: unknown dtype %d", dtype);
+    }
+}
+
+int sp_launch_decode(const uint8_t *d_in_base, long long slot, long long slot_stride_bytes,
+                     int start_pos, int n_pos, float *d_out, const int *d_order,
+                     bool do_wht, int max_bands, const SpBandLayout &bl, cudaStream_t s)
+{
+    if (n_pos == 0) return SP_OK;
+    if (!d_in_base || !d_out || n_pos < 0)
+        return sp_set_error(SP_ERR_ARG, "decode: bad arguments");
+    DecodeArgs a;
+    a.in_base = d_in_base; a.slot = slot; a.slot_stride = slot_stride_bytes;
+    a.start_pos = start_pos; a.n_pos = n_pos; a.out = d_out; a.order = d_order;
+    a.inv_sqrt_n = sp_inv_sqrt_n(bl.n); a.max_bands = max_bands; a.bl = bl;
+    switch (bl.n) {
+    case 32:  return launch_decode_t<1>(a, do_wht, s);
+    case 64:  return launch_decode_t<2>(a, do_wht, s);
+    case 128: return launch_decode_t<4>(a, do_wht, s);
+    case 256: return launch_decode_t<8>(a, do_wht, s);
+    case 512: return launch_decode_t<16>(a, do_wht, s);
+    default:
+        return sp_set_error(SP_ERR_UNSUPPORTED, "ship path: head_dim %d is not a power of two in [32,512]", bl.n);
+    }
+}
+
+// In-place VHT2 of [n_vecs][n]: the encode kernel without quantisation is
+// not reusable here, so run a small dedicated warp-per-vector kernel.
+namespace {
+template <int E>
+__global__ void k_vht2_inplace(float *data, int n_vecs, float s)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long v = (long long)blockIdx.x * kWarps + warp;
+    if (v >= n_vecs) return;
+    float *p = data + v * (32 * E) + lane * E;
+    float x[E];
+#pragma unroll
+    for (int e = 0; e < E; e++) x[e] = p[e];
+    sp_warp_wht<E>(x, lane);
+#pragma unroll
+    for (int e = 0; e < E; e++) p[e] = __fmul_rn(x[e], s);
+}
+}  // namespace
+
+extern "C" {
+
+void sp_cuda_vht2_forward(float *d_data, int n, int n_vecs, void *stream)
+{
+    sp_clear_error();
+    if (!d_data || n_vecs < 0) { sp_set_error(SP_ERR_ARG, "vht2: bad arguments"); return; }
+    if (n_vecs == 0) return;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int blocks = (n_vecs + kWarps - 1) / kWarps;
+    const float sc = sp_inv_sqrt_n(n);
+    switch (n) {
+    case 32:  k_vht2_inplace<1><<<blocks, kWarps * 32, 0, s>>>(d_data, n_vecs, sc); break;
+    case 64:  k_vht2_inplace<2><<<blocks, kWarps * 32, 0, s>>>(d_data, n_vecs, sc); break;
+    case 128: k_vht2_inplace<4><<<blocks, kWarps * 32, 0, s>>>(d_data, n_vecs, sc); break;
+    case 256: k_vht2_inplace<8><<<blocks, kWarps * 32, 0, s>>>(d_data, n_vecs, sc); break;
+    case 512: k_vht2_inplace<16><<<blocks, kWarps * 32, 0, s>>>(d_data, n_vecs, sc); break;
+    default:
+        sp_set_error(SP_ERR_UNSUPPORTED, "vht2: n=%d is not a power of two in [32,512]", n);
+        return;
+    }
+    sp_check_cuda(cudaGetLastError(), "vht2 launch");
+}
+
+static void permute(float *d_data, const int *d_order, int n, int n_vecs, void *stream, bool inverse)
+{
+    sp_clear_error();
+    if (!d_data || !d_order || n <= 0 || n > SP_MAX_HEAD_DIM || n_vecs < 0) {
+        sp_set_error(SP_ERR_ARG, "mobius: bad arguments");
+        return;
+    }
+    if (n_vecs == 0) return;
+    const int blocks = (n_vecs + kWarps - 1) / kWarps;
+    const size_t sm = (size_t)kWarps * n * 4;
+    if (inverse) k_permute<true><<<blocks, kWarps * 32, sm, (cudaStream_t)stream>>>(d_data, d_order, n, n_vecs);
+    else k_permute<false><<<blocks, kWarps * 32, sm, (cudaStream_t)stream>>>(d_data, d_order, n, n_vecs);
+    sp_check_cuda(cudaGetLastError(), "mobius launch");
+}
+
+void sp_cuda_mobius_reorder(float *d_data, const int *d_order, int n, int n_vecs, void *stream)
+{
+    permute(d_data, d_order, n, n_vecs, stream, false);
+}
+
+void sp_cuda_mobius_unreorder(float *d_data, const int *d_order, int n, int n_vecs, void *stream)
+{
+    permute(d_data, d_order, n, n_vecs, stream, true);
+}
+
+void sp_cuda_band_quantize(const float *d_input, void *d_output, const sp_band_config_t *bc,
+                           int n_vecs, void *stream)
+{
+    sp_clear_error();
+    if (!bc) { sp_set_error(SP_ERR_ARG, "band_quantize: bc is NULL"); return; }
+    SpBandLayout bl = sp_layout_from(*bc);
+    sp_launch_encode(d_input, SP_DTYPE_F32, n_vecs, 1, (uint8_t *)d_output, 0, 0, 0,
+                     nullptr, false, bl, (cudaStream_t)stream);
+}
+
+void sp_cuda_band_dequantize(const void *d_input, float *d_output, const sp_band_config_t *bc,
+                             int n_vecs, void *stream)
+{
+    sp_clear_error();
+    if (!bc) { sp_set_error(SP_ERR_ARG, "band_dequantize: bc is NULL"); return; }
+    SpBandLayout bl = sp_layout_from(*bc);
+    sp_launch_decode((const uint8_t *)d_input, 0, 0, 0, n_vecs, d_output, nullptr, false, -1,
+                     bl, (cudaStream_t)stream);
+}
+
+}  // extern "C"
