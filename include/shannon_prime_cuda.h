@@ -144,6 +144,30 @@ int  sp_cuda_attn_decode(const sp_cuda_cache_t *cc, int layer0, int n_layers,
                          float logit_scale, void *d_out, int max_bands,
                          void *stream);
 
+/* New; no counterpart in the reference.  The fused decode above for callers
+ * that cannot allocate device memory (an engine that owns every device
+ * buffer through its own allocator, such as llama.cpp's ggml backend
+ * buffers, or a plugin host that forbids a library from growing its device
+ * footprint).  Same arguments and results as sp_cuda_attn_decode, but the
+ * cache is described by plain pointers the caller owns (layout as above:
+ * slot = layer * n_heads_kv + head, slot stride max_seq_len * total_bytes;
+ * d_mobius_order = head_dim ints on the device, or NULL for no reorder) and
+ * the split partials live in a fixed 16 MiB device array inside this
+ * library instead of a cudaMalloc'd workspace.  Nothing is allocated.
+ *   Limit: n_layers * n_q_heads * 128 * (head_dim + 4) * 4 bytes must fit in
+ *   16 MiB (at head_dim 128: n_layers * n_q_heads <= 248, e.g. one layer of a
+ *   32-head model per call); larger requests return SP_ERR_ARG.
+ *   The first call on each device looks up the array's device address
+ *   (cudaGetSymbolAddress); make it before any stream capture.  All calls
+ *   share the array, so calls that overlap on the GPU race: serialise them. */
+int  sp_cuda_attn_decode_noalloc(const void *d_k_cache, const void *d_v_cache,
+                                 int max_seq_len, const sp_band_config_t *k_bands,
+                                 const sp_band_config_t *v_bands,
+                                 const int *d_mobius_order, int n_heads_kv,
+                                 int layer0, int n_layers, const void *d_q,
+                                 int n_q_heads, int kv_len, float logit_scale,
+                                 void *d_out, int max_bands, void *stream);
+
 /* ----------------------------------------- kernel launchers (for tests) -- */
 
 /* Reference shannon_prime_cuda.h:116-134.  In-place VHT2 of n_vecs

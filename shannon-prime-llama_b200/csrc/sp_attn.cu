@@ -368,3 +368,144 @@ extern "C" int sp_cuda_attn_decode(const sp_cuda_cache_t *cc, int layer0, int n_
     }
     return sp_set_error(SP_ERR_UNSUPPORTED, "attn_decode: head_dim %d", n);
 }
+
+// ------------------------------------------------ allocation-free variant --
+//
+// Some callers cannot call cudaMalloc: an engine that owns all device
+// memory through its own allocator and hands the attention op only the
+// buffers it needs (llama.cpp's ggml backend buffers work this way), or a
+// plugin host that forbids a library from growing the process's device
+// footprint after start-up.  Such a caller keeps the compressed cache,
+// queries and outputs in memory it already owns, and has no
+// sp_cuda_cache_t workspace to offer.  sp_cuda_attn_decode_noalloc runs the
+// same fused decode with its split partials in the fixed device array below.
+//
+// The array is file-scope device memory: every GPU that loads this library
+// holds SP_ATTN_STATIC_SCRATCH_BYTES of it until the process exits.  In host
+// code its name is only a host-side stand-in, not a device address, so the
+// first call on each device looks the real address up with
+// cudaGetSymbolAddress (that device current) and keeps it; make that first
+// call before any stream capture.  Every call shares the array: a call
+// writes each partial it reads before reading it, so nothing has to start
+// at zero, but calls that overlap on the GPU (two streams, two threads)
+// race on it and must be serialised by the caller.
+
+#define SP_ATTN_STATIC_SCRATCH_BYTES (16u << 20)
+
+static __device__ __align__(256) unsigned char g_attn_static_scratch[SP_ATTN_STATIC_SCRATCH_BYTES];
+
+static void *g_static_ws_addr[128];       // per-device address, set once
+
+static int static_scratch_address(void **out)
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128)
+        return sp_set_error(SP_ERR_CUDA, "attn_decode_noalloc: no current CUDA device");
+    void *p = __atomic_load_n(&g_static_ws_addr[dev], __ATOMIC_ACQUIRE);
+    if (!p) {
+        cudaError_t e = cudaGetSymbolAddress(&p, g_attn_static_scratch);
+        if (e != cudaSuccess || !p)
+            return sp_set_error(SP_ERR_CUDA, "attn_decode_noalloc: cudaGetSymbolAddress: %s",
+                                cudaGetErrorString(e));
+        __atomic_store_n(&g_static_ws_addr[dev], p, __ATOMIC_RELEASE);
+    }
+    *out = p;
+    return SP_OK;
+}
+
+extern "C" int sp_cuda_attn_decode_noalloc(const void *d_k_cache, const void *d_v_cache,
+                                           int max_seq_len, const sp_band_config_t *k_bands,
+                                           const sp_band_config_t *v_bands,
+                                           const int *d_mobius_order, int n_heads_kv,
+                                           int layer0, int n_layers, const void *d_q,
+                                           int n_q_heads, int kv_len, float logit_scale,
+                                           void *d_out, int max_bands, void *stream)
+{
+    sp_clear_error();
+    if (!d_k_cache || !d_v_cache || !k_bands || !v_bands || !d_q || !d_out)
+        return sp_set_error(SP_ERR_ARG, "attn_decode_noalloc: NULL argument");
+    const int n = k_bands->head_dim;
+    if (v_bands->head_dim != n || n < 32 || n > SP_MAX_HEAD_DIM || (n & (n - 1)))
+        return sp_set_error(SP_ERR_UNSUPPORTED, "attn_decode_noalloc: head_dim %d", n);
+    if (max_seq_len <= 0 || n_heads_kv <= 0 || layer0 < 0 || n_layers <= 0)
+        return sp_set_error(SP_ERR_ARG, "attn_decode_noalloc: bad dims");
+    if (n_q_heads <= 0 || n_q_heads % n_heads_kv || n_q_heads / n_heads_kv > 8)
+        return sp_set_error(SP_ERR_ARG, "attn_decode_noalloc: n_q_heads %d must be a multiple of %d with <= 8 per KV head",
+                            n_q_heads, n_heads_kv);
+    if (kv_len < 0 || kv_len > max_seq_len)
+        return sp_set_error(SP_ERR_ARG, "attn_decode_noalloc: kv_len %d outside [0,%d]", kv_len, max_seq_len);
+    const unsigned long long need = (unsigned long long)n_layers * n_q_heads * kAttnMaxSplits *
+                                    sp_attn_partial_stride(n) * sizeof(float);
+    if (need > SP_ATTN_STATIC_SCRATCH_BYTES)
+        return sp_set_error(SP_ERR_ARG,
+                            "attn_decode_noalloc: n_layers*n_q_heads=%d needs %llu bytes of scratch, more than "
+                            "the fixed %u (at most %llu layer x q-head pairs at head_dim %d)",
+                            n_layers * n_q_heads, need, SP_ATTN_STATIC_SCRATCH_BYTES,
+                            (unsigned long long)SP_ATTN_STATIC_SCRATCH_BYTES /
+                                (kAttnMaxSplits * sp_attn_partial_stride(n) * sizeof(float)), n);
+    void *ws = nullptr;
+    int rc = static_scratch_address(&ws);
+    if (rc) return rc;
+
+    SpAttnArgs a;
+    memset(&a, 0, sizeof(a));
+    a.k_cache = (const uint8_t *)d_k_cache;
+    a.v_cache = (const uint8_t *)d_v_cache;
+    a.k_slot_stride = (long long)max_seq_len * k_bands->total_bytes;
+    a.v_slot_stride = (long long)max_seq_len * v_bands->total_bytes;
+    a.order = d_mobius_order;
+    a.q = (const __half *)d_q;
+    a.out = (__half *)d_out;
+    a.ws = (float *)ws;
+    a.layer0 = layer0; a.n_layers = n_layers; a.n_kv_heads = n_heads_kv;
+    a.n_q_heads = n_q_heads; a.group = n_q_heads / n_heads_kv;
+    a.kv_len = kv_len;
+    a.kl = sp_layout_from(*k_bands);
+    a.vl = sp_layout_from(*v_bands);
+    a.nb_k = (max_bands < 0 || max_bands >= a.kl.n_bands) ? a.kl.n_bands : max_bands;
+    a.nb_v = (max_bands < 0 || max_bands >= a.vl.n_bands) ? a.vl.n_bands : max_bands;
+    a.logit_scale = logit_scale;
+    a.inv_sqrt_n = sp_inv_sqrt_n(n);
+    a.status = nullptr;
+
+    // The tensor-core kernel stages 16-position tiles with bulk copies, which
+    // need 16-byte aligned tile starts; other layouts take the generic kernel.
+    const bool aligned = ((uintptr_t)d_k_cache % 16 == 0) && ((uintptr_t)d_v_cache % 16 == 0) &&
+                         (max_seq_len % 16 == 0);
+    const bool use_mma = aligned && g_force_impl != 1 && sp_attn_mma_supported(a) == SP_OK;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int units = n_layers * n_heads_kv;
+    const int target_ctas = use_mma ? 148 * 4 : 148 * 8;
+    int splits = (target_ctas + units - 1) / units;
+    const int max_by_len = (kv_len + kAttnMinChunk - 1) / kAttnMinChunk;
+    if (splits > max_by_len) splits = max_by_len;
+    if (splits > kAttnMaxSplits) splits = kAttnMaxSplits;
+    if (splits < 1) splits = 1;
+    int chunk = (kv_len + splits - 1) / splits;
+    chunk = (chunk + 15) & ~15;
+    if (chunk < 16) chunk = 16;
+    a.chunk = chunk;
+    a.n_splits = kv_len == 0 ? 0 : (kv_len + chunk - 1) / chunk;
+
+    if (a.n_splits > 0) {
+        if (use_mma) {
+            rc = sp_attn_mma_launch(a, s);
+        } else {
+            switch (n) {
+            case 32:  rc = launch_generic<1>(a, s); break;
+            case 64:  rc = launch_generic<2>(a, s); break;
+            case 128: rc = launch_generic<4>(a, s); break;
+            case 256: rc = launch_generic<8>(a, s); break;
+            default:  rc = launch_generic<16>(a, s); break;
+            }
+        }
+        if (rc) return rc;
+    }
+    switch (n) {
+    case 32:  return launch_combine<1>(a, s);
+    case 64:  return launch_combine<2>(a, s);
+    case 128: return launch_combine<4>(a, s);
+    case 256: return launch_combine<8>(a, s);
+    default:  return launch_combine<16>(a, s);
+    }
+}

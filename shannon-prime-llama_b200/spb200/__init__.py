@@ -93,6 +93,9 @@ SIGNATURES = {
     "sp_cuda_read_v_batch": (_V, [_CC, _I, _I, _I, _I, _P]),
     "sp_cuda_read_batch_partial": (_I, [_CC, _I, _I, _I, _I, _I, _P, _I]),
     "sp_cuda_attn_decode": (_I, [_CC, _I, _I, _P, _I, _I, _F, _P, _I, _P]),
+    "sp_cuda_attn_decode_noalloc": (_I, [_P, _P, _I, C.POINTER(SpBandConfig),
+                                         C.POINTER(SpBandConfig), _P, _I, _I, _I, _P, _I, _I,
+                                         _F, _P, _I, _P]),
     "sp_cuda_vht2_forward": (_V, [_P, _I, _I, _P]),
     "sp_cuda_mobius_reorder": (_V, [_P, _P, _I, _I, _P]),
     "sp_cuda_mobius_unreorder": (_V, [_P, _P, _I, _I, _P]),
