@@ -342,11 +342,11 @@ extern "C" int sp_cuda_attn_decode(const sp_cuda_cache_t *cc, int layer0, int n_
     int rc = SP_OK;
     const int n = cc->config.head_dim;
     g_prof_splits = a.n_splits;
+    if (use_mma && kv_len > 0)
+        return sp_attn_mma_launch(a, s, g_prof ? g_ev[0] : nullptr, g_prof ? g_ev[1] : nullptr);
     if (a.n_splits > 0) {
         if (g_prof) cudaEventRecord(g_ev[0], s);
-        if (use_mma) {
-            rc = sp_attn_mma_launch(a, s);
-        } else {
+        {
             switch (n) {
             case 32:  rc = launch_generic<1>(a, s); break;
             case 64:  rc = launch_generic<2>(a, s); break;
@@ -487,10 +487,9 @@ extern "C" int sp_cuda_attn_decode_noalloc(const void *d_k_cache, const void *d_
     a.chunk = chunk;
     a.n_splits = kv_len == 0 ? 0 : (kv_len + chunk - 1) / chunk;
 
+    if (use_mma && kv_len > 0) return sp_attn_mma_launch(a, s);
     if (a.n_splits > 0) {
-        if (use_mma) {
-            rc = sp_attn_mma_launch(a, s);
-        } else {
+        {
             switch (n) {
             case 32:  rc = launch_generic<1>(a, s); break;
             case 64:  rc = launch_generic<2>(a, s); break;

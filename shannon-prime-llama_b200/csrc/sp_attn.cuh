@@ -38,4 +38,7 @@ __device__ inline float *sp_attn_partial(const SpAttnArgs &a, int li, int qh, in
 // Tensor-core kernel for the ship layout (sp_attn_mma.cu).  Returns
 // SP_ERR_UNSUPPORTED (without launching) when the layout does not match.
 int sp_attn_mma_supported(const SpAttnArgs &a);
-int sp_attn_mma_launch(const SpAttnArgs &a, cudaStream_t s);
+// Launches the main kernel and its own segment combine.  ev_begin/ev_end
+// (optional) are recorded around the main kernel on stream s.
+int sp_attn_mma_launch(const SpAttnArgs &a, cudaStream_t s, cudaEvent_t ev_begin = nullptr,
+                       cudaEvent_t ev_end = nullptr);

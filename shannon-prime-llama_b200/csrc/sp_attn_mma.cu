@@ -1,7 +1,649 @@
-// sp_attn_mma.cu — tensor-core fused decode for the ship layout (placeholder
-// until the kernel lands: reports the layout as unsupported so the generic
-// kernel runs).
+// sp_attn_mma.cu — tensor-core fused decode attention for the ship layout
+// (head_dim 128, K bands 32/32/32/32 at 5/5/4/3 bits, V one 3-bit band,
+// up to 4 query heads per KV head).
+//
+// The attention is taken in the VHT2 coefficient domain, as in the generic
+// kernel (sp_attn.cu): score_t = sum_i q'[i] * c_t[i] with q' the
+// transformed, Möbius-permuted query, and the V sum accumulated on the
+// dequantised coefficients, transformed once per head at the end.
+//
+// Why tensor cores here: at 70% of HBM bandwidth a B200 SM receives one
+// 126-byte K+V row every ~7 clocks, i.e. ~28 warp-instruction issue slots
+// per row across its four schedulers.  A SIMT unpack + FMA loop needs
+// ~110 warp instructions per row (4 GQA FMAs per K element, 4 per V
+// element), so the decode would be issue-bound at ~25% of HBM.  Both
+// contractions are instead done with mma.sync.m16n8k16 (fp16 in, fp32
+// accumulate) straight from registers:
+//
+//   K side:  S[16 tokens][8] = codes_K[16 tokens][16 slots] x Bq[16][8]
+//            per band (two k-steps of 16 slots per 32-code band);
+//   V side:  O[16 coeffs][8] += codes_V[16 coeffs][16 tokens] x P[16][8]
+//
+// with the 8 columns = 4 query heads x {hi, lo} fp16 halves of an fp32
+// operand (q' for K, p*scale_v for V), so both operands carry ~22 bits.
+//
+// Unpacking without conversion instructions: a packed code u masked into
+// bits d..d+b-1 of a 16-bit half is the fp16 subnormal u * 2^(d-24),
+// exact, and the tensor cores take fp16 subnormals exactly.  So an
+// A-fragment register (two fp16) is one shift/funnel-shift plus one AND of
+// the packed row, with the 2^d of each slot folded into the B operand
+// (K side) or into the per-coefficient epilogue (V side).  Code pairs in
+// one register are chosen so both land in mantissa bits:
+//   K band of b bits, lane c owns codes 8c..8c+7, registers pair code j
+//   with code j+4 (same token); V registers pair one coefficient of two
+//   consecutive tokens (16-bit windows of both rows interleaved with prmt).
+//
+// Tiles of 16 tokens (K 1216 B, V 800 B, both multiples of 16 B and
+// 16-B aligned) are staged per warp by cp.async.bulk (the TMA engine)
+// into a 4-deep ring completed on mbarriers; every wait is bounded.
+//
+// Work split: the flattened (layer, KV head, tile) space is cut into equal
+// contiguous ranges, one per CTA (a single wave on the 148 SMs), so load
+// balance is exact to a tile; a CTA writes one partial per (layer, KV head)
+// segment it touches, and a combine kernel merges the segments.
 #include "sp_attn.cuh"
 
-int sp_attn_mma_supported(const SpAttnArgs &) { return SP_ERR_UNSUPPORTED; }
-int sp_attn_mma_launch(const SpAttnArgs &, cudaStream_t) { return SP_ERR_UNSUPPORTED; }
+#include <math.h>
+#include <string.h>
+
+namespace {
+
+constexpr int kWarps = 4;             // warps per CTA
+constexpr int kStages = 4;            // ring depth per warp
+constexpr int kKTile = 16 * 76;       // 1216
+constexpr int kVTile = 16 * 50;       // 800
+constexpr int kStageBytes = kKTile + kVTile;   // 2016
+constexpr int kN = 128;
+constexpr float kEmptyMax = -1.0e30f; // running max before the first valid token
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;   // 2 s per stage wait
+
+// Fixed ship layout (checked on the host against the cache's band config).
+// Bit position of band b's first code within a K row.
+__host__ __device__ constexpr int kKBit(int b) { return b == 0 ? 16 : b == 1 ? 192 : b == 2 ? 368 : 512; }
+__host__ __device__ constexpr int kKBits(int b) { return b < 2 ? 5 : (b == 2 ? 4 : 3); }
+// fp16 scale of band b: 32-bit word of the row holding it (low half for
+// bands 0 and 2, high half for bands 1 and 3).
+__host__ __device__ constexpr int kKScaleWord(int b) { return b == 0 ? 0 : b == 1 ? 5 : b == 2 ? 11 : 15; }
+
+// Pre-shift d (the code's value is u * 2^(d-24)) of the low / high code of
+// pair p of band b, as produced by the unpack sequence of k_attn_ship_mma.
+__host__ __device__ constexpr int pair_dlo(int b, int p)
+{
+    return b < 2 ? 0 : (b == 2 ? ((p & 1) ? 4 : 0) : ((p & 1) ? 7 : 4));
+}
+__host__ __device__ constexpr int pair_dhi(int b, int p)
+{
+    return b < 2 ? 4 : (b == 2 ? ((p & 1) ? 4 : 0) : ((p & 1) ? 3 : 0));
+}
+// Pre-shift of V code j of a lane's 16-code chunk (windows of 5 codes:
+// three masked in place at bits 0,3,6, two after a shift by 9).
+__host__ __device__ constexpr int vcode_d(int j)
+{
+    return j == 15 ? 0 : ((j % 5) < 3 ? 3 * (j % 5) : 3 * (j % 5 - 3));
+}
+
+struct Sched {
+    long long total_tiles;   // T = units * tiles_per_unit
+    int tiles_per_unit;      // ceil(kv_len / 16)
+    int n_ctas;              // N
+};
+
+__host__ __device__ inline long long tile_begin(long long i, const Sched &s)
+{
+    return i * s.total_tiles / s.n_ctas;
+}
+// Index of the CTA whose range holds tile g.
+__host__ __device__ inline int cta_of_tile(long long g, const Sched &s)
+{
+    return (int)(((g + 1) * s.n_ctas + s.total_tiles - 1) / s.total_tiles) - 1;
+}
+
+// ------------------------------------------------------------------ PTX --
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p)
+{
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar,
+                                         uint64_t policy)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1], %2, [%3], %4;" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t evict_first_policy()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1)
+{
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t shf(uint32_t lo, uint32_t hi, uint32_t s)
+{
+    return __funnelshift_r(lo, hi, s);
+}
+
+// fp16 bits of x (round to nearest even) and of the residual x - fp16(x):
+// the hi/lo split of an fp32 operand.
+__device__ __forceinline__ uint32_t split_hi_lo(float x)
+{
+    __half h = __float2half_rn(x);
+    __half l = __float2half_rn(x - __half2float(h));
+    return (uint32_t)__half_as_ushort(h) | ((uint32_t)__half_as_ushort(l) << 16);
+}
+
+// Zero the non-finite halves of a half2 (the reference zeroes a band whose
+// stored scale is not finite, shannon_prime_cuda.cu:236-245).
+__device__ __forceinline__ __half2 finite_or_zero(__half2 h)
+{
+    const unsigned m = __hle2_mask(__habs2(h), __float2half2_rn(65504.0f));
+    const unsigned v = *reinterpret_cast<unsigned *>(&h) & m;
+    return *reinterpret_cast<const __half2 *>(&v);
+}
+
+struct Smem {
+    unsigned char ring[kWarps][kStages][kStageBytes];
+    unsigned char pad[16];
+    unsigned long long bar[kWarps][kStages];
+    float q[4][kN];          // transformed, permuted, scaled queries
+    float qt[4][kN];         // scratch for the permutation
+    float qsum[4][4];        // per query, per band: sum of q'
+    float qmax[4];
+    float merge[kWarps][4][4 + kN];
+};
+
+// Bounded wait on a ring stage.  Returns false (and flags the status word)
+// if the copy did not land within the spin limit.
+__device__ __forceinline__ unsigned long long global_ns()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ bool wait_stage(uint32_t bar, uint32_t parity, unsigned int *status)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (;;) {
+        for (int i = 0; i < 64; i++)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (global_ns() - t0 > kWaitLimitNs) break;
+    }
+    if (status) atomicOr(status, 1u);
+    return false;
+}
+
+__global__ void __launch_bounds__(kWarps * 32, 4)
+k_attn_ship_mma(SpAttnArgs a, Sched sc)
+{
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = lane >> 2, c = lane & 3;
+    const int cta = blockIdx.x;
+    const long long g_begin = tile_begin(cta, sc), g_end = tile_begin(cta + 1, sc);
+    const int n_t = sc.tiles_per_unit;
+    const int G = a.group;
+    const int H = a.n_kv_heads;
+
+    // ---- per-warp ring --------------------------------------------------
+    const long long my_first = g_begin + warp;
+    const int n_my = my_first < g_end ? (int)((g_end - my_first + kWarps - 1) / kWarps) : 0;
+    const uint32_t bar0 = smem_u32(&sm.bar[warp][0]);
+    const uint32_t ring0 = smem_u32(&sm.ring[warp][0][0]);
+    uint64_t policy = 0;
+    if (lane == 0) {
+        for (int s = 0; s < kStages; s++) mbar_init(bar0 + 8 * s, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        policy = evict_first_policy();
+    }
+    __syncwarp();
+
+    auto issue = [&](int k) {
+        const long long g = my_first + (long long)k * kWarps;
+        const long long u = g / n_t;
+        const int tile = (int)(g - u * n_t);
+        const long long slot = (long long)(a.layer0 + (int)(u / H)) * H + (int)(u % H);
+        const uint8_t *ksrc = a.k_cache + slot * a.k_slot_stride + (long long)tile * kKTile;
+        const uint8_t *vsrc = a.v_cache + slot * a.v_slot_stride + (long long)tile * kVTile;
+        const int st = k % kStages;
+        const uint32_t bar = bar0 + 8 * st;
+        const uint32_t dst = ring0 + st * kStageBytes;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect_tx(bar, kStageBytes);
+        bulk_g2s(dst, ksrc, kKTile, bar, policy);
+        bulk_g2s(dst + kKTile, vsrc, kVTile, bar, policy);
+    };
+    if (lane == 0)
+        for (int k = 0; k < kStages && k < n_my; k++) issue(k);
+
+    // ---- lane constants ---------------------------------------------------
+    // K: window word and shift of lane c's chunk in each band.
+    int kw[4], ks[4];
+#pragma unroll
+    for (int b = 0; b < 4; b++) {
+        const int bit = kKBit(b) + 8 * c * kKBits(b);
+        kw[b] = bit >> 5;
+        ks[b] = bit & 31;
+    }
+    // V: lane r's 16-code chunk (bits 16+48r .. ) in row A (4-byte aligned
+    // pair base) and in row B (starting 400 bits later).
+    const int vbitA = 16 + 48 * r, vbitB = 416 + 48 * r;
+    const int vwA = vbitA >> 5, vsA = vbitA & 31, vwB = vbitB >> 5, vsB = vbitB & 31;
+    const uint32_t psel = (r & 1) ? 0x7632u : 0x5410u;
+    const int src0 = (2 * c) * 4 + (r >> 1), src1 = (2 * c + 1) * 4 + (r >> 1);
+
+    int k_next = 0;                     // next of my tiles to consume
+    long long seg_start = g_begin;
+    bool failed = false;
+    while (seg_start < g_end) {
+        const long long u = seg_start / n_t;
+        const long long seg_end = min(g_end, (u + 1) * (long long)n_t);
+        const int li = (int)(u / H), h = (int)(u % H);
+
+        // ---- queries of this (layer, KV head): q' = perm(H q) * scale ----
+        __syncthreads();
+        if (warp < G) {
+            const __half *qg = a.q + ((long long)li * a.n_q_heads + h * G + warp) * kN;
+            float x[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) x[e] = __half2float(qg[lane * 4 + e]);
+            sp_warp_wht<4>(x, lane);
+            const float sc_all = a.logit_scale * 1.4426950408889634f * a.inv_sqrt_n;
+#pragma unroll
+            for (int e = 0; e < 4; e++) sm.qt[warp][lane * 4 + e] = x[e] * sc_all;
+            __syncwarp();
+            float mx = 0.0f;
+            float bs = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int i = lane * 4 + e;
+                const float v = sm.qt[warp][a.order ? a.order[i] : i];
+                sm.q[warp][i] = v;
+                mx = fmaxf(mx, fabsf(v));
+                bs += v;
+            }
+            // lanes 8b..8b+7 hold band b
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) bs += __shfl_xor_sync(0xffffffffu, bs, o);
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            if ((lane & 7) == 0) sm.qsum[warp][lane >> 3] = bs;
+            if (lane == 0) sm.qmax[warp] = mx;
+        } else if (warp < 4) {
+            for (int i = lane; i < kN; i += 32) sm.q[warp][i] = 0.0f;
+            if (lane < 4) sm.qsum[warp][lane] = 0.0f;
+            if (lane == 0) sm.qmax[warp] = 0.0f;
+        }
+        __syncthreads();
+
+        // B fragments of the K side: lane (r, c) supplies column r = query
+        // r/2, fp16 part r%2, for the slots of lane group c.
+        uint32_t bq[8][2];
+        {
+            const int g = r >> 1;
+            const float qm = sm.qmax[g];
+            const int F = qm > 1e-30f ? 6 - ilogbf(qm) : 0;
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+#pragma unroll
+                for (int p = 0; p < 4; p++) {
+                    const int lo = 32 * b + 8 * c + p, hi = lo + 4;
+                    float vlo = ldexpf(sm.q[g][lo], F - pair_dlo(b, p));
+                    float vhi = ldexpf(sm.q[g][hi], F - pair_dhi(b, p));
+                    if (b >= a.nb_k) vlo = vhi = 0.0f;
+                    const uint32_t slo = split_hi_lo(vlo), shi = split_hi_lo(vhi);
+                    const uint32_t w = (r & 1) ? ((slo >> 16) | (shi & 0xffff0000u))
+                                               : ((slo & 0xffffu) | (shi << 16));
+                    bq[2 * b + (p >> 1)][p & 1] = w;
+                }
+            }
+        }
+        // Score constants for query c: S = sum_b s_b (acc_b * kc - mq_b).
+        float kc, mq[4];
+        {
+            const float qm = sm.qmax[c];
+            const int F = qm > 1e-30f ? 6 - ilogbf(qm) : 0;
+            kc = ldexpf(1.0f, 24 - F);
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                const float m_b = (float)((1 << (kKBits(b) - 1)) - 1);
+                mq[b] = b < a.nb_k ? m_b * sm.qsum[c][b] : 0.0f;
+            }
+        }
+
+        float oacc[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; i++) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.0f;
+        float m_run = kEmptyMax, l_sum = 0.0f, p_sum = 0.0f;
+
+        // ---- my tiles of this segment ------------------------------------
+        for (;; ++k_next) {
+            const long long g = my_first + (long long)k_next * kWarps;
+            if (k_next >= n_my || g >= seg_end) break;
+            const int st = k_next % kStages;
+            if (!failed && !wait_stage(bar0 + 8 * st, (k_next / kStages) & 1, a.status)) failed = true;
+            if (failed) break;
+            const unsigned char *kt = sm.ring[warp][st];
+            const uint32_t *K32 = reinterpret_cast<const uint32_t *>(kt);
+            const uint32_t *V32 = reinterpret_cast<const uint32_t *>(kt + kKTile);
+            const int tok0 = (int)(g - u * n_t) * 16;
+
+            // -- K: unpack codes of tokens r and r+8, 4 bands --
+            float acc[4][4];
+#pragma unroll
+            for (int b = 0; b < 4; b++) acc[b][0] = acc[b][1] = acc[b][2] = acc[b][3] = 0.0f;
+            uint32_t A[2][16];
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+                const uint32_t *row = K32 + 19 * (r + 8 * hh);
+#pragma unroll
+                for (int b = 0; b < 2; b++) {
+                    const uint32_t w0 = row[kw[b]], w1 = row[kw[b] + 1];
+                    const uint32_t xl = shf(w0, w1, ks[b]), xh = w1 >> ks[b];
+                    A[hh][4 * b + 0] = xl & 0x01F0001Fu;
+                    A[hh][4 * b + 1] = shf(xl, xh, 5) & 0x01F0001Fu;
+                    A[hh][4 * b + 2] = shf(xl, xh, 10) & 0x01F0001Fu;
+                    A[hh][4 * b + 3] = shf(xl, xh, 15) & 0x01F0001Fu;
+                }
+                {
+                    const uint32_t x = shf(row[kw[2]], row[kw[2] + 1], 16);
+                    const uint32_t y = x >> 8;
+                    A[hh][8] = x & 0x000F000Fu;
+                    A[hh][9] = x & 0x00F000F0u;
+                    A[hh][10] = y & 0x000F000Fu;
+                    A[hh][11] = y & 0x00F000F0u;
+                }
+                {
+                    const uint32_t x = shf(row[kw[3]], row[kw[3] + 1], ks[3]);
+                    const uint32_t y = x << 4, z = x >> 2;
+                    A[hh][12] = y & 0x00070070u;
+                    A[hh][13] = y & 0x00380380u;
+                    A[hh][14] = z & 0x00070070u;
+                    A[hh][15] = z & 0x00380380u;
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    mma16816(acc[b], A[0][4 * b + 2 * j], A[1][4 * b + 2 * j], A[0][4 * b + 2 * j + 1],
+                             A[1][4 * b + 2 * j + 1], bq[2 * b + j][0], bq[2 * b + j][1]);
+                }
+            }
+            // -- scores of tokens r, r+8 for query c (base-2 logits) --
+            float s[2];
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+                const uint32_t *row = K32 + 19 * (r + 8 * hh);
+                const __half2 s01 = finite_or_zero(__halves2half2(
+                    __ushort_as_half((unsigned short)(row[kKScaleWord(0)] & 0xffff)),
+                    __ushort_as_half((unsigned short)(row[kKScaleWord(1)] >> 16))));
+                const __half2 s23 = finite_or_zero(__halves2half2(
+                    __ushort_as_half((unsigned short)(row[kKScaleWord(2)] & 0xffff)),
+                    __ushort_as_half((unsigned short)(row[kKScaleWord(3)] >> 16))));
+                const float f0 = __low2float(s01), f1 = __high2float(s01);
+                const float f2 = __low2float(s23), f3 = __high2float(s23);
+                float sv = f0 * fmaf(acc[0][2 * hh] + acc[0][2 * hh + 1], kc, -mq[0]);
+                sv = fmaf(f1, fmaf(acc[1][2 * hh] + acc[1][2 * hh + 1], kc, -mq[1]), sv);
+                sv = fmaf(f2, fmaf(acc[2][2 * hh] + acc[2][2 * hh + 1], kc, -mq[2]), sv);
+                sv = fmaf(f3, fmaf(acc[3][2 * hh] + acc[3][2 * hh + 1], kc, -mq[3]), sv);
+                s[hh] = (tok0 + r + 8 * hh < a.kv_len) ? sv : -INFINITY;
+            }
+            // -- online softmax (rescale only when the running max grows) --
+            const float mx = fmaxf(s[0], s[1]);
+            if (__any_sync(0xffffffffu, mx > m_run)) {
+                float mt = mx;
+                mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+                mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+                mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+                const float m_new = fmaxf(m_run, mt);
+                const float alpha = exp2f(m_run - m_new);
+                m_run = m_new;
+                l_sum *= alpha;
+                p_sum *= alpha;
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    oacc[i][0] *= alpha; oacc[i][1] *= alpha;
+                    oacc[i][2] *= alpha; oacc[i][3] *= alpha;
+                }
+            }
+            float pv[2];
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+                const int t = r + 8 * hh;
+                const unsigned short vs_bits =
+                    *reinterpret_cast<const unsigned short *>(kt + kKTile + 50 * t);
+                const __half2 vs2 = finite_or_zero(__half2half2(__ushort_as_half(vs_bits)));
+                const float p = exp2f(s[hh] - m_run);
+                l_sum += p;
+                pv[hh] = p * __low2float(vs2);
+                p_sum += pv[hh];
+            }
+            // -- P' (hi/lo) into the B layout of the V product --
+            const uint32_t pk0 = split_hi_lo(pv[0]), pk1 = split_hi_lo(pv[1]);
+            const uint32_t x0 = __shfl_sync(0xffffffffu, pk0, src0);
+            const uint32_t x1 = __shfl_sync(0xffffffffu, pk0, src1);
+            const uint32_t x2 = __shfl_sync(0xffffffffu, pk1, src0);
+            const uint32_t x3 = __shfl_sync(0xffffffffu, pk1, src1);
+            const uint32_t pb0 = __byte_perm(x0, x1, psel), pb1 = __byte_perm(x2, x3, psel);
+
+            // -- V: unpack coefficient chunk of lane r for token pairs --
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+                const uint32_t *pr = V32 + 25 * (c + 4 * hh);
+                const uint32_t a0 = pr[vwA], a1 = pr[vwA + 1], b0 = pr[vwB], b1 = pr[vwB + 1];
+                const uint32_t xal = shf(a0, a1, vsA), xah = a1 >> vsA;
+                const uint32_t xbl = shf(b0, b1, vsB), xbh = b1 >> vsB;
+                uint32_t W[4];
+                W[0] = __byte_perm(xal, xbl, 0x5410);
+                W[1] = __byte_perm(shf(xal, xah, 15), shf(xbl, xbh, 15), 0x5410);
+                W[2] = __byte_perm(shf(xal, xah, 30), shf(xbl, xbh, 30), 0x5410);
+                W[3] = __byte_perm(xah, xbh, 0x5410) >> 13;
+#pragma unroll
+                for (int wi = 0; wi < 3; wi++) {
+                    const uint32_t t9 = W[wi] >> 9;
+                    A[hh][5 * wi + 0] = W[wi] & 0x00070007u;
+                    A[hh][5 * wi + 1] = W[wi] & 0x00380038u;
+                    A[hh][5 * wi + 2] = W[wi] & 0x01C001C0u;
+                    A[hh][5 * wi + 3] = t9 & 0x00070007u;
+                    A[hh][5 * wi + 4] = t9 & 0x00380038u;
+                }
+                A[hh][15] = W[3] & 0x00070007u;
+            }
+#pragma unroll
+            for (int mt = 0; mt < 8; mt++)
+                mma16816(oacc[mt], A[0][2 * mt], A[0][2 * mt + 1], A[1][2 * mt], A[1][2 * mt + 1], pb0, pb1);
+
+            __syncwarp();
+            if (lane == 0 && k_next + kStages < n_my) issue(k_next + kStages);
+        }
+
+        // ---- warp partial -> shared memory ---------------------------------
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            l_sum += __shfl_xor_sync(0xffffffffu, l_sum, o);
+            p_sum += __shfl_xor_sync(0xffffffffu, p_sum, o);
+        }
+        {
+            const float mv = 3.0f;   // V offset 2^(3-1)-1
+            float *mrow = sm.merge[warp][c];
+#pragma unroll
+            for (int mt = 0; mt < 8; mt++) {
+#pragma unroll
+                for (int rr = 0; rr < 2; rr++) {
+                    const int j = 2 * mt + rr;
+                    const float v = ldexpf(oacc[mt][2 * rr] + oacc[mt][2 * rr + 1], 24 - vcode_d(j));
+                    mrow[4 + 16 * r + j] = v - mv * p_sum;
+                }
+            }
+            if (r == 0) {
+                mrow[0] = m_run;
+                mrow[1] = l_sum;
+            }
+        }
+        __syncthreads();
+        // ---- CTA merge -> global partial of segment j of unit u ----------
+        {
+            const int seg = cta - cta_of_tile(u * (long long)n_t, sc);
+            for (int idx = threadIdx.x; idx < G * (kN + 1); idx += blockDim.x) {
+                const int g = idx / (kN + 1), i = idx % (kN + 1);
+                float M = kEmptyMax;
+#pragma unroll
+                for (int w = 0; w < kWarps; w++) M = fmaxf(M, sm.merge[w][g][0]);
+                float v = 0.0f;
+#pragma unroll
+                for (int w = 0; w < kWarps; w++) {
+                    const float wt = exp2f(sm.merge[w][g][0] - M);
+                    v += wt * (i < kN ? sm.merge[w][g][4 + i] : sm.merge[w][g][1]);
+                }
+                float *part = sp_attn_partial(a, li, h * G + g, seg);
+                if (i < kN) {
+                    part[4 + i] = v;
+                } else {
+                    part[0] = M;
+                    part[1] = v;
+                }
+            }
+        }
+        if (failed) break;
+        seg_start = seg_end;
+    }
+    // On a timed-out wait, wait (bounded) for this warp's copies in flight
+    // before the CTA's shared memory is released.
+    if (failed) {
+        for (int k = k_next; k < n_my && k < k_next + kStages; k++)
+            wait_stage(bar0 + 8 * (k % kStages), (k / kStages) & 1, nullptr);
+    }
+}
+
+// Merge the segment partials of one (layer, q head), transform, write fp16.
+__global__ void k_attn_combine_seg(SpAttnArgs a, Sched sc)
+{
+    const int lane = threadIdx.x & 31;
+    const int qh = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (qh >= a.n_q_heads) return;
+    const int li = blockIdx.y;
+    const long long u = (long long)li * a.n_kv_heads + qh / a.group;
+    const int i0 = cta_of_tile(u * sc.tiles_per_unit, sc);
+    const int i1 = cta_of_tile((u + 1) * sc.tiles_per_unit - 1, sc);
+    const int nseg = i1 - i0 + 1;
+    float M = kEmptyMax;
+    for (int s = 0; s < nseg; s++) M = fmaxf(M, sp_attn_partial(a, li, qh, s)[0]);
+    float x[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float L = 0.0f;
+    for (int s = 0; s < nseg; s++) {
+        const float *p = sp_attn_partial(a, li, qh, s);
+        const float w = exp2f(p[0] - M);
+        L += w * p[1];
+        const float4 v = *reinterpret_cast<const float4 *>(p + 4 + lane * 4);
+        x[0] += w * v.x; x[1] += w * v.y; x[2] += w * v.z; x[3] += w * v.w;
+    }
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+    sp_warp_wht<4>(x, lane);
+    __half *o = a.out + ((long long)li * a.n_q_heads + qh) * kN + lane * 4;
+    const __half2 h01 = __floats2half2_rn(x[0] * a.inv_sqrt_n * inv, x[1] * a.inv_sqrt_n * inv);
+    const __half2 h23 = __floats2half2_rn(x[2] * a.inv_sqrt_n * inv, x[3] * a.inv_sqrt_n * inv);
+    reinterpret_cast<__half2 *>(o)[0] = h01;
+    reinterpret_cast<__half2 *>(o)[1] = h23;
+}
+
+}  // namespace
+
+int sp_attn_mma_supported(const SpAttnArgs &a)
+{
+    if (a.kl.n != 128 || a.vl.n != 128) return SP_ERR_UNSUPPORTED;
+    if (a.kl.n_bands != 4 || a.vl.n_bands != 1) return SP_ERR_UNSUPPORTED;
+    for (int b = 0; b < 4; b++)
+        if (a.kl.size[b] != 32 || a.kl.bits[b] != kKBits(b) || a.kl.byte_off[b] * 8 + 16 != kKBit(b))
+            return SP_ERR_UNSUPPORTED;
+    if (a.kl.total_bytes != 76 || a.vl.total_bytes != 50 || a.vl.bits[0] != 3) return SP_ERR_UNSUPPORTED;
+    if (a.group < 1 || a.group > 4) return SP_ERR_UNSUPPORTED;
+    // Whole 16-position tiles must lie inside each slot.
+    const long long tiles = (a.kv_len + 15) / 16;
+    if (tiles * kKTile > a.k_slot_stride || tiles * kVTile > a.v_slot_stride) return SP_ERR_UNSUPPORTED;
+    if (a.nb_k < 1 || a.nb_v < 1) return SP_ERR_UNSUPPORTED;
+    // 16-byte aligned tile starts for the bulk copies.
+    if (((uintptr_t)a.k_cache & 15) || ((uintptr_t)a.v_cache & 15) || (a.k_slot_stride & 15) ||
+        (a.v_slot_stride & 15))
+        return SP_ERR_UNSUPPORTED;
+    return SP_OK;
+}
+
+int sp_attn_mma_launch(const SpAttnArgs &a_in, cudaStream_t s, cudaEvent_t ev_begin, cudaEvent_t ev_end)
+{
+    SpAttnArgs a = a_in;
+    const size_t smem = sizeof(Smem);
+    static int occ_cached = 0, sms_cached = 0, dev_cached = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev != dev_cached) {
+        if (cudaFuncSetAttribute(k_attn_ship_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+            return sp_check_cuda(cudaGetLastError(), "attention smem attribute");
+        int occ = 0, sms = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_attn_ship_mma, kWarps * 32, smem);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        occ_cached = occ > 0 ? occ : 1;
+        sms_cached = sms > 0 ? sms : 148;
+        dev_cached = dev;
+    }
+    const int units = a.n_layers * a.n_kv_heads;
+    Sched sc;
+    sc.tiles_per_unit = (a.kv_len + 15) / 16;
+    sc.total_tiles = (long long)units * sc.tiles_per_unit;
+    long long n = (long long)sms_cached * occ_cached;
+    if (n > sc.total_tiles) n = sc.total_tiles;
+    // At most kAttnMaxSplits segments per (layer, KV head): N/units + 2.
+    if (n > (long long)units * (kAttnMaxSplits - 2)) n = (long long)units * (kAttnMaxSplits - 2);
+    sc.n_ctas = (int)n;
+    a.n_splits = 0;
+    if (ev_begin) cudaEventRecord(ev_begin, s);
+    k_attn_ship_mma<<<sc.n_ctas, kWarps * 32, smem, s>>>(a, sc);
+    if (ev_end) cudaEventRecord(ev_end, s);
+    int rc = sp_check_cuda(cudaGetLastError(), "tensor-core attention launch");
+    if (rc) return rc;
+    const int per_block = 4;
+    dim3 grid((a.n_q_heads + per_block - 1) / per_block, a.n_layers);
+    k_attn_combine_seg<<<grid, per_block * 32, 0, s>>>(a, sc);
+    return sp_check_cuda(cudaGetLastError(), "tensor-core attention combine launch");
+}
