@@ -365,8 +365,8 @@ def run_ours(args):
         "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
         "dtype": "u8 codes -> f32 accumulate (fp16 q/out)",
         "data": "synthetic (seeded; K = RoPE(N(0,1) x LogNormal(0,0.5) per dim), V = N(0,1), q = N(0,1/sqrt(128)) fp16)",
-        "config": {"workload": "config 1: fused decode, 32 layers x 32 Q / 8 KV heads x hd 128, ctx 32768, batch 1, "
-                               "ship K 5/5/4/3 + V 3-bit",
+        "config": {"workload": "config 1: fused decode, %d layers x 32 Q / 8 KV heads x hd 128, ctx 32768, batch 1, "
+                               "ship K 5/5/4/3 + V 3-bit" % N_LAYERS,
                    "l2": "inputs larger than L2 (compressed cache %.2f GB per GPU)" % (cache_bytes / 1e9),
                    "parallelism": f"kv-head shards x{ws}" if ws > 1 else "single GPU",
                    "kv_heads_per_gpu": H, "splits": splits},
@@ -396,13 +396,18 @@ def run_ours(args):
 
 
 def main():
+    global N_LAYERS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--layers", type=int, default=N_LAYERS,
+                    help="layers in the cache (profiling aid: a smaller case for ncu; "
+                         "the headline number is the default, all 32)")
     args = ap.parse_args()
+    N_LAYERS = args.layers
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -156,6 +156,15 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// 2^x on the XU pipe (one MUFU op; rel. error ~2^-22, flushes subnormal
+// results, which are far below the softmax's resolution).
+__device__ __forceinline__ float fast_exp2(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ uint32_t shf(uint32_t lo, uint32_t hi, uint32_t s)
 {
     return __funnelshift_r(lo, hi, s);
@@ -188,6 +197,7 @@ struct Smem {
     float qsum[4][4];        // per query, per band: sum of q'
     float qmax[4];
     float merge[kWarps][4][4 + kN];
+    float scl[kWarps][16][8];   // per tile: K band scales 0..3, V scale (fp32)
 };
 
 // Bounded wait on a ring stage.  Returns false (and flags the status word)
@@ -238,13 +248,24 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
     }
     __syncwarp();
 
+    // Issue cursor (lane 0): (layer index, KV head, tile) of the next of my
+    // tiles to fetch, advanced by kWarps tiles per issue without division.
+    int ic_tile = 0, ic_h = 0, ic_li = 0;
+    if (lane == 0 && n_my > 0) {
+        const long long u0 = my_first / n_t;
+        ic_tile = (int)(my_first - u0 * n_t);
+        ic_h = (int)(u0 % H);
+        ic_li = (int)(u0 / H);
+    }
     auto issue = [&](int k) {
-        const long long g = my_first + (long long)k * kWarps;
-        const long long u = g / n_t;
-        const int tile = (int)(g - u * n_t);
-        const long long slot = (long long)(a.layer0 + (int)(u / H)) * H + (int)(u % H);
-        const uint8_t *ksrc = a.k_cache + slot * a.k_slot_stride + (long long)tile * kKTile;
-        const uint8_t *vsrc = a.v_cache + slot * a.v_slot_stride + (long long)tile * kVTile;
+        const long long slot = (long long)(a.layer0 + ic_li) * H + ic_h;
+        const uint8_t *ksrc = a.k_cache + slot * a.k_slot_stride + (long long)ic_tile * kKTile;
+        const uint8_t *vsrc = a.v_cache + slot * a.v_slot_stride + (long long)ic_tile * kVTile;
+        ic_tile += kWarps;
+        while (ic_tile >= n_t) {
+            ic_tile -= n_t;
+            if (++ic_h == H) { ic_h = 0; ++ic_li; }
+        }
         const int st = k % kStages;
         const uint32_t bar = bar0 + 8 * st;
         const uint32_t dst = ring0 + st * kStageBytes;
@@ -357,17 +378,32 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
         float m_run = kEmptyMax, l_sum = 0.0f, p_sum = 0.0f;
 
         // ---- my tiles of this segment ------------------------------------
-        for (;; ++k_next) {
-            const long long g = my_first + (long long)k_next * kWarps;
-            if (k_next >= n_my || g >= seg_end) break;
+        // Tile (within the unit) of my next tile; the segment ends when it
+        // passes the unit's last tile.
+        int ctile = (int)(my_first + (long long)k_next * kWarps - u * n_t);
+        for (; k_next < n_my && ctile < n_t; ++k_next, ctile += kWarps) {
             const int st = k_next % kStages;
             if (!failed && !wait_stage(bar0 + 8 * st, (k_next / kStages) & 1, a.status)) failed = true;
             if (failed) break;
             const unsigned char *kt = sm.ring[warp][st];
             const uint32_t *K32 = reinterpret_cast<const uint32_t *>(kt);
             const uint32_t *V32 = reinterpret_cast<const uint32_t *>(kt + kKTile);
-            const int tok0 = (int)(g - u * n_t) * 16;
+            const int tok0 = ctile * 16;
 
+            // -- band scales of the tile to fp32, once per token: lane t<16
+            //    takes K bands 0,1 of token t, lane 16+t bands 2,3; every
+            //    lane converts the V scale of token t&15 --
+            {
+                const int t = lane & 15, hi = lane >> 4;
+                const uint32_t *row = K32 + 19 * t;
+                const uint32_t wa = row[hi ? kKScaleWord(2) : kKScaleWord(0)];
+                const uint32_t wb = row[hi ? kKScaleWord(3) : kKScaleWord(1)];
+                const uint32_t hw = __byte_perm(wa, wb, 0x7610);
+                const float2 f = __half22float2(finite_or_zero(*reinterpret_cast<const __half2 *>(&hw)));
+                *reinterpret_cast<float2 *>(&sm.scl[warp][t][2 * hi]) = f;
+                const unsigned short vb = *reinterpret_cast<const unsigned short *>(kt + kKTile + 50 * t);
+                sm.scl[warp][t][4] = __low2float(finite_or_zero(__half2half2(__ushort_as_half(vb))));
+            }
             // -- K: unpack codes of tokens r and r+8, 4 bands --
             float acc[4][4];
 #pragma unroll
@@ -411,23 +447,21 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
                 }
             }
             // -- scores of tokens r, r+8 for query c (base-2 logits) --
-            float s[2];
+            __syncwarp();
+            float s[2], vscale[2];
 #pragma unroll
             for (int hh = 0; hh < 2; hh++) {
-                const uint32_t *row = K32 + 19 * (r + 8 * hh);
-                const __half2 s01 = finite_or_zero(__halves2half2(
-                    __ushort_as_half((unsigned short)(row[kKScaleWord(0)] & 0xffff)),
-                    __ushort_as_half((unsigned short)(row[kKScaleWord(1)] >> 16))));
-                const __half2 s23 = finite_or_zero(__halves2half2(
-                    __ushort_as_half((unsigned short)(row[kKScaleWord(2)] & 0xffff)),
-                    __ushort_as_half((unsigned short)(row[kKScaleWord(3)] >> 16))));
-                const float f0 = __low2float(s01), f1 = __high2float(s01);
-                const float f2 = __low2float(s23), f3 = __high2float(s23);
-                float sv = f0 * fmaf(acc[0][2 * hh] + acc[0][2 * hh + 1], kc, -mq[0]);
-                sv = fmaf(f1, fmaf(acc[1][2 * hh] + acc[1][2 * hh + 1], kc, -mq[1]), sv);
-                sv = fmaf(f2, fmaf(acc[2][2 * hh] + acc[2][2 * hh + 1], kc, -mq[2]), sv);
-                sv = fmaf(f3, fmaf(acc[3][2 * hh] + acc[3][2 * hh + 1], kc, -mq[3]), sv);
-                s[hh] = (tok0 + r + 8 * hh < a.kv_len) ? sv : -INFINITY;
+                const float4 f = *reinterpret_cast<const float4 *>(&sm.scl[warp][r + 8 * hh][0]);
+                vscale[hh] = sm.scl[warp][r + 8 * hh][4];
+                float sv = f.x * fmaf(acc[0][2 * hh] + acc[0][2 * hh + 1], kc, -mq[0]);
+                sv = fmaf(f.y, fmaf(acc[1][2 * hh] + acc[1][2 * hh + 1], kc, -mq[1]), sv);
+                sv = fmaf(f.z, fmaf(acc[2][2 * hh] + acc[2][2 * hh + 1], kc, -mq[2]), sv);
+                sv = fmaf(f.w, fmaf(acc[3][2 * hh] + acc[3][2 * hh + 1], kc, -mq[3]), sv);
+                s[hh] = sv;
+            }
+            if (tok0 + 16 > a.kv_len) {       // last, partial tile of the unit
+                if (tok0 + r >= a.kv_len) s[0] = -INFINITY;
+                if (tok0 + r + 8 >= a.kv_len) s[1] = -INFINITY;
             }
             // -- online softmax (rescale only when the running max grows) --
             const float mx = fmaxf(s[0], s[1]);
@@ -437,7 +471,7 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
                 mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
                 mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
                 const float m_new = fmaxf(m_run, mt);
-                const float alpha = exp2f(m_run - m_new);
+                const float alpha = fast_exp2(m_run - m_new);
                 m_run = m_new;
                 l_sum *= alpha;
                 p_sum *= alpha;
@@ -450,17 +484,22 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
             float pv[2];
 #pragma unroll
             for (int hh = 0; hh < 2; hh++) {
-                const int t = r + 8 * hh;
-                const unsigned short vs_bits =
-                    *reinterpret_cast<const unsigned short *>(kt + kKTile + 50 * t);
-                const __half2 vs2 = finite_or_zero(__half2half2(__ushort_as_half(vs_bits)));
-                const float p = exp2f(s[hh] - m_run);
+                const float p = fast_exp2(s[hh] - m_run);
                 l_sum += p;
-                pv[hh] = p * __low2float(vs2);
+                pv[hh] = p * vscale[hh];
                 p_sum += pv[hh];
             }
             // -- P' (hi/lo) into the B layout of the V product --
-            const uint32_t pk0 = split_hi_lo(pv[0]), pk1 = split_hi_lo(pv[1]);
+            uint32_t pk0, pk1;
+            {
+                const __half2 hi2 = __floats2half2_rn(pv[0], pv[1]);
+                const float2 back = __half22float2(hi2);
+                const __half2 lo2 = __floats2half2_rn(pv[0] - back.x, pv[1] - back.y);
+                const uint32_t hb = *reinterpret_cast<const uint32_t *>(&hi2);
+                const uint32_t lb = *reinterpret_cast<const uint32_t *>(&lo2);
+                pk0 = __byte_perm(hb, lb, 0x5410);
+                pk1 = __byte_perm(hb, lb, 0x7632);
+            }
             const uint32_t x0 = __shfl_sync(0xffffffffu, pk0, src0);
             const uint32_t x1 = __shfl_sync(0xffffffffu, pk0, src1);
             const uint32_t x2 = __shfl_sync(0xffffffffu, pk1, src0);
