@@ -44,12 +44,11 @@
 #include "sp_attn.cuh"
 
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 
 namespace {
 
-constexpr int kWarps = 4;             // warps per CTA
-constexpr int kStages = 4;            // ring depth per warp
 constexpr int kKTile = 16 * 76;       // 1216
 constexpr int kVTile = 16 * 50;       // 800
 constexpr int kStageBytes = kKTile + kVTile;   // 2016
@@ -188,6 +187,7 @@ __device__ __forceinline__ __half2 finite_or_zero(__half2 h)
     return *reinterpret_cast<const __half2 *>(&v);
 }
 
+template <int kWarps, int kStages>
 struct Smem {
     unsigned char ring[kWarps][kStages][kStageBytes];
     unsigned char pad[16];
@@ -222,11 +222,15 @@ __device__ __forceinline__ bool wait_stage(uint32_t bar, uint32_t parity, unsign
     return false;
 }
 
-__global__ void __launch_bounds__(kWarps * 32, 4)
+// kWarps warps per CTA, a kStages-deep copy ring per warp, kMinBlocks CTAs
+// per SM requested from the register allocator.
+template <int kWarps, int kStages, int kMinBlocks>
+__global__ void __launch_bounds__(kWarps * 32, kMinBlocks)
 k_attn_ship_mma(SpAttnArgs a, Sched sc)
 {
+    static_assert(kWarps >= 4, "query preparation uses one warp per GQA query (up to 4)");
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
+    Smem<kWarps, kStages> &sm = *reinterpret_cast<Smem<kWarps, kStages> *>(smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r = lane >> 2, c = lane & 3;
     const int cta = blockIdx.x;
@@ -359,8 +363,9 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
                 }
             }
         }
-        // Score constants for query c: S = sum_b s_b (acc_b * kc - mq_b).
-        float kc, mq[4];
+        // Score constants for query c: s = kc * sum_b s_b (acc_b + cinit_b),
+        // cinit_b = -m_b * sum_{i in b} q'_i / kc.
+        float kc, cinit[4];
         {
             const float qm = sm.qmax[c];
             const int F = qm > 1e-30f ? 6 - ilogbf(qm) : 0;
@@ -368,14 +373,16 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
 #pragma unroll
             for (int b = 0; b < 4; b++) {
                 const float m_b = (float)((1 << (kKBits(b) - 1)) - 1);
-                mq[b] = b < a.nb_k ? m_b * sm.qsum[c][b] : 0.0f;
+                cinit[b] = b < a.nb_k ? -ldexpf(m_b * sm.qsum[c][b], F - 24) : 0.0f;
             }
         }
 
         float oacc[8][4];
 #pragma unroll
         for (int i = 0; i < 8; i++) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.0f;
-        float m_run = kEmptyMax, l_sum = 0.0f, p_sum = 0.0f;
+        // Running max of the scores in units of 1/kc (kc > 0, so it orders
+        // like the base-2 logits); nkm = -kc * m_run.
+        float m_run = kEmptyMax, nkm = 0.0f, l_sum = 0.0f, p_sum = 0.0f;
 
         // ---- my tiles of this segment ------------------------------------
         // Tile (within the unit) of my next tile; the segment ends when it
@@ -404,11 +411,9 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
                 const unsigned short vb = *reinterpret_cast<const unsigned short *>(kt + kKTile + 50 * t);
                 sm.scl[warp][t][4] = __low2float(finite_or_zero(__half2half2(__ushort_as_half(vb))));
             }
-            // -- K: unpack codes of tokens r and r+8, 4 bands --
-            float acc[4][4];
-#pragma unroll
-            for (int b = 0; b < 4; b++) acc[b][0] = acc[b][1] = acc[b][2] = acc[b][3] = 0.0f;
-            uint32_t A[2][16];
+
+            // -- K: unpack the codes of tokens r and r+8 (4 bands) --
+            uint32_t AK[2][16];
 #pragma unroll
             for (int hh = 0; hh < 2; hh++) {
                 const uint32_t *row = K32 + 19 * (r + 8 * hh);
@@ -416,63 +421,95 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
                 for (int b = 0; b < 2; b++) {
                     const uint32_t w0 = row[kw[b]], w1 = row[kw[b] + 1];
                     const uint32_t xl = shf(w0, w1, ks[b]), xh = w1 >> ks[b];
-                    A[hh][4 * b + 0] = xl & 0x01F0001Fu;
-                    A[hh][4 * b + 1] = shf(xl, xh, 5) & 0x01F0001Fu;
-                    A[hh][4 * b + 2] = shf(xl, xh, 10) & 0x01F0001Fu;
-                    A[hh][4 * b + 3] = shf(xl, xh, 15) & 0x01F0001Fu;
+                    AK[hh][4 * b + 0] = xl & 0x01F0001Fu;
+                    AK[hh][4 * b + 1] = shf(xl, xh, 5) & 0x01F0001Fu;
+                    AK[hh][4 * b + 2] = shf(xl, xh, 10) & 0x01F0001Fu;
+                    AK[hh][4 * b + 3] = shf(xl, xh, 15) & 0x01F0001Fu;
                 }
                 {
                     const uint32_t x = shf(row[kw[2]], row[kw[2] + 1], 16);
                     const uint32_t y = x >> 8;
-                    A[hh][8] = x & 0x000F000Fu;
-                    A[hh][9] = x & 0x00F000F0u;
-                    A[hh][10] = y & 0x000F000Fu;
-                    A[hh][11] = y & 0x00F000F0u;
+                    AK[hh][8] = x & 0x000F000Fu;
+                    AK[hh][9] = x & 0x00F000F0u;
+                    AK[hh][10] = y & 0x000F000Fu;
+                    AK[hh][11] = y & 0x00F000F0u;
                 }
                 {
                     const uint32_t x = shf(row[kw[3]], row[kw[3] + 1], ks[3]);
                     const uint32_t y = x << 4, z = x >> 2;
-                    A[hh][12] = y & 0x00070070u;
-                    A[hh][13] = y & 0x00380380u;
-                    A[hh][14] = z & 0x00070070u;
-                    A[hh][15] = z & 0x00380380u;
+                    AK[hh][12] = y & 0x00070070u;
+                    AK[hh][13] = y & 0x00380380u;
+                    AK[hh][14] = z & 0x00070070u;
+                    AK[hh][15] = z & 0x00380380u;
                 }
             }
+            // Band dot products; the accumulator starts at -m_b * sum(q') in
+            // its hi column, so acc_hi + acc_lo = sum_i (u_i - m_b) q'_i / kc.
+            float acc[4][4];
 #pragma unroll
             for (int b = 0; b < 4; b++) {
+                acc[b][0] = cinit[b]; acc[b][1] = 0.0f; acc[b][2] = cinit[b]; acc[b][3] = 0.0f;
 #pragma unroll
-                for (int j = 0; j < 2; j++) {
-                    mma16816(acc[b], A[0][4 * b + 2 * j], A[1][4 * b + 2 * j], A[0][4 * b + 2 * j + 1],
-                             A[1][4 * b + 2 * j + 1], bq[2 * b + j][0], bq[2 * b + j][1]);
-                }
+                for (int j = 0; j < 2; j++)
+                    mma16816(acc[b], AK[0][4 * b + 2 * j], AK[1][4 * b + 2 * j], AK[0][4 * b + 2 * j + 1],
+                             AK[1][4 * b + 2 * j + 1], bq[2 * b + j][0], bq[2 * b + j][1]);
             }
-            // -- scores of tokens r, r+8 for query c (base-2 logits) --
+
+            // -- V: unpack lane r's 16-coefficient chunk of token pairs
+            //    (2c, 2c+1) and (2c+8, 2c+9); independent of the softmax, so
+            //    issued before it --
+            uint32_t AV[2][16];
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+                const uint32_t *pr = V32 + 25 * (c + 4 * hh);
+                const uint32_t a0 = pr[vwA], a1 = pr[vwA + 1], b0 = pr[vwB], b1 = pr[vwB + 1];
+                const uint32_t xal = shf(a0, a1, vsA), xah = a1 >> vsA;
+                const uint32_t xbl = shf(b0, b1, vsB), xbh = b1 >> vsB;
+                uint32_t W[4];
+                W[0] = __byte_perm(xal, xbl, 0x5410);
+                W[1] = __byte_perm(shf(xal, xah, 15), shf(xbl, xbh, 15), 0x5410);
+                W[2] = __byte_perm(shf(xal, xah, 30), shf(xbl, xbh, 30), 0x5410);
+                W[3] = __byte_perm(xah, xbh, 0x5410) >> 13;
+#pragma unroll
+                for (int wi = 0; wi < 3; wi++) {
+                    const uint32_t t9 = W[wi] >> 9;
+                    AV[hh][5 * wi + 0] = W[wi] & 0x00070007u;
+                    AV[hh][5 * wi + 1] = W[wi] & 0x00380038u;
+                    AV[hh][5 * wi + 2] = W[wi] & 0x01C001C0u;
+                    AV[hh][5 * wi + 3] = t9 & 0x00070007u;
+                    AV[hh][5 * wi + 4] = t9 & 0x00380038u;
+                }
+                AV[hh][15] = W[3] & 0x00070007u;
+            }
+
+            // -- scores of tokens r, r+8 for query c, in units of 1/kc --
             __syncwarp();
-            float s[2], vscale[2];
+            float su[2], vscale[2];
 #pragma unroll
             for (int hh = 0; hh < 2; hh++) {
                 const float4 f = *reinterpret_cast<const float4 *>(&sm.scl[warp][r + 8 * hh][0]);
                 vscale[hh] = sm.scl[warp][r + 8 * hh][4];
-                float sv = f.x * fmaf(acc[0][2 * hh] + acc[0][2 * hh + 1], kc, -mq[0]);
-                sv = fmaf(f.y, fmaf(acc[1][2 * hh] + acc[1][2 * hh + 1], kc, -mq[1]), sv);
-                sv = fmaf(f.z, fmaf(acc[2][2 * hh] + acc[2][2 * hh + 1], kc, -mq[2]), sv);
-                sv = fmaf(f.w, fmaf(acc[3][2 * hh] + acc[3][2 * hh + 1], kc, -mq[3]), sv);
-                s[hh] = sv;
+                float v = f.x * (acc[0][2 * hh] + acc[0][2 * hh + 1]);
+                v = fmaf(f.y, acc[1][2 * hh] + acc[1][2 * hh + 1], v);
+                v = fmaf(f.z, acc[2][2 * hh] + acc[2][2 * hh + 1], v);
+                v = fmaf(f.w, acc[3][2 * hh] + acc[3][2 * hh + 1], v);
+                su[hh] = v;
             }
             if (tok0 + 16 > a.kv_len) {       // last, partial tile of the unit
-                if (tok0 + r >= a.kv_len) s[0] = -INFINITY;
-                if (tok0 + r + 8 >= a.kv_len) s[1] = -INFINITY;
+                if (tok0 + r >= a.kv_len) su[0] = -INFINITY;
+                if (tok0 + r + 8 >= a.kv_len) su[1] = -INFINITY;
             }
             // -- online softmax (rescale only when the running max grows) --
-            const float mx = fmaxf(s[0], s[1]);
+            const float mx = fmaxf(su[0], su[1]);
             if (__any_sync(0xffffffffu, mx > m_run)) {
                 float mt = mx;
                 mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
                 mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
                 mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
                 const float m_new = fmaxf(m_run, mt);
-                const float alpha = fast_exp2(m_run - m_new);
+                const float alpha = fast_exp2(kc * (m_run - m_new));
                 m_run = m_new;
+                nkm = -kc * m_new;
                 l_sum *= alpha;
                 p_sum *= alpha;
 #pragma unroll
@@ -484,7 +521,7 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
             float pv[2];
 #pragma unroll
             for (int hh = 0; hh < 2; hh++) {
-                const float p = fast_exp2(s[hh] - m_run);
+                const float p = fast_exp2(fmaf(kc, su[hh], nkm));
                 l_sum += p;
                 pv[hh] = p * vscale[hh];
                 p_sum += pv[hh];
@@ -505,33 +542,9 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
             const uint32_t x2 = __shfl_sync(0xffffffffu, pk1, src0);
             const uint32_t x3 = __shfl_sync(0xffffffffu, pk1, src1);
             const uint32_t pb0 = __byte_perm(x0, x1, psel), pb1 = __byte_perm(x2, x3, psel);
-
-            // -- V: unpack coefficient chunk of lane r for token pairs --
-#pragma unroll
-            for (int hh = 0; hh < 2; hh++) {
-                const uint32_t *pr = V32 + 25 * (c + 4 * hh);
-                const uint32_t a0 = pr[vwA], a1 = pr[vwA + 1], b0 = pr[vwB], b1 = pr[vwB + 1];
-                const uint32_t xal = shf(a0, a1, vsA), xah = a1 >> vsA;
-                const uint32_t xbl = shf(b0, b1, vsB), xbh = b1 >> vsB;
-                uint32_t W[4];
-                W[0] = __byte_perm(xal, xbl, 0x5410);
-                W[1] = __byte_perm(shf(xal, xah, 15), shf(xbl, xbh, 15), 0x5410);
-                W[2] = __byte_perm(shf(xal, xah, 30), shf(xbl, xbh, 30), 0x5410);
-                W[3] = __byte_perm(xah, xbh, 0x5410) >> 13;
-#pragma unroll
-                for (int wi = 0; wi < 3; wi++) {
-                    const uint32_t t9 = W[wi] >> 9;
-                    A[hh][5 * wi + 0] = W[wi] & 0x00070007u;
-                    A[hh][5 * wi + 1] = W[wi] & 0x00380038u;
-                    A[hh][5 * wi + 2] = W[wi] & 0x01C001C0u;
-                    A[hh][5 * wi + 3] = t9 & 0x00070007u;
-                    A[hh][5 * wi + 4] = t9 & 0x00380038u;
-                }
-                A[hh][15] = W[3] & 0x00070007u;
-            }
 #pragma unroll
             for (int mt = 0; mt < 8; mt++)
-                mma16816(oacc[mt], A[0][2 * mt], A[0][2 * mt + 1], A[1][2 * mt], A[1][2 * mt + 1], pb0, pb1);
+                mma16816(oacc[mt], AV[0][2 * mt], AV[0][2 * mt + 1], AV[1][2 * mt], AV[1][2 * mt + 1], pb0, pb1);
 
             __syncwarp();
             if (lane == 0 && k_next + kStages < n_my) issue(k_next + kStages);
@@ -556,7 +569,7 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
                 }
             }
             if (r == 0) {
-                mrow[0] = m_run;
+                mrow[0] = fmaxf(kc * m_run, kEmptyMax);   // base-2 logit units
                 mrow[1] = l_sum;
             }
         }
@@ -648,19 +661,28 @@ int sp_attn_mma_supported(const SpAttnArgs &a)
     return SP_OK;
 }
 
+// Launch configuration: 4 warps per CTA, a 4-deep ring per warp, and 3
+// CTAs per SM (12 warps, up to 168 registers per thread).  Measured on
+// config 1: 4/4/4 (16 warps, 127 registers) and 8/4/2 run within 1-2% of
+// it; configurations that force fewer registers spill and run slower, and
+// deeper rings gain nothing (a ring of 4 already sustains the copy stream
+// at the HBM rate when the compute is removed).
+constexpr int kCtaWarps = 4, kRingStages = 4, kCtasPerSm = 3;
+
 int sp_attn_mma_launch(const SpAttnArgs &a_in, cudaStream_t s, cudaEvent_t ev_begin, cudaEvent_t ev_end)
 {
     SpAttnArgs a = a_in;
-    const size_t smem = sizeof(Smem);
+    auto kernel = k_attn_ship_mma<kCtaWarps, kRingStages, kCtasPerSm>;
+    const size_t smem = sizeof(Smem<kCtaWarps, kRingStages>);
+    const int threads = kCtaWarps * 32;
     static int occ_cached = 0, sms_cached = 0, dev_cached = -1;
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev != dev_cached) {
-        if (cudaFuncSetAttribute(k_attn_ship_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-            cudaSuccess)
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return sp_check_cuda(cudaGetLastError(), "attention smem attribute");
         int occ = 0, sms = 0;
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_attn_ship_mma, kWarps * 32, smem);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, smem);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         occ_cached = occ > 0 ? occ : 1;
         sms_cached = sms > 0 ? sms : 148;
@@ -677,7 +699,7 @@ int sp_attn_mma_launch(const SpAttnArgs &a_in, cudaStream_t s, cudaEvent_t ev_be
     sc.n_ctas = (int)n;
     a.n_splits = 0;
     if (ev_begin) cudaEventRecord(ev_begin, s);
-    k_attn_ship_mma<<<sc.n_ctas, kWarps * 32, smem, s>>>(a, sc);
+    kernel<<<sc.n_ctas, threads, smem, s>>>(a, sc);
     if (ev_end) cudaEventRecord(ev_end, s);
     int rc = sp_check_cuda(cudaGetLastError(), "tensor-core attention launch");
     if (rc) return rc;
