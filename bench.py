@@ -233,6 +233,7 @@ def run_ours(args):
 
     # Fill the cache: per layer, synthetic K/V for this rank's heads.
     gen = torch.Generator(device=dev)
+    kept = []                  # inputs of 4 layers (1.07 GB fp32) for the compress timing
     t_fill = time.perf_counter()
     for layer in range(N_LAYERS):
         gen.manual_seed(SEED * 1000003 + layer)
@@ -241,8 +242,8 @@ def run_ours(args):
         v = v[:, heads].contiguous()
         rc = L.sp_cuda_write_kv_tokens(cc, layer, 0, CTX, k.data_ptr(), v.data_ptr(), 0)
         spb200.check(rc, "write_kv_tokens")
-        if layer == 0:
-            k0, v0 = k, v
+        if layer < 4:
+            kept.append((layer, k, v))
     torch.cuda.synchronize()
     t_fill = time.perf_counter() - t_fill
 
@@ -330,18 +331,22 @@ def run_ours(args):
     h2d = hq.numel() * 2 + (out.numel() * 2 if ws > 1 else 0)
     d2h = hout.numel() * 2 * (ws if ws > 1 else 1)
 
-    # Ship-path compression throughput on one full layer (K and V, fp32).
-    for _ in range(3):
-        L.sp_cuda_write_kv_tokens(cc, 0, 0, CTX, k0.data_ptr(), v0.data_ptr(), 0)
+    # Ship-path compression throughput: re-compress 4 full layers (K and V,
+    # fp32 in, 1.07 GB of inputs > L2) through the token-major entry point.
+    def compress_pass():
+        for layer, kk, vv in kept:
+            L.sp_cuda_write_kv_tokens(cc, layer, 0, CTX, kk.data_ptr(), vv.data_ptr(), 0)
+    for _ in range(2):
+        compress_pass()
     barrier()
     c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 10
+    reps = 5
     c0.record(stream)
     for _ in range(reps):
-        L.sp_cuda_write_kv_tokens(cc, 0, 0, CTX, k0.data_ptr(), v0.data_ptr(), 0)
+        compress_pass()
     c1.record(stream)
     barrier()
-    cms = max_over_ranks(c0.elapsed_time(c1) / reps)
+    cms = max_over_ranks(c0.elapsed_time(c1) / (reps * len(kept)))
     pairs = CTX * H
     comp_mpairs = pairs * ws / (cms * 1e-3) / 1e6
     comp_gbs = pairs * (2 * HD * 4 + K_ROW + V_ROW) / (cms * 1e-3) / 1e9
@@ -382,7 +387,7 @@ def run_ours(args):
         "compress": {"metric": "ship-path compress throughput (K+V pairs)", "value": comp_mpairs,
                      "unit": "Mpairs/s", "model_tokens_per_s_M": comp_mpairs / (N_KV * 1.0),
                      "achieved_gbs": comp_gbs, "frac": comp_gbs / peak,
-                     "workload": "one layer: 32768 positions x %d KV heads, fp32 in" % H,
+                     "workload": "4 layers x 32768 positions x %d KV heads, fp32 in, 5 passes; ms is per layer" % H,
                      "ms": cms},
         "cache_fill_s": t_fill,
     }

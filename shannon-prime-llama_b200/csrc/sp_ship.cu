@@ -23,6 +23,7 @@
 #include <stdarg.h>
 #include <stdio.h>
 #include <string.h>
+#include <type_traits>
 
 namespace {
 
@@ -292,6 +293,242 @@ __global__ void k_permute(float *data, const int *order, int n, int n_vecs)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Fast write path for band layouts that map onto whole lane groups.  A
+// vector of n coefficients is spread over LPV = n/8 lanes, 8 consecutive
+// coefficients per lane (two vectors per warp at head_dim 128), and every
+// band must start and end on a lane boundary and span a power-of-two,
+// aligned group of lanes.  The ship layouts (K 4 x 32, V 1 x 128 at
+// head_dim 128) qualify.  Then:
+//   - the lane's 8 reordered coefficients belong to one band, so the band
+//     absmax is an xor-reduction over the band's lane group;
+//   - the lane's 8 codes are consecutive in the band's bit stream: one bit
+//     field ORed into the packed row with two or three shared-memory
+//     atomics;
+//   - the Hartley butterfly runs 3 stages in registers and log2(LPV)
+//     stages as one shuffle plus one FMA with +-1 per element
+//     (fma(-1, v, u) rounds exactly like u - v);
+//   - the lane's Möbius gather indices are loaded once per CTA.
+// CTAs are persistent (grid-stride over vectors, token-major), and each
+// vector's lanes store its row themselves, so no CTA-wide barrier is taken.
+constexpr int kFastWarps = 8;
+constexpr int kFastE = 8;              // coefficients per lane
+constexpr int kFastRowWords = 80;      // per-vector packed-row buffer (320 B)
+
+struct FastBand {
+    int group_log2[32];    // per lane of a vector: log2 of its band's lane-group size
+    int bits[32];          // bits of its band
+    int bitpos[32];        // row bit of its first code
+    int scale_word[32];    // row word of its band's fp16 scale
+    int scale_shift[32];   // 0 or 16; -1 if the lane does not write the scale
+};
+
+struct FastArgs {
+    EncodeArgs e;
+    FastBand fb;
+    int store_width;       // 4, 2 or 1: widest aligned store for every row
+};
+
+template <int LPV, typename Tin, bool WHT>
+__global__ void __launch_bounds__(kFastWarps * 32)
+k_encode_fast(FastArgs fa)
+{
+    constexpr int E = kFastE;
+    static_assert(E == 8, "the packing below splits the lane's codes 4 + 4");
+    constexpr int VPW = 32 / LPV;             // vectors per warp
+    constexpr int n = LPV * E;
+    constexpr int kStages = LPV == 32 ? 5 : LPV == 16 ? 4 : LPV == 8 ? 3 : LPV == 4 ? 2 : 1;
+    __shared__ uint32_t s_row[kFastWarps][VPW][kFastRowWords];
+    __shared__ __align__(16) float s_buf[kFastWarps][VPW][n];
+    const EncodeArgs &a = fa.e;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int sub = lane / LPV, ln = lane % LPV;        // vector within the warp, lane within it
+    const int words = (a.bl.total_bytes + 3) >> 2;
+
+    // Lane constants.
+    int ord[E];
+#pragma unroll
+    for (int e = 0; e < E; e++) ord[e] = a.order ? a.order[ln * E + e] : ln * E + e;
+    const int glog = fa.fb.group_log2[ln];
+    const int bits = fa.fb.bits[ln];
+    const int max_val = (1 << (bits - 1)) - 1;
+    const unsigned mult = 1u << bits;
+    const int bitpos = fa.fb.bitpos[ln];
+    const int sword = fa.fb.scale_word[ln];
+    const int sshift = fa.fb.scale_shift[ln];
+    float sgn[5];                           // butterfly sign of this lane per stage
+#pragma unroll
+    for (int k = 0; k < 5; k++) sgn[k] = (ln >> k) & 1 ? -1.0f : 1.0f;
+
+    const long long n_vec = (long long)a.n_tokens * a.nh;
+    const int stride = gridDim.x * kFastWarps * VPW;
+    // (token, head) of vector v = t * nh + h, stepped without division.
+    const int dt = stride / a.nh, dh = stride - dt * a.nh;
+    long long v = ((long long)blockIdx.x * kFastWarps + warp) * VPW + sub;
+    int t = (int)(v / a.nh), h = (int)(v - (long long)t * a.nh);
+    uint32_t *row = s_row[warp][sub];
+    float *buf = s_buf[warp][sub];
+    // Every lane of the warp runs the same number of iterations (shuffles
+    // span the warp); vectors past the end are computed but not stored.
+    const long long v_first = ((long long)blockIdx.x * kFastWarps + warp) * VPW;
+    for (long long vw = v_first; vw < n_vec; vw += stride, v += stride, t += dt, h += dh) {
+        if (h >= a.nh) { h -= a.nh; t++; }
+        const bool live = v < n_vec;
+        // ---- load ----
+        float x[E];
+        const Tin *src = reinterpret_cast<const Tin *>(a.in) + (live ? v : vw) * n + ln * E;
+        if constexpr (sizeof(Tin) == 4) {
+#pragma unroll
+            for (int e = 0; e < E; e += 4) {
+                const float4 q = __ldcs(reinterpret_cast<const float4 *>(src + e));
+                x[e] = q.x; x[e + 1] = q.y; x[e + 2] = q.z; x[e + 3] = q.w;
+            }
+        } else {
+            const uint4 q = __ldcs(reinterpret_cast<const uint4 *>(src));
+            const Tin *hv = reinterpret_cast<const Tin *>(&q);
+#pragma unroll
+            for (int e = 0; e < E; e++) x[e] = sp_load_as_float(hv, e);
+        }
+        for (int j = ln; j < words; j += LPV) row[j] = 0u;
+        // ---- VHT2 (ascending butterfly lengths, as the CPU path) ----
+        if constexpr (WHT) {
+#pragma unroll
+            for (int len = 1; len < E; len <<= 1) {
+#pragma unroll
+                for (int i = 0; i < E; i += len << 1) {
+#pragma unroll
+                    for (int j = 0; j < len; j++) {
+                        const float u = x[i + j], w = x[i + j + len];
+                        x[i + j] = __fadd_rn(u, w);
+                        x[i + j + len] = __fsub_rn(u, w);
+                    }
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < kStages; k++) {
+#pragma unroll
+                for (int e = 0; e < E; e++) {
+                    const float o = __shfl_xor_sync(0xffffffffu, x[e], 1 << k);
+                    x[e] = __fmaf_rn(sgn[k], x[e], o);
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < E; e++) x[e] = __fmul_rn(x[e], a.inv_sqrt_n);
+        }
+        // ---- Möbius reorder through shared memory ----
+        if (a.order) {
+#pragma unroll
+            for (int e = 0; e < E; e += 4)
+                *reinterpret_cast<float4 *>(&buf[ln * E + e]) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
+            __syncwarp();
+#pragma unroll
+            for (int e = 0; e < E; e++) x[e] = buf[ord[e]];
+        }
+        // ---- band absmax over the lane group (fmaxf skips NaN, as the CPU
+        //      path's "a > amax" does) ----
+        float amax = 0.0f;
+#pragma unroll
+        for (int e = 0; e < E; e++) amax = fmaxf(amax, fabsf(x[e]));
+#pragma unroll
+        for (int k = 0; k < kStages; k++) {
+            const float o = __shfl_xor_sync(0xffffffffu, amax, 1 << k);
+            if (k < glog) amax = fmaxf(amax, o);
+        }
+        const float scale = amax > 0.0f ? __fdiv_rn(amax, (float)max_val) : 0.0f;
+        const __half hs = __float2half_rn(scale);
+        const float stored = __half2float(hs);
+        const float inv = stored > 0.0f ? __frcp_rn(stored) : 0.0f;     // = 1.0f / stored
+        // ---- quantise and pack the lane's codes into one field: codes
+        //      0..3 and 4..7 are accumulated Horner-style (u3*m + u2)*m ...
+        //      with m = 2^bits, one integer multiply-add per code ----
+        unsigned u[E];
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            int q = __float2int_rn(__fmul_rn(x[e], inv));    // NaN -> 0, saturating
+            q = q > max_val ? max_val : (q < -max_val ? -max_val : q);
+            u[e] = (unsigned)(q + max_val);
+        }
+        unsigned f_lo = u[3], f_hi = u[7];
+#pragma unroll
+        for (int e = 2; e >= 0; e--) {
+            f_lo = f_lo * mult + u[e];
+            f_hi = f_hi * mult + u[e + 4];
+        }
+        const unsigned long long field = ((unsigned long long)f_hi << (4 * bits)) | f_lo;
+        __syncwarp();                       // row zeroed, buf reads done
+        {
+            const int w0 = bitpos >> 5, sh = bitpos & 31;
+            const unsigned long long lo = field << sh;
+            atomicOr(&row[w0], (unsigned)lo);
+            if (E * bits + sh > 32) atomicOr(&row[w0 + 1], (unsigned)(lo >> 32));
+            if (sh && E * bits + sh > 64) atomicOr(&row[w0 + 2], (unsigned)(field >> (64 - sh)));
+            if (sshift >= 0) atomicOr(&row[sword], (unsigned)__half_as_ushort(hs) << sshift);
+        }
+        __syncwarp();
+        // ---- store the packed row ----
+        if (live) {
+            uint8_t *dst = a.out_base + (a.slot0 + h) * a.slot_stride +
+                           (long long)(a.start_pos + t) * a.bl.total_bytes;
+            const int tb = a.bl.total_bytes;
+            if (fa.store_width == 4) {
+                for (int j = ln; j < (tb >> 2); j += LPV) reinterpret_cast<uint32_t *>(dst)[j] = row[j];
+            } else if (fa.store_width == 2) {
+                const uint16_t *r16 = reinterpret_cast<const uint16_t *>(row);
+                for (int j = ln; j < (tb >> 1); j += LPV) reinterpret_cast<uint16_t *>(dst)[j] = r16[j];
+            } else {
+                const uint8_t *r8 = reinterpret_cast<const uint8_t *>(row);
+                for (int j = ln; j < tb; j += LPV) dst[j] = r8[j];
+            }
+        }
+        __syncwarp();                       // row fully read before the next zeroing
+    }
+}
+
+// Lane tables for the fast path, or false if the layout does not qualify.
+bool fast_bands(const SpBandLayout &bl, FastBand &fb)
+{
+    const int E = kFastE;
+    if (bl.n % E || bl.n / E > 32 || bl.n / E < 1) return false;
+    if ((bl.total_bytes + 3) / 4 + 3 > kFastRowWords) return false;
+    for (int b = 0; b < bl.n_bands; b++) {
+        if (bl.off[b] % E || bl.size[b] % E || bl.bits[b] < 1 || bl.bits[b] > 8) return false;
+        const int g = bl.size[b] / E;
+        if (g < 1 || (g & (g - 1)) || (bl.off[b] / E) % g) return false;
+        int glog = 0;
+        while ((1 << glog) < g) glog++;
+        for (int l = bl.off[b] / E; l < (bl.off[b] + bl.size[b]) / E; l++) {
+            fb.group_log2[l] = glog;
+            fb.bits[l] = bl.bits[b];
+            fb.bitpos[l] = 8 * (bl.byte_off[b] + 2) + (l * E - bl.off[b]) * bl.bits[b];
+            fb.scale_word[l] = bl.byte_off[b] >> 2;
+            fb.scale_shift[l] = (l * E == bl.off[b]) ? 8 * (bl.byte_off[b] & 3) : -1;
+        }
+    }
+    return true;
+}
+
+template <int LPV, typename Tin>
+int launch_encode_fast(const FastArgs &fa, bool wht, cudaStream_t s)
+{
+    static int blocks_per_sm[2] = {0, 0}, sms = 0;
+    auto k = wht ? k_encode_fast<LPV, Tin, true> : k_encode_fast<LPV, Tin, false>;
+    int &bps = blocks_per_sm[wht ? 1 : 0];
+    if (!bps) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, k, kFastWarps * 32, 0);
+        if (bps < 1) bps = 1;
+        if (sms < 1) sms = 148;
+    }
+    const long long per_cta = (long long)kFastWarps * (32 / LPV);
+    const long long n_vec = (long long)fa.e.n_tokens * fa.e.nh;
+    long long blocks = (n_vec + per_cta - 1) / per_cta;
+    if (blocks > (long long)sms * bps) blocks = (long long)sms * bps;
+    k<<<(unsigned)blocks, kFastWarps * 32, 0, s>>>(fa);
+    return sp_check_cuda(cudaGetLastError(), "encode launch");
+}
+
 size_t encode_smem(int n, int total_bytes)
 {
     return (size_t)n * 4 + (size_t)kWarps * n * 4 + (size_t)kWarps * SP_MAX_BANDS * 6 +
@@ -325,6 +562,22 @@ int launch_encode_t(const EncodeArgs &a, bool wht, cudaStream_t s)
 template <typename Tin>
 int launch_encode_dt(const EncodeArgs &a, bool wht, cudaStream_t s)
 {
+    FastArgs fa;
+    fa.e = a;
+    const uintptr_t base = (uintptr_t)(a.out_base + a.slot0 * a.slot_stride + (long long)a.start_pos * a.bl.total_bytes);
+    const int tb = a.bl.total_bytes;
+    fa.store_width = ((tb | base | (uintptr_t)a.slot_stride) & 3) == 0 ? 4
+                   : ((tb | base | (uintptr_t)a.slot_stride) & 1) == 0 ? 2 : 1;
+    // The inputs must allow 16-byte loads of each lane's 8 elements.
+    const bool in_aligned = ((uintptr_t)a.in % 16) == 0;
+    if (in_aligned && fast_bands(a.bl, fa.fb)) {
+        switch (a.bl.n / kFastE) {
+        case 4:  return launch_encode_fast<4, Tin>(fa, wht, s);
+        case 8:  return launch_encode_fast<8, Tin>(fa, wht, s);
+        case 16: return launch_encode_fast<16, Tin>(fa, wht, s);
+        case 32: return launch_encode_fast<32, Tin>(fa, wht, s);
+        }
+    }
     switch (a.bl.n) {
     case 32:  return launch_encode_t<1, Tin>(a, wht, s);
     case 64:  return launch_encode_t<2, Tin>(a, wht, s);
