@@ -43,6 +43,11 @@ SEED = 1
 METRIC = ("fused decompress-KQ/V decode latency per token @32K ctx "
           "(Llama-3-8B shape: 32 layers, 32 Q / 8 KV heads, hd 128, ship K 5/5/4/3 + V 3-bit)")
 UNIT = "us/token"
+# DRAM bytes (read + write) of one fused-decode launch per cached layer, from
+# an ncu capture of the 8-layer case of this workload
+# (dram__bytes_read.sum + dram__bytes_write.sum = 264.49 MB + 3.66 MB over 8
+# layers); traffic grows in proportion to the layers processed.
+NCU_TRAFFIC_PER_LAYER = 268.15e6 / 8
 
 
 def peaks():
@@ -111,8 +116,12 @@ def dist_env():
 
 
 def local_heads(rank: int, world: int):
-    """KV heads owned by a rank: h % world == rank (balanced for world | 8)."""
-    return [h for h in range(N_KV) if h % world == rank]
+    """KV heads owned by a rank (spb200.shard: h % world == rank for world | 8;
+    every rank keeps all layers of config 1)."""
+    from spb200 import shard
+    sh = shard.partition(N_LAYERS, N_KV, world)[rank]
+    assert sh.layer0 == 0 and sh.n_layers == N_LAYERS
+    return list(sh.heads)
 
 
 def cpu_decode_sample(n_threads: int, layers: int = 1):
@@ -376,7 +385,10 @@ def run_ours(args):
                    "parallelism": f"kv-head shards x{ws}" if ws > 1 else "single GPU",
                    "kv_heads_per_gpu": H, "splits": splits},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
+                     "frac": achieved / peak,
+                     "traffic": NCU_TRAFFIC_PER_LAYER * N_LAYERS * H / N_KV,
+                     "traffic_source": "ncu dram bytes of the 8-layer capture, scaled by layers x kv heads",
+                     "peak_source": peak_src,
                      "kernel": "fused decode main kernel", "kernel_ms": kernel_ms,
                      "algorithmic_bytes": alg_bytes},
         "e2e": {"value": e2e_ms * 1e3, "unit": UNIT, "h2d_bytes_per_step": h2d,
