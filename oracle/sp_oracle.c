@@ -289,6 +289,45 @@ void or_ship_read_batch(int n_vecs, const uint8_t *in, float *vecs,
 
 /* ------------------------------------------------------- attention -- */
 
+/* One (KV head, token chunk) task: scores of every query of the group over
+ * tokens [t0, t1), the chunk's max per query, and exp-weighted sums relative
+ * to that max (double). */
+typedef struct {
+    double mx[8];
+    double den[8];
+    double *acc;               /* [group][n] */
+} or_attn_part_t;
+
+static void or_attn_chunk(const uint8_t *ks, const uint8_t *vs, const or_bands_t *kb,
+                          const or_bands_t *vb, const int *order, const double (*qd)[1024],
+                          int group, int t0, int t1, float logit_scale, or_attn_part_t *pt)
+{
+    const int n = kb->n;
+    float kr[1024], vr[1024];
+    double *score = (double *)malloc(sizeof(double) * (size_t)(t1 - t0) * (size_t)group);
+    for (int g = 0; g < group; g++) { pt->mx[g] = -INFINITY; pt->den[g] = 0.0; }
+    for (int t = t0; t < t1; t++) {
+        or_ship_read(ks + (size_t)t * kb->total_bytes, kr, kb, order, -1);
+        for (int g = 0; g < group; g++) {
+            double sc = 0.0;
+            for (int d = 0; d < n; d++) sc += (double)kr[d] * qd[g][d];
+            sc *= (double)logit_scale;
+            score[(size_t)(t - t0) * group + g] = sc;
+            if (sc > pt->mx[g]) pt->mx[g] = sc;
+        }
+    }
+    for (int t = t0; t < t1; t++) {
+        or_ship_read(vs + (size_t)t * vb->total_bytes, vr, vb, NULL, -1);
+        for (int g = 0; g < group; g++) {
+            double pr = exp(score[(size_t)(t - t0) * group + g] - pt->mx[g]);
+            pt->den[g] += pr;
+            double *a = pt->acc + (size_t)g * n;
+            for (int d = 0; d < n; d++) a[d] += pr * (double)vr[d];
+        }
+    }
+    free(score);
+}
+
 void or_attn_decode(const uint8_t *k_slots, size_t slot_stride_k,
                     const uint8_t *v_slots, size_t slot_stride_v,
                     const or_bands_t *kb, const or_bands_t *vb,
@@ -298,49 +337,48 @@ void or_attn_decode(const uint8_t *k_slots, size_t slot_stride_k,
 {
     const int n = kb->n;
     const int group = n_q_heads / n_kv_heads;
-#ifdef _OPENMP
     if (n_threads < 1) n_threads = 1;
+    /* Token chunks per head: enough tasks for every thread (the result is
+     * the same softmax, merged with log-sum-exp weights in double). */
+    int chunks = (2 * n_threads + n_kv_heads - 1) / n_kv_heads;
+    if (chunks > kv_len) chunks = kv_len > 0 ? kv_len : 1;
+    const int n_tasks = n_kv_heads * chunks;
+    or_attn_part_t *parts = (or_attn_part_t *)calloc((size_t)n_tasks, sizeof(or_attn_part_t));
+    double *accs = (double *)calloc((size_t)n_tasks * (size_t)group * (size_t)n, sizeof(double));
+#ifdef _OPENMP
 #pragma omp parallel for num_threads(n_threads) schedule(dynamic)
 #endif
-    for (int h = 0; h < n_kv_heads; h++) {
-        float kr[1024], vr[1024];
-        double *score = (double *)malloc(sizeof(double) * (size_t)kv_len * (size_t)group);
-        double *acc = (double *)calloc((size_t)group * (size_t)n, sizeof(double));
+    for (int task = 0; task < n_tasks; task++) {
+        const int h = task / chunks, c = task % chunks;
+        const int t0 = (int)((long long)kv_len * c / chunks), t1 = (int)((long long)kv_len * (c + 1) / chunks);
         double qd[8][1024];
         for (int g = 0; g < group && g < 8; g++)
             for (int d = 0; d < n; d++)
                 qd[g][d] = (double)or_f16_to_f32(q[(size_t)(h * group + g) * n + d]);
-        const uint8_t *ks = k_slots + (size_t)h * slot_stride_k;
-        const uint8_t *vs = v_slots + (size_t)h * slot_stride_v;
-        double mx[8];
-        for (int g = 0; g < group; g++) mx[g] = -INFINITY;
-        for (int t = 0; t < kv_len; t++) {
-            or_ship_read(ks + (size_t)t * kb->total_bytes, kr, kb, order, -1);
-            for (int g = 0; g < group; g++) {
-                double s = 0.0;
-                for (int d = 0; d < n; d++) s += (double)kr[d] * qd[g][d];
-                s *= (double)logit_scale;
-                score[(size_t)t * group + g] = s;
-                if (s > mx[g]) mx[g] = s;
-            }
-        }
-        double den[8] = {0};
-        for (int t = 0; t < kv_len; t++) {
-            or_ship_read(vs + (size_t)t * vb->total_bytes, vr, vb, NULL, -1);
-            for (int g = 0; g < group; g++) {
-                double p = exp(score[(size_t)t * group + g] - mx[g]);
-                den[g] += p;
-                double *a = acc + (size_t)g * n;
-                for (int d = 0; d < n; d++) a[d] += p * (double)vr[d];
-            }
-        }
-        for (int g = 0; g < group; g++)
-            for (int d = 0; d < n; d++)
-                out[(size_t)(h * group + g) * n + d] =
-                    (float)(acc[(size_t)g * n + d] / den[g]);
-        free(score);
-        free(acc);
+        parts[task].acc = accs + (size_t)task * group * n;
+        or_attn_chunk(k_slots + (size_t)h * slot_stride_k, v_slots + (size_t)h * slot_stride_v, kb, vb,
+                      order, (const double (*)[1024])qd, group, t0, t1, logit_scale, &parts[task]);
     }
+    for (int h = 0; h < n_kv_heads; h++) {
+        for (int g = 0; g < group; g++) {
+            double M = -INFINITY;
+            for (int c = 0; c < chunks; c++) if (parts[h * chunks + c].mx[g] > M) M = parts[h * chunks + c].mx[g];
+            double den = 0.0;
+            double *o = (double *)calloc((size_t)n, sizeof(double));
+            for (int c = 0; c < chunks; c++) {
+                const or_attn_part_t *pt = &parts[h * chunks + c];
+                if (pt->mx[g] == -INFINITY) continue;
+                const double w = exp(pt->mx[g] - M);
+                den += w * pt->den[g];
+                for (int d = 0; d < n; d++) o[d] += w * pt->acc[(size_t)g * n + d];
+            }
+            for (int d = 0; d < n; d++)
+                out[(size_t)(h * group + g) * n + d] = den > 0.0 ? (float)(o[d] / den) : 0.0f;
+            free(o);
+        }
+    }
+    free(accs);
+    free(parts);
 }
 
 double or_correlation(const float *a, const float *b, int n)
