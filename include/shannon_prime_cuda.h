@@ -168,6 +168,161 @@ int  sp_cuda_attn_decode_noalloc(const void *d_k_cache, const void *d_v_cache,
                                  int n_q_heads, int kv_len, float logit_scale,
                                  void *d_out, int max_bands, void *stream);
 
+/* ------------------------------------------------- sqfree + spinor cache -- */
+/* Replaces reference sp_cuda_sqfree_cache_t (shannon_prime_cuda.h:153-230,
+ * src/backends/cuda/shannon_prime_sqfree.cu:585-1122).  Per position and
+ * K/V half the slot holds [skeleton bands][fp32 magnitude][residual levels,
+ * LSB-first][spinor sheet bits] (shannon_prime_sqfree.cu:683-686):
+ *   pad head_dim -> pad_dim (squarefree, {2,3,5,7,11}-smooth; 154 at 128)
+ *   with the mean, Vilenkin (staged prime Hartley) transform, keep sk_k
+ *   skeleton coefficients (band-quantised), predict the n_res others from
+ *   the skeleton by a Möbius CSR sum, store the (spinor-signed) deviation
+ *   with residual_bits per coefficient.
+ * The reference's fields are kept; its per-call scratch buffers are not
+ * needed (every kernel here keeps its intermediates on chip) and stay NULL. */
+typedef struct {
+    sp_config_t      config;
+    int              pad_dim;
+    int              sk_k;
+    int              n_res;
+    int              n_terms;
+    int              residual_bits;
+    int              use_spinor;
+    int              use_skel_mobius;   /* unused, as in the reference */
+    sp_band_config_t k_bands;           /* over the sk_k skeleton values */
+    sp_band_config_t v_bands;
+    int             *d_skeleton_idx;    /* [sk_k] */
+    int             *d_residual_idx;    /* [n_res] */
+    int             *d_csr_offsets;     /* [n_res + 1] */
+    int             *d_csr_skel_slot;   /* [n_terms] */
+    int             *d_csr_mu_sign;     /* [n_terms], +1 / -1 */
+    int             *d_vilenkin_factors;
+    int              n_factors;
+    unsigned char   *d_k_cache;         /* [n_slots][max_seq_len][bytes_per_pos_k] */
+    unsigned char   *d_v_cache;
+    int              bytes_per_pos_k;
+    int              bytes_per_pos_v;
+    int              max_seq_len;
+    int              n_slots;
+    float           *d_pad_scratch;     /* unused (NULL) */
+    float           *d_coeff_scratch;
+    float           *d_skel_scratch;
+    float           *d_pred_scratch;
+    float           *d_dev_scratch;
+    unsigned char   *d_levels_scratch;
+    float           *d_mag_scratch;
+    float           *d_actual_scratch;
+    unsigned char   *d_sheet_scratch;
+    void            *stream;
+    /* --- B200 build additions --- */
+    int              device;
+    void            *d_tables;          /* packed kernel tables (indices, CSR, cas) */
+    void            *d_attn_ws;         /* fused-decode partials */
+    size_t           attn_ws_bytes;
+} sp_cuda_sqfree_cache_t;
+
+/* Reference signature; the skeleton is pad_dim / 2 as in the reference CUDA
+ * cache (shannon_prime_sqfree.cu:606).  Returns 0 or SP_ERR_*. */
+int  sp_cuda_sqfree_cache_init(sp_cuda_sqfree_cache_t *cc, const sp_config_t *cfg,
+                               int max_seq_len, int residual_bits, int use_spinor,
+                               void *stream);
+/* New: skeleton = floor(sk_frac * pad_dim) (the bridge's SHANNON_PRIME_SK_FRAC,
+ * shannon_prime_llama_sqfree.c:68-71, which the reference parses but never
+ * passes on). */
+int  sp_cuda_sqfree_cache_init_ex(sp_cuda_sqfree_cache_t *cc, const sp_config_t *cfg,
+                                  int max_seq_len, int residual_bits, int use_spinor,
+                                  float sk_frac, void *stream);
+void sp_cuda_sqfree_cache_free(sp_cuda_sqfree_cache_t *cc);
+/* Reference shannon_prime_cuda.h:185-220 (device vectors of head_dim). */
+void sp_cuda_sqfree_write_k(sp_cuda_sqfree_cache_t *cc, int layer, int head, int pos,
+                            const float *d_k_vec);
+void sp_cuda_sqfree_write_v(sp_cuda_sqfree_cache_t *cc, int layer, int head, int pos,
+                            const float *d_v_vec);
+void sp_cuda_sqfree_read_k(const sp_cuda_sqfree_cache_t *cc, int layer, int head, int pos,
+                           float *d_k_out);
+void sp_cuda_sqfree_read_v(const sp_cuda_sqfree_cache_t *cc, int layer, int head, int pos,
+                           float *d_v_out);
+void sp_cuda_sqfree_read_k_batch(const sp_cuda_sqfree_cache_t *cc, int layer, int head,
+                                 int start_pos, int n_pos, float *d_k_out);
+void sp_cuda_sqfree_read_v_batch(const sp_cuda_sqfree_cache_t *cc, int layer, int head,
+                                 int start_pos, int n_pos, float *d_v_out);
+/* New: token-major write of every head of layers [layer0, layer0+n_layers):
+ * d_k / d_v are [n_layers][n_tokens][n_heads_kv][head_dim] (NULL skips). */
+int  sp_cuda_sqfree_write_kv_tokens(sp_cuda_sqfree_cache_t *cc, int layer0, int n_layers,
+                                    int start_pos, int n_tokens, const void *d_k,
+                                    const void *d_v, int dtype);
+/* New: fused decode attention over the sqfree cache, same contract as
+ * sp_cuda_attn_decode (fp16 q/out [n_layers][n_q_heads][head_dim], at most
+ * 8 query heads per KV head); scores and the V sum are taken in the
+ * Vilenkin coefficient domain, one inverse transform per query head. */
+int  sp_cuda_sqfree_attn_decode(const sp_cuda_sqfree_cache_t *cc, int layer0, int n_layers,
+                                const void *d_q, int n_q_heads, int kv_len, float logit_scale,
+                                void *d_out, void *stream);
+
+/* ------------------------------------------- hierarchical Vilenkin cache -- */
+/* Replaces reference sp_cuda_hier_cache_t (shannon_prime_cuda.h:300-377,
+ * shannon_prime_hier.cu:272-601).  Slot: [skeleton bands][fp32 magnitude]
+ * [target residual levels]; targets are predicted as W_slot . skeleton with
+ * a per-slot fp16 W [n_target][n_skeleton] uploaded after calibration. */
+typedef struct {
+    sp_config_t      config;
+    int              pad_dim;
+    int              n_skeleton;
+    int              n_target;
+    int              target_res_bits;
+    int              n_slots;
+    int              max_seq_len;
+    uint16_t        *d_W;               /* [n_slots][n_target][n_skeleton] fp16 */
+    int             *d_skeleton_idx;    /* [n_skeleton] */
+    int             *d_target_idx;      /* [n_target] */
+    int             *d_vilenkin_factors;
+    int              n_factors;
+    sp_band_config_t skel_bands;
+    int             *d_skel_band_bits;
+    unsigned char   *d_k_cache;
+    unsigned char   *d_v_cache;
+    int              bytes_per_pos_k;
+    int              bytes_per_pos_v;
+    float           *d_pad_scratch;     /* unused (NULL) */
+    float           *d_coeff_scratch;
+    float           *d_skel_scratch;
+    float           *d_pred_scratch;
+    float           *d_dev_scratch;
+    float           *d_mag_scratch;
+    unsigned char   *d_levels_scratch;
+    void            *stream;
+    /* --- B200 build additions --- */
+    int              device;
+    void            *d_tables;
+} sp_cuda_hier_cache_t;
+
+/* Reference shannon_prime_cuda.h:337-349 (caller supplies the index sets and
+ * the skeleton band layout). */
+int  sp_cuda_hier_cache_init(sp_cuda_hier_cache_t *hc, const sp_config_t *cfg,
+                             int pad_dim, int n_skeleton, int n_target, int target_res_bits,
+                             const int *skeleton_idx, const int *target_idx,
+                             const sp_band_config_t *skel_bands, int max_seq_len, int n_slots,
+                             void *stream);
+void sp_cuda_hier_cache_free(sp_cuda_hier_cache_t *hc);
+/* Reference shannon_prime_cuda.h:354-355: W_all [n_slots][n_target][n_skeleton] fp16. */
+int  sp_cuda_hier_cache_upload_W(sp_cuda_hier_cache_t *hc, const uint16_t *W_all);
+void sp_cuda_hier_write_k(sp_cuda_hier_cache_t *hc, int layer, int head, int pos,
+                          const float *d_k_vec);
+void sp_cuda_hier_write_v(sp_cuda_hier_cache_t *hc, int layer, int head, int pos,
+                          const float *d_v_vec);
+void sp_cuda_hier_read_k(const sp_cuda_hier_cache_t *hc, int layer, int head, int pos,
+                         float *d_k_out);
+void sp_cuda_hier_read_v(const sp_cuda_hier_cache_t *hc, int layer, int head, int pos,
+                         float *d_v_out);
+/* New: batched compress of layers [layer0, layer0+n_layers) in one call,
+ * inputs [n_layers][n_tokens][n_heads_kv][head_dim] (f32/f16/bf16). */
+int  sp_cuda_hier_write_kv_tokens(sp_cuda_hier_cache_t *hc, int layer0, int n_layers,
+                                  int start_pos, int n_tokens, const void *d_k,
+                                  const void *d_v, int dtype);
+/* New: batched decompress, outputs fp32 [n_layers][n_pos][n_heads_kv][head_dim]. */
+int  sp_cuda_hier_read_kv_tokens(const sp_cuda_hier_cache_t *hc, int layer0, int n_layers,
+                                 int start_pos, int n_pos, float *d_k_out, float *d_v_out);
+
 /* ----------------------------------------- kernel launchers (for tests) -- */
 
 /* Reference shannon_prime_cuda.h:116-134.  In-place VHT2 of n_vecs
@@ -193,7 +348,8 @@ int         sp_cuda_last_error(void);
 const char *sp_cuda_last_error_string(void);
 
 /* New: sizeof(sp_config_t) (which=0), sizeof(sp_band_config_t) (1),
- * sizeof(sp_cuda_cache_t) (2), so bindings can check their struct mirrors. */
+ * sizeof(sp_cuda_cache_t) (2), sizeof(sp_cuda_sqfree_cache_t) (3),
+ * sizeof(sp_cuda_hier_cache_t) (4), so bindings can check their mirrors. */
 int sp_cuda_abi_struct_size(int which);
 
 /* New, for tests and benchmarks: force the fused-decode kernel family

@@ -27,6 +27,29 @@ class Bands(C.Structure):
     ]
 
 
+OR_SQ_MAX_PD = 512
+OR_SQ_MAX_TERMS = 16384
+
+
+class Sqfree(C.Structure):
+    _fields_ = [
+        ("hd", C.c_int), ("pd", C.c_int), ("sk_k", C.c_int), ("n_res", C.c_int),
+        ("n_terms", C.c_int), ("res_bits", C.c_int), ("use_spinor", C.c_int),
+        ("skel_idx", C.c_int * OR_SQ_MAX_PD), ("res_idx", C.c_int * OR_SQ_MAX_PD),
+        ("csr_off", C.c_int * (OR_SQ_MAX_PD + 1)), ("csr_slot", C.c_int * OR_SQ_MAX_TERMS),
+        ("csr_sign", C.c_int * OR_SQ_MAX_TERMS), ("bands", Bands),
+        ("res_bytes", C.c_int), ("sheet_bytes", C.c_int), ("bytes_per_pos", C.c_int),
+    ]
+
+
+class Hier(C.Structure):
+    _fields_ = [
+        ("hd", C.c_int), ("pd", C.c_int), ("n_skel", C.c_int), ("n_target", C.c_int),
+        ("res_bits", C.c_int), ("bands", Bands), ("res_bytes", C.c_int),
+        ("bytes_per_pos", C.c_int),
+    ]
+
+
 _lib = None
 _P = C.c_void_p
 
@@ -57,6 +80,24 @@ def lib() -> C.CDLL:
         L.or_attn_decode.argtypes = [_P, C.c_size_t, _P, C.c_size_t, C.POINTER(Bands),
                                      C.POINTER(Bands), _P, C.c_int, C.c_int, C.c_int, _P,
                                      C.c_float, _P, C.c_int]
+        L.or_lane_tree_sum.restype = C.c_float
+        L.or_lane_tree_sum.argtypes = [_P, C.c_int]
+        L.or_sqfree_pad_dim.restype = C.c_int
+        L.or_sqfree_pad_dim.argtypes = [C.c_int]
+        L.or_vilenkin.argtypes = [_P, C.c_int]
+        L.or_cas_table.argtypes = [C.c_int, _P, _P]
+        L.or_sqfree_layout.restype = C.c_int
+        L.or_sqfree_layout.argtypes = [C.POINTER(Sqfree), C.c_int, C.c_int, C.c_int, _P, C.c_int, C.c_int]
+        L.or_sqfree_write_batch.argtypes = [C.c_int, _P, _P, C.POINTER(Sqfree), C.c_int]
+        L.or_sqfree_read_batch.argtypes = [C.c_int, _P, _P, C.POINTER(Sqfree), C.c_int]
+        L.or_sqfree_coeffs.argtypes = [_P, _P, C.POINTER(Sqfree)]
+        L.or_sqfree_attn_decode.argtypes = [_P, C.c_size_t, _P, C.c_size_t, C.POINTER(Sqfree),
+                                            C.POINTER(Sqfree), C.c_int, C.c_int, C.c_int, _P,
+                                            C.c_float, _P, C.c_int]
+        L.or_hier_layout.restype = C.c_int
+        L.or_hier_layout.argtypes = [C.POINTER(Hier), C.c_int, C.c_int, _P, C.c_int]
+        L.or_hier_write_batch.argtypes = [C.c_int, _P, _P, C.POINTER(Hier), _P, C.c_int]
+        L.or_hier_read_batch.argtypes = [C.c_int, _P, _P, C.POINTER(Hier), _P, C.c_int]
         L.or_correlation.restype = C.c_double
         L.or_correlation.argtypes = [_P, _P, C.c_int]
         _lib = L
@@ -173,3 +214,101 @@ def mean_vector_correlation(a: np.ndarray, b: np.ndarray) -> float:
     a2 = a.reshape(-1, a.shape[-1])
     b2 = b.reshape(-1, b.shape[-1])
     return float(np.mean([correlation(x, y) for x, y in zip(a2, b2)]))
+
+
+# ------------------------------------------------------------ sqfree / hier --
+
+def sqfree_layout(hd: int, sk_k: int | None = None, bits=(5, 4, 4, 4, 5), residual_bits: int = 3,
+                  use_spinor: bool = True, sk_frac: float | None = None) -> Sqfree:
+    """Sqfree+spinor slot layout; sk_k defaults to floor(sk_frac * pad_dim)
+    (sk_frac 0.75) or pad_dim // 2 when sk_frac is None and sk_k is None."""
+    pd = lib().or_sqfree_pad_dim(hd)
+    if sk_k is None:
+        sk_k = int(sk_frac * pd) if sk_frac is not None else pd // 2
+    L = Sqfree()
+    arr = (C.c_int * len(bits))(*bits)
+    if lib().or_sqfree_layout(C.byref(L), hd, sk_k, len(bits), arr, residual_bits,
+                              1 if use_spinor else 0) != 0:
+        raise ValueError("bad sqfree layout")
+    return L
+
+
+def sqfree_write(vecs: np.ndarray, L: Sqfree, n_threads: int | None = None) -> np.ndarray:
+    v = np.ascontiguousarray(vecs, dtype=np.float32).reshape(-1, L.hd)
+    out = np.zeros((v.shape[0], L.bytes_per_pos), np.uint8)
+    lib().or_sqfree_write_batch(v.shape[0], v.ctypes.data, out.ctypes.data, C.byref(L),
+                                n_threads or threads())
+    return out
+
+
+def sqfree_read(packed: np.ndarray, L: Sqfree, n_threads: int | None = None) -> np.ndarray:
+    p = np.ascontiguousarray(packed, dtype=np.uint8).reshape(-1, L.bytes_per_pos)
+    out = np.zeros((p.shape[0], L.hd), np.float32)
+    lib().or_sqfree_read_batch(p.shape[0], p.ctypes.data, out.ctypes.data, C.byref(L),
+                               n_threads or threads())
+    return out
+
+
+def sqfree_attn_decode(k_slots, v_slots, LK: Sqfree, LV: Sqfree, q_f16, kv_len: int,
+                       logit_scale: float = 1.0, n_threads: int | None = None) -> np.ndarray:
+    ks = np.ascontiguousarray(k_slots, dtype=np.uint8)
+    vs = np.ascontiguousarray(v_slots, dtype=np.uint8)
+    q = np.ascontiguousarray(q_f16, dtype=np.float16).view(np.uint16)
+    H, nq = ks.shape[0], q.shape[0]
+    out = np.zeros((nq, LK.hd), np.float32)
+    lib().or_sqfree_attn_decode(ks.ctypes.data, ks[0].nbytes, vs.ctypes.data, vs[0].nbytes,
+                                C.byref(LK), C.byref(LV), H, nq, kv_len, q.ctypes.data,
+                                logit_scale, out.ctypes.data, n_threads or threads())
+    return out
+
+
+def vilenkin(x: np.ndarray) -> np.ndarray:
+    y = np.ascontiguousarray(x, dtype=np.float32).copy()
+    flat = y.reshape(-1, y.shape[-1])
+    for row in flat:
+        lib().or_vilenkin(row.ctypes.data, row.shape[0])
+    return y
+
+
+def hier_layout(hd: int, bits=(5, 5), residual_bits: int = 2) -> Hier:
+    L = Hier()
+    arr = (C.c_int * len(bits))(*bits)
+    if lib().or_hier_layout(C.byref(L), hd, len(bits), arr, residual_bits) != 0:
+        raise ValueError("bad hier layout")
+    return L
+
+
+def hier_write(vecs: np.ndarray, L: Hier, W: np.ndarray, n_threads: int | None = None) -> np.ndarray:
+    v = np.ascontiguousarray(vecs, dtype=np.float32).reshape(-1, L.hd)
+    w = np.ascontiguousarray(W, dtype=np.float16).view(np.uint16)
+    assert w.shape == (L.n_target, L.n_skel)
+    out = np.zeros((v.shape[0], L.bytes_per_pos), np.uint8)
+    lib().or_hier_write_batch(v.shape[0], v.ctypes.data, out.ctypes.data, C.byref(L),
+                              w.ctypes.data, n_threads or threads())
+    return out
+
+
+def hier_read(packed: np.ndarray, L: Hier, W: np.ndarray, n_threads: int | None = None) -> np.ndarray:
+    p = np.ascontiguousarray(packed, dtype=np.uint8).reshape(-1, L.bytes_per_pos)
+    w = np.ascontiguousarray(W, dtype=np.float16).view(np.uint16)
+    out = np.zeros((p.shape[0], L.hd), np.float32)
+    lib().or_hier_read_batch(p.shape[0], p.ctypes.data, out.ctypes.data, C.byref(L),
+                             w.ctypes.data, n_threads or threads())
+    return out
+
+
+def hier_fit_W(calib: np.ndarray, L: Hier, ridge: float = 1e-6) -> np.ndarray:
+    """Predictor W [n_target][n_skel] (fp16) fitted by ridge least squares in
+    double on a calibration set of vectors: padded, transformed, skeleton
+    coefficients -> target coefficients.  Calibration is host-side work (the
+    reference fits W on the CPU and uploads it, kv_cache.cpp:519-808)."""
+    v = np.ascontiguousarray(calib, dtype=np.float32).reshape(-1, L.hd)
+    pad = np.empty((v.shape[0], L.pd), np.float32)
+    for i, row in enumerate(v):
+        pad[i, :L.hd] = row
+        pad[i, L.hd:] = lib().or_lane_tree_sum(row.ctypes.data, L.hd) / np.float32(L.hd)
+    c = vilenkin(pad).astype(np.float64)
+    S, T = c[:, :L.n_skel], c[:, L.n_skel:]
+    A = S.T @ S + ridge * np.eye(L.n_skel)
+    W = np.linalg.solve(A, S.T @ T).T
+    return W.astype(np.float16)

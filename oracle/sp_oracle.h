@@ -88,6 +88,56 @@ void or_attn_decode(const uint8_t *k_slots, size_t slot_stride_k,
                     int kv_len, const uint16_t *q, float logit_scale,
                     float *out, int n_threads);
 
+/* ---- sqfree+spinor and hierarchical Vilenkin (sp_oracle_sqfree.c) ---- */
+
+#define OR_SQ_MAX_PD 512
+#define OR_SQ_MAX_TERMS 16384
+
+typedef struct {
+    int hd, pd, sk_k, n_res, n_terms, res_bits, use_spinor;
+    int skel_idx[OR_SQ_MAX_PD];      /* skeleton slot -> coefficient index */
+    int res_idx[OR_SQ_MAX_PD];       /* residual slot -> coefficient index */
+    int csr_off[OR_SQ_MAX_PD + 1];
+    int csr_slot[OR_SQ_MAX_TERMS];
+    int csr_sign[OR_SQ_MAX_TERMS];
+    or_bands_t bands;                /* band layout over the sk_k skeleton values */
+    int res_bytes, sheet_bytes, bytes_per_pos;
+} or_sqfree_t;
+
+typedef struct {
+    int hd, pd, n_skel, n_target, res_bits;
+    or_bands_t bands;                /* over the n_skel skeleton values (indices 0..n_skel) */
+    int res_bytes, bytes_per_pos;
+} or_hier_t;
+
+float or_lane_tree_sum(const float *v, int n);
+int   or_sqfree_pad_dim(int hd);
+int   or_vilenkin_factors(int pd, int *factors);
+void  or_cas_table(int p, float *cas, float *inv_sqrt_p);
+void  or_vilenkin(float *x, int pd);
+
+int  or_sqfree_layout(or_sqfree_t *L, int hd, int sk_k, int n_bands, const int *bits,
+                      int residual_bits, int use_spinor);
+void or_sqfree_write(const float *vec, uint8_t *out, const or_sqfree_t *L);
+void or_sqfree_coeffs(const uint8_t *in, float *coeffs, const or_sqfree_t *L);
+void or_sqfree_read(const uint8_t *in, float *vec, const or_sqfree_t *L);
+void or_sqfree_write_batch(int n_vecs, const float *vecs, uint8_t *out, const or_sqfree_t *L,
+                           int n_threads);
+void or_sqfree_read_batch(int n_vecs, const uint8_t *in, float *vecs, const or_sqfree_t *L,
+                          int n_threads);
+void or_sqfree_attn_decode(const uint8_t *k_slots, size_t stride_k, const uint8_t *v_slots,
+                           size_t stride_v, const or_sqfree_t *LK, const or_sqfree_t *LV,
+                           int n_kv_heads, int n_q_heads, int kv_len, const uint16_t *q,
+                           float logit_scale, float *out, int n_threads);
+
+int  or_hier_layout(or_hier_t *L, int hd, int n_bands, const int *bits, int residual_bits);
+void or_hier_write(const float *vec, uint8_t *out, const or_hier_t *L, const uint16_t *W);
+void or_hier_read(const uint8_t *in, float *vec, const or_hier_t *L, const uint16_t *W);
+void or_hier_write_batch(int n_vecs, const float *vecs, uint8_t *out, const or_hier_t *L,
+                         const uint16_t *W, int n_threads);
+void or_hier_read_batch(int n_vecs, const uint8_t *in, float *vecs, const or_hier_t *L,
+                        const uint16_t *W, int n_threads);
+
 /* Pearson correlation accumulated in double. */
 double or_correlation(const float *a, const float *b, int n);
 

@@ -263,6 +263,8 @@ extern "C" int sp_cuda_abi_struct_size(int which)
     case 0: return (int)sizeof(sp_config_t);
     case 1: return (int)sizeof(sp_band_config_t);
     case 2: return (int)sizeof(sp_cuda_cache_t);
+    case 3: return (int)sizeof(sp_cuda_sqfree_cache_t);
+    case 4: return (int)sizeof(sp_cuda_hier_cache_t);
     }
     return -1;
 }

@@ -1,0 +1,1254 @@
+// sp_sqfree.cu — sqfree+spinor and hierarchical-Vilenkin caches on sm_100a:
+// compress, decompress and (sqfree) fused decode attention, plus the
+// reference-named C-ABI of shannon_prime_cuda.h.
+//
+// Both paths share one pipeline (reference shannon_prime_sqfree.cu:750-1069,
+// shannon_prime_hier.cu:399-571), here fused into single kernels instead of
+// the reference's ~10 launches per vector:
+//   write: pad head_dim -> pad_dim with the mean; staged Vilenkin (prime
+//          Hartley) transform; skeleton coefficients band-quantised; the
+//          other coefficients predicted from the skeleton (sqfree: Möbius CSR
+//          sum with the spinor sheet bit; hier: W . skeleton with fp16 W);
+//          deviation magnitude; residual levels packed LSB-first.
+//   read:  the inverse, predictions taken from the dequantised skeleton.
+// One warp per vector; the padded vector lives in shared memory for the
+// transform (stages of p = 2, 3, 5, 7, 11 at growing strides), every other
+// intermediate in registers or a per-warp shared buffer; the packed slot is
+// assembled in shared memory with bitwise ORs and stored by the warp.
+//
+// Exactness: every float step is the single operation the CPU restatement
+// performs (the transform's cas table is built on the host in double and
+// rounded once; each output is an fma chain over j ascending, then one
+// multiply by 1/sqrt(p); sums over lanes use the fixed "lane tree": lane l
+// sums elements l, l+32, ... in order, then an xor butterfly), so packed
+// skeleton codes, magnitudes, residual levels and sheet bits are
+// bit-identical to the CPU path.
+#include "sp_internal.cuh"
+
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <vector>
+
+namespace {
+
+constexpr int kSqMaxPd = 512;
+constexpr int kSqWarps = 8;
+constexpr int kSqRowWords = 160;     // per-warp slot buffer (640 B)
+constexpr int kSqMaxStages = 8;
+
+// Transform and layout description passed by value to every kernel.
+struct SpSqDev {
+    int hd, pd, nf;
+    int p[kSqMaxStages];
+    int cas_off[kSqMaxStages];
+    float isp[kSqMaxStages];
+    float cas[224];                   // concatenated p x p tables (2,3,5,7,11: 208)
+    int n_skel, n_res, n_terms;
+    int res_bits, use_spinor, hier;
+    int mag_off, res_off, sheet_off, bytes_per_pos;
+    SpBandLayout bl;                  // skeleton bands (bl.n = n_skel)
+    const int *tables;                // skel_idx[n_skel], res_idx[n_res], csr_off[n_res+1], csr_term[n_terms]
+};
+
+__host__ __device__ inline int tab_skel(const SpSqDev &) { return 0; }
+__host__ __device__ inline int tab_res(const SpSqDev &t) { return t.n_skel; }
+__host__ __device__ inline int tab_csr_off(const SpSqDev &t) { return t.n_skel + t.n_res; }
+__host__ __device__ inline int tab_csr_term(const SpSqDev &t) { return 2 * t.n_res + t.n_skel + 1; }
+__host__ __device__ inline int tab_len(const SpSqDev &t) { return 2 * t.n_res + t.n_skel + 1 + t.n_terms; }
+
+// ------------------------------------------------------------- device --
+
+// Sum over the warp in the lane-tree order (all lanes get the result).
+__device__ __forceinline__ float lane_tree_reduce(float s)
+{
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) s = s + __shfl_xor_sync(0xffffffffu, s, off);
+    return s;
+}
+
+// One Vilenkin stage of prime P at the given stride: every group of P
+// elements (stride apart) becomes its P x P Hartley transform.
+template <int P>
+__device__ __forceinline__ void vilenkin_stage(float *buf, int pd, int stride, const float *cas, float isp,
+                                               int lane)
+{
+    const int bs = stride * P;
+    const int groups = pd / P;
+    for (int g = lane; g < groups; g += 32) {
+        const int blk = g / stride, o = g - blk * stride;
+        const int base = blk * bs + o;
+        float x[P], y[P];
+#pragma unroll
+        for (int j = 0; j < P; j++) x[j] = buf[base + j * stride];
+#pragma unroll
+        for (int k = 0; k < P; k++) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int j = 0; j < P; j++) acc = __fmaf_rn(cas[k * P + j], x[j], acc);
+            y[k] = __fmul_rn(acc, isp);
+        }
+#pragma unroll
+        for (int k = 0; k < P; k++) buf[base + k * stride] = y[k];
+    }
+}
+
+// In-place staged Vilenkin transform of buf[0..pd) by one warp: primes in
+// ascending order, strides growing (reference shannon_prime_sqfree.cu:66-106).
+__device__ void vilenkin_warp(float *buf, const SpSqDev &t, const float *cas_s, int lane)
+{
+    int stride = 1;
+    for (int st = 0; st < t.nf; st++) {
+        const float *cas = cas_s + t.cas_off[st];
+        switch (t.p[st]) {
+        case 2:  vilenkin_stage<2>(buf, t.pd, stride, cas, t.isp[st], lane); break;
+        case 3:  vilenkin_stage<3>(buf, t.pd, stride, cas, t.isp[st], lane); break;
+        case 5:  vilenkin_stage<5>(buf, t.pd, stride, cas, t.isp[st], lane); break;
+        case 7:  vilenkin_stage<7>(buf, t.pd, stride, cas, t.isp[st], lane); break;
+        default: vilenkin_stage<11>(buf, t.pd, stride, cas, t.isp[st], lane); break;
+        }
+        __syncwarp();
+        stride *= t.p[st];
+    }
+}
+
+// OR the low `bits` bits of v into the packed row at bit position pos.
+__device__ __forceinline__ void row_or(uint32_t *row, int pos, uint32_t v, int bits)
+{
+    const int w = pos >> 5, sh = pos & 31;
+    if (v == 0) return;
+    atomicOr(&row[w], v << sh);
+    if (sh + bits > 32) atomicOr(&row[w + 1], v >> (32 - sh));
+}
+
+__device__ __forceinline__ uint32_t row_bits(const uint32_t *row, int pos, int bits)
+{
+    const int w = pos >> 5, sh = pos & 31;
+    uint32_t v = row[w] >> sh;
+    if (sh + bits > 32) v |= row[w + 1] << (32 - sh);
+    return v & ((1u << bits) - 1u);
+}
+
+__device__ __forceinline__ float row_f16(const uint32_t *row, int byte)
+{
+    const unsigned short h = (unsigned short)row_bits(row, 8 * byte, 16);
+    float f = __half2float(__ushort_as_half(h));
+    return isfinite(f) ? f : 0.0f;
+}
+
+// Band of skeleton value s.
+__device__ __forceinline__ int band_of_s(const SpBandLayout &bl, int s)
+{
+    int b = 0;
+#pragma unroll 1
+    for (int k = 1; k < bl.n_bands; k++)
+        if (s >= bl.off[k]) b = k;
+    return b;
+}
+
+// Band-quantise skel[0..n_skel) (shared) into the row (the ship quantiser:
+// amax / max_val -> fp16 scale, codes rint(x / stored scale) + max_val).
+__device__ void quantize_skeleton(const float *skel, uint32_t *row, const SpBandLayout &bl, int lane)
+{
+    for (int b = 0; b < bl.n_bands; b++) {
+        const int off = bl.off[b], sz = bl.size[b], bits = bl.bits[b];
+        float amax = 0.0f;
+        for (int i = lane; i < sz; i += 32) amax = fmaxf(amax, fabsf(skel[off + i]));
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const int max_val = (1 << (bits - 1)) - 1;
+        const float scale = amax > 0.0f ? __fdiv_rn(amax, (float)max_val) : 0.0f;
+        const __half hs = __float2half_rn(scale);
+        const float stored = __half2float(hs);
+        const float inv = stored > 0.0f ? __frcp_rn(stored) : 0.0f;
+        const int base = 8 * (bl.byte_off[b] + 2);
+        for (int i = lane; i < sz; i += 32) {
+            int q = __float2int_rn(__fmul_rn(skel[off + i], inv));
+            q = q > max_val ? max_val : (q < -max_val ? -max_val : q);
+            row_or(row, base + i * bits, (uint32_t)(q + max_val), bits);
+        }
+        if (lane == 0) row_or(row, 8 * bl.byte_off[b], (uint32_t)__half_as_ushort(hs), 16);
+    }
+}
+
+// Dequantised skeleton value s from the row (partial bands never apply).
+__device__ __forceinline__ float dequant_skel(const uint32_t *row, const SpBandLayout &bl, int s)
+{
+    const int b = band_of_s(bl, s);
+    const int bits = bl.bits[b];
+    const int max_val = (1 << (bits - 1)) - 1;
+    const float scale = row_f16(row, bl.byte_off[b]);
+    const uint32_t u = row_bits(row, 8 * (bl.byte_off[b] + 2) + (s - bl.off[b]) * bits, bits);
+    return __fmul_rn((float)((int)u - max_val), scale);
+}
+
+// Sqfree Möbius prediction of residual r from skeleton values (shared).
+__device__ __forceinline__ float csr_predict(const int *csr_off, const int *csr_term, const float *skel, int r)
+{
+    float p = 0.0f;
+    for (int k = csr_off[r]; k < csr_off[r + 1]; k++) {
+        const int term = csr_term[k];
+        const float v = skel[term >> 1];
+        p = (term & 1) ? __fsub_rn(p, v) : __fadd_rn(p, v);
+    }
+    return p;
+}
+
+__device__ __forceinline__ float hier_predict(const float *W, const float *skel, int n_skel, int r)
+{
+    const float *w = W + (size_t)r * n_skel;
+    float acc = 0.0f;
+    for (int s = 0; s < n_skel; s++) acc = __fmaf_rn(w[s], skel[s], acc);
+    return acc;
+}
+
+struct SqIo {
+    const void *in;              // write: [n_layers][n_tokens][nh][hd]
+    float *out;                  // read:  [n_layers][n_pos][nh][hd] or [n_pos][hd] (one slot)
+    uint8_t *cache;              // slab base
+    long long slot_stride;       // bytes per slot
+    int layer0, n_layers, nh, start_pos, n_tok;
+    int tokens_per_cta;
+    int store_width;             // 4, 2 or 1
+    const __half *W;             // hier: [n_slots][n_res][n_skel]
+    int single_slot;             // read of one (layer, head): output [n_pos][hd]
+};
+
+size_t sq_smem_bytes(const SpSqDev &t)
+{
+    size_t s = (size_t)tab_len(t) * 4 + 224 * 4;
+    s += (size_t)kSqWarps * (t.pd + t.n_skel + t.n_res + 4) * 4;   // buf, skel, dev
+    s += (size_t)kSqWarps * kSqRowWords * 4;
+    if (t.hier) s += (size_t)t.n_res * t.n_skel * 4;
+    return s + 64;
+}
+
+struct SqSmem {
+    int *tab;
+    float *cas;
+    float *buf, *skel, *dev;
+    uint32_t *row;
+    float *W;
+};
+
+__device__ SqSmem sq_carve(unsigned char *smem, const SpSqDev &t, int warp)
+{
+    SqSmem s;
+    s.tab = reinterpret_cast<int *>(smem);
+    s.cas = reinterpret_cast<float *>(s.tab + tab_len(t));
+    float *f = s.cas + 224;
+    const int per = t.pd + t.n_skel + t.n_res + 4;
+    float *mine = f + (size_t)warp * per;
+    s.buf = mine;
+    s.skel = mine + t.pd;
+    s.dev = s.skel + t.n_skel;
+    s.row = reinterpret_cast<uint32_t *>(f + (size_t)kSqWarps * per) + warp * kSqRowWords;
+    s.W = reinterpret_cast<float *>(reinterpret_cast<uint32_t *>(f + (size_t)kSqWarps * per) +
+                                    kSqWarps * kSqRowWords);
+    return s;
+}
+
+__device__ void sq_load_common(unsigned char *smem, const SpSqDev &t, const SqIo &io, int slot)
+{
+    SqSmem s0 = sq_carve(smem, t, 0);
+    for (int i = threadIdx.x; i < tab_len(t); i += blockDim.x) s0.tab[i] = t.tables[i];
+    for (int i = threadIdx.x; i < 224; i += blockDim.x) s0.cas[i] = t.cas[i];
+    if (t.hier) {
+        const __half *w = io.W + (size_t)slot * t.n_res * t.n_skel;
+        for (int i = threadIdx.x; i < t.n_res * t.n_skel; i += blockDim.x) s0.W[i] = __half2float(w[i]);
+    }
+    __syncthreads();
+}
+
+// Compress.  Grid: x = token chunks, y = slot within the call (layer-major).
+template <typename Tin>
+__global__ void __launch_bounds__(kSqWarps * 32)
+k_sq_encode(SpSqDev t, SqIo io)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int li = blockIdx.y / io.nh, h = blockIdx.y % io.nh;
+    const int slot = (io.layer0 + li) * io.nh + h;
+    sq_load_common(smem, t, io, slot);
+    SqSmem S = sq_carve(smem, t, warp);
+    const int *skel_idx = S.tab + tab_skel(t), *res_idx = S.tab + tab_res(t);
+    const int *csr_off = S.tab + tab_csr_off(t), *csr_term = S.tab + tab_csr_term(t);
+    const int words = (t.bytes_per_pos + 3) >> 2;
+    const int tb = blockIdx.x * io.tokens_per_cta;
+    const int te = min(io.n_tok, tb + io.tokens_per_cta);
+    for (int tok = tb + warp; tok < te; tok += kSqWarps) {
+        const Tin *src = reinterpret_cast<const Tin *>(io.in) +
+                         (((long long)li * io.n_tok + tok) * io.nh + h) * t.hd;
+        // pad with the lane-tree mean
+        float sum = 0.0f;
+        for (int i = lane; i < t.hd; i += 32) {
+            const float x = sp_load_as_float(src, i);
+            S.buf[i] = x;
+            sum = __fadd_rn(sum, x);
+        }
+        const float mean = __fdiv_rn(lane_tree_reduce(sum), (float)t.hd);
+        for (int i = t.hd + lane; i < t.pd; i += 32) S.buf[i] = mean;
+        for (int j = lane; j < words; j += 32) S.row[j] = 0u;
+        __syncwarp();
+        vilenkin_warp(S.buf, t, S.cas, lane);
+        for (int s = lane; s < t.n_skel; s += 32) S.skel[s] = S.buf[skel_idx[s]];
+        __syncwarp();
+        quantize_skeleton(S.skel, S.row, t.bl, lane);
+        if (t.n_res > 0) {
+            float asum = 0.0f;
+            for (int r = lane; r < t.n_res; r += 32) {
+                const float a = S.buf[res_idx[r]];
+                float d;
+                if (t.hier) {
+                    d = __fsub_rn(a, hier_predict(S.W, S.skel, t.n_skel, r));
+                } else {
+                    const float p = csr_predict(csr_off, csr_term, S.skel, r);
+                    if (t.use_spinor) {
+                        const float vp = __fsub_rn(a, p), vm = __fadd_rn(a, p);
+                        const bool use_minus = fabsf(vm) < fabsf(vp);
+                        d = use_minus ? vm : vp;
+                        if (use_minus) row_or(S.row, 8 * t.sheet_off + r, 1u, 1);
+                    } else {
+                        d = __fsub_rn(a, p);
+                    }
+                }
+                S.dev[r] = d;
+                asum = __fadd_rn(asum, fabsf(d));
+            }
+            float mag = __fdiv_rn(lane_tree_reduce(asum), (float)t.n_res);
+            if (mag < 1e-12f) mag = 1e-12f;
+            const int L = 1 << t.res_bits;
+            float inv, center;
+            if (t.hier) {
+                const float step = __fdiv_rn(__fmul_rn(2.0f, mag), (float)(L - 1));
+                center = __fdiv_rn((float)(L - 1), 2.0f);
+                inv = step > 0.0f ? __frcp_rn(step) : 0.0f;
+            } else {
+                center = __fmul_rn(0.5f, (float)(L - 1));
+                const float sat = __fmul_rn(mag, (float)t.res_bits);
+                const float step = __fdiv_rn(__fmul_rn(2.0f, sat), (float)(L - 1));
+                inv = __frcp_rn(step);
+            }
+            __syncwarp();
+            for (int r = lane; r < t.n_res; r += 32) {
+                const float q = __fmaf_rn(S.dev[r], inv, center);
+                int level = t.hier ? __float2int_rn(q) : (int)__fadd_rn(q, 0.5f);
+                level = level < 0 ? 0 : (level >= L ? L - 1 : level);
+                row_or(S.row, 8 * t.res_off + r * t.res_bits, (uint32_t)level, t.res_bits);
+            }
+            if (lane == 0) row_or(S.row, 8 * t.mag_off, __float_as_uint(mag) & 0xffffu, 16),
+                           row_or(S.row, 8 * t.mag_off + 16, __float_as_uint(mag) >> 16, 16);
+        }
+        __syncwarp();
+        uint8_t *dst = io.cache + (long long)slot * io.slot_stride +
+                       (long long)(io.start_pos + tok) * t.bytes_per_pos;
+        if (io.store_width == 4) {
+            for (int j = lane; j < (t.bytes_per_pos >> 2); j += 32) reinterpret_cast<uint32_t *>(dst)[j] = S.row[j];
+        } else if (io.store_width == 2) {
+            const uint16_t *r16 = reinterpret_cast<const uint16_t *>(S.row);
+            for (int j = lane; j < (t.bytes_per_pos >> 1); j += 32) reinterpret_cast<uint16_t *>(dst)[j] = r16[j];
+        } else {
+            const uint8_t *r8 = reinterpret_cast<const uint8_t *>(S.row);
+            for (int j = lane; j < t.bytes_per_pos; j += 32) dst[j] = r8[j];
+        }
+        __syncwarp();
+    }
+}
+
+// Load a packed slot into the warp's row buffer.
+__device__ __forceinline__ void load_row(uint32_t *row, const uint8_t *src, int bytes, int width, int lane)
+{
+    if (width == 4) {
+        for (int j = lane; j < (bytes >> 2); j += 32) row[j] = reinterpret_cast<const uint32_t *>(src)[j];
+        if ((bytes & 3) && lane == 0) {
+            uint32_t w = 0;
+            for (int k = bytes & ~3; k < bytes; k++) w |= (uint32_t)src[k] << (8 * (k & 3));
+            row[bytes >> 2] = w;
+        }
+    } else {
+        uint8_t *r8 = reinterpret_cast<uint8_t *>(row);
+        for (int j = lane; j < bytes; j += 32) r8[j] = src[j];
+    }
+    if (lane == 0) row[(bytes + 3) >> 2] = 0u;
+}
+
+// Coefficient vector of one packed slot into buf[0..pd) (before the inverse
+// transform).  skel/dev are per-warp shared scratch.
+__device__ void sq_coeffs(const SpSqDev &t, const SqSmem &S, const float *W, int lane)
+{
+    const int *skel_idx = S.tab + tab_skel(t), *res_idx = S.tab + tab_res(t);
+    const int *csr_off = S.tab + tab_csr_off(t), *csr_term = S.tab + tab_csr_term(t);
+    for (int i = lane; i < t.pd; i += 32) S.buf[i] = 0.0f;
+    for (int s = lane; s < t.n_skel; s += 32) S.skel[s] = dequant_skel(S.row, t.bl, s);
+    __syncwarp();
+    for (int s = lane; s < t.n_skel; s += 32) S.buf[skel_idx[s]] = S.skel[s];
+    if (t.n_res > 0) {
+        const float mag = __uint_as_float(row_bits(S.row, 8 * t.mag_off, 16) |
+                                          (row_bits(S.row, 8 * t.mag_off + 16, 16) << 16));
+        const int L = 1 << t.res_bits;
+        float step, center;
+        if (t.hier) {
+            step = __fdiv_rn(__fmul_rn(2.0f, mag), (float)(L - 1));
+            center = __fdiv_rn((float)(L - 1), 2.0f);
+        } else {
+            center = __fmul_rn(0.5f, (float)(L - 1));
+            const float sat = __fmul_rn(mag, (float)t.res_bits);
+            step = L > 1 ? __fdiv_rn(__fmul_rn(2.0f, sat), (float)(L - 1)) : 0.0f;
+        }
+        for (int r = lane; r < t.n_res; r += 32) {
+            const uint32_t lv = row_bits(S.row, 8 * t.res_off + r * t.res_bits, t.res_bits);
+            const float dev = __fmul_rn(__fsub_rn((float)lv, center), step);
+            float p;
+            if (t.hier) {
+                p = hier_predict(W, S.skel, t.n_skel, r);
+            } else {
+                p = csr_predict(csr_off, csr_term, S.skel, r);
+                if (t.use_spinor && row_bits(S.row, 8 * t.sheet_off + r, 1)) p = -p;
+            }
+            S.buf[res_idx[r]] = __fadd_rn(p, dev);
+        }
+    }
+    __syncwarp();
+}
+
+// Decompress.  Grid: x = position chunks, y = slot within the call.
+__global__ void __launch_bounds__(kSqWarps * 32)
+k_sq_decode(SpSqDev t, SqIo io)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int li = blockIdx.y / io.nh, h = blockIdx.y % io.nh;
+    const int slot = (io.layer0 + li) * io.nh + h;
+    sq_load_common(smem, t, io, slot);
+    SqSmem S = sq_carve(smem, t, warp);
+    const int tb = blockIdx.x * io.tokens_per_cta;
+    const int te = min(io.n_tok, tb + io.tokens_per_cta);
+    for (int tok = tb + warp; tok < te; tok += kSqWarps) {
+        const uint8_t *src = io.cache + (long long)slot * io.slot_stride +
+                             (long long)(io.start_pos + tok) * t.bytes_per_pos;
+        load_row(S.row, src, t.bytes_per_pos, io.store_width, lane);
+        __syncwarp();
+        sq_coeffs(t, S, S.W, lane);
+        vilenkin_warp(S.buf, t, S.cas, lane);
+        float *dst = io.single_slot ? io.out + (long long)tok * t.hd
+                                    : io.out + (((long long)li * io.n_tok + tok) * io.nh + h) * t.hd;
+        for (int i = lane; i < t.hd; i += 32) dst[i] = S.buf[i];
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------- fused decode (sqfree) --
+
+struct SqAttn {
+    const uint8_t *k_cache, *v_cache;
+    long long k_slot_stride, v_slot_stride;
+    const __half *q;
+    __half *out;
+    float *ws;                    // partials [n_layers][n_q][kSqMaxSplits][pd + 4]
+    int layer0, n_layers, n_kv_heads, n_q_heads, group, kv_len, chunk, n_splits;
+    float logit_scale;
+    int store_width_k, store_width_v;
+};
+
+constexpr int kSqMaxSplits = 64;
+constexpr int kSqAttnWarps = 4;
+
+__device__ __forceinline__ float *sq_partial(const SqAttn &a, int pd, int li, int qh, int split)
+{
+    return a.ws + (((long long)li * a.n_q_heads + qh) * kSqMaxSplits + split) * (pd + 4);
+}
+
+size_t sq_attn_smem(const SpSqDev &t, int G)
+{
+    return (size_t)tab_len(t) * 4 + 224 * 4 + (size_t)G * t.pd * 4 +
+           (size_t)kSqAttnWarps * ((t.pd + t.n_skel + t.n_res + 4) * 4 + kSqRowWords * 4) +
+           (size_t)kSqAttnWarps * 8 * (t.pd + 4) * 4 + 64;
+}
+
+// Scores and the V sum in the Vilenkin coefficient domain: the transform is
+// symmetric and self-inverse, so q . unpad(V(c)) = (V q_pad) . c with q_pad
+// the query zero-extended to pad_dim, and sum_t p_t unpad(V(c_t)) =
+// unpad(V(sum_t p_t c_t)).  One warp reconstructs one position's K
+// coefficients (skeleton slots, then the CSR-predicted residuals) and V
+// coefficients cooperatively.
+__global__ void __launch_bounds__(kSqAttnWarps * 32)
+k_sq_attn(SpSqDev tk, SpSqDev tv, SqAttn a)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int split = blockIdx.x, h = blockIdx.y, li = blockIdx.z;
+    const int layer = a.layer0 + li;
+    const int G = a.group, pd = tk.pd;
+    // shared layout: tables(K) | cas | q'[G][pd] | per-warp (buf, skel, dev, row) | acc
+    int *tab = reinterpret_cast<int *>(smem);
+    float *cas = reinterpret_cast<float *>(tab + tab_len(tk));
+    float *qp = cas + 224;
+    float *wbase = qp + G * pd;
+    const int per = pd + tk.n_skel + tk.n_res + 4;
+    SqSmem S;
+    S.tab = tab; S.cas = cas;
+    S.buf = wbase + warp * per;
+    S.skel = S.buf + pd;
+    S.dev = S.skel + tk.n_skel;
+    S.row = reinterpret_cast<uint32_t *>(wbase + kSqAttnWarps * per) + warp * kSqRowWords;
+    S.W = nullptr;
+    float *accs = reinterpret_cast<float *>(reinterpret_cast<uint32_t *>(wbase + kSqAttnWarps * per) +
+                                            kSqAttnWarps * kSqRowWords);   // [warps][G][pd + 4]
+    for (int i = threadIdx.x; i < tab_len(tk); i += blockDim.x) tab[i] = tk.tables[i];
+    for (int i = threadIdx.x; i < 224; i += blockDim.x) cas[i] = tk.cas[i];
+    __syncthreads();
+    // Transformed queries (zero-padded), base-2 logit scale folded in.
+    for (int g = warp; g < G; g += kSqAttnWarps) {
+        const __half *qg = a.q + ((long long)li * a.n_q_heads + h * G + g) * tk.hd;
+        float *b = qp + g * pd;
+        for (int i = lane; i < pd; i += 32) b[i] = i < tk.hd ? __half2float(qg[i]) : 0.0f;
+        __syncwarp();
+        vilenkin_warp(b, tk, cas, lane);
+        for (int i = lane; i < pd; i += 32) b[i] *= a.logit_scale * 1.4426950408889634f;
+    }
+    float *acc = accs + (size_t)warp * G * (pd + 4);
+    for (int i = lane; i < G * (pd + 4); i += 32) acc[i] = 0.0f;
+    __syncthreads();
+
+    float m[8], l[8];
+#pragma unroll
+    for (int g = 0; g < 8; g++) { m[g] = -INFINITY; l[g] = 0.0f; }
+    const long long slot = (long long)layer * a.n_kv_heads + h;
+    const int t_begin = split * a.chunk, t_end = min(a.kv_len, t_begin + a.chunk);
+    for (int tok = t_begin + warp; tok < t_end; tok += kSqAttnWarps) {
+        // K coefficients -> scores
+        load_row(S.row, a.k_cache + slot * a.k_slot_stride + (long long)tok * tk.bytes_per_pos,
+                 tk.bytes_per_pos, a.store_width_k, lane);
+        __syncwarp();
+        sq_coeffs(tk, S, nullptr, lane);
+        float s[8];
+#pragma unroll
+        for (int g = 0; g < 8; g++) {
+            float d = 0.0f;
+            if (g < G)
+                for (int i = lane; i < pd; i += 32) d = __fmaf_rn(qp[g * pd + i], S.buf[i], d);
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+            s[g] = d;
+        }
+        __syncwarp();
+        // V coefficients, accumulated with online-softmax weights
+        load_row(S.row, a.v_cache + slot * a.v_slot_stride + (long long)tok * tv.bytes_per_pos,
+                 tv.bytes_per_pos, a.store_width_v, lane);
+        __syncwarp();
+        sq_coeffs(tv, S, nullptr, lane);
+#pragma unroll
+        for (int g = 0; g < 8; g++) {
+            if (g >= G) break;
+            const float mn = fmaxf(m[g], s[g]);
+            const float alpha = exp2f(m[g] - mn), p = exp2f(s[g] - mn);
+            l[g] = l[g] * alpha + p;
+            m[g] = mn;
+            float *ag = acc + g * (pd + 4);
+            for (int i = lane; i < pd; i += 32) ag[4 + i] = ag[4 + i] * alpha + p * S.buf[i];
+        }
+        __syncwarp();
+    }
+    if (lane == 0)
+        for (int g = 0; g < G; g++) { acc[g * (pd + 4)] = m[g]; acc[g * (pd + 4) + 1] = l[g]; }
+    __syncthreads();
+    for (int g = 0; g < G; g++) {
+        float M = -INFINITY;
+        for (int w = 0; w < kSqAttnWarps; w++) M = fmaxf(M, accs[((size_t)w * G + g) * (pd + 4)]);
+        float *part = sq_partial(a, pd, li, h * G + g, split);
+        for (int i = threadIdx.x; i < pd + 1; i += blockDim.x) {
+            float v = 0.0f;
+            for (int w = 0; w < kSqAttnWarps; w++) {
+                const float *aw = accs + ((size_t)w * G + g) * (pd + 4);
+                const float wt = aw[0] == -INFINITY ? 0.0f : exp2f(aw[0] - M);
+                v += wt * (i < pd ? aw[4 + i] : aw[1]);
+            }
+            if (i < pd) part[4 + i] = v;
+            else { part[0] = M; part[1] = v; }
+        }
+    }
+}
+
+__global__ void k_sq_attn_combine(SpSqDev t, SqAttn a)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    float *cas = reinterpret_cast<float *>(smem);
+    float *buf = cas + 224;
+    const int lane = threadIdx.x & 31;
+    const int qh = blockIdx.x, li = blockIdx.y;
+    for (int i = lane; i < 224; i += 32) cas[i] = t.cas[i];
+    float M = -INFINITY;
+    for (int s = 0; s < a.n_splits; s++) M = fmaxf(M, sq_partial(a, t.pd, li, qh, s)[0]);
+    for (int i = lane; i < t.pd; i += 32) buf[i] = 0.0f;
+    float L = 0.0f;
+    for (int s = 0; s < a.n_splits; s++) {
+        const float *p = sq_partial(a, t.pd, li, qh, s);
+        if (p[0] == -INFINITY) continue;
+        const float w = exp2f(p[0] - M);
+        L += w * p[1];
+        for (int i = lane; i < t.pd; i += 32) buf[i] += w * p[4 + i];
+    }
+    __syncwarp();
+    vilenkin_warp(buf, t, cas, lane);
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+    __half *o = a.out + ((long long)li * a.n_q_heads + qh) * t.hd;
+    for (int i = lane; i < t.hd; i += 32) o[i] = __float2half_rn(buf[i] * inv);
+}
+
+// --------------------------------------------------------------- host --
+
+bool sq_squarefree(int m)
+{
+    for (int p = 2; p * p <= m; p++)
+        if (m % (p * p) == 0) return false;
+    return true;
+}
+
+int sq_mu(int m)
+{
+    int k = 0;
+    for (int p = 2; p * p <= m; p++) {
+        if (m % p == 0) {
+            m /= p;
+            if (m % p == 0) return 0;
+            k++;
+        }
+    }
+    if (m > 1) k++;
+    return (k & 1) ? -1 : 1;
+}
+
+// Smallest squarefree {2,3,5,7,11}-smooth number >= hd.
+int sq_pad_dim(int hd)
+{
+    for (int m = hd > 1 ? hd : 2; m <= 4 * kSqMaxPd; m++) {
+        if (!sq_squarefree(m)) continue;
+        int r = m;
+        for (int p : {2, 3, 5, 7, 11})
+            if (r % p == 0) r /= p;
+        if (r == 1) return m;
+    }
+    return -1;
+}
+
+// Fill the transform part of t for pad_dim pd.
+int sq_fill_transform(SpSqDev &t, int pd)
+{
+    t.pd = pd;
+    t.nf = 0;
+    int r = pd, off = 0;
+    for (int p : {2, 3, 5, 7, 11}) {
+        while (r % p == 0) {
+            if (t.nf >= kSqMaxStages) return -1;
+            t.p[t.nf] = p;
+            t.cas_off[t.nf] = off;
+            t.isp[t.nf] = (float)(1.0 / sqrt((double)p));
+            bool seen = false;
+            for (int k = 0; k < t.nf; k++)
+                if (t.p[k] == p) { t.cas_off[t.nf] = t.cas_off[k]; seen = true; }
+            if (!seen) {
+                if (off + p * p > 224) return -1;
+                for (int k = 0; k < p; k++)
+                    for (int j = 0; j < p; j++) {
+                        const double ang = 2.0 * 3.14159265358979323846 * (double)((k * j) % p) / (double)p;
+                        t.cas[off + k * p + j] = (float)(cos(ang) + sin(ang));
+                    }
+                off += p * p;
+            }
+            t.nf++;
+            r /= p;
+        }
+    }
+    return r == 1 ? 0 : -1;
+}
+
+int store_width_for(int bytes, long long stride, const void *base)
+{
+    const uintptr_t x = (uintptr_t)bytes | (uintptr_t)stride | (uintptr_t)base;
+    return (x & 3) == 0 ? 4 : ((x & 1) == 0 ? 2 : 1);
+}
+
+int sq_launch_encode(const SpSqDev &t, SqIo io, int dtype, cudaStream_t s)
+{
+    if (io.n_tok <= 0 || io.n_layers <= 0) return SP_OK;
+    const size_t sm = sq_smem_bytes(t);
+    io.store_width = store_width_for(t.bytes_per_pos, io.slot_stride, io.cache);
+    const int slots = io.n_layers * io.nh;
+    // enough CTAs for ~4 waves of 148 SMs, at least one warp-round each
+    int chunks = (148 * 4 + slots - 1) / slots;
+    const int max_chunks = (io.n_tok + kSqWarps - 1) / kSqWarps;
+    if (chunks > max_chunks) chunks = max_chunks;
+    if (chunks < 1) chunks = 1;
+    io.tokens_per_cta = (io.n_tok + chunks - 1) / chunks;
+    dim3 grid(chunks, slots);
+    switch (dtype) {
+    case SP_DTYPE_F32: {
+        auto k = k_sq_encode<float>;
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        k<<<grid, kSqWarps * 32, sm, s>>>(t, io);
+        break;
+    }
+    case SP_DTYPE_F16: {
+        auto k = k_sq_encode<__half>;
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        k<<<grid, kSqWarps * 32, sm, s>>>(t, io);
+        break;
+    }
+    case SP_DTYPE_BF16: {
+        auto k = k_sq_encode<__nv_bfloat16>;
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        k<<<grid, kSqWarps * 32, sm, s>>>(t, io);
+        break;
+    }
+    default: return sp_set_error(SP_ERR_ARG, "sqfree/hier write: unknown dtype %d", dtype);
+    }
+    return sp_check_cuda(cudaGetLastError(), "sqfree/hier encode launch");
+}
+
+int sq_launch_decode(const SpSqDev &t, SqIo io, cudaStream_t s)
+{
+    if (io.n_tok <= 0 || io.n_layers <= 0) return SP_OK;
+    const size_t sm = sq_smem_bytes(t);
+    io.store_width = store_width_for(t.bytes_per_pos, io.slot_stride, io.cache);
+    const int slots = io.n_layers * io.nh;
+    int chunks = (148 * 4 + slots - 1) / slots;
+    const int max_chunks = (io.n_tok + kSqWarps - 1) / kSqWarps;
+    if (chunks > max_chunks) chunks = max_chunks;
+    if (chunks < 1) chunks = 1;
+    io.tokens_per_cta = (io.n_tok + chunks - 1) / chunks;
+    cudaFuncSetAttribute(k_sq_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    k_sq_decode<<<dim3(chunks, slots), kSqWarps * 32, sm, s>>>(t, io);
+    return sp_check_cuda(cudaGetLastError(), "sqfree/hier decode launch");
+}
+
+// Host copy of the kernel description of a cache half (K or V).
+struct SqHost {
+    SpSqDev t;
+};
+
+int sq_build_desc(SpSqDev &t, int hd, int pd, int n_skel, int n_res, int n_terms,
+                  const sp_band_config_t &bands, int res_bits, int use_spinor, int hier,
+                  const int *d_tables)
+{
+    memset(&t, 0, sizeof(t));
+    t.hd = hd;
+    if (sq_fill_transform(t, pd)) return -1;
+    t.n_skel = n_skel;
+    t.n_res = n_res;
+    t.n_terms = n_terms;
+    t.res_bits = res_bits;
+    t.use_spinor = use_spinor;
+    t.hier = hier;
+    t.bl = sp_layout_from(bands);
+    t.mag_off = t.bl.total_bytes;
+    t.res_off = t.mag_off + 4;
+    t.sheet_off = t.res_off + (n_res * res_bits + 7) / 8;
+    t.bytes_per_pos = t.sheet_off + (use_spinor ? (n_res + 7) / 8 : 0);
+    t.tables = d_tables;
+    return (t.bytes_per_pos + 3) / 4 + 2 <= kSqRowWords ? 0 : -1;
+}
+
+SpSqDev sq_desc(const sp_cuda_sqfree_cache_t *cc, int which)
+{
+    SpSqDev t;
+    sq_build_desc(t, cc->config.head_dim, cc->pad_dim, cc->sk_k, cc->n_res, cc->n_terms,
+                  which ? cc->v_bands : cc->k_bands, cc->residual_bits, cc->use_spinor, 0,
+                  (const int *)cc->d_tables);
+    return t;
+}
+
+SpSqDev hier_desc(const sp_cuda_hier_cache_t *hc)
+{
+    SpSqDev t;
+    sq_build_desc(t, hc->config.head_dim, hc->pad_dim, hc->n_skeleton, hc->n_target, 0, hc->skel_bands,
+                  hc->target_res_bits, 0, 1, (const int *)hc->d_tables);
+    return t;
+}
+
+}  // namespace
+
+// ===================================================================== C-ABI
+
+extern "C" {
+
+int sp_cuda_sqfree_cache_init_ex(sp_cuda_sqfree_cache_t *cc, const sp_config_t *cfg, int max_seq_len,
+                                 int residual_bits, int use_spinor, float sk_frac, void *stream)
+{
+    sp_clear_error();
+    if (!cc || !cfg) return sp_set_error(SP_ERR_ARG, "sqfree_cache_init: NULL argument");
+    memset(cc, 0, sizeof(*cc));
+    if (cfg->n_layers <= 0 || cfg->n_heads_kv <= 0 || max_seq_len <= 0 || cfg->head_dim < 1)
+        return sp_set_error(SP_ERR_ARG, "sqfree_cache_init: bad dims");
+    if (residual_bits < 1 || residual_bits > 8)
+        return sp_set_error(SP_ERR_ARG, "sqfree_cache_init: residual_bits %d outside 1..8", residual_bits);
+    const int pd = sq_pad_dim(cfg->head_dim);
+    if (pd < 0 || pd > kSqMaxPd)
+        return sp_set_error(SP_ERR_UNSUPPORTED, "sqfree_cache_init: head_dim %d has no pad_dim <= %d",
+                            cfg->head_dim, kSqMaxPd);
+    int sk_k = sk_frac > 0.0f ? (int)floor((double)sk_frac * pd) : pd / 2;
+    if (sk_k < 1) sk_k = 1;
+    if (sk_k > pd) sk_k = pd;
+    cc->config = *cfg;
+    cc->pad_dim = pd;
+    cc->sk_k = sk_k;
+    cc->n_res = pd - sk_k;
+    cc->residual_bits = residual_bits;
+    cc->use_spinor = use_spinor ? 1 : 0;
+    cc->max_seq_len = max_seq_len;
+    cc->n_slots = cfg->n_layers * cfg->n_heads_kv;
+    cc->stream = stream;
+    cudaGetDevice(&cc->device);
+    // skeleton bands over sk_k; default 5,4,4,4,5 (shannon_prime_sqfree.cu:614-623)
+    const int defb[5] = {5, 4, 4, 4, 5};
+    int kb[SP_MAX_BANDS], vb[SP_MAX_BANDS];
+    const int knb = (cfg->k_n_bands > 0 && cfg->k_n_bands <= SP_MAX_BANDS) ? cfg->k_n_bands : 5;
+    const int vnb = (cfg->v_n_bands > 0 && cfg->v_n_bands <= SP_MAX_BANDS) ? cfg->v_n_bands : 5;
+    for (int i = 0; i < knb; i++) kb[i] = cfg->k_band_bits[i] > 0 ? cfg->k_band_bits[i] : defb[i % 5];
+    for (int i = 0; i < vnb; i++) vb[i] = cfg->v_band_bits[i] > 0 ? cfg->v_band_bits[i] : defb[i % 5];
+    if (sp_band_config_init(&cc->k_bands, sk_k, knb, kb) || sp_band_config_init(&cc->v_bands, sk_k, vnb, vb))
+        return sp_set_error(SP_ERR_ARG, "sqfree_cache_init: bad band configuration");
+    // Knight mask: squarefree-first ranking, Möbius CSR over proper divisors.
+    std::vector<int> rank, skel(sk_k), res, off, term;
+    for (int i = 0; i < pd; i++) if (sq_squarefree(i + 1)) rank.push_back(i);
+    for (int i = 0; i < pd; i++) if (!sq_squarefree(i + 1)) rank.push_back(i);
+    std::vector<int> slot_of(pd, -1);
+    for (int s = 0; s < sk_k; s++) { skel[s] = rank[s]; slot_of[rank[s]] = s; }
+    for (int i = 0; i < pd; i++) if (slot_of[i] < 0) res.push_back(i);
+    std::vector<int> csr_slot, csr_sign;
+    for (int r = 0; r < (int)res.size(); r++) {
+        off.push_back((int)term.size());
+        const int n = res[r] + 1;
+        for (int d = 1; d < n; d++) {
+            if (n % d) continue;
+            const int mu = sq_mu(n / d);
+            if (!mu || slot_of[d - 1] < 0) continue;
+            term.push_back((slot_of[d - 1] << 1) | (mu < 0 ? 1 : 0));
+            csr_slot.push_back(slot_of[d - 1]);
+            csr_sign.push_back(mu);
+        }
+    }
+    off.push_back((int)term.size());
+    cc->n_terms = (int)term.size();
+    std::vector<int> tables;
+    tables.insert(tables.end(), skel.begin(), skel.end());
+    tables.insert(tables.end(), res.begin(), res.end());
+    tables.insert(tables.end(), off.begin(), off.end());
+    tables.insert(tables.end(), term.begin(), term.end());
+    int factors[kSqMaxStages], nf = 0;
+    {
+        int r = pd;
+        for (int p : {2, 3, 5, 7, 11}) while (r % p == 0) { factors[nf++] = p; r /= p; }
+    }
+    cc->n_factors = nf;
+    SpSqDev tk;
+    const size_t k_total = (size_t)cc->n_slots * max_seq_len;
+    int rc = SP_OK;
+    auto up = [&](void **dst, const void *src, size_t bytes, const char *what) {
+        if (rc) return;
+        if ((rc = sp_check_cuda(cudaMalloc(dst, bytes > 0 ? bytes : 4), what))) return;
+        if (bytes) rc = sp_check_cuda(cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice), what);
+    };
+    up(&cc->d_tables, tables.data(), tables.size() * 4, "sqfree tables");
+    up((void **)&cc->d_skeleton_idx, skel.data(), skel.size() * 4, "skeleton idx");
+    up((void **)&cc->d_residual_idx, res.data(), res.size() * 4, "residual idx");
+    up((void **)&cc->d_csr_offsets, off.data(), off.size() * 4, "csr offsets");
+    up((void **)&cc->d_csr_skel_slot, csr_slot.data(), csr_slot.size() * 4, "csr slots");
+    up((void **)&cc->d_csr_mu_sign, csr_sign.data(), csr_sign.size() * 4, "csr signs");
+    up((void **)&cc->d_vilenkin_factors, factors, (size_t)nf * 4, "factors");
+    if (rc) { sp_cuda_sqfree_cache_free(cc); return rc; }
+    if (sq_build_desc(tk, cfg->head_dim, pd, sk_k, cc->n_res, cc->n_terms, cc->k_bands, residual_bits,
+                      cc->use_spinor, 0, (const int *)cc->d_tables)) {
+        sp_cuda_sqfree_cache_free(cc);
+        return sp_set_error(SP_ERR_UNSUPPORTED, "sqfree_cache_init: slot too large");
+    }
+    cc->bytes_per_pos_k = tk.bytes_per_pos;
+    cc->bytes_per_pos_v = sq_desc(cc, 1).bytes_per_pos;
+    if ((rc = sp_check_cuda(cudaMalloc(&cc->d_k_cache, k_total * cc->bytes_per_pos_k), "cudaMalloc K cache")) ||
+        (rc = sp_check_cuda(cudaMalloc(&cc->d_v_cache, k_total * cc->bytes_per_pos_v), "cudaMalloc V cache"))) {
+        sp_cuda_sqfree_cache_free(cc);
+        return rc;
+    }
+    cudaMemset(cc->d_k_cache, 0, k_total * cc->bytes_per_pos_k);
+    cudaMemset(cc->d_v_cache, 0, k_total * cc->bytes_per_pos_v);
+    cc->attn_ws_bytes = (size_t)cfg->n_layers * 8 * cfg->n_heads_kv * kSqMaxSplits * (pd + 4) * sizeof(float);
+    if ((rc = sp_check_cuda(cudaMalloc(&cc->d_attn_ws, cc->attn_ws_bytes), "cudaMalloc sqfree workspace")) ||
+        (rc = sp_check_cuda(cudaDeviceSynchronize(), "sqfree_cache_init"))) {
+        sp_cuda_sqfree_cache_free(cc);
+        return rc;
+    }
+    return SP_OK;
+}
+
+int sp_cuda_sqfree_cache_init(sp_cuda_sqfree_cache_t *cc, const sp_config_t *cfg, int max_seq_len,
+                              int residual_bits, int use_spinor, void *stream)
+{
+    return sp_cuda_sqfree_cache_init_ex(cc, cfg, max_seq_len, residual_bits, use_spinor, 0.0f, stream);
+}
+
+void sp_cuda_sqfree_cache_free(sp_cuda_sqfree_cache_t *cc)
+{
+    if (!cc) return;
+    cudaFree(cc->d_tables);
+    cudaFree(cc->d_skeleton_idx);
+    cudaFree(cc->d_residual_idx);
+    cudaFree(cc->d_csr_offsets);
+    cudaFree(cc->d_csr_skel_slot);
+    cudaFree(cc->d_csr_mu_sign);
+    cudaFree(cc->d_vilenkin_factors);
+    cudaFree(cc->d_k_cache);
+    cudaFree(cc->d_v_cache);
+    cudaFree(cc->d_attn_ws);
+    memset(cc, 0, sizeof(*cc));
+}
+
+static int sq_check(const sp_cuda_sqfree_cache_t *cc, int layer, int n_layers, int head, int pos, int n)
+{
+    if (!cc || !cc->d_k_cache) return sp_set_error(SP_ERR_ARG, "sqfree cache not initialised");
+    if (layer < 0 || n_layers < 0 || layer + n_layers > cc->config.n_layers || head < 0 ||
+        head >= cc->config.n_heads_kv)
+        return sp_set_error(SP_ERR_ARG, "sqfree: layer/head out of range");
+    if (pos < 0 || n < 0 || (long long)pos + n > cc->max_seq_len)
+        return sp_set_error(SP_ERR_ARG, "sqfree: positions [%d,%d) outside the cache", pos, pos + n);
+    return SP_OK;
+}
+
+static int sq_write(sp_cuda_sqfree_cache_t *cc, int which, int layer0, int n_layers, int head0, int nh,
+                    int start_pos, int n_tok, const void *d_in, int dtype)
+{
+    SpSqDev t = sq_desc(cc, which);
+    SqIo io;
+    memset(&io, 0, sizeof(io));
+    io.in = d_in;
+    io.cache = which ? cc->d_v_cache : cc->d_k_cache;
+    io.slot_stride = (long long)cc->max_seq_len * t.bytes_per_pos;
+    // a single-head write addresses slot (layer0*H + head0): shift the base
+    io.cache += (long long)head0 * io.slot_stride;
+    io.layer0 = layer0;
+    io.n_layers = n_layers;
+    io.nh = nh;
+    io.start_pos = start_pos;
+    io.n_tok = n_tok;
+    if (nh != cc->config.n_heads_kv) {
+        // one head: slot index (layer0 + li) * nh + h must map to layer*H + head0
+        io.layer0 = 0;
+        io.cache += (long long)layer0 * cc->config.n_heads_kv * io.slot_stride;
+        if (n_layers != 1) return sp_set_error(SP_ERR_ARG, "sqfree: per-head writes take one layer");
+    }
+    return sq_launch_encode(t, io, dtype, (cudaStream_t)cc->stream);
+}
+
+static int sq_read(const sp_cuda_sqfree_cache_t *cc, int which, int layer, int head, int start_pos, int n_pos,
+                   float *d_out)
+{
+    int rc = sq_check(cc, layer, 1, head, start_pos, n_pos);
+    if (rc) return rc;
+    SpSqDev t = sq_desc(cc, which);
+    SqIo io;
+    memset(&io, 0, sizeof(io));
+    io.out = d_out;
+    io.slot_stride = (long long)cc->max_seq_len * t.bytes_per_pos;
+    io.cache = (uint8_t *)(which ? cc->d_v_cache : cc->d_k_cache) +
+               ((long long)layer * cc->config.n_heads_kv + head) * io.slot_stride;
+    io.layer0 = 0;
+    io.n_layers = 1;
+    io.nh = 1;
+    io.start_pos = start_pos;
+    io.n_tok = n_pos;
+    io.single_slot = 1;
+    return sq_launch_decode(t, io, (cudaStream_t)cc->stream);
+}
+
+void sp_cuda_sqfree_write_k(sp_cuda_sqfree_cache_t *cc, int layer, int head, int pos, const float *d_k_vec)
+{
+    sp_clear_error();
+    if (sq_check(cc, layer, 1, head, pos, 1) || !d_k_vec) { if (!d_k_vec) sp_set_error(SP_ERR_ARG, "NULL vector"); return; }
+    sq_write(cc, 0, layer, 1, head, 1, pos, 1, d_k_vec, SP_DTYPE_F32);
+}
+
+void sp_cuda_sqfree_write_v(sp_cuda_sqfree_cache_t *cc, int layer, int head, int pos, const float *d_v_vec)
+{
+    sp_clear_error();
+    if (sq_check(cc, layer, 1, head, pos, 1) || !d_v_vec) { if (!d_v_vec) sp_set_error(SP_ERR_ARG, "NULL vector"); return; }
+    sq_write(cc, 1, layer, 1, head, 1, pos, 1, d_v_vec, SP_DTYPE_F32);
+}
+
+void sp_cuda_sqfree_read_k(const sp_cuda_sqfree_cache_t *cc, int layer, int head, int pos, float *d_k_out)
+{
+    sp_clear_error();
+    sq_read(cc, 0, layer, head, pos, 1, d_k_out);
+}
+
+void sp_cuda_sqfree_read_v(const sp_cuda_sqfree_cache_t *cc, int layer, int head, int pos, float *d_v_out)
+{
+    sp_clear_error();
+    sq_read(cc, 1, layer, head, pos, 1, d_v_out);
+}
+
+void sp_cuda_sqfree_read_k_batch(const sp_cuda_sqfree_cache_t *cc, int layer, int head, int start_pos,
+                                 int n_pos, float *d_k_out)
+{
+    sp_clear_error();
+    sq_read(cc, 0, layer, head, start_pos, n_pos, d_k_out);
+}
+
+void sp_cuda_sqfree_read_v_batch(const sp_cuda_sqfree_cache_t *cc, int layer, int head, int start_pos,
+                                 int n_pos, float *d_v_out)
+{
+    sp_clear_error();
+    sq_read(cc, 1, layer, head, start_pos, n_pos, d_v_out);
+}
+
+int sp_cuda_sqfree_write_kv_tokens(sp_cuda_sqfree_cache_t *cc, int layer0, int n_layers, int start_pos,
+                                   int n_tokens, const void *d_k, const void *d_v, int dtype)
+{
+    sp_clear_error();
+    int rc = sq_check(cc, layer0, n_layers, 0, start_pos, n_tokens);
+    if (rc) return rc;
+    const int H = cc->config.n_heads_kv;
+    if (d_k && (rc = sq_write(cc, 0, layer0, n_layers, 0, H, start_pos, n_tokens, d_k, dtype))) return rc;
+    if (d_v && (rc = sq_write(cc, 1, layer0, n_layers, 0, H, start_pos, n_tokens, d_v, dtype))) return rc;
+    return SP_OK;
+}
+
+int sp_cuda_sqfree_attn_decode(const sp_cuda_sqfree_cache_t *cc, int layer0, int n_layers, const void *d_q,
+                               int n_q_heads, int kv_len, float logit_scale, void *d_out, void *stream)
+{
+    sp_clear_error();
+    if (!cc || !cc->d_k_cache || !d_q || !d_out) return sp_set_error(SP_ERR_ARG, "sqfree_attn_decode: NULL argument");
+    const int H = cc->config.n_heads_kv;
+    if (layer0 < 0 || n_layers <= 0 || layer0 + n_layers > cc->config.n_layers)
+        return sp_set_error(SP_ERR_ARG, "sqfree_attn_decode: layers out of range");
+    if (n_q_heads <= 0 || n_q_heads % H || n_q_heads / H > 8)
+        return sp_set_error(SP_ERR_ARG, "sqfree_attn_decode: n_q_heads %d must be a multiple of %d with <= 8 per KV head",
+                            n_q_heads, H);
+    if (kv_len < 0 || kv_len > cc->max_seq_len)
+        return sp_set_error(SP_ERR_ARG, "sqfree_attn_decode: kv_len %d outside [0,%d]", kv_len, cc->max_seq_len);
+    SpSqDev tk = sq_desc(cc, 0), tv = sq_desc(cc, 1);
+    SqAttn a;
+    memset(&a, 0, sizeof(a));
+    a.k_cache = cc->d_k_cache;
+    a.v_cache = cc->d_v_cache;
+    a.k_slot_stride = (long long)cc->max_seq_len * tk.bytes_per_pos;
+    a.v_slot_stride = (long long)cc->max_seq_len * tv.bytes_per_pos;
+    a.q = (const __half *)d_q;
+    a.out = (__half *)d_out;
+    a.ws = (float *)cc->d_attn_ws;
+    a.layer0 = layer0;
+    a.n_layers = n_layers;
+    a.n_kv_heads = H;
+    a.n_q_heads = n_q_heads;
+    a.group = n_q_heads / H;
+    a.kv_len = kv_len;
+    a.logit_scale = logit_scale;
+    a.store_width_k = store_width_for(tk.bytes_per_pos, a.k_slot_stride, a.k_cache);
+    a.store_width_v = store_width_for(tv.bytes_per_pos, a.v_slot_stride, a.v_cache);
+    const int units = n_layers * H;
+    int splits = (148 * 8 + units - 1) / units;
+    const int max_by_len = (kv_len + 63) / 64;
+    if (splits > max_by_len) splits = max_by_len;
+    if (splits > kSqMaxSplits) splits = kSqMaxSplits;
+    if (splits < 1) splits = 1;
+    a.chunk = (kv_len + splits - 1) / splits;
+    a.n_splits = kv_len == 0 ? 0 : (kv_len + a.chunk - 1) / a.chunk;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (a.n_splits > 0) {
+        const size_t sm = sq_attn_smem(tk, a.group);
+        cudaFuncSetAttribute(k_sq_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        k_sq_attn<<<dim3(a.n_splits, H, n_layers), kSqAttnWarps * 32, sm, s>>>(tk, tv, a);
+        int rc = sp_check_cuda(cudaGetLastError(), "sqfree attention launch");
+        if (rc) return rc;
+    }
+    const size_t smc = (224 + tk.pd + 8) * sizeof(float);
+    k_sq_attn_combine<<<dim3(n_q_heads, n_layers), 32, smc, s>>>(tk, a);
+    return sp_check_cuda(cudaGetLastError(), "sqfree attention combine launch");
+}
+
+// ------------------------------------------------------------------ hier --
+
+int sp_cuda_hier_cache_init(sp_cuda_hier_cache_t *hc, const sp_config_t *cfg, int pad_dim, int n_skeleton,
+                            int n_target, int target_res_bits, const int *skeleton_idx, const int *target_idx,
+                            const sp_band_config_t *skel_bands, int max_seq_len, int n_slots, void *stream)
+{
+    sp_clear_error();
+    if (!hc || !cfg || !skeleton_idx || !target_idx || !skel_bands)
+        return sp_set_error(SP_ERR_ARG, "hier_cache_init: NULL argument");
+    memset(hc, 0, sizeof(*hc));
+    if (pad_dim < cfg->head_dim || pad_dim > kSqMaxPd || n_skeleton < 1 || n_target < 0 ||
+        n_skeleton + n_target > pad_dim || max_seq_len <= 0 || n_slots <= 0 ||
+        target_res_bits < 1 || target_res_bits > 8 || skel_bands->head_dim != n_skeleton)
+        return sp_set_error(SP_ERR_ARG, "hier_cache_init: bad dims");
+    hc->config = *cfg;
+    hc->pad_dim = pad_dim;
+    hc->n_skeleton = n_skeleton;
+    hc->n_target = n_target;
+    hc->target_res_bits = target_res_bits;
+    hc->n_slots = n_slots;
+    hc->max_seq_len = max_seq_len;
+    hc->skel_bands = *skel_bands;
+    hc->stream = stream;
+    cudaGetDevice(&hc->device);
+    std::vector<int> tables(skeleton_idx, skeleton_idx + n_skeleton);
+    tables.insert(tables.end(), target_idx, target_idx + n_target);
+    for (int r = 0; r <= n_target; r++) tables.push_back(0);      // empty CSR
+    for (int i = 0; i < n_skeleton + n_target; i++) {
+        const int v = tables[i];
+        if (v < 0 || v >= pad_dim) return sp_set_error(SP_ERR_ARG, "hier_cache_init: index %d outside pad_dim", v);
+    }
+    int factors[kSqMaxStages], nf = 0;
+    {
+        int r = pad_dim;
+        for (int p : {2, 3, 5, 7, 11}) while (r % p == 0 && nf < kSqMaxStages) { factors[nf++] = p; r /= p; }
+        if (r != 1) return sp_set_error(SP_ERR_UNSUPPORTED, "hier_cache_init: pad_dim %d not {2,3,5,7,11}-smooth", pad_dim);
+    }
+    hc->n_factors = nf;
+    int rc = SP_OK;
+    auto up = [&](void **dst, const void *src, size_t bytes, const char *what) {
+        if (rc) return;
+        if ((rc = sp_check_cuda(cudaMalloc(dst, bytes > 0 ? bytes : 4), what))) return;
+        if (bytes && src) rc = sp_check_cuda(cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice), what);
+    };
+    up(&hc->d_tables, tables.data(), tables.size() * 4, "hier tables");
+    up((void **)&hc->d_skeleton_idx, skeleton_idx, (size_t)n_skeleton * 4, "skeleton idx");
+    up((void **)&hc->d_target_idx, target_idx, (size_t)n_target * 4, "target idx");
+    up((void **)&hc->d_vilenkin_factors, factors, (size_t)nf * 4, "factors");
+    up((void **)&hc->d_skel_band_bits, skel_bands->band_bits, (size_t)skel_bands->n_bands * 4, "band bits");
+    if (rc) { sp_cuda_hier_cache_free(hc); return rc; }
+    SpSqDev t = hier_desc(hc);
+    if ((t.bytes_per_pos + 3) / 4 + 2 > kSqRowWords || sq_smem_bytes(t) > 220 * 1024) {
+        sp_cuda_hier_cache_free(hc);
+        return sp_set_error(SP_ERR_UNSUPPORTED, "hier_cache_init: slot or predictor too large");
+    }
+    hc->bytes_per_pos_k = hc->bytes_per_pos_v = t.bytes_per_pos;
+    const size_t total = (size_t)n_slots * max_seq_len * t.bytes_per_pos;
+    up((void **)&hc->d_k_cache, nullptr, total, "cudaMalloc K cache");
+    up((void **)&hc->d_v_cache, nullptr, total, "cudaMalloc V cache");
+    up((void **)&hc->d_W, nullptr, (size_t)n_slots * n_target * n_skeleton * 2, "cudaMalloc W");
+    if (rc) { sp_cuda_hier_cache_free(hc); return rc; }
+    cudaMemset(hc->d_k_cache, 0, total);
+    cudaMemset(hc->d_v_cache, 0, total);
+    cudaMemset(hc->d_W, 0, (size_t)n_slots * n_target * n_skeleton * 2);
+    if ((rc = sp_check_cuda(cudaDeviceSynchronize(), "hier_cache_init"))) { sp_cuda_hier_cache_free(hc); return rc; }
+    return SP_OK;
+}
+
+void sp_cuda_hier_cache_free(sp_cuda_hier_cache_t *hc)
+{
+    if (!hc) return;
+    cudaFree(hc->d_tables);
+    cudaFree(hc->d_skeleton_idx);
+    cudaFree(hc->d_target_idx);
+    cudaFree(hc->d_vilenkin_factors);
+    cudaFree(hc->d_skel_band_bits);
+    cudaFree(hc->d_k_cache);
+    cudaFree(hc->d_v_cache);
+    cudaFree(hc->d_W);
+    memset(hc, 0, sizeof(*hc));
+}
+
+int sp_cuda_hier_cache_upload_W(sp_cuda_hier_cache_t *hc, const uint16_t *W_all)
+{
+    sp_clear_error();
+    if (!hc || !hc->d_W || !W_all) return sp_set_error(SP_ERR_ARG, "hier_upload_W: NULL argument");
+    const size_t bytes = (size_t)hc->n_slots * hc->n_target * hc->n_skeleton * 2;
+    return sp_check_cuda(cudaMemcpy(hc->d_W, W_all, bytes, cudaMemcpyHostToDevice), "hier_upload_W");
+}
+
+static int hier_check(const sp_cuda_hier_cache_t *hc, int layer, int n_layers, int head, int pos, int n)
+{
+    if (!hc || !hc->d_k_cache) return sp_set_error(SP_ERR_ARG, "hier cache not initialised");
+    const int H = hc->config.n_heads_kv;
+    if (layer < 0 || n_layers < 0 || head < 0 || head >= H || (long long)(layer + n_layers) * H > hc->n_slots)
+        return sp_set_error(SP_ERR_ARG, "hier: layer/head out of range");
+    if (pos < 0 || n < 0 || (long long)pos + n > hc->max_seq_len)
+        return sp_set_error(SP_ERR_ARG, "hier: positions [%d,%d) outside the cache", pos, pos + n);
+    return SP_OK;
+}
+
+static int hier_io(const sp_cuda_hier_cache_t *hc, int which, int layer0, int n_layers, int head, int nh,
+                   int start_pos, int n_tok, SqIo &io)
+{
+    memset(&io, 0, sizeof(io));
+    const int H = hc->config.n_heads_kv;
+    io.slot_stride = (long long)hc->max_seq_len * hc->bytes_per_pos_k;
+    io.cache = which ? hc->d_v_cache : hc->d_k_cache;
+    io.W = (const __half *)hc->d_W;
+    io.layer0 = layer0;
+    io.n_layers = n_layers;
+    io.nh = nh;
+    io.start_pos = start_pos;
+    io.n_tok = n_tok;
+    if (nh != H) {            // single head: slot = layer0 * H + head
+        if (n_layers != 1) return sp_set_error(SP_ERR_ARG, "hier: per-head calls take one layer");
+        io.layer0 = layer0 * H + head;
+        io.nh = 1;
+    }
+    return SP_OK;
+}
+
+int sp_cuda_hier_write_kv_tokens(sp_cuda_hier_cache_t *hc, int layer0, int n_layers, int start_pos,
+                                 int n_tokens, const void *d_k, const void *d_v, int dtype)
+{
+    sp_clear_error();
+    int rc = hier_check(hc, layer0, n_layers, 0, start_pos, n_tokens);
+    if (rc) return rc;
+    SpSqDev t = hier_desc(hc);
+    const int H = hc->config.n_heads_kv;
+    for (int which = 0; which < 2; which++) {
+        const void *in = which ? d_v : d_k;
+        if (!in) continue;
+        SqIo io;
+        if ((rc = hier_io(hc, which, layer0, n_layers, 0, H, start_pos, n_tokens, io))) return rc;
+        io.in = in;
+        if ((rc = sq_launch_encode(t, io, dtype, (cudaStream_t)hc->stream))) return rc;
+    }
+    return SP_OK;
+}
+
+int sp_cuda_hier_read_kv_tokens(const sp_cuda_hier_cache_t *hc, int layer0, int n_layers, int start_pos,
+                                int n_pos, float *d_k_out, float *d_v_out)
+{
+    sp_clear_error();
+    int rc = hier_check(hc, layer0, n_layers, 0, start_pos, n_pos);
+    if (rc) return rc;
+    SpSqDev t = hier_desc(hc);
+    const int H = hc->config.n_heads_kv;
+    for (int which = 0; which < 2; which++) {
+        float *out = which ? d_v_out : d_k_out;
+        if (!out) continue;
+        SqIo io;
+        if ((rc = hier_io(hc, which, layer0, n_layers, 0, H, start_pos, n_pos, io))) return rc;
+        io.out = out;
+        if ((rc = sq_launch_decode(t, io, (cudaStream_t)hc->stream))) return rc;
+    }
+    return SP_OK;
+}
+
+static void hier_one(sp_cuda_hier_cache_t *hc, int which, int layer, int head, int pos, const float *in, float *out)
+{
+    sp_clear_error();
+    if (hier_check(hc, layer, 1, head, pos, 1)) return;
+    if (!in && !out) { sp_set_error(SP_ERR_ARG, "hier: NULL vector"); return; }
+    SpSqDev t = hier_desc(hc);
+    SqIo io;
+    if (hier_io(hc, which, layer, 1, head, 1, pos, 1, io)) return;
+    if (in) {
+        io.in = in;
+        sq_launch_encode(t, io, SP_DTYPE_F32, (cudaStream_t)hc->stream);
+    } else {
+        io.out = out;
+        io.single_slot = 1;
+        sq_launch_decode(t, io, (cudaStream_t)hc->stream);
+    }
+}
+
+void sp_cuda_hier_write_k(sp_cuda_hier_cache_t *hc, int layer, int head, int pos, const float *d_k_vec)
+{ hier_one(hc, 0, layer, head, pos, d_k_vec, nullptr); }
+void sp_cuda_hier_write_v(sp_cuda_hier_cache_t *hc, int layer, int head, int pos, const float *d_v_vec)
+{ hier_one(hc, 1, layer, head, pos, d_v_vec, nullptr); }
+void sp_cuda_hier_read_k(const sp_cuda_hier_cache_t *hc, int layer, int head, int pos, float *d_k_out)
+{ hier_one((sp_cuda_hier_cache_t *)hc, 0, layer, head, pos, nullptr, d_k_out); }
+void sp_cuda_hier_read_v(const sp_cuda_hier_cache_t *hc, int layer, int head, int pos, float *d_v_out)
+{ hier_one((sp_cuda_hier_cache_t *)hc, 1, layer, head, pos, nullptr, d_v_out); }
+
+}  // extern "C"

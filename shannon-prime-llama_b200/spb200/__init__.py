@@ -52,6 +52,44 @@ class SpCudaCache(C.Structure):
     ]
 
 
+class SpSqfreeCache(C.Structure):
+    _fields_ = [
+        ("config", SpConfig), ("pad_dim", C.c_int), ("sk_k", C.c_int), ("n_res", C.c_int),
+        ("n_terms", C.c_int), ("residual_bits", C.c_int), ("use_spinor", C.c_int),
+        ("use_skel_mobius", C.c_int), ("k_bands", SpBandConfig), ("v_bands", SpBandConfig),
+        ("d_skeleton_idx", C.c_void_p), ("d_residual_idx", C.c_void_p),
+        ("d_csr_offsets", C.c_void_p), ("d_csr_skel_slot", C.c_void_p),
+        ("d_csr_mu_sign", C.c_void_p), ("d_vilenkin_factors", C.c_void_p),
+        ("n_factors", C.c_int), ("d_k_cache", C.c_void_p), ("d_v_cache", C.c_void_p),
+        ("bytes_per_pos_k", C.c_int), ("bytes_per_pos_v", C.c_int), ("max_seq_len", C.c_int),
+        ("n_slots", C.c_int),
+        ("d_pad_scratch", C.c_void_p), ("d_coeff_scratch", C.c_void_p),
+        ("d_skel_scratch", C.c_void_p), ("d_pred_scratch", C.c_void_p),
+        ("d_dev_scratch", C.c_void_p), ("d_levels_scratch", C.c_void_p),
+        ("d_mag_scratch", C.c_void_p), ("d_actual_scratch", C.c_void_p),
+        ("d_sheet_scratch", C.c_void_p), ("stream", C.c_void_p),
+        ("device", C.c_int), ("d_tables", C.c_void_p), ("d_attn_ws", C.c_void_p),
+        ("attn_ws_bytes", C.c_size_t),
+    ]
+
+
+class SpHierCache(C.Structure):
+    _fields_ = [
+        ("config", SpConfig), ("pad_dim", C.c_int), ("n_skeleton", C.c_int),
+        ("n_target", C.c_int), ("target_res_bits", C.c_int), ("n_slots", C.c_int),
+        ("max_seq_len", C.c_int), ("d_W", C.c_void_p), ("d_skeleton_idx", C.c_void_p),
+        ("d_target_idx", C.c_void_p), ("d_vilenkin_factors", C.c_void_p), ("n_factors", C.c_int),
+        ("skel_bands", SpBandConfig), ("d_skel_band_bits", C.c_void_p),
+        ("d_k_cache", C.c_void_p), ("d_v_cache", C.c_void_p),
+        ("bytes_per_pos_k", C.c_int), ("bytes_per_pos_v", C.c_int),
+        ("d_pad_scratch", C.c_void_p), ("d_coeff_scratch", C.c_void_p),
+        ("d_skel_scratch", C.c_void_p), ("d_pred_scratch", C.c_void_p),
+        ("d_dev_scratch", C.c_void_p), ("d_mag_scratch", C.c_void_p),
+        ("d_levels_scratch", C.c_void_p), ("stream", C.c_void_p),
+        ("device", C.c_int), ("d_tables", C.c_void_p),
+    ]
+
+
 class SpLlamaParams(C.Structure):
     _fields_ = [
         ("head_dim", C.c_int), ("n_layers", C.c_int), ("n_heads_kv", C.c_int),
@@ -96,6 +134,28 @@ SIGNATURES = {
     "sp_cuda_attn_decode_noalloc": (_I, [_P, _P, _I, C.POINTER(SpBandConfig),
                                          C.POINTER(SpBandConfig), _P, _I, _I, _I, _P, _I, _I,
                                          _F, _P, _I, _P]),
+    "sp_cuda_sqfree_cache_init": (_I, [C.POINTER(SpSqfreeCache), C.POINTER(SpConfig), _I, _I, _I, _P]),
+    "sp_cuda_sqfree_cache_init_ex": (_I, [C.POINTER(SpSqfreeCache), C.POINTER(SpConfig), _I, _I, _I,
+                                          _F, _P]),
+    "sp_cuda_sqfree_cache_free": (_V, [C.POINTER(SpSqfreeCache)]),
+    "sp_cuda_sqfree_write_k": (_V, [C.POINTER(SpSqfreeCache), _I, _I, _I, _P]),
+    "sp_cuda_sqfree_write_v": (_V, [C.POINTER(SpSqfreeCache), _I, _I, _I, _P]),
+    "sp_cuda_sqfree_read_k": (_V, [C.POINTER(SpSqfreeCache), _I, _I, _I, _P]),
+    "sp_cuda_sqfree_read_v": (_V, [C.POINTER(SpSqfreeCache), _I, _I, _I, _P]),
+    "sp_cuda_sqfree_read_k_batch": (_V, [C.POINTER(SpSqfreeCache), _I, _I, _I, _I, _P]),
+    "sp_cuda_sqfree_read_v_batch": (_V, [C.POINTER(SpSqfreeCache), _I, _I, _I, _I, _P]),
+    "sp_cuda_sqfree_write_kv_tokens": (_I, [C.POINTER(SpSqfreeCache), _I, _I, _I, _I, _P, _P, _I]),
+    "sp_cuda_sqfree_attn_decode": (_I, [C.POINTER(SpSqfreeCache), _I, _I, _P, _I, _I, _F, _P, _P]),
+    "sp_cuda_hier_cache_init": (_I, [C.POINTER(SpHierCache), C.POINTER(SpConfig), _I, _I, _I, _I,
+                                     _P, _P, C.POINTER(SpBandConfig), _I, _I, _P]),
+    "sp_cuda_hier_cache_free": (_V, [C.POINTER(SpHierCache)]),
+    "sp_cuda_hier_cache_upload_W": (_I, [C.POINTER(SpHierCache), _P]),
+    "sp_cuda_hier_write_k": (_V, [C.POINTER(SpHierCache), _I, _I, _I, _P]),
+    "sp_cuda_hier_write_v": (_V, [C.POINTER(SpHierCache), _I, _I, _I, _P]),
+    "sp_cuda_hier_read_k": (_V, [C.POINTER(SpHierCache), _I, _I, _I, _P]),
+    "sp_cuda_hier_read_v": (_V, [C.POINTER(SpHierCache), _I, _I, _I, _P]),
+    "sp_cuda_hier_write_kv_tokens": (_I, [C.POINTER(SpHierCache), _I, _I, _I, _I, _P, _P, _I]),
+    "sp_cuda_hier_read_kv_tokens": (_I, [C.POINTER(SpHierCache), _I, _I, _I, _I, _P, _P]),
     "sp_cuda_vht2_forward": (_V, [_P, _I, _I, _P]),
     "sp_cuda_mobius_reorder": (_V, [_P, _P, _I, _I, _P]),
     "sp_cuda_mobius_unreorder": (_V, [_P, _P, _I, _I, _P]),
@@ -152,7 +212,7 @@ def lib() -> C.CDLL:
             f = getattr(L, name)
             f.restype = res
             f.argtypes = args
-        for which, st in enumerate((SpConfig, SpBandConfig, SpCudaCache)):
+        for which, st in enumerate((SpConfig, SpBandConfig, SpCudaCache, SpSqfreeCache, SpHierCache)):
             if L.sp_cuda_abi_struct_size(which) != C.sizeof(st):
                 raise RuntimeError(f"struct mirror {st.__name__} does not match the C ABI")
         _lib = L

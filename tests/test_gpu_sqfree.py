@@ -1,0 +1,151 @@
+"""GPU parity of the sqfree+spinor and hierarchical-Vilenkin caches against
+the CPU oracle, through the C-ABI: packed slots (skeleton codes, magnitude,
+residual levels, sheet bits) bit-exact, reconstructions exact, and the
+sqfree fused decode attention within 1e-3 relative L2."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle as O
+import spb200
+from spb200 import synth
+from spb200.sqfree import HierCache, SqfreeCache
+
+pytestmark = pytest.mark.gpu
+RTOL_L2 = 1e-3
+
+
+def _rel_l2(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def _inputs(seed, n_layers, H, T, hd, sigma=0.5):
+    k = np.zeros((n_layers, T, H, hd), np.float32)
+    v = np.zeros_like(k)
+    for layer in range(n_layers):
+        for h in range(H):
+            k[layer, :, h], v[layer, :, h] = synth.kv_slot_np(seed, layer, h, T, hd, sigma)
+    return k, v
+
+
+@pytest.mark.parametrize("hd,sk_frac,spinor,rb", [
+    (128, 0.75, True, 3),      # config 2
+    (128, None, True, 3),      # reference CUDA default skeleton pad_dim / 2
+    (128, 0.75, False, 2),
+    (64, 0.75, True, 4),
+    (256, 0.5, True, 3),
+])
+def test_sqfree_codes_and_reads_match_oracle(cuda, hd, sk_frac, spinor, rb):
+    import torch
+    L, H, T = 2, 3, 80
+    cache = SqfreeCache(hd, L, H, T, residual_bits=rb, use_spinor=spinor, sk_frac=sk_frac)
+    OL = O.sqfree_layout(hd, sk_k=cache.cc.sk_k, residual_bits=rb, use_spinor=spinor)
+    assert OL.bytes_per_pos == cache.cc.bytes_per_pos_k
+    k, v = _inputs(2, L, H, T, hd)
+    cache.write_kv_tokens(0, 0, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda())
+    torch.cuda.synchronize()
+    ks, vs = cache.slab(0).cpu().numpy(), cache.slab(1).cpu().numpy()
+    for layer in range(L):
+        for h in range(H):
+            s = layer * H + h
+            assert np.array_equal(ks[s, :T], O.sqfree_write(k[layer, :, h], OL)), (layer, h, "K")
+            assert np.array_equal(vs[s, :T], O.sqfree_write(v[layer, :, h], OL)), (layer, h, "V")
+    out = torch.empty(T, hd, device="cuda")
+    cache.read_batch(0, 1, 2, 0, out)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), O.sqfree_read(ks[1 * H + 2, :T], OL))
+    cache.read_batch(1, 0, 1, 0, out)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), O.sqfree_read(vs[1, :T], OL))
+
+
+def test_sqfree_single_vector_api(cuda):
+    import torch
+    cache = SqfreeCache(128, 2, 2, 16)
+    OL = O.sqfree_layout(128, sk_k=cache.cc.sk_k)
+    k, _ = synth.kv_slot_np(9, 0, 0, 4, 128)
+    L = spb200.lib()
+    dk = torch.from_numpy(k).cuda()
+    for pos in range(4):
+        L.sp_cuda_sqfree_write_k(C.byref(cache.cc), 1, 1, 5 + pos, dk[pos].data_ptr())
+        spb200.check(None, "write_k")
+    out = torch.empty(128, device="cuda")
+    L.sp_cuda_sqfree_read_k(C.byref(cache.cc), 1, 1, 7, out.data_ptr())
+    torch.cuda.synchronize()
+    packed = cache.slab(0).cpu().numpy()[3, 5:9]
+    assert np.array_equal(packed, O.sqfree_write(k, OL))
+    assert np.array_equal(out.cpu().numpy(), O.sqfree_read(packed[2:3], OL)[0])
+
+
+@pytest.mark.parametrize("T,G", [(1, 4), (77, 4), (1000, 4), (333, 2)])
+def test_sqfree_fused_decode_matches_oracle(cuda, T, G):
+    import torch
+    H, L, hd = 2, 2, 128
+    cache = SqfreeCache(hd, L, H, 1024)
+    OL = O.sqfree_layout(hd, sk_k=cache.cc.sk_k)
+    k, v = _inputs(5, L, H, T, hd)
+    cache.write_kv_tokens(0, 0, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda())
+    q = synth.q_np(5, L, H * G, hd, 1.0 / np.sqrt(128))
+    out = torch.empty(L, H * G, hd, dtype=torch.float16, device="cuda")
+    cache.attn_decode(0, L, torch.from_numpy(q).cuda(), T, out, logit_scale=0.9)
+    torch.cuda.synchronize()
+    ks, vs = cache.slab(0).cpu().numpy(), cache.slab(1).cpu().numpy()
+    got = out.float().cpu().numpy()
+    for layer in range(L):
+        ref = O.sqfree_attn_decode(ks[layer * H:(layer + 1) * H], vs[layer * H:(layer + 1) * H], OL, OL,
+                                   q[layer], T, 0.9)
+        assert _rel_l2(got[layer], ref) <= RTOL_L2
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_hier_codes_and_reads_match_oracle(cuda, dtype):
+    import torch
+    hd, L, H, T = 256, 2, 2, 96
+    OL = O.hier_layout(hd)
+    cache = HierCache(hd, L, H, T, OL.pd, OL.n_skel)
+    k, v = _inputs(4, L, H, T, hd, sigma=1.0)
+    tdt = getattr(torch, dtype)
+    kt, vt = torch.from_numpy(k).to(tdt), torch.from_numpy(v).to(tdt)
+    k32, v32 = kt.float().numpy(), vt.float().numpy()      # what the kernel sees
+    Ws = np.stack([O.hier_fit_W(k32[layer, :, h], OL) for layer in range(L) for h in range(H)])
+    cache.upload_W(Ws)
+    cache.write_kv_tokens(0, 0, kt.cuda(), vt.cuda())
+    torch.cuda.synchronize()
+    ks, vs = cache.slab(0).cpu().numpy(), cache.slab(1).cpu().numpy()
+    for layer in range(L):
+        for h in range(H):
+            s = layer * H + h
+            assert np.array_equal(ks[s, :T], O.hier_write(k32[layer, :, h], OL, Ws[s])), (s, "K")
+            assert np.array_equal(vs[s, :T], O.hier_write(v32[layer, :, h], OL, Ws[s])), (s, "V")
+    ko = torch.empty(L, T, H, hd, device="cuda")
+    vo = torch.empty_like(ko)
+    cache.read_kv_tokens(0, 0, ko, vo)
+    torch.cuda.synchronize()
+    ko, vo = ko.cpu().numpy(), vo.cpu().numpy()
+    for layer in range(L):
+        for h in range(H):
+            s = layer * H + h
+            assert np.array_equal(ko[layer, :, h], O.hier_read(ks[s, :T], OL, Ws[s]))
+            assert np.array_equal(vo[layer, :, h], O.hier_read(vs[s, :T], OL, Ws[s]))
+
+
+def test_hier_single_vector_api(cuda):
+    import torch
+    hd = 256
+    OL = O.hier_layout(hd)
+    cache = HierCache(hd, 1, 2, 8, OL.pd, OL.n_skel)
+    k, _ = synth.kv_slot_np(8, 0, 1, 64, hd, 1.0)
+    W = O.hier_fit_W(k, OL)
+    cache.upload_W(np.stack([W, W]))
+    L = spb200.lib()
+    dk = torch.from_numpy(k[:3]).cuda()
+    for pos in range(3):
+        L.sp_cuda_hier_write_k(C.byref(cache.hc), 0, 1, pos, dk[pos].data_ptr())
+    out = torch.empty(hd, device="cuda")
+    L.sp_cuda_hier_read_k(C.byref(cache.hc), 0, 1, 2, out.data_ptr())
+    torch.cuda.synchronize()
+    packed = cache.slab(0).cpu().numpy()[1, :3]
+    assert np.array_equal(packed, O.hier_write(k[:3], OL, W))
+    assert np.array_equal(out.cpu().numpy(), O.hier_read(packed[2:3], OL, W)[0])
