@@ -164,6 +164,147 @@ def cpu_compress_sample(n_threads: int, n_pos: int = 8192):
     return k.shape[0] / dt, n_threads
 
 
+# ------------------------------------------------- configs 2 and 4 (extras) --
+
+def _hartley_matrix(pd: int, torch, dev):
+    """The staged prime-Hartley (Vilenkin) transform of size pd as a dense
+    float64 matrix (Kronecker product of 1/sqrt(p) cas matrices, the first
+    prime acting on the fastest index digit)."""
+    import math
+    M = torch.ones(1, 1, dtype=torch.float64, device=dev)
+    r = pd
+    for p in (2, 3, 5, 7, 11):
+        while r % p == 0:
+            k = torch.arange(p, dtype=torch.float64, device=dev)
+            ang = 2 * math.pi * torch.outer(k, k) / p
+            M = torch.kron((torch.cos(ang) + torch.sin(ang)) / math.sqrt(p), M)
+            r //= p
+    return M
+
+
+def measure_sqfree(torch, dev, stream, steps: int, warmup: int, peak: float):
+    """Config 2: sqfree+spinor, hd 128 (pad 154), skeleton 0.75 (115), bands
+    5,4,4,4,5, 3 residual bits, 8 KV heads x 16384 positions x 32 layers,
+    seeded as config 0 (seed 2).  Compression throughput over all layers and
+    the fused decode step (32 query heads, GQA 4, fp16 queries)."""
+    from spb200.sqfree import SqfreeCache
+    from spb200 import synth
+    L_, H_, T_, hd = 32, 8, 16384, 128
+    cache = SqfreeCache(hd, L_, H_, T_, residual_bits=3, use_spinor=True, sk_frac=0.75,
+                        stream=stream)
+    gen = torch.Generator(device=dev)
+    inputs = []
+    for layer in range(4):
+        gen.manual_seed(2 * 1000003 + layer)
+        inputs.append(synth.kv_layer_torch(gen, T_, H_, hd, device=dev))
+    def compress_all():
+        for layer in range(L_):
+            k, v = inputs[layer % 4]
+            cache.write_kv_tokens(layer, 0, k, v)
+    compress_all()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    compress_all()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    c_ms = e0.elapsed_time(e1)
+    pairs = L_ * H_ * T_
+    bpp = cache.cc.bytes_per_pos_k + cache.cc.bytes_per_pos_v
+    q = (torch.randn(L_, 32, hd, device=dev, generator=gen) / hd ** 0.5).half()
+    out = torch.empty(L_, 32, hd, dtype=torch.float16, device=dev)
+    for _ in range(warmup):
+        cache.attn_decode(0, L_, q, T_, out, stream=stream)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(steps):
+        cache.attn_decode(0, L_, q, T_, out, stream=stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    d_ms = e0.elapsed_time(e1) / steps
+    step_bytes = pairs * bpp + 2 * 2 * L_ * 32 * hd
+    res = {
+        "workload": "config 2: sqfree+spinor hd 128 (pad 154, skeleton 115, bands 5,4,4,4,5, "
+                    "residual 3 bits), 32 layers x 8 KV heads x 16384 positions",
+        "bytes_per_pos_k": cache.cc.bytes_per_pos_k, "bytes_per_pos_v": cache.cc.bytes_per_pos_v,
+        "compression_ratio": 2 * 2 * hd / bpp,
+        "compress": {"value": pairs / (c_ms * 1e-3) / 1e6, "unit": "Mpairs/s", "ms": c_ms,
+                     "achieved_gbs": pairs * (2 * hd * 4 + bpp) / (c_ms * 1e-3) / 1e9},
+        "decode": {"value": d_ms * 1e3, "unit": "us/token", "algorithmic_bytes": step_bytes,
+                   "achieved_gbs": step_bytes / (d_ms * 1e-3) / 1e9},
+    }
+    res["compress"]["frac"] = res["compress"]["achieved_gbs"] / peak
+    res["decode"]["frac"] = res["decode"]["achieved_gbs"] / peak
+    cache.free()
+    return res
+
+
+def measure_hier(torch, dev, stream, peak: float):
+    """Config 4: hierarchical Vilenkin, hd 256 (pad 330, skeleton 30, bands
+    5,5, 2 residual bits), 16 KV heads, 64 sequences x 8192 positions
+    compressed in one call from bf16 K (log-normal sigma 1.0 channel scales,
+    RoPE) and N(0,1) V (seed 4).  The predictor W is fitted per head by
+    ridge least squares (float64) on a 4096-vector calibration sample of the
+    first sequence and shared by the sequences."""
+    from spb200.sqfree import HierCache
+    from spb200 import synth
+    S_, H_, T_, hd, pd, nsk = 64, 16, 8192, 256, 330, 30
+    cache = HierCache(hd, S_, H_, T_, pd, nsk, stream=stream)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4)
+    k = torch.empty(S_, T_, H_, hd, dtype=torch.bfloat16, device=dev)
+    v = torch.empty_like(k)
+    for sq in range(S_):
+        kk, vv = synth.kv_layer_torch(gen, T_, H_, hd, sigma=1.0, device=dev, dtype=torch.bfloat16)
+        k[sq], v[sq] = kk, vv
+    M = _hartley_matrix(pd, torch, dev)
+    Ws = []
+    for h in range(H_):
+        x = k[0, :4096, h].double()
+        pad = torch.cat([x, x.mean(1, keepdim=True).expand(-1, pd - hd)], 1)
+        c = pad @ M.T
+        Sk, Tg = c[:, :nsk], c[:, nsk:]
+        A = Sk.T @ Sk + 1e-6 * torch.eye(nsk, dtype=torch.float64, device=dev)
+        Ws.append(torch.linalg.solve(A, Sk.T @ Tg).T.half())
+    W = torch.stack(Ws)                                   # [H][300][30]
+    cache.upload_W(W.unsqueeze(0).expand(S_, -1, -1, -1).reshape(S_ * H_, pd - nsk, nsk).cpu().numpy())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cache.write_kv_tokens(0, 0, k, v)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    cache.write_kv_tokens(0, 0, k, v)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    c_ms = e0.elapsed_time(e1)
+    del v
+    ko = torch.empty(S_, T_, H_, hd, dtype=torch.float32, device=dev)
+    cache.read_kv_tokens(0, 0, ko, None)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    cache.read_kv_tokens(0, 0, ko, None)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    r_ms = e0.elapsed_time(e1)
+    pairs = S_ * H_ * T_
+    bpp = cache.hc.bytes_per_pos_k
+    corr = torch.nn.functional.cosine_similarity(ko[0, :2048].flatten(0, 1),
+                                                 k[0, :2048].float().flatten(0, 1), dim=1).mean().item()
+    res = {
+        "workload": "config 4: hier hd 256 (pad 330, skeleton 30, bands 5,5, residual 2 bits), "
+                    "16 KV heads x 64 sequences x 8192 positions, bf16 in, one call",
+        "bytes_per_pos": bpp, "compression_ratio": 2 * hd / bpp,
+        "compress": {"value": pairs / (c_ms * 1e-3) / 1e6, "unit": "Mpairs/s", "ms": c_ms,
+                     "achieved_gbs": pairs * (2 * 2 * hd + 2 * bpp) / (c_ms * 1e-3) / 1e9},
+        "decompress_k": {"value": pairs * (bpp + 4 * hd) / (r_ms * 1e-3) / 1e9, "unit": "GB/s",
+                         "ms": r_ms, "out": "fp32 [64][8192][16][256]"},
+        "k_cosine_first_2048": corr,
+    }
+    res["compress"]["frac"] = res["compress"]["achieved_gbs"] / peak
+    res["decompress_k"]["frac"] = res["decompress_k"]["value"] / peak
+    cache.free()
+    return res
+
+
 def run_reference(args):
     """--impl reference: the oracle port of the reference CPU path (the
     reference's own CPU core is an empty submodule and cannot be built),
@@ -405,6 +546,12 @@ def run_ours(args):
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if ws == 1 and not args.no_extra:
+        del kept
+        torch.cuda.empty_cache()
+        line["sqfree"] = measure_sqfree(torch, dev, stream, max(3, args.steps // 2), args.warmup, peak)
+        torch.cuda.empty_cache()
+        line["hier"] = measure_hier(torch, dev, stream, peak)
     if rank == 0:
         print(json.dumps(line), flush=True)
     L.sp_llama_free(ctx)
@@ -420,6 +567,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the config 2 (sqfree) and config 4 (hier) measurements")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="layers in the cache (profiling aid: a smaller case for ncu; "
                          "the headline number is the default, all 32)")
