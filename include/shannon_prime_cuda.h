@@ -219,6 +219,7 @@ typedef struct {
     void            *d_tables;          /* packed kernel tables (indices, CSR, cas) */
     void            *d_attn_ws;         /* fused-decode partials */
     size_t           attn_ws_bytes;
+    int              csr_max_terms;     /* most Möbius terms of one residual */
 } sp_cuda_sqfree_cache_t;
 
 /* Reference signature; the skeleton is pad_dim / 2 as in the reference CUDA

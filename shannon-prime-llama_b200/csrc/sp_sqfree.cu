@@ -570,6 +570,351 @@ k_sq_attn(SpSqDev tk, SpSqDev tv, SqAttn a)
     }
 }
 
+// Sum N per-lane values over the warp; every lane gets all N sums.  For N = 4
+// the values are reduced in a transposed butterfly (2 + 1 + 3 shuffles and 4
+// broadcasts instead of 20 shuffles).
+template <int N>
+__device__ __forceinline__ void warp_sum_multi(float (&v)[N], int lane)
+{
+    if constexpr (N == 4) {
+        const bool b4 = lane & 16, b3 = lane & 8;
+        float k0 = b4 ? v[2] : v[0], k1 = b4 ? v[3] : v[1];
+        const float g0 = b4 ? v[0] : v[2], g1 = b4 ? v[1] : v[3];
+        k0 += __shfl_xor_sync(0xffffffffu, g0, 16);
+        k1 += __shfl_xor_sync(0xffffffffu, g1, 16);
+        float kk = b3 ? k1 : k0;
+        const float gg = b3 ? k0 : k1;
+        kk += __shfl_xor_sync(0xffffffffu, gg, 8);
+        kk += __shfl_xor_sync(0xffffffffu, kk, 4);
+        kk += __shfl_xor_sync(0xffffffffu, kk, 2);
+        kk += __shfl_xor_sync(0xffffffffu, kk, 1);
+#pragma unroll
+        for (int j = 0; j < 4; j++) v[j] = __shfl_sync(0xffffffffu, kk, 8 * j);
+    } else {
+#pragma unroll
+        for (int j = 0; j < N; j++)
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) v[j] += __shfl_xor_sync(0xffffffffu, v[j], o);
+    }
+}
+
+constexpr int kSqRing = 4;          // positions prefetched ahead per warp
+
+__host__ __device__ inline int sq_ring_row_words(const SpSqDev &tk, const SpSqDev &tv)
+{
+    const int w = (tk.bytes_per_pos > tv.bytes_per_pos ? tk.bytes_per_pos : tv.bytes_per_pos);
+    return ((w + 3) >> 2) + 2;       // + guard words read past the row end
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p)
+{
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// Per-lane field descriptor: word << 16 | shift << 8 | (bits - 1) << 4 | band
+// (bits 1..16), so a field is funnelshift(row[word], row[word + 1], shift)
+// & mask(bits).
+__device__ __forceinline__ int field_desc(int bitpos, int bits, int band)
+{
+    return ((bitpos >> 5) << 16) | ((bitpos & 31) << 8) | ((bits - 1) << 4) | band;
+}
+
+__device__ __forceinline__ uint32_t field_get(const uint32_t *row, int d)
+{
+    const int w = d >> 16, sh = (d >> 8) & 31, bm1 = (d >> 4) & 15;
+    return __funnelshift_r(row[w], row[w + 1], sh) & ((2u << bm1) - 1u);
+}
+
+// Per-lane slot descriptor of skeleton value s.
+__device__ __forceinline__ int slot_desc(const SpBandLayout &bl, int s)
+{
+    const int b = band_of_s(bl, s);
+    return field_desc(8 * (bl.byte_off[b] + 2) + (s - bl.off[b]) * bl.bits[b], bl.bits[b], b);
+}
+
+// Skeleton values of the lane's KS slots from the row in smem (band scales
+// converted once per row by lanes 0..n_bands-1 and fetched by shuffle).
+template <int KS>
+__device__ __forceinline__ void skel_values(const uint32_t *row, int scdesc, const int (&desc)[KS],
+                                            const float (&offs)[KS], int n_skel, int lane, float (&val)[KS],
+                                            float *skbuf)
+{
+    // lane b < n_bands converts band b's fp16 scale (0 if not finite)
+    float bsc = __half2float(__ushort_as_half((unsigned short)field_get(row, scdesc)));
+    bsc = fabsf(bsc) <= 65504.0f ? bsc : 0.0f;
+#pragma unroll
+    for (int k = 0; k < KS; k++) {
+        const int d = desc[k];
+        const float sc = __shfl_sync(0xffffffffu, bsc, d & 15);
+        const float u = (float)field_get(row, d);
+        const int s = lane + 32 * k;
+        val[k] = s < n_skel ? (u - offs[k]) * sc : 0.0f;
+        if (s < n_skel) skbuf[s] = val[k];
+    }
+}
+
+constexpr int kSqMaxTerms = 8;       // Möbius terms per residual held in registers
+
+// Residual coefficients of the lane's KR slots (after skel_values + syncwarp).
+// terms[k][j]: the lane's CSR terms (skeleton slot << 1 | negative), nt[k]
+// their count; step_mul = 2 * bits / (L - 1), so step = mag * step_mul.
+template <int KR>
+__device__ __forceinline__ void res_values(const uint32_t *row, int magw, const int (&lvdesc)[KR],
+                                           const int (&shdesc)[KR], const int (&terms)[KR][kSqMaxTerms],
+                                           const int (&nt)[KR], float center, float step_mul, const float *skbuf,
+                                           float (&val)[KR])
+{
+    const float mag = __uint_as_float(__funnelshift_r(row[magw >> 8], row[(magw >> 8) + 1], magw & 31));
+    const float step = mag * step_mul;
+#pragma unroll
+    for (int k = 0; k < KR; k++) {
+        float p = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kSqMaxTerms; j++) {
+            if (j < nt[k]) {
+                const float v = skbuf[terms[k][j] >> 1];
+                p = (terms[k][j] & 1) ? p - v : p + v;
+            }
+        }
+        const float lv = (float)field_get(row, lvdesc[k]);
+        if (shdesc[k] >= 0 && field_get(row, shdesc[k])) p = -p;
+        val[k] = nt[k] >= 0 ? p + (lv - center) * step : 0.0f;
+    }
+}
+
+// Register-resident fused decode: lane l owns skeleton slots l, l+32, ...
+// (KS of them) and residual slots l, l+32, ... (KR), holds its slots' q'
+// entries and V accumulators in registers, and only the skeleton values go
+// through shared memory (the Möbius prediction reads other lanes' slots).
+__device__ __forceinline__ float ex2_fast(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+template <int GT, int KS, int KR>
+__global__ void __launch_bounds__(kSqAttnWarps * 32, 3)
+k_sq_attn_reg(SpSqDev tk, SpSqDev tv, SqAttn a)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int split = blockIdx.x, h = blockIdx.y, li = blockIdx.z;
+    const int layer = a.layer0 + li;
+    const int G = a.group, pd = tk.pd;
+    int *tab = reinterpret_cast<int *>(smem);
+    float *cas = reinterpret_cast<float *>(tab + tab_len(tk));
+    float *qp = cas + 224;                                       // [GT][pd]
+    float *skb = qp + GT * pd + warp * (tk.n_skel + 4);          // per warp
+    // per warp: a ring of kSqRing stages, each the K row then the V row
+    const int rw = sq_ring_row_words(tk, tv);
+    uint32_t *ring = reinterpret_cast<uint32_t *>(qp + GT * pd + kSqAttnWarps * (tk.n_skel + 4)) +
+                     warp * kSqRing * 2 * rw;
+    float *merge = reinterpret_cast<float *>(reinterpret_cast<uint32_t *>(qp + GT * pd + kSqAttnWarps * (tk.n_skel + 4)) +
+                                             kSqAttnWarps * kSqRing * 2 * rw);    // [warps][GT][pd + 4]
+    for (int i = threadIdx.x; i < tab_len(tk); i += blockDim.x) tab[i] = tk.tables[i];
+    for (int i = threadIdx.x; i < 224; i += blockDim.x) cas[i] = tk.cas[i];
+    __syncthreads();
+    for (int g = warp; g < GT; g += kSqAttnWarps) {
+        float *b = qp + g * pd;
+        const __half *qg = a.q + ((long long)li * a.n_q_heads + h * G + g) * tk.hd;
+        for (int i = lane; i < pd; i += 32) b[i] = (g < G && i < tk.hd) ? __half2float(qg[i]) : 0.0f;
+        __syncwarp();
+        vilenkin_warp(b, tk, cas, lane);
+        for (int i = lane; i < pd; i += 32) b[i] *= a.logit_scale * 1.4426950408889634f;
+    }
+    __syncthreads();
+    const int *skel_idx = tab + tab_skel(tk), *res_idx = tab + tab_res(tk);
+    const int *csr_off = tab + tab_csr_off(tk), *csr_term = tab + tab_csr_term(tk);
+    int terms[KR][kSqMaxTerms], nt[KR];
+#pragma unroll
+    for (int k = 0; k < KR; k++) {
+        const int r = lane + 32 * k;
+        nt[k] = r < tk.n_res ? csr_off[r + 1] - csr_off[r] : 0;
+#pragma unroll
+        for (int j = 0; j < kSqMaxTerms; j++) terms[k][j] = j < nt[k] ? csr_term[csr_off[r] + j] : 0;
+    }
+    const int Lr = 1 << tk.res_bits;
+    const float center = 0.5f * (float)(Lr - 1);
+    const float kmul = Lr > 1 ? 2.0f * (float)tk.res_bits / (float)(Lr - 1) : 0.0f;
+    const float vmul = Lr > 1 ? 2.0f * (float)tv.res_bits / (float)(Lr - 1) : 0.0f;
+    int kdesc[KS], vdesc[KS], lvk[KR], lvv[KR], shk[KR], shv[KR];
+    float koffs[KS], voffs[KS];
+    float qs[GT][KS], qr[GT][KR];
+    const int ksc = field_desc(8 * tk.bl.byte_off[lane < tk.bl.n_bands ? lane : 0], 16, 0);
+    const int vsc = field_desc(8 * tv.bl.byte_off[lane < tv.bl.n_bands ? lane : 0], 16, 0);
+    const int kmag = ((8 * tk.mag_off) >> 5 << 8) | ((8 * tk.mag_off) & 31);
+    const int vmag = ((8 * tv.mag_off) >> 5 << 8) | ((8 * tv.mag_off) & 31);
+#pragma unroll
+    for (int k = 0; k < KR; k++) {
+        const int r = lane + 32 * k, rc = r < tk.n_res ? r : 0;
+        lvk[k] = field_desc(8 * tk.res_off + rc * tk.res_bits, tk.res_bits, 0);
+        lvv[k] = field_desc(8 * tv.res_off + rc * tv.res_bits, tv.res_bits, 0);
+        shk[k] = tk.use_spinor ? field_desc(8 * tk.sheet_off + rc, 1, 0) : -1;
+        shv[k] = tv.use_spinor ? field_desc(8 * tv.sheet_off + rc, 1, 0) : -1;
+        if (r >= tk.n_res) nt[k] = -1;          // not a residual slot: value 0
+    }
+#pragma unroll
+    for (int k = 0; k < KS; k++) {
+        const int s = lane + 32 * k;
+        const int sc = s < tk.n_skel ? s : 0;
+        kdesc[k] = slot_desc(tk.bl, sc);
+        vdesc[k] = slot_desc(tv.bl, sc);
+        koffs[k] = (float)((1 << (tk.bl.bits[band_of_s(tk.bl, sc)] - 1)) - 1);
+        voffs[k] = (float)((1 << (tv.bl.bits[band_of_s(tv.bl, sc)] - 1)) - 1);
+#pragma unroll
+        for (int g = 0; g < GT; g++) qs[g][k] = s < tk.n_skel ? qp[g * pd + skel_idx[s]] : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < KR; k++) {
+        const int r = lane + 32 * k;
+#pragma unroll
+        for (int g = 0; g < GT; g++) qr[g][k] = r < tk.n_res ? qp[g * pd + res_idx[r]] : 0.0f;
+    }
+    float as[GT][KS], ar[GT][KR], m[GT], l[GT];
+#pragma unroll
+    for (int g = 0; g < GT; g++) {
+        m[g] = -INFINITY;
+        l[g] = 0.0f;
+#pragma unroll
+        for (int k = 0; k < KS; k++) as[g][k] = 0.0f;
+#pragma unroll
+        for (int k = 0; k < KR; k++) ar[g][k] = 0.0f;
+    }
+    const long long slot = (long long)layer * a.n_kv_heads + h;
+    const int t_begin = split * a.chunk, t_end = min(a.kv_len, t_begin + a.chunk);
+    const uint8_t *kbase = a.k_cache + slot * a.k_slot_stride;
+    const uint8_t *vbase = a.v_cache + slot * a.v_slot_stride;
+    const int kw = tk.bytes_per_pos >> 2, vw = tv.bytes_per_pos >> 2;   // 4-byte rows (checked on the host)
+    // Prefetch rows kSqRing positions ahead with 4-byte cp.async per lane.
+    auto issue = [&](int tok, int st) {
+        uint32_t *dk = ring + st * 2 * rw, *dv = dk + rw;
+        if (tok < t_end) {
+            const uint32_t *sk = reinterpret_cast<const uint32_t *>(kbase + (long long)tok * tk.bytes_per_pos);
+            const uint32_t *svp = reinterpret_cast<const uint32_t *>(vbase + (long long)tok * tv.bytes_per_pos);
+            for (int j = lane; j < kw; j += 32)
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dk + j)), "l"(sk + j) : "memory");
+            for (int j = lane; j < vw; j += 32)
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dv + j)), "l"(svp + j) : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    if (lane == 0)
+        for (int st = 0; st < kSqRing; st++) { ring[st * 2 * rw + kw] = 0u; ring[st * 2 * rw + rw + vw] = 0u; }
+    __syncwarp();
+    for (int st = 0; st < kSqRing; st++) issue(t_begin + warp + st * kSqAttnWarps, st);
+    int it = 0;
+    for (int tok = t_begin + warp; tok < t_end; tok += kSqAttnWarps, it++) {
+        const int st = it % kSqRing;
+        asm volatile("cp.async.wait_group %0;" ::"n"(kSqRing - 1) : "memory");
+        __syncwarp();
+        const uint32_t *row = ring + st * 2 * rw;
+        // ---- K: scores ----
+        float sv[KS], rv[KR];
+        skel_values<KS>(row, ksc, kdesc, koffs, tk.n_skel, lane, sv, skb);
+        __syncwarp();
+        res_values<KR>(row, kmag, lvk, shk, terms, nt, center, kmul, skb, rv);
+        float sc[GT];
+#pragma unroll
+        for (int g = 0; g < GT; g++) {
+            float d = 0.0f;
+#pragma unroll
+            for (int k = 0; k < KS; k++) d = __fmaf_rn(qs[g][k], sv[k], d);
+#pragma unroll
+            for (int k = 0; k < KR; k++) d = __fmaf_rn(qr[g][k], rv[k], d);
+            sc[g] = d;
+        }
+        warp_sum_multi<GT>(sc, lane);
+        float p[GT];
+#pragma unroll
+        for (int g = 0; g < GT; g++) {
+            if (sc[g] > m[g]) {                 // uniform across the warp
+                const float alpha = ex2_fast(m[g] - sc[g]);
+                m[g] = sc[g];
+                l[g] *= alpha;
+#pragma unroll
+                for (int k = 0; k < KS; k++) as[g][k] *= alpha;
+#pragma unroll
+                for (int k = 0; k < KR; k++) ar[g][k] *= alpha;
+            }
+            p[g] = ex2_fast(sc[g] - m[g]);
+            l[g] += p[g];
+        }
+        __syncwarp();
+        // ---- V: accumulate ----
+        row += rw;
+        skel_values<KS>(row, vsc, vdesc, voffs, tv.n_skel, lane, sv, skb);
+        __syncwarp();
+        res_values<KR>(row, vmag, lvv, shv, terms, nt, center, vmul, skb, rv);
+#pragma unroll
+        for (int g = 0; g < GT; g++) {
+#pragma unroll
+            for (int k = 0; k < KS; k++) as[g][k] = __fmaf_rn(p[g], sv[k], as[g][k]);
+#pragma unroll
+            for (int k = 0; k < KR; k++) ar[g][k] = __fmaf_rn(p[g], rv[k], ar[g][k]);
+        }
+        __syncwarp();
+        issue(tok + kSqRing * kSqAttnWarps, st);
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    // ---- merge the warps, write the CTA's partial ----
+    float *mw = merge + (size_t)warp * GT * (pd + 4);
+#pragma unroll
+    for (int g = 0; g < GT; g++) {
+#pragma unroll
+        for (int k = 0; k < KS; k++) {
+            const int s = lane + 32 * k;
+            if (s < tk.n_skel) mw[g * (pd + 4) + 4 + skel_idx[s]] = as[g][k];
+        }
+#pragma unroll
+        for (int k = 0; k < KR; k++) {
+            const int r = lane + 32 * k;
+            if (r < tk.n_res) mw[g * (pd + 4) + 4 + res_idx[r]] = ar[g][k];
+        }
+        if (lane == 0) { mw[g * (pd + 4)] = m[g]; mw[g * (pd + 4) + 1] = l[g]; }
+    }
+    __syncthreads();
+    for (int g = 0; g < G; g++) {
+        float M = -INFINITY;
+        for (int w = 0; w < kSqAttnWarps; w++) M = fmaxf(M, merge[((size_t)w * GT + g) * (pd + 4)]);
+        float *part = sq_partial(a, pd, li, h * G + g, split);
+        for (int i = threadIdx.x; i < pd + 1; i += blockDim.x) {
+            float v = 0.0f;
+            for (int w = 0; w < kSqAttnWarps; w++) {
+                const float *aw = merge + ((size_t)w * GT + g) * (pd + 4);
+                const float wt = aw[0] == -INFINITY ? 0.0f : exp2f(aw[0] - M);
+                v += wt * (i < pd ? aw[4 + i] : aw[1]);
+            }
+            if (i < pd) part[4 + i] = v;
+            else { part[0] = M; part[1] = v; }
+        }
+    }
+}
+
+size_t sq_attn_reg_smem(const SpSqDev &t, const SpSqDev &tv, int GT)
+{
+    return (size_t)tab_len(t) * 4 + 224 * 4 + (size_t)GT * t.pd * 4 + (size_t)kSqAttnWarps * (t.n_skel + 4) * 4 +
+           (size_t)kSqAttnWarps * kSqRing * 2 * sq_ring_row_words(t, tv) * 4 +
+           (size_t)kSqAttnWarps * GT * (t.pd + 4) * 4 + 64;
+}
+
+using SqAttnKernel = void (*)(SpSqDev, SpSqDev, SqAttn);
+
+// Register-resident instantiations: (query group bound, skeleton slots per
+// lane, residual slots per lane) for the sqfree shapes of head_dim 64, 128
+// and 256 at skeleton fractions 0.5 and 0.75.
+SqAttnKernel sq_attn_reg_kernel(int G, int KS, int KR, int *GT)
+{
+#define SQ_CASE(ks, kr)                                                                 \
+    if (KS == ks && KR == kr) {                                                         \
+        if (G <= 4) { *GT = 4; return k_sq_attn_reg<4, ks, kr>; }                       \
+        *GT = 8; return k_sq_attn_reg<8, ks, kr>;                                       \
+    }
+    SQ_CASE(4, 2) SQ_CASE(3, 3) SQ_CASE(2, 1) SQ_CASE(2, 2) SQ_CASE(8, 3) SQ_CASE(6, 6)
+#undef SQ_CASE
+    return nullptr;
+}
+
 __global__ void k_sq_attn_combine(SpSqDev t, SqAttn a)
 {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -830,6 +1175,8 @@ int sp_cuda_sqfree_cache_init_ex(sp_cuda_sqfree_cache_t *cc, const sp_config_t *
     }
     off.push_back((int)term.size());
     cc->n_terms = (int)term.size();
+    for (size_t r = 0; r + 1 < off.size(); r++)
+        if (off[r + 1] - off[r] > cc->csr_max_terms) cc->csr_max_terms = off[r + 1] - off[r];
     std::vector<int> tables;
     tables.insert(tables.end(), skel.begin(), skel.end());
     tables.insert(tables.end(), res.begin(), res.end());
@@ -1052,7 +1399,17 @@ int sp_cuda_sqfree_attn_decode(const sp_cuda_sqfree_cache_t *cc, int layer0, int
     a.chunk = (kv_len + splits - 1) / splits;
     a.n_splits = kv_len == 0 ? 0 : (kv_len + a.chunk - 1) / a.chunk;
     cudaStream_t s = (cudaStream_t)stream;
-    if (a.n_splits > 0) {
+    int GT = 0;
+    SqAttnKernel kreg = sq_attn_reg_kernel(a.group, (tk.n_skel + 31) / 32, (tk.n_res + 31) / 32, &GT);
+    // the prefetch ring copies rows in 4-byte pieces; Möbius terms live in registers
+    if (a.store_width_k != 4 || a.store_width_v != 4 || cc->csr_max_terms > kSqMaxTerms) kreg = nullptr;
+    if (a.n_splits > 0 && kreg) {
+        const size_t sm = sq_attn_reg_smem(tk, tv, GT);
+        cudaFuncSetAttribute(kreg, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        kreg<<<dim3(a.n_splits, H, n_layers), kSqAttnWarps * 32, sm, s>>>(tk, tv, a);
+        int rc = sp_check_cuda(cudaGetLastError(), "sqfree attention launch");
+        if (rc) return rc;
+    } else if (a.n_splits > 0) {
         const size_t sm = sq_attn_smem(tk, a.group);
         cudaFuncSetAttribute(k_sq_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
         k_sq_attn<<<dim3(a.n_splits, H, n_layers), kSqAttnWarps * 32, sm, s>>>(tk, tv, a);

@@ -79,15 +79,20 @@ def test_sqfree_single_vector_api(cuda):
     assert np.array_equal(out.cpu().numpy(), O.sqfree_read(packed[2:3], OL)[0])
 
 
-@pytest.mark.parametrize("T,G", [(1, 4), (77, 4), (1000, 4), (333, 2)])
-def test_sqfree_fused_decode_matches_oracle(cuda, T, G):
+@pytest.mark.parametrize("T,G,hd,sk_frac", [
+    (1, 4, 128, 0.75), (77, 4, 128, 0.75), (1000, 4, 128, 0.75), (333, 2, 128, 0.75),
+    (300, 8, 128, 0.75), (300, 4, 128, None), (300, 4, 256, 0.75), (200, 4, 32, 0.75),
+])
+def test_sqfree_fused_decode_matches_oracle(cuda, T, G, hd, sk_frac):
+    """Register-resident kernel for the common slot shapes; the shared-memory
+    kernel for the others (hd 32: one skeleton and one residual slot per lane)."""
     import torch
-    H, L, hd = 2, 2, 128
-    cache = SqfreeCache(hd, L, H, 1024)
+    H, L = 2, 2
+    cache = SqfreeCache(hd, L, H, 1024, sk_frac=sk_frac)
     OL = O.sqfree_layout(hd, sk_k=cache.cc.sk_k)
     k, v = _inputs(5, L, H, T, hd)
     cache.write_kv_tokens(0, 0, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda())
-    q = synth.q_np(5, L, H * G, hd, 1.0 / np.sqrt(128))
+    q = synth.q_np(5, L, H * G, hd, 1.0 / np.sqrt(hd))
     out = torch.empty(L, H * G, hd, dtype=torch.float16, device="cuda")
     cache.attn_decode(0, L, torch.from_numpy(q).cuda(), T, out, logit_scale=0.9)
     torch.cuda.synchronize()
