@@ -312,7 +312,6 @@ __global__ void k_permute(float *data, const int *order, int n, int n_vecs)
 // CTAs are persistent (grid-stride over vectors, token-major), and each
 // vector's lanes store its row themselves, so no CTA-wide barrier is taken.
 constexpr int kFastWarps = 8;
-constexpr int kFastE = 8;              // coefficients per lane
 constexpr int kFastRowWords = 80;      // per-vector packed-row buffer (320 B)
 
 struct FastBand {
@@ -329,12 +328,11 @@ struct FastArgs {
     int store_width;       // 4, 2 or 1: widest aligned store for every row
 };
 
-template <int LPV, typename Tin, bool WHT>
+template <int LPV, int E, typename Tin, bool WHT>
 __global__ void __launch_bounds__(kFastWarps * 32)
 k_encode_fast(FastArgs fa)
 {
-    constexpr int E = kFastE;
-    static_assert(E == 8, "the packing below splits the lane's codes 4 + 4");
+    static_assert(E == 8 || E == 16, "codes are packed in groups of 8");
     constexpr int VPW = 32 / LPV;             // vectors per warp
     constexpr int n = LPV * E;
     constexpr int kStages = LPV == 32 ? 5 : LPV == 16 ? 4 : LPV == 8 ? 3 : LPV == 4 ? 2 : 1;
@@ -384,10 +382,13 @@ k_encode_fast(FastArgs fa)
                 x[e] = q.x; x[e + 1] = q.y; x[e + 2] = q.z; x[e + 3] = q.w;
             }
         } else {
-            const uint4 q = __ldcs(reinterpret_cast<const uint4 *>(src));
-            const Tin *hv = reinterpret_cast<const Tin *>(&q);
 #pragma unroll
-            for (int e = 0; e < E; e++) x[e] = sp_load_as_float(hv, e);
+            for (int e = 0; e < E; e += 8) {
+                const uint4 q = __ldcs(reinterpret_cast<const uint4 *>(src + e));
+                const Tin *hv = reinterpret_cast<const Tin *>(&q);
+#pragma unroll
+                for (int i = 0; i < 8; i++) x[e + i] = sp_load_as_float(hv, i);
+            }
         }
         for (int j = ln; j < words; j += LPV) row[j] = 0u;
         // ---- VHT2 (ascending butterfly lengths, as the CPU path) ----
@@ -448,22 +449,25 @@ k_encode_fast(FastArgs fa)
             q = q > max_val ? max_val : (q < -max_val ? -max_val : q);
             u[e] = (unsigned)(q + max_val);
         }
-        unsigned f_lo = u[3], f_hi = u[7];
-#pragma unroll
-        for (int e = 2; e >= 0; e--) {
-            f_lo = f_lo * mult + u[e];
-            f_hi = f_hi * mult + u[e + 4];
-        }
-        const unsigned long long field = ((unsigned long long)f_hi << (4 * bits)) | f_lo;
         __syncwarp();                       // row zeroed, buf reads done
-        {
-            const int w0 = bitpos >> 5, sh = bitpos & 31;
+#pragma unroll
+        for (int g = 0; g < E / 8; g++) {
+            // codes 8g..8g+7 as one field of 8 * bits <= 64 bits
+            unsigned f_lo = u[8 * g + 3], f_hi = u[8 * g + 7];
+#pragma unroll
+            for (int e = 2; e >= 0; e--) {
+                f_lo = f_lo * mult + u[8 * g + e];
+                f_hi = f_hi * mult + u[8 * g + 4 + e];
+            }
+            const unsigned long long field = ((unsigned long long)f_hi << (4 * bits)) | f_lo;
+            const int pos = bitpos + 8 * g * bits;
+            const int w0 = pos >> 5, sh = pos & 31;
             const unsigned long long lo = field << sh;
             atomicOr(&row[w0], (unsigned)lo);
-            if (E * bits + sh > 32) atomicOr(&row[w0 + 1], (unsigned)(lo >> 32));
-            if (sh && E * bits + sh > 64) atomicOr(&row[w0 + 2], (unsigned)(field >> (64 - sh)));
-            if (sshift >= 0) atomicOr(&row[sword], (unsigned)__half_as_ushort(hs) << sshift);
+            if (8 * bits + sh > 32) atomicOr(&row[w0 + 1], (unsigned)(lo >> 32));
+            if (sh && 8 * bits + sh > 64) atomicOr(&row[w0 + 2], (unsigned)(field >> (64 - sh)));
         }
+        if (sshift >= 0) atomicOr(&row[sword], (unsigned)__half_as_ushort(hs) << sshift);
         __syncwarp();
         // ---- store the packed row ----
         if (live) {
@@ -484,10 +488,10 @@ k_encode_fast(FastArgs fa)
     }
 }
 
-// Lane tables for the fast path, or false if the layout does not qualify.
-bool fast_bands(const SpBandLayout &bl, FastBand &fb)
+// Lane tables for the fast path at E coefficients per lane, or false if the
+// layout does not qualify.
+bool fast_bands(const SpBandLayout &bl, int E, FastBand &fb)
 {
-    const int E = kFastE;
     if (bl.n % E || bl.n / E > 32 || bl.n / E < 1) return false;
     if ((bl.total_bytes + 3) / 4 + 3 > kFastRowWords) return false;
     for (int b = 0; b < bl.n_bands; b++) {
@@ -507,11 +511,11 @@ bool fast_bands(const SpBandLayout &bl, FastBand &fb)
     return true;
 }
 
-template <int LPV, typename Tin>
+template <int LPV, int E, typename Tin>
 int launch_encode_fast(const FastArgs &fa, bool wht, cudaStream_t s)
 {
     static int blocks_per_sm[2] = {0, 0}, sms = 0;
-    auto k = wht ? k_encode_fast<LPV, Tin, true> : k_encode_fast<LPV, Tin, false>;
+    auto k = wht ? k_encode_fast<LPV, E, Tin, true> : k_encode_fast<LPV, E, Tin, false>;
     int &bps = blocks_per_sm[wht ? 1 : 0];
     if (!bps) {
         int dev = 0;
@@ -570,12 +574,15 @@ int launch_encode_dt(const EncodeArgs &a, bool wht, cudaStream_t s)
                    : ((tb | base | (uintptr_t)a.slot_stride) & 1) == 0 ? 2 : 1;
     // The inputs must allow 16-byte loads of each lane's 8 elements.
     const bool in_aligned = ((uintptr_t)a.in % 16) == 0;
-    if (in_aligned && fast_bands(a.bl, fa.fb)) {
-        switch (a.bl.n / kFastE) {
-        case 4:  return launch_encode_fast<4, Tin>(fa, wht, s);
-        case 8:  return launch_encode_fast<8, Tin>(fa, wht, s);
-        case 16: return launch_encode_fast<16, Tin>(fa, wht, s);
-        case 32: return launch_encode_fast<32, Tin>(fa, wht, s);
+    // 8 coefficients per lane (two head_dim-128 vectors per warp); 16 per lane
+    // (four vectors per warp) measured 5% slower on config 1 at the same
+    // occupancy, so only 8 is dispatched.
+    if (in_aligned && fast_bands(a.bl, 8, fa.fb)) {
+        switch (a.bl.n / 8) {
+        case 4:  return launch_encode_fast<4, 8, Tin>(fa, wht, s);
+        case 8:  return launch_encode_fast<8, 8, Tin>(fa, wht, s);
+        case 16: return launch_encode_fast<16, 8, Tin>(fa, wht, s);
+        case 32: return launch_encode_fast<32, 8, Tin>(fa, wht, s);
         }
     }
     switch (a.bl.n) {
