@@ -182,14 +182,14 @@ def _hartley_matrix(pd: int, torch, dev):
     return M
 
 
-def measure_sqfree(torch, dev, stream, steps: int, warmup: int, peak: float):
+def measure_sqfree(torch, dev, stream, steps: int, warmup: int, peak: float, scale: int = 1):
     """Config 2: sqfree+spinor, hd 128 (pad 154), skeleton 0.75 (115), bands
     5,4,4,4,5, 3 residual bits, 8 KV heads x 16384 positions x 32 layers,
     seeded as config 0 (seed 2).  Compression throughput over all layers and
     the fused decode step (32 query heads, GQA 4, fp16 queries)."""
     from spb200.sqfree import SqfreeCache
     from spb200 import synth
-    L_, H_, T_, hd = 32, 8, 16384, 128
+    L_, H_, T_, hd = 32 // scale, 8, 16384, 128
     cache = SqfreeCache(hd, L_, H_, T_, residual_bits=3, use_spinor=True, sk_frac=0.75,
                         stream=stream)
     gen = torch.Generator(device=dev)
@@ -225,7 +225,7 @@ def measure_sqfree(torch, dev, stream, steps: int, warmup: int, peak: float):
     step_bytes = pairs * bpp + 2 * 2 * L_ * 32 * hd
     res = {
         "workload": "config 2: sqfree+spinor hd 128 (pad 154, skeleton 115, bands 5,4,4,4,5, "
-                    "residual 3 bits), 32 layers x 8 KV heads x 16384 positions",
+                    "residual 3 bits), %d layers x 8 KV heads x 16384 positions" % L_,
         "bytes_per_pos_k": cache.cc.bytes_per_pos_k, "bytes_per_pos_v": cache.cc.bytes_per_pos_v,
         "compression_ratio": 2 * 2 * hd / bpp,
         "compress": {"value": pairs / (c_ms * 1e-3) / 1e6, "unit": "Mpairs/s", "ms": c_ms,
@@ -239,7 +239,7 @@ def measure_sqfree(torch, dev, stream, steps: int, warmup: int, peak: float):
     return res
 
 
-def measure_hier(torch, dev, stream, peak: float):
+def measure_hier(torch, dev, stream, peak: float, scale: int = 1):
     """Config 4: hierarchical Vilenkin, hd 256 (pad 330, skeleton 30, bands
     5,5, 2 residual bits), 16 KV heads, 64 sequences x 8192 positions
     compressed in one call from bf16 K (log-normal sigma 1.0 channel scales,
@@ -248,7 +248,7 @@ def measure_hier(torch, dev, stream, peak: float):
     first sequence and shared by the sequences."""
     from spb200.sqfree import HierCache
     from spb200 import synth
-    S_, H_, T_, hd, pd, nsk = 64, 16, 8192, 256, 330, 30
+    S_, H_, T_, hd, pd, nsk = 64 // scale, 16, 8192, 256, 330, 30
     cache = HierCache(hd, S_, H_, T_, pd, nsk, stream=stream)
     gen = torch.Generator(device=dev)
     gen.manual_seed(4)
@@ -291,12 +291,12 @@ def measure_hier(torch, dev, stream, peak: float):
                                                  k[0, :2048].float().flatten(0, 1), dim=1).mean().item()
     res = {
         "workload": "config 4: hier hd 256 (pad 330, skeleton 30, bands 5,5, residual 2 bits), "
-                    "16 KV heads x 64 sequences x 8192 positions, bf16 in, one call",
+                    "16 KV heads x %d sequences x 8192 positions, bf16 in, one call" % S_,
         "bytes_per_pos": bpp, "compression_ratio": 2 * hd / bpp,
         "compress": {"value": pairs / (c_ms * 1e-3) / 1e6, "unit": "Mpairs/s", "ms": c_ms,
                      "achieved_gbs": pairs * (2 * 2 * hd + 2 * bpp) / (c_ms * 1e-3) / 1e9},
         "decompress_k": {"value": pairs * (bpp + 4 * hd) / (r_ms * 1e-3) / 1e9, "unit": "GB/s",
-                         "ms": r_ms, "out": "fp32 [64][8192][16][256]"},
+                         "ms": r_ms, "out": "fp32 [%d][8192][16][256]" % S_},
         "k_cosine_first_2048": corr,
     }
     res["compress"]["frac"] = res["compress"]["achieved_gbs"] / peak
@@ -549,9 +549,10 @@ def run_ours(args):
     if ws == 1 and not args.no_extra:
         del kept
         torch.cuda.empty_cache()
-        line["sqfree"] = measure_sqfree(torch, dev, stream, max(3, args.steps // 2), args.warmup, peak)
+        line["sqfree"] = measure_sqfree(torch, dev, stream, max(3, args.steps // 2), args.warmup, peak,
+                                        args.extras_scale)
         torch.cuda.empty_cache()
-        line["hier"] = measure_hier(torch, dev, stream, peak)
+        line["hier"] = measure_hier(torch, dev, stream, peak, args.extras_scale)
     if rank == 0:
         print(json.dumps(line), flush=True)
     L.sp_llama_free(ctx)
@@ -567,6 +568,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--extras-scale", type=int, default=1,
+                    help="divide config 2 layers and config 4 sequences by this (profiling aid)")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the config 2 (sqfree) and config 4 (hier) measurements")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
