@@ -19,8 +19,12 @@
  *     hd 64 (shannon_prime_llama.h:336-338, shannon_prime_vulkan.c:99-105);
  *     correlation thresholds K > 0.985, V > 0.950 at hd 128
  *     (test_adreno_phone.log:50-51);
- *   - the reference's own CUDA quantiser, compiled from its source by
- *     oracle/build_ref.sh, run on the same coefficients (GPU tests).
+ *   - the sqfree / hierarchical restatement (sp_oracle_sqfree.c) is pinned
+ *     by an independent float64 Kronecker-product Hartley matrix, a direct
+ *     restatement of the Knight mask and Möbius CSR, and slot sizes.
+ * The reference's own CPU and CUDA sources for this path include the absent
+ * core header (shannon_prime_cuda.h:12, shannon_prime_adreno.h:12), so no
+ * reference binary can be built here.
  * Unpinned: the Möbius order table itself (restated as squarefree-first,
  * ascending) and the core's tie rounding (restated as round-half-even, the
  * reference CUDA kernel's __float2int_rn).
