@@ -187,16 +187,16 @@ __device__ __forceinline__ __half2 finite_or_zero(__half2 h)
     return *reinterpret_cast<const __half2 *>(&v);
 }
 
-template <int kWarps, int kStages>
+template <int kWarps, int kStages, int GT>
 struct Smem {
     unsigned char ring[kWarps][kStages][kStageBytes];
     unsigned char pad[16];
     unsigned long long bar[kWarps][kStages];
-    float q[4][kN];          // transformed, permuted, scaled queries
-    float qt[4][kN];         // scratch for the permutation
-    float qsum[4][4];        // per query, per band: sum of q'
-    float qmax[4];
-    float merge[kWarps][4][4 + kN];
+    float q[GT][kN];         // transformed, permuted, scaled queries
+    float qt[GT][kN];        // scratch for the permutation
+    float qsum[GT][4];       // per query, per band: sum of q'
+    float qmax[GT];
+    float merge[kWarps][GT][4 + kN];
     float scl[kWarps][16][8];   // per tile: K band scales 0..3, V scale (fp32)
 };
 
@@ -224,13 +224,16 @@ __device__ __forceinline__ bool wait_stage(uint32_t bar, uint32_t parity, unsign
 
 // kWarps warps per CTA, a kStages-deep copy ring per warp, kMinBlocks CTAs
 // per SM requested from the register allocator.
-template <int kWarps, int kStages, int kMinBlocks>
+// GT query heads per KV head (4 or 8): NT = GT / 4 column tiles of the MMAs,
+// each 4 queries x {hi, lo}.
+template <int kWarps, int kStages, int kMinBlocks, int GT>
 __global__ void __launch_bounds__(kWarps * 32, kMinBlocks)
 k_attn_ship_mma(SpAttnArgs a, Sched sc)
 {
-    static_assert(kWarps >= 4, "query preparation uses one warp per GQA query (up to 4)");
+    static_assert(GT == 4 || GT == 8, "4 or 8 query heads per KV head");
+    constexpr int NT = GT / 4;
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    Smem<kWarps, kStages> &sm = *reinterpret_cast<Smem<kWarps, kStages> *>(smem_raw);
+    Smem<kWarps, kStages, GT> &sm = *reinterpret_cast<Smem<kWarps, kStages, GT> *>(smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r = lane >> 2, c = lane & 3;
     const int cta = blockIdx.x;
@@ -307,45 +310,48 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
 
         // ---- queries of this (layer, KV head): q' = perm(H q) * scale ----
         __syncthreads();
-        if (warp < G) {
-            const __half *qg = a.q + ((long long)li * a.n_q_heads + h * G + warp) * kN;
-            float x[4];
+        for (int g = warp; g < GT; g += kWarps) {
+            if (g < G) {
+                const __half *qg = a.q + ((long long)li * a.n_q_heads + h * G + g) * kN;
+                float x[4];
 #pragma unroll
-            for (int e = 0; e < 4; e++) x[e] = __half2float(qg[lane * 4 + e]);
-            sp_warp_wht<4>(x, lane);
-            const float sc_all = a.logit_scale * 1.4426950408889634f * a.inv_sqrt_n;
+                for (int e = 0; e < 4; e++) x[e] = __half2float(qg[lane * 4 + e]);
+                sp_warp_wht<4>(x, lane);
+                const float sc_all = a.logit_scale * 1.4426950408889634f * a.inv_sqrt_n;
 #pragma unroll
-            for (int e = 0; e < 4; e++) sm.qt[warp][lane * 4 + e] = x[e] * sc_all;
-            __syncwarp();
-            float mx = 0.0f;
-            float bs = 0.0f;
+                for (int e = 0; e < 4; e++) sm.qt[g][lane * 4 + e] = x[e] * sc_all;
+                __syncwarp();
+                float mx = 0.0f;
+                float bs = 0.0f;
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int i = lane * 4 + e;
-                const float v = sm.qt[warp][a.order ? a.order[i] : i];
-                sm.q[warp][i] = v;
-                mx = fmaxf(mx, fabsf(v));
-                bs += v;
+                for (int e = 0; e < 4; e++) {
+                    const int i = lane * 4 + e;
+                    const float v = sm.qt[g][a.order ? a.order[i] : i];
+                    sm.q[g][i] = v;
+                    mx = fmaxf(mx, fabsf(v));
+                    bs += v;
+                }
+                // lanes 8b..8b+7 hold band b
+#pragma unroll
+                for (int o = 1; o < 8; o <<= 1) bs += __shfl_xor_sync(0xffffffffu, bs, o);
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                if ((lane & 7) == 0) sm.qsum[g][lane >> 3] = bs;
+                if (lane == 0) sm.qmax[g] = mx;
+            } else {
+                for (int i = lane; i < kN; i += 32) sm.q[g][i] = 0.0f;
+                if (lane < 4) sm.qsum[g][lane] = 0.0f;
+                if (lane == 0) sm.qmax[g] = 0.0f;
             }
-            // lanes 8b..8b+7 hold band b
-#pragma unroll
-            for (int o = 1; o < 8; o <<= 1) bs += __shfl_xor_sync(0xffffffffu, bs, o);
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            if ((lane & 7) == 0) sm.qsum[warp][lane >> 3] = bs;
-            if (lane == 0) sm.qmax[warp] = mx;
-        } else if (warp < 4) {
-            for (int i = lane; i < kN; i += 32) sm.q[warp][i] = 0.0f;
-            if (lane < 4) sm.qsum[warp][lane] = 0.0f;
-            if (lane == 0) sm.qmax[warp] = 0.0f;
         }
         __syncthreads();
 
         // B fragments of the K side: lane (r, c) supplies column r = query
         // r/2, fp16 part r%2, for the slots of lane group c.
-        uint32_t bq[8][2];
-        {
-            const int g = r >> 1;
+        uint32_t bq[NT][8][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            const int g = 4 * nt + (r >> 1);
             const float qm = sm.qmax[g];
             const int F = qm > 1e-30f ? 6 - ilogbf(qm) : 0;
 #pragma unroll
@@ -359,30 +365,36 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
                     const uint32_t slo = split_hi_lo(vlo), shi = split_hi_lo(vhi);
                     const uint32_t w = (r & 1) ? ((slo >> 16) | (shi & 0xffff0000u))
                                                : ((slo & 0xffffu) | (shi << 16));
-                    bq[2 * b + (p >> 1)][p & 1] = w;
+                    bq[nt][2 * b + (p >> 1)][p & 1] = w;
                 }
             }
         }
-        // Score constants for query c: s = kc * sum_b s_b (acc_b + cinit_b),
+        // Score constants for query 4nt + c: s = kc * sum_b s_b (acc_b + cinit_b),
         // cinit_b = -m_b * sum_{i in b} q'_i / kc.
-        float kc, cinit[4];
-        {
-            const float qm = sm.qmax[c];
+        float kc[NT], cinit[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            const int g = 4 * nt + c;
+            const float qm = sm.qmax[g];
             const int F = qm > 1e-30f ? 6 - ilogbf(qm) : 0;
-            kc = ldexpf(1.0f, 24 - F);
+            kc[nt] = ldexpf(1.0f, 24 - F);
 #pragma unroll
             for (int b = 0; b < 4; b++) {
                 const float m_b = (float)((1 << (kKBits(b) - 1)) - 1);
-                cinit[b] = b < a.nb_k ? -ldexpf(m_b * sm.qsum[c][b], F - 24) : 0.0f;
+                cinit[nt][b] = b < a.nb_k ? -ldexpf(m_b * sm.qsum[g][b], F - 24) : 0.0f;
             }
         }
 
-        float oacc[8][4];
+        float oacc[NT][8][4];
 #pragma unroll
-        for (int i = 0; i < 8; i++) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.0f;
+        for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+            for (int i = 0; i < 8; i++) oacc[nt][i][0] = oacc[nt][i][1] = oacc[nt][i][2] = oacc[nt][i][3] = 0.0f;
         // Running max of the scores in units of 1/kc (kc > 0, so it orders
         // like the base-2 logits); nkm = -kc * m_run.
-        float m_run = kEmptyMax, nkm = 0.0f, l_sum = 0.0f, p_sum = 0.0f;
+        float m_run[NT], nkm[NT], l_sum[NT], p_sum[NT];
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) { m_run[nt] = kEmptyMax; nkm[nt] = 0.0f; l_sum[nt] = 0.0f; p_sum[nt] = 0.0f; }
 
         // ---- my tiles of this segment ------------------------------------
         // Tile (within the unit) of my next tile; the segment ends when it
@@ -445,14 +457,16 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
             }
             // Band dot products; the accumulator starts at -m_b * sum(q') in
             // its hi column, so acc_hi + acc_lo = sum_i (u_i - m_b) q'_i / kc.
-            float acc[4][4];
+            float acc[NT][4][4];
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++)
 #pragma unroll
             for (int b = 0; b < 4; b++) {
-                acc[b][0] = cinit[b]; acc[b][1] = 0.0f; acc[b][2] = cinit[b]; acc[b][3] = 0.0f;
+                acc[nt][b][0] = cinit[nt][b]; acc[nt][b][1] = 0.0f; acc[nt][b][2] = cinit[nt][b]; acc[nt][b][3] = 0.0f;
 #pragma unroll
                 for (int j = 0; j < 2; j++)
-                    mma16816(acc[b], AK[0][4 * b + 2 * j], AK[1][4 * b + 2 * j], AK[0][4 * b + 2 * j + 1],
-                             AK[1][4 * b + 2 * j + 1], bq[2 * b + j][0], bq[2 * b + j][1]);
+                    mma16816(acc[nt][b], AK[0][4 * b + 2 * j], AK[1][4 * b + 2 * j], AK[0][4 * b + 2 * j + 1],
+                             AK[1][4 * b + 2 * j + 1], bq[nt][2 * b + j][0], bq[nt][2 * b + j][1]);
             }
 
             // -- V: unpack lane r's 16-coefficient chunk of token pairs
@@ -484,67 +498,76 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
 
             // -- scores of tokens r, r+8 for query c, in units of 1/kc --
             __syncwarp();
-            float su[2], vscale[2];
+            float vscale[2];
+            float4 fs[2];
 #pragma unroll
             for (int hh = 0; hh < 2; hh++) {
-                const float4 f = *reinterpret_cast<const float4 *>(&sm.scl[warp][r + 8 * hh][0]);
+                fs[hh] = *reinterpret_cast<const float4 *>(&sm.scl[warp][r + 8 * hh][0]);
                 vscale[hh] = sm.scl[warp][r + 8 * hh][4];
-                float v = f.x * (acc[0][2 * hh] + acc[0][2 * hh + 1]);
-                v = fmaf(f.y, acc[1][2 * hh] + acc[1][2 * hh + 1], v);
-                v = fmaf(f.z, acc[2][2 * hh] + acc[2][2 * hh + 1], v);
-                v = fmaf(f.w, acc[3][2 * hh] + acc[3][2 * hh + 1], v);
-                su[hh] = v;
             }
-            if (tok0 + 16 > a.kv_len) {       // last, partial tile of the unit
-                if (tok0 + r >= a.kv_len) su[0] = -INFINITY;
-                if (tok0 + r + 8 >= a.kv_len) su[1] = -INFINITY;
-            }
-            // -- online softmax (rescale only when the running max grows) --
-            const float mx = fmaxf(su[0], su[1]);
-            if (__any_sync(0xffffffffu, mx > m_run)) {
-                float mt = mx;
-                mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
-                mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
-                mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
-                const float m_new = fmaxf(m_run, mt);
-                const float alpha = fast_exp2(kc * (m_run - m_new));
-                m_run = m_new;
-                nkm = -kc * m_new;
-                l_sum *= alpha;
-                p_sum *= alpha;
 #pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    oacc[i][0] *= alpha; oacc[i][1] *= alpha;
-                    oacc[i][2] *= alpha; oacc[i][3] *= alpha;
+            for (int nt = 0; nt < NT; nt++) {
+                float su[2];
+#pragma unroll
+                for (int hh = 0; hh < 2; hh++) {
+                    const float4 f = fs[hh];
+                    float v = f.x * (acc[nt][0][2 * hh] + acc[nt][0][2 * hh + 1]);
+                    v = fmaf(f.y, acc[nt][1][2 * hh] + acc[nt][1][2 * hh + 1], v);
+                    v = fmaf(f.z, acc[nt][2][2 * hh] + acc[nt][2][2 * hh + 1], v);
+                    v = fmaf(f.w, acc[nt][3][2 * hh] + acc[nt][3][2 * hh + 1], v);
+                    su[hh] = v;
                 }
-            }
-            float pv[2];
+                if (tok0 + 16 > a.kv_len) {       // last, partial tile of the unit
+                    if (tok0 + r >= a.kv_len) su[0] = -INFINITY;
+                    if (tok0 + r + 8 >= a.kv_len) su[1] = -INFINITY;
+                }
+                // -- online softmax (rescale only when the running max grows) --
+                const float mx = fmaxf(su[0], su[1]);
+                if (__any_sync(0xffffffffu, mx > m_run[nt])) {
+                    float mt = mx;
+                    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+                    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+                    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+                    const float m_new = fmaxf(m_run[nt], mt);
+                    const float alpha = fast_exp2(kc[nt] * (m_run[nt] - m_new));
+                    m_run[nt] = m_new;
+                    nkm[nt] = -kc[nt] * m_new;
+                    l_sum[nt] *= alpha;
+                    p_sum[nt] *= alpha;
 #pragma unroll
-            for (int hh = 0; hh < 2; hh++) {
-                const float p = fast_exp2(fmaf(kc, su[hh], nkm));
-                l_sum += p;
-                pv[hh] = p * vscale[hh];
-                p_sum += pv[hh];
-            }
-            // -- P' (hi/lo) into the B layout of the V product --
-            uint32_t pk0, pk1;
-            {
-                const __half2 hi2 = __floats2half2_rn(pv[0], pv[1]);
-                const float2 back = __half22float2(hi2);
-                const __half2 lo2 = __floats2half2_rn(pv[0] - back.x, pv[1] - back.y);
-                const uint32_t hb = *reinterpret_cast<const uint32_t *>(&hi2);
-                const uint32_t lb = *reinterpret_cast<const uint32_t *>(&lo2);
-                pk0 = __byte_perm(hb, lb, 0x5410);
-                pk1 = __byte_perm(hb, lb, 0x7632);
-            }
-            const uint32_t x0 = __shfl_sync(0xffffffffu, pk0, src0);
-            const uint32_t x1 = __shfl_sync(0xffffffffu, pk0, src1);
-            const uint32_t x2 = __shfl_sync(0xffffffffu, pk1, src0);
-            const uint32_t x3 = __shfl_sync(0xffffffffu, pk1, src1);
-            const uint32_t pb0 = __byte_perm(x0, x1, psel), pb1 = __byte_perm(x2, x3, psel);
+                    for (int i = 0; i < 8; i++) {
+                        oacc[nt][i][0] *= alpha; oacc[nt][i][1] *= alpha;
+                        oacc[nt][i][2] *= alpha; oacc[nt][i][3] *= alpha;
+                    }
+                }
+                float pv[2];
 #pragma unroll
-            for (int mt = 0; mt < 8; mt++)
-                mma16816(oacc[mt], AV[0][2 * mt], AV[0][2 * mt + 1], AV[1][2 * mt], AV[1][2 * mt + 1], pb0, pb1);
+                for (int hh = 0; hh < 2; hh++) {
+                    const float p = fast_exp2(fmaf(kc[nt], su[hh], nkm[nt]));
+                    l_sum[nt] += p;
+                    pv[hh] = p * vscale[hh];
+                    p_sum[nt] += pv[hh];
+                }
+                // -- P' (hi/lo) into the B layout of the V product --
+                uint32_t pk0, pk1;
+                {
+                    const __half2 hi2 = __floats2half2_rn(pv[0], pv[1]);
+                    const float2 back = __half22float2(hi2);
+                    const __half2 lo2 = __floats2half2_rn(pv[0] - back.x, pv[1] - back.y);
+                    const uint32_t hb = *reinterpret_cast<const uint32_t *>(&hi2);
+                    const uint32_t lb = *reinterpret_cast<const uint32_t *>(&lo2);
+                    pk0 = __byte_perm(hb, lb, 0x5410);
+                    pk1 = __byte_perm(hb, lb, 0x7632);
+                }
+                const uint32_t x0 = __shfl_sync(0xffffffffu, pk0, src0);
+                const uint32_t x1 = __shfl_sync(0xffffffffu, pk0, src1);
+                const uint32_t x2 = __shfl_sync(0xffffffffu, pk1, src0);
+                const uint32_t x3 = __shfl_sync(0xffffffffu, pk1, src1);
+                const uint32_t pb0 = __byte_perm(x0, x1, psel), pb1 = __byte_perm(x2, x3, psel);
+#pragma unroll
+                for (int mt = 0; mt < 8; mt++)
+                    mma16816(oacc[nt][mt], AV[0][2 * mt], AV[0][2 * mt + 1], AV[1][2 * mt], AV[1][2 * mt + 1], pb0, pb1);
+            }
 
             __syncwarp();
             if (lane == 0 && k_next + kStages < n_my) issue(k_next + kStages);
@@ -552,25 +575,26 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
 
         // ---- warp partial -> shared memory ---------------------------------
 #pragma unroll
-        for (int o = 4; o < 32; o <<= 1) {
-            l_sum += __shfl_xor_sync(0xffffffffu, l_sum, o);
-            p_sum += __shfl_xor_sync(0xffffffffu, p_sum, o);
-        }
-        {
+        for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {
+                l_sum[nt] += __shfl_xor_sync(0xffffffffu, l_sum[nt], o);
+                p_sum[nt] += __shfl_xor_sync(0xffffffffu, p_sum[nt], o);
+            }
             const float mv = 3.0f;   // V offset 2^(3-1)-1
-            float *mrow = sm.merge[warp][c];
+            float *mrow = sm.merge[warp][4 * nt + c];
 #pragma unroll
             for (int mt = 0; mt < 8; mt++) {
 #pragma unroll
                 for (int rr = 0; rr < 2; rr++) {
                     const int j = 2 * mt + rr;
-                    const float v = ldexpf(oacc[mt][2 * rr] + oacc[mt][2 * rr + 1], 24 - vcode_d(j));
-                    mrow[4 + 16 * r + j] = v - mv * p_sum;
+                    const float v = ldexpf(oacc[nt][mt][2 * rr] + oacc[nt][mt][2 * rr + 1], 24 - vcode_d(j));
+                    mrow[4 + 16 * r + j] = v - mv * p_sum[nt];
                 }
             }
             if (r == 0) {
-                mrow[0] = fmaxf(kc * m_run, kEmptyMax);   // base-2 logit units
-                mrow[1] = l_sum;
+                mrow[0] = fmaxf(kc[nt] * m_run[nt], kEmptyMax);   // base-2 logit units
+                mrow[1] = l_sum[nt];
             }
         }
         __syncthreads();
@@ -649,7 +673,7 @@ int sp_attn_mma_supported(const SpAttnArgs &a)
         if (a.kl.size[b] != 32 || a.kl.bits[b] != kKBits(b) || a.kl.byte_off[b] * 8 + 16 != kKBit(b))
             return SP_ERR_UNSUPPORTED;
     if (a.kl.total_bytes != 76 || a.vl.total_bytes != 50 || a.vl.bits[0] != 3) return SP_ERR_UNSUPPORTED;
-    if (a.group < 1 || a.group > 4) return SP_ERR_UNSUPPORTED;
+    if (a.group < 1 || a.group > 8) return SP_ERR_UNSUPPORTED;
     // Whole 16-position tiles must lie inside each slot.
     const long long tiles = (a.kv_len + 15) / 16;
     if (tiles * kKTile > a.k_slot_stride || tiles * kVTile > a.v_slot_stride) return SP_ERR_UNSUPPORTED;
@@ -667,32 +691,36 @@ int sp_attn_mma_supported(const SpAttnArgs &a)
 // it; configurations that force fewer registers spill and run slower, and
 // deeper rings gain nothing (a ring of 4 already sustains the copy stream
 // at the HBM rate when the compute is removed).
-constexpr int kCtaWarps = 4, kRingStages = 4, kCtasPerSm = 3;
+// Up to 8 query heads per KV head (two column tiles, more registers): 2 CTAs/SM.
+constexpr int kCtaWarps = 4, kRingStages = 4, kCtasPerSm = 3, kCtasPerSm8 = 2;
 
 int sp_attn_mma_launch(const SpAttnArgs &a_in, cudaStream_t s, cudaEvent_t ev_begin, cudaEvent_t ev_end)
 {
     SpAttnArgs a = a_in;
-    auto kernel = k_attn_ship_mma<kCtaWarps, kRingStages, kCtasPerSm>;
-    const size_t smem = sizeof(Smem<kCtaWarps, kRingStages>);
+    const bool wide = a.group > 4;
+    void (*kernel)(SpAttnArgs, Sched) = wide ? k_attn_ship_mma<kCtaWarps, kRingStages, kCtasPerSm8, 8>
+                                             : k_attn_ship_mma<kCtaWarps, kRingStages, kCtasPerSm, 4>;
+    const size_t smem = wide ? sizeof(Smem<kCtaWarps, kRingStages, 8>) : sizeof(Smem<kCtaWarps, kRingStages, 4>);
     const int threads = kCtaWarps * 32;
-    static int occ_cached = 0, sms_cached = 0, dev_cached = -1;
+    static int occ_cached[2] = {0, 0}, sms_cached = 0, dev_cached[2] = {-1, -1};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev != dev_cached) {
+    if (dev != dev_cached[wide]) {
         if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return sp_check_cuda(cudaGetLastError(), "attention smem attribute");
         int occ = 0, sms = 0;
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, smem);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        occ_cached = occ > 0 ? occ : 1;
+        occ_cached[wide] = occ > 0 ? occ : 1;
         sms_cached = sms > 0 ? sms : 148;
-        dev_cached = dev;
+        dev_cached[wide] = dev;
     }
+    const int occ_now = occ_cached[wide];
     const int units = a.n_layers * a.n_kv_heads;
     Sched sc;
     sc.tiles_per_unit = (a.kv_len + 15) / 16;
     sc.total_tiles = (long long)units * sc.tiles_per_unit;
-    long long n = (long long)sms_cached * occ_cached;
+    long long n = (long long)sms_cached * occ_now;
     if (n > sc.total_tiles) n = sc.total_tiles;
     // At most kAttnMaxSplits segments per (layer, KV head): N/units + 2.
     if (n > (long long)units * (kAttnMaxSplits - 2)) n = (long long)units * (kAttnMaxSplits - 2);

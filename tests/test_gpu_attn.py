@@ -125,3 +125,24 @@ def test_kv_len_zero_and_errors(cuda):
     rc = L.sp_cuda_attn_decode(C.byref(cache.cc), 0, 1, q.data_ptr(), 8, 10_000, 1.0,
                                out.data_ptr(), -1, None)
     assert rc == spb200.SP_ERR_ARG                       # kv_len beyond the cache
+
+
+@pytest.mark.parametrize("G,kv_len", [(8, 2000), (8, 17), (3, 700), (1, 999)])
+def test_ship_decode_group_sizes(cuda, G, kv_len):
+    """The tensor-core kernel serves 1..8 query heads per KV head (8: two
+    MMA column tiles, as config 3's 32 Q / 4 KV heads)."""
+    import torch
+    n, H, L = 128, 2, 2
+    cache = _build(torch, L, H, 2048, n, seed=12)
+    q = synth.q_np(12, L, H * G, n, 1.0 / np.sqrt(128))
+    out = torch.empty(L, H * G, n, dtype=torch.float16, device="cuda")
+    spb200.lib().sp_cuda_attn_force_impl(2)          # the tensor-core kernel must take it
+    try:
+        cache.attn_decode(0, L, torch.from_numpy(q).cuda(), kv_len, out, logit_scale=0.7)
+        torch.cuda.synchronize()
+    finally:
+        spb200.lib().sp_cuda_attn_force_impl(0)
+    got = out.float().cpu().numpy()
+    for layer in range(L):
+        ref = _oracle(cache, layer, q[layer], kv_len, n, KB, VB, True, 0.7)
+        assert _rel_l2(got[layer], ref) <= RTOL_L2, (layer, G)
