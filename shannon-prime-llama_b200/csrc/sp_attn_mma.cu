@@ -148,7 +148,7 @@ __device__ __forceinline__ uint64_t evict_first_policy()
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1)
 {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
         "{%8,%9}, {%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -197,7 +197,7 @@ struct Smem {
     float qsum[GT][4];       // per query, per band: sum of q'
     float qmax[GT];
     float merge[kWarps][GT][4 + kN];
-    float scl[kWarps][16][8];   // per tile: K band scales 0..3, V scale (fp32)
+    float scl[kWarps][kStages][16][8];   // per stage: K band scales 0..3, V scale (fp32)
 };
 
 // Bounded wait on a ring stage.  Returns false (and flags the status word)
@@ -256,30 +256,41 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
     __syncwarp();
 
     // Issue cursor (lane 0): (layer index, KV head, tile) of the next of my
-    // tiles to fetch, advanced by kWarps tiles per issue without division.
+    // tiles to fetch and its K / V source addresses, advanced by kWarps
+    // tiles per issue.
     int ic_tile = 0, ic_h = 0, ic_li = 0;
+    const uint8_t *ic_k = nullptr, *ic_v = nullptr;
+    auto ic_point = [&]() {
+        const long long slot = (long long)(a.layer0 + ic_li) * H + ic_h;
+        ic_k = a.k_cache + slot * a.k_slot_stride + (long long)ic_tile * kKTile;
+        ic_v = a.v_cache + slot * a.v_slot_stride + (long long)ic_tile * kVTile;
+    };
     if (lane == 0 && n_my > 0) {
         const long long u0 = my_first / n_t;
         ic_tile = (int)(my_first - u0 * n_t);
         ic_h = (int)(u0 % H);
         ic_li = (int)(u0 / H);
+        ic_point();
     }
     auto issue = [&](int k) {
-        const long long slot = (long long)(a.layer0 + ic_li) * H + ic_h;
-        const uint8_t *ksrc = a.k_cache + slot * a.k_slot_stride + (long long)ic_tile * kKTile;
-        const uint8_t *vsrc = a.v_cache + slot * a.v_slot_stride + (long long)ic_tile * kVTile;
-        ic_tile += kWarps;
-        while (ic_tile >= n_t) {
-            ic_tile -= n_t;
-            if (++ic_h == H) { ic_h = 0; ++ic_li; }
-        }
         const int st = k % kStages;
         const uint32_t bar = bar0 + 8 * st;
         const uint32_t dst = ring0 + st * kStageBytes;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         mbar_expect_tx(bar, kStageBytes);
-        bulk_g2s(dst, ksrc, kKTile, bar, policy);
-        bulk_g2s(dst + kKTile, vsrc, kVTile, bar, policy);
+        bulk_g2s(dst, ic_k, kKTile, bar, policy);
+        bulk_g2s(dst + kKTile, ic_v, kVTile, bar, policy);
+        ic_tile += kWarps;
+        if (ic_tile < n_t) {
+            ic_k += kWarps * kKTile;
+            ic_v += kWarps * kVTile;
+        } else {
+            while (ic_tile >= n_t) {
+                ic_tile -= n_t;
+                if (++ic_h == H) { ic_h = 0; ++ic_li; }
+            }
+            ic_point();
+        }
     };
     if (lane == 0)
         for (int k = 0; k < kStages && k < n_my; k++) issue(k);
@@ -397,21 +408,20 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
         for (int nt = 0; nt < NT; nt++) { m_run[nt] = kEmptyMax; nkm[nt] = 0.0f; l_sum[nt] = 0.0f; p_sum[nt] = 0.0f; }
 
         // ---- my tiles of this segment ------------------------------------
-        // Tile (within the unit) of my next tile; the segment ends when it
-        // passes the unit's last tile.
-        int ctile = (int)(my_first + (long long)k_next * kWarps - u * n_t);
-        for (; k_next < n_my && ctile < n_t; ++k_next, ctile += kWarps) {
-            const int st = k_next % kStages;
-            if (!failed && !wait_stage(bar0 + 8 * st, (k_next / kStages) & 1, a.status)) failed = true;
-            if (failed) break;
+        // Two-stage software pipeline: iteration k computes the K-side
+        // scores of tile k+1 and the softmax weights + V product of tile k
+        // in one straight-line block, so the two dependency chains
+        // interleave in the schedule.  The running max is updated with the
+        // scores of tile k+1 only after tile k's weights are formed.
+        //
+        // K side of the tile in ring stage st (positions tok0..tok0+15):
+        // band scales to fp32 (scl[st]), code unpack, band MMAs, and the
+        // scores of positions r, r+8 for query 4nt+c in units of 1/kc.
+        auto k_scores = [&](int st, int tok0, float (&su)[NT][2]) {
             const unsigned char *kt = sm.ring[warp][st];
             const uint32_t *K32 = reinterpret_cast<const uint32_t *>(kt);
-            const uint32_t *V32 = reinterpret_cast<const uint32_t *>(kt + kKTile);
-            const int tok0 = ctile * 16;
-
-            // -- band scales of the tile to fp32, once per token: lane t<16
-            //    takes K bands 0,1 of token t, lane 16+t bands 2,3; every
-            //    lane converts the V scale of token t&15 --
+            // lane t<16 converts K bands 0,1 of position t, lane 16+t bands
+            // 2,3; every lane converts the V scale of position t&15.
             {
                 const int t = lane & 15, hi = lane >> 4;
                 const uint32_t *row = K32 + 19 * t;
@@ -419,12 +429,10 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
                 const uint32_t wb = row[hi ? kKScaleWord(3) : kKScaleWord(1)];
                 const uint32_t hw = __byte_perm(wa, wb, 0x7610);
                 const float2 f = __half22float2(finite_or_zero(*reinterpret_cast<const __half2 *>(&hw)));
-                *reinterpret_cast<float2 *>(&sm.scl[warp][t][2 * hi]) = f;
+                *reinterpret_cast<float2 *>(&sm.scl[warp][st][t][2 * hi]) = f;
                 const unsigned short vb = *reinterpret_cast<const unsigned short *>(kt + kKTile + 50 * t);
-                sm.scl[warp][t][4] = __low2float(finite_or_zero(__half2half2(__ushort_as_half(vb))));
+                sm.scl[warp][st][t][4] = __low2float(finite_or_zero(__half2half2(__ushort_as_half(vb))));
             }
-
-            // -- K: unpack the codes of tokens r and r+8 (4 bands) --
             uint32_t AK[2][16];
 #pragma unroll
             for (int hh = 0; hh < 2; hh++) {
@@ -461,17 +469,60 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
 #pragma unroll
             for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-            for (int b = 0; b < 4; b++) {
-                acc[nt][b][0] = cinit[nt][b]; acc[nt][b][1] = 0.0f; acc[nt][b][2] = cinit[nt][b]; acc[nt][b][3] = 0.0f;
+                for (int b = 0; b < 4; b++) {
+                    acc[nt][b][0] = cinit[nt][b]; acc[nt][b][1] = 0.0f; acc[nt][b][2] = cinit[nt][b]; acc[nt][b][3] = 0.0f;
 #pragma unroll
-                for (int j = 0; j < 2; j++)
-                    mma16816(acc[nt][b], AK[0][4 * b + 2 * j], AK[1][4 * b + 2 * j], AK[0][4 * b + 2 * j + 1],
-                             AK[1][4 * b + 2 * j + 1], bq[nt][2 * b + j][0], bq[nt][2 * b + j][1]);
+                    for (int j = 0; j < 2; j++)
+                        mma16816(acc[nt][b], AK[0][4 * b + 2 * j], AK[1][4 * b + 2 * j], AK[0][4 * b + 2 * j + 1],
+                                 AK[1][4 * b + 2 * j + 1], bq[nt][2 * b + j][0], bq[nt][2 * b + j][1]);
+                }
+            __syncwarp();
+            float4 fs[2];
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) fs[hh] = *reinterpret_cast<const float4 *>(&sm.scl[warp][st][r + 8 * hh][0]);
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+                for (int hh = 0; hh < 2; hh++) {
+                    const float4 f = fs[hh];
+                    float v = f.x * (acc[nt][0][2 * hh] + acc[nt][0][2 * hh + 1]);
+                    v = fmaf(f.y, acc[nt][1][2 * hh] + acc[nt][1][2 * hh + 1], v);
+                    v = fmaf(f.z, acc[nt][2][2 * hh] + acc[nt][2][2 * hh + 1], v);
+                    v = fmaf(f.w, acc[nt][3][2 * hh] + acc[nt][3][2 * hh + 1], v);
+                    su[nt][hh] = tok0 + r + 8 * hh < a.kv_len ? v : -INFINITY;
+                }
             }
-
-            // -- V: unpack lane r's 16-coefficient chunk of token pairs
-            //    (2c, 2c+1) and (2c+8, 2c+9); independent of the softmax, so
-            //    issued before it --
+        };
+        // Online softmax max update (rescale only when the running max grows).
+        auto update_max = [&](const float (&su)[NT][2]) {
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+                const float mx = fmaxf(su[nt][0], su[nt][1]);
+                if (__any_sync(0xffffffffu, mx > m_run[nt])) {
+                    float mt = mx;
+                    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+                    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+                    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+                    const float m_new = fmaxf(m_run[nt], mt);
+                    const float alpha = fast_exp2(kc[nt] * (m_run[nt] - m_new));
+                    m_run[nt] = m_new;
+                    nkm[nt] = -kc[nt] * m_new;
+                    l_sum[nt] *= alpha;
+                    p_sum[nt] *= alpha;
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        oacc[nt][i][0] *= alpha; oacc[nt][i][1] *= alpha;
+                        oacc[nt][i][2] *= alpha; oacc[nt][i][3] *= alpha;
+                    }
+                }
+            }
+        };
+        // Softmax weights of the tile in stage st and its V product: lane r
+        // unpacks its 16-coefficient chunk of position pairs (2c, 2c+1) and
+        // (2c+8, 2c+9).
+        auto v_step = [&](int st, const float (&su)[NT][2]) {
+            const unsigned char *kt = sm.ring[warp][st];
+            const uint32_t *V32 = reinterpret_cast<const uint32_t *>(kt + kKTile);
             uint32_t AV[2][16];
 #pragma unroll
             for (int hh = 0; hh < 2; hh++) {
@@ -495,60 +546,20 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
                 }
                 AV[hh][15] = W[3] & 0x00070007u;
             }
-
-            // -- scores of tokens r, r+8 for query c, in units of 1/kc --
-            __syncwarp();
             float vscale[2];
-            float4 fs[2];
 #pragma unroll
-            for (int hh = 0; hh < 2; hh++) {
-                fs[hh] = *reinterpret_cast<const float4 *>(&sm.scl[warp][r + 8 * hh][0]);
-                vscale[hh] = sm.scl[warp][r + 8 * hh][4];
-            }
+            for (int hh = 0; hh < 2; hh++) vscale[hh] = sm.scl[warp][st][r + 8 * hh][4];
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
-                float su[2];
-#pragma unroll
-                for (int hh = 0; hh < 2; hh++) {
-                    const float4 f = fs[hh];
-                    float v = f.x * (acc[nt][0][2 * hh] + acc[nt][0][2 * hh + 1]);
-                    v = fmaf(f.y, acc[nt][1][2 * hh] + acc[nt][1][2 * hh + 1], v);
-                    v = fmaf(f.z, acc[nt][2][2 * hh] + acc[nt][2][2 * hh + 1], v);
-                    v = fmaf(f.w, acc[nt][3][2 * hh] + acc[nt][3][2 * hh + 1], v);
-                    su[hh] = v;
-                }
-                if (tok0 + 16 > a.kv_len) {       // last, partial tile of the unit
-                    if (tok0 + r >= a.kv_len) su[0] = -INFINITY;
-                    if (tok0 + r + 8 >= a.kv_len) su[1] = -INFINITY;
-                }
-                // -- online softmax (rescale only when the running max grows) --
-                const float mx = fmaxf(su[0], su[1]);
-                if (__any_sync(0xffffffffu, mx > m_run[nt])) {
-                    float mt = mx;
-                    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
-                    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
-                    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
-                    const float m_new = fmaxf(m_run[nt], mt);
-                    const float alpha = fast_exp2(kc[nt] * (m_run[nt] - m_new));
-                    m_run[nt] = m_new;
-                    nkm[nt] = -kc[nt] * m_new;
-                    l_sum[nt] *= alpha;
-                    p_sum[nt] *= alpha;
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        oacc[nt][i][0] *= alpha; oacc[nt][i][1] *= alpha;
-                        oacc[nt][i][2] *= alpha; oacc[nt][i][3] *= alpha;
-                    }
-                }
                 float pv[2];
 #pragma unroll
                 for (int hh = 0; hh < 2; hh++) {
-                    const float p = fast_exp2(fmaf(kc[nt], su[hh], nkm[nt]));
+                    const float p = fast_exp2(fmaf(kc[nt], su[nt][hh], nkm[nt]));
                     l_sum[nt] += p;
                     pv[hh] = p * vscale[hh];
                     p_sum[nt] += pv[hh];
                 }
-                // -- P' (hi/lo) into the B layout of the V product --
+                // P' (hi/lo) into the B layout of the V product.
                 uint32_t pk0, pk1;
                 {
                     const __half2 hi2 = __floats2half2_rn(pv[0], pv[1]);
@@ -568,9 +579,38 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
                 for (int mt = 0; mt < 8; mt++)
                     mma16816(oacc[nt][mt], AV[0][2 * mt], AV[0][2 * mt + 1], AV[1][2 * mt], AV[1][2 * mt + 1], pb0, pb1);
             }
+        };
 
-            __syncwarp();
-            if (lane == 0 && k_next + kStages < n_my) issue(k_next + kStages);
+        int ctile = (int)(my_first + (long long)k_next * kWarps - u * n_t);
+        if (k_next < n_my && ctile < n_t) {
+            float su[NT][2];
+            if (!wait_stage(bar0 + 8 * (k_next % kStages), (k_next / kStages) & 1, a.status)) {
+                failed = true;
+            } else {
+                k_scores(k_next % kStages, ctile * 16, su);
+                update_max(su);
+            }
+            while (!failed) {
+                const int kn = k_next + 1, ctn = ctile + kWarps;
+                const bool has_next = kn < n_my && ctn < n_t;
+                if (has_next && !wait_stage(bar0 + 8 * (kn % kStages), (kn / kStages) & 1, a.status)) {
+                    failed = true;
+                    break;
+                }
+                // Without a next tile of this segment, the scores below are
+                // taken on whatever the next stage holds and discarded.
+                float sn[NT][2];
+                k_scores(kn % kStages, ctn * 16, sn);
+                v_step(k_next % kStages, su);
+                if (has_next) update_max(sn);
+                __syncwarp();
+                if (lane == 0 && k_next + kStages < n_my) issue(k_next + kStages);
+                k_next = kn;
+                ctile = ctn;
+                if (!has_next) break;
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) { su[nt][0] = sn[nt][0]; su[nt][1] = sn[nt][1]; }
+            }
         }
 
         // ---- warp partial -> shared memory ---------------------------------

@@ -113,6 +113,125 @@ __device__ void vilenkin_warp(float *buf, const SpSqDev &t, const float *cas_s, 
     }
 }
 
+// Hartley (cas) tables of the five primes, concatenated in the order
+// 2, 3, 5, 7, 11 (offsets 0, 4, 13, 38, 87), and 1/sqrt(p) in the same
+// order, as fp32 values computed on the host in double.  In constant memory
+// every lane reads the same entry, so each fma takes its coefficient
+// straight from the constant bank.
+__constant__ float c_sq_cas[208];
+__constant__ float c_sq_isp[5];
+
+template <int P>
+__host__ __device__ constexpr int prime_slot()
+{
+    return P == 2 ? 0 : P == 3 ? 1 : P == 5 ? 2 : P == 7 ? 3 : 4;
+}
+template <int P>
+__host__ __device__ constexpr int cas_base()
+{
+    return P == 2 ? 0 : P == 3 ? 4 : P == 5 ? 13 : P == 7 ? 38 : 87;
+}
+
+// One stage of the compile-time transform: the same arithmetic as
+// vilenkin_stage (an fma chain over j, then one multiply by 1/sqrt(p)), with
+// the group layout fixed at compile time.
+template <int PD, int P, int STRIDE>
+__device__ __forceinline__ void vstage_c(float *buf, int lane)
+{
+    constexpr int groups = PD / P;
+    const float isp = c_sq_isp[prime_slot<P>()];
+#pragma unroll
+    for (int g0 = 0; g0 < groups; g0 += 32) {
+        const int g = g0 + lane;
+        if (g < groups) {
+            const int blk = g / STRIDE;
+            const int base = blk * (STRIDE * P) + (g - blk * STRIDE);
+            float x[P];
+#pragma unroll
+            for (int j = 0; j < P; j++) x[j] = buf[base + j * STRIDE];
+#pragma unroll
+            for (int k = 0; k < P; k++) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int j = 0; j < P; j++) acc = __fmaf_rn(c_sq_cas[cas_base<P>() + k * P + j], x[j], acc);
+                buf[base + k * STRIDE] = __fmul_rn(acc, isp);
+            }
+        }
+    }
+}
+
+// Compile-time staged transform of buf[0..PD) for the pad sizes of head_dim
+// 32, 64, 128 and 256 (33 = 3.11, 66 = 2.3.11, 154 = 2.7.11,
+// 330 = 2.3.5.11): primes ascending, strides growing.
+template <int PD>
+__device__ __forceinline__ void vilenkin_pd(float *buf, int lane)
+{
+    if constexpr (PD == 33) {
+        vstage_c<33, 3, 1>(buf, lane); __syncwarp();
+        vstage_c<33, 11, 3>(buf, lane); __syncwarp();
+    } else if constexpr (PD == 66) {
+        vstage_c<66, 2, 1>(buf, lane); __syncwarp();
+        vstage_c<66, 3, 2>(buf, lane); __syncwarp();
+        vstage_c<66, 11, 6>(buf, lane); __syncwarp();
+    } else if constexpr (PD == 154) {
+        vstage_c<154, 2, 1>(buf, lane); __syncwarp();
+        vstage_c<154, 7, 2>(buf, lane); __syncwarp();
+        vstage_c<154, 11, 14>(buf, lane); __syncwarp();
+    } else {
+        static_assert(PD == 330, "pad size without a compile-time plan");
+        vstage_c<330, 2, 1>(buf, lane); __syncwarp();
+        vstage_c<330, 3, 2>(buf, lane); __syncwarp();
+        vstage_c<330, 5, 6>(buf, lane); __syncwarp();
+        vstage_c<330, 11, 30>(buf, lane); __syncwarp();
+    }
+}
+
+__host__ __device__ constexpr bool sq_fast_pd(int pd) { return pd == 33 || pd == 66 || pd == 154 || pd == 330; }
+
+// Transform by the compile-time plan when PD names one, else by the
+// table-driven stages.
+template <int PD>
+__device__ __forceinline__ void vilenkin_sel(float *buf, const SpSqDev &t, const float *cas_s, int lane)
+{
+    if constexpr (PD != 0) vilenkin_pd<PD>(buf, lane);
+    else vilenkin_warp(buf, t, cas_s, lane);
+}
+
+// Row stride (floats) of the fp32 copy of W in shared memory: a multiple of
+// 4 with an odd quotient, so the 16-byte loads of 8 consecutive rows hit
+// distinct banks.
+__host__ __device__ inline int hier_w_stride(int n_skel)
+{
+    int ws = (n_skel + 3) & ~3;
+    if (((ws >> 2) & 1) == 0) ws += 4;
+    return ws;
+}
+
+// W . skeleton for residual r with the skeleton held in registers (the fma
+// chain in s order of hier_predict).
+template <int NSK>
+__device__ __forceinline__ float hier_predict_reg(const float *W, int ws, const float (&sk)[NSK], int r)
+{
+    const float *w = W + (size_t)r * ws;
+    float acc = 0.0f;
+#pragma unroll
+    for (int s0 = 0; s0 < NSK; s0 += 4) {
+        const float4 w4 = *reinterpret_cast<const float4 *>(w + s0);
+        acc = __fmaf_rn(w4.x, sk[s0], acc);
+        if (s0 + 1 < NSK) acc = __fmaf_rn(w4.y, sk[s0 + 1], acc);
+        if (s0 + 2 < NSK) acc = __fmaf_rn(w4.z, sk[s0 + 2], acc);
+        if (s0 + 3 < NSK) acc = __fmaf_rn(w4.w, sk[s0 + 3], acc);
+    }
+    return acc;
+}
+
+template <int NSK>
+__device__ __forceinline__ void load_skel_regs(const float *skel, float (&sk)[NSK])
+{
+#pragma unroll
+    for (int s = 0; s < NSK; s++) sk[s] = skel[s];
+}
+
 // OR the low `bits` bits of v into the packed row at bit position pos.
 __device__ __forceinline__ void row_or(uint32_t *row, int pos, uint32_t v, int bits)
 {
@@ -197,7 +316,7 @@ __device__ __forceinline__ float csr_predict(const int *csr_off, const int *csr_
 
 __device__ __forceinline__ float hier_predict(const float *W, const float *skel, int n_skel, int r)
 {
-    const float *w = W + (size_t)r * n_skel;
+    const float *w = W + (size_t)r * hier_w_stride(n_skel);
     float acc = 0.0f;
     for (int s = 0; s < n_skel; s++) acc = __fmaf_rn(w[s], skel[s], acc);
     return acc;
@@ -220,7 +339,7 @@ size_t sq_smem_bytes(const SpSqDev &t)
     size_t s = (size_t)tab_len(t) * 4 + 224 * 4;
     s += (size_t)kSqWarps * (t.pd + t.n_skel + t.n_res + 4) * 4;   // buf, skel, dev
     s += (size_t)kSqWarps * kSqRowWords * 4;
-    if (t.hier) s += (size_t)t.n_res * t.n_skel * 4;
+    if (t.hier) s += (size_t)t.n_res * hier_w_stride(t.n_skel) * 4;
     return s + 64;
 }
 
@@ -244,8 +363,9 @@ __device__ SqSmem sq_carve(unsigned char *smem, const SpSqDev &t, int warp)
     s.skel = mine + t.pd;
     s.dev = s.skel + t.n_skel;
     s.row = reinterpret_cast<uint32_t *>(f + (size_t)kSqWarps * per) + warp * kSqRowWords;
-    s.W = reinterpret_cast<float *>(reinterpret_cast<uint32_t *>(f + (size_t)kSqWarps * per) +
-                                    kSqWarps * kSqRowWords);
+    const uintptr_t w0 = reinterpret_cast<uintptr_t>(reinterpret_cast<uint32_t *>(f + (size_t)kSqWarps * per) +
+                                                     kSqWarps * kSqRowWords);
+    s.W = reinterpret_cast<float *>((w0 + 15) & ~uintptr_t(15));    // 16-byte rows for float4 loads
     return s;
 }
 
@@ -256,13 +376,17 @@ __device__ void sq_load_common(unsigned char *smem, const SpSqDev &t, const SqIo
     for (int i = threadIdx.x; i < 224; i += blockDim.x) s0.cas[i] = t.cas[i];
     if (t.hier) {
         const __half *w = io.W + (size_t)slot * t.n_res * t.n_skel;
-        for (int i = threadIdx.x; i < t.n_res * t.n_skel; i += blockDim.x) s0.W[i] = __half2float(w[i]);
+        const int ws = hier_w_stride(t.n_skel);
+        for (int i = threadIdx.x; i < t.n_res * t.n_skel; i += blockDim.x) {
+            const int r = i / t.n_skel, c = i - r * t.n_skel;
+            s0.W[r * ws + c] = __half2float(w[i]);
+        }
     }
     __syncthreads();
 }
 
 // Compress.  Grid: x = token chunks, y = slot within the call (layer-major).
-template <typename Tin>
+template <typename Tin, int PD>
 __global__ void __launch_bounds__(kSqWarps * 32)
 k_sq_encode(SpSqDev t, SqIo io)
 {
@@ -291,17 +415,23 @@ k_sq_encode(SpSqDev t, SqIo io)
         for (int i = t.hd + lane; i < t.pd; i += 32) S.buf[i] = mean;
         for (int j = lane; j < words; j += 32) S.row[j] = 0u;
         __syncwarp();
-        vilenkin_warp(S.buf, t, S.cas, lane);
+        vilenkin_sel<PD>(S.buf, t, S.cas, lane);
         for (int s = lane; s < t.n_skel; s += 32) S.skel[s] = S.buf[skel_idx[s]];
         __syncwarp();
         quantize_skeleton(S.skel, S.row, t.bl, lane);
         if (t.n_res > 0) {
+            constexpr int NSK = PD > 0 ? PD / 11 : 1;    // hier skeleton size of the compile-time plans
+            float skr[NSK];
+            if constexpr (PD > 0) if (t.hier) load_skel_regs(S.skel, skr);
             float asum = 0.0f;
             for (int r = lane; r < t.n_res; r += 32) {
                 const float a = S.buf[res_idx[r]];
                 float d;
                 if (t.hier) {
-                    d = __fsub_rn(a, hier_predict(S.W, S.skel, t.n_skel, r));
+                    float p;
+                    if constexpr (PD > 0) p = hier_predict_reg<NSK>(S.W, hier_w_stride(NSK), skr, r);
+                    else p = hier_predict(S.W, S.skel, t.n_skel, r);
+                    d = __fsub_rn(a, p);
                 } else {
                     const float p = csr_predict(csr_off, csr_term, S.skel, r);
                     if (t.use_spinor) {
@@ -375,6 +505,7 @@ __device__ __forceinline__ void load_row(uint32_t *row, const uint8_t *src, int 
 
 // Coefficient vector of one packed slot into buf[0..pd) (before the inverse
 // transform).  skel/dev are per-warp shared scratch.
+template <int PD>
 __device__ void sq_coeffs(const SpSqDev &t, const SqSmem &S, const float *W, int lane)
 {
     const int *skel_idx = S.tab + tab_skel(t), *res_idx = S.tab + tab_res(t);
@@ -396,12 +527,16 @@ __device__ void sq_coeffs(const SpSqDev &t, const SqSmem &S, const float *W, int
             const float sat = __fmul_rn(mag, (float)t.res_bits);
             step = L > 1 ? __fdiv_rn(__fmul_rn(2.0f, sat), (float)(L - 1)) : 0.0f;
         }
+        constexpr int NSK = PD > 0 ? PD / 11 : 1;
+        float skr[NSK];
+        if constexpr (PD > 0) if (t.hier) { __syncwarp(); load_skel_regs(S.skel, skr); }
         for (int r = lane; r < t.n_res; r += 32) {
             const uint32_t lv = row_bits(S.row, 8 * t.res_off + r * t.res_bits, t.res_bits);
             const float dev = __fmul_rn(__fsub_rn((float)lv, center), step);
             float p;
             if (t.hier) {
-                p = hier_predict(W, S.skel, t.n_skel, r);
+                if constexpr (PD > 0) p = hier_predict_reg<NSK>(W, hier_w_stride(NSK), skr, r);
+                else p = hier_predict(W, S.skel, t.n_skel, r);
             } else {
                 p = csr_predict(csr_off, csr_term, S.skel, r);
                 if (t.use_spinor && row_bits(S.row, 8 * t.sheet_off + r, 1)) p = -p;
@@ -413,6 +548,7 @@ __device__ void sq_coeffs(const SpSqDev &t, const SqSmem &S, const float *W, int
 }
 
 // Decompress.  Grid: x = position chunks, y = slot within the call.
+template <int PD>
 __global__ void __launch_bounds__(kSqWarps * 32)
 k_sq_decode(SpSqDev t, SqIo io)
 {
@@ -429,8 +565,8 @@ k_sq_decode(SpSqDev t, SqIo io)
                              (long long)(io.start_pos + tok) * t.bytes_per_pos;
         load_row(S.row, src, t.bytes_per_pos, io.store_width, lane);
         __syncwarp();
-        sq_coeffs(t, S, S.W, lane);
-        vilenkin_warp(S.buf, t, S.cas, lane);
+        sq_coeffs<PD>(t, S, S.W, lane);
+        vilenkin_sel<PD>(S.buf, t, S.cas, lane);
         float *dst = io.single_slot ? io.out + (long long)tok * t.hd
                                     : io.out + (((long long)li * io.n_tok + tok) * io.nh + h) * t.hd;
         for (int i = lane; i < t.hd; i += 32) dst[i] = S.buf[i];
@@ -521,7 +657,7 @@ k_sq_attn(SpSqDev tk, SpSqDev tv, SqAttn a)
         load_row(S.row, a.k_cache + slot * a.k_slot_stride + (long long)tok * tk.bytes_per_pos,
                  tk.bytes_per_pos, a.store_width_k, lane);
         __syncwarp();
-        sq_coeffs(tk, S, nullptr, lane);
+        sq_coeffs<0>(tk, S, nullptr, lane);
         float s[8];
 #pragma unroll
         for (int g = 0; g < 8; g++) {
@@ -537,7 +673,7 @@ k_sq_attn(SpSqDev tk, SpSqDev tv, SqAttn a)
         load_row(S.row, a.v_cache + slot * a.v_slot_stride + (long long)tok * tv.bytes_per_pos,
                  tv.bytes_per_pos, a.store_width_v, lane);
         __syncwarp();
-        sq_coeffs(tv, S, nullptr, lane);
+        sq_coeffs<0>(tv, S, nullptr, lane);
 #pragma unroll
         for (int g = 0; g < 8; g++) {
             if (g >= G) break;
@@ -1014,6 +1150,15 @@ int store_width_for(int bytes, long long stride, const void *base)
     return (x & 3) == 0 ? 4 : ((x & 1) == 0 ? 2 : 1);
 }
 
+// Pad size of the compile-time plan for t (0: table-driven kernels).  The
+// hier plans assume the skeleton of pad_dim / 11 values.
+int sq_plan_pd(const SpSqDev &t)
+{
+    if (!sq_fast_pd(t.pd)) return 0;
+    if (t.hier && t.n_skel != t.pd / 11) return 0;
+    return t.pd;
+}
+
 int sq_launch_encode(const SpSqDev &t, SqIo io, int dtype, cudaStream_t s)
 {
     if (io.n_tok <= 0 || io.n_layers <= 0) return SP_OK;
@@ -1027,27 +1172,20 @@ int sq_launch_encode(const SpSqDev &t, SqIo io, int dtype, cudaStream_t s)
     if (chunks < 1) chunks = 1;
     io.tokens_per_cta = (io.n_tok + chunks - 1) / chunks;
     dim3 grid(chunks, slots);
+    const int pd = sq_plan_pd(t);
+    void (*k)(SpSqDev, SqIo) = nullptr;
+#define SQ_ENC(T)                                                                          \
+    k = pd == 33 ? k_sq_encode<T, 33> : pd == 66 ? k_sq_encode<T, 66> :                    \
+        pd == 154 ? k_sq_encode<T, 154> : pd == 330 ? k_sq_encode<T, 330> : k_sq_encode<T, 0>
     switch (dtype) {
-    case SP_DTYPE_F32: {
-        auto k = k_sq_encode<float>;
-        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-        k<<<grid, kSqWarps * 32, sm, s>>>(t, io);
-        break;
-    }
-    case SP_DTYPE_F16: {
-        auto k = k_sq_encode<__half>;
-        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-        k<<<grid, kSqWarps * 32, sm, s>>>(t, io);
-        break;
-    }
-    case SP_DTYPE_BF16: {
-        auto k = k_sq_encode<__nv_bfloat16>;
-        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-        k<<<grid, kSqWarps * 32, sm, s>>>(t, io);
-        break;
-    }
+    case SP_DTYPE_F32: SQ_ENC(float); break;
+    case SP_DTYPE_F16: SQ_ENC(__half); break;
+    case SP_DTYPE_BF16: SQ_ENC(__nv_bfloat16); break;
     default: return sp_set_error(SP_ERR_ARG, "sqfree/hier write: unknown dtype %d", dtype);
     }
+#undef SQ_ENC
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    k<<<grid, kSqWarps * 32, sm, s>>>(t, io);
     return sp_check_cuda(cudaGetLastError(), "sqfree/hier encode launch");
 }
 
@@ -1062,8 +1200,11 @@ int sq_launch_decode(const SpSqDev &t, SqIo io, cudaStream_t s)
     if (chunks > max_chunks) chunks = max_chunks;
     if (chunks < 1) chunks = 1;
     io.tokens_per_cta = (io.n_tok + chunks - 1) / chunks;
-    cudaFuncSetAttribute(k_sq_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    k_sq_decode<<<dim3(chunks, slots), kSqWarps * 32, sm, s>>>(t, io);
+    const int pd = sq_plan_pd(t);
+    void (*k)(SpSqDev, SqIo) = pd == 33 ? k_sq_decode<33> : pd == 66 ? k_sq_decode<66>
+                             : pd == 154 ? k_sq_decode<154> : pd == 330 ? k_sq_decode<330> : k_sq_decode<0>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    k<<<dim3(chunks, slots), kSqWarps * 32, sm, s>>>(t, io);
     return sp_check_cuda(cudaGetLastError(), "sqfree/hier decode launch");
 }
 
@@ -1071,6 +1212,31 @@ int sq_launch_decode(const SpSqDev &t, SqIo io, cudaStream_t s)
 struct SqHost {
     SpSqDev t;
 };
+
+// Upload the constant-memory cas tables to the current device (once per
+// device; called from the cache constructors, outside any stream capture).
+int sq_upload_constants()
+{
+    static bool done[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && done[dev]) return SP_OK;
+    float cas[208], isp[5];
+    int off = 0, i = 0;
+    for (int p : {2, 3, 5, 7, 11}) {
+        for (int k = 0; k < p; k++)
+            for (int j = 0; j < p; j++) {
+                const double ang = 2.0 * 3.14159265358979323846 * (double)((k * j) % p) / (double)p;
+                cas[off + k * p + j] = (float)(cos(ang) + sin(ang));
+            }
+        off += p * p;
+        isp[i++] = (float)(1.0 / sqrt((double)p));
+    }
+    int rc = sp_check_cuda(cudaMemcpyToSymbol(c_sq_cas, cas, sizeof(cas)), "sqfree cas tables");
+    if (!rc) rc = sp_check_cuda(cudaMemcpyToSymbol(c_sq_isp, isp, sizeof(isp)), "sqfree cas tables");
+    if (!rc && dev >= 0 && dev < 64) done[dev] = true;
+    return rc;
+}
 
 int sq_build_desc(SpSqDev &t, int hd, int pd, int n_skel, int n_res, int n_terms,
                   const sp_band_config_t &bands, int res_bits, int use_spinor, int hier,
@@ -1219,7 +1385,8 @@ int sp_cuda_sqfree_cache_init_ex(sp_cuda_sqfree_cache_t *cc, const sp_config_t *
     cudaMemset(cc->d_k_cache, 0, k_total * cc->bytes_per_pos_k);
     cudaMemset(cc->d_v_cache, 0, k_total * cc->bytes_per_pos_v);
     cc->attn_ws_bytes = (size_t)cfg->n_layers * 8 * cfg->n_heads_kv * kSqMaxSplits * (pd + 4) * sizeof(float);
-    if ((rc = sp_check_cuda(cudaMalloc(&cc->d_attn_ws, cc->attn_ws_bytes), "cudaMalloc sqfree workspace")) ||
+    if ((rc = sq_upload_constants()) ||
+        (rc = sp_check_cuda(cudaMalloc(&cc->d_attn_ws, cc->attn_ws_bytes), "cudaMalloc sqfree workspace")) ||
         (rc = sp_check_cuda(cudaDeviceSynchronize(), "sqfree_cache_init"))) {
         sp_cuda_sqfree_cache_free(cc);
         return rc;
@@ -1485,7 +1652,10 @@ int sp_cuda_hier_cache_init(sp_cuda_hier_cache_t *hc, const sp_config_t *cfg, in
     cudaMemset(hc->d_k_cache, 0, total);
     cudaMemset(hc->d_v_cache, 0, total);
     cudaMemset(hc->d_W, 0, (size_t)n_slots * n_target * n_skeleton * 2);
-    if ((rc = sp_check_cuda(cudaDeviceSynchronize(), "hier_cache_init"))) { sp_cuda_hier_cache_free(hc); return rc; }
+    if ((rc = sq_upload_constants()) || (rc = sp_check_cuda(cudaDeviceSynchronize(), "hier_cache_init"))) {
+        sp_cuda_hier_cache_free(hc);
+        return rc;
+    }
     return SP_OK;
 }
 
