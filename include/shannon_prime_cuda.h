@@ -220,6 +220,9 @@ typedef struct {
     void            *d_attn_ws;         /* fused-decode partials */
     size_t           attn_ws_bytes;
     int              csr_max_terms;     /* most Möbius terms of one residual */
+    int              lane_max_terms;    /* most Möbius terms of one lane under the balanced
+                                           residual-to-lane assignment of the blocked decode
+                                           (0: the assignment needs more than 2 residuals per lane) */
 } sp_cuda_sqfree_cache_t;
 
 /* Reference signature; the skeleton is pad_dim / 2 as in the reference CUDA

@@ -42,6 +42,7 @@
 // balance is exact to a tile; a CTA writes one partial per (layer, KV head)
 // segment it touches, and a combine kernel merges the segments.
 #include "sp_attn.cuh"
+#include "sp_bulk.cuh"
 
 #include <math.h>
 #include <stdlib.h>
@@ -54,7 +55,6 @@ constexpr int kVTile = 16 * 50;       // 800
 constexpr int kStageBytes = kKTile + kVTile;   // 2016
 constexpr int kN = 128;
 constexpr float kEmptyMax = -1.0e30f; // running max before the first valid token
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;   // 2 s per stage wait
 
 // Fixed ship layout (checked on the host against the cache's band config).
 // Bit position of band b's first code within a K row.
@@ -99,51 +99,12 @@ __host__ __device__ inline int cta_of_tile(long long g, const Sched &s)
 
 // ------------------------------------------------------------------ PTX --
 
-__device__ __forceinline__ uint32_t smem_u32(const void *p)
-{
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count)
-{
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
-{
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
-{
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar,
-                                         uint64_t policy)
-{
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
-        "[%0], [%1], %2, [%3], %4;" ::"r"(dst),
-        "l"(src), "r"(bytes), "r"(bar), "l"(policy)
-        : "memory");
-}
-
-__device__ __forceinline__ uint64_t evict_first_policy()
-{
-    uint64_t p;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-    return p;
-}
+using spb::smem_u32;
+using spb::mbar_init;
+using spb::mbar_expect_tx;
+using spb::bulk_g2s;
+using spb::evict_first_policy;
+using spb::wait_stage;
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1)
@@ -200,28 +161,6 @@ struct Smem {
     float scl[kWarps][kStages][16][8];   // per stage: K band scales 0..3, V scale (fp32)
 };
 
-// Bounded wait on a ring stage.  Returns false (and flags the status word)
-// if the copy did not land within the spin limit.
-__device__ __forceinline__ unsigned long long global_ns()
-{
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
-
-__device__ __forceinline__ bool wait_stage(uint32_t bar, uint32_t parity, unsigned int *status)
-{
-    if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long t0 = global_ns();
-    for (;;) {
-        for (int i = 0; i < 64; i++)
-            if (mbar_try_wait(bar, parity)) return true;
-        if (global_ns() - t0 > kWaitLimitNs) break;
-    }
-    if (status) atomicOr(status, 1u);
-    return false;
-}
-
 // kWarps warps per CTA, a kStages-deep copy ring per warp, kMinBlocks CTAs
 // per SM requested from the register allocator.
 // GT query heads per KV head (4 or 8): NT = GT / 4 column tiles of the MMAs,
@@ -250,7 +189,7 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
     uint64_t policy = 0;
     if (lane == 0) {
         for (int s = 0; s < kStages; s++) mbar_init(bar0 + 8 * s, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        spb::mbar_init_fence();
         policy = evict_first_policy();
     }
     __syncwarp();
@@ -276,7 +215,7 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
         const int st = k % kStages;
         const uint32_t bar = bar0 + 8 * st;
         const uint32_t dst = ring0 + st * kStageBytes;
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        spb::fence_proxy_async();
         mbar_expect_tx(bar, kStageBytes);
         bulk_g2s(dst, ic_k, kKTile, bar, policy);
         bulk_g2s(dst + kKTile, ic_v, kVTile, bar, policy);

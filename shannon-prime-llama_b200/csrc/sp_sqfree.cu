@@ -24,11 +24,13 @@
 // skeleton codes, magnitudes, residual levels and sheet bits are
 // bit-identical to the CPU path.
 #include "sp_internal.cuh"
+#include "sp_bulk.cuh"
 
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <algorithm>
 #include <vector>
 
 namespace {
@@ -421,17 +423,33 @@ k_sq_encode(SpSqDev t, SqIo io)
         quantize_skeleton(S.skel, S.row, t.bl, lane);
         if (t.n_res > 0) {
             constexpr int NSK = PD > 0 ? PD / 11 : 1;    // hier skeleton size of the compile-time plans
-            float skr[NSK];
-            if constexpr (PD > 0) if (t.hier) load_skel_regs(S.skel, skr);
             float asum = 0.0f;
-            for (int r = lane; r < t.n_res; r += 32) {
+            bool done = false;
+            if constexpr (PD > 0) {
+                if (t.hier) {
+                    // the lane's W . skeleton predictions as independent fma
+                    // chains (same per-lane order of the |d| sum)
+                    constexpr int KR = (PD + 31) / 32;
+                    float skr[NSK];
+                    load_skel_regs(S.skel, skr);
+#pragma unroll
+                    for (int k = 0; k < KR; k++) {
+                        const int r = lane + 32 * k;
+                        if (r < t.n_res) {
+                            const float p = hier_predict_reg<NSK>(S.W, hier_w_stride(NSK), skr, r);
+                            const float d = __fsub_rn(S.buf[res_idx[r]], p);
+                            S.dev[r] = d;
+                            asum = __fadd_rn(asum, fabsf(d));
+                        }
+                    }
+                    done = true;
+                }
+            }
+            for (int r = lane; r < t.n_res && !done; r += 32) {
                 const float a = S.buf[res_idx[r]];
                 float d;
                 if (t.hier) {
-                    float p;
-                    if constexpr (PD > 0) p = hier_predict_reg<NSK>(S.W, hier_w_stride(NSK), skr, r);
-                    else p = hier_predict(S.W, S.skel, t.n_skel, r);
-                    d = __fsub_rn(a, p);
+                    d = __fsub_rn(a, hier_predict(S.W, S.skel, t.n_skel, r));
                 } else {
                     const float p = csr_predict(csr_off, csr_term, S.skel, r);
                     if (t.use_spinor) {
@@ -528,15 +546,33 @@ __device__ void sq_coeffs(const SpSqDev &t, const SqSmem &S, const float *W, int
             step = L > 1 ? __fdiv_rn(__fmul_rn(2.0f, sat), (float)(L - 1)) : 0.0f;
         }
         constexpr int NSK = PD > 0 ? PD / 11 : 1;
-        float skr[NSK];
-        if constexpr (PD > 0) if (t.hier) { __syncwarp(); load_skel_regs(S.skel, skr); }
+        if constexpr (PD > 0) {
+            if (t.hier) {
+                // lane's residuals as independent W . skeleton fma chains
+                constexpr int KR = (PD + 31) / 32;
+                float skr[NSK];
+                __syncwarp();
+                load_skel_regs(S.skel, skr);
+#pragma unroll
+                for (int k = 0; k < KR; k++) {
+                    const int r = lane + 32 * k;
+                    if (r < t.n_res) {
+                        const uint32_t lv = row_bits(S.row, 8 * t.res_off + r * t.res_bits, t.res_bits);
+                        const float dev = __fmul_rn(__fsub_rn((float)lv, center), step);
+                        const float p = hier_predict_reg<NSK>(W, hier_w_stride(NSK), skr, r);
+                        S.buf[res_idx[r]] = __fadd_rn(p, dev);
+                    }
+                }
+                __syncwarp();
+                return;
+            }
+        }
         for (int r = lane; r < t.n_res; r += 32) {
             const uint32_t lv = row_bits(S.row, 8 * t.res_off + r * t.res_bits, t.res_bits);
             const float dev = __fmul_rn(__fsub_rn((float)lv, center), step);
             float p;
             if (t.hier) {
-                if constexpr (PD > 0) p = hier_predict_reg<NSK>(W, hier_w_stride(NSK), skr, r);
-                else p = hier_predict(W, S.skel, t.n_skel, r);
+                p = hier_predict(W, S.skel, t.n_skel, r);
             } else {
                 p = csr_predict(csr_off, csr_term, S.skel, r);
                 if (t.use_spinor && row_bits(S.row, 8 * t.sheet_off + r, 1)) p = -p;
@@ -585,6 +621,7 @@ struct SqAttn {
     int layer0, n_layers, n_kv_heads, n_q_heads, group, kv_len, chunk, n_splits;
     float logit_scale;
     int store_width_k, store_width_v;
+    unsigned int *status;         // bit 0: a bounded copy wait ran out
 };
 
 constexpr int kSqMaxSplits = 64;
@@ -1027,6 +1064,452 @@ k_sq_attn_reg(SpSqDev tk, SpSqDev tv, SqAttn a)
     }
 }
 
+// ------------------------------------------- fused decode (sqfree), blocked --
+// Register-resident decode over 4-position blocks staged by bulk copies.
+// Per lane: KS consecutive skeleton slots (one 64-bit window per field,
+// dequantised as ((u | 2^23 bits) - (2^23 + m_b)) * scale, which equals
+// (u - m_b) * scale exactly), up to KR residual slots assigned on the host
+// so that the Möbius terms are spread evenly (at most KT terms per lane,
+// each an fma with a +-1 or 0 coefficient into one of the lane's residual
+// sums, which adds or subtracts exactly as the CSR sum does).  Two positions
+// are processed per step: their skeleton values share one 8-byte
+// shared-memory word per slot, their 8 scores one transposed butterfly,
+// and one softmax update covers both.
+constexpr int kSq3Warps = 4;
+constexpr int kSq3Stages = 4;
+constexpr int kSq3Block = 4;           // positions per bulk copy
+constexpr int kSq3LaneRes = 2;         // residual slots per lane in the assignment table
+
+__host__ __device__ inline int sq3_tab_len(const SpSqDev &t) { return tab_len(t) + 32 * kSq3LaneRes; }
+
+size_t sq_attn3_smem(const SpSqDev &tk, const SpSqDev &tv)
+{
+    size_t s = (size_t)sq3_tab_len(tk) * 4 + 224 * 4 + (size_t)4 * tk.pd * 4;
+    s = (s + 7) & ~size_t(7);
+    s += (size_t)kSq3Warps * 2 * (tk.n_skel + 2) * 4;
+    s = (s + 15) & ~size_t(15);
+    s += (size_t)kSq3Warps * kSq3Stages * kSq3Block * (tk.bytes_per_pos + tv.bytes_per_pos);
+    s += (size_t)kSq3Warps * kSq3Stages * 8;
+    s += (size_t)kSq3Warps * 4 * (tk.pd + 4) * 4;
+    return s + 64;
+}
+
+// Sum of 8 values over the warp (all lanes get all 8 sums).
+__device__ __forceinline__ void warp_sum8(float (&v)[8], int lane)
+{
+    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+    float k[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float keep = b4 ? v[4 + i] : v[i], give = b4 ? v[i] : v[4 + i];
+        k[i] = keep + __shfl_xor_sync(0xffffffffu, give, 16);
+    }
+    float m[2];
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const float keep = b3 ? k[2 + i] : k[i], give = b3 ? k[i] : k[2 + i];
+        m[i] = keep + __shfl_xor_sync(0xffffffffu, give, 8);
+    }
+    float x = b2 ? m[1] : m[0];
+    const float gx = b2 ? m[0] : m[1];
+    x += __shfl_xor_sync(0xffffffffu, gx, 4);
+    x += __shfl_xor_sync(0xffffffffu, x, 2);
+    x += __shfl_xor_sync(0xffffffffu, x, 1);
+    // lane with bits (b4, b3, b2) holds sum index 4*b4 + 2*b3 + b2
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = __shfl_sync(0xffffffffu, x, 4 * j);
+}
+
+// Per-lane field descriptors of one cache half (K or V).
+template <int KS, int KR>
+struct Sq3Fields {
+    int wo[KS], sh[KS], bd[KS];        // byte offset of the field's word, shift, band
+    uint32_t mk[KS];                   // code mask (0 for an absent slot)
+    float mo[KS];                      // 2^23 + m_b (2^23 for an absent slot)
+    int sc_wo, sc_sh;                  // lane b < n_bands: its band scale
+    int mag_wo, mag_sh;
+    int lwo[KR], lsh[KR], swo[KR], ssh[KR];
+    uint32_t lmask;
+    int spinor;
+    float step_mul, center;
+};
+
+template <int KS, int KR>
+__device__ __forceinline__ void sq3_fields(const SpSqDev &t, int lane, const int (&rr)[KR], Sq3Fields<KS, KR> &f)
+{
+#pragma unroll
+    for (int k = 0; k < KS; k++) {
+        const int s = KS * lane + k;
+        const bool ok = s < t.n_skel;
+        const int sc = ok ? s : 0;
+        const int b = band_of_s(t.bl, sc);
+        const int bits = t.bl.bits[b];
+        const int pos = 8 * (t.bl.byte_off[b] + 2) + (sc - t.bl.off[b]) * bits;
+        f.wo[k] = (pos >> 5) * 4;
+        f.sh[k] = pos & 31;
+        f.bd[k] = b;
+        f.mk[k] = ok ? (1u << bits) - 1u : 0u;
+        f.mo[k] = ok ? 8388608.0f + (float)((1 << (bits - 1)) - 1) : 8388608.0f;
+    }
+    const int bl = lane < t.bl.n_bands ? lane : 0;
+    f.sc_wo = t.bl.byte_off[bl] / 4 * 4;
+    f.sc_sh = 8 * (t.bl.byte_off[bl] & 3);
+    f.mag_wo = t.mag_off / 4 * 4;
+    f.mag_sh = 8 * (t.mag_off & 3);
+#pragma unroll
+    for (int j = 0; j < KR; j++) {
+        const int r = rr[j] >= 0 ? rr[j] : 0;
+        const int lp = 8 * t.res_off + r * t.res_bits, sp = 8 * t.sheet_off + r;
+        f.lwo[j] = (lp >> 5) * 4;
+        f.lsh[j] = lp & 31;
+        f.swo[j] = (sp >> 5) * 4;
+        f.ssh[j] = sp & 31;
+    }
+    f.lmask = (1u << t.res_bits) - 1u;
+    f.spinor = t.use_spinor;
+    const int L = 1 << t.res_bits;
+    f.step_mul = L > 1 ? 2.0f * (float)t.res_bits / (float)(L - 1) : 0.0f;
+    f.center = 0.5f * (float)(L - 1);
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr)
+{
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ float2 lds_f2(uint32_t addr)
+{
+    float2 v;
+    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ void sts_f2(uint32_t addr, float x, float y)
+{
+    asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(x), "f"(y) : "memory");
+}
+
+// 32 bits of a staged row starting at bit sh of the word at byte offset wo
+// (row: shared-memory address).
+__device__ __forceinline__ uint32_t sq3_word2(uint32_t row, int wo, int sh)
+{
+    return __funnelshift_r(lds32(row + wo), lds32(row + wo + 4), sh);
+}
+
+// Coefficient values of positions A (row rA) and B (row rA + bpp): the
+// lane's skeleton slots (also stored to skb as (A, B) pairs) and residuals.
+template <int KS, int KR, int KT>
+__device__ __forceinline__ void sq3_values(uint32_t rA, int bpp, const Sq3Fields<KS, KR> &f,
+                                           int n_bands, int n_skel, float *skb, uint32_t skb_s, int lane,
+                                           const int (&toff)[KT], const float (&tcf)[KT], int n0,
+                                           float (&vA)[KS], float (&vB)[KS], float (&cA)[KR], float (&cB)[KR])
+{
+    const uint32_t rB = rA + bpp;
+    float scA = 0.0f, scB = 0.0f;
+    if (lane < n_bands) {
+        scA = __half2float(__ushort_as_half((unsigned short)(sq3_word2(rA, f.sc_wo, f.sc_sh) & 0xffffu)));
+        scB = __half2float(__ushort_as_half((unsigned short)(sq3_word2(rB, f.sc_wo, f.sc_sh) & 0xffffu)));
+        scA = fabsf(scA) <= 65504.0f ? scA : 0.0f;
+        scB = fabsf(scB) <= 65504.0f ? scB : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < KS; k++) {
+        const float sa = __shfl_sync(0xffffffffu, scA, f.bd[k]);
+        const float sb = __shfl_sync(0xffffffffu, scB, f.bd[k]);
+        const uint32_t xa = (sq3_word2(rA, f.wo[k], f.sh[k]) & f.mk[k]) | 0x4B000000u;
+        const uint32_t xb = (sq3_word2(rB, f.wo[k], f.sh[k]) & f.mk[k]) | 0x4B000000u;
+        vA[k] = __fmul_rn(__fsub_rn(__uint_as_float(xa), f.mo[k]), sa);
+        vB[k] = __fmul_rn(__fsub_rn(__uint_as_float(xb), f.mo[k]), sb);
+        const int s = KS * lane + k;
+        if (s < n_skel) sts_f2(skb_s + 8 * s, vA[k], vB[k]);
+    }
+    __syncwarp();
+    const float stepA = __uint_as_float(sq3_word2(rA, f.mag_wo, f.mag_sh)) * f.step_mul;
+    const float stepB = __uint_as_float(sq3_word2(rB, f.mag_wo, f.mag_sh)) * f.step_mul;
+    float pA[KR], pB[KR];
+#pragma unroll
+    for (int j = 0; j < KR; j++) { pA[j] = 0.0f; pB[j] = 0.0f; }
+    static_assert(KR == 2, "two residual sums per lane");
+#pragma unroll
+    for (int t = 0; t < KT; t++) {
+        const float2 v = lds_f2(skb_s + toff[t]);
+        // terms t < n0 belong to the lane's first residual, the rest to the second
+        const float c0 = t < n0 ? tcf[t] : 0.0f, c1 = t < n0 ? 0.0f : tcf[t];
+        pA[0] = __fmaf_rn(c0, v.x, pA[0]);
+        pB[0] = __fmaf_rn(c0, v.y, pB[0]);
+        pA[1] = __fmaf_rn(c1, v.x, pA[1]);
+        pB[1] = __fmaf_rn(c1, v.y, pB[1]);
+    }
+#pragma unroll
+    for (int j = 0; j < KR; j++) {
+        const uint32_t la = (sq3_word2(rA, f.lwo[j], f.lsh[j]) & f.lmask) | 0x4B000000u;
+        const uint32_t lb = (sq3_word2(rB, f.lwo[j], f.lsh[j]) & f.lmask) | 0x4B000000u;
+        const float da = __fmul_rn(__fsub_rn(__fsub_rn(__uint_as_float(la), 8388608.0f), f.center), stepA);
+        const float db = __fmul_rn(__fsub_rn(__fsub_rn(__uint_as_float(lb), 8388608.0f), f.center), stepB);
+        float a = pA[j], b = pB[j];
+        if (f.spinor) {
+            const uint32_t sa = sq3_word2(rA, f.swo[j], f.ssh[j]) << 31;   // sheet bit -> sign
+            const uint32_t sb = sq3_word2(rB, f.swo[j], f.ssh[j]) << 31;
+            a = __uint_as_float(__float_as_uint(a) ^ sa);
+            b = __uint_as_float(__float_as_uint(b) ^ sb);
+        }
+        cA[j] = __fadd_rn(a, da);
+        cB[j] = __fadd_rn(b, db);
+    }
+}
+
+template <int KS, int KR, int KT>
+__global__ void __launch_bounds__(kSq3Warps * 32, 3)
+k_sq_attn3(SpSqDev tk, SpSqDev tv, SqAttn a)
+{
+    constexpr int GT = 4;
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int split = blockIdx.x, h = blockIdx.y, li = blockIdx.z;
+    const int layer = a.layer0 + li;
+    const int G = a.group, pd = tk.pd;
+    const int ntab = sq3_tab_len(tk);
+    int *tab = reinterpret_cast<int *>(smem);
+    float *cas = reinterpret_cast<float *>(tab + ntab);
+    float *qp = cas + 224;
+    float *skb_all = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(qp + GT * pd) + 7) & ~uintptr_t(7));
+    float *skb = skb_all + warp * 2 * (tk.n_skel + 2);
+    const uint32_t skb_s = spb::smem_u32(skb);
+    unsigned char *ring_all = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(skb_all + kSq3Warps * 2 * (tk.n_skel + 2)) + 15) & ~uintptr_t(15));
+    const int kblk = kSq3Block * tk.bytes_per_pos, vblk = kSq3Block * tv.bytes_per_pos;
+    const int stage_bytes = kblk + vblk;
+    unsigned char *ring = ring_all + warp * kSq3Stages * stage_bytes;
+    unsigned long long *bars = reinterpret_cast<unsigned long long *>(ring_all + kSq3Warps * kSq3Stages * stage_bytes);
+    float *merge = reinterpret_cast<float *>(bars + kSq3Warps * kSq3Stages);
+
+    // ---- copy ring: blocks of 4 positions, warp w takes blocks w, w+4, ...
+    const int t_begin = split * a.chunk, t_end = min(a.kv_len, t_begin + a.chunk);
+    const int n_blk = (t_end - t_begin + kSq3Block - 1) / kSq3Block;
+    const int n_my = warp < n_blk ? (n_blk - warp + kSq3Warps - 1) / kSq3Warps : 0;
+    const long long slot = (long long)layer * a.n_kv_heads + h;
+    const uint8_t *kbase = a.k_cache + slot * a.k_slot_stride;
+    const uint8_t *vbase = a.v_cache + slot * a.v_slot_stride;
+    const uint32_t bar0 = spb::smem_u32(bars + warp * kSq3Stages);
+    const uint32_t ring0 = spb::smem_u32(ring);
+    uint64_t policy = 0;
+    if (lane == 0) {
+        for (int st = 0; st < kSq3Stages; st++) spb::mbar_init(bar0 + 8 * st, 1);
+        spb::mbar_init_fence();
+        policy = spb::evict_first_policy();
+    }
+    __syncwarp();
+    // Block k of this warp: first position, and whether all 4 positions exist
+    // (only those are bulk-copied; a ragged last block is loaded by lanes).
+    auto blk_pos = [&](int k) { return t_begin + (warp + k * kSq3Warps) * kSq3Block; };
+    auto issue = [&](int k) {
+        const int p0 = blk_pos(k);
+        if (p0 + kSq3Block > t_end) return;
+        const int st = k % kSq3Stages;
+        const uint32_t bar = bar0 + 8 * st, dst = ring0 + st * stage_bytes;
+        spb::fence_proxy_async();
+        spb::mbar_expect_tx(bar, stage_bytes);
+        spb::bulk_g2s(dst, kbase + (long long)p0 * tk.bytes_per_pos, kblk, bar, policy);
+        spb::bulk_g2s(dst + kblk, vbase + (long long)p0 * tv.bytes_per_pos, vblk, bar, policy);
+    };
+    if (lane == 0)
+        for (int k = 0; k < kSq3Stages && k < n_my; k++) issue(k);
+
+    // ---- tables, queries --------------------------------------------------
+    for (int i = threadIdx.x; i < ntab; i += blockDim.x) tab[i] = tk.tables[i];
+    for (int i = threadIdx.x; i < 224; i += blockDim.x) cas[i] = tk.cas[i];
+    __syncthreads();
+    for (int g = warp; g < GT; g += kSq3Warps) {
+        float *b = qp + g * pd;
+        const __half *qg = a.q + ((long long)li * a.n_q_heads + h * G + (g < G ? g : 0)) * tk.hd;
+        for (int i = lane; i < pd; i += 32) b[i] = (g < G && i < tk.hd) ? __half2float(qg[i]) : 0.0f;
+        __syncwarp();
+        vilenkin_warp(b, tk, cas, lane);
+        for (int i = lane; i < pd; i += 32) b[i] *= a.logit_scale * 1.4426950408889634f;
+    }
+    __syncthreads();
+    const int *skel_idx = tab + tab_skel(tk), *res_idx = tab + tab_res(tk);
+    const int *csr_off = tab + tab_csr_off(tk), *csr_term = tab + tab_csr_term(tk);
+    const int *lane_res = tab + tab_len(tk);
+
+    // ---- lane constants ---------------------------------------------------
+    int rr[KR];
+#pragma unroll
+    for (int j = 0; j < KR; j++) rr[j] = lane_res[kSq3LaneRes * lane + j];
+    // flattened Möbius terms: byte offset of the (A, B) skeleton pair and
+    // the coefficient into each of the lane's residual sums
+    int toff[KT], n0;
+    float tcf[KT];
+    {
+        int n[KR], o[KR];
+#pragma unroll
+        for (int j = 0; j < KR; j++) {
+            n[j] = rr[j] >= 0 ? csr_off[rr[j] + 1] - csr_off[rr[j]] : 0;
+            o[j] = rr[j] >= 0 ? csr_off[rr[j]] : 0;
+        }
+#pragma unroll
+        for (int t = 0; t < KT; t++) {
+            int idx = t, which = -1;
+#pragma unroll
+            for (int j = 0; j < KR; j++) {
+                if (which < 0 && idx < n[j]) which = j;
+                else if (which < 0) idx -= n[j];
+            }
+            int term = 0;
+#pragma unroll
+            for (int j = 0; j < KR; j++)
+                if (which == j) term = csr_term[o[j] + idx];
+            toff[t] = which >= 0 ? 8 * (term >> 1) : 0;
+            tcf[t] = which >= 0 ? ((term & 1) ? -1.0f : 1.0f) : 0.0f;
+        }
+        n0 = n[0];
+    }
+    // K and V rows share one layout (checked on the host)
+    Sq3Fields<KS, KR> fk;
+    sq3_fields<KS, KR>(tk, lane, rr, fk);
+    float qs[GT][KS], qr[GT][KR];
+#pragma unroll
+    for (int g = 0; g < GT; g++) {
+#pragma unroll
+        for (int k = 0; k < KS; k++) {
+            const int s = KS * lane + k;
+            qs[g][k] = s < tk.n_skel ? qp[g * pd + skel_idx[s]] : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < KR; j++) qr[g][j] = rr[j] >= 0 ? qp[g * pd + res_idx[rr[j]]] : 0.0f;
+    }
+    float as[GT][KS], ar[GT][KR], m[GT], l[GT];
+#pragma unroll
+    for (int g = 0; g < GT; g++) {
+        m[g] = -INFINITY;
+        l[g] = 0.0f;
+#pragma unroll
+        for (int k = 0; k < KS; k++) as[g][k] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < KR; j++) ar[g][j] = 0.0f;
+    }
+
+    // ---- blocks -----------------------------------------------------------
+    bool failed = false;
+    int k_fail = 0;
+    for (int k = 0; k < n_my; k++) {
+        const int st = k % kSq3Stages;
+        const int p0 = blk_pos(k);
+        const int nvalid = min(kSq3Block, t_end - p0);
+        unsigned char *sk_row = ring + st * stage_bytes;
+        unsigned char *sv_row = sk_row + kblk;
+        const uint32_t sk_s = ring0 + st * stage_bytes, sv_s = sk_s + kblk;
+        if (nvalid == kSq3Block) {
+            if (!spb::wait_stage(bar0 + 8 * st, (k / kSq3Stages) & 1, a.status)) {
+                failed = true;
+                k_fail = k;
+                break;
+            }
+        } else {
+            // ragged last block: lanes copy the valid rows, zero the rest
+            const int kw = tk.bytes_per_pos / 4, vw = tv.bytes_per_pos / 4;
+            for (int i = lane; i < kSq3Block * kw; i += 32)
+                reinterpret_cast<uint32_t *>(sk_row)[i] =
+                    i < nvalid * kw ? reinterpret_cast<const uint32_t *>(kbase + (long long)p0 * tk.bytes_per_pos)[i] : 0u;
+            for (int i = lane; i < kSq3Block * vw; i += 32)
+                reinterpret_cast<uint32_t *>(sv_row)[i] =
+                    i < nvalid * vw ? reinterpret_cast<const uint32_t *>(vbase + (long long)p0 * tv.bytes_per_pos)[i] : 0u;
+            __syncwarp();
+        }
+#pragma unroll 1
+        for (int pp = 0; pp < kSq3Block; pp += 2) {
+            if (pp >= nvalid) break;
+            const bool okB = pp + 1 < nvalid;
+            float vA[KS], vB[KS], cA[KR], cB[KR];
+            sq3_values<KS, KR, KT>(sk_s + pp * tk.bytes_per_pos, tk.bytes_per_pos, fk, tk.bl.n_bands, tk.n_skel,
+                                   skb, skb_s, lane, toff, tcf, n0, vA, vB, cA, cB);
+            float sc[8];
+#pragma unroll
+            for (int g = 0; g < GT; g++) {
+                float dA = 0.0f, dB = 0.0f;
+#pragma unroll
+                for (int kk = 0; kk < KS; kk++) {
+                    dA = __fmaf_rn(qs[g][kk], vA[kk], dA);
+                    dB = __fmaf_rn(qs[g][kk], vB[kk], dB);
+                }
+#pragma unroll
+                for (int j = 0; j < KR; j++) {
+                    dA = __fmaf_rn(qr[g][j], cA[j], dA);
+                    dB = __fmaf_rn(qr[g][j], cB[j], dB);
+                }
+                sc[g] = dA;
+                sc[4 + g] = dB;
+            }
+            warp_sum8(sc, lane);
+            __syncwarp();
+            sq3_values<KS, KR, KT>(sv_s + pp * tv.bytes_per_pos, tv.bytes_per_pos, fk, tv.bl.n_bands, tv.n_skel,
+                                   skb, skb_s, lane, toff, tcf, n0, vA, vB, cA, cB);
+#pragma unroll
+            for (int g = 0; g < GT; g++) {
+                const float sA = sc[g], sB = okB ? sc[4 + g] : -INFINITY;
+                const float mx = fmaxf(sA, sB);
+                if (mx > m[g]) {                 // uniform across the warp
+                    const float alpha = ex2_fast(m[g] - mx);
+                    m[g] = mx;
+                    l[g] *= alpha;
+#pragma unroll
+                    for (int kk = 0; kk < KS; kk++) as[g][kk] *= alpha;
+#pragma unroll
+                    for (int j = 0; j < KR; j++) ar[g][j] *= alpha;
+                }
+                const float pa = ex2_fast(sA - m[g]), pb = ex2_fast(sB - m[g]);
+                l[g] += pa + pb;
+#pragma unroll
+                for (int kk = 0; kk < KS; kk++) as[g][kk] = __fmaf_rn(pb, vB[kk], __fmaf_rn(pa, vA[kk], as[g][kk]));
+#pragma unroll
+                for (int j = 0; j < KR; j++) ar[g][j] = __fmaf_rn(pb, cB[j], __fmaf_rn(pa, cA[j], ar[g][j]));
+            }
+            __syncwarp();
+        }
+        __syncwarp();
+        if (lane == 0 && k + kSq3Stages < n_my) issue(k + kSq3Stages);
+    }
+    if (failed) {
+        // bounded wait for this warp's bulk copies still in flight (blocks
+        // k_fail .. k_fail + stages - 1 were issued) before the CTA exits
+        for (int k = k_fail; k < n_my && k < k_fail + kSq3Stages; k++)
+            if (blk_pos(k) + kSq3Block <= t_end)
+                spb::wait_stage(bar0 + 8 * (k % kSq3Stages), (k / kSq3Stages) & 1, nullptr);
+    }
+    // ---- merge the warps, write the CTA's partial ---------------------------
+    float *mw = merge + (size_t)warp * GT * (pd + 4);
+#pragma unroll
+    for (int g = 0; g < GT; g++) {
+#pragma unroll
+        for (int kk = 0; kk < KS; kk++) {
+            const int s = KS * lane + kk;
+            if (s < tk.n_skel) mw[g * (pd + 4) + 4 + skel_idx[s]] = as[g][kk];
+        }
+#pragma unroll
+        for (int j = 0; j < KR; j++)
+            if (rr[j] >= 0) mw[g * (pd + 4) + 4 + res_idx[rr[j]]] = ar[g][j];
+        if (lane == 0) { mw[g * (pd + 4)] = m[g]; mw[g * (pd + 4) + 1] = l[g]; }
+    }
+    __syncthreads();
+    for (int g = 0; g < G; g++) {
+        float M = -INFINITY;
+        for (int w = 0; w < kSq3Warps; w++) M = fmaxf(M, merge[((size_t)w * GT + g) * (pd + 4)]);
+        float *part = sq_partial(a, pd, li, h * G + g, split);
+        for (int i = threadIdx.x; i < pd + 1; i += blockDim.x) {
+            float v = 0.0f;
+            for (int w = 0; w < kSq3Warps; w++) {
+                const float *aw = merge + ((size_t)w * GT + g) * (pd + 4);
+                const float wt = aw[0] == -INFINITY ? 0.0f : exp2f(aw[0] - M);
+                v += wt * (i < pd ? aw[4 + i] : aw[1]);
+            }
+            if (i < pd) part[4 + i] = v;
+            else { part[0] = M; part[1] = v; }
+        }
+    }
+}
+
 size_t sq_attn_reg_smem(const SpSqDev &t, const SpSqDev &tv, int GT)
 {
     return (size_t)tab_len(t) * 4 + 224 * 4 + (size_t)GT * t.pd * 4 + (size_t)kSqAttnWarps * (t.n_skel + 4) * 4 +
@@ -1348,6 +1831,29 @@ int sp_cuda_sqfree_cache_init_ex(sp_cuda_sqfree_cache_t *cc, const sp_config_t *
     tables.insert(tables.end(), res.begin(), res.end());
     tables.insert(tables.end(), off.begin(), off.end());
     tables.insert(tables.end(), term.begin(), term.end());
+    // Residual -> lane assignment of the blocked decode: residuals by
+    // decreasing term count, each to the least-loaded lane holding fewer than
+    // kSq3LaneRes of them (ties: lower lane).  Table: [32][kSq3LaneRes], -1 free.
+    {
+        std::vector<int> lane_res(32 * kSq3LaneRes, -1), load(32, 0), cnt(32, 0), order(res.size());
+        for (size_t r = 0; r < res.size(); r++) order[r] = (int)r;
+        std::stable_sort(order.begin(), order.end(), [&](int x, int y) {
+            return off[x + 1] - off[x] > off[y + 1] - off[y];
+        });
+        bool fits = true;
+        for (int r : order) {
+            int best = -1;
+            for (int ln = 0; ln < 32; ln++)
+                if (cnt[ln] < kSq3LaneRes && (best < 0 || load[ln] < load[best])) best = ln;
+            if (best < 0) { fits = false; break; }
+            lane_res[kSq3LaneRes * best + cnt[best]++] = r;
+            load[best] += off[r + 1] - off[r];
+        }
+        cc->lane_max_terms = 0;
+        if (fits)
+            for (int ln = 0; ln < 32; ln++) cc->lane_max_terms = std::max(cc->lane_max_terms, std::max(load[ln], 1));
+        tables.insert(tables.end(), lane_res.begin(), lane_res.end());
+    }
     int factors[kSqMaxStages], nf = 0;
     {
         int r = pd;
@@ -1385,8 +1891,10 @@ int sp_cuda_sqfree_cache_init_ex(sp_cuda_sqfree_cache_t *cc, const sp_config_t *
     cudaMemset(cc->d_k_cache, 0, k_total * cc->bytes_per_pos_k);
     cudaMemset(cc->d_v_cache, 0, k_total * cc->bytes_per_pos_v);
     cc->attn_ws_bytes = (size_t)cfg->n_layers * 8 * cfg->n_heads_kv * kSqMaxSplits * (pd + 4) * sizeof(float);
+    // + 16 bytes: the decode's status word follows the partials
     if ((rc = sq_upload_constants()) ||
-        (rc = sp_check_cuda(cudaMalloc(&cc->d_attn_ws, cc->attn_ws_bytes), "cudaMalloc sqfree workspace")) ||
+        (rc = sp_check_cuda(cudaMalloc(&cc->d_attn_ws, cc->attn_ws_bytes + 16), "cudaMalloc sqfree workspace")) ||
+        (rc = sp_check_cuda(cudaMemset(cc->d_attn_ws, 0, cc->attn_ws_bytes + 16), "sqfree workspace")) ||
         (rc = sp_check_cuda(cudaDeviceSynchronize(), "sqfree_cache_init"))) {
         sp_cuda_sqfree_cache_free(cc);
         return rc;
@@ -1566,6 +2074,35 @@ int sp_cuda_sqfree_attn_decode(const sp_cuda_sqfree_cache_t *cc, int layer0, int
     a.chunk = (kv_len + splits - 1) / splits;
     a.n_splits = kv_len == 0 ? 0 : (kv_len + a.chunk - 1) / a.chunk;
     cudaStream_t s = (cudaStream_t)stream;
+    a.status = reinterpret_cast<unsigned int *>(reinterpret_cast<char *>(cc->d_attn_ws) + cc->attn_ws_bytes);
+    // Blocked kernel: up to 4 queries per KV head, 4 skeleton slots and 2
+    // residuals per lane, 8 Möbius terms per lane, 4-byte rows, and 16-byte
+    // aligned 4-position blocks for the bulk copies.
+    bool same_layout = tk.bytes_per_pos == tv.bytes_per_pos && tk.bl.n_bands == tv.bl.n_bands &&
+                       tk.res_off == tv.res_off && tk.sheet_off == tv.sheet_off && tk.mag_off == tv.mag_off &&
+                       tk.res_bits == tv.res_bits && tk.use_spinor == tv.use_spinor;
+    for (int b = 0; same_layout && b < tk.bl.n_bands; b++)
+        same_layout = tk.bl.bits[b] == tv.bl.bits[b] && tk.bl.off[b] == tv.bl.off[b] &&
+                      tk.bl.size[b] == tv.bl.size[b] && tk.bl.byte_off[b] == tv.bl.byte_off[b];
+    const bool blocked = same_layout && a.group <= 4 && tk.n_skel <= 128 && cc->lane_max_terms > 0 &&
+                         cc->lane_max_terms <= 8 &&
+                         tk.bytes_per_pos % 4 == 0 && tv.bytes_per_pos % 4 == 0 &&
+                         a.k_slot_stride % 16 == 0 && a.v_slot_stride % 16 == 0 &&
+                         ((uintptr_t)a.k_cache & 15) == 0 && ((uintptr_t)a.v_cache & 15) == 0 &&
+                         getenv("SHANNON_PRIME_SQFREE_DECODE_REG") == nullptr;
+    if (blocked && a.n_splits > 0) {
+        a.chunk = (a.chunk + 15) / 16 * 16;
+        a.n_splits = (kv_len + a.chunk - 1) / a.chunk;
+        const size_t sm = sq_attn3_smem(tk, tv);
+        auto k3 = k_sq_attn3<4, 2, 8>;
+        cudaFuncSetAttribute(k3, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        k3<<<dim3(a.n_splits, H, n_layers), kSq3Warps * 32, sm, s>>>(tk, tv, a);
+        int rc = sp_check_cuda(cudaGetLastError(), "sqfree attention launch");
+        if (rc) return rc;
+        const size_t smc = (224 + tk.pd + 8) * sizeof(float);
+        k_sq_attn_combine<<<dim3(n_q_heads, n_layers), 32, smc, s>>>(tk, a);
+        return sp_check_cuda(cudaGetLastError(), "sqfree attention combine launch");
+    }
     int GT = 0;
     SqAttnKernel kreg = sq_attn_reg_kernel(a.group, (tk.n_skel + 31) / 32, (tk.n_res + 31) / 32, &GT);
     // the prefetch ring copies rows in 4-byte pieces; Möbius terms live in registers

@@ -70,6 +70,7 @@ class SpSqfreeCache(C.Structure):
         ("d_sheet_scratch", C.c_void_p), ("stream", C.c_void_p),
         ("device", C.c_int), ("d_tables", C.c_void_p), ("d_attn_ws", C.c_void_p),
         ("attn_ws_bytes", C.c_size_t), ("csr_max_terms", C.c_int),
+        ("lane_max_terms", C.c_int),
     ]
 
 
