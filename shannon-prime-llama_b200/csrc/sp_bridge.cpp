@@ -300,6 +300,17 @@ int sp_llama_write_kv_tokens(sp_llama_ctx_t *ctx, int layer, int start_pos, int 
     return SP_OK;
 }
 
+// True if p is page-locked host memory known to the CUDA runtime.
+static bool host_pinned(const void *p)
+{
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeHost;
+}
+
 int sp_llama_attn_decode(sp_llama_ctx_t *ctx, int layer0, int n_layers, const uint16_t *q_f16,
                          int n_q_heads, int kv_len, float logit_scale, uint16_t *out_f16,
                          int max_bands)
@@ -307,14 +318,19 @@ int sp_llama_attn_decode(sp_llama_ctx_t *ctx, int layer0, int n_layers, const ui
     if (!ctx || !q_f16 || !out_f16 || n_layers <= 0) return SP_ERR_ARG;
     const size_t elems = (size_t)n_layers * n_q_heads * ctx->config.head_dim;
     if (elems > ctx->qo_elems) return SP_ERR_ARG;
-    memcpy(ctx->h_q, q_f16, 2 * elems);
-    cudaMemcpyAsync(ctx->d_q, ctx->h_q, 2 * elems, cudaMemcpyHostToDevice, ctx->stream);
+    // Page-locked caller buffers are copied from / to directly; pageable ones
+    // go through the context's pinned staging buffers.
+    const bool q_pinned = host_pinned(q_f16), out_pinned = host_pinned(out_f16);
+    if (!q_pinned) memcpy(ctx->h_q, q_f16, 2 * elems);
+    cudaMemcpyAsync(ctx->d_q, q_pinned ? (const void *)q_f16 : ctx->h_q, 2 * elems, cudaMemcpyHostToDevice,
+                    ctx->stream);
     int rc = sp_cuda_attn_decode(&ctx->cache, layer0, n_layers, ctx->d_q, n_q_heads, kv_len,
                                  logit_scale, ctx->d_out, max_bands, ctx->stream);
     if (rc) return rc;
-    cudaMemcpyAsync(ctx->h_out, ctx->d_out, 2 * elems, cudaMemcpyDeviceToHost, ctx->stream);
+    cudaMemcpyAsync(out_pinned ? (void *)out_f16 : ctx->h_out, ctx->d_out, 2 * elems, cudaMemcpyDeviceToHost,
+                    ctx->stream);
     if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) return SP_ERR_CUDA;
-    memcpy(out_f16, ctx->h_out, 2 * elems);
+    if (!out_pinned) memcpy(out_f16, ctx->h_out, 2 * elems);
     return SP_OK;
 }
 

@@ -99,3 +99,10 @@ def test_bridge_fused_decode_host_buffers(bridge):
     ref = O.attn_decode(kp, vp, n, KB, VB, True, q[0], T, 1.0)
     err = np.linalg.norm(out[0].astype(np.float64) - ref) / np.linalg.norm(ref)
     assert err <= 1e-3
+    # page-locked caller buffers take the direct-copy path: same result
+    import torch
+    qp = torch.from_numpy(q).pin_memory()
+    op = torch.zeros(out.shape, dtype=torch.float16).pin_memory()
+    rc = L.sp_llama_attn_decode(ctx, 0, 1, qp.data_ptr(), H * G, T, 1.0, op.data_ptr(), -1)
+    assert rc == 0
+    np.testing.assert_array_equal(op.numpy(), out)
