@@ -26,6 +26,9 @@
 
 #include "shannon_prime.h"
 
+#include <stdbool.h>
+#include <stdint.h>
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -329,6 +332,48 @@ int  sp_cuda_hier_read_kv_tokens(const sp_cuda_hier_cache_t *hc, int layer0, int
 
 /* ----------------------------------------- kernel launchers (for tests) -- */
 
+/* ---------------------------------------------------------------------------
+ * Cold storage: per-layer pinned host mirror of a cache slab (the warm tier
+ * of the reference's GPU <-> CPU <-> disk offload, shannon_prime_cuda.h:233-286,
+ * called by src/engine/kv_cache.cpp:1401-1520).
+ *
+ * A layer slab is the n_heads_kv * max_seq_len * packed_stride bytes of one
+ * layer in d_k_cache or d_v_cache.  Writebacks mirror byte ranges of the slab:
+ * positions [start_pos, start_pos + n_pos) cover slab bytes
+ * [start_pos, start_pos + n_pos) * n_heads * packed_stride, appended at
+ * write_head of the pinned buffer; a range that does not fit wraps the buffer
+ * to offset 0 (ring mode).  A restore copies the first n_pos * n_heads *
+ * packed_stride bytes of the buffer back to the start of the slab, and is
+ * refused once the buffer has wrapped.  Copies are async on `stream`.
+ * ------------------------------------------------------------------------- */
+typedef struct {
+    uint8_t *h_pinned;           /* page-locked staging buffer (capacity bytes) */
+    int64_t  capacity;
+    int      packed_stride;      /* bytes per position per head */
+    int      n_heads;
+    int64_t  write_head;         /* byte offset of the next writeback */
+    int64_t  oldest_pos;         /* oldest position held (-1: none yet) */
+    int64_t  newest_pos;         /* newest position written */
+    bool     ring_mode;          /* the buffer has wrapped */
+    bool     initialized;
+} sp_cuda_cold_layer_t;
+
+/* 0 on success, -1 on bad arguments or a failed page-locked allocation. */
+int  sp_cuda_cold_layer_init(sp_cuda_cold_layer_t *cl, int64_t cap_bytes, int packed_stride, int n_heads);
+void sp_cuda_cold_layer_free(sp_cuda_cold_layer_t *cl);
+/* Async device -> host copy of positions [start_pos, start_pos + n_pos) of a
+ * layer slab (d_packed = the slab's device address).  0 on success, -1 on bad
+ * arguments or a range larger than the buffer. */
+int  sp_cuda_cold_writeback(sp_cuda_cold_layer_t *cl, const void *d_packed, int start_pos, int n_pos,
+                            void *stream);
+/* Async host -> device copy of positions [0, n_pos) back to the slab start.
+ * -1 in ring mode, on bad arguments, or for more bytes than the buffer holds. */
+int  sp_cuda_cold_restore(const sp_cuda_cold_layer_t *cl, void *d_packed, int n_pos, void *stream);
+/* Async copies of arbitrary buffers on `stream`. */
+void sp_cuda_d2h_async(void *dst_host, const void *src_device, int64_t n_bytes, void *stream);
+void sp_cuda_h2d_async(void *dst_device, const void *src_host, int64_t n_bytes, void *stream);
+
+
 /* Reference shannon_prime_cuda.h:116-134.  In-place VHT2 of n_vecs
  * vectors (power-of-two n, 32 <= n <= SP_MAX_HEAD_DIM). */
 void sp_cuda_vht2_forward(float *d_data, int n, int n_vecs, void *stream);
@@ -353,7 +398,8 @@ const char *sp_cuda_last_error_string(void);
 
 /* New: sizeof(sp_config_t) (which=0), sizeof(sp_band_config_t) (1),
  * sizeof(sp_cuda_cache_t) (2), sizeof(sp_cuda_sqfree_cache_t) (3),
- * sizeof(sp_cuda_hier_cache_t) (4), so bindings can check their mirrors. */
+ * sizeof(sp_cuda_hier_cache_t) (4), sizeof(sp_cuda_cold_layer_t) (5), so
+ * bindings can check their mirrors. */
 int sp_cuda_abi_struct_size(int which);
 
 /* New, for tests and benchmarks: force the fused-decode kernel family

@@ -265,6 +265,7 @@ extern "C" int sp_cuda_abi_struct_size(int which)
     case 2: return (int)sizeof(sp_cuda_cache_t);
     case 3: return (int)sizeof(sp_cuda_sqfree_cache_t);
     case 4: return (int)sizeof(sp_cuda_hier_cache_t);
+    case 5: return (int)sizeof(sp_cuda_cold_layer_t);
     }
     return -1;
 }

@@ -91,6 +91,15 @@ class SpHierCache(C.Structure):
     ]
 
 
+class SpColdLayer(C.Structure):
+    """sp_cuda_cold_layer_t: pinned host mirror of one layer slab."""
+    _fields_ = [
+        ("h_pinned", C.c_void_p), ("capacity", C.c_int64), ("packed_stride", C.c_int),
+        ("n_heads", C.c_int), ("write_head", C.c_int64), ("oldest_pos", C.c_int64),
+        ("newest_pos", C.c_int64), ("ring_mode", C.c_bool), ("initialized", C.c_bool),
+    ]
+
+
 class SpLlamaParams(C.Structure):
     _fields_ = [
         ("head_dim", C.c_int), ("n_layers", C.c_int), ("n_heads_kv", C.c_int),
@@ -166,6 +175,12 @@ SIGNATURES = {
     "sp_cuda_last_error": (_I, []),
     "sp_cuda_last_error_string": (C.c_char_p, []),
     "sp_cuda_abi_struct_size": (_I, [_I]),
+    "sp_cuda_cold_layer_init": (_I, [C.POINTER(SpColdLayer), C.c_int64, _I, _I]),
+    "sp_cuda_cold_layer_free": (_V, [C.POINTER(SpColdLayer)]),
+    "sp_cuda_cold_writeback": (_I, [C.POINTER(SpColdLayer), _P, _I, _I, _P]),
+    "sp_cuda_cold_restore": (_I, [C.POINTER(SpColdLayer), _P, _I, _P]),
+    "sp_cuda_d2h_async": (_V, [_P, _P, C.c_int64, _P]),
+    "sp_cuda_h2d_async": (_V, [_P, _P, C.c_int64, _P]),
     "sp_cuda_attn_force_impl": (_V, [_I]),
     "sp_cuda_attn_profile": (_V, [_I]),
     "sp_cuda_attn_last_kernel_ms": (_F, []),
@@ -213,7 +228,8 @@ def lib() -> C.CDLL:
             f = getattr(L, name)
             f.restype = res
             f.argtypes = args
-        for which, st in enumerate((SpConfig, SpBandConfig, SpCudaCache, SpSqfreeCache, SpHierCache)):
+        for which, st in enumerate((SpConfig, SpBandConfig, SpCudaCache, SpSqfreeCache, SpHierCache,
+                                     SpColdLayer)):
             if L.sp_cuda_abi_struct_size(which) != C.sizeof(st):
                 raise RuntimeError(f"struct mirror {st.__name__} does not match the C ABI")
         _lib = L
