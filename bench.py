@@ -306,17 +306,18 @@ def measure_hier(torch, dev, stream, peak: float, scale: int = 1):
 
 
 def measure_config3(torch, dist, dev, stream, ws: int, rank: int, steps: int, warmup: int, peak: float,
-                    max_over_ranks, barrier):
+                    max_over_ranks, barrier, scale: int = 1):
     """Config 3: MoE-scale long context, 48 layers, 32 Q / 4 KV heads (8 query
     heads per KV head), head_dim 128, ctx 131072, batch 4 (four independent
     caches), ship K 5/5/4/3 + V 3-bit, seeded as config 0 (seed 3).  The
     (layer, KV head) slots are partitioned over the ranks (spb200.shard:
     heads first, then layer halves at 8 GPUs); the four sequences of a rank
     are its cache layers seq * L_local + l, attended in one call, and one
-    all-gather of the per-head fp16 outputs completes the step."""
+    all-gather of the per-head fp16 outputs completes the step.  scale > 1
+    (profiling only) keeps 48 / scale layers (at least 2)."""
     import spb200
     from spb200 import shard, synth
-    L3, Q3, KV3, CTX3, B3 = 48, 32, 4, 131072, 4
+    L3, Q3, KV3, CTX3, B3 = max(2, 48 // max(1, scale)), 32, 4, 131072, 4
     sh = shard.partition(L3, KV3, ws)[rank]
     Hl, Ll, G = len(sh.heads), sh.n_layers, Q3 // KV3
     cache = spb200.Cache(HD, B3 * Ll, Hl, CTX3, KB, VB, True, stream)
@@ -357,8 +358,8 @@ def measure_config3(torch, dist, dev, stream, ws: int, rank: int, steps: int, wa
     ms = max_over_ranks(e0.elapsed_time(e1) / steps)
     bytes_all = B3 * L3 * KV3 * CTX3 * (K_ROW + V_ROW)
     res = {
-        "workload": "config 3: 48 layers x 32 Q / 4 KV heads x hd 128, ctx 131072, batch 4, ship 5/5/4/3 + V3, "
-                    "(layer, KV head) slots sharded over %d GPU(s)" % ws,
+        "workload": "config 3: %d layers x 32 Q / 4 KV heads x hd 128, ctx 131072, batch 4, ship 5/5/4/3 + V3, "
+                    "(layer, KV head) slots sharded over %d GPU(s)" % (L3, ws),
         "value": ms * 1e3, "unit": "us/step (batch 4)", "tokens_per_s": B3 / (ms * 1e-3),
         "cache_bytes_total": bytes_all,
         "achieved_gbs_total": bytes_all / (ms * 1e-3) / 1e9,
@@ -614,7 +615,7 @@ def run_ours(args):
         del kept
         torch.cuda.empty_cache()
         line["config3"] = measure_config3(torch, dist, dev, stream, ws, rank, max(3, args.steps // 2),
-                                          args.warmup, peak, max_over_ranks, barrier)
+                                          args.warmup, peak, max_over_ranks, barrier, args.extras_scale)
     if ws == 1 and not args.no_extra:
         torch.cuda.empty_cache()
         line["sqfree"] = measure_sqfree(torch, dev, stream, max(3, args.steps // 2), args.warmup, peak,
