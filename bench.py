@@ -305,6 +305,18 @@ def measure_hier(torch, dev, stream, peak: float, scale: int = 1):
     return res
 
 
+def peer_gather(torch, n_rows: int, n_q_total: int, dev):
+    """(PeerGather, description) for the fused decode + all-gather, or
+    (None, why) when symmetric memory cannot be set up (NCCL is used then)."""
+    try:
+        from spb200.gather import PeerGather
+        return (PeerGather(n_rows, n_q_total, HD, dev),
+                "fused: the combine kernel stores each output row into every rank's symmetric-memory "
+                "buffer over NVLink, then a bounded flag wait")
+    except Exception as e:  # noqa: BLE001 - reported in the JSON line
+        return None, ("nccl all_gather (peer memory unavailable: %s: %s)" % (type(e).__name__, e))[:240]
+
+
 def measure_config3(torch, dist, dev, stream, ws: int, rank: int, steps: int, warmup: int, peak: float,
                     max_over_ranks, barrier, scale: int = 1):
     """Config 3: MoE-scale long context, 48 layers, 32 Q / 4 KV heads (8 query
@@ -315,6 +327,8 @@ def measure_config3(torch, dist, dev, stream, ws: int, rank: int, steps: int, wa
     are its cache layers seq * L_local + l, attended in one call, and one
     all-gather of the per-head fp16 outputs completes the step.  scale > 1
     (profiling only) keeps 48 / scale layers (at least 2)."""
+    import ctypes as C
+
     import spb200
     from spb200 import shard, synth
     L3, Q3, KV3, CTX3, B3 = max(2, 48 // max(1, scale)), 32, 4, 131072, 4
@@ -339,8 +353,19 @@ def measure_config3(torch, dist, dev, stream, ws: int, rank: int, steps: int, wa
     Lm, Qm = shard.max_shard_shape(shards, G)
     blk = torch.zeros(B3 * Lm, Qm, HD, dtype=torch.float16, device=dev)
     gathered = [torch.empty_like(blk) for _ in range(ws)] if ws > 1 else None
+    gather, collective = None, "none (single GPU)"
+    if ws > 1:
+        # destination rows: sequence b, global layer; global query heads
+        gather, collective = peer_gather(torch, B3 * L3, Q3, dev)
+        dst_layer = torch.tensor([b * L3 + sh.layer0 + l for b in range(B3) for l in range(Ll)],
+                                 dtype=torch.int32, device=dev)
+        dst_qhead = qidx.to(torch.int32)
 
     def step():
+        if gather is not None:
+            gather.decode(C.byref(cache.cc), 0, B3 * Ll, q, Hl * G, CTX3, dst_layer, dst_qhead,
+                          1.0 / HD ** 0.5, -1, stream)
+            return
         cache.attn_decode(0, B3 * Ll, q, CTX3, out, logit_scale=1.0 / HD ** 0.5, stream=stream)
         if ws > 1:
             blk.view(B3, Lm, Qm, HD)[:, :Ll, :Hl * G] = out.view(B3, Ll, Hl * G, HD)
@@ -365,6 +390,7 @@ def measure_config3(torch, dist, dev, stream, ws: int, rank: int, steps: int, wa
         "achieved_gbs_total": bytes_all / (ms * 1e-3) / 1e9,
         "frac_of_n_gpu_peak": bytes_all / (ms * 1e-3) / 1e9 / (peak * ws),
         "scaling": "strong",
+        "collective": collective,
     }
     cache.free()
     return res
@@ -469,8 +495,19 @@ def run_ours(args):
     q = q_all[:, qidx].contiguous()
     out = torch.empty(N_LAYERS, nq_local, HD, dtype=torch.float16, device=dev)
     gathered = [torch.empty_like(out) for _ in range(ws)] if ws > 1 else None
+    # Multi-GPU: the combine kernel stores every output row straight into each
+    # rank's symmetric-memory gather buffer (sp_cuda_attn_decode_allgather);
+    # NCCL all_gather only if peer memory cannot be set up.
+    gather, collective = None, "none (single GPU)"
+    if ws > 1:
+        gather, collective = peer_gather(torch, N_LAYERS, N_Q, dev)
+        dst_layer = torch.arange(N_LAYERS, dtype=torch.int32, device=dev)
+        dst_qhead = qidx.to(torch.int32)
 
     def step():
+        if gather is not None:
+            gather.decode(cc, 0, N_LAYERS, q, nq_local, CTX, dst_layer, dst_qhead, 1.0, -1, stream)
+            return
         rc = L.sp_cuda_attn_decode(cc, 0, N_LAYERS, q.data_ptr(), nq_local, CTX, 1.0,
                                    out.data_ptr(), -1, stream.cuda_stream)
         if rc:
@@ -525,7 +562,18 @@ def run_ours(args):
     hout = torch.empty(out.shape, dtype=torch.float16).pin_memory()
     hgat = [torch.empty(out.shape, dtype=torch.float16) for _ in range(ws)]
 
+    dq = torch.empty_like(q)
+    hfull = torch.empty(N_LAYERS, N_Q, HD, dtype=torch.float16).pin_memory() if gather is not None else None
+
     def e2e_step():
+        if gather is not None:
+            # host q in (pinned) -> fused decode + gather -> whole output back
+            with torch.cuda.stream(stream):
+                dq.copy_(hq, non_blocking=True)
+                gather.decode(cc, 0, N_LAYERS, dq, nq_local, CTX, dst_layer, dst_qhead, 1.0, -1, stream)
+                hfull.copy_(gather.out, non_blocking=True)
+            stream.synchronize()
+            return
         rc = L.sp_llama_attn_decode(ctx, 0, N_LAYERS, hq.data_ptr(), nq_local, CTX, 1.0,
                                     hout.data_ptr(), -1)
         if rc:
@@ -543,8 +591,11 @@ def run_ours(args):
         e2e_step()
     barrier()
     e2e_ms = max_over_ranks((time.perf_counter() - t0) / args.steps * 1e3)
-    h2d = hq.numel() * 2 + (out.numel() * 2 if ws > 1 else 0)
-    d2h = hout.numel() * 2 * (ws if ws > 1 else 1)
+    if gather is not None:
+        h2d, d2h = hq.numel() * 2, hfull.numel() * 2
+    else:
+        h2d = hq.numel() * 2 + (out.numel() * 2 if ws > 1 else 0)
+        d2h = hout.numel() * 2 * (ws if ws > 1 else 1)
 
     # Ship-path compression throughput: re-compress 4 full layers (K and V,
     # fp32 in, 1.07 GB of inputs > L2) through the token-major entry point.
@@ -579,6 +630,8 @@ def run_ours(args):
         cpu["compress_cores"] = n_threads
 
     launches_per_step = 2        # fused decode kernel + split combine kernel
+    if gather is not None:
+        launches_per_step = 3    # + the bounded wait for the peers' flags
     line = {
         "metric": METRIC, "value": ms * 1e3, "unit": UNIT, "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -589,6 +642,7 @@ def run_ours(args):
                                "ship K 5/5/4/3 + V 3-bit" % N_LAYERS,
                    "l2": "inputs larger than L2 (compressed cache %.2f GB per GPU)" % (cache_bytes / 1e9),
                    "parallelism": f"kv-head shards x{ws}" if ws > 1 else "single GPU",
+                   "collective": collective,
                    "kv_heads_per_gpu": H, "splits": splits},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak,
@@ -599,7 +653,8 @@ def run_ours(args):
                      "algorithmic_bytes": alg_bytes},
         "e2e": {"value": e2e_ms * 1e3, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
-                "path": "sp_llama_attn_decode (host q in, host out back)"},
+                "path": ("sp_cuda_attn_decode_allgather (pinned host q in, gathered output of all ranks back)"
+                         if gather is not None else "sp_llama_attn_decode (host q in, host out back)")},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
         "compress": {"metric": "ship-path compress throughput (K+V pairs)", "value": comp_mpairs,

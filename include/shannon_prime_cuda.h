@@ -332,6 +332,31 @@ int  sp_cuda_hier_read_kv_tokens(const sp_cuda_hier_cache_t *hc, int layer0, int
 
 /* ----------------------------------------- kernel launchers (for tests) -- */
 
+/* New: fused decode + all-gather over peer memory, for a cache sharded over
+ * the GPUs of one node (one process per GPU).  Runs the same decode as
+ * sp_cuda_attn_decode on this rank's (layer, KV head) slots; the combine
+ * kernel then stores every fp16 output row directly into each rank's gather
+ * buffer (NVLink peer stores), at row
+ *     d_dst_layer[l] * n_q_heads_total + d_dst_qhead[h]   (rows of head_dim fp16)
+ * for local layer l and local query head h, and its last block writes `epoch`
+ * into uint32 slot `rank` of the flag array at byte flags_offset of every
+ * buffer.  A final kernel waits (bounded, 2 s) until all `world` slots of this
+ * rank's own flag array reach `epoch`; stream work after the call sees the
+ * whole gathered output.
+ *   d_local_buf    this rank's gather buffer
+ *   d_peer_bufs    device array [world] of every rank's buffer as mapped in
+ *                  this process (its own at index rank), e.g. from CUDA IPC or
+ *                  symmetric memory
+ *   d_dst_layer    device int [n_layers];  d_dst_qhead: device int [n_q_heads]
+ *   epoch          increases by one per call (flags are never reset)
+ * A wait that runs out sets bit 1 of the cache's d_status word.  Calls on one
+ * cache must not overlap on the GPU. */
+int sp_cuda_attn_decode_allgather(const sp_cuda_cache_t *cc, int layer0, int n_layers, const void *d_q,
+                                  int n_q_heads, int kv_len, float logit_scale, int max_bands,
+                                  void *d_local_buf, void *const *d_peer_bufs, const int *d_dst_layer,
+                                  const int *d_dst_qhead, int n_q_heads_total, long long flags_offset,
+                                  int rank, int world, unsigned int epoch, void *stream);
+
 /* ---------------------------------------------------------------------------
  * Cold storage: per-layer pinned host mirror of a cache slab (the warm tier
  * of the reference's GPU <-> CPU <-> disk offload, shannon_prime_cuda.h:233-286,

@@ -191,27 +191,30 @@ __global__ void k_attn_combine(SpAttnArgs a)
     constexpr int n = 32 * E;
     const int lane = threadIdx.x & 31;
     const int qh = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (qh >= a.n_q_heads) return;
     const int li = blockIdx.y;
-    float M = -INFINITY;
-    for (int s = 0; s < a.n_splits; s++) M = fmaxf(M, sp_attn_partial(a, li, qh, s)[0]);
-    float x[E];
+    if (qh < a.n_q_heads) {
+        float M = -INFINITY;
+        for (int s = 0; s < a.n_splits; s++) M = fmaxf(M, sp_attn_partial(a, li, qh, s)[0]);
+        float x[E];
 #pragma unroll
-    for (int e = 0; e < E; e++) x[e] = 0.0f;
-    float L = 0.0f;
-    for (int s = 0; s < a.n_splits; s++) {
-        const float *p = sp_attn_partial(a, li, qh, s);
-        if (p[0] == -INFINITY) continue;
-        const float w = exp2f(p[0] - M);
-        L += w * p[1];
+        for (int e = 0; e < E; e++) x[e] = 0.0f;
+        float L = 0.0f;
+        for (int s = 0; s < a.n_splits; s++) {
+            const float *p = sp_attn_partial(a, li, qh, s);
+            if (p[0] == -INFINITY) continue;
+            const float w = exp2f(p[0] - M);
+            L += w * p[1];
 #pragma unroll
-        for (int e = 0; e < E; e++) x[e] += w * p[4 + lane * E + e];
+            for (int e = 0; e < E; e++) x[e] += w * p[4 + lane * E + e];
+        }
+        const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+        sp_warp_wht<E>(x, lane);
+        __half h[E];
+#pragma unroll
+        for (int e = 0; e < E; e++) h[e] = __float2half_rn(x[e] * a.inv_sqrt_n * inv);
+        sp_attn_store_row<E>(a, li, qh, lane, h);
     }
-    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-    sp_warp_wht<E>(x, lane);
-    __half *o = a.out + ((long long)li * a.n_q_heads + qh) * n + lane * E;
-#pragma unroll
-    for (int e = 0; e < E; e++) o[e] = __float2half_rn(x[e] * a.inv_sqrt_n * inv);
+    sp_attn_gather_signal(a);
 }
 
 template <int E>
@@ -277,12 +280,11 @@ extern "C" float sp_cuda_attn_last_kernel_ms(void)
 
 extern "C" int sp_cuda_attn_last_splits(void) { return g_prof_splits; }
 
-extern "C" int sp_cuda_attn_decode(const sp_cuda_cache_t *cc, int layer0, int n_layers,
-                                   const void *d_q, int n_q_heads, int kv_len,
-                                   float logit_scale, void *d_out, int max_bands, void *stream)
+// Validate a decode call and fill its kernel arguments and split chunking.
+static int attn_prepare(const sp_cuda_cache_t *cc, int layer0, int n_layers, const void *d_q, int n_q_heads,
+                        int kv_len, float logit_scale, int max_bands, SpAttnArgs &a, bool &use_mma)
 {
-    sp_clear_error();
-    if (!cc || !cc->d_k_cache || !d_q || !d_out)
+    if (!cc || !cc->d_k_cache || !d_q)
         return sp_set_error(SP_ERR_ARG, "attn_decode: NULL argument");
     const int H = cc->config.n_heads_kv;
     if (layer0 < 0 || n_layers <= 0 || layer0 + n_layers > cc->config.n_layers)
@@ -296,7 +298,6 @@ extern "C" int sp_cuda_attn_decode(const sp_cuda_cache_t *cc, int layer0, int n_
     if (cudaSetDevice(cc->device) != cudaSuccess)
         return sp_set_error(SP_ERR_CUDA, "attn_decode: cudaSetDevice");
 
-    SpAttnArgs a;
     memset(&a, 0, sizeof(a));
     a.k_cache = (const uint8_t *)cc->d_k_cache;
     a.v_cache = (const uint8_t *)cc->d_v_cache;
@@ -304,7 +305,6 @@ extern "C" int sp_cuda_attn_decode(const sp_cuda_cache_t *cc, int layer0, int n_
     a.v_slot_stride = (long long)cc->max_seq_len * cc->v_bands.total_bytes;
     a.order = cc->config.use_mobius_mask ? cc->d_mobius_order : nullptr;
     a.q = (const __half *)d_q;
-    a.out = (__half *)d_out;
     a.ws = (float *)cc->d_attn_ws;
     a.layer0 = layer0; a.n_layers = n_layers; a.n_kv_heads = H;
     a.n_q_heads = n_q_heads; a.group = n_q_heads / H;
@@ -317,8 +317,7 @@ extern "C" int sp_cuda_attn_decode(const sp_cuda_cache_t *cc, int layer0, int n_
     a.inv_sqrt_n = sp_inv_sqrt_n(cc->config.head_dim);
     a.status = cc->d_status;
 
-    cudaStream_t s = (cudaStream_t)stream;
-    const bool use_mma = g_force_impl != 1 && sp_attn_mma_supported(a) == SP_OK;
+    use_mma = g_force_impl != 1 && sp_attn_mma_supported(a) == SP_OK;
     if (g_force_impl == 2 && !use_mma)
         return sp_set_error(SP_ERR_UNSUPPORTED, "attn_decode: tensor-core path does not support this layout");
 
@@ -338,11 +337,16 @@ extern "C" int sp_cuda_attn_decode(const sp_cuda_cache_t *cc, int layer0, int n_
     a.n_splits = kv_len == 0 ? 0 : (kv_len + chunk - 1) / chunk;
     if (a.n_splits > kAttnMaxSplits)
         return sp_set_error(SP_ERR_ARG, "attn_decode: too many splits");
+    return SP_OK;
+}
 
+// Main kernel(s) and the combine of a prepared call.
+static int attn_launch(const SpAttnArgs &a, bool use_mma, cudaStream_t s)
+{
     int rc = SP_OK;
-    const int n = cc->config.head_dim;
+    const int n = a.kl.n;
     g_prof_splits = a.n_splits;
-    if (use_mma && kv_len > 0)
+    if (use_mma && a.kv_len > 0)
         return sp_attn_mma_launch(a, s, g_prof ? g_ev[0] : nullptr, g_prof ? g_ev[1] : nullptr);
     if (a.n_splits > 0) {
         if (g_prof) cudaEventRecord(g_ev[0], s);
@@ -367,6 +371,81 @@ extern "C" int sp_cuda_attn_decode(const sp_cuda_cache_t *cc, int layer0, int n_
     case 512: return launch_combine<16>(a, s);
     }
     return sp_set_error(SP_ERR_UNSUPPORTED, "attn_decode: head_dim %d", n);
+}
+
+extern "C" int sp_cuda_attn_decode(const sp_cuda_cache_t *cc, int layer0, int n_layers,
+                                   const void *d_q, int n_q_heads, int kv_len,
+                                   float logit_scale, void *d_out, int max_bands, void *stream)
+{
+    sp_clear_error();
+    if (!d_out) return sp_set_error(SP_ERR_ARG, "attn_decode: NULL argument");
+    SpAttnArgs a;
+    bool use_mma = false;
+    int rc = attn_prepare(cc, layer0, n_layers, d_q, n_q_heads, kv_len, logit_scale, max_bands, a, use_mma);
+    if (rc) return rc;
+    a.out = (__half *)d_out;
+    return attn_launch(a, use_mma, (cudaStream_t)stream);
+}
+
+// ----------------------------------------------- fused decode + all-gather --
+
+// Bounded wait (2 s) until every rank's flag in this rank's buffer shows
+// `epoch` (wrap-safe); on timeout bit 1 of *status is set.
+__global__ void k_gather_wait(const unsigned int *flags, int world, unsigned int epoch, unsigned int *status)
+{
+    const int p = threadIdx.x;
+    if (p >= world) return;
+    unsigned long long t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (;;) {
+        unsigned int v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + p) : "memory");
+        if ((int)(v - epoch) >= 0) return;
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (t - t0 > 2000000000ull) {
+            atomicOr(status, 2u);
+            return;
+        }
+        __nanosleep(200);
+    }
+}
+
+extern "C" int sp_cuda_attn_decode_allgather(const sp_cuda_cache_t *cc, int layer0, int n_layers,
+                                             const void *d_q, int n_q_heads, int kv_len, float logit_scale,
+                                             int max_bands, void *d_local_buf, void *const *d_peer_bufs,
+                                             const int *d_dst_layer, const int *d_dst_qhead, int n_q_heads_total,
+                                             long long flags_offset, int rank, int world, unsigned int epoch,
+                                             void *stream)
+{
+    sp_clear_error();
+    if (!d_local_buf || !d_peer_bufs || !d_dst_layer || !d_dst_qhead)
+        return sp_set_error(SP_ERR_ARG, "attn_decode_allgather: NULL argument");
+    if (world < 1 || rank < 0 || rank >= world || world > 32 || n_q_heads_total < n_q_heads)
+        return sp_set_error(SP_ERR_ARG, "attn_decode_allgather: rank %d / world %d / heads %d of %d", rank, world,
+                            n_q_heads, n_q_heads_total);
+    if (flags_offset < 0 || (flags_offset & 3))
+        return sp_set_error(SP_ERR_ARG, "attn_decode_allgather: flags_offset must be a non-negative multiple of 4");
+    SpAttnArgs a;
+    bool use_mma = false;
+    int rc = attn_prepare(cc, layer0, n_layers, d_q, n_q_heads, kv_len, logit_scale, max_bands, a, use_mma);
+    if (rc) return rc;
+    a.g.peers = d_peer_bufs;
+    a.g.dst_layer = d_dst_layer;
+    a.g.dst_qhead = d_dst_qhead;
+    a.g.n_q_total = n_q_heads_total;
+    a.g.flags_offset = flags_offset;
+    a.g.rank = rank;
+    a.g.world = world;
+    a.g.epoch = epoch;
+    a.g.block_count = cc->d_status + 1;          // zero between calls
+    a.g.n_blocks = (unsigned)(((n_q_heads + 3) / 4) * n_layers);   // both combine grids: 4 rows per block
+    cudaStream_t s = (cudaStream_t)stream;
+    if ((rc = attn_launch(a, use_mma, s))) return rc;
+    k_gather_wait<<<1, 32, 0, s>>>(reinterpret_cast<const unsigned int *>(
+                                       reinterpret_cast<const unsigned char *>(d_local_buf) + flags_offset),
+                                   world, epoch, cc->d_status);
+    return sp_check_cuda(cudaGetLastError(), "attn_decode_allgather wait launch");
 }
 
 // ------------------------------------------------ allocation-free variant --

@@ -9,6 +9,23 @@
 constexpr int kAttnMaxSplits = 128;
 constexpr int kAttnMinChunk = 64;       // tokens; multiple of 16
 
+// Fused all-gather epilogue of the combine kernels (world == 0: off, the
+// outputs go to SpAttnArgs::out).  Each output row is stored straight into
+// every rank's gather buffer (peer addresses mapped into this process), at
+// row dst_layer[li] * n_q_total + dst_qhead[qh]; the last combine block then
+// writes `epoch` into slot `rank` of every rank's flag array.
+struct SpGather {
+    void *const *peers;                 // device array [world]
+    const int *dst_layer;               // [n_layers] destination layer row
+    const int *dst_qhead;               // [n_q_heads] destination query-head column
+    int n_q_total;                      // query heads per destination layer row
+    long long flags_offset;             // bytes: [world] uint32 flags in each buffer
+    int rank, world;
+    unsigned int epoch;
+    unsigned int *block_count;          // device counter, zero between calls
+    unsigned int n_blocks;              // combine blocks in the call
+};
+
 struct SpAttnArgs {
     const uint8_t *k_cache;
     const uint8_t *v_cache;
@@ -25,7 +42,56 @@ struct SpAttnArgs {
     float inv_sqrt_n;
     unsigned int *status;               // device error word
     SpBandLayout kl, vl;
+    SpGather g;
 };
+
+// Store one lane's E output halves of row (li, qh): locally, or into every
+// rank's gather buffer.
+template <int E>
+__device__ __forceinline__ void sp_attn_store_row(const SpAttnArgs &a, int li, int qh, int lane, const __half (&h)[E])
+{
+    const int n = 32 * E;
+    if (a.g.world == 0) {
+        __half *o = a.out + ((long long)li * a.n_q_heads + qh) * n + lane * E;
+#pragma unroll
+        for (int e = 0; e < E; e++) o[e] = h[e];
+        return;
+    }
+    const long long off = ((long long)a.g.dst_layer[li] * a.g.n_q_total + a.g.dst_qhead[qh]) * n + lane * E;
+    for (int p = 0; p < a.g.world; p++) {
+        __half *o = reinterpret_cast<__half *>(a.g.peers[p]) + off;
+        if constexpr (E == 4) {
+            uint2 w;
+            w.x = (uint32_t)__half_as_ushort(h[0]) | ((uint32_t)__half_as_ushort(h[1]) << 16);
+            w.y = (uint32_t)__half_as_ushort(h[2]) | ((uint32_t)__half_as_ushort(h[3]) << 16);
+            *reinterpret_cast<uint2 *>(o) = w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < E; e++) o[e] = h[e];
+        }
+    }
+}
+
+// After a combine block's rows are stored: the last block of the call
+// raises this rank's flag in every rank's buffer.  Called by every thread.
+__device__ __forceinline__ void sp_attn_gather_signal(const SpAttnArgs &a)
+{
+    if (a.g.world == 0) return;
+    __threadfence_system();             // this thread's peer stores before the count
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned int prev = atomicAdd(a.g.block_count, 1u);
+        if (prev == a.g.n_blocks - 1) {
+            __threadfence_system();
+            *a.g.block_count = 0u;
+            for (int p = 0; p < a.g.world; p++) {
+                unsigned int *f = reinterpret_cast<unsigned int *>(
+                    reinterpret_cast<unsigned char *>(a.g.peers[p]) + a.g.flags_offset) + a.g.rank;
+                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(a.g.epoch) : "memory");
+            }
+        }
+    }
+}
 
 __host__ __device__ inline long long sp_attn_partial_stride(int n) { return n + 4; }
 

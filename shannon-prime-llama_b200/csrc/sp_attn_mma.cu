@@ -611,13 +611,9 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
     }
 }
 
-// Merge the segment partials of one (layer, q head), transform, write fp16.
-__global__ void k_attn_combine_seg(SpAttnArgs a, Sched sc)
+// Segment merge of one (layer, q head) row.
+__device__ __forceinline__ void combine_row(const SpAttnArgs &a, const Sched &sc, int li, int qh, int lane)
 {
-    const int lane = threadIdx.x & 31;
-    const int qh = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (qh >= a.n_q_heads) return;
-    const int li = blockIdx.y;
     const long long u = (long long)li * a.n_kv_heads + qh / a.group;
     const int i0 = cta_of_tile(u * sc.tiles_per_unit, sc);
     const int i1 = cta_of_tile((u + 1) * sc.tiles_per_unit - 1, sc);
@@ -635,12 +631,23 @@ __global__ void k_attn_combine_seg(SpAttnArgs a, Sched sc)
     }
     const float inv = L > 0.0f ? 1.0f / L : 0.0f;
     sp_warp_wht<4>(x, lane);
-    __half *o = a.out + ((long long)li * a.n_q_heads + qh) * kN + lane * 4;
-    const __half2 h01 = __floats2half2_rn(x[0] * a.inv_sqrt_n * inv, x[1] * a.inv_sqrt_n * inv);
-    const __half2 h23 = __floats2half2_rn(x[2] * a.inv_sqrt_n * inv, x[3] * a.inv_sqrt_n * inv);
-    reinterpret_cast<__half2 *>(o)[0] = h01;
-    reinterpret_cast<__half2 *>(o)[1] = h23;
+    __half h[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) h[e] = __float2half_rn(x[e] * a.inv_sqrt_n * inv);
+    sp_attn_store_row<4>(a, li, qh, lane, h);
 }
+
+// Merge the segment partials of one (layer, q head), transform, write fp16
+// (locally, or into every rank's gather buffer).
+__global__ void k_attn_combine_seg(SpAttnArgs a, Sched sc)
+{
+    const int lane = threadIdx.x & 31;
+    const int qh = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int li = blockIdx.y;
+    if (qh < a.n_q_heads) combine_row(a, sc, li, qh, lane);
+    sp_attn_gather_signal(a);
+}
+
 
 }  // namespace
 
