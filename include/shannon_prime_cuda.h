@@ -301,6 +301,9 @@ typedef struct {
     /* --- B200 build additions --- */
     int              device;
     void            *d_tables;
+    float           *d_vrows;           /* [head_dim][pad_dim] rows of the transform matrix */
+    void            *d_recon;           /* [n_slots][head_dim][K + 8] fp16 reconstruction matrices
+                                           of the tensor-core batched read (NULL: not used) */
 } sp_cuda_hier_cache_t;
 
 /* Reference shannon_prime_cuda.h:337-349 (caller supplies the index sets and

@@ -1752,12 +1752,277 @@ SpSqDev sq_desc(const sp_cuda_sqfree_cache_t *cc, int which)
     return t;
 }
 
+// ------------------------------------------ hier decompress on tensor cores --
+// Decompression is linear in the dequantised slot: with c = [sk ; W sk + dev]
+// placed at the skeleton / residual coefficient indices, the output is
+//     out = V[:hd, :] c = (V_s + V_r W) sk + V_r dev
+// (V the orthonormal staged transform, V_s / V_r its columns at the skeleton
+// / residual indices).  Per slot the build kernel forms
+//     B = [ V_s + V_r W  |  V_r ]        (hd rows, K = 16 * n_bands + pad16(n_res))
+// in fp16, one 16-wide K block per skeleton band and the residuals after;
+// a decode tile of 16 positions is then one [16 x K] x [K x hd] product on
+// mma.sync, with A = the dequantised values (fp16) built in registers and B
+// staged in shared memory and fetched with ldmatrix.  The result is within
+// 1e-3 relative L2 of the exact reconstruction (fp16 A and B: ~3e-4), which
+// is the bound for reconstructed K/V; the per-vector read APIs keep the exact
+// SIMT kernel.
+constexpr int kHrWarps = 8;
+
+__host__ __device__ inline int hr_kp(int n_bands, int n_res) { return 16 * n_bands + (n_res + 15) / 16 * 16; }
+// Row stride of B in halves: K + 8, so 8 consecutive rows of 16 bytes land on
+// distinct bank groups for ldmatrix.
+__host__ __device__ inline int hr_stride(int n_bands, int n_res) { return hr_kp(n_bands, n_res) + 8; }
+
+// Transform matrix rows 0..hd-1 (fp32, [hd][pd]) of the staged Vilenkin
+// transform, from the transform of unit vectors in double (same stages and
+// tables as the codec).
+std::vector<float> hr_transform_rows(int pd, int hd)
+{
+    std::vector<double> x(pd), y(pd);
+    std::vector<float> v((size_t)hd * pd);
+    int f[kSqMaxStages], nf = 0, r = pd;
+    for (int p : {2, 3, 5, 7, 11}) while (r % p == 0) { f[nf++] = p; r /= p; }
+    for (int i = 0; i < pd; i++) {
+        for (int j = 0; j < pd; j++) x[j] = j == i ? 1.0 : 0.0;
+        int stride = 1;
+        for (int st = 0; st < nf; st++) {
+            const int p = f[st], bs = stride * p;
+            const double isp = 1.0 / sqrt((double)p);
+            for (int blk = 0; blk < pd / bs; blk++)
+                for (int o = 0; o < stride; o++) {
+                    const int base = blk * bs + o;
+                    double g[11];
+                    for (int j = 0; j < p; j++) g[j] = x[base + j * stride];
+                    for (int k = 0; k < p; k++) {
+                        double acc = 0.0;
+                        for (int j = 0; j < p; j++) {
+                            const double ang = 2.0 * 3.14159265358979323846 * (double)((k * j) % p) / (double)p;
+                            acc += (cos(ang) + sin(ang)) * g[j];
+                        }
+                        y[base + k * stride] = acc * isp;
+                    }
+                }
+            for (int j = 0; j < pd; j++) x[j] = y[j];
+            stride *= p;
+        }
+        for (int j = 0; j < hd; j++) v[(size_t)j * pd + i] = (float)x[j];   // column i = T e_i
+    }
+    return v;
+}
+
+// B of every slot: grid x = slot, one thread per output row j.
+__global__ void k_hier_build_recon(const float *vrows, const __half *W, const int *skel_idx, const int *res_idx,
+                                   SpBandLayout bl, int hd, int pd, int n_skel, int n_res, __half *recon)
+{
+    const int slot = blockIdx.x, stride = hr_stride(bl.n_bands, n_res);
+    const __half *w = W + (size_t)slot * n_res * n_skel;
+    for (int j = threadIdx.x; j < hd; j += blockDim.x) {
+        const float *vj = vrows + (size_t)j * pd;
+        __half *bj = recon + ((size_t)slot * hd + j) * stride;
+        for (int k = 0; k < stride; k++) bj[k] = __float2half_rn(0.0f);
+        for (int s = 0; s < n_skel; s++) {
+            int b = 0;
+            for (int q = 1; q < bl.n_bands; q++) if (s >= bl.off[q]) b = q;
+            float m = vj[skel_idx[s]];
+            for (int r = 0; r < n_res; r++) m = fmaf(vj[res_idx[r]], __half2float(w[(size_t)r * n_skel + s]), m);
+            bj[16 * b + (s - bl.off[b])] = __float2half_rn(m);
+        }
+        for (int r = 0; r < n_res; r++) bj[16 * bl.n_bands + r] = __float2half_rn(vj[res_idx[r]]);
+    }
+}
+
+struct HrArgs {
+    const uint8_t *cache;         // slab base
+    const uint8_t *cache_end;     // one past the slab's last byte
+    long long slot_stride;
+    const __half *recon;          // [n_slots][hd][stride]
+    float *out;                   // [n_layers][n_tok][nh][hd]
+    int layer0, n_layers, nh, start_pos, n_tok, tokens_per_cta;
+};
+
+__device__ __forceinline__ uint32_t hr_bits(const uint32_t *w, int pos)
+{
+    return __funnelshift_r(w[pos >> 5], w[(pos >> 5) + 1], pos & 31);
+}
+
+__device__ __forceinline__ void hr_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
+{
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi)
+{
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// NB skeleton bands (each <= 16 values), KSR residual K blocks, 2-bit residual
+// levels, hd a multiple of 64 (HD).
+template <int NB, int KSR, int HD>
+__global__ void __launch_bounds__(kHrWarps * 32, 1)
+k_hier_recon(SpSqDev t, HrArgs h)
+{
+    constexpr int KS = NB + KSR, KP = 16 * KS, STRIDE = KP + 8;
+    extern __shared__ __align__(16) unsigned char smem[];
+    __half *Bs = reinterpret_cast<__half *>(smem);
+    const int bpp = t.bytes_per_pos;
+    const int stage_words = (16 * bpp + 8) / 4 + 2;
+    uint32_t *stage_all = reinterpret_cast<uint32_t *>(smem + (size_t)HD * STRIDE * 2);
+    uint16_t *lut = reinterpret_cast<uint16_t *>(stage_all + kHrWarps * stage_words);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    const int li = blockIdx.y / h.nh, hh = blockIdx.y % h.nh;
+    const int slot = (h.layer0 + li) * h.nh + hh;
+
+    // B of this slot -> shared memory (16-byte copies)
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(h.recon + (size_t)slot * HD * STRIDE);
+        uint4 *dst = reinterpret_cast<uint4 *>(Bs);
+        for (int i = threadIdx.x; i < HD * STRIDE / 8; i += blockDim.x) dst[i] = src[i];
+    }
+    if (threadIdx.x < 16) {       // PRMT selectors: nibble (l0 | l1 << 2) -> halves T[l0], T[l1]
+        const int l0 = threadIdx.x & 3, l1 = threadIdx.x >> 2;
+        lut[threadIdx.x] = (uint16_t)((2 * l0) | ((2 * l0 + 1) << 4) | ((2 * l1) << 8) | ((2 * l1 + 1) << 12));
+    }
+    __syncthreads();
+
+    uint32_t *stw = stage_all + warp * stage_words;
+    const uint8_t *slot_base = h.cache + (long long)slot * h.slot_stride;
+    const int L = 1 << t.res_bits;
+    const float center = __fdiv_rn((float)(L - 1), 2.0f);
+    const int tb = blockIdx.x * h.tokens_per_cta, te = min(h.n_tok, tb + h.tokens_per_cta);
+    // ldmatrix row address of this lane: matrix lane>>3, row lane&7
+    const int lm = lane >> 3, lr = lane & 7;
+    const uint32_t b_lane = spb::smem_u32(Bs) + (uint32_t)(((8 * (lm >> 1) + lr) * STRIDE + 8 * (lm & 1)) * 2);
+
+    for (int p0 = tb + 16 * warp; p0 < te; p0 += 16 * kHrWarps) {
+        const int nrows = min(16, te - p0);
+        // ---- stage the tile's packed rows (word-aligned copy) ----
+        const uint8_t *gs = slot_base + (long long)(h.start_pos + p0) * bpp;
+        const uint8_t *ga = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(gs) & ~uintptr_t(3));
+        const int soff = (int)(gs - ga);
+        const int nwords = (nrows * bpp + soff + 3) / 4;
+        __syncwarp();
+        for (int i = lane; i < stage_words; i += 32) {
+            uint32_t v = 0;
+            if (i < nwords) {
+                const uint8_t *p = ga + 4 * i;
+                if (p + 4 <= h.cache_end) {
+                    v = *reinterpret_cast<const uint32_t *>(p);
+                } else {
+                    for (int b = 0; b < 4; b++)
+                        if (p + b < h.cache_end) v |= (uint32_t)p[b] << (8 * b);
+                }
+            }
+            stw[i] = v;
+        }
+        __syncwarp();
+        // ---- A fragments: rows g and g+8 of the tile ----
+        uint32_t A[KS][4];
+#pragma unroll
+        for (int hv = 0; hv < 2; hv++) {
+            const int v = g + 8 * hv;
+            const int rb = 8 * (soff + v * bpp);
+            // residual value table T[lv] = (lv - center) * step, fp16
+            const float mag = __uint_as_float(hr_bits(stw, rb + 8 * t.mag_off));
+            const float step = __fdiv_rn(__fmul_rn(2.0f, mag), (float)(L - 1));
+            const uint32_t tlo = pack_h2(__fmul_rn(__fsub_rn(0.0f, center), step), __fmul_rn(__fsub_rn(1.0f, center), step));
+            const uint32_t thi = pack_h2(__fmul_rn(__fsub_rn(2.0f, center), step), __fmul_rn(__fsub_rn(3.0f, center), step));
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                float sc = __half2float(__ushort_as_half((unsigned short)(hr_bits(stw, rb + 8 * t.bl.byte_off[b]) & 0xffffu)));
+                sc = fabsf(sc) <= 65504.0f ? sc : 0.0f;
+                const int bits = t.bl.bits[b];
+                const uint32_t mask = (1u << bits) - 1u;
+                const float m = (float)((1 << (bits - 1)) - 1);
+                const int cb = rb + 8 * (t.bl.byte_off[b] + 2);
+                float q[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int i = 2 * c + (e & 1) + 8 * (e >> 1);
+                    const uint32_t u = i < t.bl.size[b] ? (hr_bits(stw, cb + i * bits) & mask) : 0u;
+                    q[e] = i < t.bl.size[b] ? __fmul_rn(__fsub_rn((float)u, m), sc) : 0.0f;
+                }
+                A[b][hv] = pack_h2(q[0], q[1]);
+                A[b][2 + hv] = pack_h2(q[2], q[3]);
+            }
+            const int resb = rb + 8 * t.res_off;
+#pragma unroll
+            for (int j = 0; j < KSR; j++) {
+                const uint32_t w = hr_bits(stw, resb + 32 * j);
+                A[NB + j][hv] = __byte_perm(tlo, thi, lut[(w >> (4 * c)) & 15u]);
+                A[NB + j][2 + hv] = __byte_perm(tlo, thi, lut[(w >> (4 * c + 16)) & 15u]);
+            }
+        }
+        // ---- products: 64 output columns at a time ----
+        float *orow0 = h.out + (((long long)li * h.n_tok + p0 + g) * h.nh + hh) * HD;
+        const long long rstep8 = 8LL * h.nh * HD;
+#pragma unroll 1
+        for (int n0 = 0; n0 < HD; n0 += 64) {
+            float acc[8][4];
+#pragma unroll
+            for (int nt = 0; nt < 8; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+#pragma unroll
+            for (int ks = 0; ks < KS; ks++) {
+#pragma unroll
+                for (int np = 0; np < 4; np++) {
+                    uint32_t b0, b1, b2, b3;
+                    const uint32_t addr = b_lane + (uint32_t)(((n0 + 16 * np) * STRIDE + 16 * ks) * 2);
+                    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                                 : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3) : "r"(addr));
+                    hr_mma(acc[2 * np], A[ks], b0, b1);
+                    hr_mma(acc[2 * np + 1], A[ks], b2, b3);
+                }
+            }
+#pragma unroll
+            for (int nt = 0; nt < 8; nt++) {
+                const int col = n0 + 8 * nt + 2 * c;
+                if (g < nrows) *reinterpret_cast<float2 *>(orow0 + col) = make_float2(acc[nt][0], acc[nt][1]);
+                if (g + 8 < nrows) *reinterpret_cast<float2 *>(orow0 + rstep8 + col) = make_float2(acc[nt][2], acc[nt][3]);
+            }
+        }
+    }
+}
+
+size_t hr_smem_bytes(const SpSqDev &t, int hd)
+{
+    const int stride = hr_stride(t.bl.n_bands, t.n_res);
+    const int stage_words = (16 * t.bytes_per_pos + 8) / 4 + 2;
+    return (size_t)hd * stride * 2 + (size_t)kHrWarps * stage_words * 4 + 64;
+}
+
+// The tensor-core kernel for the slot shape, or nullptr (then the SIMT kernel
+// serves the read).
+using HrKernel = void (*)(SpSqDev, HrArgs);
+HrKernel hr_kernel(const SpSqDev &t)
+{
+    if (!t.hier || t.res_bits != 2 || t.hd != 256) return nullptr;
+    for (int b = 0; b < t.bl.n_bands; b++) if (t.bl.size[b] > 16) return nullptr;
+    if (hr_smem_bytes(t, t.hd) > 220 * 1024) return nullptr;
+    const int ksr = (t.n_res + 15) / 16;
+    if (t.bl.n_bands == 2 && ksr == 19) return k_hier_recon<2, 19, 256>;
+    return nullptr;
+}
+
 SpSqDev hier_desc(const sp_cuda_hier_cache_t *hc)
 {
     SpSqDev t;
     sq_build_desc(t, hc->config.head_dim, hc->pad_dim, hc->n_skeleton, hc->n_target, 0, hc->skel_bands,
                   hc->target_res_bits, 0, 1, (const int *)hc->d_tables);
     return t;
+}
+
+// (Re)build the per-slot reconstruction matrices from the current W.
+int hr_build(const sp_cuda_hier_cache_t *hc)
+{
+    if (!hc->d_recon) return SP_OK;
+    const SpSqDev t = hier_desc(hc);
+    k_hier_build_recon<<<hc->n_slots, 256, 0, (cudaStream_t)hc->stream>>>(
+        hc->d_vrows, (const __half *)hc->d_W, hc->d_skeleton_idx, hc->d_target_idx, t.bl, hc->config.head_dim,
+        hc->pad_dim, hc->n_skeleton, hc->n_target, (__half *)hc->d_recon);
+    return sp_check_cuda(cudaGetLastError(), "hier reconstruction build");
 }
 
 }  // namespace
@@ -2189,6 +2454,14 @@ int sp_cuda_hier_cache_init(sp_cuda_hier_cache_t *hc, const sp_config_t *cfg, in
     cudaMemset(hc->d_k_cache, 0, total);
     cudaMemset(hc->d_v_cache, 0, total);
     cudaMemset(hc->d_W, 0, (size_t)n_slots * n_target * n_skeleton * 2);
+    if (hr_kernel(t)) {      // tensor-core batched read: transform rows + per-slot matrices
+        const std::vector<float> vr = hr_transform_rows(pad_dim, cfg->head_dim);
+        up((void **)&hc->d_vrows, vr.data(), vr.size() * 4, "hier transform rows");
+        up(&hc->d_recon, nullptr,
+           (size_t)n_slots * cfg->head_dim * hr_stride(t.bl.n_bands, n_target) * 2, "hier reconstruction");
+        if (!rc) rc = hr_build(hc);
+        if (rc) { sp_cuda_hier_cache_free(hc); return rc; }
+    }
     if ((rc = sq_upload_constants()) || (rc = sp_check_cuda(cudaDeviceSynchronize(), "hier_cache_init"))) {
         sp_cuda_hier_cache_free(hc);
         return rc;
@@ -2207,6 +2480,8 @@ void sp_cuda_hier_cache_free(sp_cuda_hier_cache_t *hc)
     cudaFree(hc->d_k_cache);
     cudaFree(hc->d_v_cache);
     cudaFree(hc->d_W);
+    cudaFree(hc->d_vrows);
+    cudaFree(hc->d_recon);
     memset(hc, 0, sizeof(*hc));
 }
 
@@ -2215,7 +2490,8 @@ int sp_cuda_hier_cache_upload_W(sp_cuda_hier_cache_t *hc, const uint16_t *W_all)
     sp_clear_error();
     if (!hc || !hc->d_W || !W_all) return sp_set_error(SP_ERR_ARG, "hier_upload_W: NULL argument");
     const size_t bytes = (size_t)hc->n_slots * hc->n_target * hc->n_skeleton * 2;
-    return sp_check_cuda(cudaMemcpy(hc->d_W, W_all, bytes, cudaMemcpyHostToDevice), "hier_upload_W");
+    int rc = sp_check_cuda(cudaMemcpy(hc->d_W, W_all, bytes, cudaMemcpyHostToDevice), "hier_upload_W");
+    return rc ? rc : hr_build(hc);
 }
 
 static int hier_check(const sp_cuda_hier_cache_t *hc, int layer, int n_layers, int head, int pos, int n)
@@ -2283,6 +2559,28 @@ int sp_cuda_hier_read_kv_tokens(const sp_cuda_hier_cache_t *hc, int layer0, int 
         SqIo io;
         if ((rc = hier_io(hc, which, layer0, n_layers, 0, H, start_pos, n_pos, io))) return rc;
         io.out = out;
+        HrKernel hk = hc->d_recon && !getenv("SHANNON_PRIME_HIER_READ_SIMT") ? hr_kernel(t) : nullptr;
+        if (hk && n_pos > 0) {
+            HrArgs a;
+            a.cache = io.cache;
+            a.slot_stride = io.slot_stride;
+            a.cache_end = io.cache + (long long)hc->n_slots * io.slot_stride;
+            a.recon = (const __half *)hc->d_recon;
+            a.out = out;
+            a.layer0 = layer0; a.n_layers = n_layers; a.nh = H; a.start_pos = start_pos; a.n_tok = n_pos;
+            const int slots = n_layers * H;
+            int chunks = (148 * 2 + slots - 1) / slots;
+            const int max_chunks = (n_pos + 16 * kHrWarps - 1) / (16 * kHrWarps);
+            if (chunks > max_chunks) chunks = max_chunks;
+            if (chunks < 1) chunks = 1;
+            a.tokens_per_cta = ((n_pos + chunks - 1) / chunks + 15) / 16 * 16;
+            chunks = (n_pos + a.tokens_per_cta - 1) / a.tokens_per_cta;
+            const size_t sm = hr_smem_bytes(t, t.hd);
+            cudaFuncSetAttribute(hk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+            hk<<<dim3(chunks, slots), kHrWarps * 32, sm, (cudaStream_t)hc->stream>>>(t, a);
+            if ((rc = sp_check_cuda(cudaGetLastError(), "hier tensor-core read launch"))) return rc;
+            continue;
+        }
         if ((rc = sq_launch_decode(t, io, (cudaStream_t)hc->stream))) return rc;
     }
     return SP_OK;
