@@ -1767,6 +1767,7 @@ SpSqDev sq_desc(const sp_cuda_sqfree_cache_t *cc, int which)
 // is the bound for reconstructed K/V; the per-vector read APIs keep the exact
 // SIMT kernel.
 constexpr int kHrWarps = 8;
+constexpr int kHrPrefetchWords = 16;    // staged words per lane: rows of up to 127 bytes
 
 __host__ __device__ inline int hr_kp(int n_bands, int n_res) { return 16 * n_bands + (n_res + 15) / 16 * 16; }
 // Row stride of B in halves: K + 8, so 8 consecutive rows of 16 bytes land on
@@ -1897,28 +1898,42 @@ k_hier_recon(SpSqDev t, HrArgs h)
     const int lm = lane >> 3, lr = lane & 7;
     const uint32_t b_lane = spb::smem_u32(Bs) + (uint32_t)(((8 * (lm >> 1) + lr) * STRIDE + 8 * (lm & 1)) * 2);
 
-    for (int p0 = tb + 16 * warp; p0 < te; p0 += 16 * kHrWarps) {
+    // The packed rows of a tile (word-aligned cover, zero past the tile) are
+    // loaded into registers one tile ahead: lane holds words lane + 32 i.
+    constexpr int NPW = kHrPrefetchWords;
+    uint32_t pf[NPW];
+    auto fetch = [&](int p0) {
         const int nrows = min(16, te - p0);
-        // ---- stage the tile's packed rows (word-aligned copy) ----
         const uint8_t *gs = slot_base + (long long)(h.start_pos + p0) * bpp;
         const uint8_t *ga = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(gs) & ~uintptr_t(3));
-        const int soff = (int)(gs - ga);
-        const int nwords = (nrows * bpp + soff + 3) / 4;
-        __syncwarp();
-        for (int i = lane; i < stage_words; i += 32) {
+        const int nwords = (nrows * bpp + (int)(gs - ga) + 3) / 4;
+#pragma unroll
+        for (int i = 0; i < NPW; i++) {
+            const int wi = lane + 32 * i;
             uint32_t v = 0;
-            if (i < nwords) {
-                const uint8_t *p = ga + 4 * i;
+            if (wi < nwords) {
+                const uint8_t *p = ga + 4 * wi;
                 if (p + 4 <= h.cache_end) {
-                    v = *reinterpret_cast<const uint32_t *>(p);
+                    v = __ldcs(reinterpret_cast<const unsigned int *>(p));
                 } else {
                     for (int b = 0; b < 4; b++)
                         if (p + b < h.cache_end) v |= (uint32_t)p[b] << (8 * b);
                 }
             }
-            stw[i] = v;
+            pf[i] = v;
         }
+    };
+    if (tb + 16 * warp < te) fetch(tb + 16 * warp);
+    for (int p0 = tb + 16 * warp; p0 < te; p0 += 16 * kHrWarps) {
+        const int nrows = min(16, te - p0);
+        const uint8_t *gs = slot_base + (long long)(h.start_pos + p0) * bpp;
+        const int soff = (int)(reinterpret_cast<uintptr_t>(gs) & 3);
         __syncwarp();
+#pragma unroll
+        for (int i = 0; i < NPW; i++)
+            if (lane + 32 * i < stage_words) stw[lane + 32 * i] = pf[i];
+        __syncwarp();
+        if (p0 + 16 * kHrWarps < te) fetch(p0 + 16 * kHrWarps);
         // ---- A fragments: rows g and g+8 of the tile ----
         uint32_t A[KS][4];
 #pragma unroll
@@ -2001,6 +2016,7 @@ HrKernel hr_kernel(const SpSqDev &t)
     if (!t.hier || t.res_bits != 2 || t.hd != 256) return nullptr;
     for (int b = 0; b < t.bl.n_bands; b++) if (t.bl.size[b] > 16) return nullptr;
     if (hr_smem_bytes(t, t.hd) > 220 * 1024) return nullptr;
+    if ((16 * t.bytes_per_pos + 8) / 4 + 2 > 32 * kHrPrefetchWords) return nullptr;
     const int ksr = (t.n_res + 15) / 16;
     if (t.bl.n_bands == 2 && ksr == 19) return k_hier_recon<2, 19, 256>;
     return nullptr;
