@@ -55,6 +55,7 @@ constexpr int kVTile = 16 * 50;       // 800
 constexpr int kStageBytes = kKTile + kVTile;   // 2016
 constexpr int kN = 128;
 constexpr float kEmptyMax = -1.0e30f; // running max before the first valid token
+constexpr int kFlushTiles = 16;       // tiles between V-accumulator recentrings
 
 // Fixed ship layout (checked on the host against the cache's band config).
 // Bit position of band b's first code within a K row.
@@ -74,11 +75,15 @@ __host__ __device__ constexpr int pair_dhi(int b, int p)
 {
     return b < 2 ? 4 : (b == 2 ? ((p & 1) ? 4 : 0) : ((p & 1) ? 3 : 0));
 }
-// Pre-shift of V code j of a lane's 16-code chunk (windows of 5 codes:
-// three masked in place at bits 0,3,6, two after a shift by 9).
+// Pre-shift of V code j of a lane's 16-code chunk (windows of 5 codes at
+// bits 0,3,6,9,12: the first two taken after a left shift by 4 (d 4, 7), the
+// third in place (d 6), the last two after a right shift by 5 (d 4, 7);
+// code 15 at d 4).  The tensor cores' products lose precision on the
+// smallest subnormals (codes below bit 4 of a half: up to 2e-6 of an MMA's
+// magnitude at d = 0, a systematic error), so no code sits there.
 __host__ __device__ constexpr int vcode_d(int j)
 {
-    return j == 15 ? 0 : ((j % 5) < 3 ? 3 * (j % 5) : 3 * (j % 5 - 3));
+    return j == 15 ? 4 : ((j % 5) == 2 ? 6 : ((j % 5) == 0 || (j % 5) == 3) ? 4 : 7);
 }
 
 struct Sched {
@@ -345,6 +350,32 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
         float m_run[NT], nkm[NT], l_sum[NT], p_sum[NT];
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) { m_run[nt] = kEmptyMax; nkm[nt] = 0.0f; l_sum[nt] = 0.0f; p_sum[nt] = 0.0f; }
+        // The MMAs accumulate p * vscale * u over the raw codes u (0..6); the
+        // offset 3 * sum(p * vscale) comes off afterwards.  Over a long, flat
+        // softmax the raw sum is ~3 sqrt(T) times the centered one, and the
+        // tensor cores' accumulation (not IEEE-rounded per add) drifts in
+        // proportion to the accumulator's size: 1e-3 of the output after a
+        // few hundred tiles.  Every kFlushTiles tiles the window's offset is
+        // taken off the accumulators with fp32 fmas, so they stay centered.
+        int n_since_flush = 0;
+        auto recenter = [&]() {
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+                float ps = p_sum[nt];                   // window sum over the warp's positions
+#pragma unroll
+                for (int o = 4; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+                const float off = -3.0f * ps;           // V offset 2^(3-1)-1
+#pragma unroll
+                for (int mt = 0; mt < 8; mt++) {
+#pragma unroll
+                    for (int rr = 0; rr < 2; rr++)      // hi column, in units of 2^(d-24)
+                        oacc[nt][mt][2 * rr] = fmaf(off, 1.0f / (float)(1 << (24 - vcode_d(2 * mt + rr))),
+                                                    oacc[nt][mt][2 * rr]);
+                }
+                p_sum[nt] = 0.0f;
+            }
+            n_since_flush = 0;
+        };
 
         // ---- my tiles of this segment ------------------------------------
         // Two-stage software pipeline: iteration k computes the K-side
@@ -473,17 +504,19 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
                 W[0] = __byte_perm(xal, xbl, 0x5410);
                 W[1] = __byte_perm(shf(xal, xah, 15), shf(xbl, xbh, 15), 0x5410);
                 W[2] = __byte_perm(shf(xal, xah, 30), shf(xbl, xbh, 30), 0x5410);
-                W[3] = __byte_perm(xah, xbh, 0x5410) >> 13;
+                W[3] = __byte_perm(xah, xbh, 0x5410) >> 9;
+                // every code lands at bit 4 or above of its half: the tensor
+                // cores lose precision on the smallest subnormals (d < 4)
 #pragma unroll
                 for (int wi = 0; wi < 3; wi++) {
-                    const uint32_t t9 = W[wi] >> 9;
-                    AV[hh][5 * wi + 0] = W[wi] & 0x00070007u;
-                    AV[hh][5 * wi + 1] = W[wi] & 0x00380038u;
+                    const uint32_t l4 = W[wi] << 4, r5 = W[wi] >> 5;
+                    AV[hh][5 * wi + 0] = l4 & 0x00700070u;
+                    AV[hh][5 * wi + 1] = l4 & 0x03800380u;
                     AV[hh][5 * wi + 2] = W[wi] & 0x01C001C0u;
-                    AV[hh][5 * wi + 3] = t9 & 0x00070007u;
-                    AV[hh][5 * wi + 4] = t9 & 0x00380038u;
+                    AV[hh][5 * wi + 3] = r5 & 0x00700070u;
+                    AV[hh][5 * wi + 4] = r5 & 0x03800380u;
                 }
-                AV[hh][15] = W[3] & 0x00070007u;
+                AV[hh][15] = W[3] & 0x00700070u;
             }
             float vscale[2];
 #pragma unroll
@@ -541,6 +574,7 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
                 float sn[NT][2];
                 k_scores(kn % kStages, ctn * 16, sn);
                 v_step(k_next % kStages, su);
+                if (++n_since_flush == kFlushTiles) recenter();
                 if (has_next) update_max(sn);
                 __syncwarp();
                 if (lane == 0 && k_next + kStages < n_my) issue(k_next + kStages);
