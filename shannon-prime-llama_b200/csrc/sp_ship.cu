@@ -351,6 +351,7 @@ k_encode_fast(FastArgs fa)
     const int bits = fa.fb.bits[ln];
     const int max_val = (1 << (bits - 1)) - 1;
     const unsigned mult = 1u << bits;
+    const unsigned off4 = (unsigned)max_val * (1u + mult + mult * mult + mult * mult * mult);
     const int bitpos = fa.fb.bitpos[ln];
     const int sword = fa.fb.scale_word[ln];
     const int sshift = fa.fb.scale_shift[ln];
@@ -440,25 +441,28 @@ k_encode_fast(FastArgs fa)
         const float stored = __half2float(hs);
         const float inv = stored > 0.0f ? __frcp_rn(stored) : 0.0f;     // = 1.0f / stored
         // ---- quantise and pack the lane's codes into one field: codes
-        //      0..3 and 4..7 are accumulated Horner-style (u3*m + u2)*m ...
+        //      0..3 and 4..7 are accumulated Horner-style (q3*m + q2)*m ...
         //      with m = 2^bits, one integer multiply-add per code ----
-        unsigned u[E];
+        int qv[E];
 #pragma unroll
         for (int e = 0; e < E; e++) {
-            int q = __float2int_rn(__fmul_rn(x[e], inv));    // NaN -> 0, saturating
-            q = q > max_val ? max_val : (q < -max_val ? -max_val : q);
-            u[e] = (unsigned)(q + max_val);
+            const int q = __float2int_rn(__fmul_rn(x[e], inv));   // NaN -> 0, saturating
+            qv[e] = min(max(q, -max_val), max_val);
         }
         __syncwarp();                       // row zeroed, buf reads done
 #pragma unroll
         for (int g = 0; g < E / 8; g++) {
-            // codes 8g..8g+7 as one field of 8 * bits <= 64 bits
-            unsigned f_lo = u[8 * g + 3], f_hi = u[8 * g + 7];
+            // codes 8g..8g+7 as one field of 8 * bits <= 64 bits, over the
+            // signed codes; the offset max_val of all four codes of a half
+            // is added once (exact modulo 2^32: the field fits in 32 bits)
+            unsigned f_lo = (unsigned)qv[8 * g + 3], f_hi = (unsigned)qv[8 * g + 7];
 #pragma unroll
             for (int e = 2; e >= 0; e--) {
-                f_lo = f_lo * mult + u[8 * g + e];
-                f_hi = f_hi * mult + u[8 * g + 4 + e];
+                f_lo = f_lo * mult + (unsigned)qv[8 * g + e];
+                f_hi = f_hi * mult + (unsigned)qv[8 * g + 4 + e];
             }
+            f_lo += off4;
+            f_hi += off4;
             const unsigned long long field = ((unsigned long long)f_hi << (4 * bits)) | f_lo;
             const int pos = bitpos + 8 * g * bits;
             const int w0 = pos >> 5, sh = pos & 31;
