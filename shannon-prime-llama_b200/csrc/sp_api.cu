@@ -193,7 +193,7 @@ static int write_one_half(sp_cuda_cache_t *cc, int which, int layer, int head0, 
     return sp_launch_encode(d_in, dtype, n_tokens, nh, base,
                             (long long)layer * cc->config.n_heads_kv + head0,
                             (long long)cc->max_seq_len * bc.total_bytes, start_pos, order, true,
-                            bl, (cudaStream_t)cc->stream);
+                            bl, (cudaStream_t)cc->stream, true, cc->d_status);
 }
 
 extern "C" int sp_cuda_write_kv_tokens(sp_cuda_cache_t *cc, int layer, int start_pos,

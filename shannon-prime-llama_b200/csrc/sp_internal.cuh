@@ -36,7 +36,14 @@ float sp_inv_sqrt_n(int n);
 int sp_launch_encode(const void *d_in, int dtype, int n_tokens, int nh,
                      uint8_t *d_out_base, long long slot0, long long slot_stride_bytes,
                      int start_pos, const int *d_order, bool do_wht,
-                     const SpBandLayout &bl, cudaStream_t s);
+                     const SpBandLayout &bl, cudaStream_t s, bool std_order = false,
+                     unsigned int *d_status = nullptr);
+// Lane-per-vector ship encoder (sp_ship_lane.cu): returns 1 and sets *rc
+// when it takes the call (head_dim 128 ship layouts, standard order).
+int sp_encode_lane_try(const void *d_in, int dtype, int n_tokens, int nh, uint8_t *d_out_base,
+                       long long slot0, long long slot_stride, int start_pos, bool std_order,
+                       const int *d_order, bool do_wht, const SpBandLayout &bl, unsigned int *d_status,
+                       cudaStream_t s, int *rc);
 int sp_launch_decode(const uint8_t *d_in_base, long long slot, long long slot_stride_bytes,
                      int start_pos, int n_pos, float *d_out, const int *d_order,
                      bool do_wht, int max_bands, const SpBandLayout &bl, cudaStream_t s);

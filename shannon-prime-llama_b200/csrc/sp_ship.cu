@@ -624,11 +624,16 @@ int launch_decode_t(const DecodeArgs &a, bool wht, cudaStream_t s)
 int sp_launch_encode(const void *d_in, int dtype, int n_tokens, int nh,
                      uint8_t *d_out_base, long long slot0, long long slot_stride_bytes,
                      int start_pos, const int *d_order, bool do_wht,
-                     const SpBandLayout &bl, cudaStream_t s)
+                     const SpBandLayout &bl, cudaStream_t s, bool std_order,
+                     unsigned int *d_status)
 {
     if (n_tokens == 0) return SP_OK;
     if (!d_in || !d_out_base || n_tokens < 0 || nh <= 0)
         return sp_set_error(SP_ERR_ARG, "encode: bad arguments");
+    int rc = SP_OK;
+    if (sp_encode_lane_try(d_in, dtype, n_tokens, nh, d_out_base, slot0, slot_stride_bytes, start_pos,
+                           std_order, d_order, do_wht, bl, d_status, s, &rc))
+        return rc;
     EncodeArgs a;
     a.in = d_in; a.out_base = d_out_base; a.slot0 = slot0; a.slot_stride = slot_stride_bytes;
     a.n_tokens = n_tokens; a.nh = nh; a.start_pos = start_pos; a.order = d_order;

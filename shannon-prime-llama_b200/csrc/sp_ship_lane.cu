@@ -1,0 +1,336 @@
+// sp_ship_lane.cu — lane-per-vector ship encoder for head_dim 128.
+//
+// The write path (VHT2 -> Möbius reorder -> band quantise -> pack, reference
+// sp_cuda_write_k/_v, shannon_prime_cuda.cu:474-521, 565-620) for the two
+// ship layouts at head_dim 128: K bands 4 x 32 at 5/5/4/3 bits with the
+// squarefree-first order (76-byte rows), V one 128-code band at 3 bits
+// (50-byte rows).
+//
+// One thread owns one whole vector.  A warp takes 32 consecutive positions
+// of one head:
+//   - each lane bulk-copies its 512-byte input row (cp.async.bulk, the TMA
+//     engine, no multicast) into shared memory, rotated by 16*(lane & 7)
+//     bytes so the lane's 16-byte reads of the 8 lanes of a phase fall in
+//     distinct banks; the copy of the next batch is issued as soon as the
+//     current one sits in registers, so it streams under the arithmetic;
+//   - the 128-point Hartley butterfly runs entirely in the thread's
+//     registers (896 IEEE adds, no shuffles);
+//   - the Möbius order and the band layout are compile-time, so the
+//     reorder is register renaming and every code's bit position is a
+//     constant: one shift-add per code into the row's words;
+//   - the 32 packed rows of the batch are contiguous in the slot, so they
+//     are staged in shared memory and written back by one bulk store.
+// That is about 60 warp instructions per vector, against ~190 for the
+// lane-group kernel in sp_ship.cu, which remains the path for every other
+// layout and for a caller-supplied Möbius table.
+//
+// Bit-exactness: the arithmetic is the same sequence of single IEEE
+// operations as the CPU restatement (ascending butterfly lengths, then
+// x * (1/sqrt(n)); band absmax skipping NaN; IEEE amax / m; fp16 RNE scale;
+// IEEE 1/stored; rint; clamp), so codes equal those of the lane-group
+// kernel and of the oracle.
+#include "sp_internal.cuh"
+#include "sp_bulk.cuh"
+
+#include <stdlib.h>
+
+namespace {
+
+constexpr int kLN = 128;              // coefficients per vector
+constexpr int kLaneWarps = 4;         // warps per CTA
+constexpr int kLaneMinBlocks = 3;     // CTAs per SM (12 warps, <= 170 registers)
+
+// Compile-time ship layouts.  KS: K (4 bands of 32, 5/5/4/3 bits, Möbius
+// order); otherwise V (1 band of 128 at 3 bits, natural order).
+template <bool KS> struct LaneLayout;
+template <> struct LaneLayout<true> {
+    static constexpr int NB = 4, TB = 76, SIZE = 32;
+    __host__ __device__ static constexpr int bits(int b) { return b < 2 ? 5 : (b == 2 ? 4 : 3); }
+    __host__ __device__ static constexpr int byte_off(int b) { return b == 0 ? 0 : b == 1 ? 22 : b == 2 ? 44 : 62; }
+};
+template <> struct LaneLayout<false> {
+    static constexpr int NB = 1, TB = 50, SIZE = 128;
+    __host__ __device__ static constexpr int bits(int) { return 3; }
+    __host__ __device__ static constexpr int byte_off(int) { return 0; }
+};
+
+__host__ __device__ constexpr bool lane_squarefree(int n)
+{
+    for (int p = 2; p * p <= n; p++)
+        if (n % (p * p) == 0) return false;
+    return true;
+}
+
+// Squarefree-first order of 0..127 (indices i with i+1 squarefree,
+// ascending, then the rest ascending): the table sp_mobius_mask_init
+// builds for every cache.
+struct LaneOrder { int v[kLN]; };
+__host__ __device__ constexpr LaneOrder lane_order()
+{
+    LaneOrder o{};
+    int k = 0;
+    for (int i = 0; i < kLN; i++)
+        if (lane_squarefree(i + 1)) o.v[k++] = i;
+    for (int i = 0; i < kLN; i++)
+        if (!lane_squarefree(i + 1)) o.v[k++] = i;
+    return o;
+}
+
+struct LaneArgs {
+    const void *in;            // [n_tokens][nh][128]
+    uint8_t *out_base;         // slab base
+    long long slot0;           // slot of head 0
+    long long slot_stride;     // bytes per slot
+    int n_tokens;
+    int nh;
+    int start_pos;
+    int n_batches;             // nh * ceil(n_tokens / 32)
+    float inv_sqrt_n;
+    unsigned int *status;      // bit 0: a bulk copy did not land in time
+};
+
+template <typename Tin, bool KS>
+struct LaneSmem {
+    static constexpr int RB = kLN * (int)sizeof(Tin);          // input row bytes
+    static constexpr int OB = 32 * LaneLayout<KS>::TB;         // packed rows of a batch
+    unsigned char in[kLaneWarps][32][RB];
+    unsigned char out[kLaneWarps][(OB + 15) & ~15];
+    unsigned long long bar[kLaneWarps];
+};
+
+__device__ __forceinline__ void bulk_s2g(void *dst, uint32_t src, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read()
+{
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all()
+{
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+template <typename Tin>
+__device__ __forceinline__ void lane_unpack16(const uint4 &w, float *x)
+{
+    if constexpr (sizeof(Tin) == 4) {
+        x[0] = __uint_as_float(w.x); x[1] = __uint_as_float(w.y);
+        x[2] = __uint_as_float(w.z); x[3] = __uint_as_float(w.w);
+    } else {
+        const Tin *h = reinterpret_cast<const Tin *>(&w);
+#pragma unroll
+        for (int i = 0; i < 8; i++) x[i] = sp_load_as_float(h, i);
+    }
+}
+
+template <typename Tin, bool KS>
+__global__ void __launch_bounds__(kLaneWarps * 32, kLaneMinBlocks)
+k_encode_lane(LaneArgs a)
+{
+    using L = LaneLayout<KS>;
+    using S = LaneSmem<Tin, KS>;
+    constexpr int RB = S::RB;
+    constexpr int C = RB / 16;                  // 16-byte chunks per input row
+    constexpr int TB = L::TB;
+    constexpr int W = (TB + 3) / 4;             // row words (the last may be partial)
+    constexpr int EPC = 16 / (int)sizeof(Tin);  // elements per chunk
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    S &sm = *reinterpret_cast<S *>(smem_raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rot = lane & 7;                   // chunk rotation of this lane's row
+    const uint32_t bar = spb::smem_u32(&sm.bar[warp]);
+    const uint32_t my_in = spb::smem_u32(&sm.in[warp][lane][0]);
+    const int gw = blockIdx.x * kLaneWarps + warp, n_w = gridDim.x * kLaneWarps;
+
+    uint64_t policy = 0;
+    if (lane == 0) {
+        spb::mbar_init(bar, 1);
+        spb::mbar_init_fence();
+    }
+    policy = spb::evict_first_policy();
+    __syncwarp();
+
+    // Batch g: head g % nh, positions 32 * (g / nh) ...; lane = position.
+    auto issue = [&](int g) {
+        const int h = g % a.nh, t = (g / a.nh) * 32 + lane;
+        const int live = min(32, a.n_tokens - (g / a.nh) * 32);
+        if (lane == 0) spb::mbar_expect_tx(bar, (uint32_t)(live * RB));
+        __syncwarp();
+        if (lane < live) {
+            const unsigned char *src =
+                reinterpret_cast<const unsigned char *>(a.in) + ((long long)t * a.nh + h) * RB;
+            // chunk j of the row lands at chunk (j - rot) mod C
+            spb::bulk_g2s(my_in, src + 16 * rot, (uint32_t)(RB - 16 * rot), bar, policy);
+            if (rot) spb::bulk_g2s(my_in + RB - 16 * rot, src, (uint32_t)(16 * rot), bar, policy);
+        }
+    };
+
+    uint32_t parity = 0;
+    if (gw < a.n_batches) issue(gw);
+    for (int g = gw; g < a.n_batches; g += n_w) {
+        const int h = g % a.nh, tb = g / a.nh;
+        const int live = min(32, a.n_tokens - tb * 32);
+        if (!spb::wait_stage(bar, parity, a.status)) {
+            spb::wait_stage(bar, parity, nullptr);   // the late copy, bounded, before the CTA exits
+            break;
+        }
+        parity ^= 1u;
+
+        // ---- row -> registers, then the next batch's copy -----------------
+        float x[kLN];
+#pragma unroll
+        for (int j = 0; j < C; j++) {
+            const uint4 w = *reinterpret_cast<const uint4 *>(&sm.in[warp][lane][((j - rot) & (C - 1)) * 16]);
+            lane_unpack16<Tin>(w, &x[j * EPC]);
+        }
+        __syncwarp();
+        spb::fence_proxy_async();
+        if (g + n_w < a.n_batches) issue(g + n_w);
+
+        // ---- VHT2: ascending butterfly lengths, then x * (1/sqrt(n)) -------
+#pragma unroll
+        for (int len = 1; len < kLN; len <<= 1) {
+#pragma unroll
+            for (int i = 0; i < kLN; i += len << 1) {
+#pragma unroll
+                for (int j = 0; j < len; j++) {
+                    const float u = x[i + j], v = x[i + j + len];
+                    x[i + j] = __fadd_rn(u, v);
+                    x[i + j + len] = __fsub_rn(u, v);
+                }
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < kLN; e++) x[e] = __fmul_rn(x[e], a.inv_sqrt_n);
+
+        // ---- bands: absmax, fp16 scale, codes, pack --------------------
+        constexpr LaneOrder ord = lane_order();
+        uint32_t row[W];
+#pragma unroll
+        for (int k = 0; k < W; k++) row[k] = 0u;
+#pragma unroll
+        for (int b = 0; b < L::NB; b++) {
+            const int bits = L::bits(b);
+            const int mv = (1 << (bits - 1)) - 1;
+            float amax = 0.0f;
+#pragma unroll
+            for (int k = 0; k < L::SIZE; k++) {
+                const int i = KS ? ord.v[b * L::SIZE + k] : k;
+                amax = fmaxf(amax, fabsf(x[i]));
+            }
+            const float scale = amax > 0.0f ? __fdiv_rn(amax, (float)mv) : 0.0f;
+            const __half hs = __float2half_rn(scale);
+            const float stored = __half2float(hs);
+            const float inv = stored > 0.0f ? __frcp_rn(stored) : 0.0f;
+            const int sbit = 8 * L::byte_off(b);
+            row[sbit >> 5] |= (uint32_t)__half_as_ushort(hs) << (sbit & 31);
+#pragma unroll
+            for (int k = 0; k < L::SIZE; k++) {
+                const int i = KS ? ord.v[b * L::SIZE + k] : k;
+                int q = __float2int_rn(__fmul_rn(x[i], inv));     // NaN -> 0, saturating
+                q = min(max(q, -mv), mv);
+                const uint32_t u = (uint32_t)(q + mv);
+                const int p = sbit + 16 + k * bits;
+                row[p >> 5] += u << (p & 31);
+                if ((p & 31) + bits > 32) row[(p >> 5) + 1] += u >> (32 - (p & 31));
+            }
+        }
+
+        // ---- stage the batch's rows, write them back ---------------------
+        if (lane == 0) bulk_wait_read();        // previous batch's store has read the stage
+        __syncwarp();
+        unsigned char *stage = sm.out[warp];
+        if constexpr ((TB & 3) == 0) {
+            uint32_t *r32 = reinterpret_cast<uint32_t *>(stage + lane * TB);
+#pragma unroll
+            for (int k = 0; k < W; k++) r32[k] = row[k];
+        } else {
+            uint16_t *r16 = reinterpret_cast<uint16_t *>(stage + lane * TB);
+#pragma unroll
+            for (int k = 0; k < TB / 2; k++) r16[k] = (uint16_t)(row[k >> 1] >> (16 * (k & 1)));
+        }
+        spb::fence_proxy_async();
+        __syncwarp();
+        uint8_t *dst = a.out_base + (a.slot0 + h) * a.slot_stride + (long long)(a.start_pos + tb * 32) * TB;
+        const uint32_t bytes = (uint32_t)(live * TB);
+        if ((((uintptr_t)dst | bytes) & 15) == 0) {
+            if (lane == 0) bulk_s2g(dst, spb::smem_u32(stage), bytes);
+        } else if ((((uintptr_t)dst | TB) & 3) == 0) {
+            const uint32_t *s32 = reinterpret_cast<const uint32_t *>(stage);
+            for (uint32_t i = lane; i < bytes / 4; i += 32) reinterpret_cast<uint32_t *>(dst)[i] = s32[i];
+        } else if ((((uintptr_t)dst | TB) & 1) == 0) {
+            const uint16_t *s16 = reinterpret_cast<const uint16_t *>(stage);
+            for (uint32_t i = lane; i < bytes / 2; i += 32) reinterpret_cast<uint16_t *>(dst)[i] = s16[i];
+        } else {
+            for (uint32_t i = lane; i < bytes; i += 32) dst[i] = stage[i];
+        }
+        __syncwarp();
+    }
+    if (lane == 0) bulk_wait_all();
+}
+
+template <typename Tin, bool KS>
+int launch_lane(const LaneArgs &a, cudaStream_t s)
+{
+    auto k = k_encode_lane<Tin, KS>;
+    const size_t smem = sizeof(LaneSmem<Tin, KS>);
+    static int occ = 0, sms = 0, dev_done = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev != dev_done) {
+        if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return sp_check_cuda(cudaGetLastError(), "lane encoder smem attribute");
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, kLaneWarps * 32, smem);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (occ < 1) occ = 1;
+        if (sms < 1) sms = 148;
+        dev_done = dev;
+    }
+    long long blocks = ((long long)a.n_batches + kLaneWarps - 1) / kLaneWarps;
+    if (blocks > (long long)sms * occ) blocks = (long long)sms * occ;
+    k<<<(unsigned)blocks, kLaneWarps * 32, smem, s>>>(a);
+    return sp_check_cuda(cudaGetLastError(), "lane encoder launch");
+}
+
+}  // namespace
+
+// Ship layouts at head_dim 128 with the standard squarefree-first order (K)
+// or no reorder (V): 1 if the lane-per-vector encoder takes the call.
+int sp_encode_lane_try(const void *d_in, int dtype, int n_tokens, int nh, uint8_t *d_out_base,
+                       long long slot0, long long slot_stride, int start_pos, bool std_order,
+                       const int *d_order, bool do_wht, const SpBandLayout &bl, unsigned int *d_status,
+                       cudaStream_t s, int *rc)
+{
+    if (!do_wht || bl.n != kLN || n_tokens <= 0 || nh <= 0) return 0;
+    if (getenv("SHANNON_PRIME_ENCODE_LANEGROUP")) return 0;
+    bool ks;
+    if (bl.n_bands == 4 && bl.total_bytes == 76 && d_order && std_order) {
+        for (int b = 0; b < 4; b++)
+            if (bl.off[b] != 32 * b || bl.size[b] != 32 || bl.bits[b] != LaneLayout<true>::bits(b) ||
+                bl.byte_off[b] != LaneLayout<true>::byte_off(b))
+                return 0;
+        ks = true;
+    } else if (bl.n_bands == 1 && bl.total_bytes == 50 && !d_order && bl.bits[0] == 3 && bl.size[0] == 128 &&
+               bl.byte_off[0] == 0) {
+        ks = false;
+    } else {
+        return 0;
+    }
+    if ((uintptr_t)d_in & 15) return 0;
+    if ((long long)nh * ((n_tokens + 31) / 32) > 0x7fffffffLL) return 0;
+    LaneArgs a;
+    a.in = d_in; a.out_base = d_out_base; a.slot0 = slot0; a.slot_stride = slot_stride;
+    a.n_tokens = n_tokens; a.nh = nh; a.start_pos = start_pos;
+    a.n_batches = nh * ((n_tokens + 31) / 32);
+    a.inv_sqrt_n = sp_inv_sqrt_n(kLN);
+    a.status = d_status;
+    switch (dtype) {
+    case SP_DTYPE_F32:  *rc = ks ? launch_lane<float, true>(a, s) : launch_lane<float, false>(a, s); return 1;
+    case SP_DTYPE_F16:  *rc = ks ? launch_lane<__half, true>(a, s) : launch_lane<__half, false>(a, s); return 1;
+    case SP_DTYPE_BF16: *rc = ks ? launch_lane<__nv_bfloat16, true>(a, s) : launch_lane<__nv_bfloat16, false>(a, s); return 1;
+    default: return 0;
+    }
+}

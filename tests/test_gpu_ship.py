@@ -193,3 +193,33 @@ def test_argument_errors(cuda):
     cfg = spb200.make_config(96, 1, 1)
     bad = spb200.SpCudaCache()
     assert L.sp_cuda_cache_init(C.byref(bad), C.byref(cfg), 16, None) == spb200.SP_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("start,T,dt", [(3, 77, "float32"), (8, 64, "float32"), (0, 33, "bfloat16"),
+                                        (5, 100, "float16")])
+def test_ship_lane_encoder_ragged(cuda, monkeypatch, start, T, dt):
+    """The lane-per-vector ship encoder (head_dim 128) at unaligned start
+    positions and partial 32-position batches: codes bit-exact with the
+    oracle and with the lane-group encoder (SHANNON_PRIME_ENCODE_LANEGROUP)."""
+    torch = _torch()
+    H, n = 3, 128
+    k, v = _layer_inputs(21, H, T, n, sigma=1.0)
+    tk = torch.from_numpy(k).to(getattr(torch, dt)).cuda()
+    tv = torch.from_numpy(v).to(getattr(torch, dt)).cuda()
+    slabs = []
+    for lanegroup in (False, True):
+        if lanegroup:
+            monkeypatch.setenv("SHANNON_PRIME_ENCODE_LANEGROUP", "1")
+        cache = spb200.Cache(n, 2, H, 112)
+        cache.write_kv_tokens(1, start, tk, tv)
+        torch.cuda.synchronize()
+        slabs.append((cache.slab(0).cpu().numpy(), cache.slab(1).cpu().numpy()))
+        monkeypatch.delenv("SHANNON_PRIME_ENCODE_LANEGROUP", raising=False)
+    (kl, vl), (kg, vg) = slabs
+    assert np.array_equal(kl, kg) and np.array_equal(vl, vg)
+    k32, v32 = tk.float().cpu().numpy(), tv.float().cpu().numpy()
+    for h in range(H):
+        assert np.array_equal(kl[H + h, start:start + T], O.ship_write(k32[:, h], KB, True))
+        assert np.array_equal(vl[H + h, start:start + T], O.ship_write(v32[:, h], VB, False))
+        assert not kl[H + h, :start].any() and not kl[H + h, start + T:].any()
+        assert not vl[H + h, :start].any() and not vl[H + h, start + T:].any()
