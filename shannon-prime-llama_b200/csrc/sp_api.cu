@@ -203,6 +203,18 @@ extern "C" int sp_cuda_write_kv_tokens(sp_cuda_cache_t *cc, int layer, int start
     int rc = check_pos(cc, layer, 0, start_pos, n_tokens);
     if (rc) return rc;
     const int H = cc->config.n_heads_kv;
+    // Both halves in one launch when the lane encoder takes them.
+    if (d_k && d_v && n_tokens > 0) {
+        const SpBandLayout kbl = sp_layout_from(cc->k_bands), vbl = sp_layout_from(cc->v_bands);
+        const long long slot0 = (long long)layer * H;
+        if (sp_encode_lane_kv(d_k, d_v, dtype, n_tokens, H, start_pos, (uint8_t *)cc->d_k_cache, slot0,
+                              (long long)cc->max_seq_len * cc->k_bands.total_bytes, kbl,
+                              cc->config.use_mobius_mask ? cc->d_mobius_order : nullptr, true,
+                              (uint8_t *)cc->d_v_cache, slot0,
+                              (long long)cc->max_seq_len * cc->v_bands.total_bytes, vbl, cc->d_status,
+                              (cudaStream_t)cc->stream, &rc))
+            return rc;
+    }
     if (d_k && (rc = write_one_half(cc, 0, layer, 0, H, start_pos, n_tokens, d_k, dtype))) return rc;
     if (d_v && (rc = write_one_half(cc, 1, layer, 0, H, start_pos, n_tokens, d_v, dtype))) return rc;
     return SP_OK;

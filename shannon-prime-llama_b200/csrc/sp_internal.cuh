@@ -44,6 +44,13 @@ int sp_encode_lane_try(const void *d_in, int dtype, int n_tokens, int nh, uint8_
                        long long slot0, long long slot_stride, int start_pos, bool std_order,
                        const int *d_order, bool do_wht, const SpBandLayout &bl, unsigned int *d_status,
                        cudaStream_t s, int *rc);
+// Both halves of one layer's tokens in one lane-encoder launch (null input =
+// half skipped); 0 when the layouts or inputs do not qualify.
+int sp_encode_lane_kv(const void *d_k, const void *d_v, int dtype, int n_tokens, int nh, int start_pos,
+                      uint8_t *k_base, long long k_slot0, long long k_slot_stride, const SpBandLayout &kbl,
+                      const int *d_order, bool std_order,
+                      uint8_t *v_base, long long v_slot0, long long v_slot_stride, const SpBandLayout &vbl,
+                      unsigned int *d_status, cudaStream_t s, int *rc);
 int sp_launch_decode(const uint8_t *d_in_base, long long slot, long long slot_stride_bytes,
                      int start_pos, int n_pos, float *d_out, const int *d_order,
                      bool do_wht, int max_bands, const SpBandLayout &bl, cudaStream_t s);

@@ -76,25 +76,33 @@ __host__ __device__ constexpr LaneOrder lane_order()
     return o;
 }
 
-struct LaneArgs {
+struct LaneHalf {
     const void *in;            // [n_tokens][nh][128]
     uint8_t *out_base;         // slab base
     long long slot0;           // slot of head 0
     long long slot_stride;     // bytes per slot
+};
+
+// One launch encodes the K half (half 0, K layout) and/or the V half
+// (half 1, V layout) of the same tokens.
+struct LaneArgs {
+    LaneHalf half[2];
+    int first;                 // first half present (0 = K, 1 = V)
+    int n_halves;              // 1 or 2
     int n_tokens;
     int nh;
     int start_pos;
-    int n_batches;             // nh * ceil(n_tokens / 32)
+    int nb;                    // batches per half: nh * ceil(n_tokens / 32)
     float inv_sqrt_n;
     unsigned int *status;      // bit 0: a bulk copy did not land in time
 };
 
-template <typename Tin, bool KS>
+template <typename Tin>
 struct LaneSmem {
     static constexpr int RB = kLN * (int)sizeof(Tin);          // input row bytes
-    static constexpr int OB = 32 * LaneLayout<KS>::TB;         // packed rows of a batch
+    static constexpr int OB = 32 * 76;                         // packed rows of a batch (K is the larger)
     unsigned char in[kLaneWarps][32][RB];
-    unsigned char out[kLaneWarps][(OB + 15) & ~15];
+    unsigned char out[kLaneWarps][OB];
     unsigned long long bar[kLaneWarps];
 };
 
@@ -126,16 +134,83 @@ __device__ __forceinline__ void lane_unpack16(const uint4 &w, float *x)
     }
 }
 
-template <typename Tin, bool KS>
+// Quantise and pack the lane's transformed vector into its row, stage the
+// warp's 32 rows in shared memory and write them back (one bulk store when
+// the batch's rows are 16-byte aligned in the slot, else plain stores).
+template <bool KS>
+__device__ __forceinline__ void lane_pack_store(const float (&x)[kLN], unsigned char *stage, uint8_t *dst,
+                                                int live, int lane)
+{
+    using L = LaneLayout<KS>;
+    constexpr int TB = L::TB;
+    constexpr int W = (TB + 3) / 4;             // row words (the last may be partial)
+    constexpr LaneOrder ord = lane_order();
+    uint32_t row[W];
+#pragma unroll
+    for (int k = 0; k < W; k++) row[k] = 0u;
+#pragma unroll
+    for (int b = 0; b < L::NB; b++) {
+        const int bits = L::bits(b);
+        const int mv = (1 << (bits - 1)) - 1;
+        float amax = 0.0f;
+#pragma unroll
+        for (int k = 0; k < L::SIZE; k++) {
+            const int i = KS ? ord.v[b * L::SIZE + k] : k;
+            amax = fmaxf(amax, fabsf(x[i]));
+        }
+        const float scale = amax > 0.0f ? __fdiv_rn(amax, (float)mv) : 0.0f;
+        const __half hs = __float2half_rn(scale);
+        const float stored = __half2float(hs);
+        const float inv = stored > 0.0f ? __frcp_rn(stored) : 0.0f;
+        const int sbit = 8 * L::byte_off(b);
+        row[sbit >> 5] |= (uint32_t)__half_as_ushort(hs) << (sbit & 31);
+#pragma unroll
+        for (int k = 0; k < L::SIZE; k++) {
+            const int i = KS ? ord.v[b * L::SIZE + k] : k;
+            int q = __float2int_rn(__fmul_rn(x[i], inv));     // NaN -> 0, saturating
+            q = min(max(q, -mv), mv);
+            const uint32_t u = (uint32_t)(q + mv);
+            const int p = sbit + 16 + k * bits;
+            row[p >> 5] += u << (p & 31);
+            if ((p & 31) + bits > 32) row[(p >> 5) + 1] += u >> (32 - (p & 31));
+        }
+    }
+
+    if (lane == 0) bulk_wait_read();            // the previous batch's store has read the stage
+    __syncwarp();
+    if constexpr ((TB & 3) == 0) {
+        uint32_t *r32 = reinterpret_cast<uint32_t *>(stage + lane * TB);
+#pragma unroll
+        for (int k = 0; k < W; k++) r32[k] = row[k];
+    } else {
+        uint16_t *r16 = reinterpret_cast<uint16_t *>(stage + lane * TB);
+#pragma unroll
+        for (int k = 0; k < TB / 2; k++) r16[k] = (uint16_t)(row[k >> 1] >> (16 * (k & 1)));
+    }
+    spb::fence_proxy_async();
+    __syncwarp();
+    const uint32_t bytes = (uint32_t)(live * TB);
+    if ((((uintptr_t)dst | bytes) & 15) == 0) {
+        if (lane == 0) bulk_s2g(dst, spb::smem_u32(stage), bytes);
+    } else if ((((uintptr_t)dst | TB) & 3) == 0) {
+        const uint32_t *s32 = reinterpret_cast<const uint32_t *>(stage);
+        for (uint32_t i = lane; i < bytes / 4; i += 32) reinterpret_cast<uint32_t *>(dst)[i] = s32[i];
+    } else if ((((uintptr_t)dst | TB) & 1) == 0) {
+        const uint16_t *s16 = reinterpret_cast<const uint16_t *>(stage);
+        for (uint32_t i = lane; i < bytes / 2; i += 32) reinterpret_cast<uint16_t *>(dst)[i] = s16[i];
+    } else {
+        for (uint32_t i = lane; i < bytes; i += 32) dst[i] = stage[i];
+    }
+    __syncwarp();
+}
+
+template <typename Tin>
 __global__ void __launch_bounds__(kLaneWarps * 32, kLaneMinBlocks)
 k_encode_lane(LaneArgs a)
 {
-    using L = LaneLayout<KS>;
-    using S = LaneSmem<Tin, KS>;
+    using S = LaneSmem<Tin>;
     constexpr int RB = S::RB;
     constexpr int C = RB / 16;                  // 16-byte chunks per input row
-    constexpr int TB = L::TB;
-    constexpr int W = (TB + 3) / 4;             // row words (the last may be partial)
     constexpr int EPC = 16 / (int)sizeof(Tin);  // elements per chunk
     extern __shared__ __align__(128) unsigned char smem_raw[];
     S &sm = *reinterpret_cast<S *>(smem_raw);
@@ -144,24 +219,26 @@ k_encode_lane(LaneArgs a)
     const uint32_t bar = spb::smem_u32(&sm.bar[warp]);
     const uint32_t my_in = spb::smem_u32(&sm.in[warp][lane][0]);
     const int gw = blockIdx.x * kLaneWarps + warp, n_w = gridDim.x * kLaneWarps;
+    const int n_total = a.nb * a.n_halves;
 
-    uint64_t policy = 0;
     if (lane == 0) {
         spb::mbar_init(bar, 1);
         spb::mbar_init_fence();
     }
-    policy = spb::evict_first_policy();
+    const uint64_t policy = spb::evict_first_policy();
     __syncwarp();
 
-    // Batch g: head g % nh, positions 32 * (g / nh) ...; lane = position.
+    // Batch g: half first + g / nb; within it head gl % nh, positions
+    // 32 * (gl / nh) ...; lane = position.
     auto issue = [&](int g) {
-        const int h = g % a.nh, t = (g / a.nh) * 32 + lane;
-        const int live = min(32, a.n_tokens - (g / a.nh) * 32);
+        const int hx = a.first + g / a.nb, gl = g % a.nb;
+        const int h = gl % a.nh, t0 = (gl / a.nh) * 32;
+        const int live = min(32, a.n_tokens - t0);
         if (lane == 0) spb::mbar_expect_tx(bar, (uint32_t)(live * RB));
         __syncwarp();
         if (lane < live) {
-            const unsigned char *src =
-                reinterpret_cast<const unsigned char *>(a.in) + ((long long)t * a.nh + h) * RB;
+            const unsigned char *src = reinterpret_cast<const unsigned char *>(hx ? a.half[1].in : a.half[0].in) +
+                                       ((long long)(t0 + lane) * a.nh + h) * RB;
             // chunk j of the row lands at chunk (j - rot) mod C
             spb::bulk_g2s(my_in, src + 16 * rot, (uint32_t)(RB - 16 * rot), bar, policy);
             if (rot) spb::bulk_g2s(my_in + RB - 16 * rot, src, (uint32_t)(16 * rot), bar, policy);
@@ -169,10 +246,11 @@ k_encode_lane(LaneArgs a)
     };
 
     uint32_t parity = 0;
-    if (gw < a.n_batches) issue(gw);
-    for (int g = gw; g < a.n_batches; g += n_w) {
-        const int h = g % a.nh, tb = g / a.nh;
-        const int live = min(32, a.n_tokens - tb * 32);
+    if (gw < n_total) issue(gw);
+    for (int g = gw; g < n_total; g += n_w) {
+        const int hx = a.first + g / a.nb, gl = g % a.nb;
+        const int h = gl % a.nh, t0 = (gl / a.nh) * 32;
+        const int live = min(32, a.n_tokens - t0);
         if (!spb::wait_stage(bar, parity, a.status)) {
             spb::wait_stage(bar, parity, nullptr);   // the late copy, bounded, before the CTA exits
             break;
@@ -188,7 +266,7 @@ k_encode_lane(LaneArgs a)
         }
         __syncwarp();
         spb::fence_proxy_async();
-        if (g + n_w < a.n_batches) issue(g + n_w);
+        if (g + n_w < n_total) issue(g + n_w);
 
         // ---- VHT2: ascending butterfly lengths, then x * (1/sqrt(n)) -------
 #pragma unroll
@@ -206,77 +284,20 @@ k_encode_lane(LaneArgs a)
 #pragma unroll
         for (int e = 0; e < kLN; e++) x[e] = __fmul_rn(x[e], a.inv_sqrt_n);
 
-        // ---- bands: absmax, fp16 scale, codes, pack --------------------
-        constexpr LaneOrder ord = lane_order();
-        uint32_t row[W];
-#pragma unroll
-        for (int k = 0; k < W; k++) row[k] = 0u;
-#pragma unroll
-        for (int b = 0; b < L::NB; b++) {
-            const int bits = L::bits(b);
-            const int mv = (1 << (bits - 1)) - 1;
-            float amax = 0.0f;
-#pragma unroll
-            for (int k = 0; k < L::SIZE; k++) {
-                const int i = KS ? ord.v[b * L::SIZE + k] : k;
-                amax = fmaxf(amax, fabsf(x[i]));
-            }
-            const float scale = amax > 0.0f ? __fdiv_rn(amax, (float)mv) : 0.0f;
-            const __half hs = __float2half_rn(scale);
-            const float stored = __half2float(hs);
-            const float inv = stored > 0.0f ? __frcp_rn(stored) : 0.0f;
-            const int sbit = 8 * L::byte_off(b);
-            row[sbit >> 5] |= (uint32_t)__half_as_ushort(hs) << (sbit & 31);
-#pragma unroll
-            for (int k = 0; k < L::SIZE; k++) {
-                const int i = KS ? ord.v[b * L::SIZE + k] : k;
-                int q = __float2int_rn(__fmul_rn(x[i], inv));     // NaN -> 0, saturating
-                q = min(max(q, -mv), mv);
-                const uint32_t u = (uint32_t)(q + mv);
-                const int p = sbit + 16 + k * bits;
-                row[p >> 5] += u << (p & 31);
-                if ((p & 31) + bits > 32) row[(p >> 5) + 1] += u >> (32 - (p & 31));
-            }
-        }
-
-        // ---- stage the batch's rows, write them back ---------------------
-        if (lane == 0) bulk_wait_read();        // previous batch's store has read the stage
-        __syncwarp();
-        unsigned char *stage = sm.out[warp];
-        if constexpr ((TB & 3) == 0) {
-            uint32_t *r32 = reinterpret_cast<uint32_t *>(stage + lane * TB);
-#pragma unroll
-            for (int k = 0; k < W; k++) r32[k] = row[k];
-        } else {
-            uint16_t *r16 = reinterpret_cast<uint16_t *>(stage + lane * TB);
-#pragma unroll
-            for (int k = 0; k < TB / 2; k++) r16[k] = (uint16_t)(row[k >> 1] >> (16 * (k & 1)));
-        }
-        spb::fence_proxy_async();
-        __syncwarp();
-        uint8_t *dst = a.out_base + (a.slot0 + h) * a.slot_stride + (long long)(a.start_pos + tb * 32) * TB;
-        const uint32_t bytes = (uint32_t)(live * TB);
-        if ((((uintptr_t)dst | bytes) & 15) == 0) {
-            if (lane == 0) bulk_s2g(dst, spb::smem_u32(stage), bytes);
-        } else if ((((uintptr_t)dst | TB) & 3) == 0) {
-            const uint32_t *s32 = reinterpret_cast<const uint32_t *>(stage);
-            for (uint32_t i = lane; i < bytes / 4; i += 32) reinterpret_cast<uint32_t *>(dst)[i] = s32[i];
-        } else if ((((uintptr_t)dst | TB) & 1) == 0) {
-            const uint16_t *s16 = reinterpret_cast<const uint16_t *>(stage);
-            for (uint32_t i = lane; i < bytes / 2; i += 32) reinterpret_cast<uint16_t *>(dst)[i] = s16[i];
-        } else {
-            for (uint32_t i = lane; i < bytes; i += 32) dst[i] = stage[i];
-        }
-        __syncwarp();
+        const LaneHalf &hf = hx ? a.half[1] : a.half[0];
+        uint8_t *dst = hf.out_base + (hf.slot0 + h) * hf.slot_stride +
+                       (long long)(a.start_pos + t0) * (hx ? LaneLayout<false>::TB : LaneLayout<true>::TB);
+        if (hx == 0) lane_pack_store<true>(x, sm.out[warp], dst, live, lane);
+        else lane_pack_store<false>(x, sm.out[warp], dst, live, lane);
     }
     if (lane == 0) bulk_wait_all();
 }
 
-template <typename Tin, bool KS>
+template <typename Tin>
 int launch_lane(const LaneArgs &a, cudaStream_t s)
 {
-    auto k = k_encode_lane<Tin, KS>;
-    const size_t smem = sizeof(LaneSmem<Tin, KS>);
+    auto k = k_encode_lane<Tin>;
+    const size_t smem = sizeof(LaneSmem<Tin>);
     static int occ = 0, sms = 0, dev_done = -1;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -289,48 +310,78 @@ int launch_lane(const LaneArgs &a, cudaStream_t s)
         if (sms < 1) sms = 148;
         dev_done = dev;
     }
-    long long blocks = ((long long)a.n_batches + kLaneWarps - 1) / kLaneWarps;
+    long long blocks = ((long long)a.nb * a.n_halves + kLaneWarps - 1) / kLaneWarps;
     if (blocks > (long long)sms * occ) blocks = (long long)sms * occ;
     k<<<(unsigned)blocks, kLaneWarps * 32, smem, s>>>(a);
     return sp_check_cuda(cudaGetLastError(), "lane encoder launch");
 }
 
+// Which half a layout is for the lane encoder: 0 = K ship layout with the
+// standard order, 1 = V ship layout without reorder, -1 = not eligible.
+int lane_half_of(const SpBandLayout &bl, const int *d_order, bool std_order)
+{
+    if (bl.n != kLN) return -1;
+    if (bl.n_bands == 4 && bl.total_bytes == 76 && d_order && std_order) {
+        for (int b = 0; b < 4; b++)
+            if (bl.off[b] != 32 * b || bl.size[b] != 32 || bl.bits[b] != LaneLayout<true>::bits(b) ||
+                bl.byte_off[b] != LaneLayout<true>::byte_off(b))
+                return -1;
+        return 0;
+    }
+    if (bl.n_bands == 1 && bl.total_bytes == 50 && !d_order && bl.bits[0] == 3 && bl.size[0] == 128 &&
+        bl.byte_off[0] == 0)
+        return 1;
+    return -1;
+}
+
 }  // namespace
 
-// Ship layouts at head_dim 128 with the standard squarefree-first order (K)
-// or no reorder (V): 1 if the lane-per-vector encoder takes the call.
+// Lane-per-vector encode of the K and/or V half of n_tokens tokens
+// ([n_tokens][nh][128] inputs; a null input skips its half).  Returns 1 and
+// sets *rc when it takes the call: both present halves must have the ship
+// layouts at head_dim 128 (K with the standard squarefree-first order) and
+// 16-byte aligned inputs.  Otherwise 0 (nothing launched).
+int sp_encode_lane_kv(const void *d_k, const void *d_v, int dtype, int n_tokens, int nh, int start_pos,
+                      uint8_t *k_base, long long k_slot0, long long k_slot_stride, const SpBandLayout &kbl,
+                      const int *d_order, bool std_order,
+                      uint8_t *v_base, long long v_slot0, long long v_slot_stride, const SpBandLayout &vbl,
+                      unsigned int *d_status, cudaStream_t s, int *rc)
+{
+    if (n_tokens <= 0 || nh <= 0 || (!d_k && !d_v)) return 0;
+    if (getenv("SHANNON_PRIME_ENCODE_LANEGROUP")) return 0;
+    if (d_k && (lane_half_of(kbl, d_order, std_order) != 0 || ((uintptr_t)d_k & 15))) return 0;
+    if (d_v && (lane_half_of(vbl, nullptr, false) != 1 || ((uintptr_t)d_v & 15))) return 0;
+    if (dtype != SP_DTYPE_F32 && dtype != SP_DTYPE_F16 && dtype != SP_DTYPE_BF16) return 0;
+    if (2LL * nh * ((n_tokens + 31) / 32) > 0x7fffffffLL) return 0;
+    LaneArgs a;
+    a.half[0] = LaneHalf{d_k, k_base, k_slot0, k_slot_stride};
+    a.half[1] = LaneHalf{d_v, v_base, v_slot0, v_slot_stride};
+    a.first = d_k ? 0 : 1;
+    a.n_halves = (d_k && d_v) ? 2 : 1;
+    a.n_tokens = n_tokens; a.nh = nh; a.start_pos = start_pos;
+    a.nb = nh * ((n_tokens + 31) / 32);
+    a.inv_sqrt_n = sp_inv_sqrt_n(kLN);
+    a.status = d_status;
+    switch (dtype) {
+    case SP_DTYPE_F32:  *rc = launch_lane<float>(a, s); break;
+    case SP_DTYPE_F16:  *rc = launch_lane<__half>(a, s); break;
+    default:            *rc = launch_lane<__nv_bfloat16>(a, s); break;
+    }
+    return 1;
+}
+
+// One half through the lane encoder (the sp_launch_encode hook).
 int sp_encode_lane_try(const void *d_in, int dtype, int n_tokens, int nh, uint8_t *d_out_base,
                        long long slot0, long long slot_stride, int start_pos, bool std_order,
                        const int *d_order, bool do_wht, const SpBandLayout &bl, unsigned int *d_status,
                        cudaStream_t s, int *rc)
 {
-    if (!do_wht || bl.n != kLN || n_tokens <= 0 || nh <= 0) return 0;
-    if (getenv("SHANNON_PRIME_ENCODE_LANEGROUP")) return 0;
-    bool ks;
-    if (bl.n_bands == 4 && bl.total_bytes == 76 && d_order && std_order) {
-        for (int b = 0; b < 4; b++)
-            if (bl.off[b] != 32 * b || bl.size[b] != 32 || bl.bits[b] != LaneLayout<true>::bits(b) ||
-                bl.byte_off[b] != LaneLayout<true>::byte_off(b))
-                return 0;
-        ks = true;
-    } else if (bl.n_bands == 1 && bl.total_bytes == 50 && !d_order && bl.bits[0] == 3 && bl.size[0] == 128 &&
-               bl.byte_off[0] == 0) {
-        ks = false;
-    } else {
-        return 0;
-    }
-    if ((uintptr_t)d_in & 15) return 0;
-    if ((long long)nh * ((n_tokens + 31) / 32) > 0x7fffffffLL) return 0;
-    LaneArgs a;
-    a.in = d_in; a.out_base = d_out_base; a.slot0 = slot0; a.slot_stride = slot_stride;
-    a.n_tokens = n_tokens; a.nh = nh; a.start_pos = start_pos;
-    a.n_batches = nh * ((n_tokens + 31) / 32);
-    a.inv_sqrt_n = sp_inv_sqrt_n(kLN);
-    a.status = d_status;
-    switch (dtype) {
-    case SP_DTYPE_F32:  *rc = ks ? launch_lane<float, true>(a, s) : launch_lane<float, false>(a, s); return 1;
-    case SP_DTYPE_F16:  *rc = ks ? launch_lane<__half, true>(a, s) : launch_lane<__half, false>(a, s); return 1;
-    case SP_DTYPE_BF16: *rc = ks ? launch_lane<__nv_bfloat16, true>(a, s) : launch_lane<__nv_bfloat16, false>(a, s); return 1;
-    default: return 0;
-    }
+    if (!do_wht) return 0;
+    const int hx = lane_half_of(bl, d_order, std_order);
+    if (hx < 0) return 0;
+    if (hx == 0)
+        return sp_encode_lane_kv(d_in, nullptr, dtype, n_tokens, nh, start_pos, d_out_base, slot0, slot_stride, bl,
+                                 d_order, std_order, nullptr, 0, 0, bl, d_status, s, rc);
+    return sp_encode_lane_kv(nullptr, d_in, dtype, n_tokens, nh, start_pos, nullptr, 0, 0, bl, nullptr, false,
+                             d_out_base, slot0, slot_stride, bl, d_status, s, rc);
 }
