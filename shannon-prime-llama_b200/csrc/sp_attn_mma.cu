@@ -403,49 +403,56 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
                 const unsigned short vb = *reinterpret_cast<const unsigned short *>(kt + kKTile + 50 * t);
                 sm.scl[warp][st][t][4] = __low2float(finite_or_zero(__half2half2(__ushort_as_half(vb))));
             }
-            uint32_t AK[2][16];
-#pragma unroll
-            for (int hh = 0; hh < 2; hh++) {
-                const uint32_t *row = K32 + 19 * (r + 8 * hh);
-#pragma unroll
-                for (int b = 0; b < 2; b++) {
-                    const uint32_t w0 = row[kw[b]], w1 = row[kw[b] + 1];
-                    const uint32_t xl = shf(w0, w1, ks[b]), xh = w1 >> ks[b];
-                    AK[hh][4 * b + 0] = xl & 0x01F0001Fu;
-                    AK[hh][4 * b + 1] = shf(xl, xh, 5) & 0x01F0001Fu;
-                    AK[hh][4 * b + 2] = shf(xl, xh, 10) & 0x01F0001Fu;
-                    AK[hh][4 * b + 3] = shf(xl, xh, 15) & 0x01F0001Fu;
-                }
-                {
-                    const uint32_t x = shf(row[kw[2]], row[kw[2] + 1], 16);
-                    const uint32_t y = x >> 8;
-                    AK[hh][8] = x & 0x000F000Fu;
-                    AK[hh][9] = x & 0x00F000F0u;
-                    AK[hh][10] = y & 0x000F000Fu;
-                    AK[hh][11] = y & 0x00F000F0u;
-                }
-                {
-                    const uint32_t x = shf(row[kw[3]], row[kw[3] + 1], ks[3]);
-                    const uint32_t y = x << 4, z = x >> 2;
-                    AK[hh][12] = y & 0x00070070u;
-                    AK[hh][13] = y & 0x00380380u;
-                    AK[hh][14] = z & 0x00070070u;
-                    AK[hh][15] = z & 0x00380380u;
-                }
-            }
             // Band dot products; the accumulator starts at -m_b * sum(q') in
             // its hi column, so acc_hi + acc_lo = sum_i (u_i - m_b) q'_i / kc.
+            // Each MMA's A quad is unpacked right before it, so the four
+            // registers can be allocated as the operand tuple directly.
             float acc[NT][4][4];
 #pragma unroll
             for (int nt = 0; nt < NT; nt++)
 #pragma unroll
                 for (int b = 0; b < 4; b++) {
                     acc[nt][b][0] = cinit[nt][b]; acc[nt][b][1] = 0.0f; acc[nt][b][2] = cinit[nt][b]; acc[nt][b][3] = 0.0f;
-#pragma unroll
-                    for (int j = 0; j < 2; j++)
-                        mma16816(acc[nt][b], AK[0][4 * b + 2 * j], AK[1][4 * b + 2 * j], AK[0][4 * b + 2 * j + 1],
-                                 AK[1][4 * b + 2 * j + 1], bq[nt][2 * b + j][0], bq[nt][2 * b + j][1]);
                 }
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                // band window of rows r and r+8: x (low), y (high / shifted)
+                uint32_t wx[2], wy[2];
+#pragma unroll
+                for (int hh = 0; hh < 2; hh++) {
+                    const uint32_t *row = K32 + 19 * (r + 8 * hh);
+                    if (b < 2) {
+                        const uint32_t w0 = row[kw[b]], w1 = row[kw[b] + 1];
+                        wx[hh] = shf(w0, w1, ks[b]);
+                        wy[hh] = w1 >> ks[b];
+                    } else if (b == 2) {
+                        wx[hh] = shf(row[kw[2]], row[kw[2] + 1], 16);
+                        wy[hh] = wx[hh] >> 8;
+                    } else {
+                        const uint32_t x = shf(row[kw[3]], row[kw[3] + 1], ks[3]);
+                        wx[hh] = x << 4;
+                        wy[hh] = x >> 2;
+                    }
+                }
+                auto code = [&](int hh, int i) -> uint32_t {
+                    if (b < 2) {
+                        const uint32_t v = i == 0 ? wx[hh] : shf(wx[hh], wy[hh], 5 * i);
+                        return v & 0x01F0001Fu;
+                    } else if (b == 2) {
+                        return (i < 2 ? wx[hh] : wy[hh]) & ((i & 1) ? 0x00F000F0u : 0x000F000Fu);
+                    } else {
+                        return (i < 2 ? wx[hh] : wy[hh]) & ((i & 1) ? 0x00380380u : 0x00070070u);
+                    }
+                };
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    const uint32_t a0 = code(0, 2 * j), a1 = code(1, 2 * j), a2 = code(0, 2 * j + 1),
+                                   a3 = code(1, 2 * j + 1);
+#pragma unroll
+                    for (int nt = 0; nt < NT; nt++)
+                        mma16816(acc[nt][b], a0, a1, a2, a3, bq[nt][2 * b + j][0], bq[nt][2 * b + j][1]);
+                }
+            }
             __syncwarp();
             float4 fs[2];
 #pragma unroll
@@ -493,34 +500,38 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
         auto v_step = [&](int st, const float (&su)[NT][2]) {
             const unsigned char *kt = sm.ring[warp][st];
             const uint32_t *V32 = reinterpret_cast<const uint32_t *>(kt + kKTile);
-            uint32_t AV[2][16];
+            // 16-bit windows of the two position rows, interleaved per half:
+            // W[hh][wi] holds 5 codes of each row (the last one code).
+            uint32_t W[2][4];
 #pragma unroll
             for (int hh = 0; hh < 2; hh++) {
                 const uint32_t *pr = V32 + 25 * (c + 4 * hh);
                 const uint32_t a0 = pr[vwA], a1 = pr[vwA + 1], b0 = pr[vwB], b1 = pr[vwB + 1];
                 const uint32_t xal = shf(a0, a1, vsA), xah = a1 >> vsA;
                 const uint32_t xbl = shf(b0, b1, vsB), xbh = b1 >> vsB;
-                uint32_t W[4];
-                W[0] = __byte_perm(xal, xbl, 0x5410);
-                W[1] = __byte_perm(shf(xal, xah, 15), shf(xbl, xbh, 15), 0x5410);
-                W[2] = __byte_perm(shf(xal, xah, 30), shf(xbl, xbh, 30), 0x5410);
-                W[3] = __byte_perm(xah, xbh, 0x5410) >> 9;
-                // every code lands at bit 4 or above of its half: the tensor
-                // cores lose precision on the smallest subnormals (d < 4)
-#pragma unroll
-                for (int wi = 0; wi < 3; wi++) {
-                    const uint32_t l4 = W[wi] << 4, r5 = W[wi] >> 5;
-                    AV[hh][5 * wi + 0] = l4 & 0x00700070u;
-                    AV[hh][5 * wi + 1] = l4 & 0x03800380u;
-                    AV[hh][5 * wi + 2] = W[wi] & 0x01C001C0u;
-                    AV[hh][5 * wi + 3] = r5 & 0x00700070u;
-                    AV[hh][5 * wi + 4] = r5 & 0x03800380u;
-                }
-                AV[hh][15] = W[3] & 0x00700070u;
+                W[hh][0] = __byte_perm(xal, xbl, 0x5410);
+                W[hh][1] = __byte_perm(shf(xal, xah, 15), shf(xbl, xbh, 15), 0x5410);
+                W[hh][2] = __byte_perm(shf(xal, xah, 30), shf(xbl, xbh, 30), 0x5410);
+                W[hh][3] = __byte_perm(xah, xbh, 0x5410) >> 9;
             }
+            // Register j of the chunk: every code lands at bit 4 or above of
+            // its half (the tensor cores lose precision on the smallest
+            // subnormals, d < 4).
+            auto vreg = [&](int hh, int j) -> uint32_t {
+                if (j == 15) return W[hh][3] & 0x00700070u;
+                const uint32_t w = W[hh][j / 5];
+                switch (j % 5) {
+                case 0: return (w << 4) & 0x00700070u;
+                case 1: return (w << 4) & 0x03800380u;
+                case 2: return w & 0x01C001C0u;
+                case 3: return (w >> 5) & 0x00700070u;
+                default: return (w >> 5) & 0x03800380u;
+                }
+            };
             float vscale[2];
 #pragma unroll
             for (int hh = 0; hh < 2; hh++) vscale[hh] = sm.scl[warp][st][r + 8 * hh][4];
+            uint32_t pb[NT][2];
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
                 float pv[2];
@@ -546,10 +557,15 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
                 const uint32_t x1 = __shfl_sync(0xffffffffu, pk0, src1);
                 const uint32_t x2 = __shfl_sync(0xffffffffu, pk1, src0);
                 const uint32_t x3 = __shfl_sync(0xffffffffu, pk1, src1);
-                const uint32_t pb0 = __byte_perm(x0, x1, psel), pb1 = __byte_perm(x2, x3, psel);
+                pb[nt][0] = __byte_perm(x0, x1, psel);
+                pb[nt][1] = __byte_perm(x2, x3, psel);
+            }
 #pragma unroll
-                for (int mt = 0; mt < 8; mt++)
-                    mma16816(oacc[nt][mt], AV[0][2 * mt], AV[0][2 * mt + 1], AV[1][2 * mt], AV[1][2 * mt + 1], pb0, pb1);
+            for (int mt = 0; mt < 8; mt++) {
+                const uint32_t a0 = vreg(0, 2 * mt), a1 = vreg(0, 2 * mt + 1), a2 = vreg(1, 2 * mt),
+                               a3 = vreg(1, 2 * mt + 1);
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) mma16816(oacc[nt][mt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
             }
         };
 
