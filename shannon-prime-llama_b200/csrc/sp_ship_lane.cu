@@ -8,11 +8,13 @@
 //
 // One thread owns one whole vector.  A warp takes 32 consecutive positions
 // of one head:
-//   - each lane bulk-copies its 512-byte input row (cp.async.bulk, the TMA
-//     engine, no multicast) into shared memory, rotated by 16*(lane & 7)
-//     bytes so the lane's 16-byte reads of the 8 lanes of a phase fall in
-//     distinct banks; the copy of the next batch is issued as soon as the
-//     current one sits in registers, so it streams under the arithmetic;
+//   - one elected lane fetches the batch's 32 input rows with tiled TMA
+//     copies (cp.async.bulk.tensor over a [tokens][heads][128] tensor map,
+//     128-byte column slices, no multicast) into shared memory with the
+//     128-byte swizzle, so each lane's 16-byte reads of its own row fall in
+//     distinct banks for the 8 lanes of a phase; the copy of the next batch
+//     is issued as soon as the current one sits in registers, so it
+//     streams under the arithmetic;
 //   - the 128-point Hartley butterfly runs entirely in the thread's
 //     registers (896 IEEE adds, no shuffles);
 //   - the Möbius order and the band layout are compile-time, so the
@@ -32,7 +34,10 @@
 #include "sp_internal.cuh"
 #include "sp_bulk.cuh"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <stdlib.h>
+#include <string.h>
 
 namespace {
 
@@ -97,11 +102,17 @@ struct LaneArgs {
     unsigned int *status;      // bit 0: a bulk copy did not land in time
 };
 
+// Tensor maps of the two halves' inputs ([n_tokens][nh][128], 128-byte
+// boxes of 32 tokens x 1 head, 128-byte swizzle).
+struct alignas(64) LaneMaps {
+    CUtensorMap m[2];
+};
+
 template <typename Tin>
 struct LaneSmem {
     static constexpr int RB = kLN * (int)sizeof(Tin);          // input row bytes
     static constexpr int OB = 32 * 76;                         // packed rows of a batch (K is the larger)
-    unsigned char in[kLaneWarps][32][RB];
+    alignas(1024) unsigned char in[kLaneWarps][32][RB];
     unsigned char out[kLaneWarps][OB];
     unsigned long long bar[kLaneWarps];
 };
@@ -250,7 +261,7 @@ __device__ __forceinline__ void lane_pack_store(const float (&x)[kLN], unsigned 
 
 template <typename Tin>
 __global__ void __launch_bounds__(kLaneWarps * 32, kLaneMinBlocks)
-k_encode_lane(LaneArgs a)
+k_encode_lane(LaneArgs a, const __grid_constant__ LaneMaps maps)
 {
     using S = LaneSmem<Tin>;
     constexpr int RB = S::RB;
@@ -259,12 +270,17 @@ k_encode_lane(LaneArgs a)
     extern __shared__ __align__(128) unsigned char smem_raw[];
     S &sm = *reinterpret_cast<S *>(smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int rot = lane & 7;                   // chunk rotation of this lane's row
+    constexpr int NQ = RB / 128;                // 128-byte column slices per row
     const uint32_t bar = spb::smem_u32(&sm.bar[warp]);
-    const uint32_t my_in = spb::smem_u32(&sm.in[warp][lane][0]);
+    const uint32_t in0 = spb::smem_u32(&sm.in[warp][0][0]);
     const int gw = blockIdx.x * kLaneWarps + warp, n_w = gridDim.x * kLaneWarps;
     const int n_total = a.nb * a.n_halves;
 
+    // The 128-byte swizzle needs 1024-byte aligned slices.
+    if (in0 & 1023) {
+        if (threadIdx.x == 0 && a.status) atomicOr(a.status, 4u);
+        return;
+    }
     if (lane == 0) {
         spb::mbar_init(bar, 1);
         spb::mbar_init_fence();
@@ -273,19 +289,21 @@ k_encode_lane(LaneArgs a)
     __syncwarp();
 
     // Batch g: half first + g / nb; within it head gl % nh, positions
-    // 32 * (gl / nh) ...; lane = position.
+    // 32 * (gl / nh) ...; lane = position.  Rows past n_tokens are filled
+    // with zeros by the copy (and never stored).
     auto issue = [&](int g) {
-        const int hx = a.first + g / a.nb, gl = g % a.nb;
-        const int h = gl % a.nh, t0 = (gl / a.nh) * 32;
-        const int live = min(32, a.n_tokens - t0);
-        if (lane == 0) spb::mbar_expect_tx(bar, (uint32_t)(live * RB));
-        __syncwarp();
-        if (lane < live) {
-            const unsigned char *src = reinterpret_cast<const unsigned char *>(hx ? a.half[1].in : a.half[0].in) +
-                                       ((long long)(t0 + lane) * a.nh + h) * RB;
-            // chunk j of the row lands at chunk (j - rot) mod C
-            spb::bulk_g2s(my_in, src + 16 * rot, (uint32_t)(RB - 16 * rot), bar, policy);
-            if (rot) spb::bulk_g2s(my_in + RB - 16 * rot, src, (uint32_t)(16 * rot), bar, policy);
+        if (lane == 0) {
+            const int hx = a.first + g / a.nb, gl = g % a.nb;
+            const int h = gl % a.nh, t0 = (gl / a.nh) * 32;
+            const CUtensorMap *tm = hx ? &maps.m[1] : &maps.m[0];
+            spb::mbar_expect_tx(bar, (uint32_t)(32 * RB));
+#pragma unroll
+            for (int q = 0; q < NQ; q++)
+                asm volatile(
+                    "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                    ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(in0 + q * 4096),
+                    "l"(tm), "r"(q * (128 / (int)sizeof(Tin))), "r"(h), "r"(t0), "r"(bar), "l"(policy)
+                    : "memory");
         }
     };
 
@@ -305,7 +323,9 @@ k_encode_lane(LaneArgs a)
         float x[kLN];
 #pragma unroll
         for (int j = 0; j < C; j++) {
-            const uint4 w = *reinterpret_cast<const uint4 *>(&sm.in[warp][lane][((j - rot) & (C - 1)) * 16]);
+            // chunk j = slice j / 8, 16-byte chunk j % 8, swizzled by row
+            const int off = (j >> 3) * 4096 + lane * 128 + (((j & 7) ^ (lane & 7)) << 4);
+            const uint4 w = *reinterpret_cast<const uint4 *>(&sm.in[warp][0][0] + off);
             lane_unpack16<Tin>(w, &x[j * EPC]);
         }
         __syncwarp();
@@ -338,7 +358,7 @@ k_encode_lane(LaneArgs a)
 }
 
 template <typename Tin>
-int launch_lane(const LaneArgs &a, cudaStream_t s)
+int launch_lane(const LaneArgs &a, const LaneMaps &maps, cudaStream_t s)
 {
     auto k = k_encode_lane<Tin>;
     const size_t smem = sizeof(LaneSmem<Tin>);
@@ -356,7 +376,7 @@ int launch_lane(const LaneArgs &a, cudaStream_t s)
     }
     long long blocks = ((long long)a.nb * a.n_halves + kLaneWarps - 1) / kLaneWarps;
     if (blocks > (long long)sms * occ) blocks = (long long)sms * occ;
-    k<<<(unsigned)blocks, kLaneWarps * 32, smem, s>>>(a);
+    k<<<(unsigned)blocks, kLaneWarps * 32, smem, s>>>(a, maps);
     return sp_check_cuda(cudaGetLastError(), "lane encoder launch");
 }
 
@@ -379,6 +399,42 @@ int lane_half_of(const SpBandLayout &bl, const int *d_order, bool std_order)
 }
 
 }  // namespace
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no
+// libcuda link); null if the driver does not provide it.
+PFN_cuTensorMapEncodeTiled_v12000 lane_encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// Map of [n_tokens][nh][128] elements: box = 128 bytes of one row x 1 head
+// x 32 tokens, 128-byte swizzle.
+bool lane_map(CUtensorMap *m, const void *in, int dtype, int n_tokens, int nh)
+{
+    auto fn = lane_encode_fn();
+    if (!fn) return false;
+    const int es = dtype == SP_DTYPE_F32 ? 4 : 2;
+    const CUtensorMapDataType dt = dtype == SP_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == SP_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                         : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const cuuint64_t dims[3] = {(cuuint64_t)kLN, (cuuint64_t)nh, (cuuint64_t)n_tokens};
+    const cuuint64_t strides[2] = {(cuuint64_t)kLN * es, (cuuint64_t)kLN * es * nh};
+    const cuuint32_t box[3] = {(cuuint32_t)(128 / es), 1, 32};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(m, dt, 3, const_cast<void *>(in), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 // Lane-per-vector encode of the K and/or V half of n_tokens tokens
 // ([n_tokens][nh][128] inputs; a null input skips its half).  Returns 1 and
@@ -406,10 +462,15 @@ int sp_encode_lane_kv(const void *d_k, const void *d_v, int dtype, int n_tokens,
     a.nb = nh * ((n_tokens + 31) / 32);
     a.inv_sqrt_n = sp_inv_sqrt_n(kLN);
     a.status = d_status;
+    LaneMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    if ((d_k && !lane_map(&maps.m[0], d_k, dtype, n_tokens, nh)) ||
+        (d_v && !lane_map(&maps.m[1], d_v, dtype, n_tokens, nh)))
+        return 0;
     switch (dtype) {
-    case SP_DTYPE_F32:  *rc = launch_lane<float>(a, s); break;
-    case SP_DTYPE_F16:  *rc = launch_lane<__half>(a, s); break;
-    default:            *rc = launch_lane<__nv_bfloat16>(a, s); break;
+    case SP_DTYPE_F32:  *rc = launch_lane<float>(a, maps, s); break;
+    case SP_DTYPE_F16:  *rc = launch_lane<__half>(a, maps, s); break;
+    default:            *rc = launch_lane<__nv_bfloat16>(a, maps, s); break;
     }
     return 1;
 }
