@@ -26,12 +26,17 @@
 #include "sp_internal.cuh"
 #include "sp_bulk.cuh"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 #include <algorithm>
 #include <vector>
+#include <type_traits>
+#include <utility>
 
 namespace {
 
@@ -1560,6 +1565,406 @@ __global__ void k_sq_attn_combine(SpSqDev t, SqAttn a)
     for (int i = lane; i < t.hd; i += 32) o[i] = __float2half_rn(buf[i] * inv);
 }
 
+// ------------------------------------------------ lane-per-vector sqfree --
+// Compress for the sqfree+spinor layout at head_dim 128 (pad 154 = 2.7.11,
+// skeleton of SK = 115 values (sk_frac 0.75), bands 5,4,4,4,5,
+// 3-bit residuals, sheet bits).  One thread owns one whole vector, as in the
+// ship lane encoder: the warp's 32 input rows arrive by tiled TMA copies
+// (128-byte swizzle) from one elected lane, the pad mean, the 154-point
+// staged transform, the skeleton quantiser, the Möbius CSR prediction, the
+// spinor choice and the residual quantiser all run in the thread's registers
+// with compile-time tables, and the 32 packed slots leave by one bulk store.
+// Every float operation is the one k_sq_encode performs, in the same order
+// (the lane-tree sums of the mean and of |dev| are replayed as the same
+// tree), so slots are bit-identical.
+constexpr int kSlPD = 154, kSlHD = 128, kSlNR = 3;   // pad, head_dim, residual bits
+constexpr int kSlWarps = 4;
+__host__ __device__ constexpr int sl_bits(int b) { return b == 0 || b == 4 ? 5 : 4; }
+
+template <int SK>
+struct SlTab {
+    int skel[SK];
+    int res[kSlPD - SK];
+    int off[kSlPD - SK + 1];
+    int term[384];                // (slot << 1) | negative
+    int term_res[384];            // residual of each term
+    int band_off[5], band_size[5], band_byte[5];
+    int mag_off, res_off, sheet_off, bytes;
+};
+
+__host__ __device__ constexpr bool sl_sqfree(int m)
+{
+    for (int p = 2; p * p <= m; p++)
+        if (m % (p * p) == 0) return false;
+    return true;
+}
+__host__ __device__ constexpr int sl_mu(int m)
+{
+    int k = 0;
+    for (int p = 2; p * p <= m; p++) {
+        if (m % p == 0) {
+            m /= p;
+            if (m % p == 0) return 0;
+            k++;
+        }
+    }
+    if (m > 1) k++;
+    return (k & 1) ? -1 : 1;
+}
+
+// The tables sp_cuda_sqfree_cache_init_ex builds (squarefree-first Knight
+// ranking, residual CSR over proper divisors with Möbius signs, skeleton
+// bands as sp_band_config_init) and the slot byte layout of sq_build_desc.
+template <int SK>
+__host__ __device__ constexpr SlTab<SK> sl_tab()
+{
+    SlTab<SK> t{};
+    int rank[kSlPD] = {};
+    int k = 0;
+    for (int i = 0; i < kSlPD; i++) if (sl_sqfree(i + 1)) rank[k++] = i;
+    for (int i = 0; i < kSlPD; i++) if (!sl_sqfree(i + 1)) rank[k++] = i;
+    int slot_of[kSlPD] = {};
+    for (int i = 0; i < kSlPD; i++) slot_of[i] = -1;
+    for (int s = 0; s < SK; s++) { t.skel[s] = rank[s]; slot_of[rank[s]] = s; }
+    int nr = 0;
+    for (int i = 0; i < kSlPD; i++) if (slot_of[i] < 0) t.res[nr++] = i;
+    int nt = 0;
+    for (int r = 0; r < kSlPD - SK; r++) {
+        t.off[r] = nt;
+        const int n = t.res[r] + 1;
+        for (int d = 1; d < n; d++) {
+            if (n % d) continue;
+            const int mu = sl_mu(n / d);
+            if (!mu || slot_of[d - 1] < 0) continue;
+            t.term_res[nt] = r;
+            t.term[nt++] = (slot_of[d - 1] << 1) | (mu < 0 ? 1 : 0);
+        }
+    }
+    t.off[kSlPD - SK] = nt;
+    int byte = 0;
+    for (int b = 0; b < 5; b++) {
+        t.band_off[b] = b * (SK / 5);
+        t.band_size[b] = b == 4 ? SK - 4 * (SK / 5) : SK / 5;
+        t.band_byte[b] = byte;
+        byte += 2 + (t.band_size[b] * sl_bits(b) + 7) / 8;
+    }
+    t.mag_off = byte;
+    t.res_off = byte + 4;
+    t.sheet_off = t.res_off + ((kSlPD - SK) * kSlNR + 7) / 8;
+    t.bytes = t.sheet_off + (kSlPD - SK + 7) / 8;
+    return t;
+}
+
+// The tables of the one compiled skeleton size, evaluated at compile time;
+// device code reads them only inside constant expressions, so every table
+// lookup becomes a register name.
+constexpr int kSlSK = 115;
+constexpr int kSlNRes = kSlPD - kSlSK;
+constexpr SlTab<kSlSK> kSlTab = sl_tab<kSlSK>();
+constexpr int kSlNT = kSlTab.off[kSlNRes];
+constexpr int kSlBytes = kSlTab.bytes, kSlMagOff = kSlTab.mag_off, kSlResOff = kSlTab.res_off,
+              kSlSheetOff = kSlTab.sheet_off;
+// Byte offset of skeleton band b (bands of kSlSK / 5 values).
+__host__ __device__ constexpr int sl_band_byte(int b)
+{
+    int byte = 0;
+    for (int k = 0; k < b; k++) byte += 2 + ((kSlSK / 5) * sl_bits(k) + 7) / 8;
+    return byte;
+}
+
+template <int I>
+__device__ __forceinline__ float sl_skel_of(const float (&x)[kSlPD])
+{
+    constexpr int i = kSlTab.skel[I];
+    return x[i];
+}
+template <int I>
+__device__ __forceinline__ float sl_res_of(const float (&x)[kSlPD])
+{
+    constexpr int i = kSlTab.res[I];
+    return x[i];
+}
+template <size_t... I>
+__device__ __forceinline__ void sl_gather(const float (&x)[kSlPD], float (&sk)[kSlSK], float (&rs)[kSlNRes],
+                                          std::index_sequence<I...>)
+{
+    ((sk[I] = sl_skel_of<I>(x)), ...);
+}
+template <size_t... I>
+__device__ __forceinline__ void sl_gather_res(const float (&x)[kSlPD], float (&rs)[kSlNRes], std::index_sequence<I...>)
+{
+    ((rs[I] = sl_res_of<I>(x)), ...);
+}
+// CSR term K: pr[r] +/-= skeleton value (csr_predict's chain, term by term).
+template <int K>
+__device__ __forceinline__ void sl_term(float (&pr)[kSlNRes], const float (&sk)[kSlSK])
+{
+    constexpr int term = kSlTab.term[K], r = kSlTab.term_res[K], si = term >> 1;
+    pr[r] = (term & 1) ? __fsub_rn(pr[r], sk[si]) : __fadd_rn(pr[r], sk[si]);
+}
+template <size_t... K>
+__device__ __forceinline__ void sl_terms(float (&pr)[kSlNRes], const float (&sk)[kSlSK], std::index_sequence<K...>)
+{
+    (sl_term<K>(pr, sk), ...);
+}
+
+template <int SK>
+struct SlArgs {
+    uint8_t *cache;              // slab base (head 0 of slot numbering)
+    long long slot_stride;
+    int layer0, n_layers, nh, start_pos, n_tok;
+    int nb;                      // batches: n_layers * nh * ceil(n_tok / 32)
+    unsigned int *status;
+};
+
+struct alignas(64) SlMap { CUtensorMap m; };
+
+template <typename Tin>
+__device__ __forceinline__ void lane_unpack16_sq(const uint4 &w, float *x)
+{
+    if constexpr (sizeof(Tin) == 4) {
+        x[0] = __uint_as_float(w.x); x[1] = __uint_as_float(w.y);
+        x[2] = __uint_as_float(w.z); x[3] = __uint_as_float(w.w);
+    } else {
+        const Tin *hv = reinterpret_cast<const Tin *>(&w);
+#pragma unroll
+        for (int i = 0; i < 8; i++) x[i] = sp_load_as_float(hv, i);
+    }
+}
+__device__ __forceinline__ void sl_bulk_s2g(void *dst, uint32_t src, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void sl_bulk_wait_read()
+{
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+template <typename Tin>
+struct SlSmem {
+    static constexpr int RB = kSlHD * (int)sizeof(Tin);
+    alignas(1024) unsigned char in[kSlWarps][32][RB];
+    unsigned char out[kSlWarps][32 * 100];
+    unsigned long long bar[kSlWarps];
+};
+
+// One stage of prime P at stride STRIDE of the compile-time plan, in the
+// thread's registers (vstage_c's arithmetic).
+template <int P, int STRIDE>
+__device__ __forceinline__ void sl_stage(float (&x)[kSlPD])
+{
+    const float isp = c_sq_isp[prime_slot<P>()];
+#pragma unroll
+    for (int g = 0; g < kSlPD / P; g++) {
+        const int blk = g / STRIDE, base = blk * (STRIDE * P) + (g - blk * STRIDE);
+        float y[P];
+#pragma unroll
+        for (int kk = 0; kk < P; kk++) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int j = 0; j < P; j++) acc = __fmaf_rn(c_sq_cas[cas_base<P>() + kk * P + j], x[base + j * STRIDE], acc);
+            y[kk] = __fmul_rn(acc, isp);
+        }
+#pragma unroll
+        for (int kk = 0; kk < P; kk++) x[base + kk * STRIDE] = y[kk];
+    }
+}
+
+// Sum of v[0..32) in the order lane_tree_reduce adds them across a warp.
+__device__ __forceinline__ float sl_tree32(float (&v)[32])
+{
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+        for (int j = 0; j < off; j++) v[j] = __fadd_rn(v[j], v[j + off]);
+    return v[0];
+}
+
+template <typename Tin, int SK>
+__global__ void __launch_bounds__(kSlWarps * 32, 2)
+k_sq_encode_lane(SlArgs<SK> a, const __grid_constant__ SlMap map)
+{
+    static_assert(SK == kSlSK, "one compiled skeleton size");
+    constexpr int NR = kSlPD - SK;
+    constexpr int TB = kSlBytes;
+    constexpr int W = (TB + 3) / 4;
+    static_assert(TB % 4 == 0 && TB <= 100, "slot rows of whole words, at most 100 bytes");
+    using S = SlSmem<Tin>;
+    constexpr int RB = S::RB, C = RB / 16, NQ = RB / 128, EPC = 16 / (int)sizeof(Tin);
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    S &sm = *reinterpret_cast<S *>(smem_raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t bar = spb::smem_u32(&sm.bar[warp]);
+    const uint32_t in0 = spb::smem_u32(&sm.in[warp][0][0]);
+    const int gw = blockIdx.x * kSlWarps + warp, n_w = gridDim.x * kSlWarps;
+    const int nbt = (a.n_tok + 31) >> 5;
+    if (in0 & 1023) {
+        if (threadIdx.x == 0 && a.status) atomicOr(a.status, 4u);
+        return;
+    }
+    if (lane == 0) {
+        spb::mbar_init(bar, 1);
+        spb::mbar_init_fence();
+    }
+    const uint64_t policy = spb::evict_first_policy();
+    __syncwarp();
+    // batch g: slot g / nbt (layer-major, then head), tokens 32 * (g % nbt) ...
+    auto issue = [&](int g) {
+        if (lane == 0) {
+            const int sl = g / nbt, li = sl / a.nh, h = sl - li * a.nh, t0 = (g - sl * nbt) * 32;
+            spb::mbar_expect_tx(bar, (uint32_t)(32 * RB));
+#pragma unroll
+            for (int q = 0; q < NQ; q++)
+                asm volatile(
+                    "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                    ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(in0 + q * 4096),
+                    "l"(&map.m), "r"(q * (128 / (int)sizeof(Tin))), "r"(h), "r"(li * a.n_tok + t0), "r"(bar),
+                    "l"(policy)
+                    : "memory");
+        }
+    };
+    uint32_t parity = 0;
+    if (gw < a.nb) issue(gw);
+    for (int g = gw; g < a.nb; g += n_w) {
+        const int sl = g / nbt, li = sl / a.nh, h = sl - li * a.nh, t0 = (g - sl * nbt) * 32;
+        const int live = min(32, a.n_tok - t0);
+        if (!spb::wait_stage(bar, parity, a.status)) {
+            spb::wait_stage(bar, parity, nullptr);
+            break;
+        }
+        parity ^= 1u;
+        float x[kSlPD];
+#pragma unroll
+        for (int j = 0; j < C; j++) {
+            const int off = (j >> 3) * 4096 + lane * 128 + (((j & 7) ^ (lane & 7)) << 4);
+            const uint4 w = *reinterpret_cast<const uint4 *>(&sm.in[warp][0][0] + off);
+            lane_unpack16_sq<Tin>(w, &x[j * EPC]);
+        }
+        __syncwarp();
+        spb::fence_proxy_async();
+        if (g + n_w < a.nb) issue(g + n_w);
+
+        // ---- pad with the lane-tree mean ----
+        {
+            float part[32];
+#pragma unroll
+            for (int l = 0; l < 32; l++) {
+                float s = 0.0f;
+#pragma unroll
+                for (int i = l; i < kSlHD; i += 32) s = __fadd_rn(s, x[i]);
+                part[l] = s;
+            }
+            const float mean = __fdiv_rn(sl_tree32(part), (float)kSlHD);
+#pragma unroll
+            for (int i = kSlHD; i < kSlPD; i++) x[i] = mean;
+        }
+        // ---- staged transform 2.7.11 ----
+        sl_stage<2, 1>(x);
+        sl_stage<7, 2>(x);
+        sl_stage<11, 14>(x);
+
+        uint32_t row[W];
+#pragma unroll
+        for (int k = 0; k < W; k++) row[k] = 0u;
+        auto put = [&](int p, uint32_t v, int bits) {
+            row[p >> 5] |= v << (p & 31);
+            if ((p & 31) + bits > 32) row[(p >> 5) + 1] |= v >> (32 - (p & 31));
+        };
+        // ---- skeleton / residual coefficients in table order ----
+        float sk[kSlSK], rs[kSlNRes];
+        sl_gather(x, sk, rs, std::make_index_sequence<kSlSK>{});
+        sl_gather_res(x, rs, std::make_index_sequence<kSlNRes>{});
+        // ---- skeleton bands (the ship quantiser) ----
+        constexpr int BS = SK / 5;           // every band holds SK / 5 values
+        static_assert(SK % 5 == 0, "equal skeleton bands");
+#pragma unroll
+        for (int b = 0; b < 5; b++) {
+            const int bits = sl_bits(b), mv = (1 << (bits - 1)) - 1;
+            float am[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int i = 0; i < BS; i++) am[i & 3] = fmaxf(am[i & 3], fabsf(sk[b * BS + i]));
+            const float amax = fmaxf(fmaxf(am[0], am[1]), fmaxf(am[2], am[3]));
+            const float scale = amax > 0.0f ? __fdiv_rn(amax, (float)mv) : 0.0f;
+            const __half hs = __float2half_rn(scale);
+            const float stored = __half2float(hs);
+            const float inv = stored > 0.0f ? __frcp_rn(stored) : 0.0f;
+            put(8 * sl_band_byte(b), (uint32_t)__half_as_ushort(hs), 16);
+#pragma unroll
+            for (int i = 0; i < BS; i++) {
+                int q = __float2int_rn(__fmul_rn(sk[b * BS + i], inv));
+                q = q > mv ? mv : (q < -mv ? -mv : q);
+                put(8 * (sl_band_byte(b) + 2) + i * bits, (uint32_t)(q + mv), bits);
+            }
+        }
+        // ---- residuals: Möbius prediction from the skeleton, spinor sheet ----
+        float pr[NR];
+#pragma unroll
+        for (int r = 0; r < NR; r++) pr[r] = 0.0f;
+        sl_terms(pr, sk, std::make_index_sequence<kSlNT>{});
+        float dev[NR];
+#pragma unroll
+        for (int r = 0; r < NR; r++) {
+            const float av = rs[r], p = pr[r];
+            const float vp = __fsub_rn(av, p), vm = __fadd_rn(av, p);
+            const bool use_minus = fabsf(vm) < fabsf(vp);
+            const float d = use_minus ? vm : vp;
+            put(8 * kSlSheetOff + r, use_minus ? 1u : 0u, 1);
+            dev[r] = d;
+        }
+        // lane l of k_sq_encode sums |dev| of r = l, l + 32, ... in order
+        float part[32];
+#pragma unroll
+        for (int l = 0; l < 32; l++) {
+            float sacc = 0.0f;
+#pragma unroll
+            for (int r = l; r < NR; r += 32) sacc = __fadd_rn(sacc, fabsf(dev[r]));
+            part[l] = sacc;
+        }
+        float mag = __fdiv_rn(sl_tree32(part), (float)NR);
+        if (mag < 1e-12f) mag = 1e-12f;
+        {
+            constexpr int L = 1 << kSlNR;
+            const float center = __fmul_rn(0.5f, (float)(L - 1));
+            const float sat = __fmul_rn(mag, (float)kSlNR);
+            const float step = __fdiv_rn(__fmul_rn(2.0f, sat), (float)(L - 1));
+            const float inv = __frcp_rn(step);
+#pragma unroll
+            for (int r = 0; r < NR; r++) {
+                const float q = __fmaf_rn(dev[r], inv, center);
+                int level = (int)__fadd_rn(q, 0.5f);
+                level = level < 0 ? 0 : (level >= L ? L - 1 : level);
+                put(8 * kSlResOff + r * kSlNR, (uint32_t)level, kSlNR);
+            }
+            put(8 * kSlMagOff, __float_as_uint(mag), 32);
+        }
+
+        // ---- stage the 32 slots, write them back ----
+        if (lane == 0) sl_bulk_wait_read();
+        __syncwarp();
+        unsigned char *stage = sm.out[warp];
+        {
+            uint32_t *r32 = reinterpret_cast<uint32_t *>(stage + lane * TB);
+#pragma unroll
+            for (int k = 0; k < TB / 4; k++) r32[k] = row[k];
+        }
+        spb::fence_proxy_async();
+        __syncwarp();
+        const int slot = (a.layer0 + li) * a.nh + h;
+        uint8_t *dst = a.cache + (long long)slot * a.slot_stride + (long long)(a.start_pos + t0) * TB;
+        const uint32_t bytes = (uint32_t)(live * TB);
+        if ((((uintptr_t)dst | bytes) & 15) == 0) {
+            if (lane == 0) sl_bulk_s2g(dst, spb::smem_u32(stage), bytes);
+        } else {
+            const uint32_t *s32 = reinterpret_cast<const uint32_t *>(stage);
+            for (uint32_t i = lane; i < bytes / 4; i += 32) reinterpret_cast<uint32_t *>(dst)[i] = s32[i];
+        }
+        __syncwarp();
+    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // --------------------------------------------------------------- host --
 
 bool sq_squarefree(int m)
@@ -1642,9 +2047,98 @@ int sq_plan_pd(const SpSqDev &t)
     return t.pd;
 }
 
-int sq_launch_encode(const SpSqDev &t, SqIo io, int dtype, cudaStream_t s)
+// cuTensorMapEncodeTiled through the runtime's driver entry point.
+PFN_cuTensorMapEncodeTiled_v12000 sq_encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// The lane-per-vector sqfree encoder when t is its layout (sqfree+spinor,
+// head_dim 128, pad 154, skeleton 115, bands 5,4,4,4,5, 3-bit residuals):
+// 1 and *rc set if it took the call.
+template <typename Tin>
+int sq_lane_launch(const SpSqDev &t, const SqIo &io, int dtype, unsigned int *status, cudaStream_t s, int *rc)
+{
+    constexpr int SK = kSlSK;
+    constexpr const SlTab<SK> &T = kSlTab;
+    if (t.hier || !t.use_spinor || t.hd != kSlHD || t.pd != kSlPD || t.n_skel != SK || t.n_res != kSlPD - SK ||
+        t.res_bits != kSlNR || t.bl.n_bands != 5 || t.mag_off != T.mag_off || t.res_off != T.res_off ||
+        t.sheet_off != T.sheet_off || t.bytes_per_pos != T.bytes || t.n_terms != T.off[kSlPD - SK])
+        return 0;
+
+    for (int b = 0; b < 5; b++)
+        if (t.bl.bits[b] != sl_bits(b) || t.bl.off[b] != T.band_off[b] || t.bl.size[b] != T.band_size[b] ||
+            t.bl.byte_off[b] != T.band_byte[b])
+            return 0;
+    if (((uintptr_t)io.in & 15) || ((uintptr_t)io.cache & 3) || (io.slot_stride & 3)) return 0;
+    if (getenv("SHANNON_PRIME_SQFREE_ENCODE_WARP")) return 0;
+    auto fn = sq_encode_fn();
+    if (!fn) return 0;
+    const long long nb = (long long)io.n_layers * io.nh * ((io.n_tok + 31) / 32);
+    if (nb > 0x7fffffffLL || (long long)io.n_layers * io.n_tok > 0xffffffffLL) return 0;
+    SlMap map;
+    memset(&map, 0, sizeof(map));
+    const int es = (int)sizeof(Tin);
+    const CUtensorMapDataType dt = dtype == SP_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == SP_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                         : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const cuuint64_t dims[3] = {(cuuint64_t)kSlHD, (cuuint64_t)io.nh, (cuuint64_t)io.n_layers * io.n_tok};
+    const cuuint64_t strides[2] = {(cuuint64_t)kSlHD * es, (cuuint64_t)kSlHD * es * io.nh};
+    const cuuint32_t box[3] = {(cuuint32_t)(128 / es), 1, 32};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (fn(&map.m, dt, 3, const_cast<void *>(io.in), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return 0;
+    SlArgs<SK> a;
+    a.cache = io.cache; a.slot_stride = io.slot_stride;
+    a.layer0 = io.layer0; a.n_layers = io.n_layers; a.nh = io.nh; a.start_pos = io.start_pos; a.n_tok = io.n_tok;
+    a.nb = (int)nb;
+    a.status = status;
+    auto k = k_sq_encode_lane<Tin, SK>;
+    const size_t smem = sizeof(SlSmem<Tin>);
+    static int occ[3] = {0, 0, 0}, sms = 0, dev_done[3] = {-1, -1, -1};
+    const int ti = sizeof(Tin) == 4 ? 0 : (std::is_same<Tin, __half>::value ? 1 : 2);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev != dev_done[ti]) {
+        if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+            *rc = sp_check_cuda(cudaGetLastError(), "sqfree lane encoder smem attribute");
+            return 1;
+        }
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ[ti], k, kSlWarps * 32, smem);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (occ[ti] < 1) occ[ti] = 1;
+        if (sms < 1) sms = 148;
+        dev_done[ti] = dev;
+    }
+    long long blocks = (nb + kSlWarps - 1) / kSlWarps;
+    if (blocks > (long long)sms * occ[ti]) blocks = (long long)sms * occ[ti];
+    k<<<(unsigned)blocks, kSlWarps * 32, smem, s>>>(a, map);
+    *rc = sp_check_cuda(cudaGetLastError(), "sqfree lane encoder launch");
+    return 1;
+}
+
+int sq_launch_encode(const SpSqDev &t, SqIo io, int dtype, cudaStream_t s, unsigned int *status = nullptr)
 {
     if (io.n_tok <= 0 || io.n_layers <= 0) return SP_OK;
+    {
+        int rc = SP_OK;
+        const int took = dtype == SP_DTYPE_F32 ? sq_lane_launch<float>(t, io, dtype, status, s, &rc)
+                       : dtype == SP_DTYPE_F16 ? sq_lane_launch<__half>(t, io, dtype, status, s, &rc)
+                       : dtype == SP_DTYPE_BF16 ? sq_lane_launch<__nv_bfloat16>(t, io, dtype, status, s, &rc) : 0;
+        if (took) return rc;
+    }
     const size_t sm = sq_smem_bytes(t);
     io.store_width = store_width_for(t.bytes_per_pos, io.slot_stride, io.cache);
     const int slots = io.n_layers * io.nh;
@@ -2238,7 +2732,9 @@ static int sq_write(sp_cuda_sqfree_cache_t *cc, int which, int layer0, int n_lay
         io.cache += (long long)layer0 * cc->config.n_heads_kv * io.slot_stride;
         if (n_layers != 1) return sp_set_error(SP_ERR_ARG, "sqfree: per-head writes take one layer");
     }
-    return sq_launch_encode(t, io, dtype, (cudaStream_t)cc->stream);
+    return sq_launch_encode(t, io, dtype, (cudaStream_t)cc->stream,
+                            reinterpret_cast<unsigned int *>(reinterpret_cast<char *>(cc->d_attn_ws) +
+                                                             cc->attn_ws_bytes));
 }
 
 static int sq_read(const sp_cuda_sqfree_cache_t *cc, int which, int layer, int head, int start_pos, int n_pos,

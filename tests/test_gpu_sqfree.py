@@ -201,3 +201,38 @@ def _has_lib(name):
         return True
     except OSError:
         return False
+
+
+@pytest.mark.parametrize("start,T,dt", [(0, 64, "float32"), (3, 77, "float32"), (5, 40, "bfloat16"),
+                                        (8, 33, "float16")])
+def test_sqfree_lane_encoder_matches_warp_encoder(cuda, monkeypatch, start, T, dt):
+    """The lane-per-vector sqfree encoder (config 2 layout) writes the same
+    slots as the warp-per-vector encoder (SHANNON_PRIME_SQFREE_ENCODE_WARP)
+    and as the oracle, at unaligned start positions, partial 32-position
+    batches, half-precision inputs and edge values."""
+    import torch
+    L, H, hd = 2, 3, 128
+    k, v = _inputs(7, L, H, T, hd, sigma=1.0)
+    k[0, 0, 0] = 0.0                       # zero vector
+    k[1, 1, 2] = 3e4                       # fp16 scale overflow
+    v[0, 2, 1, :7] = 1e-30                 # tiny values
+    tk = torch.from_numpy(k).to(getattr(torch, dt)).cuda()
+    tv = torch.from_numpy(v).to(getattr(torch, dt)).cuda()
+    slabs = []
+    for warp_path in (False, True):
+        if warp_path:
+            monkeypatch.setenv("SHANNON_PRIME_SQFREE_ENCODE_WARP", "1")
+        cache = SqfreeCache(hd, L, H, 128, sk_frac=0.75)
+        cache.write_kv_tokens(0, start, tk, tv)
+        torch.cuda.synchronize()
+        slabs.append((cache.slab(0).cpu().numpy(), cache.slab(1).cpu().numpy()))
+        monkeypatch.delenv("SHANNON_PRIME_SQFREE_ENCODE_WARP", raising=False)
+    (kl, vl), (kw, vw) = slabs
+    assert np.array_equal(kl, kw) and np.array_equal(vl, vw)
+    OL = O.sqfree_layout(hd, sk_k=cache.cc.sk_k, residual_bits=3, use_spinor=True)
+    k32, v32 = tk.float().cpu().numpy(), tv.float().cpu().numpy()
+    for layer in range(L):
+        for h in range(H):
+            s = layer * H + h
+            assert np.array_equal(kl[s, start:start + T], O.sqfree_write(k32[layer, :, h], OL))
+            assert np.array_equal(vl[s, start:start + T], O.sqfree_write(v32[layer, :, h], OL))
