@@ -1708,16 +1708,18 @@ __device__ __forceinline__ void sl_terms(float (&pr)[kSlNRes], const float (&sk)
     (sl_term<K>(pr, sk), ...);
 }
 
+// One launch writes the K half (0) and/or the V half (1) of the same tokens.
 template <int SK>
 struct SlArgs {
-    uint8_t *cache;              // slab base (head 0 of slot numbering)
-    long long slot_stride;
+    uint8_t *cache[2];           // slab bases (head 0 of the slot numbering)
+    long long slot_stride[2];
+    int first, n_halves;         // first half present, 1 or 2 halves
     int layer0, n_layers, nh, start_pos, n_tok;
-    int nb;                      // batches: n_layers * nh * ceil(n_tok / 32)
+    int nb;                      // batches per half: n_layers * nh * ceil(n_tok / 32)
     unsigned int *status;
 };
 
-struct alignas(64) SlMap { CUtensorMap m; };
+struct alignas(64) SlMap { CUtensorMap m[2]; };
 
 template <typename Tin>
 __device__ __forceinline__ void lane_unpack16_sq(const uint4 &w, float *x)
@@ -1800,6 +1802,7 @@ k_sq_encode_lane(SlArgs<SK> a, const __grid_constant__ SlMap map)
     const uint32_t in0 = spb::smem_u32(&sm.in[warp][0][0]);
     const int gw = blockIdx.x * kSlWarps + warp, n_w = gridDim.x * kSlWarps;
     const int nbt = (a.n_tok + 31) >> 5;
+    const int n_total = a.nb * a.n_halves;
     if (in0 & 1023) {
         if (threadIdx.x == 0 && a.status) atomicOr(a.status, 4u);
         return;
@@ -1810,25 +1813,29 @@ k_sq_encode_lane(SlArgs<SK> a, const __grid_constant__ SlMap map)
     }
     const uint64_t policy = spb::evict_first_policy();
     __syncwarp();
-    // batch g: slot g / nbt (layer-major, then head), tokens 32 * (g % nbt) ...
+    // batch g: half first + g / nb; within it slot gl / nbt (layer-major,
+    // then head), tokens 32 * (gl % nbt) ...
     auto issue = [&](int g) {
         if (lane == 0) {
-            const int sl = g / nbt, li = sl / a.nh, h = sl - li * a.nh, t0 = (g - sl * nbt) * 32;
+            const int hx = a.first + g / a.nb, gl = g % a.nb;
+            const int sl = gl / nbt, li = sl / a.nh, h = sl - li * a.nh, t0 = (gl - sl * nbt) * 32;
+            const CUtensorMap *tm = hx ? &map.m[1] : &map.m[0];
             spb::mbar_expect_tx(bar, (uint32_t)(32 * RB));
 #pragma unroll
             for (int q = 0; q < NQ; q++)
                 asm volatile(
                     "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
                     ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(in0 + q * 4096),
-                    "l"(&map.m), "r"(q * (128 / (int)sizeof(Tin))), "r"(h), "r"(li * a.n_tok + t0), "r"(bar),
+                    "l"(tm), "r"(q * (128 / (int)sizeof(Tin))), "r"(h), "r"(li * a.n_tok + t0), "r"(bar),
                     "l"(policy)
                     : "memory");
         }
     };
     uint32_t parity = 0;
-    if (gw < a.nb) issue(gw);
-    for (int g = gw; g < a.nb; g += n_w) {
-        const int sl = g / nbt, li = sl / a.nh, h = sl - li * a.nh, t0 = (g - sl * nbt) * 32;
+    if (gw < n_total) issue(gw);
+    for (int g = gw; g < n_total; g += n_w) {
+        const int hx = a.first + g / a.nb, gl = g % a.nb;
+        const int sl = gl / nbt, li = sl / a.nh, h = sl - li * a.nh, t0 = (gl - sl * nbt) * 32;
         const int live = min(32, a.n_tok - t0);
         if (!spb::wait_stage(bar, parity, a.status)) {
             spb::wait_stage(bar, parity, nullptr);
@@ -1844,7 +1851,7 @@ k_sq_encode_lane(SlArgs<SK> a, const __grid_constant__ SlMap map)
         }
         __syncwarp();
         spb::fence_proxy_async();
-        if (g + n_w < a.nb) issue(g + n_w);
+        if (g + n_w < n_total) issue(g + n_w);
 
         // ---- pad with the lane-tree mean ----
         {
@@ -1952,7 +1959,8 @@ k_sq_encode_lane(SlArgs<SK> a, const __grid_constant__ SlMap map)
         spb::fence_proxy_async();
         __syncwarp();
         const int slot = (a.layer0 + li) * a.nh + h;
-        uint8_t *dst = a.cache + (long long)slot * a.slot_stride + (long long)(a.start_pos + t0) * TB;
+        uint8_t *dst = (hx ? a.cache[1] : a.cache[0]) + (long long)slot * (hx ? a.slot_stride[1] : a.slot_stride[0]) +
+                       (long long)(a.start_pos + t0) * TB;
         const uint32_t bytes = (uint32_t)(live * TB);
         if ((((uintptr_t)dst | bytes) & 15) == 0) {
             if (lane == 0) sl_bulk_s2g(dst, spb::smem_u32(stage), bytes);
@@ -2063,32 +2071,28 @@ PFN_cuTensorMapEncodeTiled_v12000 sq_encode_fn()
     return fn;
 }
 
-// The lane-per-vector sqfree encoder when t is its layout (sqfree+spinor,
-// head_dim 128, pad 154, skeleton 115, bands 5,4,4,4,5, 3-bit residuals):
-// 1 and *rc set if it took the call.
-template <typename Tin>
-int sq_lane_launch(const SpSqDev &t, const SqIo &io, int dtype, unsigned int *status, cudaStream_t s, int *rc)
+// Whether t is the layout of the lane-per-vector sqfree encoder
+// (sqfree+spinor, head_dim 128, pad 154, skeleton 115, bands 5,4,4,4,5,
+// 3-bit residuals) and io's buffers suit it.
+bool sq_lane_fits(const SpSqDev &t, const SqIo &io)
 {
-    constexpr int SK = kSlSK;
-    constexpr const SlTab<SK> &T = kSlTab;
-    if (t.hier || !t.use_spinor || t.hd != kSlHD || t.pd != kSlPD || t.n_skel != SK || t.n_res != kSlPD - SK ||
+    constexpr const SlTab<kSlSK> &T = kSlTab;
+    if (t.hier || !t.use_spinor || t.hd != kSlHD || t.pd != kSlPD || t.n_skel != kSlSK || t.n_res != kSlNRes ||
         t.res_bits != kSlNR || t.bl.n_bands != 5 || t.mag_off != T.mag_off || t.res_off != T.res_off ||
-        t.sheet_off != T.sheet_off || t.bytes_per_pos != T.bytes || t.n_terms != T.off[kSlPD - SK])
-        return 0;
-
+        t.sheet_off != T.sheet_off || t.bytes_per_pos != T.bytes || t.n_terms != T.off[kSlNRes])
+        return false;
     for (int b = 0; b < 5; b++)
         if (t.bl.bits[b] != sl_bits(b) || t.bl.off[b] != T.band_off[b] || t.bl.size[b] != T.band_size[b] ||
             t.bl.byte_off[b] != T.band_byte[b])
-            return 0;
-    if (((uintptr_t)io.in & 15) || ((uintptr_t)io.cache & 3) || (io.slot_stride & 3)) return 0;
-    if (getenv("SHANNON_PRIME_SQFREE_ENCODE_WARP")) return 0;
+            return false;
+    return !(((uintptr_t)io.in & 15) || ((uintptr_t)io.cache & 3) || (io.slot_stride & 3));
+}
+
+bool sq_lane_map(CUtensorMap *m, const SqIo &io, int dtype)
+{
     auto fn = sq_encode_fn();
-    if (!fn) return 0;
-    const long long nb = (long long)io.n_layers * io.nh * ((io.n_tok + 31) / 32);
-    if (nb > 0x7fffffffLL || (long long)io.n_layers * io.n_tok > 0xffffffffLL) return 0;
-    SlMap map;
-    memset(&map, 0, sizeof(map));
-    const int es = (int)sizeof(Tin);
+    if (!fn) return false;
+    const int es = dtype == SP_DTYPE_F32 ? 4 : 2;
     const CUtensorMapDataType dt = dtype == SP_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                  : dtype == SP_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                          : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -2096,16 +2100,44 @@ int sq_lane_launch(const SpSqDev &t, const SqIo &io, int dtype, unsigned int *st
     const cuuint64_t strides[2] = {(cuuint64_t)kSlHD * es, (cuuint64_t)kSlHD * es * io.nh};
     const cuuint32_t box[3] = {(cuuint32_t)(128 / es), 1, 32};
     const cuuint32_t estr[3] = {1, 1, 1};
-    if (fn(&map.m, dt, 3, const_cast<void *>(io.in), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        return 0;
-    SlArgs<SK> a;
-    a.cache = io.cache; a.slot_stride = io.slot_stride;
-    a.layer0 = io.layer0; a.n_layers = io.n_layers; a.nh = io.nh; a.start_pos = io.start_pos; a.n_tok = io.n_tok;
+    return fn(m, dt, 3, const_cast<void *>(io.in), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// K (io[0]) and/or V (io[1], null = skipped) of the same tokens through the
+// lane-per-vector encoder: 1 and *rc set if it took the call.
+template <typename Tin>
+int sq_lane_launch(const SpSqDev *t[2], const SqIo *io[2], int dtype, unsigned int *status, cudaStream_t s,
+                   int *rc)
+{
+    if (getenv("SHANNON_PRIME_SQFREE_ENCODE_WARP")) return 0;
+    const SqIo *i0 = io[0] ? io[0] : io[1];
+    if (!i0) return 0;
+    for (int hx = 0; hx < 2; hx++)
+        if (io[hx] && (!sq_lane_fits(*t[hx], *io[hx]) || io[hx]->n_tok != i0->n_tok || io[hx]->nh != i0->nh ||
+                       io[hx]->n_layers != i0->n_layers || io[hx]->layer0 != i0->layer0 ||
+                       io[hx]->start_pos != i0->start_pos))
+            return 0;
+    const long long nb = (long long)i0->n_layers * i0->nh * ((i0->n_tok + 31) / 32);
+    if (2 * nb > 0x7fffffffLL || (long long)i0->n_layers * i0->n_tok > 0xffffffffLL) return 0;
+    SlMap map;
+    memset(&map, 0, sizeof(map));
+    SlArgs<kSlSK> a;
+    memset(&a, 0, sizeof(a));
+    for (int hx = 0; hx < 2; hx++) {
+        if (!io[hx]) continue;
+        if (!sq_lane_map(&map.m[hx], *io[hx], dtype)) return 0;
+        a.cache[hx] = io[hx]->cache;
+        a.slot_stride[hx] = io[hx]->slot_stride;
+    }
+    a.first = io[0] ? 0 : 1;
+    a.n_halves = (io[0] && io[1]) ? 2 : 1;
+    a.layer0 = i0->layer0; a.n_layers = i0->n_layers; a.nh = i0->nh; a.start_pos = i0->start_pos;
+    a.n_tok = i0->n_tok;
     a.nb = (int)nb;
     a.status = status;
-    auto k = k_sq_encode_lane<Tin, SK>;
+    auto k = k_sq_encode_lane<Tin, kSlSK>;
     const size_t smem = sizeof(SlSmem<Tin>);
     static int occ[3] = {0, 0, 0}, sms = 0, dev_done[3] = {-1, -1, -1};
     const int ti = sizeof(Tin) == 4 ? 0 : (std::is_same<Tin, __half>::value ? 1 : 2);
@@ -2122,11 +2154,18 @@ int sq_lane_launch(const SpSqDev &t, const SqIo &io, int dtype, unsigned int *st
         if (sms < 1) sms = 148;
         dev_done[ti] = dev;
     }
-    long long blocks = (nb + kSlWarps - 1) / kSlWarps;
+    long long blocks = (nb * a.n_halves + kSlWarps - 1) / kSlWarps;
     if (blocks > (long long)sms * occ[ti]) blocks = (long long)sms * occ[ti];
     k<<<(unsigned)blocks, kSlWarps * 32, smem, s>>>(a, map);
     *rc = sp_check_cuda(cudaGetLastError(), "sqfree lane encoder launch");
     return 1;
+}
+
+int sq_lane_try(const SpSqDev *t[2], const SqIo *io[2], int dtype, unsigned int *status, cudaStream_t s, int *rc)
+{
+    return dtype == SP_DTYPE_F32 ? sq_lane_launch<float>(t, io, dtype, status, s, rc)
+         : dtype == SP_DTYPE_F16 ? sq_lane_launch<__half>(t, io, dtype, status, s, rc)
+         : dtype == SP_DTYPE_BF16 ? sq_lane_launch<__nv_bfloat16>(t, io, dtype, status, s, rc) : 0;
 }
 
 int sq_launch_encode(const SpSqDev &t, SqIo io, int dtype, cudaStream_t s, unsigned int *status = nullptr)
@@ -2134,10 +2173,9 @@ int sq_launch_encode(const SpSqDev &t, SqIo io, int dtype, cudaStream_t s, unsig
     if (io.n_tok <= 0 || io.n_layers <= 0) return SP_OK;
     {
         int rc = SP_OK;
-        const int took = dtype == SP_DTYPE_F32 ? sq_lane_launch<float>(t, io, dtype, status, s, &rc)
-                       : dtype == SP_DTYPE_F16 ? sq_lane_launch<__half>(t, io, dtype, status, s, &rc)
-                       : dtype == SP_DTYPE_BF16 ? sq_lane_launch<__nv_bfloat16>(t, io, dtype, status, s, &rc) : 0;
-        if (took) return rc;
+        const SpSqDev *tt[2] = {&t, nullptr};
+        const SqIo *ii[2] = {&io, nullptr};
+        if (sq_lane_try(tt, ii, dtype, status, s, &rc)) return rc;
     }
     const size_t sm = sq_smem_bytes(t);
     io.store_width = store_width_for(t.bytes_per_pos, io.slot_stride, io.cache);
@@ -2710,11 +2748,9 @@ static int sq_check(const sp_cuda_sqfree_cache_t *cc, int layer, int n_layers, i
     return SP_OK;
 }
 
-static int sq_write(sp_cuda_sqfree_cache_t *cc, int which, int layer0, int n_layers, int head0, int nh,
-                    int start_pos, int n_tok, const void *d_in, int dtype)
+static int sq_write_io(sp_cuda_sqfree_cache_t *cc, int which, int layer0, int n_layers, int head0, int nh,
+                       int start_pos, int n_tok, const void *d_in, const SpSqDev &t, SqIo &io)
 {
-    SpSqDev t = sq_desc(cc, which);
-    SqIo io;
     memset(&io, 0, sizeof(io));
     io.in = d_in;
     io.cache = which ? cc->d_v_cache : cc->d_k_cache;
@@ -2732,9 +2768,22 @@ static int sq_write(sp_cuda_sqfree_cache_t *cc, int which, int layer0, int n_lay
         io.cache += (long long)layer0 * cc->config.n_heads_kv * io.slot_stride;
         if (n_layers != 1) return sp_set_error(SP_ERR_ARG, "sqfree: per-head writes take one layer");
     }
-    return sq_launch_encode(t, io, dtype, (cudaStream_t)cc->stream,
-                            reinterpret_cast<unsigned int *>(reinterpret_cast<char *>(cc->d_attn_ws) +
-                                                             cc->attn_ws_bytes));
+    return SP_OK;
+}
+
+static unsigned int *sq_status(const sp_cuda_sqfree_cache_t *cc)
+{
+    return reinterpret_cast<unsigned int *>(reinterpret_cast<char *>(cc->d_attn_ws) + cc->attn_ws_bytes);
+}
+
+static int sq_write(sp_cuda_sqfree_cache_t *cc, int which, int layer0, int n_layers, int head0, int nh,
+                    int start_pos, int n_tok, const void *d_in, int dtype)
+{
+    SpSqDev t = sq_desc(cc, which);
+    SqIo io;
+    int rc = sq_write_io(cc, which, layer0, n_layers, head0, nh, start_pos, n_tok, d_in, t, io);
+    if (rc) return rc;
+    return sq_launch_encode(t, io, dtype, (cudaStream_t)cc->stream, sq_status(cc));
 }
 
 static int sq_read(const sp_cuda_sqfree_cache_t *cc, int which, int layer, int head, int start_pos, int n_pos,
@@ -2805,6 +2854,17 @@ int sp_cuda_sqfree_write_kv_tokens(sp_cuda_sqfree_cache_t *cc, int layer0, int n
     int rc = sq_check(cc, layer0, n_layers, 0, start_pos, n_tokens);
     if (rc) return rc;
     const int H = cc->config.n_heads_kv;
+    if (d_k && d_v && n_tokens > 0) {
+        // both halves in one launch when the lane encoder takes them
+        SpSqDev tk = sq_desc(cc, 0), tv = sq_desc(cc, 1);
+        SqIo ik, iv;
+        if ((rc = sq_write_io(cc, 0, layer0, n_layers, 0, H, start_pos, n_tokens, d_k, tk, ik)) ||
+            (rc = sq_write_io(cc, 1, layer0, n_layers, 0, H, start_pos, n_tokens, d_v, tv, iv)))
+            return rc;
+        const SpSqDev *tt[2] = {&tk, &tv};
+        const SqIo *ii[2] = {&ik, &iv};
+        if (sq_lane_try(tt, ii, dtype, sq_status(cc), (cudaStream_t)cc->stream, &rc)) return rc;
+    }
     if (d_k && (rc = sq_write(cc, 0, layer0, n_layers, 0, H, start_pos, n_tokens, d_k, dtype))) return rc;
     if (d_v && (rc = sq_write(cc, 1, layer0, n_layers, 0, H, start_pos, n_tokens, d_v, dtype))) return rc;
     return SP_OK;
