@@ -106,3 +106,8 @@ def test_bridge_fused_decode_host_buffers(bridge):
     rc = L.sp_llama_attn_decode(ctx, 0, 1, qp.data_ptr(), H * G, T, 1.0, op.data_ptr(), -1)
     assert rc == 0
     np.testing.assert_array_equal(op.numpy(), out)
+    # pinned q with a pageable output: same bytes
+    out2 = np.zeros_like(out)
+    rc = L.sp_llama_attn_decode(ctx, 0, 1, qp.data_ptr(), H * G, T, 1.0, out2.ctypes.data, -1)
+    assert rc == 0
+    np.testing.assert_array_equal(out2, out)
