@@ -147,6 +147,21 @@ int  sp_cuda_attn_decode(const sp_cuda_cache_t *cc, int layer0, int n_layers,
                          float logit_scale, void *d_out, int max_bands,
                          void *stream);
 
+/* Replaces the CPU ggml custom2 op llama_sp_kq_compute
+ * (src/engine/llama_sp_fused_kq.cpp:82-165, userdata llama_sp_kq_userdata,
+ * src/engine/llama_sp_fused_kq.h:45-56) on the GPU: for one head's packed
+ * rows (d_packed = k_packed_buf_per_head, [n_kv][total_bytes_per_pos];
+ * is_v selects the V layout) and n_head_q query rows (d_q, f32 or f16,
+ * q_row_stride bytes apart = Q's nb[1]), writes the fp32 scores
+ * dst[qh][kv] = dot(decompressed row kv, q row qh) at d_dst + qh *
+ * dst_row_stride bytes (= dst's nb[1]), as the reference op does for all of
+ * its ith/nth slices at once.  Ship rows at head_dim 128 only (K 76 B with
+ * the squarefree-first order, V 50 B), at most 64 query rows; other shapes
+ * return SP_ERR_UNSUPPORTED.  Stream-ordered, allocates nothing. */
+int  sp_cuda_kq_scores(const void *d_packed, int total_bytes_per_pos, int is_v, int head_dim,
+                       int n_kv, const void *d_q, int q_dtype, long long q_row_stride,
+                       int n_head_q, float *d_dst, long long dst_row_stride, void *stream);
+
 /* New; no counterpart in the reference.  The fused decode above for callers
  * that cannot allocate device memory (an engine that owns every device
  * buffer through its own allocator, such as llama.cpp's ggml backend

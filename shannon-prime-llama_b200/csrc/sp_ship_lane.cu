@@ -490,3 +490,139 @@ int sp_encode_lane_try(const void *d_in, int dtype, int n_tokens, int nh, uint8_
     return sp_encode_lane_kv(nullptr, d_in, dtype, n_tokens, nh, start_pos, nullptr, 0, 0, bl, nullptr, false,
                              d_out_base, slot0, slot_stride, bl, d_status, s, rc);
 }
+
+// ------------------------------------------------ fused decompress-KQ op --
+// GPU counterpart of the reference's CPU ggml op llama_sp_kq_compute
+// (src/engine/llama_sp_fused_kq.cpp:82-165): for one head's packed rows
+// (k_packed_buf_per_head, total_bytes_per_pos, is_v of its userdata) and
+// n_head_q query rows, dst[qh][kv] = dot(decompress(row kv), q[qh]) in fp32.
+// The dot is taken in the coefficient domain (q' = perm(H q) / sqrt(n), the
+// transform being orthonormal and symmetric), so no row is reconstructed.
+// One thread owns one position: its row is staged through shared memory with
+// coalesced loads, its 128 coefficients are dequantised into registers with
+// the compile-time layout, and the transformed queries are read from shared
+// memory as broadcast 16-byte loads (4 heads per load).
+namespace {
+
+constexpr int kKqThreads = 128;       // positions per CTA
+constexpr int kKqMaxHeads = 64;
+
+template <bool KS>
+__global__ void __launch_bounds__(kKqThreads)
+k_kq_scores_lane(const uint8_t *packed, int n_kv, const void *q, int q_f16, long long q_stride, int n_head_q,
+                 float *dst, long long dst_stride, float inv_sqrt_n)
+{
+    using L = LaneLayout<KS>;
+    constexpr int TB = L::TB, TH = TB / 2;     // row bytes, halfwords
+    constexpr LaneOrder ord = lane_order();
+    __shared__ __align__(16) float qs[kLN][kKqMaxHeads];   // q'[coefficient][head]
+    __shared__ uint16_t rows[kKqThreads * TH];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nq4 = (n_head_q + 3) & ~3;
+
+    // ---- q' = perm(H q) / sqrt(n), one warp per head ----
+    for (int g = warp; g < nq4; g += kKqThreads / 32) {
+        float x[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int i = lane * 4 + e;
+            float v = 0.0f;
+            if (g < n_head_q) {
+                const uint8_t *qr = reinterpret_cast<const uint8_t *>(q) + g * q_stride;
+                v = q_f16 ? __half2float(reinterpret_cast<const __half *>(qr)[i])
+                          : reinterpret_cast<const float *>(qr)[i];
+            }
+            x[e] = v;
+        }
+        sp_warp_wht<4>(x, lane);
+        __shared__ float tmp[kKqThreads / 32][kLN];
+#pragma unroll
+        for (int e = 0; e < 4; e++) tmp[warp][lane * 4 + e] = x[e] * inv_sqrt_n;
+        __syncwarp();
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int j = lane * 4 + e;
+            qs[j][g] = tmp[warp][KS ? ord.v[j] : j];
+        }
+        __syncwarp();
+    }
+    // ---- this CTA's rows, coalesced, into shared memory ----
+    const long long kv0 = (long long)blockIdx.x * kKqThreads;
+    const int n_here = (int)min((long long)kKqThreads, n_kv - kv0);
+    const uint16_t *src = reinterpret_cast<const uint16_t *>(packed + kv0 * TB);
+    for (int i = tid; i < n_here * TH; i += kKqThreads) rows[i] = src[i];
+    __syncthreads();
+    if (tid >= n_here) return;
+
+    // ---- dequantise the thread's row (stored order) ----
+    const uint16_t *r16 = rows + tid * TH;
+    auto bits_at = [&](int p, int nb) -> uint32_t {          // nb <= 16 bits at bit p of the row
+        const int h = p >> 4, sh = p & 15;
+        uint32_t w = r16[h];
+        if (sh + nb > 16) w |= (uint32_t)r16[h + 1] << 16;
+        return (w >> sh) & ((1u << nb) - 1u);
+    };
+    float c[kLN];
+#pragma unroll
+    for (int b = 0; b < L::NB; b++) {
+        const int bits = L::bits(b), mv = (1 << (bits - 1)) - 1;
+        const int sbit = 8 * L::byte_off(b);
+        float scale = __half2float(__ushort_as_half((unsigned short)bits_at(sbit, 16)));
+        if (!isfinite(scale)) scale = 0.0f;
+#pragma unroll
+        for (int k = 0; k < L::SIZE; k++)
+            c[b * L::SIZE + k] = (float)((int)bits_at(sbit + 16 + k * bits, bits) - mv) * scale;
+    }
+    // ---- dots, 4 heads per pass ----
+    float *out = dst + (kv0 + tid);
+    for (int g0 = 0; g0 < n_head_q; g0 += 4) {
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int j = 0; j < kLN; j++) {
+            const float4 w = *reinterpret_cast<const float4 *>(&qs[j][g0]);
+            acc[0] = fmaf(c[j], w.x, acc[0]);
+            acc[1] = fmaf(c[j], w.y, acc[1]);
+            acc[2] = fmaf(c[j], w.z, acc[2]);
+            acc[3] = fmaf(c[j], w.w, acc[3]);
+        }
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+            if (g0 + e < n_head_q)
+                *reinterpret_cast<float *>(reinterpret_cast<char *>(out) + (long long)(g0 + e) * dst_stride) = acc[e];
+    }
+}
+
+}  // namespace
+
+extern "C" int sp_cuda_kq_scores(const void *d_packed, int total_bytes_per_pos, int is_v, int head_dim, int n_kv,
+                                 const void *d_q, int q_dtype, long long q_row_stride, int n_head_q,
+                                 float *d_dst, long long dst_row_stride, void *stream)
+{
+    sp_clear_error();
+    if (n_kv < 0 || n_head_q < 1 || !d_packed || !d_q || !d_dst)
+        return sp_set_error(SP_ERR_ARG, "kq_scores: bad arguments");
+    if (n_kv == 0) return SP_OK;
+    if (head_dim != kLN || n_head_q > kKqMaxHeads ||
+        total_bytes_per_pos != (is_v ? LaneLayout<false>::TB : LaneLayout<true>::TB))
+        return sp_set_error(SP_ERR_UNSUPPORTED,
+                            "kq_scores: head_dim 128 ship rows (K 76 B, V 50 B), at most %d query rows",
+                            kKqMaxHeads);
+    if (q_dtype != SP_DTYPE_F32 && q_dtype != SP_DTYPE_F16)
+        return sp_set_error(SP_ERR_ARG, "kq_scores: q must be f32 or f16");
+    const int es = q_dtype == SP_DTYPE_F32 ? 4 : 2;
+    if (((uintptr_t)d_packed & 1) || ((uintptr_t)d_q % es) || (q_row_stride % es) || ((uintptr_t)d_dst & 3) ||
+        (dst_row_stride & 3) || q_row_stride < (long long)es * head_dim || dst_row_stride < 4LL * n_kv)
+        return sp_set_error(SP_ERR_ARG, "kq_scores: misaligned pointer or stride");
+    const unsigned blocks = (unsigned)((n_kv + kKqThreads - 1) / kKqThreads);
+    cudaStream_t s = (cudaStream_t)stream;
+    const float isn = sp_inv_sqrt_n(kLN);
+    if (is_v)
+        k_kq_scores_lane<false><<<blocks, kKqThreads, 0, s>>>((const uint8_t *)d_packed, n_kv, d_q,
+                                                              q_dtype == SP_DTYPE_F16, q_row_stride, n_head_q,
+                                                              d_dst, dst_row_stride, isn);
+    else
+        k_kq_scores_lane<true><<<blocks, kKqThreads, 0, s>>>((const uint8_t *)d_packed, n_kv, d_q,
+                                                             q_dtype == SP_DTYPE_F16, q_row_stride, n_head_q,
+                                                             d_dst, dst_row_stride, isn);
+    return sp_check_cuda(cudaGetLastError(), "kq_scores launch");
+}
