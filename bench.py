@@ -617,6 +617,30 @@ def run_ours(args):
     comp_mpairs = pairs * ws / (cms * 1e-3) / 1e6
     comp_gbs = pairs * (2 * HD * 4 + K_ROW + V_ROW) / (cms * 1e-3) / 1e9
 
+    # The scores-only op (sp_cuda_kq_scores, the GPU body of the reference's
+    # ggml fused-KQ op): every (layer, KV head) slot of 4 layers against its
+    # G query rows, fp32 scores [G][CTX] per slot.
+    kq_dst = torch.empty(H, G, CTX, dtype=torch.float32, device=dev)
+    kslot = int(cc.contents.max_seq_len) * K_ROW
+    kbase = int(cc.contents.d_k_cache or 0)
+
+    def kq_pass():
+        for layer in range(4):
+            for h in range(H):
+                L.sp_cuda_kq_scores(kbase + (layer * H + h) * kslot, K_ROW, 0, HD, CTX,
+                                    q[layer, h * G].data_ptr(), 1, HD * 2, G, kq_dst[h].data_ptr(),
+                                    CTX * 4, stream.cuda_stream)
+    kq_pass()
+    barrier()
+    c0.record(stream)
+    for _ in range(reps):
+        kq_pass()
+    c1.record(stream)
+    barrier()
+    kq_ms = max_over_ranks(c0.elapsed_time(c1) / (reps * 4 * H))     # per slot
+    kq_bytes = CTX * K_ROW + G * CTX * 4 + G * HD * 2
+    kq_gbs = kq_bytes / (kq_ms * 1e-3) / 1e9
+
     # CPU baseline (rank 0, N = 1): the oracle on a bounded sample.
     cpu = None
     if ws == 1 and not args.no_cpu:
@@ -662,6 +686,10 @@ def run_ours(args):
                      "achieved_gbs": comp_gbs, "frac": comp_gbs / peak,
                      "workload": "4 layers x 32768 positions x %d KV heads, fp32 in, 5 passes; ms is per layer" % H,
                      "ms": cms},
+        "kq_op": {"metric": "fused decompress-KQ scores op (sp_cuda_kq_scores), per (layer, KV head) slot",
+                  "value": kq_ms * 1e3, "unit": "us/slot", "achieved_gbs": kq_gbs, "frac": kq_gbs / peak,
+                  "workload": "4 layers x %d KV heads, %d query rows per slot, ctx %d, fp32 scores out" % (H, G, CTX),
+                  "bytes_per_slot": kq_bytes},
         "cache_fill_s": t_fill,
     }
     if cpu is not None:
