@@ -641,6 +641,25 @@ def run_ours(args):
     kq_bytes = CTX * K_ROW + G * CTX * 4 + G * HD * 2
     kq_gbs = kq_bytes / (kq_ms * 1e-3) / 1e9
 
+    # Ship read (the reference-named decompress, fp32 rows out): every slot of
+    # one layer, one sp_cuda_read_batch_partial call per (KV head, K or V).
+    rd_out = torch.empty(CTX, HD, dtype=torch.float32, device=dev)
+
+    def read_pass():
+        for which in (0, 1):
+            for h in range(H):
+                L.sp_cuda_read_batch_partial(cc, which, 0, h, 0, CTX, rd_out.data_ptr(), -1)
+    read_pass()
+    barrier()
+    c0.record(stream)
+    for _ in range(reps):
+        read_pass()
+    c1.record(stream)
+    barrier()
+    rd_ms = max_over_ranks(c0.elapsed_time(c1) / (reps * 2 * H))      # per (slot, half)
+    rd_bytes = CTX * ((K_ROW + V_ROW) / 2 + HD * 4)
+    rd_gbs = rd_bytes / (rd_ms * 1e-3) / 1e9
+
     # CPU baseline (rank 0, N = 1): the oracle on a bounded sample.
     cpu = None
     if ws == 1 and not args.no_cpu:
@@ -690,6 +709,9 @@ def run_ours(args):
                   "value": kq_ms * 1e3, "unit": "us/slot", "achieved_gbs": kq_gbs, "frac": kq_gbs / peak,
                   "workload": "4 layers x %d KV heads, %d query rows per slot, ctx %d, fp32 scores out" % (H, G, CTX),
                   "bytes_per_slot": kq_bytes},
+        "read": {"metric": "ship read (decompress to fp32 rows) per (layer, KV head, K or V) slot",
+                 "value": rd_gbs, "unit": "GB/s", "ms_per_slot": rd_ms, "frac": rd_gbs / peak,
+                 "workload": "layer 0, %d KV heads x K and V, %d positions, fp32 [pos][128] out" % (H, CTX)},
         "cache_fill_s": t_fill,
     }
     if cpu is not None:

@@ -252,7 +252,7 @@ extern "C" int sp_cuda_read_batch_partial(const sp_cuda_cache_t *cc, int which, 
     const int *order = which ? nullptr : (cc->config.use_mobius_mask ? cc->d_mobius_order : nullptr);
     return sp_launch_decode(base, (long long)layer * cc->config.n_heads_kv + head,
                             (long long)cc->max_seq_len * bc.total_bytes, start_pos, n_pos, d_out,
-                            order, true, max_bands, bl, (cudaStream_t)cc->stream);
+                            order, true, max_bands, bl, (cudaStream_t)cc->stream, true, cc->d_status);
 }
 
 extern "C" void sp_cuda_read_k(const sp_cuda_cache_t *cc, int layer, int head, int pos, float *d_k_out)

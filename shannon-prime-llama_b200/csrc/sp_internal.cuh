@@ -53,7 +53,12 @@ int sp_encode_lane_kv(const void *d_k, const void *d_v, int dtype, int n_tokens,
                       unsigned int *d_status, cudaStream_t s, int *rc);
 int sp_launch_decode(const uint8_t *d_in_base, long long slot, long long slot_stride_bytes,
                      int start_pos, int n_pos, float *d_out, const int *d_order,
-                     bool do_wht, int max_bands, const SpBandLayout &bl, cudaStream_t s);
+                     bool do_wht, int max_bands, const SpBandLayout &bl, cudaStream_t s,
+                     bool std_order = false, unsigned int *d_status = nullptr);
+// Lane-per-vector ship read (sp_ship_lane.cu): 1 and *rc set if it took the call.
+int sp_decode_lane_try(const uint8_t *d_rows, int n_pos, float *d_out, const int *d_order, bool std_order,
+                       bool do_wht, int max_bands, const SpBandLayout &bl, unsigned int *d_status, cudaStream_t s,
+                       int *rc);
 
 // ---------------------------------------------------------------- device --
 

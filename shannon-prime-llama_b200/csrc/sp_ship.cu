@@ -648,11 +648,18 @@ int sp_launch_encode(const void *d_in, int dtype, int n_tokens, int nh,
 
 int sp_launch_decode(const uint8_t *d_in_base, long long slot, long long slot_stride_bytes,
                      int start_pos, int n_pos, float *d_out, const int *d_order,
-                     bool do_wht, int max_bands, const SpBandLayout &bl, cudaStream_t s)
+                     bool do_wht, int max_bands, const SpBandLayout &bl, cudaStream_t s,
+                     bool std_order, unsigned int *d_status)
 {
     if (n_pos == 0) return SP_OK;
     if (!d_in_base || !d_out || n_pos < 0)
         return sp_set_error(SP_ERR_ARG, "decode: bad arguments");
+    {
+        int rc = SP_OK;
+        const uint8_t *rows = d_in_base + slot * slot_stride_bytes + (long long)start_pos * bl.total_bytes;
+        if (sp_decode_lane_try(rows, n_pos, d_out, d_order, std_order, do_wht, max_bands, bl, d_status, s, &rc))
+            return rc;
+    }
     DecodeArgs a;
     a.in_base = d_in_base; a.slot = slot; a.slot_stride = slot_stride_bytes;
     a.start_pos = start_pos; a.n_pos = n_pos; a.out = d_out; a.order = d_order;

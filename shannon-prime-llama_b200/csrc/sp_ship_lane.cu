@@ -626,3 +626,165 @@ extern "C" int sp_cuda_kq_scores(const void *d_packed, int total_bytes_per_pos, 
                                                              d_dst, dst_row_stride, isn);
     return sp_check_cuda(cudaGetLastError(), "kq_scores launch");
 }
+
+// ------------------------------------------------- lane-per-vector read --
+// The ship read (reference sp_cuda_read_k/_v[_batch], shannon_prime_cuda.cu:
+// 524-559, 622-657: dequantise -> Möbius unreorder -> VHT2 -> fp32 rows) for
+// the head_dim-128 ship layouts, one thread per position: the warp's 32
+// packed rows are loaded coalesced into shared memory, each thread
+// dequantises its row with the compile-time layout (bands at or beyond
+// max_bands read as zero), unreorders by register renaming, runs the
+// butterfly in registers, and writes its fp32 row into a 128-byte-swizzled
+// shared-memory tile that one elected lane stores with tiled TMA copies.
+// Same IEEE operations in the same order as k_decode, so rows are
+// bit-identical.
+namespace {
+
+struct alignas(64) ReadMap { CUtensorMap m; };
+
+template <bool KS>
+struct ReadSmem {
+    alignas(1024) unsigned char out[kLaneWarps][4][4096];      // 4 column slices x 32 rows x 128 B
+    uint16_t rows[kLaneWarps][32 * LaneLayout<KS>::TB / 2];
+};
+
+template <bool KS>
+__global__ void __launch_bounds__(kLaneWarps * 32, kLaneMinBlocks)
+k_decode_lane(const uint8_t *packed, int n_pos, int nb_use, float inv_sqrt_n, unsigned int *status,
+              const __grid_constant__ ReadMap map)
+{
+    using L = LaneLayout<KS>;
+    constexpr int TB = L::TB, TH = TB / 2;
+    constexpr LaneOrder ord = lane_order();
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    ReadSmem<KS> &sm = *reinterpret_cast<ReadSmem<KS> *>(smem_raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t out0 = spb::smem_u32(&sm.out[warp][0][0]);
+    if (out0 & 1023) {
+        if (threadIdx.x == 0 && status) atomicOr(status, 4u);
+        return;
+    }
+    const int n_b = (n_pos + 31) >> 5;
+    for (int bt = blockIdx.x * kLaneWarps + warp; bt < n_b; bt += gridDim.x * kLaneWarps) {
+        const int t0 = bt * 32, live = min(32, n_pos - t0);
+        uint16_t *rows = sm.rows[warp];
+        const uint16_t *src = reinterpret_cast<const uint16_t *>(packed + (long long)t0 * TB);
+        for (int i = lane; i < live * TH; i += 32) rows[i] = src[i];
+        __syncwarp();
+        const uint16_t *r16 = rows + lane * TH;
+        auto bits_at = [&](int p, int nb) -> uint32_t {
+            const int h = p >> 4, sh = p & 15;
+            uint32_t w = r16[h];
+            if (sh + nb > 16) w |= (uint32_t)r16[h + 1] << 16;
+            return (w >> sh) & ((1u << nb) - 1u);
+        };
+        float x[kLN];
+#pragma unroll
+        for (int b = 0; b < L::NB; b++) {
+            const int bits = L::bits(b), mv = (1 << (bits - 1)) - 1;
+            const int sbit = 8 * L::byte_off(b);
+            float scale = __half2float(__ushort_as_half((unsigned short)bits_at(sbit, 16)));
+            if (!isfinite(scale)) scale = 0.0f;
+            const bool on = b < nb_use;
+#pragma unroll
+            for (int k = 0; k < L::SIZE; k++) {
+                const int j = b * L::SIZE + k;                 // stored index
+                const float v = on ? __fmul_rn((float)((int)bits_at(sbit + 16 + k * bits, bits) - mv), scale)
+                                   : 0.0f;
+                x[KS ? ord.v[j] : j] = v;                      // unreorder
+            }
+        }
+#pragma unroll
+        for (int len = 1; len < kLN; len <<= 1) {
+#pragma unroll
+            for (int i = 0; i < kLN; i += len << 1) {
+#pragma unroll
+                for (int j = 0; j < len; j++) {
+                    const float u = x[i + j], v = x[i + j + len];
+                    x[i + j] = __fadd_rn(u, v);
+                    x[i + j + len] = __fsub_rn(u, v);
+                }
+            }
+        }
+        if (lane == 0) bulk_wait_read();        // the previous batch's stores have read the tile
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < kLN / 4; c++) {
+            const int off = (c >> 3) * 4096 + lane * 128 + (((c & 7) ^ (lane & 7)) << 4);
+            *reinterpret_cast<float4 *>(&sm.out[warp][0][0] + off) =
+                make_float4(__fmul_rn(x[4 * c], inv_sqrt_n), __fmul_rn(x[4 * c + 1], inv_sqrt_n),
+                            __fmul_rn(x[4 * c + 2], inv_sqrt_n), __fmul_rn(x[4 * c + 3], inv_sqrt_n));
+        }
+        spb::fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+                asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                                 &map.m),
+                             "r"(q * 32), "r"(t0), "r"(out0 + q * 4096)
+                             : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+        (void)live;
+    }
+    if (lane == 0) bulk_wait_all();
+}
+
+template <bool KS>
+int launch_read_lane(const uint8_t *packed, int n_pos, int nb_use, float *d_out, unsigned int *status,
+                     cudaStream_t s)
+{
+    auto fn = lane_encode_fn();
+    if (!fn) return 1;
+    ReadMap map;
+    memset(&map, 0, sizeof(map));
+    const cuuint64_t dims[2] = {(cuuint64_t)kLN, (cuuint64_t)n_pos};
+    const cuuint64_t strides[1] = {(cuuint64_t)kLN * 4};
+    const cuuint32_t box[2] = {32, 32};
+    const cuuint32_t estr[2] = {1, 1};
+    if (fn(&map.m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, d_out, dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return 1;
+    auto k = k_decode_lane<KS>;
+    const size_t smem = sizeof(ReadSmem<KS>);
+    static int occ = 0, sms = 0, dev_done = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev != dev_done) {
+        if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+            sp_check_cuda(cudaGetLastError(), "lane read smem attribute");
+            return -1;
+        }
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, kLaneWarps * 32, smem);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (occ < 1) occ = 1;
+        if (sms < 1) sms = 148;
+        dev_done = dev;
+    }
+    const long long n_b = (n_pos + 31) / 32;
+    long long blocks = (n_b + kLaneWarps - 1) / kLaneWarps;
+    if (blocks > (long long)sms * occ) blocks = (long long)sms * occ;
+    k<<<(unsigned)blocks, kLaneWarps * 32, smem, s>>>(packed, n_pos, nb_use, sp_inv_sqrt_n(kLN), status, map);
+    return sp_check_cuda(cudaGetLastError(), "lane read launch") ? -1 : 0;
+}
+
+}  // namespace
+
+// The lane-per-vector read for the head_dim-128 ship layouts (K with the
+// standard order): 1 and *rc set if it took the call.
+int sp_decode_lane_try(const uint8_t *d_rows, int n_pos, float *d_out, const int *d_order, bool std_order,
+                       bool do_wht, int max_bands, const SpBandLayout &bl, unsigned int *d_status, cudaStream_t s,
+                       int *rc)
+{
+    if (!do_wht || n_pos <= 0 || getenv("SHANNON_PRIME_DECODE_WARP")) return 0;
+    const int hx = lane_half_of(bl, d_order, std_order);
+    if (hx < 0 || ((uintptr_t)d_rows & 1) || ((uintptr_t)d_out & 15)) return 0;
+    const int nb_use = (max_bands < 0 || max_bands >= bl.n_bands) ? bl.n_bands : max_bands;
+    const int r = hx == 0 ? launch_read_lane<true>(d_rows, n_pos, nb_use, d_out, d_status, s)
+                          : launch_read_lane<false>(d_rows, n_pos, nb_use, d_out, d_status, s);
+    if (r > 0) return 0;                        // no tensor-map encoder: the warp kernel reads
+    *rc = r ? sp_set_error(SP_ERR_CUDA, "lane read failed") : SP_OK;
+    return 1;
+}

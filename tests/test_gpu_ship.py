@@ -223,3 +223,31 @@ def test_ship_lane_encoder_ragged(cuda, monkeypatch, start, T, dt):
         assert np.array_equal(vl[H + h, start:start + T], O.ship_write(v32[:, h], VB, False))
         assert not kl[H + h, :start].any() and not kl[H + h, start + T:].any()
         assert not vl[H + h, :start].any() and not vl[H + h, start + T:].any()
+
+
+@pytest.mark.parametrize("start,T", [(0, 4096), (3, 77), (5, 1)])
+def test_ship_lane_read_matches_warp_read_and_oracle(cuda, monkeypatch, start, T):
+    """The lane-per-vector ship read (head_dim 128) returns the rows of the
+    warp-per-position read (SHANNON_PRIME_DECODE_WARP) and of the oracle,
+    bit for bit, for full and partial band reads and ragged ranges."""
+    torch = _torch()
+    H, n = 2, 128
+    k, v = _layer_inputs(31, H, T, n, sigma=1.0)
+    cache = spb200.Cache(n, 1, H, 4112)
+    cache.write_kv_tokens(0, start, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda())
+    torch.cuda.synchronize()
+    kp = cache.slab(0).cpu().numpy()[:, start:start + T]
+    vp = cache.slab(1).cpu().numpy()[:, start:start + T]
+    for which, packed, bands, mob in ((0, kp, KB, True), (1, vp, VB, False)):
+        for mb in (-1, 0, 1, 3):
+            outs = []
+            for warp_path in (False, True):
+                if warp_path:
+                    monkeypatch.setenv("SHANNON_PRIME_DECODE_WARP", "1")
+                out = torch.full((T, n), 5.0, device="cuda")
+                cache.read_batch(which, 0, 1, start, out, max_bands=mb)
+                torch.cuda.synchronize()
+                outs.append(out.cpu().numpy())
+                monkeypatch.delenv("SHANNON_PRIME_DECODE_WARP", raising=False)
+            np.testing.assert_array_equal(outs[0], outs[1])
+            np.testing.assert_array_equal(outs[0], O.ship_read(packed[1], n, bands, mob, max_bands=mb))
