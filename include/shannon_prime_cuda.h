@@ -65,7 +65,10 @@ typedef struct {
     size_t           attn_ws_bytes;
     int              attn_max_q_heads; /* q heads per layer the workspace is sized for */
     int              attn_ws_layers;   /* layers per call the workspace is sized for */
-    unsigned int    *d_status;       /* device-side error word (bounded waits) */
+    unsigned int    *d_status;       /* device-side error word: bit 0 a bounded copy wait ran
+                                        out, bit 1 the cross-GPU gather wait ran out, bit 2 a
+                                        lane kernel found its shared memory misaligned for the
+                                        128-byte swizzle and wrote nothing */
 } sp_cuda_cache_t;
 
 /* ------------------------------------------------------------ lifecycle -- */
