@@ -1709,6 +1709,28 @@ __device__ __forceinline__ void sl_terms(float (&pr)[kSlNRes], const float (&sk)
 }
 
 // One launch writes the K half (0) and/or the V half (1) of the same tokens.
+// Skeleton and residual values back to coefficient positions (the inverse
+// of sl_gather / sl_gather_res).
+template <int I>
+__device__ __forceinline__ void sl_put_skel(float (&x)[kSlPD], const float (&sk)[kSlSK])
+{
+    constexpr int i = kSlTab.skel[I];
+    x[i] = sk[I];
+}
+template <int I>
+__device__ __forceinline__ void sl_put_res(float (&x)[kSlPD], const float (&rs)[kSlNRes])
+{
+    constexpr int i = kSlTab.res[I];
+    x[i] = rs[I];
+}
+template <size_t... I, size_t... R>
+__device__ __forceinline__ void sl_scatter(float (&x)[kSlPD], const float (&sk)[kSlSK], const float (&rs)[kSlNRes],
+                                           std::index_sequence<I...>, std::index_sequence<R...>)
+{
+    (sl_put_skel<I>(x, sk), ...);
+    (sl_put_res<R>(x, rs), ...);
+}
+
 template <int SK>
 struct SlArgs {
     uint8_t *cache[2];           // slab bases (head 0 of the slot numbering)
@@ -1969,6 +1991,103 @@ k_sq_encode_lane(SlArgs<SK> a, const __grid_constant__ SlMap map)
             for (uint32_t i = lane; i < bytes / 4; i += 32) reinterpret_cast<uint32_t *>(dst)[i] = s32[i];
         }
         __syncwarp();
+    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// Lane-per-vector read of the same layout: one thread per position
+// rebuilds the 154 coefficients in registers (skeleton dequantised with the
+// ship rule, residuals as the signed Möbius prediction plus the dequantised
+// deviation, the order of sq_coeffs), runs the self-inverse transform and
+// writes the first 128 values through a 128-byte-swizzled tile and tiled
+// TMA stores.  Bit-identical with k_sq_decode.
+struct alignas(64) SlOutMap { CUtensorMap m; };
+
+struct SlReadSmem {
+    alignas(1024) unsigned char out[kSlWarps][4][4096];
+    uint32_t rows[kSlWarps][32 * 25];               // 32 slots of 100 bytes
+};
+
+__global__ void __launch_bounds__(kSlWarps * 32, 2)
+k_sq_decode_lane(const uint8_t *slab, int n_pos, unsigned int *status, const __grid_constant__ SlOutMap map)
+{
+    constexpr int NR = kSlNRes, TW = kSlBytes / 4;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    SlReadSmem &sm = *reinterpret_cast<SlReadSmem *>(smem_raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t out0 = spb::smem_u32(&sm.out[warp][0][0]);
+    if (out0 & 1023) {
+        if (threadIdx.x == 0 && status) atomicOr(status, 4u);
+        return;
+    }
+    const int n_b = (n_pos + 31) >> 5;
+    for (int bt = blockIdx.x * kSlWarps + warp; bt < n_b; bt += gridDim.x * kSlWarps) {
+        const int t0 = bt * 32, live = min(32, n_pos - t0);
+        uint32_t *rows = sm.rows[warp];
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(slab + (long long)t0 * kSlBytes);
+        for (int i = lane; i < live * TW; i += 32) rows[i] = src[i];
+        __syncwarp();
+        const uint32_t *rw = rows + lane * TW;
+        auto bits_at = [&](int p, int nb) -> uint32_t {
+            const int w = p >> 5, sh = p & 31;
+            uint32_t v = rw[w] >> sh;
+            if (sh + nb > 32) v |= rw[w + 1] << (32 - sh);
+            return nb == 32 ? v : (v & ((1u << nb) - 1u));
+        };
+        // skeleton values in slot order
+        constexpr int BS = kSlSK / 5;
+        float sk[kSlSK];
+#pragma unroll
+        for (int b = 0; b < 5; b++) {
+            const int bits = sl_bits(b), mv = (1 << (bits - 1)) - 1;
+            float scale = __half2float(__ushort_as_half((unsigned short)bits_at(8 * sl_band_byte(b), 16)));
+            if (!isfinite(scale)) scale = 0.0f;
+#pragma unroll
+            for (int i = 0; i < BS; i++)
+                sk[b * BS + i] =
+                    __fmul_rn((float)((int)bits_at(8 * (sl_band_byte(b) + 2) + i * bits, bits) - mv), scale);
+        }
+        const float mag = __uint_as_float(bits_at(8 * kSlMagOff, 32));
+        constexpr int L = 1 << kSlNR;
+        const float center = __fmul_rn(0.5f, (float)(L - 1));
+        const float sat = __fmul_rn(mag, (float)kSlNR);
+        const float step = __fdiv_rn(__fmul_rn(2.0f, sat), (float)(L - 1));
+        float pr[NR];
+#pragma unroll
+        for (int r = 0; r < NR; r++) pr[r] = 0.0f;
+        sl_terms(pr, sk, std::make_index_sequence<kSlNT>{});
+        float rs[NR];
+#pragma unroll
+        for (int r = 0; r < NR; r++) {
+            const float lv = (float)bits_at(8 * kSlResOff + r * kSlNR, kSlNR);
+            const float dev = __fmul_rn(__fsub_rn(lv, center), step);
+            const float p = bits_at(8 * kSlSheetOff + r, 1) ? -pr[r] : pr[r];
+            rs[r] = __fadd_rn(p, dev);
+        }
+        float x[kSlPD];
+        sl_scatter(x, sk, rs, std::make_index_sequence<kSlSK>{}, std::make_index_sequence<NR>{});
+        sl_stage<2, 1>(x);
+        sl_stage<7, 2>(x);
+        sl_stage<11, 14>(x);
+        if (lane == 0) sl_bulk_wait_read();
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < kSlHD / 4; c++) {
+            const int off = (c >> 3) * 4096 + lane * 128 + (((c & 7) ^ (lane & 7)) << 4);
+            *reinterpret_cast<float4 *>(&sm.out[warp][0][0] + off) =
+                make_float4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
+        }
+        spb::fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+                asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                                 &map.m),
+                             "r"(q * 32), "r"(t0), "r"(out0 + q * 4096)
+                             : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
     }
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
@@ -2804,6 +2923,40 @@ static int sq_read(const sp_cuda_sqfree_cache_t *cc, int which, int layer, int h
     io.start_pos = start_pos;
     io.n_tok = n_pos;
     io.single_slot = 1;
+    if (sq_lane_fits(t, io) && !getenv("SHANNON_PRIME_SQFREE_DECODE_WARP") && !((uintptr_t)d_out & 15) &&
+        !(((uintptr_t)io.cache + (uintptr_t)start_pos * t.bytes_per_pos) & 3)) {
+        auto fn = sq_encode_fn();
+        SlOutMap map;
+        memset(&map, 0, sizeof(map));
+        const cuuint64_t dims[2] = {(cuuint64_t)kSlHD, (cuuint64_t)n_pos};
+        const cuuint64_t strides[1] = {(cuuint64_t)kSlHD * 4};
+        const cuuint32_t box[2] = {32, 32};
+        const cuuint32_t estr[2] = {1, 1};
+        if (fn && fn(&map.m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, d_out, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+            const size_t smem = sizeof(SlReadSmem);
+            static int occ = 0, sms = 0, dev_done = -1;
+            int dev = 0;
+            cudaGetDevice(&dev);
+            if (dev != dev_done) {
+                if (cudaFuncSetAttribute(k_sq_decode_lane, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+                    cudaSuccess)
+                    return sp_check_cuda(cudaGetLastError(), "sqfree lane read smem attribute");
+                cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_sq_decode_lane, kSlWarps * 32, smem);
+                cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+                if (occ < 1) occ = 1;
+                if (sms < 1) sms = 148;
+                dev_done = dev;
+            }
+            const long long n_b = (n_pos + 31) / 32;
+            long long blocks = (n_b + kSlWarps - 1) / kSlWarps;
+            if (blocks > (long long)sms * occ) blocks = (long long)sms * occ;
+            k_sq_decode_lane<<<(unsigned)blocks, kSlWarps * 32, smem, (cudaStream_t)cc->stream>>>(
+                io.cache + (long long)start_pos * t.bytes_per_pos, n_pos, sq_status(cc), map);
+            return sp_check_cuda(cudaGetLastError(), "sqfree lane read launch");
+        }
+    }
     return sq_launch_decode(t, io, (cudaStream_t)cc->stream);
 }
 

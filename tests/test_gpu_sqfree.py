@@ -236,3 +236,30 @@ def test_sqfree_lane_encoder_matches_warp_encoder(cuda, monkeypatch, start, T, d
             s = layer * H + h
             assert np.array_equal(kl[s, start:start + T], O.sqfree_write(k32[layer, :, h], OL))
             assert np.array_equal(vl[s, start:start + T], O.sqfree_write(v32[layer, :, h], OL))
+
+
+@pytest.mark.parametrize("start,T", [(0, 96), (3, 77), (6, 1)])
+def test_sqfree_lane_read_matches_warp_read(cuda, monkeypatch, start, T):
+    """The lane-per-vector sqfree read (config 2 layout) returns the rows of
+    the warp-per-vector read (SHANNON_PRIME_SQFREE_DECODE_WARP) and of the
+    oracle, bit for bit."""
+    import torch
+    L, H, hd = 1, 2, 128
+    k, v = _inputs(9, L, H, T, hd, sigma=1.0)
+    cache = SqfreeCache(hd, L, H, 128, sk_frac=0.75)
+    cache.write_kv_tokens(0, start, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda())
+    torch.cuda.synchronize()
+    OL = O.sqfree_layout(hd, sk_k=cache.cc.sk_k, residual_bits=3, use_spinor=True)
+    for which in (0, 1):
+        outs = []
+        for warp_path in (False, True):
+            if warp_path:
+                monkeypatch.setenv("SHANNON_PRIME_SQFREE_DECODE_WARP", "1")
+            out = torch.full((T, hd), 5.0, device="cuda")
+            cache.read_batch(which, 0, 1, start, out)
+            torch.cuda.synchronize()
+            outs.append(out.cpu().numpy())
+            monkeypatch.delenv("SHANNON_PRIME_SQFREE_DECODE_WARP", raising=False)
+        np.testing.assert_array_equal(outs[0], outs[1])
+        slab = cache.slab(which).cpu().numpy()[1, start:start + T]
+        np.testing.assert_array_equal(outs[0], O.sqfree_read(slab, OL))
