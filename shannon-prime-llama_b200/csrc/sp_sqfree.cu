@@ -408,15 +408,44 @@ k_sq_encode(SpSqDev t, SqIo io)
     const int words = (t.bytes_per_pos + 3) >> 2;
     const int tb = blockIdx.x * io.tokens_per_cta;
     const int te = min(io.n_tok, tb + io.tokens_per_cta);
+    // The next vector's inputs (up to 8 per lane, head_dim <= 256) are
+    // loaded into registers while the current one is processed.
+    constexpr int KP = 8;
+    auto src_of = [&](int tk) {
+        return reinterpret_cast<const Tin *>(io.in) + (((long long)li * io.n_tok + tk) * io.nh + h) * t.hd;
+    };
+    const bool pre_ok = t.hd <= 32 * KP;
+    float pre[KP];
+    if (pre_ok && tb + warp < te) {
+        const Tin *s0 = src_of(tb + warp);
+#pragma unroll
+        for (int k = 0; k < KP; k++) pre[k] = lane + 32 * k < t.hd ? sp_load_as_float(s0, lane + 32 * k) : 0.0f;
+    }
     for (int tok = tb + warp; tok < te; tok += kSqWarps) {
-        const Tin *src = reinterpret_cast<const Tin *>(io.in) +
-                         (((long long)li * io.n_tok + tok) * io.nh + h) * t.hd;
+        const Tin *src = src_of(tok);
         // pad with the lane-tree mean
         float sum = 0.0f;
-        for (int i = lane; i < t.hd; i += 32) {
-            const float x = sp_load_as_float(src, i);
-            S.buf[i] = x;
-            sum = __fadd_rn(sum, x);
+        if (pre_ok) {
+#pragma unroll
+            for (int k = 0; k < KP; k++) {
+                const int i = lane + 32 * k;
+                if (i < t.hd) {
+                    S.buf[i] = pre[k];
+                    sum = __fadd_rn(sum, pre[k]);
+                }
+            }
+            if (tok + kSqWarps < te) {
+                const Tin *sn = src_of(tok + kSqWarps);
+#pragma unroll
+                for (int k = 0; k < KP; k++)
+                    if (lane + 32 * k < t.hd) pre[k] = sp_load_as_float(sn, lane + 32 * k);
+            }
+        } else {
+            for (int i = lane; i < t.hd; i += 32) {
+                const float x = sp_load_as_float(src, i);
+                S.buf[i] = x;
+                sum = __fadd_rn(sum, x);
+            }
         }
         const float mean = __fdiv_rn(lane_tree_reduce(sum), (float)t.hd);
         for (int i = t.hd + lane; i < t.pd; i += 32) S.buf[i] = mean;
