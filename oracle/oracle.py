@@ -2,7 +2,8 @@
 
 TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and
 bench.py's CPU-baseline legs, never by the shipped library.  See
-oracle/sp_oracle.h for what pins the restatement ("partially pinned").
+oracle/sp_oracle.h for what pins the restatement (the reference's own CUDA
+code, run on a B200: tests/golden/ref_*.npz).
 """
 from __future__ import annotations
 
@@ -312,3 +313,91 @@ def hier_fit_W(calib: np.ndarray, L: Hier, ridge: float = 1e-6) -> np.ndarray:
     A = S.T @ S + ridge * np.eye(L.n_skel)
     W = np.linalg.solve(A, S.T @ T).T
     return W.astype(np.float16)
+
+
+# ------------------------------------------------- residual stages (pinning) --
+
+def _stage_lib():
+    L = lib()
+    if not getattr(L, "_stages_bound", False):
+        L.or_sq_predict.argtypes = [C.POINTER(Sqfree), _P, _P]
+        L.or_hier_predict.argtypes = [C.POINTER(Hier), _P, _P, _P]
+        L.or_sq_spinor.argtypes = [_P, _P, C.c_int, _P, _P]
+        L.or_residual_mag.restype = C.c_float
+        L.or_residual_mag.argtypes = [_P, C.c_int]
+        for f in ("or_sq_levels", "or_hier_levels"):
+            getattr(L, f).argtypes = [_P, C.c_int, C.c_int, C.c_float, _P]
+        for f in ("or_sq_unlevels", "or_hier_unlevels"):
+            getattr(L, f).argtypes = [_P, C.c_int, C.c_int, C.c_float, _P]
+        L._stages_bound = True
+    return L
+
+
+def sq_predict(L: Sqfree, skel: np.ndarray) -> np.ndarray:
+    s = np.ascontiguousarray(skel, np.float32).reshape(-1, L.sk_k)
+    out = np.zeros((s.shape[0], L.n_res), np.float32)
+    for i in range(s.shape[0]):
+        _stage_lib().or_sq_predict(C.byref(L), s[i].ctypes.data, out[i].ctypes.data)
+    return out
+
+
+def hier_predict(L: Hier, W: np.ndarray, skel: np.ndarray) -> np.ndarray:
+    w = np.ascontiguousarray(W, np.float16).view(np.uint16)
+    s = np.ascontiguousarray(skel, np.float32).reshape(-1, L.n_skel)
+    out = np.zeros((s.shape[0], L.n_target), np.float32)
+    for i in range(s.shape[0]):
+        _stage_lib().or_hier_predict(C.byref(L), w.ctypes.data, s[i].ctypes.data,
+                                     out[i].ctypes.data)
+    return out
+
+
+def sq_spinor(actual: np.ndarray, pred: np.ndarray):
+    a = np.ascontiguousarray(actual, np.float32)
+    p = np.ascontiguousarray(pred, np.float32)
+    n = a.shape[-1]
+    dev = np.zeros_like(a)
+    sheet = np.zeros((a.shape[0], (n + 7) // 8), np.uint8)
+    for i in range(a.shape[0]):
+        _stage_lib().or_sq_spinor(a[i].ctypes.data, p[i].ctypes.data, n, dev[i].ctypes.data,
+                                  sheet[i].ctypes.data)
+    return dev, sheet
+
+
+def residual_mag(dev: np.ndarray) -> np.ndarray:
+    d = np.ascontiguousarray(dev, np.float32)
+    return np.array([_stage_lib().or_residual_mag(r.ctypes.data, d.shape[-1]) for r in d],
+                    np.float32)
+
+
+def residual_levels(dev: np.ndarray, bits: int, mag: np.ndarray, form: str) -> np.ndarray:
+    """form 'sqfree' (round-half-up of fma + 0.5, sat = mag*bits) or 'hier'
+    (rint of the fma, step from mag)."""
+    d = np.ascontiguousarray(dev, np.float32)
+    out = np.zeros(d.shape, np.uint8)
+    f = _stage_lib().or_sq_levels if form == "sqfree" else _stage_lib().or_hier_levels
+    for i in range(d.shape[0]):
+        f(d[i].ctypes.data, d.shape[-1], bits, float(mag[i]), out[i].ctypes.data)
+    return out
+
+
+def residual_unlevels(lv: np.ndarray, bits: int, mag: np.ndarray, form: str) -> np.ndarray:
+    v = np.ascontiguousarray(lv, np.uint8)
+    out = np.zeros(v.shape, np.float32)
+    f = _stage_lib().or_sq_unlevels if form == "sqfree" else _stage_lib().or_hier_unlevels
+    for i in range(v.shape[0]):
+        f(v[i].ctypes.data, v.shape[-1], bits, float(mag[i]), out[i].ctypes.data)
+    return out
+
+
+def pack_levels(lv: np.ndarray, bits: int) -> np.ndarray:
+    """LSB-first level packing, ceil(n*bits/8) bytes per row."""
+    v = np.ascontiguousarray(lv, np.uint8)
+    n = v.shape[-1]
+    nb = (n * bits + 7) // 8
+    out = np.zeros((v.shape[0], nb), np.uint8)
+    for i in range(n):
+        b = i * bits
+        out[:, b >> 3] |= (v[:, i].astype(np.uint16) << (b & 7)).astype(np.uint8)
+        if (b & 7) + bits > 8 and (b >> 3) + 1 < nb:
+            out[:, (b >> 3) + 1] |= (v[:, i] >> (8 - (b & 7))).astype(np.uint8)
+    return out

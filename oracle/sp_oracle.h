@@ -5,29 +5,33 @@
  * calls this code; only tests/, __graft_entry__.smoke() and bench.py's CPU
  * baseline legs use it, as the checker and as the timed CPU baseline.
  *
- * Parity status: PARTIALLY PINNED.  The reference CPU path (sp_shadow_*,
- * sp_band_*, sp_vht2_forward_f32, sp_mobius_mask_init in the core library
- * lib/shannon-prime) is an empty git submodule in the reference checkout
- * (.gitmodules:1-3), so it can be neither built nor run.  What pins it:
- *   - VHT2 follows the NEON restatement shannon_prime_adreno.c:270-309
- *     (unnormalised ascending-len butterfly, then x 1.0f/sqrtf(n)), which
- *     the reference's own test log reports as bit-equal to the core at
- *     hd 32/64/128 (android_build/test_adreno_phone.log:44-46);
- *   - band quantise/dequantise follow the reference kernels
- *     shannon_prime_cuda.cu:131-270 operation by operation;
- *   - known answers: packed bytes K 76 / V 50 at hd 128, K 42 / V 26 at
- *     hd 64 (shannon_prime_llama.h:336-338, shannon_prime_vulkan.c:99-105);
- *     correlation thresholds K > 0.985, V > 0.950 at hd 128
- *     (test_adreno_phone.log:50-51);
- *   - the sqfree / hierarchical restatement (sp_oracle_sqfree.c) is pinned
- *     by an independent float64 Kronecker-product Hartley matrix, a direct
- *     restatement of the Knight mask and Möbius CSR, and slot sizes.
- * The reference's own CPU and CUDA sources for this path include the absent
- * core header (shannon_prime_cuda.h:12, shannon_prime_adreno.h:12), so no
- * reference binary can be built here.
- * Unpinned: the Möbius order table itself (restated as squarefree-first,
- * ascending) and the core's tie rounding (restated as round-half-even, the
- * reference CUDA kernel's __float2int_rn).
+ * Parity status: PINNED to the reference's own CUDA code, run on a B200.
+ * The reference CPU path (sp_shadow_*, sp_band_*, sp_vht2_forward_f32,
+ * sp_mobius_mask_init in the core library lib/shannon-prime) is an empty git
+ * submodule in the reference checkout (.gitmodules:1-3), so it cannot run.
+ * The reference's CUDA sources src/backends/cuda/shannon_prime_{cuda,sqfree,
+ * hier}.cu do build, unmodified, against include/shannon_prime.h
+ * (oracle/ref/Makefile -> oracle/_ref); tests/golden/make_ref_fixtures.py
+ * ran them and tests/test_ref_fixtures.py checks this oracle against what
+ * they computed:
+ *   - band quantiser (shannon_prime_cuda.cu:131-204): bit-exact on 65,536
+ *     config-0 rows and 128 edge rows;
+ *   - the reference's whole write (:565-620) equals this quantiser on the
+ *     reference CUDA form of the VHT2 (per-stage x1/sqrt2, :37-75) bit for
+ *     bit; this oracle's VHT2 follows the CPU core's form (NEON restatement
+ *     shannon_prime_adreno.c:270-309, reported bit-equal to the core at
+ *     hd 32/64/128 in android_build/test_adreno_phone.log:44-46), and the
+ *     two forms differ in about 1e-4 of bands (fp16-scale midpoints and
+ *     half-integer ties, each checked);
+ *   - sqfree Möbius prediction, spinor choice, residual levels, packing and
+ *     dequantisation, and the hier W.skeleton product, levels and
+ *     dequantisation: bit-exact; the hier magnitude differs by <= 2 ulp (sum
+ *     order) with no level changed.
+ * Choices of the absent core that no reference code fixes (tables): the
+ * Möbius order (squarefree-first, ascending), the Knight skeleton ranking
+ * and CSR, the sqfree pad mean (true mean; the reference kernel sums warp 0
+ * only), cas tables in double (the reference uses __cosf/__sinf; agreement
+ * within 5e-5 is checked).
  */
 #ifndef SP_ORACLE_H
 #define SP_ORACLE_H
@@ -141,6 +145,16 @@ void or_hier_write_batch(int n_vecs, const float *vecs, uint8_t *out, const or_h
                          const uint16_t *W, int n_threads);
 void or_hier_read_batch(int n_vecs, const uint8_t *in, float *vecs, const or_hier_t *L,
                         const uint16_t *W, int n_threads);
+
+/* Residual stages (each checked against the reference's own kernel). */
+void  or_sq_predict(const or_sqfree_t *L, const float *sk, float *pred);
+void  or_hier_predict(const or_hier_t *L, const uint16_t *W, const float *sk, float *pred);
+void  or_sq_spinor(const float *actual, const float *pred, int n, float *dev, uint8_t *sheet);
+float or_residual_mag(const float *dev, int n);
+void  or_sq_levels(const float *dev, int n, int bits, float mag, uint8_t *lv);
+void  or_sq_unlevels(const uint8_t *lv, int n, int bits, float mag, float *dev);
+void  or_hier_levels(const float *dev, int n, int bits, float mag, uint8_t *lv);
+void  or_hier_unlevels(const uint8_t *lv, int n, int bits, float mag, float *dev);
 
 /* Pearson correlation accumulated in double. */
 double or_correlation(const float *a, const float *b, int n);

@@ -218,7 +218,7 @@ static void or_pad(const float *vec, int hd, int pd, float *out)
     for (int i = 0; i < pd; i++) out[i] = i < hd ? vec[i] : mean;
 }
 
-static void or_sq_predict(const or_sqfree_t *L, const float *sk, float *pred)
+void or_sq_predict(const or_sqfree_t *L, const float *sk, float *pred)
 {
     for (int r = 0; r < L->n_res; r++) {
         float p = 0.0f;
@@ -228,9 +228,91 @@ static void or_sq_predict(const or_sqfree_t *L, const float *sk, float *pred)
     }
 }
 
+/* Residual stages, exported so the tests can check each one against the
+ * reference's own kernels (shannon_prime_sqfree.cu:212-240, 490-530;
+ * shannon_prime_hier.cu:112-190) on identical inputs. */
+
+/* Spinor sheet choice (shannon_prime_sqfree.cu:212-240): dev = a - p unless
+ * |a + p| < |a - p|, in which case dev = a + p and the sheet bit is set.
+ * sheet[] must start zeroed. */
+void or_sq_spinor(const float *actual, const float *pred, int n, float *dev, uint8_t *sheet)
+{
+    for (int r = 0; r < n; r++) {
+        const float vp = actual[r] - pred[r], vm = actual[r] + pred[r];
+        const int use_minus = fabsf(vm) < fabsf(vp);
+        dev[r] = use_minus ? vm : vp;
+        if (use_minus) sheet[r >> 3] |= (uint8_t)(1u << (r & 7));
+    }
+}
+
+/* mean |dev| with the 1e-12 floor (shannon_prime_sqfree.cu:490-508,
+ * shannon_prime_hier.cu:112-140).  The sum runs in the lane-tree order of
+ * the B200 kernels, which may differ from the reference's 256-thread
+ * shared-memory tree in the last bit. */
+float or_residual_mag(const float *dev, int n)
+{
+    float ad[OR_SQ_MAX_PD];
+    for (int r = 0; r < n; r++) ad[r] = fabsf(dev[r]);
+    float mag = or_lane_tree_sum(ad, n) / (float)n;
+    return mag < 1e-12f ? 1e-12f : mag;
+}
+
+/* Sqfree levels (shannon_prime_sqfree.cu:514-532): sat = mag*bits,
+ * step = 2 sat/(L-1), level = (int)(dev*(1/step) + center + 0.5) with the
+ * product and sum contracted into one fma, clamped to [0, L). */
+void or_sq_levels(const float *dev, int n, int bits, float mag, uint8_t *lv)
+{
+    const int Lv = 1 << bits;
+    const float center = 0.5f * (float)(Lv - 1);
+    const float sat = mag * (float)bits;
+    const float step = (2.0f * sat) / (float)(Lv - 1);
+    const float inv = 1.0f / step;
+    for (int r = 0; r < n; r++) {
+        int level = (int)(fmaf(dev[r], inv, center) + 0.5f);
+        if (level < 0) level = 0;
+        if (level >= Lv) level = Lv - 1;
+        lv[r] = (uint8_t)level;
+    }
+}
+
+/* Sqfree deviations from levels (shannon_prime_sqfree.cu:535-548). */
+void or_sq_unlevels(const uint8_t *lv, int n, int bits, float mag, float *dev)
+{
+    const int Lv = 1 << bits;
+    const float center = 0.5f * (float)(Lv - 1);
+    const float sat = mag * (float)bits;
+    const float step = Lv > 1 ? (2.0f * sat / (float)(Lv - 1)) : 0.0f;
+    for (int r = 0; r < n; r++) dev[r] = ((float)lv[r] - center) * step;
+}
+
+/* Hier levels (shannon_prime_hier.cu:150-172): step = 2 mag/(L-1),
+ * q = rint(fma(dev, 1/step, center)), clamped. */
+void or_hier_levels(const float *dev, int n, int bits, float mag, uint8_t *lv)
+{
+    const int Lv = 1 << bits;
+    const float step = 2.0f * mag / (float)(Lv - 1);
+    const float center = (float)(Lv - 1) / 2.0f;
+    const float inv = step > 0.0f ? 1.0f / step : 0.0f;
+    for (int t = 0; t < n; t++) {
+        int q = (int)rintf(fmaf(dev[t], inv, center));
+        if (q < 0) q = 0;
+        if (q >= Lv) q = Lv - 1;
+        lv[t] = (uint8_t)q;
+    }
+}
+
+/* Hier deviations from levels (shannon_prime_hier.cu:178-192). */
+void or_hier_unlevels(const uint8_t *lv, int n, int bits, float mag, float *dev)
+{
+    const int Lv = 1 << bits;
+    const float step = 2.0f * mag / (float)(Lv - 1);
+    const float center = (float)(Lv - 1) / 2.0f;
+    for (int t = 0; t < n; t++) dev[t] = ((float)lv[t] - center) * step;
+}
+
 void or_sqfree_write(const float *vec, uint8_t *out, const or_sqfree_t *L)
 {
-    float c[OR_SQ_MAX_PD], sk[OR_SQ_MAX_PD], pred[OR_SQ_MAX_PD], dev[OR_SQ_MAX_PD], ad[OR_SQ_MAX_PD];
+    float c[OR_SQ_MAX_PD], sk[OR_SQ_MAX_PD], pred[OR_SQ_MAX_PD], act[OR_SQ_MAX_PD], dev[OR_SQ_MAX_PD];
     uint8_t lv[OR_SQ_MAX_PD];
     or_pad(vec, L->hd, L->pd, c);
     or_vilenkin(c, L->pd);
@@ -239,33 +321,14 @@ void or_sqfree_write(const float *vec, uint8_t *out, const or_sqfree_t *L)
     or_band_quantize(sk, out, &L->bands);
     if (L->n_res == 0) return;
     or_sq_predict(L, sk, pred);
-    uint8_t *sheet = out + L->bands.total_bytes + 4 + L->res_bytes;
-    for (int r = 0; r < L->n_res; r++) {
-        const float a = c[L->res_idx[r]], p = pred[r];
-        if (L->use_spinor) {
-            const float vp = a - p, vm = a + p;
-            const int use_minus = fabsf(vm) < fabsf(vp);
-            dev[r] = use_minus ? vm : vp;
-            if (use_minus) sheet[r >> 3] |= (uint8_t)(1u << (r & 7));
-        } else {
-            dev[r] = a - p;
-        }
-        ad[r] = fabsf(dev[r]);
-    }
-    float mag = or_lane_tree_sum(ad, L->n_res) / (float)L->n_res;
-    if (mag < 1e-12f) mag = 1e-12f;
+    for (int r = 0; r < L->n_res; r++) act[r] = c[L->res_idx[r]];
+    if (L->use_spinor)
+        or_sq_spinor(act, pred, L->n_res, dev, out + L->bands.total_bytes + 4 + L->res_bytes);
+    else
+        for (int r = 0; r < L->n_res; r++) dev[r] = act[r] - pred[r];
+    const float mag = or_residual_mag(dev, L->n_res);
     memcpy(out + L->bands.total_bytes, &mag, 4);
-    const int Lv = 1 << L->res_bits;
-    const float center = 0.5f * (float)(Lv - 1);
-    const float sat = mag * (float)L->res_bits;
-    const float step = (2.0f * sat) / (float)(Lv - 1);
-    const float inv = 1.0f / step;
-    for (int r = 0; r < L->n_res; r++) {
-        int level = (int)(fmaf(dev[r], inv, center) + 0.5f);
-        if (level < 0) level = 0;
-        if (level >= Lv) level = Lv - 1;
-        lv[r] = (uint8_t)level;
-    }
+    or_sq_levels(dev, L->n_res, L->res_bits, mag, lv);
     or_pack_levels(lv, L->n_res, L->res_bits, out + L->bands.total_bytes + 4, L->res_bytes);
 }
 
@@ -283,15 +346,12 @@ void or_sqfree_coeffs(const uint8_t *in, float *c, const or_sqfree_t *L)
     memcpy(&mag, in + L->bands.total_bytes, 4);
     or_unpack_levels(in + L->bands.total_bytes + 4, L->n_res, L->res_bits, lv, L->res_bytes);
     const uint8_t *sheet = in + L->bands.total_bytes + 4 + L->res_bytes;
-    const int Lv = 1 << L->res_bits;
-    const float center = 0.5f * (float)(Lv - 1);
-    const float sat = mag * (float)L->res_bits;
-    const float step = Lv > 1 ? (2.0f * sat / (float)(Lv - 1)) : 0.0f;
+    float dev[OR_SQ_MAX_PD];
+    or_sq_unlevels(lv, L->n_res, L->res_bits, mag, dev);
     for (int r = 0; r < L->n_res; r++) {
-        const float dev = ((float)lv[r] - center) * step;
         float p = pred[r];
         if (L->use_spinor && (sheet[r >> 3] >> (r & 7) & 1)) p = -p;
-        c[L->res_idx[r]] = p + dev;
+        c[L->res_idx[r]] = p + dev[r];
     }
 }
 
@@ -386,7 +446,7 @@ int or_hier_layout(or_hier_t *L, int hd, int n_bands, const int *bits, int resid
     return 0;
 }
 
-static void or_hier_predict(const or_hier_t *L, const uint16_t *W, const float *sk, float *pred)
+void or_hier_predict(const or_hier_t *L, const uint16_t *W, const float *sk, float *pred)
 {
     for (int t = 0; t < L->n_target; t++) {
         float acc = 0.0f;
@@ -398,30 +458,17 @@ static void or_hier_predict(const or_hier_t *L, const uint16_t *W, const float *
 
 void or_hier_write(const float *vec, uint8_t *out, const or_hier_t *L, const uint16_t *W)
 {
-    float c[OR_SQ_MAX_PD], pred[OR_SQ_MAX_PD], dev[OR_SQ_MAX_PD], ad[OR_SQ_MAX_PD];
+    float c[OR_SQ_MAX_PD], pred[OR_SQ_MAX_PD], dev[OR_SQ_MAX_PD];
     uint8_t lv[OR_SQ_MAX_PD];
     or_pad(vec, L->hd, L->pd, c);
     or_vilenkin(c, L->pd);
     memset(out, 0, (size_t)L->bytes_per_pos);
     or_band_quantize(c, out, &L->bands);              /* skeleton = c[0 .. n_skel) */
     or_hier_predict(L, W, c, pred);
-    for (int t = 0; t < L->n_target; t++) {
-        dev[t] = c[L->n_skel + t] - pred[t];
-        ad[t] = fabsf(dev[t]);
-    }
-    float mag = or_lane_tree_sum(ad, L->n_target) / (float)L->n_target;
-    if (mag < 1e-12f) mag = 1e-12f;
+    for (int t = 0; t < L->n_target; t++) dev[t] = c[L->n_skel + t] - pred[t];
+    const float mag = or_residual_mag(dev, L->n_target);
     memcpy(out + L->bands.total_bytes, &mag, 4);
-    const int Lv = 1 << L->res_bits;
-    const float step = 2.0f * mag / (float)(Lv - 1);
-    const float center = (float)(Lv - 1) / 2.0f;
-    const float inv = step > 0.0f ? 1.0f / step : 0.0f;
-    for (int t = 0; t < L->n_target; t++) {
-        int q = (int)rintf(fmaf(dev[t], inv, center));
-        if (q < 0) q = 0;
-        if (q >= Lv) q = Lv - 1;
-        lv[t] = (uint8_t)q;
-    }
+    or_hier_levels(dev, L->n_target, L->res_bits, mag, lv);
     or_pack_levels(lv, L->n_target, L->res_bits, out + L->bands.total_bytes + 4, L->res_bytes);
 }
 
@@ -434,10 +481,9 @@ void or_hier_read(const uint8_t *in, float *vec, const or_hier_t *L, const uint1
     float mag;
     memcpy(&mag, in + L->bands.total_bytes, 4);
     or_unpack_levels(in + L->bands.total_bytes + 4, L->n_target, L->res_bits, lv, L->res_bytes);
-    const int Lv = 1 << L->res_bits;
-    const float step = 2.0f * mag / (float)(Lv - 1);
-    const float center = (float)(Lv - 1) / 2.0f;
-    for (int t = 0; t < L->n_target; t++) c[L->n_skel + t] = pred[t] + ((float)lv[t] - center) * step;
+    float dev[OR_SQ_MAX_PD];
+    or_hier_unlevels(lv, L->n_target, L->res_bits, mag, dev);
+    for (int t = 0; t < L->n_target; t++) c[L->n_skel + t] = pred[t] + dev[t];
     or_vilenkin(c, L->pd);
     memcpy(vec, c, sizeof(float) * (size_t)L->hd);
 }
