@@ -615,6 +615,33 @@ def run_ours(args):
         h2d = hq.numel() * 2 + (out.numel() * 2 if ws > 1 else 0)
         d2h = hout.numel() * 2 * (ws if ws > 1 else 1)
 
+    # Multi-GPU correctness, once after timing: the gathered rows of every
+    # rank against each rank's own local decode of its shard (bit-exact).
+    gather_check = None
+    if ws > 1:
+        L.sp_cuda_attn_decode(cc, 0, N_LAYERS, q.data_ptr(), nq_local, CTX, 1.0,
+                              out.data_ptr(), -1, stream.cuda_stream)
+        stream.synchronize()
+        locs = [torch.empty_like(out) for _ in range(ws)]
+        dist.all_gather(locs, out)
+        if gather is not None:
+            gather.decode(cc, 0, N_LAYERS, q, nq_local, CTX, dst_layer, dst_qhead, 1.0, -1, stream)
+            stream.synchronize()
+            got = gather.out
+        else:
+            step()
+            torch.cuda.synchronize()
+            got = torch.empty(N_LAYERS, N_Q, HD, dtype=torch.float16, device=dev)
+            for r in range(ws):
+                got[:, [h * G + g for h in range(N_KV) if h % ws == r for g in range(G)]] = gathered[r]
+        expect = torch.empty(N_LAYERS, N_Q, HD, dtype=torch.float16, device=dev)
+        for r in range(ws):
+            expect[:, [h * G + g for h in range(N_KV) if h % ws == r for g in range(G)]] = locs[r]
+        bad = torch.tensor([float((got != expect).any(dim=-1).sum())], device=dev)
+        dist.all_reduce(bad, op=dist.ReduceOp.SUM)
+        gather_check = {"rows": N_LAYERS * N_Q * ws, "mismatches": int(bad.item()),
+                        "what": "gathered rows on every rank vs the owning rank's local decode, bit-exact"}
+
     # Ship-path compression throughput: re-compress 4 full layers (K and V,
     # fp32 in, 1.07 GB of inputs > L2) through the token-major entry point.
     def compress_pass():
@@ -732,6 +759,8 @@ def run_ours(args):
                  "workload": "layer 0, %d KV heads x K and V, %d positions, fp32 [pos][128] out" % (H, CTX)},
         "cache_fill_s": t_fill,
     }
+    if gather_check is not None:
+        line["gather_check"] = gather_check
     if cpu is not None:
         line["cpu_baseline"] = cpu
     if not args.no_extra:

@@ -180,7 +180,12 @@ int  sp_cuda_kq_scores(const void *d_packed, int total_bytes_per_pos, int is_v, 
  *   32-head model per call); larger requests return SP_ERR_ARG.
  *   The first call on each device looks up the array's device address
  *   (cudaGetSymbolAddress); make it before any stream capture.  All calls
- *   share the array, so calls that overlap on the GPU race: serialise them. */
+ *   share the array, so calls that overlap on the GPU race: serialise them.
+ *   The addresses are kept for the life of the process: a cudaDeviceReset
+ *   after the first call on a device is not supported.
+ *   Failures inside the kernels (a bounded copy wait that ran out) set bit 0
+ *   of a status word that all calls on the device share, like the array;
+ *   read it with sp_cuda_attn_decode_noalloc_status. */
 int  sp_cuda_attn_decode_noalloc(const void *d_k_cache, const void *d_v_cache,
                                  int max_seq_len, const sp_band_config_t *k_bands,
                                  const sp_band_config_t *v_bands,
@@ -188,6 +193,10 @@ int  sp_cuda_attn_decode_noalloc(const void *d_k_cache, const void *d_v_cache,
                                  int layer0, int n_layers, const void *d_q,
                                  int n_q_heads, int kv_len, float logit_scale,
                                  void *d_out, int max_bands, void *stream);
+/* New: the shared status word of sp_cuda_attn_decode_noalloc on the current
+ * device, read after the stream's work (synchronises `stream`); clear != 0
+ * resets it to 0 afterwards.  Allocates nothing. */
+int  sp_cuda_attn_decode_noalloc_status(unsigned int *status_out, int clear, void *stream);
 
 /* ------------------------------------------------- sqfree + spinor cache -- */
 /* Replaces reference sp_cuda_sqfree_cache_t (shannon_prime_cuda.h:153-230,
@@ -364,6 +373,16 @@ int  sp_cuda_hier_read_kv_tokens(const sp_cuda_hier_cache_t *hc, int layer0, int
  * buffer.  A final kernel waits (bounded, 2 s) until all `world` slots of this
  * rank's own flag array reach `epoch`; stream work after the call sees the
  * whole gathered output.
+ *   epoch_stride   bytes between two copies of the gathered rows in each
+ *                  buffer: the rows of call `epoch` start at byte
+ *                  (epoch & 1) * epoch_stride.  With two copies a rank may
+ *                  issue call e+1 while a slower rank still reads call e's
+ *                  rows (each rank's reads of call e must be stream-ordered
+ *                  before its own call e+1, which is what raises its flag
+ *                  for e+1, and no rank passes call e+1's wait before all
+ *                  flags show e+1).  0 = one copy: the caller must then keep
+ *                  every rank from starting call e+1 until all ranks have
+ *                  consumed call e (a barrier).
  *   d_local_buf    this rank's gather buffer
  *   d_peer_bufs    device array [world] of every rank's buffer as mapped in
  *                  this process (its own at index rank), e.g. from CUDA IPC or
@@ -376,7 +395,8 @@ int sp_cuda_attn_decode_allgather(const sp_cuda_cache_t *cc, int layer0, int n_l
                                   int n_q_heads, int kv_len, float logit_scale, int max_bands,
                                   void *d_local_buf, void *const *d_peer_bufs, const int *d_dst_layer,
                                   const int *d_dst_qhead, int n_q_heads_total, long long flags_offset,
-                                  int rank, int world, unsigned int epoch, void *stream);
+                                  long long epoch_stride, int rank, int world, unsigned int epoch,
+                                  void *stream);
 
 /* ---------------------------------------------------------------------------
  * Cold storage: per-layer pinned host mirror of a cache slab (the warm tier

@@ -280,6 +280,34 @@ extern "C" float sp_cuda_attn_last_kernel_ms(void)
 
 extern "C" int sp_cuda_attn_last_splits(void) { return g_prof_splits; }
 
+// Kernel choice and split chunking of a filled SpAttnArgs, shared by every
+// decode entry point.  `aligned`: the caches and their slot stride allow the
+// tensor-core kernel's 16-byte aligned bulk copies of 16-position tiles.
+static int attn_plan(SpAttnArgs &a, bool aligned, bool &use_mma)
+{
+    use_mma = aligned && g_force_impl != 1 && sp_attn_mma_supported(a) == SP_OK;
+    if (g_force_impl == 2 && !use_mma)
+        return sp_set_error(SP_ERR_UNSUPPORTED, "attn_decode: tensor-core path does not support this layout");
+
+    // Chunking: enough CTAs to fill the 148 SMs several times over, chunks of
+    // at least kAttnMinChunk tokens, at most kAttnMaxSplits chunks.
+    const int units = a.n_layers * a.n_kv_heads;
+    const int target_ctas = use_mma ? 148 * 4 : 148 * 8;
+    int splits = (target_ctas + units - 1) / units;
+    const int max_by_len = (a.kv_len + kAttnMinChunk - 1) / kAttnMinChunk;
+    if (splits > max_by_len) splits = max_by_len;
+    if (splits > kAttnMaxSplits) splits = kAttnMaxSplits;
+    if (splits < 1) splits = 1;
+    int chunk = (a.kv_len + splits - 1) / splits;
+    chunk = (chunk + 15) & ~15;
+    if (chunk < 16) chunk = 16;
+    a.chunk = chunk;
+    a.n_splits = a.kv_len == 0 ? 0 : (a.kv_len + chunk - 1) / chunk;
+    if (a.n_splits > kAttnMaxSplits)
+        return sp_set_error(SP_ERR_ARG, "attn_decode: too many splits");
+    return SP_OK;
+}
+
 // Validate a decode call and fill its kernel arguments and split chunking.
 static int attn_prepare(const sp_cuda_cache_t *cc, int layer0, int n_layers, const void *d_q, int n_q_heads,
                         int kv_len, float logit_scale, int max_bands, SpAttnArgs &a, bool &use_mma)
@@ -317,27 +345,7 @@ static int attn_prepare(const sp_cuda_cache_t *cc, int layer0, int n_layers, con
     a.inv_sqrt_n = sp_inv_sqrt_n(cc->config.head_dim);
     a.status = cc->d_status;
 
-    use_mma = g_force_impl != 1 && sp_attn_mma_supported(a) == SP_OK;
-    if (g_force_impl == 2 && !use_mma)
-        return sp_set_error(SP_ERR_UNSUPPORTED, "attn_decode: tensor-core path does not support this layout");
-
-    // Chunking: enough CTAs to fill the 148 SMs several times over, chunks of
-    // at least kAttnMinChunk tokens, at most kAttnMaxSplits chunks.
-    const int units = n_layers * H;
-    const int target_ctas = use_mma ? 148 * 4 : 148 * 8;
-    int splits = (target_ctas + units - 1) / units;
-    const int max_by_len = (kv_len + kAttnMinChunk - 1) / kAttnMinChunk;
-    if (splits > max_by_len) splits = max_by_len;
-    if (splits > kAttnMaxSplits) splits = kAttnMaxSplits;
-    if (splits < 1) splits = 1;
-    int chunk = (kv_len + splits - 1) / splits;
-    chunk = (chunk + 15) & ~15;
-    if (chunk < 16) chunk = 16;
-    a.chunk = chunk;
-    a.n_splits = kv_len == 0 ? 0 : (kv_len + chunk - 1) / chunk;
-    if (a.n_splits > kAttnMaxSplits)
-        return sp_set_error(SP_ERR_ARG, "attn_decode: too many splits");
-    return SP_OK;
+    return attn_plan(a, true, use_mma);
 }
 
 // Main kernel(s) and the combine of a prepared call.
@@ -415,8 +423,8 @@ extern "C" int sp_cuda_attn_decode_allgather(const sp_cuda_cache_t *cc, int laye
                                              const void *d_q, int n_q_heads, int kv_len, float logit_scale,
                                              int max_bands, void *d_local_buf, void *const *d_peer_bufs,
                                              const int *d_dst_layer, const int *d_dst_qhead, int n_q_heads_total,
-                                             long long flags_offset, int rank, int world, unsigned int epoch,
-                                             void *stream)
+                                             long long flags_offset, long long epoch_stride, int rank, int world,
+                                             unsigned int epoch, void *stream)
 {
     sp_clear_error();
     if (!d_local_buf || !d_peer_bufs || !d_dst_layer || !d_dst_qhead)
@@ -426,6 +434,8 @@ extern "C" int sp_cuda_attn_decode_allgather(const sp_cuda_cache_t *cc, int laye
                             n_q_heads, n_q_heads_total);
     if (flags_offset < 0 || (flags_offset & 3))
         return sp_set_error(SP_ERR_ARG, "attn_decode_allgather: flags_offset must be a non-negative multiple of 4");
+    if (epoch_stride < 0 || (epoch_stride & 15))
+        return sp_set_error(SP_ERR_ARG, "attn_decode_allgather: epoch_stride must be a non-negative multiple of 16");
     SpAttnArgs a;
     bool use_mma = false;
     int rc = attn_prepare(cc, layer0, n_layers, d_q, n_q_heads, kv_len, logit_scale, max_bands, a, use_mma);
@@ -435,6 +445,7 @@ extern "C" int sp_cuda_attn_decode_allgather(const sp_cuda_cache_t *cc, int laye
     a.g.dst_qhead = d_dst_qhead;
     a.g.n_q_total = n_q_heads_total;
     a.g.flags_offset = flags_offset;
+    a.g.rows_offset = (epoch & 1u) ? epoch_stride : 0;
     a.g.rank = rank;
     a.g.world = world;
     a.g.epoch = epoch;
@@ -473,23 +484,52 @@ extern "C" int sp_cuda_attn_decode_allgather(const sp_cuda_cache_t *cc, int laye
 
 static __device__ __align__(256) unsigned char g_attn_static_scratch[SP_ATTN_STATIC_SCRATCH_BYTES];
 
-static void *g_static_ws_addr[128];       // per-device address, set once
+// Error word of the allocation-free decode, shared by every call on a device
+// like the scratch: bit 0 is set when a bounded copy wait of the tensor-core
+// kernel ran out (that warp's tiles are then missing from the output).
+// sp_cuda_attn_decode_noalloc_status reads and optionally clears it.
+static __device__ unsigned int g_attn_static_status;
 
-static int static_scratch_address(void **out)
+static void *g_static_ws_addr[128];       // per-device addresses, set once
+static void *g_static_status_addr[128];
+
+// The device addresses are looked up once per device and kept for the life
+// of the process; a cudaDeviceReset after the first call on a device is not
+// supported (the module's memory, and so the cached addresses, go away).
+static int static_scratch_address(void **out, unsigned int **status)
 {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128)
         return sp_set_error(SP_ERR_CUDA, "attn_decode_noalloc: no current CUDA device");
     void *p = __atomic_load_n(&g_static_ws_addr[dev], __ATOMIC_ACQUIRE);
-    if (!p) {
+    void *st = __atomic_load_n(&g_static_status_addr[dev], __ATOMIC_ACQUIRE);
+    if (!p || !st) {
         cudaError_t e = cudaGetSymbolAddress(&p, g_attn_static_scratch);
-        if (e != cudaSuccess || !p)
+        if (e == cudaSuccess) e = cudaGetSymbolAddress(&st, g_attn_static_status);
+        if (e != cudaSuccess || !p || !st)
             return sp_set_error(SP_ERR_CUDA, "attn_decode_noalloc: cudaGetSymbolAddress: %s",
                                 cudaGetErrorString(e));
+        __atomic_store_n(&g_static_status_addr[dev], st, __ATOMIC_RELEASE);
         __atomic_store_n(&g_static_ws_addr[dev], p, __ATOMIC_RELEASE);
     }
     *out = p;
+    *status = (unsigned int *)st;
     return SP_OK;
+}
+
+extern "C" int sp_cuda_attn_decode_noalloc_status(unsigned int *status_out, int clear, void *stream)
+{
+    sp_clear_error();
+    if (!status_out) return sp_set_error(SP_ERR_ARG, "attn_decode_noalloc_status: NULL argument");
+    void *ws = nullptr;
+    unsigned int *st = nullptr;
+    int rc = static_scratch_address(&ws, &st);
+    if (rc) return rc;
+    cudaStream_t s = (cudaStream_t)stream;
+    cudaError_t e = cudaMemcpyAsync(status_out, st, sizeof(unsigned int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess && clear) e = cudaMemsetAsync(st, 0, sizeof(unsigned int), s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    return sp_check_cuda(e, "attn_decode_noalloc_status");
 }
 
 extern "C" int sp_cuda_attn_decode_noalloc(const void *d_k_cache, const void *d_v_cache,
@@ -523,7 +563,8 @@ extern "C" int sp_cuda_attn_decode_noalloc(const void *d_k_cache, const void *d_
                             (unsigned long long)SP_ATTN_STATIC_SCRATCH_BYTES /
                                 (kAttnMaxSplits * sp_attn_partial_stride(n) * sizeof(float)), n);
     void *ws = nullptr;
-    int rc = static_scratch_address(&ws);
+    unsigned int *status = nullptr;
+    int rc = static_scratch_address(&ws, &status);
     if (rc) return rc;
 
     SpAttnArgs a;
@@ -545,45 +586,13 @@ extern "C" int sp_cuda_attn_decode_noalloc(const void *d_k_cache, const void *d_
     a.nb_v = (max_bands < 0 || max_bands >= a.vl.n_bands) ? a.vl.n_bands : max_bands;
     a.logit_scale = logit_scale;
     a.inv_sqrt_n = sp_inv_sqrt_n(n);
-    a.status = nullptr;
+    a.status = status;
 
     // The tensor-core kernel stages 16-position tiles with bulk copies, which
     // need 16-byte aligned tile starts; other layouts take the generic kernel.
     const bool aligned = ((uintptr_t)d_k_cache % 16 == 0) && ((uintptr_t)d_v_cache % 16 == 0) &&
                          (max_seq_len % 16 == 0);
-    const bool use_mma = aligned && g_force_impl != 1 && sp_attn_mma_supported(a) == SP_OK;
-    cudaStream_t s = (cudaStream_t)stream;
-    const int units = n_layers * n_heads_kv;
-    const int target_ctas = use_mma ? 148 * 4 : 148 * 8;
-    int splits = (target_ctas + units - 1) / units;
-    const int max_by_len = (kv_len + kAttnMinChunk - 1) / kAttnMinChunk;
-    if (splits > max_by_len) splits = max_by_len;
-    if (splits > kAttnMaxSplits) splits = kAttnMaxSplits;
-    if (splits < 1) splits = 1;
-    int chunk = (kv_len + splits - 1) / splits;
-    chunk = (chunk + 15) & ~15;
-    if (chunk < 16) chunk = 16;
-    a.chunk = chunk;
-    a.n_splits = kv_len == 0 ? 0 : (kv_len + chunk - 1) / chunk;
-
-    if (use_mma && kv_len > 0) return sp_attn_mma_launch(a, s);
-    if (a.n_splits > 0) {
-        {
-            switch (n) {
-            case 32:  rc = launch_generic<1>(a, s); break;
-            case 64:  rc = launch_generic<2>(a, s); break;
-            case 128: rc = launch_generic<4>(a, s); break;
-            case 256: rc = launch_generic<8>(a, s); break;
-            default:  rc = launch_generic<16>(a, s); break;
-            }
-        }
-        if (rc) return rc;
-    }
-    switch (n) {
-    case 32:  return launch_combine<1>(a, s);
-    case 64:  return launch_combine<2>(a, s);
-    case 128: return launch_combine<4>(a, s);
-    case 256: return launch_combine<8>(a, s);
-    default:  return launch_combine<16>(a, s);
-    }
+    bool use_mma = false;
+    if ((rc = attn_plan(a, aligned, use_mma))) return rc;
+    return attn_launch(a, use_mma, (cudaStream_t)stream);
 }

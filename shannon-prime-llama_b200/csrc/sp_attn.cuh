@@ -20,6 +20,7 @@ struct SpGather {
     const int *dst_qhead;               // [n_q_heads] destination query-head column
     int n_q_total;                      // query heads per destination layer row
     long long flags_offset;             // bytes: [world] uint32 flags in each buffer
+    long long rows_offset;              // bytes: this call's copy of the rows in each buffer
     int rank, world;
     unsigned int epoch;
     unsigned int *block_count;          // device counter, zero between calls
@@ -59,7 +60,8 @@ __device__ __forceinline__ void sp_attn_store_row(const SpAttnArgs &a, int li, i
     }
     const long long off = ((long long)a.g.dst_layer[li] * a.g.n_q_total + a.g.dst_qhead[qh]) * n + lane * E;
     for (int p = 0; p < a.g.world; p++) {
-        __half *o = reinterpret_cast<__half *>(a.g.peers[p]) + off;
+        __half *o = reinterpret_cast<__half *>(reinterpret_cast<unsigned char *>(a.g.peers[p]) +
+                                               a.g.rows_offset) + off;
         if constexpr (E == 4) {
             uint2 w;
             w.x = (uint32_t)__half_as_ushort(h[0]) | ((uint32_t)__half_as_ushort(h[1]) << 16);

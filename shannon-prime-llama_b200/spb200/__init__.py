@@ -142,11 +142,12 @@ SIGNATURES = {
     "sp_cuda_read_batch_partial": (_I, [_CC, _I, _I, _I, _I, _I, _P, _I]),
     "sp_cuda_attn_decode": (_I, [_CC, _I, _I, _P, _I, _I, _F, _P, _I, _P]),
     "sp_cuda_attn_decode_allgather": (_I, [_CC, _I, _I, _P, _I, _I, _F, _I, _P, _P, _P, _P, _I, C.c_longlong,
-                                           _I, _I, C.c_uint, _P]),
+                                           C.c_longlong, _I, _I, C.c_uint, _P]),
     "sp_cuda_kq_scores": (_I, [_P, _I, _I, _I, _I, _P, _I, C.c_longlong, _I, _P, C.c_longlong, _P]),
     "sp_cuda_attn_decode_noalloc": (_I, [_P, _P, _I, C.POINTER(SpBandConfig),
                                          C.POINTER(SpBandConfig), _P, _I, _I, _I, _P, _I, _I,
                                          _F, _P, _I, _P]),
+    "sp_cuda_attn_decode_noalloc_status": (_I, [C.POINTER(C.c_uint), _I, _P]),
     "sp_cuda_sqfree_cache_init": (_I, [C.POINTER(SpSqfreeCache), C.POINTER(SpConfig), _I, _I, _I, _P]),
     "sp_cuda_sqfree_cache_init_ex": (_I, [C.POINTER(SpSqfreeCache), C.POINTER(SpConfig), _I, _I, _I,
                                           _F, _P]),

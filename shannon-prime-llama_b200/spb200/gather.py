@@ -1,7 +1,10 @@
 """Peer-memory gather buffers for the fused decode + all-gather
 (sp_cuda_attn_decode_allgather): one symmetric-memory buffer per rank holding
-the gathered fp16 outputs [n_rows][n_q_total][head_dim] followed by a
-[32] uint32 flag array, mapped into every rank of the group.
+two copies of the gathered fp16 outputs [n_rows][n_q_total][head_dim] (odd
+and even epochs) followed by a [32] uint32 flag array, mapped into every rank
+of the group.  With two copies a rank may start the next call while a slower
+rank still reads the current one, as long as each rank's reads are
+stream-ordered before its own next call.
 
 The caller allocates it once per (shape, group), then passes `peers_dev`
 (device array of every rank's buffer address), the buffer's own address,
@@ -31,7 +34,8 @@ class PeerGather:
             raise ValueError(f"world {self.world} > {MAX_WORLD}")
         self.shape = (n_rows, n_q_total, head_dim)
         out_bytes = n_rows * n_q_total * head_dim * 2
-        self.flags_offset = (out_bytes + 255) // 256 * 256
+        self.epoch_stride = (out_bytes + 255) // 256 * 256
+        self.flags_offset = 2 * self.epoch_stride
         self.buf = symm.empty(self.flags_offset + 4 * MAX_WORLD, dtype=torch.uint8, device=device)
         self.buf.zero_()
         torch.cuda.synchronize(device)
@@ -39,8 +43,14 @@ class PeerGather:
         dist.barrier(group=self.group)          # every rank's flags are zero before any call
         torch.cuda.synchronize(device)
         self.peers_dev = int(self.hdl.buffer_ptrs_dev)
-        self.out = self.buf[:out_bytes].view(torch.float16).view(*self.shape)
+        self._copies = [self.buf[c * self.epoch_stride:c * self.epoch_stride + out_bytes]
+                        .view(torch.float16).view(*self.shape) for c in range(2)]
         self.epoch = 0
+
+    @property
+    def out(self):
+        """The gathered rows of the latest call (epoch)."""
+        return self._copies[self.epoch & 1]
 
     def decode(self, cc, layer0: int, n_layers: int, q, n_q_heads: int, kv_len: int, dst_layer, dst_qhead,
                logit_scale: float = 1.0, max_bands: int = -1, stream=None) -> None:
@@ -52,5 +62,6 @@ class PeerGather:
         rc = lib().sp_cuda_attn_decode_allgather(
             cc, layer0, n_layers, q.data_ptr(), n_q_heads, kv_len, logit_scale, max_bands,
             self.buf.data_ptr(), self.peers_dev, dst_layer.data_ptr(), dst_qhead.data_ptr(),
-            self.shape[1], self.flags_offset, self.rank, self.world, C.c_uint(self.epoch & 0xffffffff), s)
+            self.shape[1], self.flags_offset, self.epoch_stride, self.rank, self.world,
+            C.c_uint(self.epoch & 0xffffffff), s)
         check(rc, "sp_cuda_attn_decode_allgather")

@@ -4,9 +4,13 @@ against each rank's own single-GPU decode of the same shard.
 
 Cache: 3 layers x 8 KV heads x hd 128, 700 positions (a partial last tile),
 4 query heads per KV head; rank r owns KV heads h % world == r.  Every rank
-checks, for three consecutive calls (epochs 1..3), that every row of its
-gathered buffer equals (bit for bit) the owning rank's local decode, and
-that the cache's status word stays clear."""
+checks, for three consecutive calls (epochs 1..3) with a barrier between
+them, that every row of its gathered buffer equals (bit for bit) the owning
+rank's local decode; then for eight calls issued back to back with no
+barrier or host synchronisation between them, each with different queries,
+and with one rank delayed by a spin on its stream, that every call's rows
+(copied out on the stream right after the call) are right; and that the
+cache's status word stays clear."""
 import os
 import sys
 
@@ -59,6 +63,35 @@ def main():
             print(f"rank {rank} epoch {pg.epoch}: mismatch at {bad}", flush=True)
             sys.exit(1)
         dist.barrier()
+    # back to back: queries differ per call, so a late overwrite would show
+    n_bb = 8
+    qs = [(q.float() * (1.0 + 0.07 * e)).half() for e in range(n_bb)]
+    expects = []
+    for e in range(n_bb):
+        loc = torch.empty_like(local)
+        cache.attn_decode(0, L, qs[e], T, loc, logit_scale=0.8)
+        rows = [torch.empty_like(loc) for _ in range(world)]
+        dist.all_gather(rows, loc)
+        ex = torch.empty(L, H * G, HD, dtype=torch.float16, device=dev)
+        for r in range(world):
+            cols = [h * G + g for h in range(H) if h % world == r for g in range(G)]
+            ex[:, cols] = rows[r]
+        expects.append(ex)
+    torch.cuda.synchronize()
+    dist.barrier()
+    got = []
+    for e in range(n_bb):
+        if rank == 1 and e % 3 == 1:
+            torch.cuda._sleep(2_000_000)        # this rank lags behind on its stream
+        pg.decode(C_byref(cache), 0, L, qs[e], len(qcols), T, dst_layer, dst_qhead, logit_scale=0.8)
+        got.append(pg.out.clone())
+    torch.cuda.synchronize()
+    for e in range(n_bb):
+        if not torch.equal(got[e], expects[e]):
+            bad = (got[e] != expects[e]).nonzero()[:5].tolist()
+            print(f"rank {rank} back-to-back call {e}: mismatch at {bad}", flush=True)
+            sys.exit(1)
+    dist.barrier()
     status = torch.zeros(4, dtype=torch.int32)
     spb200.lib().sp_cuda_d2h_async(status.data_ptr(), cache.cc.d_status, 16, None)
     torch.cuda.synchronize()

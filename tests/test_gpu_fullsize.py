@@ -7,9 +7,12 @@ size-independent properties (the CPU oracle only sees sampled slots):
   codes bit-exact with the oracle's writer, and a repeated decode bit-identical;
 - config 3 shape, one layer (4 KV heads x 131072 positions, 8 query heads per
   KV head): tensor-core against SIMT decode and one oracle head;
-- config 2 (sqfree, 16384 positions): blocked against register decode;
+- config 2 (sqfree, 16384 positions): blocked against register decode, a
+  sampled slot's bytes bit-exact with the oracle's writer and a sampled
+  head's decode against the oracle's attention over all 16384 positions;
 - config 4 (hier, 8192 positions x 16 heads): tensor-core batched read against
-  the exact SIMT read.
+  the exact SIMT read, a sampled slot's bytes bit-exact with the oracle's
+  writer and its tensor-core read against the oracle's read.
 
 Tolerance: relative L2 <= 1e-3 per output, as in the small-size tests."""
 import numpy as np
@@ -105,9 +108,12 @@ def test_config2_sqfree_full_length(cuda, monkeypatch):
     cache = SqfreeCache(n, L, H, T, sk_frac=0.75)
     gen = torch.Generator(device="cuda")
     gen.manual_seed(2)
+    kept = None
     for layer in range(L):
         k, v = synth.kv_layer_torch(gen, T, H, n)
         cache.write_kv_tokens(layer, 0, k.unsqueeze(0), v.unsqueeze(0))
+        if layer == 1:
+            kept = (k[:, 3].cpu().numpy(), v[:, 3].cpu().numpy())
     q = torch.from_numpy(synth.q_np(2, L, H * G, n, 1.0 / np.sqrt(n))).cuda()
     outs = []
     for reg in (False, True):
@@ -119,6 +125,15 @@ def test_config2_sqfree_full_length(cuda, monkeypatch):
         outs.append(out.float().cpu().numpy())
     for layer in range(L):
         assert _rel(outs[0][layer], outs[1][layer]) <= RTOL
+    OL = O.sqfree_layout(n, sk_k=cache.cc.sk_k)
+    ks, vs = cache.slab(0).cpu().numpy(), cache.slab(1).cpu().numpy()
+    slot = 1 * H + 3
+    assert np.array_equal(ks[slot, :T], O.sqfree_write(kept[0], OL))
+    assert np.array_equal(vs[slot, :T], O.sqfree_write(kept[1], OL))
+    h = 3
+    ref = O.sqfree_attn_decode(ks[slot:slot + 1], vs[slot:slot + 1], OL, OL,
+                               q.cpu().numpy()[1, h * G:(h + 1) * G], T, 1.0)
+    assert _rel(outs[0][1, h * G:(h + 1) * G], ref) <= RTOL
 
 
 def test_config4_hier_full_length(cuda, monkeypatch):
@@ -145,3 +160,9 @@ def test_config4_hier_full_length(cuda, monkeypatch):
         outs.append(ko.cpu().numpy())
     for h in range(H):
         assert _rel(outs[0][0, :, h], outs[1][0, :, h]) <= RTOL, h
+    h = 7
+    kh = k[:, h].float().cpu().numpy()
+    packed = cache.slab(0).cpu().numpy()[h, :T]
+    assert np.array_equal(packed, O.hier_write(kh, OL, W[h]))
+    ref = O.hier_read(packed, OL, W[h])
+    assert _rel(outs[0][0, :, h], ref) <= RTOL
