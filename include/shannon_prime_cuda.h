@@ -55,7 +55,8 @@ typedef struct {
     int              max_seq_len;
     int             *d_mobius_order; /* [head_dim] forward permutation (NULL: Möbius off) */
     int             *d_mobius_inv;   /* [head_dim] inverse permutation */
-    float           *d_scratch;      /* [head_dim] kept for layout compatibility; unused */
+    float           *d_scratch;      /* at least [head_dim] floats (the reference's size); here the
+                                        fp16 query/output staging of sp_ggml_attn_decode */
     void            *stream;
 
     /* --- B200 build additions --- */
@@ -438,6 +439,32 @@ int  sp_cuda_cold_restore(const sp_cuda_cold_layer_t *cl, void *d_packed, int n_
 /* Async copies of arbitrary buffers on `stream`. */
 void sp_cuda_d2h_async(void *dst_host, const void *src_device, int64_t n_bytes, void *stream);
 void sp_cuda_h2d_async(void *dst_device, const void *src_host, int64_t n_bytes, void *stream);
+
+/* ---------------------------------------------------------------------------
+ * Disk tier: save / load of a ship cache's compressed slabs, replacing the
+ * engine's KvCache::save_to_disk / load_from_disk / load_from_disk_partial
+ * (src/engine/kv_cache.h:133-147, kv_cache.cpp:1535-1585, which call the
+ * core's sp_shadow_cache_save / _load / _load_partial, CHANGELOG.md:41-61).
+ * One file per layer, {prefix}.L{layer}.bin: a 64-byte header ("VHT2",
+ * version, model hash, n_pos, shape and band layout, header checksum), then
+ * the layer's K rows and V rows of positions [0, n_pos):
+ *   version 2  per-vector interleaved ([head][pos][row bytes]);
+ *   version 3  band-major ([band][head][pos][band bytes]), so a partial load
+ *              reads only the first max_bands bands from disk.
+ * model_hash: the caller's FNV-1a 64 hash of the model path (sp_fnv1a64).
+ * Loads check the header against the cache's shape and layout, and the hash
+ * strictly unless SP_DISK_HASH_STRICT=0 (then a mismatch only warns).
+ * Save returns 0; load returns n_pos; errors return a negative SP_ERR_*.
+ * Synchronous on the cache's stream; staging buffers are allocated per call. */
+uint64_t sp_fnv1a64(const void *data, size_t n);
+int sp_cuda_cache_save(const sp_cuda_cache_t *cc, const char *prefix, int n_pos, uint64_t model_hash,
+                       int version);
+int sp_cuda_cache_load(sp_cuda_cache_t *cc, const char *prefix, uint64_t expected_hash);
+/* Bands at or beyond max_bands are not read (v3) and are stored as zeros, so
+ * reads and the fused decode see exactly a partial-band read
+ * (shannon_prime_llama.h:240-255); max_bands < 0 loads everything. */
+int sp_cuda_cache_load_partial(sp_cuda_cache_t *cc, const char *prefix, uint64_t expected_hash,
+                               int max_bands);
 
 
 /* Reference shannon_prime_cuda.h:116-134.  In-place VHT2 of n_vecs

@@ -96,7 +96,7 @@ extern "C" int sp_cuda_cache_init(sp_cuda_cache_t *cc, const sp_config_t *cfg,
     int rc = SP_OK;
     if ((rc = sp_check_cuda(cudaMalloc(&cc->d_k_cache, k_total), "cudaMalloc K cache")) ||
         (rc = sp_check_cuda(cudaMalloc(&cc->d_v_cache, v_total), "cudaMalloc V cache")) ||
-        (rc = sp_check_cuda(cudaMalloc(&cc->d_scratch, cfg->head_dim * sizeof(float)), "cudaMalloc scratch")) ||
+        (rc = sp_check_cuda(cudaMalloc(&cc->d_scratch, sp_io_scratch_bytes(cfg)), "cudaMalloc scratch")) ||
         (rc = sp_check_cuda(cudaMalloc(&cc->d_status, 16), "cudaMalloc status"))) {
         sp_cuda_cache_free(cc);
         return rc;

@@ -25,6 +25,8 @@
 #include <math.h>
 #include <string.h>
 
+#include <atomic>
+
 namespace {
 
 constexpr int kAttnWarps = 4;
@@ -250,15 +252,19 @@ size_t sp_attn_workspace_bytes(const sp_cuda_cache_t *cc)
            sp_attn_partial_stride(cc->config.head_dim) * sizeof(float);
 }
 
-static int g_force_impl = 0;   // 0 auto, 1 generic SIMT, 2 tensor-core
+// Diagnostic kernel choice, process-wide (tests use it to compare the two
+// kernels): 0 auto, 1 generic SIMT, 2 tensor-core.  Atomic, so host threads
+// may read it while another sets it.
+static std::atomic<int> g_force_impl{0};
 
-extern "C" void sp_cuda_attn_force_impl(int impl) { g_force_impl = impl; }
+extern "C" void sp_cuda_attn_force_impl(int impl) { g_force_impl.store(impl, std::memory_order_relaxed); }
 
 // Optional timing of the main (non-combine) kernel with CUDA events recorded
-// on the caller's stream, for the benchmark's roofline figure.
-static bool g_prof = false;
-static cudaEvent_t g_ev[2] = {nullptr, nullptr};
-static int g_prof_splits = 0;
+// on the caller's stream, for the benchmark's roofline figure.  Per host
+// thread: a thread enables it and reads back its own last call.
+static thread_local bool g_prof = false;
+static thread_local cudaEvent_t g_ev[2] = {nullptr, nullptr};
+static thread_local int g_prof_splits = 0;
 
 extern "C" void sp_cuda_attn_profile(int enable)
 {

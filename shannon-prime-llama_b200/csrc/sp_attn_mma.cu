@@ -44,6 +44,7 @@
 #include "sp_attn.cuh"
 #include "sp_bulk.cuh"
 
+#include <atomic>
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
@@ -170,7 +171,9 @@ struct Smem {
 // per SM requested from the register allocator.
 // GT query heads per KV head (4 or 8): NT = GT / 4 column tiles of the MMAs,
 // each 4 queries x {hi, lo}.
-template <int kWarps, int kStages, int kMinBlocks, int GT>
+// NBK: K bands read (4, or fewer for a partial-band read, which then skips
+// the unpack and the MMAs of the bands it leaves out).
+template <int kWarps, int kStages, int kMinBlocks, int GT, int NBK>
 __global__ void __launch_bounds__(kWarps * 32, kMinBlocks)
 k_attn_ship_mma(SpAttnArgs a, Sched sc)
 {
@@ -416,6 +419,9 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
                 }
 #pragma unroll
             for (int b = 0; b < 4; b++) {
+                // Bands a partial read leaves out keep their zero start and
+                // contribute nothing.
+                if (b >= NBK) continue;
                 // band window of rows r and r+8: x (low), y (high / shifted)
                 uint32_t wx[2], wy[2];
 #pragma unroll
@@ -734,24 +740,41 @@ int sp_attn_mma_launch(const SpAttnArgs &a_in, cudaStream_t s, cudaEvent_t ev_be
 {
     SpAttnArgs a = a_in;
     const bool wide = a.group > 4;
-    void (*kernel)(SpAttnArgs, Sched) = wide ? k_attn_ship_mma<kCtaWarps, kRingStages, kCtasPerSm8, 8>
-                                             : k_attn_ship_mma<kCtaWarps, kRingStages, kCtasPerSm, 4>;
+    using Kern = void (*)(SpAttnArgs, Sched);
+    static const Kern narrow_k[4] = {k_attn_ship_mma<kCtaWarps, kRingStages, kCtasPerSm, 4, 1>,
+                                     k_attn_ship_mma<kCtaWarps, kRingStages, kCtasPerSm, 4, 2>,
+                                     k_attn_ship_mma<kCtaWarps, kRingStages, kCtasPerSm, 4, 3>,
+                                     k_attn_ship_mma<kCtaWarps, kRingStages, kCtasPerSm, 4, 4>};
+    static const Kern wide_k[4] = {k_attn_ship_mma<kCtaWarps, kRingStages, kCtasPerSm8, 8, 1>,
+                                   k_attn_ship_mma<kCtaWarps, kRingStages, kCtasPerSm8, 8, 2>,
+                                   k_attn_ship_mma<kCtaWarps, kRingStages, kCtasPerSm8, 8, 3>,
+                                   k_attn_ship_mma<kCtaWarps, kRingStages, kCtasPerSm8, 8, 4>};
+    const int nbk = a.nb_k < 1 ? 1 : (a.nb_k > 4 ? 4 : a.nb_k);
+    Kern kernel = wide ? wide_k[nbk - 1] : narrow_k[nbk - 1];
     const size_t smem = wide ? sizeof(Smem<kCtaWarps, kRingStages, 8>) : sizeof(Smem<kCtaWarps, kRingStages, 4>);
     const int threads = kCtaWarps * 32;
-    static int occ_cached[2] = {0, 0}, sms_cached = 0, dev_cached[2] = {-1, -1};
+    // Per device and per kernel: the shared-memory attribute is set and the
+    // occupancy looked up once.  The table is written with atomics, so
+    // host threads driving different devices (or the same one) may race on
+    // it harmlessly: both compute the same values.
+    constexpr int kMaxDev = 64;
+    static std::atomic<int> occ_tab[kMaxDev][2][4];
+    static std::atomic<int> sms_tab[kMaxDev];
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev != dev_cached[wide]) {
+    if (dev < 0 || dev >= kMaxDev) return sp_set_error(SP_ERR_CUDA, "tensor-core attention: device %d", dev);
+    int occ_now = occ_tab[dev][wide][nbk - 1].load(std::memory_order_acquire);
+    if (occ_now == 0) {
         if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return sp_check_cuda(cudaGetLastError(), "attention smem attribute");
         int occ = 0, sms = 0;
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, smem);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        occ_cached[wide] = occ > 0 ? occ : 1;
-        sms_cached = sms > 0 ? sms : 148;
-        dev_cached[wide] = dev;
+        sms_tab[dev].store(sms > 0 ? sms : 148, std::memory_order_relaxed);
+        occ_now = occ > 0 ? occ : 1;
+        occ_tab[dev][wide][nbk - 1].store(occ_now, std::memory_order_release);
     }
-    const int occ_now = occ_cached[wide];
+    const int sms_cached = sms_tab[dev].load(std::memory_order_relaxed);
     const int units = a.n_layers * a.n_kv_heads;
     Sched sc;
     sc.tiles_per_unit = (a.kv_len + 15) / 16;

@@ -29,6 +29,17 @@ int  sp_set_error(int code, const char *fmt, ...);
 void sp_clear_error();
 int  sp_check_cuda(cudaError_t e, const char *what);
 
+// Bytes of sp_cuda_cache_t::d_scratch: the staging rows of the ggml-shaped
+// decode (sp_ggml.cu): fp16 queries and fp16 outputs of one token, up to 8
+// query heads per KV head, and never less than the reference's [head_dim]
+// floats.
+inline size_t sp_io_scratch_bytes(const sp_config_t *cfg)
+{
+    const size_t io = 2ull * 8 * cfg->n_heads_kv * cfg->head_dim * 2;
+    const size_t ref = (size_t)cfg->head_dim * 4;
+    return io > ref ? io : ref;
+}
+
 // 1/sqrt(n) exactly as the CPU path computes it (IEEE sqrt, IEEE divide).
 float sp_inv_sqrt_n(int n);
 

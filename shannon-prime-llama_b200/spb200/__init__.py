@@ -10,10 +10,13 @@ streams.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent.parent
-LIB_PATH = PKG / "lib" / "libshannon_prime_b200.so"
+# SPB200_LIB selects another build of the same library (e.g. one compiled
+# with different tuning flags); the default is the in-tree build.
+LIB_PATH = Path(os.environ["SPB200_LIB"]) if os.environ.get("SPB200_LIB") else PKG / "lib" / "libshannon_prime_b200.so"
 
 SP_MAX_BANDS = 16
 SP_OK, SP_ERR_ARG, SP_ERR_CUDA, SP_ERR_UNSUPPORTED, SP_ERR_TIMEOUT = 0, -1, -2, -3, -4
@@ -148,6 +151,11 @@ SIGNATURES = {
                                          C.POINTER(SpBandConfig), _P, _I, _I, _I, _P, _I, _I,
                                          _F, _P, _I, _P]),
     "sp_cuda_attn_decode_noalloc_status": (_I, [C.POINTER(C.c_uint), _I, _P]),
+    "sp_fnv1a64": (C.c_uint64, [C.c_char_p, C.c_size_t]),
+    "sp_ggml_attn_decode": (_I, [_CC, _I, _P, _I, _P, _P, _P, _I, _P, _P, _F, _I, _I, _P]),
+    "sp_cuda_cache_save": (_I, [_CC, C.c_char_p, _I, C.c_uint64, _I]),
+    "sp_cuda_cache_load": (_I, [_CC, C.c_char_p, C.c_uint64]),
+    "sp_cuda_cache_load_partial": (_I, [_CC, C.c_char_p, C.c_uint64, _I]),
     "sp_cuda_sqfree_cache_init": (_I, [C.POINTER(SpSqfreeCache), C.POINTER(SpConfig), _I, _I, _I, _P]),
     "sp_cuda_sqfree_cache_init_ex": (_I, [C.POINTER(SpSqfreeCache), C.POINTER(SpConfig), _I, _I, _I,
                                           _F, _P]),
@@ -229,6 +237,8 @@ def lib() -> C.CDLL:
             raise RuntimeError(f"{LIB_PATH} is missing: run shannon-prime-llama_b200/build.py")
         L = C.CDLL(str(LIB_PATH))
         for name, (res, args) in SIGNATURES.items():
+            if os.environ.get("SPB200_LIB") and not hasattr(L, name):
+                continue        # another build may predate some entry points
             f = getattr(L, name)
             f.restype = res
             f.argtypes = args
