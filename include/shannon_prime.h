@@ -51,8 +51,10 @@ typedef struct {
 
     int use_mobius_mask;        /* squarefree-first reorder of K coefficients */
 
-    /* Accepted for API compatibility; this build rejects non-zero values
-     * (ternary and fp8 band modes are not on the B200 hot path). */
+    /* Bit b of a ternary mask stores band b as {-1, 0, +1} at 2 bits per
+     * code whatever its band_bits (the band quantiser at m = 1).  use_fp8 is
+     * rejected by sp_cuda_cache_init; the bridge treats it as advisory and
+     * uses integer bands, as the reference bridge does. */
     uint32_t k_ternary_mask;
     uint32_t v_ternary_mask;
     int use_fp8;

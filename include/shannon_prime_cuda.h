@@ -441,6 +441,17 @@ void sp_cuda_d2h_async(void *dst_host, const void *src_device, int64_t n_bytes, 
 void sp_cuda_h2d_async(void *dst_device, const void *src_host, int64_t n_bytes, void *stream);
 
 /* ---------------------------------------------------------------------------
+ * System 1 <-> 2 dual cache: merged read on the GPU, replacing
+ * DualKvCache::read_merged_gpu (src/engine/kv_cache.cpp:1832-1860), which
+ * reads System 1 for every position and leaves the System 2 positions
+ * unmerged on the GPU.  Rows of row_floats floats: row p of d_out is row p
+ * of d_sys2 when bit p of d_route_bits (uint32 words, bit p%32 of word p/32)
+ * is set, else row p of d_sys1.  d_out may be d_sys1 (then only the System 2
+ * rows are written).  One launch, stream-ordered; allocates nothing. */
+int sp_cuda_dual_merge(const float *d_sys1, const float *d_sys2, const uint32_t *d_route_bits,
+                       int n_pos, int row_floats, float *d_out, void *stream);
+
+/* ---------------------------------------------------------------------------
  * Disk tier: save / load of a ship cache's compressed slabs, replacing the
  * engine's KvCache::save_to_disk / load_from_disk / load_from_disk_partial
  * (src/engine/kv_cache.h:133-147, kv_cache.cpp:1535-1585, which call the

@@ -10,10 +10,11 @@
  *     backend and SHANNON_PRIME_BACKEND are accepted and ignored (the
  *     reference's CPU/Adreno/Hexagon backends are not built; there is no
  *     CPU fallback).  Init returns NULL when no CUDA device is usable.
- *   - SHANNON_PRIME_FP8 and *_TERNARY_BANDS are recognised and rejected with
- *     a one-line warning (integer bands are used), as the reference bridge
- *     does for FP8 on backends without an fp8 path (shannon_prime_llama.c:
- *     313-326).
+ *   - SHANNON_PRIME_{K,V}_TERNARY_BANDS (and the DRAFT_ forms) set the
+ *     ternary band masks (shannon_prime_llama.c:142-166, 283-285).
+ *     SHANNON_PRIME_FP8 is recognised and answered with a one-line warning
+ *     (integer bands are used), as the reference bridge does on backends
+ *     without an fp8 path (shannon_prime_llama.c:313-326).
  *   - PrimePE factors (core sp_prime_pe_freq_factors, absent from the
  *     reference checkout) are not computed: sp_llama_get_freq_factors()
  *     returns NULL and sp_llama_get_n_freqs() 0, the reference's

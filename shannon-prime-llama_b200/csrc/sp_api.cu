@@ -80,11 +80,21 @@ extern "C" int sp_cuda_cache_init(sp_cuda_cache_t *cc, const sp_config_t *cfg,
         return sp_set_error(SP_ERR_ARG, "cache_init: bad dims");
     if (!pow2_in_range(cfg->head_dim))
         return sp_set_error(SP_ERR_UNSUPPORTED, "cache_init: head_dim %d not a power of two in [32,512]", cfg->head_dim);
-    if (cfg->use_fp8 || cfg->k_ternary_mask || cfg->v_ternary_mask)
-        return sp_set_error(SP_ERR_UNSUPPORTED, "cache_init: fp8/ternary band modes are not implemented");
+    if (cfg->use_fp8)
+        return sp_set_error(SP_ERR_UNSUPPORTED, "cache_init: fp8 bands are not implemented (the bridge falls "
+                            "back to integer bands, as the reference bridge does)");
     cc->config = *cfg;
-    if (sp_band_config_init(&cc->k_bands, cfg->head_dim, cfg->k_n_bands, cfg->k_band_bits) ||
-        sp_band_config_init(&cc->v_bands, cfg->head_dim, cfg->v_n_bands, cfg->v_band_bits))
+    // Ternary noise-tail bands (the core's sp_band_config_init_ext ternary
+    // mask, CHANGELOG.md:107-114): bit b set stores band b as {-1, 0, +1}
+    // at 2 bits per code whatever its band_bits, i.e. the band quantiser at
+    // 2 bits (m = 1, scale = max|x|).
+    int kbits[SP_MAX_BANDS], vbits[SP_MAX_BANDS];
+    for (int b = 0; b < SP_MAX_BANDS; b++) {
+        kbits[b] = (cfg->k_ternary_mask >> b) & 1u ? 2 : cfg->k_band_bits[b];
+        vbits[b] = (cfg->v_ternary_mask >> b) & 1u ? 2 : cfg->v_band_bits[b];
+    }
+    if (sp_band_config_init(&cc->k_bands, cfg->head_dim, cfg->k_n_bands, kbits) ||
+        sp_band_config_init(&cc->v_bands, cfg->head_dim, cfg->v_n_bands, vbits))
         return sp_set_error(SP_ERR_ARG, "cache_init: bad band configuration");
     cc->max_seq_len = (max_seq_len + 15) & ~15;
     cc->stream = stream;

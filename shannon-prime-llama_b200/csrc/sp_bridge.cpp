@@ -65,6 +65,30 @@ int role_bits(const char *base, sp_llama_role_t role, int *bits, int max_n)
     return i;
 }
 
+// Band indices (comma-separated, e.g. "3" or "2,3") -> bit mask for
+// sp_config_t::{k,v}_ternary_mask, as the reference bridge builds it
+// (shannon_prime_llama.c:142-166): indices outside [0, 32) and tokens that
+// do not start with a digit are ignored; unset or empty gives 0.
+uint32_t role_ternary_mask(const char *base, sp_llama_role_t role)
+{
+    const char *v = role_getenv(base, role);
+    uint32_t mask = 0u;
+    if (!v) return mask;
+    for (const char *p = v; *p;) {
+        while (*p == ' ' || *p == '\t') p++;
+        if (*p >= '0' && *p <= '9') {
+            char *end = nullptr;
+            const long idx = strtol(p, &end, 10);
+            if (idx >= 0 && idx < 32) mask |= 1u << idx;
+            p = end;
+        }
+        while (*p && *p != ',') p++;        // rest of this token
+        if (*p == ',') p++;
+        while (*p == ' ' || *p == '\t') p++;
+    }
+    return mask;
+}
+
 void apply_draft_preset(sp_config_t *cfg)
 {
     const char *preset = getenv("SHANNON_PRIME_DRAFT_PRESET");
@@ -115,11 +139,14 @@ sp_llama_ctx_t *sp_llama_init_with_role(const sp_llama_params_t *params, sp_llam
     n = role_bits("V_BITS", role, cfg.v_band_bits, SP_MAX_BANDS);
     if (n > 0) cfg.v_n_bands = n;
     cfg.use_mobius_mask = role_bool("MOBIUS", role, 1);
-    const char *kt = role_getenv("K_TERNARY_BANDS", role);
-    const char *vt = role_getenv("V_TERNARY_BANDS", role);
-    if ((kt && *kt) || (vt && *vt) || role_bool("FP8", role, 0))
-        fprintf(stderr, "[Shannon-Prime] ternary/FP8 band modes requested but this build has "
-                        "integer bands only; using integer bands\n");
+    cfg.k_ternary_mask = role_ternary_mask("K_TERNARY_BANDS", role);
+    cfg.v_ternary_mask = role_ternary_mask("V_TERNARY_BANDS", role);
+    // FP8 is advisory at the bridge, as in the reference
+    // (shannon_prime_llama.c:287-326): no backend behind this bridge has an
+    // fp8 path, so the request is logged and integer bands are used.
+    if (role_bool("FP8", role, 0))
+        fprintf(stderr, "[Shannon-Prime] SHANNON_PRIME_FP8=1 requested but this backend has no fp8 "
+                        "band path; falling back to int\n");
     return sp_llama_init_config(params, &cfg);
 }
 
@@ -142,7 +169,6 @@ sp_llama_ctx_t *sp_llama_init_config(const sp_llama_params_t *params, const sp_c
         ctx->own_stream = true;
     }
     sp_config_t c = *cfg;
-    c.k_ternary_mask = c.v_ternary_mask = 0;
     c.use_fp8 = 0;
     if (sp_cuda_cache_init(&ctx->cache, &c, params->max_seq_len, ctx->stream) != SP_OK) {
         fprintf(stderr, "[Shannon-Prime] cache init failed: %s\n", sp_cuda_last_error_string());

@@ -152,6 +152,7 @@ SIGNATURES = {
                                          _F, _P, _I, _P]),
     "sp_cuda_attn_decode_noalloc_status": (_I, [C.POINTER(C.c_uint), _I, _P]),
     "sp_fnv1a64": (C.c_uint64, [C.c_char_p, C.c_size_t]),
+    "sp_cuda_dual_merge": (_I, [_P, _P, _P, _I, _I, _P, _P]),
     "sp_ggml_attn_decode": (_I, [_CC, _I, _P, _I, _P, _P, _P, _I, _P, _P, _F, _I, _I, _P]),
     "sp_cuda_cache_save": (_I, [_CC, C.c_char_p, _I, C.c_uint64, _I]),
     "sp_cuda_cache_load": (_I, [_CC, C.c_char_p, C.c_uint64]),
