@@ -171,6 +171,65 @@ struct Smem {
 // per SM requested from the register allocator.
 // GT query heads per KV head (4 or 8): NT = GT / 4 column tiles of the MMAs,
 // each 4 queries x {hi, lo}.
+// Segment merge of one (layer, q head) row.
+__device__ __forceinline__ void combine_row(const SpAttnArgs &a, const Sched &sc, int li, int qh, int lane)
+{
+    const long long u = (long long)li * a.n_kv_heads + qh / a.group;
+    const int i0 = cta_of_tile(u * sc.tiles_per_unit, sc);
+    const int i1 = cta_of_tile((u + 1) * sc.tiles_per_unit - 1, sc);
+    const int nseg = i1 - i0 + 1;
+    // Segment maxima and sums are loaded by the lanes in parallel (32
+    // segments per round), the weights broadcast, and the accumulator loads
+    // issued four segments at a time, so the merge costs a few L2 round
+    // trips rather than one per segment.
+    float M = kEmptyMax;
+    for (int s0 = 0; s0 < nseg; s0 += 32) {
+        const int s = s0 + lane;
+        if (s < nseg) M = fmaxf(M, __ldcg(sp_attn_partial(a, li, qh, s)));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float x[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float L = 0.0f;
+    for (int s0 = 0; s0 < nseg; s0 += 32) {
+        const int s = s0 + lane;
+        float w = 0.0f;
+        if (s < nseg) {
+            const float *p = sp_attn_partial(a, li, qh, s);
+            w = exp2f(__ldcg(p) - M);
+            L += w * __ldcg(p + 1);
+        }
+        const int n_here = min(32, nseg - s0);
+        int j = 0;
+        for (; j + 4 <= n_here; j += 4) {
+            float4 v[4];
+            float wj[4];
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                v[t] = __ldcg(reinterpret_cast<const float4 *>(sp_attn_partial(a, li, qh, s0 + j + t) + 4 + lane * 4));
+                wj[t] = __shfl_sync(0xffffffffu, w, j + t);
+            }
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                x[0] += wj[t] * v[t].x; x[1] += wj[t] * v[t].y; x[2] += wj[t] * v[t].z; x[3] += wj[t] * v[t].w;
+            }
+        }
+        for (; j < n_here; j++) {
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(sp_attn_partial(a, li, qh, s0 + j) + 4 + lane * 4));
+            const float wj = __shfl_sync(0xffffffffu, w, j);
+            x[0] += wj * v.x; x[1] += wj * v.y; x[2] += wj * v.z; x[3] += wj * v.w;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+    sp_warp_wht<4>(x, lane);
+    __half h[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) h[e] = __float2half_rn(x[e] * a.inv_sqrt_n * inv);
+    sp_attn_store_row<4>(a, li, qh, lane, h);
+}
+
 // NBK: K bands read (4, or fewer for a partial-band read, which then skips
 // the unpack and the MMAs of the bands it leaves out).
 template <int kWarps, int kStages, int kMinBlocks, int GT, int NBK>
@@ -665,32 +724,6 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
         for (int k = k_next; k < n_my && k < k_next + kStages; k++)
             wait_stage(bar0 + 8 * (k % kStages), (k / kStages) & 1, nullptr);
     }
-}
-
-// Segment merge of one (layer, q head) row.
-__device__ __forceinline__ void combine_row(const SpAttnArgs &a, const Sched &sc, int li, int qh, int lane)
-{
-    const long long u = (long long)li * a.n_kv_heads + qh / a.group;
-    const int i0 = cta_of_tile(u * sc.tiles_per_unit, sc);
-    const int i1 = cta_of_tile((u + 1) * sc.tiles_per_unit - 1, sc);
-    const int nseg = i1 - i0 + 1;
-    float M = kEmptyMax;
-    for (int s = 0; s < nseg; s++) M = fmaxf(M, sp_attn_partial(a, li, qh, s)[0]);
-    float x[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    float L = 0.0f;
-    for (int s = 0; s < nseg; s++) {
-        const float *p = sp_attn_partial(a, li, qh, s);
-        const float w = exp2f(p[0] - M);
-        L += w * p[1];
-        const float4 v = *reinterpret_cast<const float4 *>(p + 4 + lane * 4);
-        x[0] += w * v.x; x[1] += w * v.y; x[2] += w * v.z; x[3] += w * v.w;
-    }
-    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-    sp_warp_wht<4>(x, lane);
-    __half h[4];
-#pragma unroll
-    for (int e = 0; e < 4; e++) h[e] = __float2half_rn(x[e] * a.inv_sqrt_n * inv);
-    sp_attn_store_row<4>(a, li, qh, lane, h);
 }
 
 // Merge the segment partials of one (layer, q head), transform, write fp16
