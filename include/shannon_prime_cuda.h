@@ -332,6 +332,8 @@ typedef struct {
     float           *d_vrows;           /* [head_dim][pad_dim] rows of the transform matrix */
     void            *d_recon;           /* [n_slots][head_dim][K + 8] fp16 reconstruction matrices
                                            of the tensor-core batched read (NULL: not used) */
+    unsigned int    *d_status;          /* device error word: bit 0 a bounded wait of the tcgen05
+                                           read ran out (its tiles are missing from the output) */
 } sp_cuda_hier_cache_t;
 
 /* Reference shannon_prime_cuda.h:337-349 (caller supplies the index sets and

@@ -2681,6 +2681,355 @@ k_hier_recon(SpSqDev t, HrArgs h)
     }
 }
 
+// ---------------------------------------------------------------------------
+// The same reconstruction on the 5th-generation tensor cores (tcgen05):
+// one persistent CTA per SM, 128 positions per tile, D = A x B with
+//   A [128 positions x 336] fp16  (dequantised skeleton bands, 16 each, then
+//                                   the residual deviations): built by the
+//                                   thread that owns the position and written
+//                                   to tensor memory (tcgen05.st), one row per
+//                                   TMEM lane;
+//   B [336 x 256] fp16            (the slot's reconstruction matrix, resident
+//                                   in shared memory in the K-major core-
+//                                   matrix layout, reloaded when the slot
+//                                   changes);
+//   D [128 x 256] fp32            (tensor memory; drained by tcgen05.ld, one
+//                                   output row per thread).
+// One elected thread issues the 21 K=16 MMAs (kind::f16, A from tensor
+// memory, B by shared-memory descriptor) and commits them to an mbarrier;
+// every wait is bounded and sets status bit 0 on timeout.
+
+namespace tc {
+
+constexpr int kM = 128;            // positions per tile (= TMEM lanes = threads)
+constexpr int kN = 256;            // output columns (head_dim)
+constexpr int kKSteps = 21;        // 2 skeleton bands + 19 residual blocks of 16
+constexpr int kKGroups = 2 * kKSteps;          // 8-element core-matrix columns
+constexpr int kBBytes = kN * kKGroups * 16;    // 172032
+constexpr int kThreads = 2 * kM;  // two warps per TMEM lane quarter
+constexpr int kResSplit = 9;       // residual K blocks of the first warp of a quarter (it also has 2 skeleton blocks)
+constexpr int kPfWords = 13;       // prefetched words per thread
+constexpr int kXStride = 36;       // floats per row of the output staging block (32 + 4: no bank conflicts)
+constexpr int kStageWords = kThreads * kPfWords;   // 3328 >= (128 * 103 + 6) / 4 + 2 words of packed rows
+constexpr uint32_t kColD = 0;      // TMEM columns 0..255: D
+constexpr uint32_t kColA = 256;    // TMEM columns 256..423: A (168 x 32 bit)
+constexpr int kTmemCols = 512;
+
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8])
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};"
+                 ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]),
+                 "r"(v[7]) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16])
+{
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+                 "%12, %13, %14, %15}, [%16];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                   "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+                   "=r"(v[14]), "=r"(v[15])
+                 : "r"(taddr));
+}
+
+// Shared-memory matrix descriptor, K-major, no swizzle: core matrices of 8
+// rows x 16 bytes stored contiguously; lbo = bytes between the two K halves
+// of one MMA, sbo = bytes between consecutive groups of 8 rows.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo)
+{
+    uint64_t d = 0;
+    d |= (uint64_t)((addr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;                      // descriptor version for sm_100
+    return d;                                    // base offset 0, legacy LBO mode, no swizzle
+}
+
+// Instruction descriptor of kind::f16: f16 A and B, f32 D, both K-major,
+// M = 128, N = 256.
+constexpr uint32_t kIdesc = (1u << 4)            // D format f32
+                          | (0u << 7) | (0u << 10) // A, B f16
+                          | ((uint32_t)(kN >> 3) << 17)
+                          | ((uint32_t)(kM >> 4) << 24);
+
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %3, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %4, {%5, %5, %5, %5}, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(accumulate), "r"(kIdesc), "r"(0u) : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+}  // namespace tc
+
+struct HrTcArgs {
+    HrArgs h;
+    unsigned int *status;
+    long long total_tiles;        // n_layers * nh * tiles_per_slot
+    int tiles_per_slot;
+};
+
+__global__ void __launch_bounds__(tc::kThreads, 1)
+k_hier_recon_tc(SpSqDev t, HrTcArgs ta)
+{
+    using namespace tc;
+    const HrArgs &h = ta.h;
+    extern __shared__ __align__(128) unsigned char smem[];
+    unsigned char *Bs = smem;                                          // kBBytes
+    uint32_t *stage = reinterpret_cast<uint32_t *>(smem + kBBytes);    // kStageWords
+    uint16_t *lut = reinterpret_cast<uint16_t *>(stage + kStageWords);  // 16
+    unsigned long long *bar = reinterpret_cast<unsigned long long *>(lut + 16);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + 1);
+    int *ok_flag = reinterpret_cast<int *>(tmem_slot + 1);
+    float *xbuf = reinterpret_cast<float *>(smem + kBBytes + kStageWords * 4 + 128);   // [8 warps][32][kXStride]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // Warps w and w + 4 share TMEM lanes 32 (w % 4) .. +31 (a warp reaches
+    // only its quarter of the lanes): both serve the same 32 positions,
+    // warp w the first 11 K blocks of their A rows and the first 128 output
+    // columns, warp w + 4 the other 10 K blocks and columns.
+    const int quarter = warp & 3, half = warp >> 2;
+    const int row = 32 * quarter + lane;
+    const uint32_t bar_a = spb::smem_u32(bar);
+
+    const long long g0 = blockIdx.x * ta.total_tiles / gridDim.x;
+    const long long g1 = (blockIdx.x + 1) * ta.total_tiles / gridDim.x;
+
+    if (tid < 16) {       // PRMT selectors: nibble (l0 | l1 << 2) -> halves T[l0], T[l1]
+        const int l0 = tid & 3, l1 = tid >> 2;
+        lut[tid] = (uint16_t)((2 * l0) | ((2 * l0 + 1) << 4) | ((2 * l1) << 8) | ((2 * l1 + 1) << 12));
+    }
+    if (tid == 0) {
+        spb::mbar_init(bar_a, 1);
+        spb::mbar_init_fence();
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(spb::smem_u32(tmem_slot)), "r"((uint32_t)kTmemCols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
+
+    const int L = 1 << t.res_bits;
+    const float center = __fdiv_rn((float)(L - 1), 2.0f);
+    const int bpp = t.bytes_per_pos;
+    int cur_slot = -1;
+    uint32_t phase = 0;
+    bool failed = false;
+
+    // Packed rows of tile gg: the word-aligned cover of its rows, word
+    // tid + kThreads i in pf[i] (zero past the rows), loaded one tile ahead.
+    uint32_t pf[kPfWords];
+    int pf_soff = 0;
+    auto prefetch = [&](long long gg) {
+        const int sl = (int)(gg / ta.tiles_per_slot);
+        const int q0 = (int)(gg - (long long)sl * ta.tiles_per_slot) * kM;
+        const int li = sl / h.nh, hh = sl - li * h.nh;
+        const int slot = (h.layer0 + li) * h.nh + hh;
+        const int nr = min(kM, h.n_tok - q0);
+        const uint8_t *gs = h.cache + (long long)slot * h.slot_stride + (long long)(h.start_pos + q0) * bpp;
+        const uint8_t *ga = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(gs) & ~uintptr_t(3));
+        pf_soff = (int)(gs - ga);
+        const int nwords = (nr * bpp + pf_soff + 3) / 4;
+#pragma unroll
+        for (int i = 0; i < kPfWords; i++) {
+            const int w = tid + kThreads * i;
+            const uint8_t *p = ga + 4 * w;
+            uint32_t v = 0;
+            if (w < nwords) {
+                if (p + 4 <= h.cache_end) {
+                    v = __ldcs(reinterpret_cast<const unsigned int *>(p));
+                } else {
+                    for (int b = 0; b < 4; b++)
+                        if (p + b < h.cache_end) v |= (uint32_t)p[b] << (8 * b);
+                }
+            }
+            pf[i] = v;
+        }
+    };
+    if (g0 < g1) prefetch(g0);
+
+    for (long long g = g0; g < g1 && !failed; g++) {
+        const int sl = (int)(g / ta.tiles_per_slot);               // slot within the call
+        const int p0 = (int)(g - (long long)sl * ta.tiles_per_slot) * kM;
+        const int li = sl / h.nh, hh = sl - li * h.nh;
+        const int slot = (h.layer0 + li) * h.nh + hh;
+        const int nrows = min(kM, h.n_tok - p0);
+        // ---- B of the slot -> shared memory, core-matrix layout ----------
+        if (slot != cur_slot) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(h.recon + (size_t)slot * kN * (16 * kKSteps + 8));
+            // thread = one row n of B; its 42 chunks are loaded 14 at a time
+            // before they are stored
+            const int n = tid;
+            unsigned char *dst = Bs + (n >> 3) * kKGroups * 128 + (n & 7) * 16;
+#pragma unroll 1
+            for (int kg0 = 0; kg0 < kKGroups; kg0 += 14) {
+                uint4 v[14];
+#pragma unroll
+                for (int j = 0; j < 14; j++) v[j] = __ldg(src + (size_t)n * (kKGroups + 1) + kg0 + j);
+#pragma unroll
+                for (int j = 0; j < 14; j++) *reinterpret_cast<uint4 *>(dst + (kg0 + j) * 128) = v[j];
+            }
+            cur_slot = slot;
+            spb::fence_proxy_async();      // generic writes of B before the tensor core reads them
+        }
+        // ---- packed rows of the tile -> shared memory, from the registers
+        // prefetched during the previous tile
+        const int soff = pf_soff;
+#pragma unroll
+        for (int i = 0; i < kPfWords; i++) stage[tid + kThreads * i] = pf[i];
+        __syncthreads();
+        if (g + 1 < g1) prefetch(g + 1);
+
+        // ---- A row blocks of this thread -> tensor memory ------------------
+        {
+            const bool live = row < nrows;
+            const int rb = 8 * (soff + row * bpp);
+            const float mag = live ? __uint_as_float(hr_bits(stage, rb + 8 * t.mag_off)) : 0.0f;
+            const float step = __fdiv_rn(__fmul_rn(2.0f, mag), (float)(L - 1));
+            const uint32_t tlo = pack_h2(__fmul_rn(__fsub_rn(0.0f, center), step), __fmul_rn(__fsub_rn(1.0f, center), step));
+            const uint32_t thi = pack_h2(__fmul_rn(__fsub_rn(2.0f, center), step), __fmul_rn(__fsub_rn(3.0f, center), step));
+            if (half == 0) {
+#pragma unroll
+                for (int b = 0; b < 2; b++) {
+                    float sc = live ? __half2float(__ushort_as_half(
+                                          (unsigned short)(hr_bits(stage, rb + 8 * t.bl.byte_off[b]) & 0xffffu)))
+                                    : 0.0f;
+                    sc = fabsf(sc) <= 65504.0f ? sc : 0.0f;
+                    const int bits = t.bl.bits[b];
+                    const uint32_t mask = (1u << bits) - 1u;
+                    const float m = (float)((1 << (bits - 1)) - 1);
+                    const int cb = rb + 8 * (t.bl.byte_off[b] + 2);
+                    uint32_t v[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        float q[2];
+#pragma unroll
+                        for (int k = 0; k < 2; k++) {
+                            const int i = 2 * e + k;
+                            const bool ok = live && i < t.bl.size[b];
+                            const uint32_t u = ok ? (hr_bits(stage, cb + i * bits) & mask) : 0u;
+                            q[k] = ok ? __fmul_rn(__fsub_rn((float)u, m), sc) : 0.0f;
+                        }
+                        v[e] = pack_h2(q[0], q[1]);
+                    }
+                    tmem_st8(tmem + lane_base + kColA + 8 * b, v);
+                }
+            }
+            const int resb = rb + 8 * t.res_off;
+            const int j0 = half == 0 ? 0 : kResSplit, j1 = half == 0 ? kResSplit : kKSteps - 2;
+#pragma unroll 1
+            for (int j = j0; j < j1; j++) {
+                const int r0 = 16 * j;
+                const uint32_t w = live ? hr_bits(stage, resb + 32 * j) : 0u;
+                // residuals past n_res meet zero rows of B; write them as 0
+                uint32_t v[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    const uint32_t sel = lut[(w >> (4 * e)) & 15u];
+                    v[e] = (live && r0 + 2 * e < t.n_res) ? __byte_perm(tlo, thi, sel) : 0u;
+                }
+                tmem_st8(tmem + lane_base + kColA + 8 * (2 + j), v);
+            }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        }
+        fence_before();
+        __syncthreads();
+        // ---- MMAs (one thread) -------------------------------------------
+        if (tid == 0) {
+            fence_after();
+            const uint32_t bsm = spb::smem_u32(Bs);
+#pragma unroll 1
+            for (int s = 0; s < kKSteps; s++) {
+                const uint64_t bd = smem_desc(bsm + (uint32_t)(2 * s) * 128u, 128u, (uint32_t)kKGroups * 128u);
+                mma_f16_ts(tmem + kColD, tmem + kColA + 8 * s, bd, s > 0 ? 1u : 0u);
+            }
+            mma_commit(bar_a);
+        }
+        // ---- wait for the products (bounded; thread 0 decides for the CTA)
+        if (tid == 0) *ok_flag = spb::wait_stage(bar_a, phase, ta.status) ? 1 : 0;
+        __syncthreads();
+        if (!*ok_flag) {
+            failed = true;
+            break;
+        }
+        phase ^= 1u;
+        fence_after();
+        // ---- D -> global: each warp moves its 32 rows x 128 columns in
+        // blocks of 32 columns through shared memory, so that every store
+        // instruction writes four whole 128-byte row segments
+        {
+            float *xb = xbuf + warp * 32 * kXStride;
+            const int r4 = lane >> 3, c4 = (lane & 7) * 4;
+#pragma unroll 1
+            for (int c0 = 0; c0 < 128; c0 += 32) {
+                uint32_t v[2][16];
+                tmem_ld16(tmem + lane_base + kColD + 128 * half + c0, v[0]);
+                tmem_ld16(tmem + lane_base + kColD + 128 * half + c0 + 16, v[1]);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                for (int j = 0; j < 2; j++)
+#pragma unroll
+                    for (int e = 0; e < 16; e += 4)
+                        *reinterpret_cast<float4 *>(xb + lane * kXStride + 16 * j + e) =
+                            make_float4(__uint_as_float(v[j][e]), __uint_as_float(v[j][e + 1]),
+                                        __uint_as_float(v[j][e + 2]), __uint_as_float(v[j][e + 3]));
+                __syncwarp();
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int rr = 4 * i + r4;                 // row within the warp's 32
+                    const int prow = 32 * quarter + rr;
+                    if (prow < nrows) {
+                        float *o = h.out + (((long long)li * h.n_tok + p0 + prow) * h.nh + hh) * kN + 128 * half + c0 + c4;
+                        __stcs(reinterpret_cast<float4 *>(o), *reinterpret_cast<const float4 *>(xb + rr * kXStride + c4));
+                    }
+                }
+                __syncwarp();
+            }
+        }
+        fence_before();
+        __syncthreads();       // D drained and the stage read before the next tile reuses them
+    }
+    if (failed) {
+        // The commit may still arrive: wait once more (bounded) before the
+        // tensor memory is released.
+        if (tid == 0) spb::wait_stage(bar_a, phase, nullptr);
+        __syncthreads();
+    }
+    fence_after();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)kTmemCols)
+                     : "memory");
+}
+
+size_t hr_tc_smem_bytes()
+{
+    return (size_t)tc::kBBytes + tc::kStageWords * 4 + 128 + (size_t)8 * 32 * tc::kXStride * 4;
+}
+
+// The tcgen05 read serves the shape its matrices are laid out for: two
+// skeleton bands of at most 16 values, 19 residual blocks (n_res <= 304),
+// 2-bit residuals, head_dim 256, rows of at most 103 bytes.
+bool hr_tc_supported(const SpSqDev &t)
+{
+    if (!t.hier || t.res_bits != 2 || t.hd != 256 || t.bl.n_bands != 2) return false;
+    if (t.bl.size[0] > 16 || t.bl.size[1] > 16 || (t.n_res + 15) / 16 != 19) return false;
+    return (tc::kM * t.bytes_per_pos + 3 + 3) / 4 + 2 <= tc::kStageWords;
+}
+
 size_t hr_smem_bytes(const SpSqDev &t, int hd)
 {
     const int stride = hr_stride(t.bl.n_bands, t.n_res);
@@ -3208,6 +3557,8 @@ int sp_cuda_hier_cache_init(sp_cuda_hier_cache_t *hc, const sp_config_t *cfg, in
     cudaMemset(hc->d_k_cache, 0, total);
     cudaMemset(hc->d_v_cache, 0, total);
     cudaMemset(hc->d_W, 0, (size_t)n_slots * n_target * n_skeleton * 2);
+    up((void **)&hc->d_status, nullptr, 16, "cudaMalloc hier status");
+    if (!rc) cudaMemset(hc->d_status, 0, 16);
     if (hr_kernel(t)) {      // tensor-core batched read: transform rows + per-slot matrices
         const std::vector<float> vr = hr_transform_rows(pad_dim, cfg->head_dim);
         up((void **)&hc->d_vrows, vr.data(), vr.size() * 4, "hier transform rows");
@@ -3236,6 +3587,7 @@ void sp_cuda_hier_cache_free(sp_cuda_hier_cache_t *hc)
     cudaFree(hc->d_W);
     cudaFree(hc->d_vrows);
     cudaFree(hc->d_recon);
+    cudaFree(hc->d_status);
     memset(hc, 0, sizeof(*hc));
 }
 
@@ -3314,6 +3666,27 @@ int sp_cuda_hier_read_kv_tokens(const sp_cuda_hier_cache_t *hc, int layer0, int 
         if ((rc = hier_io(hc, which, layer0, n_layers, 0, H, start_pos, n_pos, io))) return rc;
         io.out = out;
         HrKernel hk = hc->d_recon && !getenv("SHANNON_PRIME_HIER_READ_SIMT") ? hr_kernel(t) : nullptr;
+        if (hk && n_pos > 0 && hr_tc_supported(t) && !getenv("SHANNON_PRIME_HIER_READ_MMA_SYNC")) {
+            HrTcArgs ta;
+            ta.h.cache = io.cache;
+            ta.h.slot_stride = io.slot_stride;
+            ta.h.cache_end = io.cache + (long long)hc->n_slots * io.slot_stride;
+            ta.h.recon = (const __half *)hc->d_recon;
+            ta.h.out = out;
+            ta.h.layer0 = layer0; ta.h.n_layers = n_layers; ta.h.nh = H; ta.h.start_pos = start_pos;
+            ta.h.n_tok = n_pos; ta.h.tokens_per_cta = 0;
+            ta.status = hc->d_status;
+            ta.tiles_per_slot = (n_pos + tc::kM - 1) / tc::kM;
+            ta.total_tiles = (long long)n_layers * H * ta.tiles_per_slot;
+            int sms = 148;
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, hc->device);
+            const long long grid = ta.total_tiles < sms ? ta.total_tiles : sms;
+            const size_t sm = hr_tc_smem_bytes();
+            cudaFuncSetAttribute(k_hier_recon_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+            k_hier_recon_tc<<<(unsigned)grid, tc::kThreads, sm, (cudaStream_t)hc->stream>>>(t, ta);
+            if ((rc = sp_check_cuda(cudaGetLastError(), "hier tcgen05 read launch"))) return rc;
+            continue;
+        }
         if (hk && n_pos > 0) {
             HrArgs a;
             a.cache = io.cache;

@@ -91,6 +91,7 @@ class SpHierCache(C.Structure):
         ("d_dev_scratch", C.c_void_p), ("d_mag_scratch", C.c_void_p),
         ("d_levels_scratch", C.c_void_p), ("stream", C.c_void_p),
         ("device", C.c_int), ("d_tables", C.c_void_p), ("d_vrows", C.c_void_p), ("d_recon", C.c_void_p),
+        ("d_status", C.c_void_p),
     ]
 
 

@@ -151,15 +151,18 @@ def test_config4_hier_full_length(cuda, monkeypatch):
     k, v = synth.kv_layer_torch(gen, T, H, hd, sigma=1.0, dtype=torch.bfloat16)
     cache.write_kv_tokens(0, 0, k.unsqueeze(0), v.unsqueeze(0))
     outs = []
-    for simt in (False, True):
-        if simt:
-            monkeypatch.setenv("SHANNON_PRIME_HIER_READ_SIMT", "1")
+    # tcgen05 read (default), mma.sync read, exact SIMT read
+    for env in (None, "SHANNON_PRIME_HIER_READ_MMA_SYNC", "SHANNON_PRIME_HIER_READ_SIMT"):
+        if env:
+            monkeypatch.setenv(env, "1")
         ko = torch.empty(1, T, H, hd, device="cuda")
         cache.read_kv_tokens(0, 0, ko, None)
         torch.cuda.synchronize()
         outs.append(ko.cpu().numpy())
     for h in range(H):
-        assert _rel(outs[0][0, :, h], outs[1][0, :, h]) <= RTOL, h
+        assert _rel(outs[0][0, :, h], outs[2][0, :, h]) <= RTOL, h
+        assert _rel(outs[1][0, :, h], outs[2][0, :, h]) <= RTOL, h
+    outs.pop(1)
     h = 7
     kh = k[:, h].float().cpu().numpy()
     packed = cache.slab(0).cpu().numpy()[h, :T]
