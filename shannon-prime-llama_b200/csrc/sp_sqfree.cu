@@ -2784,7 +2784,7 @@ k_hier_recon_tc(SpSqDev t, HrTcArgs ta)
 {
     using namespace tc;
     const HrArgs &h = ta.h;
-    extern __shared__ __align__(128) unsigned char smem[];
+    extern __shared__ __align__(16) unsigned char smem[];
     unsigned char *Bs = smem;                                          // kBBytes
     uint32_t *stage = reinterpret_cast<uint32_t *>(smem + kBBytes);    // kStageWords
     uint16_t *lut = reinterpret_cast<uint16_t *>(stage + kStageWords);  // 16
@@ -2930,19 +2930,27 @@ k_hier_recon_tc(SpSqDev t, HrTcArgs ta)
                 }
             }
             const int resb = rb + 8 * t.res_off;
-            const int j0 = half == 0 ? 0 : kResSplit, j1 = half == 0 ? kResSplit : kKSteps - 2;
-#pragma unroll 1
-            for (int j = j0; j < j1; j++) {
-                const int r0 = 16 * j;
-                const uint32_t w = live ? hr_bits(stage, resb + 32 * j) : 0u;
-                // residuals past n_res meet zero rows of B; write them as 0
-                uint32_t v[8];
+            const int j0 = half == 0 ? 0 : kResSplit;
+            const int nj = half == 0 ? kResSplit : kKSteps - 2 - kResSplit;
+            // all of this thread's residual words first (independent loads),
+            // then the blocks
+            uint32_t rw[kKSteps - 2 - kResSplit];
 #pragma unroll
-                for (int e = 0; e < 8; e++) {
-                    const uint32_t sel = lut[(w >> (4 * e)) & 15u];
-                    v[e] = (live && r0 + 2 * e < t.n_res) ? __byte_perm(tlo, thi, sel) : 0u;
+            for (int j = 0; j < kKSteps - 2 - kResSplit; j++)
+                rw[j] = (live && j < nj) ? hr_bits(stage, resb + 32 * (j0 + j)) : 0u;
+#pragma unroll
+            for (int j = 0; j < kKSteps - 2 - kResSplit; j++) {
+                if (j < nj) {
+                    const int r0 = 16 * (j0 + j);
+                    // residuals past n_res meet zero rows of B; write them as 0
+                    uint32_t v[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        const uint32_t sel = lut[(rw[j] >> (4 * e)) & 15u];
+                        v[e] = (live && r0 + 2 * e < t.n_res) ? __byte_perm(tlo, thi, sel) : 0u;
+                    }
+                    tmem_st8(tmem + lane_base + kColA + 8 * (2 + j0 + j), v);
                 }
-                tmem_st8(tmem + lane_base + kColA + 8 * (2 + j), v);
             }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         }
