@@ -138,11 +138,13 @@ def cpu_decode_sample(n_threads: int, layers: int = 1):
         kp[h] = O.ship_write(k, KB, True, n_threads)
         vp[h] = O.ship_write(v, VB, False, n_threads)
     q = synth.q_np(SEED, 1, N_Q, HD, 1.0 / 128 ** 0.5)[0]
-    t0 = time.perf_counter()
+    O.attn_decode(kp, vp, HD, KB, VB, True, q, CTX, 1.0, n_threads)      # warm-up pass
+    times = []
     for _ in range(layers):
+        t0 = time.perf_counter()
         O.attn_decode(kp, vp, HD, KB, VB, True, q, CTX, 1.0, n_threads)
-    dt = (time.perf_counter() - t0) / layers
-    return dt, n_threads
+        times.append(time.perf_counter() - t0)
+    return times, n_threads
 
 
 def cpu_compress_sample(n_threads: int, n_pos: int = 8192):
@@ -435,10 +437,12 @@ def run_reference(args):
     q = synth.q_np(SEED, 1, N_Q, HD, 1.0 / 128 ** 0.5)[0]
     for _ in range(args.warmup):
         O.attn_decode(kp, vp, HD, KB, VB, True, q, CTX, 1.0, n_threads)
-    t0 = time.perf_counter()
+    times = []
     for _ in range(args.steps):
+        t0 = time.perf_counter()
         O.attn_decode(kp, vp, HD, KB, VB, True, q, CTX, 1.0, n_threads)
-    per_layer = (time.perf_counter() - t0) / args.steps
+        times.append(time.perf_counter() - t0)
+    per_layer = statistics.median(times)
     us_tok = per_layer * N_LAYERS * 1e6
     cores = n_threads
     line = {
@@ -449,7 +453,9 @@ def run_reference(args):
         "config": {"workload": "config 1: 32L x 32Q/8KV x hd128, ctx 32768, batch 1, ship 5/5/4/3 + V3",
                    "sample": "1 of 32 layers per step, scaled x32"},
         "cpu_baseline": {"value": us_tok, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": "one layer (8 KV heads x 32768 positions) per step, x32"},
+                         "min": min(times) * N_LAYERS * 1e6, "passes": len(times),
+                         "sample": "one layer (8 KV heads x 32768 positions) per step, median over the "
+                                   "timed steps (min also given), x32"},
         "e2e": {"value": us_tok, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference CPU core (lib/shannon-prime) is absent from the reference checkout; "
                 "this is the CPU restatement of its algorithm (oracle/sp_oracle.c), OpenMP over (KV head, token chunk) tasks on every host thread",
@@ -709,9 +715,11 @@ def run_ours(args):
     cpu = None
     if ws == 1 and not args.no_cpu:
         n_threads = os.cpu_count() or 1
-        per_layer, cores = cpu_decode_sample(n_threads, layers=3)
-        cpu = {"value": per_layer * N_LAYERS * 1e6, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": "3 passes over one layer (8 KV heads x 32768 positions), scaled x32 layers",
+        times, cores = cpu_decode_sample(n_threads, layers=5)
+        cpu = {"value": statistics.median(times) * N_LAYERS * 1e6, "unit": UNIT, "cores": cores, "kind": "port",
+               "min": min(times) * N_LAYERS * 1e6, "passes": len(times),
+               "sample": "one layer (8 KV heads x 32768 positions) per pass, 1 warm-up + 5 timed passes, "
+                         "median (min also given), scaled x32 layers; OpenMP on every host thread",
                "compress_mpairs_s": None}
         mp, _ = cpu_compress_sample(n_threads)
         cpu["compress_mpairs_s"] = mp / 1e6
