@@ -191,7 +191,7 @@ def measure_sqfree(torch, dev, stream, steps: int, warmup: int, peak: float, sca
     the fused decode step (32 query heads, GQA 4, fp16 queries)."""
     from spb200.sqfree import SqfreeCache
     from spb200 import synth
-    L_, H_, T_, hd = 32 // scale, 8, 16384, 128
+    L_, H_, T_, hd = max(1, 32 // scale), 8, 16384, 128
     cache = SqfreeCache(hd, L_, H_, T_, residual_bits=3, use_spinor=True, sk_frac=0.75,
                         stream=stream)
     gen = torch.Generator(device=dev)
@@ -268,7 +268,7 @@ def measure_hier(torch, dev, stream, peak: float, scale: int = 1):
     first sequence and shared by the sequences."""
     from spb200.sqfree import HierCache
     from spb200 import synth
-    S_, H_, T_, hd, pd, nsk = 64 // scale, 16, 8192, 256, 330, 30
+    S_, H_, T_, hd, pd, nsk = max(1, 64 // scale), 16, 8192, 256, 330, 30
     cache = HierCache(hd, S_, H_, T_, pd, nsk, stream=stream)
     gen = torch.Generator(device=dev)
     gen.manual_seed(4)
@@ -675,8 +675,10 @@ def run_ours(args):
     kslot = int(cc.contents.max_seq_len) * K_ROW
     kbase = int(cc.contents.d_k_cache or 0)
 
+    kq_layers = min(4, N_LAYERS)
+
     def kq_pass():
-        for layer in range(4):
+        for layer in range(kq_layers):
             for h in range(H):
                 L.sp_cuda_kq_scores(kbase + (layer * H + h) * kslot, K_ROW, 0, HD, CTX,
                                     q[layer, h * G].data_ptr(), 1, HD * 2, G, kq_dst[h].data_ptr(),
@@ -688,7 +690,7 @@ def run_ours(args):
         kq_pass()
     c1.record(stream)
     barrier()
-    kq_ms = max_over_ranks(c0.elapsed_time(c1) / (reps * 4 * H))     # per slot
+    kq_ms = max_over_ranks(c0.elapsed_time(c1) / (reps * kq_layers * H))     # per slot
     kq_bytes = CTX * K_ROW + G * CTX * 4 + G * HD * 2
     kq_gbs = kq_bytes / (kq_ms * 1e-3) / 1e9
 
