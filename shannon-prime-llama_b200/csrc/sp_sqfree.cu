@@ -34,6 +34,7 @@
 #include <stdlib.h>
 #include <string.h>
 #include <algorithm>
+#include <atomic>
 #include <vector>
 #include <type_traits>
 #include <utility>
@@ -656,9 +657,11 @@ struct SqAttn {
     float logit_scale;
     int store_width_k, store_width_v;
     unsigned int *status;         // bit 0: a bounded copy wait ran out
+    float *qws;                   // lane decode: transformed queries [n_layers][n_q][kSaQWords]
 };
 
 constexpr int kSqMaxSplits = 64;
+constexpr int kSaQWords = 164;
 constexpr int kSqAttnWarps = 4;
 
 __device__ __forceinline__ float *sq_partial(const SqAttn &a, int pd, int li, int qh, int split)
@@ -2121,6 +2124,491 @@ k_sq_decode_lane(const uint8_t *slab, int n_pos, unsigned int *status, const __g
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
+// -------------------------------------------- fused decode, lane per slot --
+// Fused decode attention for the same layout (k_sq_attn_lane): one thread
+// rebuilds the 154 coefficients of one position's K (then V) slot in its
+// registers from compile-time field offsets, as the lane read does, and the
+// two contractions run on the tensor cores (mma.sync m16n8k16, fp16 in,
+// fp32 accumulate) over a warp's 32 positions:
+//   scores  S[32 pos][8]   = C_K[32 pos][160] x Q[160][8]
+//   values  O[160][8]     += C_V^T[160][32 pos] x W[32 pos][8]
+// with the 8 columns = 4 query heads x {hi, lo} fp16 halves of an fp32
+// operand (the transformed query for K, the softmax weight for V).  The
+// coefficient rows go through a per-warp shared-memory tile as fp16 (times
+// 2^-4, which keeps any coefficient of a finite slot inside the fp16 range)
+// and come back as MMA fragments by ldmatrix (transposed for the V side).
+// Coefficients are in slot order: skeleton slots 0..114, residuals 0..38,
+// six zero columns; the query is transformed once per CTA and gathered into
+// the same order, so the score is the coefficient-domain dot product
+// q'.c = q.unpad(V c) of the other decode kernels.
+//
+// Residual predictions are accumulated slot by slot (each skeleton value is
+// added into the residuals whose Möbius terms name it, in slot order) so a
+// thread keeps 39 running sums instead of all 115 skeleton values.
+constexpr int kSaWarps = 4, kSaStages = 2;
+constexpr int kSaRowHalves = 168;                 // 160 + 8: conflict-free ldmatrix rows
+constexpr int kSaTile = 32 * kSlBytes;            // 3200 bytes of K (or V) rows per tile
+
+struct SaTerms {
+    int slot[kSlNT], res[kSlNT], neg[kSlNT];
+    int grp[16];                                  // first term of skeleton group k (slots 8k..8k+7)
+};
+__host__ __device__ constexpr SaTerms sa_terms()
+{
+    SaTerms t{};
+    int n = 0;
+    for (int s = 0; s < kSlSK; s++) {
+        if ((s & 7) == 0) t.grp[s >> 3] = n;
+        for (int k = 0; k < kSlNT; k++)
+            if ((kSlTab.term[k] >> 1) == s) {
+                t.slot[n] = s;
+                t.res[n] = kSlTab.term_res[k];
+                t.neg[n] = kSlTab.term[k] & 1;
+                n++;
+            }
+    }
+    for (int g = (kSlSK + 7) / 8; g < 16; g++) t.grp[g] = n;
+    return t;
+}
+constexpr SaTerms kSaTerms = sa_terms();
+
+// Pad index of coefficient j of the slot order.
+__host__ __device__ constexpr int sa_pd_of(int j)
+{
+    return j < kSlSK ? kSlTab.skel[j] : kSlTab.res[j - kSlSK];
+}
+struct SaPdIdx { int v[kSlPD]; };
+__host__ __device__ constexpr SaPdIdx sa_pd_idx()
+{
+    SaPdIdx x{};
+    for (int j = 0; j < kSlPD; j++) x.v[sa_pd_of(j)] = j;     // slot-order index of pad index i
+    return x;
+}
+__constant__ SaPdIdx c_sa_j_of = sa_pd_idx();
+
+template <int P, int NB>
+__device__ __forceinline__ uint32_t sa_bits(const uint32_t (&w)[26])
+{
+    constexpr int i = P >> 5, s = P & 31;
+    constexpr uint32_t m = NB == 32 ? 0xffffffffu : (1u << NB) - 1u;
+    if constexpr (s + NB > 32) return __funnelshift_r(w[i], w[i + 1], s) & m;
+    else return (w[i] >> s) & m;
+}
+
+// Skeleton value of slot S (times 2^-4): (u - m_b) * scale_b, exact.
+template <int S>
+__device__ __forceinline__ float sa_skel(const uint32_t (&w)[26], const float (&scl)[5])
+{
+    constexpr int BS = kSlSK / 5, b = S / BS, bits = sl_bits(b), mv = (1 << (bits - 1)) - 1;
+    constexpr int pos = 8 * (sl_band_byte(b) + 2) + (S - b * BS) * bits;
+    const uint32_t u = sa_bits<pos, bits>(w) | 0x4B000000u;
+    return __fmul_rn(__fsub_rn(__uint_as_float(u), 8388608.0f + (float)mv), scl[b]);
+}
+
+template <int K>
+__device__ __forceinline__ void sa_term(float (&pr)[kSlNRes], float v)
+{
+    constexpr int r = kSaTerms.res[K];
+    constexpr bool neg = kSaTerms.neg[K] != 0;
+    pr[r] = neg ? __fsub_rn(pr[r], v) : __fadd_rn(pr[r], v);
+}
+// Terms [B, E) of the slot-sorted list whose slot is S.
+template <int S, int B, int E>
+__device__ __forceinline__ void sa_terms_of(float (&pr)[kSlNRes], float v)
+{
+    if constexpr (B < E) {
+        if constexpr (kSaTerms.slot[B] == S) sa_term<B>(pr, v);
+        sa_terms_of<S, B + 1, E>(pr, v);
+    }
+}
+
+__device__ __forceinline__ void sa_st4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d)
+{
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+                 : "memory");
+}
+__device__ __forceinline__ uint32_t sa_h2(float lo, float hi)
+{
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+template <int S>
+__device__ __forceinline__ float sa_skel_or0(const uint32_t (&w)[26], const float (&scl)[5])
+{
+    if constexpr (S < kSlSK) return sa_skel<S>(w, scl);
+    else return 0.0f;
+}
+template <int G, size_t... I>
+__device__ __forceinline__ void sa_group_vals(const uint32_t (&w)[26], const float (&scl)[5], float (&pr)[kSlNRes],
+                                              float (&v)[8], std::index_sequence<I...>)
+{
+    ((v[I] = sa_skel_or0<8 * G + (int)I>(w, scl)), ...);
+    (sa_terms_of<8 * G + (int)I, kSaTerms.grp[G], kSaTerms.grp[G + 1]>(pr, v[I]), ...);
+}
+// Skeleton group G (slots 8G..8G+7): values, their Möbius terms, and (for a
+// group of skeleton slots only) one 16-byte store of the fp16 row; the
+// values of the last, partial group are returned in v.
+template <int G>
+__device__ __forceinline__ void sa_group(const uint32_t (&w)[26], const float (&scl)[5], float (&pr)[kSlNRes],
+                                         uint32_t row, float (&v)[8])
+{
+    sa_group_vals<G>(w, scl, pr, v, std::make_index_sequence<8>{});
+    if constexpr (8 * G + 8 <= kSlSK)
+        sa_st4(row + 16 * G, sa_h2(v[0], v[1]), sa_h2(v[2], v[3]), sa_h2(v[4], v[5]), sa_h2(v[6], v[7]));
+}
+template <size_t... G>
+__device__ __forceinline__ void sa_groups(const uint32_t (&w)[26], const float (&scl)[5], float (&pr)[kSlNRes],
+                                          uint32_t row, float (&v)[8], std::index_sequence<G...>)
+{
+    (sa_group<(int)G>(w, scl, pr, row, v), ...);
+}
+template <int B>
+__device__ __forceinline__ float sa_scale(const uint32_t (&w)[26])
+{
+    const float s = __half2float(__ushort_as_half((unsigned short)sa_bits<8 * sl_band_byte(B), 16>(w)));
+    return fabsf(s) <= 65504.0f ? __fmul_rn(s, 0.0625f) : 0.0f;
+}
+template <size_t... B>
+__device__ __forceinline__ void sa_scales(const uint32_t (&w)[26], float (&scl)[5], std::index_sequence<B...>)
+{
+    ((scl[B] = sa_scale<(int)B>(w)), ...);
+}
+// Residual R (times 2^-4): the signed Möbius prediction plus the deviation.
+template <int R>
+__device__ __forceinline__ float sa_res(const uint32_t (&w)[26], const float (&pr)[kSlNRes], float step, float nc)
+{
+    const uint32_t lv = sa_bits<8 * kSlResOff + R * kSlNR, kSlNR>(w) | 0x4B000000u;
+    const float dev = __fmaf_rn(__fsub_rn(__uint_as_float(lv), 8388608.0f), step, nc);
+    const uint32_t sgn = sa_bits<8 * kSlSheetOff + R, 1>(w) << 31;
+    return __fadd_rn(__uint_as_float(__float_as_uint(pr[R]) ^ sgn), dev);
+}
+template <size_t... R>
+__device__ __forceinline__ void sa_residuals(const uint32_t (&w)[26], const float (&pr)[kSlNRes], float step,
+                                             float nc, float *c, std::index_sequence<R...>)
+{
+    ((c[R] = sa_res<(int)R>(w, pr, step, nc)), ...);
+}
+
+// One slot (row words in w, w[25] zero) to its fp16 staging row (shared-
+// memory address row): 160 halves, coefficients times 2^-4 in slot order.
+__device__ __forceinline__ void sa_slot_row(const uint32_t (&w)[26], uint32_t row)
+{
+    constexpr int NG = (kSlSK + 7) / 8;           // 15 groups; the last holds slots 112..114
+    constexpr int J0 = 8 * (NG - 1);
+    static_assert(kSlSK - J0 + kSlNRes <= 48 && J0 + 48 == 160, "tail of 48 halves");
+    float scl[5];
+    sa_scales(w, scl, std::make_index_sequence<5>{});
+    float pr[kSlNRes];
+#pragma unroll
+    for (int r = 0; r < kSlNRes; r++) pr[r] = 0.0f;
+    float v[8];
+    sa_groups(w, scl, pr, row, v, std::make_index_sequence<NG>{});
+    constexpr int L = 1 << kSlNR;
+    const float mag = __uint_as_float(sa_bits<8 * kSlMagOff, 32>(w));
+    const float step = __fmul_rn(__fdiv_rn(__fmul_rn(2.0f, __fmul_rn(mag, (float)kSlNR)), (float)(L - 1)), 0.0625f);
+    const float nc = -0.5f * (float)(L - 1) * step;
+    float c[48];
+#pragma unroll
+    for (int j = 0; j < 48; j++) c[j] = j < kSlSK - J0 ? v[j < 8 ? j : 0] : 0.0f;
+    sa_residuals(w, pr, step, nc, c + (kSlSK - J0), std::make_index_sequence<kSlNRes>{});
+#pragma unroll
+    for (int g = 0; g < 6; g++)
+        sa_st4(row + 2 * J0 + 16 * g, sa_h2(c[8 * g], c[8 * g + 1]), sa_h2(c[8 * g + 2], c[8 * g + 3]),
+               sa_h2(c[8 * g + 4], c[8 * g + 5]), sa_h2(c[8 * g + 6], c[8 * g + 7]));
+}
+
+__device__ __forceinline__ void sa_ldsm4(uint32_t addr, uint32_t (&r)[4])
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ void sa_ldsm4t(uint32_t addr, uint32_t (&r)[4])
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ void sa_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
+{
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// fp16 of x (hi) or of x - fp16(x) (lo).
+__device__ __forceinline__ __half sa_part(float x, int lo)
+{
+    const __half h = __float2half_rn(x);
+    return lo ? __float2half_rn(x - __half2float(h)) : h;
+}
+
+struct SaSmem {
+    uint32_t ring[kSaWarps][kSaStages][2][kSaTile / 4];
+    uint32_t ct[kSaWarps][32 * kSaRowHalves / 2];
+    uint32_t wt[kSaWarps][8 * 20];                  // weights [column][position], 40-half rows
+    unsigned long long bar[kSaWarps][kSaStages];
+    float q[4][160];                                // transformed queries, slot order, 2^F scaled
+    int qf[4];
+};
+
+// The transformed queries of the lane decode, one thread per (layer, query
+// head): q' = V q_pad * logit_scale * log2(e) in slot order (160 words,
+// six zeros at the end), times 2^F with F chosen so max|q'| lands in
+// [64, 128), and F itself in word 160.
+__global__ void __launch_bounds__(32)
+k_sa_query(SqAttn a)
+{
+    const int i = blockIdx.x * 32 + threadIdx.x;
+    if (i >= a.n_layers * a.n_q_heads) return;
+    const __half *qg = a.q + (long long)i * kSlHD;
+    float x[kSlPD];
+#pragma unroll
+    for (int j = 0; j < kSlPD; j++) x[j] = j < kSlHD ? __half2float(qg[j]) : 0.0f;
+    sl_stage<2, 1>(x);
+    sl_stage<7, 2>(x);
+    sl_stage<11, 14>(x);
+    const float s = a.logit_scale * 1.4426950408889634f;
+    float mx = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kSlPD; j++) mx = fmaxf(mx, fabsf(x[j] * s));
+    const int F = mx > 1e-30f ? 6 - ilogbf(mx) : 0;
+    const float sf = ldexpf(s, F);
+    float sk[kSlSK], rs[kSlNRes];
+    sl_gather(x, sk, rs, std::make_index_sequence<kSlSK>{});
+    sl_gather_res(x, rs, std::make_index_sequence<kSlNRes>{});
+    float *o = a.qws + (long long)i * kSaQWords;
+#pragma unroll
+    for (int j = 0; j < kSlSK; j++) o[j] = sk[j] * sf;
+#pragma unroll
+    for (int j = 0; j < kSlNRes; j++) o[kSlSK + j] = rs[j] * sf;
+#pragma unroll
+    for (int j = kSlPD; j < 160; j++) o[j] = 0.0f;
+    o[160] = (float)F;
+}
+
+__global__ void __launch_bounds__(kSaWarps * 32, 2)
+k_sq_attn_lane(SqAttn a)
+{
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    SaSmem &sm = *reinterpret_cast<SaSmem *>(smem_raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = lane >> 2, c = lane & 3;
+    const int split = blockIdx.x, h = blockIdx.y, li = blockIdx.z;
+    const int G = a.group;
+
+    // ---- copy ring: tiles of 32 positions, warp w takes tiles w, w+4, ...
+    const int t_begin = split * a.chunk, t_end = min(a.kv_len, t_begin + a.chunk);
+    const int n_blk = (t_end - t_begin + 31) / 32;
+    const int n_my = warp < n_blk ? (n_blk - warp + kSaWarps - 1) / kSaWarps : 0;
+    const long long slot = (long long)(a.layer0 + li) * a.n_kv_heads + h;
+    const uint8_t *kbase = a.k_cache + slot * a.k_slot_stride;
+    const uint8_t *vbase = a.v_cache + slot * a.v_slot_stride;
+    const uint32_t bar0 = spb::smem_u32(&sm.bar[warp][0]);
+    const uint32_t ring0 = spb::smem_u32(&sm.ring[warp][0][0][0]);
+    uint64_t policy = 0;
+    if (lane == 0) {
+        for (int st = 0; st < kSaStages; st++) spb::mbar_init(bar0 + 8 * st, 1);
+        spb::mbar_init_fence();
+        policy = spb::evict_first_policy();
+    }
+    __syncwarp();
+    auto blk_pos = [&](int k) { return t_begin + (warp + k * kSaWarps) * 32; };
+    auto issue = [&](int k) {
+        const int p0 = blk_pos(k);
+        if (p0 + 32 > t_end) return;
+        const int st = k % kSaStages;
+        const uint32_t bar = bar0 + 8 * st, dst = ring0 + st * 2 * kSaTile;
+        spb::fence_proxy_async();
+        spb::mbar_expect_tx(bar, 2 * kSaTile);
+        spb::bulk_g2s(dst, kbase + (long long)p0 * kSlBytes, kSaTile, bar, policy);
+        spb::bulk_g2s(dst + kSaTile, vbase + (long long)p0 * kSlBytes, kSaTile, bar, policy);
+    };
+    if (lane == 0)
+        for (int k = 0; k < kSaStages && k < n_my; k++) issue(k);
+
+    // ---- queries (k_sa_query's output for this layer and KV head) -------
+    for (int i = threadIdx.x; i < 4 * 160; i += blockDim.x) {
+        const int g = i / 160, j = i - g * 160;
+        sm.q[g][j] = g < G ? a.qws[((long long)li * a.n_q_heads + h * G + g) * kSaQWords + j] : 0.0f;
+    }
+    if (threadIdx.x < 4) {
+        const int g = threadIdx.x;
+        sm.qf[g] = g < G ? (int)a.qws[((long long)li * a.n_q_heads + h * G + g) * kSaQWords + 160] : 0;
+    }
+    __syncthreads();
+    // B fragments of the score MMAs: column r = query r/2, half r%2.
+    uint32_t bq[10][2];
+    {
+        const int g = r >> 1, lo = r & 1;
+#pragma unroll
+        for (int ks = 0; ks < 10; ks++)
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+                const int k0 = 16 * ks + 8 * hh + 2 * c;
+                const __half2 v = __halves2half2(sa_part(sm.q[g][k0], lo), sa_part(sm.q[g][k0 + 1], lo));
+                bq[ks][hh] = *reinterpret_cast<const uint32_t *>(&v);
+            }
+    }
+    // score of query c = kc * (acc_hi + acc_lo): 2^-F for the query, 2^4 for
+    // the coefficients
+    const float kc = ldexpf(1.0f, 4 - sm.qf[c]);
+
+    const uint32_t ct0 = spb::smem_u32(&sm.ct[warp][0]);
+    const uint32_t my_row = ct0 + lane * (2 * kSaRowHalves);
+    __half *wt = reinterpret_cast<__half *>(&sm.wt[warp][0]);
+    const uint32_t wt0 = spb::smem_u32(wt);
+    // ldmatrix row addresses: K side (rows = positions), V side (transposed)
+    const int lq = lane >> 3, l8 = lane & 7;
+    const uint32_t ka = ct0 + ((lq & 1) * 8 + l8) * (2 * kSaRowHalves) + (lq >> 1) * 16;
+    const uint32_t va = ct0 + ((lq >> 1) * 8 + l8) * (2 * kSaRowHalves) + (lq & 1) * 16;
+
+    float o[10][4];
+#pragma unroll
+    for (int mt = 0; mt < 10; mt++) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.0f;
+    float m_run = -INFINITY, l_sum = 0.0f;
+
+    bool failed = false;
+    int k_fail = 0;
+    for (int k = 0; k < n_my; k++) {
+        const int st = k % kSaStages;
+        const int p0 = blk_pos(k);
+        const int nvalid = min(32, t_end - p0);
+        uint32_t *krow = sm.ring[warp][st][0];
+        uint32_t *vrow = sm.ring[warp][st][1];
+        if (nvalid == 32) {
+            if (!spb::wait_stage(bar0 + 8 * st, (k / kSaStages) & 1, a.status)) {
+                failed = true;
+                k_fail = k;
+                break;
+            }
+        } else {
+            // ragged last tile: lanes copy the valid rows, zero the rest
+            constexpr int TW = kSlBytes / 4;
+            const uint32_t *ks = reinterpret_cast<const uint32_t *>(kbase + (long long)p0 * kSlBytes);
+            const uint32_t *vs = reinterpret_cast<const uint32_t *>(vbase + (long long)p0 * kSlBytes);
+            for (int i = lane; i < 32 * TW; i += 32) {
+                krow[i] = i < nvalid * TW ? ks[i] : 0u;
+                vrow[i] = i < nvalid * TW ? vs[i] : 0u;
+            }
+            __syncwarp();
+        }
+        // ---- K: coefficient rows, score MMAs ----------------------------
+        {
+            uint32_t w[26];
+#pragma unroll
+            for (int i = 0; i < 25; i++) w[i] = krow[lane * 25 + i];
+            w[25] = 0u;
+            sa_slot_row(w, my_row);
+        }
+        __syncwarp();
+        float s[2][4];
+#pragma unroll
+        for (int mt = 0; mt < 2; mt++) {
+            s[mt][0] = s[mt][1] = s[mt][2] = s[mt][3] = 0.0f;
+#pragma unroll
+            for (int ks = 0; ks < 10; ks++) {
+                uint32_t af[4];
+                sa_ldsm4(ka + mt * 16 * (2 * kSaRowHalves) + ks * 32, af);
+                sa_mma(s[mt], af, bq[ks][0], bq[ks][1]);
+            }
+        }
+        // ---- online softmax of query c over positions r, r+8, 16+r, 24+r -
+        float sc[4];
+#pragma unroll
+        for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+                const int t = 16 * mt + 8 * hh + r;
+                sc[2 * mt + hh] = t < nvalid ? kc * (s[mt][2 * hh] + s[mt][2 * hh + 1]) : -INFINITY;
+            }
+        float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        if (mx > m_run) {
+            const float alpha = ex2_fast(m_run - mx);
+            m_run = mx;
+            l_sum *= alpha;
+#pragma unroll
+            for (int mt = 0; mt < 10; mt++) {
+                o[mt][0] *= alpha; o[mt][1] *= alpha; o[mt][2] *= alpha; o[mt][3] *= alpha;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float p = ex2_fast(sc[i] - m_run);
+            l_sum += p;
+            const int t = 16 * (i >> 1) + 8 * (i & 1) + r;
+            const __half ph = __float2half_rn(p);
+            wt[(2 * c) * 40 + t] = ph;
+            wt[(2 * c + 1) * 40 + t] = __float2half_rn(p - __half2float(ph));
+        }
+        __syncwarp();
+        // ---- V: coefficient rows, value MMAs ----------------------------
+        {
+            uint32_t w[26];
+#pragma unroll
+            for (int i = 0; i < 25; i++) w[i] = vrow[lane * 25 + i];
+            w[25] = 0u;
+            sa_slot_row(w, my_row);
+        }
+        __syncwarp();
+        if (lane == 0 && k + kSaStages < n_my) issue(k + kSaStages);
+        uint32_t bw[2][2];
+#pragma unroll
+        for (int kt = 0; kt < 2; kt++)
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++)
+                bw[kt][hh] = lds32(wt0 + 2 * (r * 40 + 16 * kt + 8 * hh + 2 * c));
+#pragma unroll
+        for (int mt = 0; mt < 10; mt++)
+#pragma unroll
+            for (int kt = 0; kt < 2; kt++) {
+                uint32_t af[4];
+                sa_ldsm4t(va + kt * 16 * (2 * kSaRowHalves) + mt * 32, af);
+                sa_mma(o[mt], af, bw[kt][0], bw[kt][1]);
+            }
+        __syncwarp();
+    }
+    if (failed) {
+        for (int k = k_fail; k < n_my && k < k_fail + kSaStages; k++)
+            if (blk_pos(k) + 32 <= t_end) spb::wait_stage(bar0 + 8 * (k % kSaStages), (k / kSaStages) & 1, nullptr);
+    }
+    // ---- merge the warps, write the CTA's partial ---------------------------
+#pragma unroll
+    for (int o2 = 4; o2 < 32; o2 <<= 1) l_sum += __shfl_xor_sync(0xffffffffu, l_sum, o2);
+    __syncwarp();
+    float *mw = reinterpret_cast<float *>(&sm.ct[warp][0]);       // [4 queries][4 + 160]
+#pragma unroll
+    for (int mt = 0; mt < 10; mt++)
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++)
+            mw[c * 164 + 4 + 16 * mt + 8 * hh + r] = 16.0f * (o[mt][2 * hh] + o[mt][2 * hh + 1]);
+    if (r == 0) { mw[c * 164] = m_run; mw[c * 164 + 1] = l_sum; }
+    __syncthreads();
+    for (int g = 0; g < G; g++) {
+        float M = -INFINITY;
+        for (int w = 0; w < kSaWarps; w++) M = fmaxf(M, reinterpret_cast<const float *>(&sm.ct[w][0])[g * 164]);
+        float *part = sq_partial(a, kSlPD, li, h * G + g, split);
+        for (int i = threadIdx.x; i < kSlPD + 1; i += blockDim.x) {
+            const int j = i < kSlPD ? c_sa_j_of.v[i] : 0;
+            float v = 0.0f;
+            for (int w = 0; w < kSaWarps; w++) {
+                const float *aw = reinterpret_cast<const float *>(&sm.ct[w][0]) + g * 164;
+                const float wgt = aw[0] == -INFINITY ? 0.0f : exp2f(aw[0] - M);
+                v += wgt * (i < kSlPD ? aw[4 + j] : aw[1]);
+            }
+            if (i < kSlPD) part[4 + i] = v;
+            else { part[0] = M; part[1] = v; }
+        }
+    }
+}
+
 // --------------------------------------------------------------- host --
 
 bool sq_squarefree(int m)
@@ -2234,6 +2722,21 @@ bool sq_lane_fits(const SpSqDev &t, const SqIo &io)
             t.bl.byte_off[b] != T.band_byte[b])
             return false;
     return !(((uintptr_t)io.in & 15) || ((uintptr_t)io.cache & 3) || (io.slot_stride & 3));
+}
+
+// The fused lane decode's layout: the compiled config-2 slot.
+bool sa_fits(const SpSqDev &t)
+{
+    constexpr const SlTab<kSlSK> &T = kSlTab;
+    if (t.hier || !t.use_spinor || t.hd != kSlHD || t.pd != kSlPD || t.n_skel != kSlSK || t.n_res != kSlNRes ||
+        t.res_bits != kSlNR || t.bl.n_bands != 5 || t.mag_off != T.mag_off || t.res_off != T.res_off ||
+        t.sheet_off != T.sheet_off || t.bytes_per_pos != T.bytes || t.n_terms != T.off[kSlNRes])
+        return false;
+    for (int b = 0; b < 5; b++)
+        if (t.bl.bits[b] != sl_bits(b) || t.bl.off[b] != T.band_off[b] || t.bl.size[b] != T.band_size[b] ||
+            t.bl.byte_off[b] != T.band_byte[b])
+            return false;
+    return true;
 }
 
 bool sq_lane_map(CUtensorMap *m, const SqIo &io, int dtype)
@@ -3084,6 +3587,13 @@ int hr_build(const sp_cuda_hier_cache_t *hc)
 
 extern "C" {
 
+// Bytes of the lane decode's query area, after the partials and the status
+// word of the attention workspace.
+static size_t sq_qws_bytes(const sp_config_t *cfg)
+{
+    return (size_t)cfg->n_layers * 8 * cfg->n_heads_kv * kSaQWords * sizeof(float);
+}
+
 int sp_cuda_sqfree_cache_init_ex(sp_cuda_sqfree_cache_t *cc, const sp_config_t *cfg, int max_seq_len,
                                  int residual_bits, int use_spinor, float sk_frac, void *stream)
 {
@@ -3211,8 +3721,10 @@ int sp_cuda_sqfree_cache_init_ex(sp_cuda_sqfree_cache_t *cc, const sp_config_t *
     cc->attn_ws_bytes = (size_t)cfg->n_layers * 8 * cfg->n_heads_kv * kSqMaxSplits * (pd + 4) * sizeof(float);
     // + 16 bytes: the decode's status word follows the partials
     if ((rc = sq_upload_constants()) ||
-        (rc = sp_check_cuda(cudaMalloc(&cc->d_attn_ws, cc->attn_ws_bytes + 16), "cudaMalloc sqfree workspace")) ||
-        (rc = sp_check_cuda(cudaMemset(cc->d_attn_ws, 0, cc->attn_ws_bytes + 16), "sqfree workspace")) ||
+        (rc = sp_check_cuda(cudaMalloc(&cc->d_attn_ws, cc->attn_ws_bytes + 16 + sq_qws_bytes(cfg)),
+                            "cudaMalloc sqfree workspace")) ||
+        (rc = sp_check_cuda(cudaMemset(cc->d_attn_ws, 0, cc->attn_ws_bytes + 16 + sq_qws_bytes(cfg)),
+                            "sqfree workspace")) ||
         (rc = sp_check_cuda(cudaDeviceSynchronize(), "sqfree_cache_init"))) {
         sp_cuda_sqfree_cache_free(cc);
         return rc;
@@ -3466,6 +3978,50 @@ int sp_cuda_sqfree_attn_decode(const sp_cuda_sqfree_cache_t *cc, int layer0, int
                          a.k_slot_stride % 16 == 0 && a.v_slot_stride % 16 == 0 &&
                          ((uintptr_t)a.k_cache & 15) == 0 && ((uintptr_t)a.v_cache & 15) == 0 &&
                          getenv("SHANNON_PRIME_SQFREE_DECODE_REG") == nullptr;
+    // Lane-per-slot tensor-core kernel: the compiled config-2 layout for K
+    // and V, up to 4 queries per KV head, 16-byte aligned 32-position tiles.
+    const bool lane_tc = a.group <= 4 && sa_fits(tk) && sa_fits(tv) && a.k_slot_stride % 16 == 0 &&
+                         a.v_slot_stride % 16 == 0 && ((uintptr_t)a.k_cache & 15) == 0 &&
+                         ((uintptr_t)a.v_cache & 15) == 0 && getenv("SHANNON_PRIME_SQFREE_DECODE_BLOCKED") == nullptr &&
+                         getenv("SHANNON_PRIME_SQFREE_DECODE_REG") == nullptr;
+    if (lane_tc && kv_len > 0) {
+        static std::atomic<int> occ_dev{-1}, occ_val{0}, occ_sms{0};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const size_t sm = sizeof(SaSmem);
+        if (occ_dev.load() != dev) {
+            if (cudaFuncSetAttribute(k_sq_attn_lane, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
+                return sp_check_cuda(cudaGetLastError(), "sqfree lane attention smem attribute");
+            int occ = 0, sms = 0;
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_sq_attn_lane, kSaWarps * 32, sm);
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+            occ_val = occ < 1 ? 1 : occ;
+            occ_sms = sms < 1 ? 148 : sms;
+            occ_dev = dev;
+        }
+        // Splits: the count (at most one tile per warp's worth of positions
+        // per split and kSqMaxSplits) whose CTAs fill the last wave best.
+        const long long slots = (long long)occ_val.load() * occ_sms.load();
+        const int max_s = std::max(1, std::min(kSqMaxSplits, (kv_len + 32 * kSaWarps - 1) / (32 * kSaWarps)));
+        int best = 1;
+        double best_eff = -1.0;
+        for (int sp = 1; sp <= max_s; sp++) {
+            const long long ctas = (long long)units * sp;
+            const long long waves = (ctas + slots - 1) / slots;
+            const double eff = (double)ctas / (double)(waves * slots);
+            if (eff > best_eff + 1e-9) { best_eff = eff; best = sp; }
+        }
+        a.chunk = ((kv_len + best - 1) / best + 31) / 32 * 32;
+        a.n_splits = (kv_len + a.chunk - 1) / a.chunk;
+        a.qws = reinterpret_cast<float *>(reinterpret_cast<char *>(cc->d_attn_ws) + cc->attn_ws_bytes + 16);
+        k_sa_query<<<(n_layers * n_q_heads + 31) / 32, 32, 0, s>>>(a);
+        k_sq_attn_lane<<<dim3(a.n_splits, H, n_layers), kSaWarps * 32, sm, s>>>(a);
+        int rc = sp_check_cuda(cudaGetLastError(), "sqfree lane attention launch");
+        if (rc) return rc;
+        const size_t smc = (224 + tk.pd + 8) * sizeof(float);
+        k_sq_attn_combine<<<dim3(n_q_heads, n_layers), 32, smc, s>>>(tk, a);
+        return sp_check_cuda(cudaGetLastError(), "sqfree attention combine launch");
+    }
     if (blocked && a.n_splits > 0) {
         a.chunk = (a.chunk + 15) / 16 * 16;
         a.n_splits = (kv_len + a.chunk - 1) / a.chunk;

@@ -167,9 +167,10 @@ def test_hier_single_vector_api(cuda):
 
 @pytest.mark.parametrize("T", [5, 64, 1001])
 def test_sqfree_blocked_and_register_decodes_agree(cuda, T, monkeypatch):
-    """The blocked decode (4-position bulk-copied blocks, balanced residual
-    lanes) and the register kernel it replaces give the same attention, and
-    the blocked decode leaves its status word clear."""
+    """The lane decode (one thread per slot, tensor-core contractions), the
+    blocked decode (4-position bulk-copied blocks, balanced residual lanes)
+    and the register kernel give the same attention, and the decodes leave
+    their status word clear."""
     import torch
     H, L, G, hd = 2, 2, 4, 128
     cache = SqfreeCache(hd, L, H, 2048, sk_frac=0.75)
@@ -178,14 +179,15 @@ def test_sqfree_blocked_and_register_decodes_agree(cuda, T, monkeypatch):
     cache.write_kv_tokens(0, 0, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda())
     q = torch.from_numpy(synth.q_np(9, L, H * G, hd, 1.0 / np.sqrt(hd))).cuda()
     outs = []
-    for reg in (False, True):
-        if reg:
-            monkeypatch.setenv("SHANNON_PRIME_SQFREE_DECODE_REG", "1")
+    for env in (None, "SHANNON_PRIME_SQFREE_DECODE_BLOCKED", "SHANNON_PRIME_SQFREE_DECODE_REG"):
+        if env:
+            monkeypatch.setenv(env, "1")
         out = torch.empty(L, H * G, hd, dtype=torch.float16, device="cuda")
         cache.attn_decode(0, L, q, T, out, logit_scale=0.7)
         torch.cuda.synchronize()
         outs.append(out.float().cpu().numpy())
-    assert _rel_l2(outs[0], outs[1]) <= 1e-3
+    assert _rel_l2(outs[0], outs[2]) <= 1e-3
+    assert _rel_l2(outs[1], outs[2]) <= 1e-3
     # status word: 4 bytes after the partials in the decode workspace
     cudart = C.CDLL("libcudart.so.12") if _has_lib("libcudart.so.12") else None
     if cudart is not None:
