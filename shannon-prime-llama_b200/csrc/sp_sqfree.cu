@@ -2145,7 +2145,7 @@ k_sq_decode_lane(const uint8_t *slab, int n_pos, unsigned int *status, const __g
 // Residual predictions are accumulated slot by slot (each skeleton value is
 // added into the residuals whose Möbius terms name it, in slot order) so a
 // thread keeps 39 running sums instead of all 115 skeleton values.
-constexpr int kSaWarps = 4, kSaStages = 2;
+constexpr int kSaWarps = 4;
 constexpr int kSaRowHalves = 168;                 // 160 + 8: conflict-free ldmatrix rows
 constexpr int kSaTile = 32 * kSlBytes;            // 3200 bytes of K (or V) rows per tile
 
@@ -2348,10 +2348,11 @@ __device__ __forceinline__ __half sa_part(float x, int lo)
 }
 
 struct SaSmem {
-    uint32_t ring[kSaWarps][kSaStages][2][kSaTile / 4];
+    uint32_t kring[kSaWarps][kSaTile / 4];          // one tile of K rows per warp
+    uint32_t vring[kSaWarps][kSaTile / 4];          // and of V rows
     uint32_t ct[kSaWarps][32 * kSaRowHalves / 2];
     uint32_t wt[kSaWarps][8 * 20];                  // weights [column][position], 40-half rows
-    unsigned long long bar[kSaWarps][kSaStages];
+    unsigned long long bar[kSaWarps][2];            // K, V copy completion
     float q[4][160];                                // transformed queries, slot order, 2^F scaled
     int qf[4];
 };
@@ -2391,7 +2392,7 @@ k_sa_query(SqAttn a)
     o[160] = (float)F;
 }
 
-__global__ void __launch_bounds__(kSaWarps * 32, 2)
+__global__ void __launch_bounds__(kSaWarps * 32, 3)
 k_sq_attn_lane(SqAttn a)
 {
     extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -2401,7 +2402,9 @@ k_sq_attn_lane(SqAttn a)
     const int split = blockIdx.x, h = blockIdx.y, li = blockIdx.z;
     const int G = a.group;
 
-    // ---- copy ring: tiles of 32 positions, warp w takes tiles w, w+4, ...
+    // ---- copies: tiles of 32 positions, warp w takes tiles w, w+4, ...;
+    // one K and one V buffer per warp, each refilled as soon as its rows are
+    // in registers, so a copy has the rest of the tile's work to land.
     const int t_begin = split * a.chunk, t_end = min(a.kv_len, t_begin + a.chunk);
     const int n_blk = (t_end - t_begin + 31) / 32;
     const int n_my = warp < n_blk ? (n_blk - warp + kSaWarps - 1) / kSaWarps : 0;
@@ -2409,27 +2412,28 @@ k_sq_attn_lane(SqAttn a)
     const uint8_t *kbase = a.k_cache + slot * a.k_slot_stride;
     const uint8_t *vbase = a.v_cache + slot * a.v_slot_stride;
     const uint32_t bar0 = spb::smem_u32(&sm.bar[warp][0]);
-    const uint32_t ring0 = spb::smem_u32(&sm.ring[warp][0][0][0]);
+    const uint32_t kring0 = spb::smem_u32(&sm.kring[warp][0]), vring0 = spb::smem_u32(&sm.vring[warp][0]);
     uint64_t policy = 0;
     if (lane == 0) {
-        for (int st = 0; st < kSaStages; st++) spb::mbar_init(bar0 + 8 * st, 1);
+        spb::mbar_init(bar0, 1);
+        spb::mbar_init(bar0 + 8, 1);
         spb::mbar_init_fence();
         policy = spb::evict_first_policy();
     }
     __syncwarp();
     auto blk_pos = [&](int k) { return t_begin + (warp + k * kSaWarps) * 32; };
-    auto issue = [&](int k) {
+    int issued_k = 0, issued_v = 0, waited_k = 0, waited_v = 0;   // copies issued / completions consumed
+    auto issue = [&](int k, int half) {
         const int p0 = blk_pos(k);
         if (p0 + 32 > t_end) return;
-        const int st = k % kSaStages;
-        const uint32_t bar = bar0 + 8 * st, dst = ring0 + st * 2 * kSaTile;
+        const uint32_t bar = bar0 + 8 * half;
         spb::fence_proxy_async();
-        spb::mbar_expect_tx(bar, 2 * kSaTile);
-        spb::bulk_g2s(dst, kbase + (long long)p0 * kSlBytes, kSaTile, bar, policy);
-        spb::bulk_g2s(dst + kSaTile, vbase + (long long)p0 * kSlBytes, kSaTile, bar, policy);
+        spb::mbar_expect_tx(bar, kSaTile);
+        spb::bulk_g2s(half ? vring0 : kring0, (half ? vbase : kbase) + (long long)p0 * kSlBytes, kSaTile, bar,
+                      policy);
+        if (half) issued_v++; else issued_k++;
     };
-    if (lane == 0)
-        for (int k = 0; k < kSaStages && k < n_my; k++) issue(k);
+    if (lane == 0 && n_my > 0) { issue(0, 0); issue(0, 1); }
 
     // ---- queries (k_sa_query's output for this layer and KV head) -------
     for (int i = threadIdx.x; i < 4 * 160; i += blockDim.x) {
@@ -2473,112 +2477,116 @@ k_sq_attn_lane(SqAttn a)
     float m_run = -INFINITY, l_sum = 0.0f;
 
     bool failed = false;
-    int k_fail = 0;
     for (int k = 0; k < n_my; k++) {
-        const int st = k % kSaStages;
         const int p0 = blk_pos(k);
         const int nvalid = min(32, t_end - p0);
-        uint32_t *krow = sm.ring[warp][st][0];
-        uint32_t *vrow = sm.ring[warp][st][1];
-        if (nvalid == 32) {
-            if (!spb::wait_stage(bar0 + 8 * st, (k / kSaStages) & 1, a.status)) {
-                failed = true;
-                k_fail = k;
-                break;
-            }
-        } else {
-            // ragged last tile: lanes copy the valid rows, zero the rest
+        const uint32_t *krow = sm.kring[warp];
+        const uint32_t *vrow = sm.vring[warp];
+        if (nvalid < 32) {
+            // ragged last tile (no copy was issued for it): lanes copy the
+            // valid rows and zero the rest
             constexpr int TW = kSlBytes / 4;
             const uint32_t *ks = reinterpret_cast<const uint32_t *>(kbase + (long long)p0 * kSlBytes);
             const uint32_t *vs = reinterpret_cast<const uint32_t *>(vbase + (long long)p0 * kSlBytes);
             for (int i = lane; i < 32 * TW; i += 32) {
-                krow[i] = i < nvalid * TW ? ks[i] : 0u;
-                vrow[i] = i < nvalid * TW ? vs[i] : 0u;
+                sm.kring[warp][i] = i < nvalid * TW ? ks[i] : 0u;
+                sm.vring[warp][i] = i < nvalid * TW ? vs[i] : 0u;
             }
             __syncwarp();
         }
-        // ---- K: coefficient rows, score MMAs ----------------------------
-        {
-            uint32_t w[26];
-#pragma unroll
-            for (int i = 0; i < 25; i++) w[i] = krow[lane * 25 + i];
-            w[25] = 0u;
-            sa_slot_row(w, my_row);
-        }
-        __syncwarp();
-        float s[2][4];
-#pragma unroll
-        for (int mt = 0; mt < 2; mt++) {
-            s[mt][0] = s[mt][1] = s[mt][2] = s[mt][3] = 0.0f;
-#pragma unroll
-            for (int ks = 0; ks < 10; ks++) {
-                uint32_t af[4];
-                sa_ldsm4(ka + mt * 16 * (2 * kSaRowHalves) + ks * 32, af);
-                sa_mma(s[mt], af, bq[ks][0], bq[ks][1]);
+        // K half, then V half; one copy of the (long, straight-line) slot
+        // rebuild serves both.
+#pragma unroll 1
+        for (int half = 0; half < 2; half++) {
+            if (nvalid == 32) {
+                if (!spb::wait_stage(bar0 + 8 * half, (half ? waited_v : waited_k) & 1, a.status)) {
+                    failed = true;
+                    break;
+                }
+                if (half) waited_v++; else waited_k++;
             }
-        }
-        // ---- online softmax of query c over positions r, r+8, 16+r, 24+r -
-        float sc[4];
+            {
+                const uint32_t *rows = half ? vrow : krow;
+                uint32_t w[26];
 #pragma unroll
-        for (int mt = 0; mt < 2; mt++)
-#pragma unroll
-            for (int hh = 0; hh < 2; hh++) {
-                const int t = 16 * mt + 8 * hh + r;
-                sc[2 * mt + hh] = t < nvalid ? kc * (s[mt][2 * hh] + s[mt][2 * hh + 1]) : -INFINITY;
+                for (int i = 0; i < 25; i++) w[i] = rows[lane * 25 + i];
+                w[25] = 0u;
+                __syncwarp();
+                if (lane == 0 && k + 1 < n_my) issue(k + 1, half);
+                sa_slot_row(w, my_row);
             }
-        float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-        if (mx > m_run) {
-            const float alpha = ex2_fast(m_run - mx);
-            m_run = mx;
-            l_sum *= alpha;
+            __syncwarp();
+            if (half == 0) {
+                // ---- scores, then the online softmax of query c over
+                // positions r, r+8, 16+r, 24+r
+                float s[2][4];
 #pragma unroll
-            for (int mt = 0; mt < 10; mt++) {
-                o[mt][0] *= alpha; o[mt][1] *= alpha; o[mt][2] *= alpha; o[mt][3] *= alpha;
+                for (int mt = 0; mt < 2; mt++) {
+                    s[mt][0] = s[mt][1] = s[mt][2] = s[mt][3] = 0.0f;
+#pragma unroll
+                    for (int ks = 0; ks < 10; ks++) {
+                        uint32_t af[4];
+                        sa_ldsm4(ka + mt * 16 * (2 * kSaRowHalves) + ks * 32, af);
+                        sa_mma(s[mt], af, bq[ks][0], bq[ks][1]);
+                    }
+                }
+                float sc[4];
+#pragma unroll
+                for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+                    for (int hh = 0; hh < 2; hh++) {
+                        const int t = 16 * mt + 8 * hh + r;
+                        sc[2 * mt + hh] = t < nvalid ? kc * (s[mt][2 * hh] + s[mt][2 * hh + 1]) : -INFINITY;
+                    }
+                float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                if (mx > m_run) {
+                    const float alpha = ex2_fast(m_run - mx);
+                    m_run = mx;
+                    l_sum *= alpha;
+#pragma unroll
+                    for (int mt = 0; mt < 10; mt++) {
+                        o[mt][0] *= alpha; o[mt][1] *= alpha; o[mt][2] *= alpha; o[mt][3] *= alpha;
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float p = ex2_fast(sc[i] - m_run);
+                    l_sum += p;
+                    const int t = 16 * (i >> 1) + 8 * (i & 1) + r;
+                    const __half ph = __float2half_rn(p);
+                    wt[(2 * c) * 40 + t] = ph;
+                    wt[(2 * c + 1) * 40 + t] = __float2half_rn(p - __half2float(ph));
+                }
+            } else {
+                // ---- values
+                uint32_t bw[2][2];
+#pragma unroll
+                for (int kt = 0; kt < 2; kt++)
+#pragma unroll
+                    for (int hh = 0; hh < 2; hh++)
+                        bw[kt][hh] = lds32(wt0 + 2 * (r * 40 + 16 * kt + 8 * hh + 2 * c));
+#pragma unroll
+                for (int mt = 0; mt < 10; mt++)
+#pragma unroll
+                    for (int kt = 0; kt < 2; kt++) {
+                        uint32_t af[4];
+                        sa_ldsm4t(va + kt * 16 * (2 * kSaRowHalves) + mt * 32, af);
+                        sa_mma(o[mt], af, bw[kt][0], bw[kt][1]);
+                    }
             }
+            __syncwarp();
         }
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float p = ex2_fast(sc[i] - m_run);
-            l_sum += p;
-            const int t = 16 * (i >> 1) + 8 * (i & 1) + r;
-            const __half ph = __float2half_rn(p);
-            wt[(2 * c) * 40 + t] = ph;
-            wt[(2 * c + 1) * 40 + t] = __float2half_rn(p - __half2float(ph));
-        }
-        __syncwarp();
-        // ---- V: coefficient rows, value MMAs ----------------------------
-        {
-            uint32_t w[26];
-#pragma unroll
-            for (int i = 0; i < 25; i++) w[i] = vrow[lane * 25 + i];
-            w[25] = 0u;
-            sa_slot_row(w, my_row);
-        }
-        __syncwarp();
-        if (lane == 0 && k + kSaStages < n_my) issue(k + kSaStages);
-        uint32_t bw[2][2];
-#pragma unroll
-        for (int kt = 0; kt < 2; kt++)
-#pragma unroll
-            for (int hh = 0; hh < 2; hh++)
-                bw[kt][hh] = lds32(wt0 + 2 * (r * 40 + 16 * kt + 8 * hh + 2 * c));
-#pragma unroll
-        for (int mt = 0; mt < 10; mt++)
-#pragma unroll
-            for (int kt = 0; kt < 2; kt++) {
-                uint32_t af[4];
-                sa_ldsm4t(va + kt * 16 * (2 * kSaRowHalves) + mt * 32, af);
-                sa_mma(o[mt], af, bw[kt][0], bw[kt][1]);
-            }
-        __syncwarp();
+        if (failed) break;
     }
-    if (failed) {
-        for (int k = k_fail; k < n_my && k < k_fail + kSaStages; k++)
-            if (blk_pos(k) + 32 <= t_end) spb::wait_stage(bar0 + 8 * (k % kSaStages), (k / kSaStages) & 1, nullptr);
+    if (failed && lane == 0) {
+        // bounded waits for this warp's copies still in flight before exit
+        for (; waited_k < issued_k; waited_k++) spb::wait_stage(bar0, waited_k & 1, nullptr);
+        for (; waited_v < issued_v; waited_v++) spb::wait_stage(bar0 + 8, waited_v & 1, nullptr);
     }
+    __syncwarp();
     // ---- merge the warps, write the CTA's partial ---------------------------
 #pragma unroll
     for (int o2 = 4; o2 < 32; o2 <<= 1) l_sum += __shfl_xor_sync(0xffffffffu, l_sum, o2);
