@@ -2839,13 +2839,6 @@ int sq_launch_encode(const SpSqDev &t, SqIo io, int dtype, cudaStream_t s, unsig
     const size_t sm = sq_smem_bytes(t);
     io.store_width = store_width_for(t.bytes_per_pos, io.slot_stride, io.cache);
     const int slots = io.n_layers * io.nh;
-    // enough CTAs for ~4 waves of 148 SMs, at least one warp-round each
-    int chunks = (148 * 4 + slots - 1) / slots;
-    const int max_chunks = (io.n_tok + kSqWarps - 1) / kSqWarps;
-    if (chunks > max_chunks) chunks = max_chunks;
-    if (chunks < 1) chunks = 1;
-    io.tokens_per_cta = (io.n_tok + chunks - 1) / chunks;
-    dim3 grid(chunks, slots);
     const int pd = sq_plan_pd(t);
     void (*k)(SpSqDev, SqIo) = nullptr;
 #define SQ_ENC(T)                                                                          \
@@ -2859,6 +2852,26 @@ int sq_launch_encode(const SpSqDev &t, SqIo io, int dtype, cudaStream_t s, unsig
     }
 #undef SQ_ENC
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    // Token chunks per slot: the count (from enough for ~4 waves up to 4x
+    // that, at least one warp-round of tokens each) whose CTAs fill the last
+    // wave best, so a long call does not end on a partly empty wave.
+    int occ = 0, dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, kSqWarps * 32, sm);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long resident = (long long)std::max(occ, 1) * std::max(sms, 1);
+    const int max_chunks = std::max(1, (io.n_tok + kSqWarps - 1) / kSqWarps);
+    const int c0 = std::min(max_chunks, std::max(1, (int)((4 * resident + slots - 1) / slots)));
+    int chunks = c0;
+    double best = -1.0;
+    for (int c = c0; c <= std::min(max_chunks, 4 * c0); c++) {
+        const long long ctas = (long long)slots * c;
+        const double eff = (double)ctas / (double)(((ctas + resident - 1) / resident) * resident);
+        if (eff > best + 1e-3) { best = eff; chunks = c; }
+    }
+    io.tokens_per_cta = (io.n_tok + chunks - 1) / chunks;
+    chunks = (io.n_tok + io.tokens_per_cta - 1) / io.tokens_per_cta;
+    dim3 grid(chunks, slots);
     k<<<grid, kSqWarps * 32, sm, s>>>(t, io);
     return sp_check_cuda(cudaGetLastError(), "sqfree/hier encode launch");
 }
