@@ -4,6 +4,8 @@ float64 Kronecker-product Hartley matrix, the Knight mask and Möbius CSR
 against a direct restatement, slot sizes, the lane-tree reduction order, and
 round-trip quality."""
 import math
+import sys
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -134,3 +136,27 @@ def test_hier_round_trip_with_fitted_predictor():
     W = O.hier_fit_W(k[:2048], H)
     kr = O.hier_read(O.hier_write(k[2048:], H, W), H, W)
     assert O.mean_vector_correlation(k[2048:], kr) > 0.9
+
+
+def test_hier_prediction_order_changes_slot_bytes():
+    """Why the hier encoder keeps the W . skeleton product as the oracle's
+    sequential fp32 fma chain instead of a tensor-core product: a prediction
+    summed in another order, even an exactly rounded one from split fp16
+    operands (what two tensor-core passes would at best give), leaves the
+    residual levels alone on these inputs but changes the stored fp32
+    magnitude (mean |deviation|, 4 bytes of the slot) of a large share of
+    vectors, so the slots would no longer be byte-identical."""
+    sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
+    import ref_inputs as RI
+    L, W, sk, tgt = RI.hier_stages(n=1024)
+    p_seq = O.hier_predict(L, W, sk)
+    hi = sk.astype(np.float16).astype(np.float64)
+    lo = (sk.astype(np.float64) - hi).astype(np.float16).astype(np.float64)
+    p_tc = ((hi + lo) @ W.astype(np.float64).T).astype(np.float32)
+    d0, d1 = tgt - p_seq, tgt - p_tc
+    m0, m1 = O.residual_mag(d0), O.residual_mag(d1)
+    l0 = O.residual_levels(d0, 2, m0, "hier")
+    l1 = O.residual_levels(d1, 2, m1, "hier")
+    assert np.mean(p_seq != p_tc) > 0.5
+    assert np.count_nonzero(l0 != l1) <= 1e-5 * l0.size
+    assert np.mean(m0 != m1) > 0.05
