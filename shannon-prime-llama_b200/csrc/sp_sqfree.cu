@@ -2827,6 +2827,298 @@ int sq_lane_try(const SpSqDev *t[2], const SqIo *io[2], int dtype, unsigned int 
          : dtype == SP_DTYPE_BF16 ? sq_lane_launch<__nv_bfloat16>(t, io, dtype, status, s, rc) : 0;
 }
 
+// ----------------------------------------------- lane-per-vector hier write --
+// Compress for the hier layout of head_dim 256 (pad 330 = 2.3.5.11, skeleton
+// of 30 values in two 15-value bands of 5 bits, 300 targets at 2 bits).  One
+// thread owns one whole vector, so none of the warp encoder's cross-lane
+// bookkeeping (group loops, shuffles, shared-memory atomics on the slot
+// image) is left; every float operation is the one k_sq_encode performs, in
+// the same order (the lane-tree sums of the inputs and of |dev| are replayed
+// as the same tree), so slots are bit-identical.
+//   pass 0  the input sum (lane-tree order) -> pad mean;
+//   pass A  the transform stages 2, 3, 5 act inside blocks of 30 consecutive
+//           coefficients (30 = 2.3.5): each block is loaded from the input
+//           (or the mean) into registers, transformed there and stored into
+//           the thread's 330-float row in shared memory;
+//   pass B  the stride-30 stage 11: 30 groups of 11 values, all 330 outputs
+//           written back; the skeleton then goes to registers;
+//   pass C  prediction W . skeleton (fp32 fma chain in skeleton order, W rows
+//           read as broadcasts) and the deviation, in place;
+//   pass D  magnitude (lane-tree order), levels, packing into the row words,
+//           which the warp then writes out byte-contiguously.
+constexpr int kHlWarps = 4;
+constexpr int kHlPD = 330, kHlHD = 256, kHlSK = 30, kHlNR = 300;
+constexpr int kHlRow = 357;              // floats per thread: 330 + 26 row words + 1 (odd: conflict-free)
+constexpr int kHlWs = 32;                // W row stride in floats (16-byte loads)
+constexpr int kHlBandBits = 5, kHlBand = 15;
+constexpr int kHlU = 6;                  // residuals per prediction step (divides 300)
+constexpr int kHlMagOff = 24, kHlResOff = 28, kHlBytes = 103;
+__host__ __device__ constexpr int hl_band_byte(int b) { return b == 0 ? 0 : 12; }
+
+struct HlArgs {
+    const void *in;              // [n_layers][n_tok][nh][256]
+    uint8_t *cache;
+    long long slot_stride;
+    int layer0, nh, start_pos, n_tok, tokens_per_cta;
+    const __half *W;             // [n_slots][300][30]
+    const int *tables;           // skel_idx[30], res_idx[300]
+};
+
+size_t hl_smem_bytes()
+{
+    return (size_t)kHlNR * kHlWs * 4 + (size_t)kHlWarps * 32 * kHlRow * 4 + (size_t)(kHlSK + kHlNR) * 4 + 16;
+}
+
+// Stage of prime P at stride STRIDE inside one 30-block held in registers
+// (vstage_c's arithmetic and group layout restricted to the block).
+template <int P, int STRIDE>
+__device__ __forceinline__ void hl_stage(float (&x)[30])
+{
+    const float isp = c_sq_isp[prime_slot<P>()];
+#pragma unroll
+    for (int g = 0; g < 30 / P; g++) {
+        const int blk = g / STRIDE, base = blk * (STRIDE * P) + (g - blk * STRIDE);
+        float y[P];
+#pragma unroll
+        for (int k = 0; k < P; k++) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int j = 0; j < P; j++) acc = __fmaf_rn(c_sq_cas[cas_base<P>() + k * P + j], x[base + j * STRIDE], acc);
+            y[k] = __fmul_rn(acc, isp);
+        }
+#pragma unroll
+        for (int k = 0; k < P; k++) x[base + k * STRIDE] = y[k];
+    }
+}
+
+template <typename Tin>
+__global__ void __launch_bounds__(kHlWarps * 32, 1)
+k_hier_encode_lane(HlArgs a)
+{
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    float *Ws = reinterpret_cast<float *>(smem_raw);                      // [300][32]
+    float *rows = Ws + kHlNR * kHlWs;                                      // [128][357]
+    int *tab = reinterpret_cast<int *>(rows + kHlWarps * 32 * kHlRow);     // skel_idx, res_idx
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int li = blockIdx.y / a.nh, h = blockIdx.y % a.nh;
+    const int slot = (a.layer0 + li) * a.nh + h;
+    {
+        const __half *w = a.W + (size_t)slot * kHlNR * kHlSK;
+        for (int i = threadIdx.x; i < kHlNR * kHlWs; i += blockDim.x) {
+            const int r = i / kHlWs, s = i - r * kHlWs;
+            Ws[i] = s < kHlSK ? __half2float(w[r * kHlSK + s]) : 0.0f;
+        }
+        for (int i = threadIdx.x; i < kHlSK + kHlNR; i += blockDim.x) tab[i] = a.tables[i];
+    }
+    __syncthreads();
+    float *y = rows + (size_t)threadIdx.x * kHlRow;
+    uint32_t *rw = reinterpret_cast<uint32_t *>(y + kHlPD);               // 26 row words
+    const int tb = blockIdx.x * a.tokens_per_cta;
+    const int te = min(a.n_tok, tb + a.tokens_per_cta);
+    for (int t0 = tb + warp * 32; t0 < te; t0 += kHlWarps * 32) {
+        const int tok = t0 + lane;
+        const bool live = tok < te;
+        const Tin *src = reinterpret_cast<const Tin *>(a.in) +
+                         (((long long)li * a.n_tok + (live ? tok : t0)) * a.nh + h) * kHlHD;
+        // ---- pass 0: lane-tree sum of the inputs, which land in y[0..256) --
+        float part[32];
+#pragma unroll
+        for (int l = 0; l < 32; l++) part[l] = 0.0f;
+        constexpr int EPV = 16 / (int)sizeof(Tin);          // elements per 16-byte load
+#pragma unroll
+        for (int i = 0; i < kHlHD; i += EPV) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(src + i);
+            float x[EPV];
+            lane_unpack16_sq<Tin>(v, x);
+#pragma unroll
+            for (int e = 0; e < EPV; e++) {
+                part[(i + e) & 31] = __fadd_rn(part[(i + e) & 31], x[e]);
+                y[i + e] = x[e];
+            }
+        }
+        const float mean = __fdiv_rn(sl_tree32(part), (float)kHlHD);
+#pragma unroll
+        for (int i = kHlHD; i < kHlPD; i++) y[i] = mean;
+        // ---- pass A: stages 2, 3, 5 per block of 30 ------------------------
+#pragma unroll 1
+        for (int b = 0; b < kHlPD / 30; b++) {
+            float x[30];
+#pragma unroll
+            for (int i = 0; i < 30; i++) x[i] = y[30 * b + i];
+            hl_stage<2, 1>(x);
+            hl_stage<3, 2>(x);
+            hl_stage<5, 6>(x);
+#pragma unroll
+            for (int i = 0; i < 30; i++) y[30 * b + i] = x[i];
+        }
+        // ---- pass B: stage 11 at stride 30 ---------------------------------
+        {
+            const float isp = c_sq_isp[prime_slot<11>()];
+#pragma unroll 1
+            for (int g = 0; g < 30; g++) {
+                float x[11];
+#pragma unroll
+                for (int j = 0; j < 11; j++) x[j] = y[g + 30 * j];
+#pragma unroll
+                for (int k = 0; k < 11; k++) {
+                    float acc = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 11; j++) acc = __fmaf_rn(c_sq_cas[cas_base<11>() + k * 11 + j], x[j], acc);
+                    y[g + 30 * k] = __fmul_rn(acc, isp);
+                }
+            }
+        }
+        float sk[kHlSK];
+#pragma unroll
+        for (int s = 0; s < kHlSK; s++) sk[s] = y[tab[s]];
+        // ---- skeleton bands -------------------------------------------------
+        uint32_t row[26];
+#pragma unroll
+        for (int w = 0; w < 26; w++) row[w] = 0u;
+#pragma unroll
+        for (int b = 0; b < 2; b++) {
+            float amax = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kHlBand; i++) amax = fmaxf(amax, fabsf(sk[kHlBand * b + i]));
+            constexpr int mv = (1 << (kHlBandBits - 1)) - 1;
+            const float scale = amax > 0.0f ? __fdiv_rn(amax, (float)mv) : 0.0f;
+            const __half hs = __float2half_rn(scale);
+            const float stored = __half2float(hs);
+            const float inv = stored > 0.0f ? __frcp_rn(stored) : 0.0f;
+            const int sb = 8 * hl_band_byte(b);
+            row[sb >> 5] |= (uint32_t)__half_as_ushort(hs) << (sb & 31);
+#pragma unroll
+            for (int i = 0; i < kHlBand; i++) {
+                int q = __float2int_rn(__fmul_rn(sk[kHlBand * b + i], inv));
+                q = q > mv ? mv : (q < -mv ? -mv : q);
+                const uint32_t u = (uint32_t)(q + mv);
+                const int pos = 8 * (hl_band_byte(b) + 2) + i * kHlBandBits;
+                row[pos >> 5] |= u << (pos & 31);
+                if ((pos & 31) + kHlBandBits > 32) row[(pos >> 5) + 1] |= u >> (32 - (pos & 31));
+            }
+        }
+        // ---- pass C: prediction and deviation, in place; kHlU residuals
+        // at a time so their fma chains interleave
+#pragma unroll 1
+        for (int r0 = 0; r0 < kHlNR; r0 += kHlU) {
+            float acc[kHlU];
+#pragma unroll
+            for (int u = 0; u < kHlU; u++) acc[u] = 0.0f;
+#pragma unroll
+            for (int s0 = 0; s0 < kHlSK; s0 += 4) {
+#pragma unroll
+                for (int u = 0; u < kHlU; u++) {
+                    const float4 w4 = reinterpret_cast<const float4 *>(Ws + (r0 + u) * kHlWs)[s0 >> 2];
+                    acc[u] = __fmaf_rn(w4.x, sk[s0], acc[u]);
+                    acc[u] = __fmaf_rn(w4.y, sk[s0 + 1], acc[u]);
+                    if (s0 + 2 < kHlSK) acc[u] = __fmaf_rn(w4.z, sk[s0 + 2], acc[u]);
+                    if (s0 + 3 < kHlSK) acc[u] = __fmaf_rn(w4.w, sk[s0 + 3], acc[u]);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kHlU; u++) {
+                const int i = tab[kHlSK + r0 + u];
+                y[i] = __fsub_rn(y[i], acc[u]);
+            }
+        }
+        // ---- pass D: magnitude, levels, packing -----------------------------
+#pragma unroll
+        for (int l = 0; l < 32; l++) {
+            float s = 0.0f;
+#pragma unroll
+            for (int r = l; r < kHlNR; r += 32) s = __fadd_rn(s, fabsf(y[tab[kHlSK + r]]));
+            part[l] = s;
+        }
+        float mag = __fdiv_rn(sl_tree32(part), (float)kHlNR);
+        if (mag < 1e-12f) mag = 1e-12f;
+        const float step = __fdiv_rn(__fmul_rn(2.0f, mag), 3.0f);
+        const float center = __fdiv_rn(3.0f, 2.0f);
+        const float inv = step > 0.0f ? __frcp_rn(step) : 0.0f;
+        row[kHlMagOff / 4] = __float_as_uint(mag);
+        static_assert(kHlMagOff % 4 == 0 && kHlResOff % 4 == 0, "word-aligned magnitude and levels");
+#pragma unroll
+        for (int w = 0; w < kHlResOff / 4; w++) rw[w] = row[w];
+#pragma unroll 1
+        for (int w = 0; w < (2 * kHlNR + 31) / 32; w++) {
+            uint32_t word = 0u;
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const int r = 16 * w + j;
+                if (r < kHlNR) {
+                    int level = __float2int_rn(__fmaf_rn(y[tab[kHlSK + r]], inv, center));
+                    level = level < 0 ? 0 : (level > 3 ? 3 : level);
+                    word |= (uint32_t)level << (2 * j);
+                }
+            }
+            rw[kHlResOff / 4 + w] = word;
+        }
+        __syncwarp();
+        // ---- the warp's rows, byte-contiguous in the slot -------------------
+        const int n_live = min(32, te - t0);
+        uint8_t *dst = a.cache + (long long)slot * a.slot_stride + (long long)(a.start_pos + t0) * kHlBytes;
+        const float *wbase = rows + (size_t)(warp * 32) * kHlRow;
+        for (int i = lane; i < n_live * kHlBytes; i += 32) {
+            const int t = i / kHlBytes, bb = i - t * kHlBytes;
+            dst[i] = reinterpret_cast<const uint8_t *>(wbase + (size_t)t * kHlRow + kHlPD)[bb];
+        }
+        __syncwarp();
+    }
+}
+
+// The lane writer's layout: hd 256, pad 330, skeleton 30 in two 15-value
+// 5-bit bands, 300 targets at 2 bits (103-byte slots).
+bool hl_fits(const SpSqDev &t)
+{
+    return t.hier && t.hd == kHlHD && t.pd == kHlPD && t.n_skel == kHlSK && t.n_res == kHlNR && t.res_bits == 2 &&
+           t.bl.n_bands == 2 && t.bl.bits[0] == kHlBandBits && t.bl.bits[1] == kHlBandBits &&
+           t.bl.size[0] == kHlBand && t.bl.size[1] == kHlBand && t.bl.off[1] == kHlBand &&
+           t.bl.byte_off[0] == hl_band_byte(0) && t.bl.byte_off[1] == hl_band_byte(1) && t.mag_off == kHlMagOff &&
+           t.res_off == kHlResOff && t.bytes_per_pos == kHlBytes;
+}
+
+int hl_launch(const SpSqDev &t, const SqIo &io, int dtype, cudaStream_t s, bool *done)
+{
+    *done = false;
+    if (!hl_fits(t) || !io.W || getenv("SHANNON_PRIME_HIER_ENCODE_WARP")) return SP_OK;
+    if (dtype != SP_DTYPE_F32 && dtype != SP_DTYPE_F16 && dtype != SP_DTYPE_BF16) return SP_OK;
+    if (((uintptr_t)io.in & 15)) return SP_OK;        // 16-byte row loads (rows are 256 elements)
+    void (*k)(HlArgs) = dtype == SP_DTYPE_F32 ? k_hier_encode_lane<float>
+                      : dtype == SP_DTYPE_F16 ? k_hier_encode_lane<__half> : k_hier_encode_lane<__nv_bfloat16>;
+    const size_t sm = hl_smem_bytes();
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
+        return sp_check_cuda(cudaGetLastError(), "hier lane write smem attribute");
+    HlArgs a;
+    a.in = io.in;
+    a.cache = io.cache;
+    a.slot_stride = io.slot_stride;
+    a.layer0 = io.layer0;
+    a.nh = io.nh;
+    a.start_pos = io.start_pos;
+    a.n_tok = io.n_tok;
+    a.W = io.W;
+    a.tables = t.tables;
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms < 1) sms = 148;
+    const int slots = io.n_layers * io.nh;
+    // chunks of whole warp tiles; the count that fills the last wave best
+    const int max_chunks = std::max(1, (io.n_tok + 32 * kHlWarps - 1) / (32 * kHlWarps));
+    const int c0 = std::min(max_chunks, std::max(1, (4 * sms + slots - 1) / slots));
+    int chunks = c0;
+    double best = -1.0;
+    for (int c = c0; c <= std::min(max_chunks, 4 * c0); c++) {
+        const long long ctas = (long long)slots * c;
+        const double eff = (double)ctas / (double)(((ctas + sms - 1) / sms) * sms);
+        if (eff > best + 1e-3) { best = eff; chunks = c; }
+    }
+    a.tokens_per_cta = ((io.n_tok + chunks - 1) / chunks + 31) / 32 * 32;
+    chunks = (io.n_tok + a.tokens_per_cta - 1) / a.tokens_per_cta;
+    k<<<dim3(chunks, slots), kHlWarps * 32, sm, s>>>(a);
+    *done = true;
+    return sp_check_cuda(cudaGetLastError(), "hier lane write launch");
+}
+
 int sq_launch_encode(const SpSqDev &t, SqIo io, int dtype, cudaStream_t s, unsigned int *status = nullptr)
 {
     if (io.n_tok <= 0 || io.n_layers <= 0) return SP_OK;
@@ -2835,6 +3127,8 @@ int sq_launch_encode(const SpSqDev &t, SqIo io, int dtype, cudaStream_t s, unsig
         const SpSqDev *tt[2] = {&t, nullptr};
         const SqIo *ii[2] = {&io, nullptr};
         if (sq_lane_try(tt, ii, dtype, status, s, &rc)) return rc;
+        bool done = false;
+        if ((rc = hl_launch(t, io, dtype, s, &done)) || done) return rc;
     }
     const size_t sm = sq_smem_bytes(t);
     io.store_width = store_width_for(t.bytes_per_pos, io.slot_stride, io.cache);

@@ -265,3 +265,35 @@ def test_sqfree_lane_read_matches_warp_read(cuda, monkeypatch, start, T):
         np.testing.assert_array_equal(outs[0], outs[1])
         slab = cache.slab(which).cpu().numpy()[1, start:start + T]
         np.testing.assert_array_equal(outs[0], O.sqfree_read(slab, OL))
+
+
+@pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])
+@pytest.mark.parametrize("start,T", [(0, 300), (5, 77), (13, 1)])
+def test_hier_lane_and_warp_encoders_agree(cuda, dtype, start, T, monkeypatch):
+    """The lane-per-vector hier writer (hd 256 layout) and the warp encoder
+    write identical slots, also for ragged tiles at unaligned positions, and
+    both equal the oracle."""
+    import torch
+    hd, L, H = 256, 2, 3
+    OL = O.hier_layout(hd)
+    k, _ = _inputs(6, L, H, T, hd, sigma=1.0)
+    tdt = getattr(torch, dtype)
+    kt = torch.from_numpy(k).to(tdt)
+    k32 = kt.float().numpy()
+    Ws = np.stack([O.hier_fit_W(np.concatenate([k32[layer, :, h]] * 4)[:max(64, T)], OL)
+                   for layer in range(L) for h in range(H)])
+    slabs = []
+    for warp_enc in (False, True):
+        if warp_enc:
+            monkeypatch.setenv("SHANNON_PRIME_HIER_ENCODE_WARP", "1")
+        cache = HierCache(hd, L, H, 512, OL.pd, OL.n_skel)
+        cache.upload_W(Ws)
+        cache.write_kv_tokens(0, start, kt.cuda(), None)
+        torch.cuda.synchronize()
+        slabs.append(cache.slab(0).cpu().numpy())
+    assert np.array_equal(slabs[0], slabs[1])
+    for layer in range(L):
+        for h in range(H):
+            s = layer * H + h
+            assert np.array_equal(slabs[0][s, start:start + T], O.hier_write(k32[layer, :, h], OL, Ws[s]))
+            assert not slabs[0][s, :start].any() and not slabs[0][s, start + T:].any()
