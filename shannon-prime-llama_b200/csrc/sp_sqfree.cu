@@ -2846,12 +2846,10 @@ int sq_lane_try(const SpSqDev *t[2], const SqIo *io[2], int dtype, unsigned int 
 //           read as broadcasts) and the deviation, in place;
 //   pass D  magnitude (lane-tree order), levels, packing into the row words,
 //           which the warp then writes out byte-contiguously.
-constexpr int kHlWarps = 4;
 constexpr int kHlPD = 330, kHlHD = 256, kHlSK = 30, kHlNR = 300;
 constexpr int kHlRow = 357;              // floats per thread: 330 + 26 row words + 1 (odd: conflict-free)
 constexpr int kHlWs = 32;                // W row stride in floats (16-byte loads)
 constexpr int kHlBandBits = 5, kHlBand = 15;
-constexpr int kHlU = 6;                  // residuals per prediction step (divides 300)
 constexpr int kHlMagOff = 24, kHlResOff = 28, kHlBytes = 103;
 __host__ __device__ constexpr int hl_band_byte(int b) { return b == 0 ? 0 : 12; }
 
@@ -2866,7 +2864,7 @@ struct HlArgs {
 
 size_t hl_smem_bytes()
 {
-    return (size_t)kHlNR * kHlWs * 4 + (size_t)kHlWarps * 32 * kHlRow * 4 + (size_t)(kHlSK + kHlNR) * 4 + 16;
+    return (size_t)kHlNR * kHlWs * 4 + (size_t)128 * kHlRow * 4 + (size_t)(kHlSK + kHlNR) * 4 + 16;
 }
 
 // Stage of prime P at stride STRIDE inside one 30-block held in registers
@@ -2891,15 +2889,21 @@ __device__ __forceinline__ void hl_stage(float (&x)[30])
     }
 }
 
-template <typename Tin>
-__global__ void __launch_bounds__(kHlWarps * 32, 1)
+// R lanes share one vector (32 / R vectors per warp, 128 per CTA); role
+// rho = lane / (32 / R) takes the rho-th share of each split pass.
+template <typename Tin, int R>
+__global__ void __launch_bounds__(R * 128, 1)
 k_hier_encode_lane(HlArgs a)
 {
+    constexpr int VPW = 32 / R, NW = 4 * R;          // vectors per warp, warps per CTA
+    constexpr int U = R == 4 ? 5 : 6;                // residuals per prediction step
+    static_assert((kHlNR / R) % U == 0, "prediction steps tile a role's residuals");
     extern __shared__ __align__(16) unsigned char smem_raw[];
     float *Ws = reinterpret_cast<float *>(smem_raw);                      // [300][32]
     float *rows = Ws + kHlNR * kHlWs;                                      // [128][357]
-    int *tab = reinterpret_cast<int *>(rows + kHlWarps * 32 * kHlRow);     // skel_idx, res_idx
+    int *tab = reinterpret_cast<int *>(rows + 128 * kHlRow);               // skel_idx, res_idx
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int v = lane % VPW, role = lane / VPW;
     const int li = blockIdx.y / a.nh, h = blockIdx.y % a.nh;
     const int slot = (a.layer0 + li) * a.nh + h;
     {
@@ -2911,37 +2915,48 @@ k_hier_encode_lane(HlArgs a)
         for (int i = threadIdx.x; i < kHlSK + kHlNR; i += blockDim.x) tab[i] = a.tables[i];
     }
     __syncthreads();
-    float *y = rows + (size_t)threadIdx.x * kHlRow;
+    float *y = rows + (size_t)(warp * VPW + v) * kHlRow;
     uint32_t *rw = reinterpret_cast<uint32_t *>(y + kHlPD);               // 26 row words
+    // this role's shares: transform blocks, stage-11 groups, residuals, level words
+    const int b0 = (kHlPD / 30) * role / R, b1 = (kHlPD / 30) * (role + 1) / R;
+    const int g0 = 30 * role / R, g1 = 30 * (role + 1) / R;
+    const int r0 = kHlNR / R * role;
+    constexpr int NWORD = (2 * kHlNR + 31) / 32;
+    const int w0 = NWORD * role / R, w1 = NWORD * (role + 1) / R;
+    const int lo = 30 * b0, hi = 30 * b1;                                  // y range of the blocks
     const int tb = blockIdx.x * a.tokens_per_cta;
     const int te = min(a.n_tok, tb + a.tokens_per_cta);
-    for (int t0 = tb + warp * 32; t0 < te; t0 += kHlWarps * 32) {
-        const int tok = t0 + lane;
+    for (int t0 = tb + warp * VPW; t0 < te; t0 += NW * VPW) {
+        const int tok = t0 + v;
         const bool live = tok < te;
         const Tin *src = reinterpret_cast<const Tin *>(a.in) +
                          (((long long)li * a.n_tok + (live ? tok : t0)) * a.nh + h) * kHlHD;
-        // ---- pass 0: lane-tree sum of the inputs, which land in y[0..256) --
+        // ---- pass 0: lane-tree sum of the inputs (every role); each role
+        // stores the inputs of its own blocks and their mean pad
         float part[32];
 #pragma unroll
         for (int l = 0; l < 32; l++) part[l] = 0.0f;
         constexpr int EPV = 16 / (int)sizeof(Tin);          // elements per 16-byte load
+#pragma unroll 1
+        for (int k = 0; k < kHlHD / 32; k++) {
+            float x[32];
 #pragma unroll
-        for (int i = 0; i < kHlHD; i += EPV) {
-            const uint4 v = *reinterpret_cast<const uint4 *>(src + i);
-            float x[EPV];
-            lane_unpack16_sq<Tin>(v, x);
+            for (int c = 0; c < 32; c += EPV) {
+                const uint4 q = *reinterpret_cast<const uint4 *>(src + 32 * k + c);
+                lane_unpack16_sq<Tin>(q, &x[c]);
+            }
 #pragma unroll
-            for (int e = 0; e < EPV; e++) {
-                part[(i + e) & 31] = __fadd_rn(part[(i + e) & 31], x[e]);
-                y[i + e] = x[e];
+            for (int l = 0; l < 32; l++) {
+                part[l] = __fadd_rn(part[l], x[l]);
+                const int i = 32 * k + l;
+                if (i >= lo && i < hi) y[i] = x[l];
             }
         }
         const float mean = __fdiv_rn(sl_tree32(part), (float)kHlHD);
-#pragma unroll
-        for (int i = kHlHD; i < kHlPD; i++) y[i] = mean;
-        // ---- pass A: stages 2, 3, 5 per block of 30 ------------------------
+        for (int i = max(lo, kHlHD); i < hi; i++) y[i] = mean;
+        // ---- pass A: stages 2, 3, 5 on this role's blocks of 30 ------------
 #pragma unroll 1
-        for (int b = 0; b < kHlPD / 30; b++) {
+        for (int b = b0; b < b1; b++) {
             float x[30];
 #pragma unroll
             for (int i = 0; i < 30; i++) x[i] = y[30 * b + i];
@@ -2951,11 +2966,13 @@ k_hier_encode_lane(HlArgs a)
 #pragma unroll
             for (int i = 0; i < 30; i++) y[30 * b + i] = x[i];
         }
-        // ---- pass B: stage 11 at stride 30 ---------------------------------
+        __syncwarp();
+        // ---- pass B: stage 11 at stride 30 on this role's groups (a
+        // group's outputs replace its own inputs) -----------------------------
         {
             const float isp = c_sq_isp[prime_slot<11>()];
 #pragma unroll 1
-            for (int g = 0; g < 30; g++) {
+            for (int g = g0; g < g1; g++) {
                 float x[11];
 #pragma unroll
                 for (int j = 0; j < 11; j++) x[j] = y[g + 30 * j];
@@ -2968,47 +2985,53 @@ k_hier_encode_lane(HlArgs a)
                 }
             }
         }
+        __syncwarp();
         float sk[kHlSK];
 #pragma unroll
         for (int s = 0; s < kHlSK; s++) sk[s] = y[tab[s]];
-        // ---- skeleton bands -------------------------------------------------
-        uint32_t row[26];
+        // ---- skeleton bands (role 0) -----------------------------------------
+        if (role == 0) {
+            uint32_t row[6];
 #pragma unroll
-        for (int w = 0; w < 26; w++) row[w] = 0u;
+            for (int w = 0; w < 6; w++) row[w] = 0u;
 #pragma unroll
-        for (int b = 0; b < 2; b++) {
-            float amax = 0.0f;
+            for (int b = 0; b < 2; b++) {
+                float amax = 0.0f;
 #pragma unroll
-            for (int i = 0; i < kHlBand; i++) amax = fmaxf(amax, fabsf(sk[kHlBand * b + i]));
-            constexpr int mv = (1 << (kHlBandBits - 1)) - 1;
-            const float scale = amax > 0.0f ? __fdiv_rn(amax, (float)mv) : 0.0f;
-            const __half hs = __float2half_rn(scale);
-            const float stored = __half2float(hs);
-            const float inv = stored > 0.0f ? __frcp_rn(stored) : 0.0f;
-            const int sb = 8 * hl_band_byte(b);
-            row[sb >> 5] |= (uint32_t)__half_as_ushort(hs) << (sb & 31);
+                for (int i = 0; i < kHlBand; i++) amax = fmaxf(amax, fabsf(sk[kHlBand * b + i]));
+                constexpr int mv = (1 << (kHlBandBits - 1)) - 1;
+                const float scale = amax > 0.0f ? __fdiv_rn(amax, (float)mv) : 0.0f;
+                const __half hs = __float2half_rn(scale);
+                const float stored = __half2float(hs);
+                const float inv = stored > 0.0f ? __frcp_rn(stored) : 0.0f;
+                const int sb = 8 * hl_band_byte(b);
+                row[sb >> 5] |= (uint32_t)__half_as_ushort(hs) << (sb & 31);
 #pragma unroll
-            for (int i = 0; i < kHlBand; i++) {
-                int q = __float2int_rn(__fmul_rn(sk[kHlBand * b + i], inv));
-                q = q > mv ? mv : (q < -mv ? -mv : q);
-                const uint32_t u = (uint32_t)(q + mv);
-                const int pos = 8 * (hl_band_byte(b) + 2) + i * kHlBandBits;
-                row[pos >> 5] |= u << (pos & 31);
-                if ((pos & 31) + kHlBandBits > 32) row[(pos >> 5) + 1] |= u >> (32 - (pos & 31));
+                for (int i = 0; i < kHlBand; i++) {
+                    int q = __float2int_rn(__fmul_rn(sk[kHlBand * b + i], inv));
+                    q = q > mv ? mv : (q < -mv ? -mv : q);
+                    const uint32_t u = (uint32_t)(q + mv);
+                    const int pos = 8 * (hl_band_byte(b) + 2) + i * kHlBandBits;
+                    row[pos >> 5] |= u << (pos & 31);
+                    if ((pos & 31) + kHlBandBits > 32) row[(pos >> 5) + 1] |= u >> (32 - (pos & 31));
+                }
             }
-        }
-        // ---- pass C: prediction and deviation, in place; kHlU residuals
-        // at a time so their fma chains interleave
-#pragma unroll 1
-        for (int r0 = 0; r0 < kHlNR; r0 += kHlU) {
-            float acc[kHlU];
+            static_assert(kHlMagOff == 24, "skeleton bands fill words 0-5");
 #pragma unroll
-            for (int u = 0; u < kHlU; u++) acc[u] = 0.0f;
+            for (int w = 0; w < 6; w++) rw[w] = row[w];
+        }
+        // ---- pass C: prediction and deviation, in place, on this role's
+        // residuals, U at a time so their fma chains interleave
+#pragma unroll 1
+        for (int rr = r0; rr < r0 + kHlNR / R; rr += U) {
+            float acc[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) acc[u] = 0.0f;
 #pragma unroll
             for (int s0 = 0; s0 < kHlSK; s0 += 4) {
 #pragma unroll
-                for (int u = 0; u < kHlU; u++) {
-                    const float4 w4 = reinterpret_cast<const float4 *>(Ws + (r0 + u) * kHlWs)[s0 >> 2];
+                for (int u = 0; u < U; u++) {
+                    const float4 w4 = reinterpret_cast<const float4 *>(Ws + (rr + u) * kHlWs)[s0 >> 2];
                     acc[u] = __fmaf_rn(w4.x, sk[s0], acc[u]);
                     acc[u] = __fmaf_rn(w4.y, sk[s0 + 1], acc[u]);
                     if (s0 + 2 < kHlSK) acc[u] = __fmaf_rn(w4.z, sk[s0 + 2], acc[u]);
@@ -3016,12 +3039,13 @@ k_hier_encode_lane(HlArgs a)
                 }
             }
 #pragma unroll
-            for (int u = 0; u < kHlU; u++) {
-                const int i = tab[kHlSK + r0 + u];
+            for (int u = 0; u < U; u++) {
+                const int i = tab[kHlSK + rr + u];
                 y[i] = __fsub_rn(y[i], acc[u]);
             }
         }
-        // ---- pass D: magnitude, levels, packing -----------------------------
+        __syncwarp();
+        // ---- pass D: magnitude (every role), this role's level words -------
 #pragma unroll
         for (int l = 0; l < 32; l++) {
             float s = 0.0f;
@@ -3034,12 +3058,10 @@ k_hier_encode_lane(HlArgs a)
         const float step = __fdiv_rn(__fmul_rn(2.0f, mag), 3.0f);
         const float center = __fdiv_rn(3.0f, 2.0f);
         const float inv = step > 0.0f ? __frcp_rn(step) : 0.0f;
-        row[kHlMagOff / 4] = __float_as_uint(mag);
-        static_assert(kHlMagOff % 4 == 0 && kHlResOff % 4 == 0, "word-aligned magnitude and levels");
-#pragma unroll
-        for (int w = 0; w < kHlResOff / 4; w++) rw[w] = row[w];
+        static_assert(kHlMagOff % 4 == 0 && kHlResOff == kHlMagOff + 4, "word-aligned fields");
+        if (role == 0) rw[kHlMagOff / 4] = __float_as_uint(mag);
 #pragma unroll 1
-        for (int w = 0; w < (2 * kHlNR + 31) / 32; w++) {
+        for (int w = w0; w < w1; w++) {
             uint32_t word = 0u;
 #pragma unroll
             for (int j = 0; j < 16; j++) {
@@ -3054,9 +3076,9 @@ k_hier_encode_lane(HlArgs a)
         }
         __syncwarp();
         // ---- the warp's rows, byte-contiguous in the slot -------------------
-        const int n_live = min(32, te - t0);
+        const int n_live = min(VPW, te - t0);
         uint8_t *dst = a.cache + (long long)slot * a.slot_stride + (long long)(a.start_pos + t0) * kHlBytes;
-        const float *wbase = rows + (size_t)(warp * 32) * kHlRow;
+        const float *wbase = rows + (size_t)(warp * VPW) * kHlRow;
         for (int i = lane; i < n_live * kHlBytes; i += 32) {
             const int t = i / kHlBytes, bb = i - t * kHlBytes;
             dst[i] = reinterpret_cast<const uint8_t *>(wbase + (size_t)t * kHlRow + kHlPD)[bb];
@@ -3082,8 +3104,11 @@ int hl_launch(const SpSqDev &t, const SqIo &io, int dtype, cudaStream_t s, bool 
     if (!hl_fits(t) || !io.W || getenv("SHANNON_PRIME_HIER_ENCODE_WARP")) return SP_OK;
     if (dtype != SP_DTYPE_F32 && dtype != SP_DTYPE_F16 && dtype != SP_DTYPE_BF16) return SP_OK;
     if (((uintptr_t)io.in & 15)) return SP_OK;        // 16-byte row loads (rows are 256 elements)
-    void (*k)(HlArgs) = dtype == SP_DTYPE_F32 ? k_hier_encode_lane<float>
-                      : dtype == SP_DTYPE_F16 ? k_hier_encode_lane<__half> : k_hier_encode_lane<__nv_bfloat16>;
+    // two lanes per vector, 8 warps per CTA (four lanes, 16 warps at 128
+    // registers, measured slower: 45.0 against 31.0 ms for config 4)
+    constexpr int R = 2;
+    void (*k)(HlArgs) = dtype == SP_DTYPE_F32 ? k_hier_encode_lane<float, R>
+                      : dtype == SP_DTYPE_F16 ? k_hier_encode_lane<__half, R> : k_hier_encode_lane<__nv_bfloat16, R>;
     const size_t sm = hl_smem_bytes();
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
         return sp_check_cuda(cudaGetLastError(), "hier lane write smem attribute");
@@ -3103,7 +3128,7 @@ int hl_launch(const SpSqDev &t, const SqIo &io, int dtype, cudaStream_t s, bool 
     if (sms < 1) sms = 148;
     const int slots = io.n_layers * io.nh;
     // chunks of whole warp tiles; the count that fills the last wave best
-    const int max_chunks = std::max(1, (io.n_tok + 32 * kHlWarps - 1) / (32 * kHlWarps));
+    const int max_chunks = std::max(1, (io.n_tok + 127) / 128);
     const int c0 = std::min(max_chunks, std::max(1, (4 * sms + slots - 1) / slots));
     int chunks = c0;
     double best = -1.0;
@@ -3112,9 +3137,9 @@ int hl_launch(const SpSqDev &t, const SqIo &io, int dtype, cudaStream_t s, bool 
         const double eff = (double)ctas / (double)(((ctas + sms - 1) / sms) * sms);
         if (eff > best + 1e-3) { best = eff; chunks = c; }
     }
-    a.tokens_per_cta = ((io.n_tok + chunks - 1) / chunks + 31) / 32 * 32;
+    a.tokens_per_cta = ((io.n_tok + chunks - 1) / chunks + 7) / 8 * 8;
     chunks = (io.n_tok + a.tokens_per_cta - 1) / a.tokens_per_cta;
-    k<<<dim3(chunks, slots), kHlWarps * 32, sm, s>>>(a);
+    k<<<dim3(chunks, slots), R * 128, sm, s>>>(a);
     *done = true;
     return sp_check_cuda(cudaGetLastError(), "hier lane write launch");
 }
