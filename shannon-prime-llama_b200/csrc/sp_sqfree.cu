@@ -1571,30 +1571,71 @@ SqAttnKernel sq_attn_reg_kernel(int G, int KS, int KR, int *GT)
     return nullptr;
 }
 
-__global__ void k_sq_attn_combine(SpSqDev t, SqAttn a)
+// Split merge of one (layer, query head): 128 threads.  The splits' maxima
+// and sums are read in parallel, the weights go to shared memory, and every
+// coefficient's sum over the splits keeps several independent loads in
+// flight; one warp then applies the transform.
+constexpr int kSqCombineThreads = 128;
+
+__global__ void __launch_bounds__(kSqCombineThreads)
+k_sq_attn_combine(SpSqDev t, SqAttn a)
 {
     extern __shared__ __align__(16) unsigned char smem[];
     float *cas = reinterpret_cast<float *>(smem);
     float *buf = cas + 224;
-    const int lane = threadIdx.x & 31;
+    float *wts = buf + ((t.pd + 3) & ~3);
+    float *red = wts + kSqMaxSplits;                 // [4 warps][2]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int qh = blockIdx.x, li = blockIdx.y;
-    for (int i = lane; i < 224; i += 32) cas[i] = t.cas[i];
-    float M = -INFINITY;
-    for (int s = 0; s < a.n_splits; s++) M = fmaxf(M, sq_partial(a, t.pd, li, qh, s)[0]);
-    for (int i = lane; i < t.pd; i += 32) buf[i] = 0.0f;
-    float L = 0.0f;
-    for (int s = 0; s < a.n_splits; s++) {
-        const float *p = sq_partial(a, t.pd, li, qh, s);
-        if (p[0] == -INFINITY) continue;
-        const float w = exp2f(p[0] - M);
-        L += w * p[1];
-        for (int i = lane; i < t.pd; i += 32) buf[i] += w * p[4 + i];
+    for (int i = tid; i < 224; i += blockDim.x) cas[i] = t.cas[i];
+    const int ns = a.n_splits;
+    float m = -INFINITY, l = 0.0f;
+    for (int s = tid; s < ns; s += blockDim.x) m = fmaxf(m, __ldcg(sq_partial(a, t.pd, li, qh, s)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[2 * warp] = m;
+    __syncthreads();
+    float M = red[0];
+    for (int w = 1; w < kSqCombineThreads / 32; w++) M = fmaxf(M, red[2 * w]);
+    for (int s = tid; s < kSqMaxSplits; s += blockDim.x) {
+        float w = 0.0f;
+        if (s < ns) {
+            const float *p = sq_partial(a, t.pd, li, qh, s);
+            const float ms = __ldcg(p);
+            if (ms != -INFINITY) {
+                w = exp2f(ms - M);
+                l += w * __ldcg(p + 1);
+            }
+        }
+        wts[s] = w;
     }
-    __syncwarp();
-    vilenkin_warp(buf, t, cas, lane);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    if (lane == 0) red[2 * warp + 1] = l;
+    __syncthreads();
+    float L = 0.0f;
+    for (int w = 0; w < kSqCombineThreads / 32; w++) L += red[2 * w + 1];
+    for (int i = tid; i < t.pd; i += blockDim.x) {
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        int s = 0;
+        for (; s + 4 <= ns; s += 4) {
+#pragma unroll
+            for (int u = 0; u < 4; u++) acc[u] += wts[s + u] * __ldcg(sq_partial(a, t.pd, li, qh, s + u) + 4 + i);
+        }
+        for (; s < ns; s++) acc[0] += wts[s] * __ldcg(sq_partial(a, t.pd, li, qh, s) + 4 + i);
+        buf[i] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    }
+    __syncthreads();
+    if (warp == 0) vilenkin_warp(buf, t, cas, lane);
+    __syncthreads();
     const float inv = L > 0.0f ? 1.0f / L : 0.0f;
     __half *o = a.out + ((long long)li * a.n_q_heads + qh) * t.hd;
-    for (int i = lane; i < t.hd; i += 32) o[i] = __float2half_rn(buf[i] * inv);
+    for (int i = tid; i < t.hd; i += blockDim.x) o[i] = __float2half_rn(buf[i] * inv);
+}
+
+size_t sq_combine_smem(const SpSqDev &t)
+{
+    return (224 + ((t.pd + 3) & ~3) + kSqMaxSplits + 2 * (kSqCombineThreads / 32)) * sizeof(float);
 }
 
 // ------------------------------------------------ lane-per-vector sqfree --
@@ -2357,39 +2398,44 @@ struct SaSmem {
     int qf[4];
 };
 
-// The transformed queries of the lane decode, one thread per (layer, query
-// head): q' = V q_pad * logit_scale * log2(e) in slot order (160 words,
-// six zeros at the end), times 2^F with F chosen so max|q'| lands in
-// [64, 128), and F itself in word 160.
-__global__ void __launch_bounds__(32)
+// The transformed queries of the lane decode, one warp per (layer, query
+// head): q' = V q_pad * logit_scale * log2(e) in slot order (160 words, six
+// zeros at the end), times 2^F with F chosen so max|q'| lands in [64, 128),
+// and F itself in word 160.
+struct SaPdOf { int v[160]; };
+__host__ __device__ constexpr SaPdOf sa_pd_of_tab()
+{
+    SaPdOf x{};
+    for (int j = 0; j < 160; j++) x.v[j] = j < kSlPD ? sa_pd_of(j) : -1;
+    return x;
+}
+__constant__ SaPdOf c_sa_pd_of = sa_pd_of_tab();
+
+__global__ void __launch_bounds__(128)
 k_sa_query(SqAttn a)
 {
-    const int i = blockIdx.x * 32 + threadIdx.x;
+    __shared__ float qbuf[4][kSlPD + 2];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int i = blockIdx.x * 4 + warp;
     if (i >= a.n_layers * a.n_q_heads) return;
+    float *b = qbuf[warp];
     const __half *qg = a.q + (long long)i * kSlHD;
-    float x[kSlPD];
-#pragma unroll
-    for (int j = 0; j < kSlPD; j++) x[j] = j < kSlHD ? __half2float(qg[j]) : 0.0f;
-    sl_stage<2, 1>(x);
-    sl_stage<7, 2>(x);
-    sl_stage<11, 14>(x);
+    for (int j = lane; j < kSlPD; j += 32) b[j] = j < kSlHD ? __half2float(qg[j]) : 0.0f;
+    __syncwarp();
+    vilenkin_pd<kSlPD>(b, lane);
     const float s = a.logit_scale * 1.4426950408889634f;
     float mx = 0.0f;
+    for (int j = lane; j < kSlPD; j += 32) mx = fmaxf(mx, fabsf(b[j] * s));
 #pragma unroll
-    for (int j = 0; j < kSlPD; j++) mx = fmaxf(mx, fabsf(x[j] * s));
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     const int F = mx > 1e-30f ? 6 - ilogbf(mx) : 0;
     const float sf = ldexpf(s, F);
-    float sk[kSlSK], rs[kSlNRes];
-    sl_gather(x, sk, rs, std::make_index_sequence<kSlSK>{});
-    sl_gather_res(x, rs, std::make_index_sequence<kSlNRes>{});
     float *o = a.qws + (long long)i * kSaQWords;
-#pragma unroll
-    for (int j = 0; j < kSlSK; j++) o[j] = sk[j] * sf;
-#pragma unroll
-    for (int j = 0; j < kSlNRes; j++) o[kSlSK + j] = rs[j] * sf;
-#pragma unroll
-    for (int j = kSlPD; j < 160; j++) o[j] = 0.0f;
-    o[160] = (float)F;
+    for (int j = lane; j < 160; j += 32) {
+        const int pi = c_sa_pd_of.v[j];
+        o[j] = pi >= 0 ? b[pi] * sf : 0.0f;
+    }
+    if (lane == 0) o[160] = (float)F;
 }
 
 __global__ void __launch_bounds__(kSaWarps * 32, 3)
@@ -4354,12 +4400,11 @@ int sp_cuda_sqfree_attn_decode(const sp_cuda_sqfree_cache_t *cc, int layer0, int
         a.chunk = ((kv_len + best - 1) / best + 31) / 32 * 32;
         a.n_splits = (kv_len + a.chunk - 1) / a.chunk;
         a.qws = reinterpret_cast<float *>(reinterpret_cast<char *>(cc->d_attn_ws) + cc->attn_ws_bytes + 16);
-        k_sa_query<<<(n_layers * n_q_heads + 31) / 32, 32, 0, s>>>(a);
+        k_sa_query<<<(n_layers * n_q_heads + 3) / 4, 128, 0, s>>>(a);
         k_sq_attn_lane<<<dim3(a.n_splits, H, n_layers), kSaWarps * 32, sm, s>>>(a);
         int rc = sp_check_cuda(cudaGetLastError(), "sqfree lane attention launch");
         if (rc) return rc;
-        const size_t smc = (224 + tk.pd + 8) * sizeof(float);
-        k_sq_attn_combine<<<dim3(n_q_heads, n_layers), 32, smc, s>>>(tk, a);
+        k_sq_attn_combine<<<dim3(n_q_heads, n_layers), kSqCombineThreads, sq_combine_smem(tk), s>>>(tk, a);
         return sp_check_cuda(cudaGetLastError(), "sqfree attention combine launch");
     }
     if (blocked && a.n_splits > 0) {
@@ -4371,8 +4416,7 @@ int sp_cuda_sqfree_attn_decode(const sp_cuda_sqfree_cache_t *cc, int layer0, int
         k3<<<dim3(a.n_splits, H, n_layers), kSq3Warps * 32, sm, s>>>(tk, tv, a);
         int rc = sp_check_cuda(cudaGetLastError(), "sqfree attention launch");
         if (rc) return rc;
-        const size_t smc = (224 + tk.pd + 8) * sizeof(float);
-        k_sq_attn_combine<<<dim3(n_q_heads, n_layers), 32, smc, s>>>(tk, a);
+        k_sq_attn_combine<<<dim3(n_q_heads, n_layers), kSqCombineThreads, sq_combine_smem(tk), s>>>(tk, a);
         return sp_check_cuda(cudaGetLastError(), "sqfree attention combine launch");
     }
     int GT = 0;
@@ -4392,8 +4436,7 @@ int sp_cuda_sqfree_attn_decode(const sp_cuda_sqfree_cache_t *cc, int layer0, int
         int rc = sp_check_cuda(cudaGetLastError(), "sqfree attention launch");
         if (rc) return rc;
     }
-    const size_t smc = (224 + tk.pd + 8) * sizeof(float);
-    k_sq_attn_combine<<<dim3(n_q_heads, n_layers), 32, smc, s>>>(tk, a);
+    k_sq_attn_combine<<<dim3(n_q_heads, n_layers), kSqCombineThreads, sq_combine_smem(tk), s>>>(tk, a);
     return sp_check_cuda(cudaGetLastError(), "sqfree attention combine launch");
 }
 
