@@ -509,7 +509,9 @@ const char *sp_cuda_last_error_string(void);
 int sp_cuda_abi_struct_size(int which);
 
 /* New, for tests and benchmarks: force the fused-decode kernel family
- * (0 = automatic, 1 = generic SIMT kernel, 2 = tensor-core ship kernel). */
+ * (0 = automatic, 1 = generic SIMT kernel, 2 = mma.sync tensor-core ship
+ * kernel, 3 = tcgen05 ship kernel; 0 takes 2 where the layout allows, else
+ * 1; 3 needs whole 128-position tiles inside each slot). */
 void sp_cuda_attn_force_impl(int impl);
 
 /* New, for benchmarks: when enabled, sp_cuda_attn_decode records CUDA events

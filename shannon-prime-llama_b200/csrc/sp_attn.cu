@@ -253,7 +253,7 @@ size_t sp_attn_workspace_bytes(const sp_cuda_cache_t *cc)
 }
 
 // Diagnostic kernel choice, process-wide (tests use it to compare the two
-// kernels): 0 auto, 1 generic SIMT, 2 tensor-core.  Atomic, so host threads
+// kernels): 0 auto, 1 generic SIMT, 2 mma.sync tensor-core, 3 tcgen05.  Atomic, so host threads
 // may read it while another sets it.
 static std::atomic<int> g_force_impl{0};
 
@@ -294,6 +294,8 @@ static int attn_plan(SpAttnArgs &a, bool aligned, bool &use_mma)
     use_mma = aligned && g_force_impl != 1 && sp_attn_mma_supported(a) == SP_OK;
     if (g_force_impl == 2 && !use_mma)
         return sp_set_error(SP_ERR_UNSUPPORTED, "attn_decode: tensor-core path does not support this layout");
+    if (g_force_impl == 3 && !(use_mma && sp_attn_tc_supported(a) == SP_OK))
+        return sp_set_error(SP_ERR_UNSUPPORTED, "attn_decode: tcgen05 path does not support this layout");
 
     // Chunking: enough CTAs to fill the 148 SMs several times over, chunks of
     // at least kAttnMinChunk tokens, at most kAttnMaxSplits chunks.
@@ -360,8 +362,13 @@ static int attn_launch(const SpAttnArgs &a, bool use_mma, cudaStream_t s)
     int rc = SP_OK;
     const int n = a.kl.n;
     g_prof_splits = a.n_splits;
-    if (use_mma && a.kv_len > 0)
+    if (use_mma && a.kv_len > 0) {
+        // mma.sync kernel; the tcgen05 kernel on request (impl 3: measured
+        // slower on the ship layout, 471 vs 345 us for config 1)
+        if (g_force_impl == 3)
+            return sp_attn_tc_launch(a, s, g_prof ? g_ev[0] : nullptr, g_prof ? g_ev[1] : nullptr);
         return sp_attn_mma_launch(a, s, g_prof ? g_ev[0] : nullptr, g_prof ? g_ev[1] : nullptr);
+    }
     if (a.n_splits > 0) {
         if (g_prof) cudaEventRecord(g_ev[0], s);
         {

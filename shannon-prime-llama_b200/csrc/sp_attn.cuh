@@ -110,3 +110,32 @@ int sp_attn_mma_supported(const SpAttnArgs &a);
 // (optional) are recorded around the main kernel on stream s.
 int sp_attn_mma_launch(const SpAttnArgs &a, cudaStream_t s, cudaEvent_t ev_begin = nullptr,
                        cudaEvent_t ev_end = nullptr);
+
+// Work split of the tensor-core decode kernels: the flattened (layer, KV
+// head, tile) space is cut into n_ctas equal contiguous ranges, one per CTA;
+// a CTA writes one partial per (layer, KV head) segment it touches.
+struct SpSched {
+    long long total_tiles;   // units * tiles_per_unit
+    int tiles_per_unit;      // ceil(kv_len / tile)
+    int n_ctas;
+};
+
+__host__ __device__ inline long long sp_tile_begin(long long i, const SpSched &s)
+{
+    return i * s.total_tiles / s.n_ctas;
+}
+// Index of the CTA whose range holds tile g.
+__host__ __device__ inline int sp_cta_of_tile(long long g, const SpSched &s)
+{
+    return (int)(((g + 1) * s.n_ctas + s.total_tiles - 1) / s.total_tiles) - 1;
+}
+
+// Segment combine of a tensor-core decode (sp_attn_mma.cu): merges the
+// partials the schedule wrote, applies the inverse VHT2, writes fp16 rows
+// (locally or into the gather buffers).
+int sp_attn_seg_combine_launch(const SpAttnArgs &a, const SpSched &sc, cudaStream_t s);
+
+// tcgen05 kernel for the ship layout (sp_attn_tc.cu).
+int sp_attn_tc_supported(const SpAttnArgs &a);
+int sp_attn_tc_launch(const SpAttnArgs &a, cudaStream_t s, cudaEvent_t ev_begin = nullptr,
+                      cudaEvent_t ev_end = nullptr);

@@ -87,21 +87,10 @@ __host__ __device__ constexpr int vcode_d(int j)
     return j == 15 ? 4 : ((j % 5) == 2 ? 6 : ((j % 5) == 0 || (j % 5) == 3) ? 4 : 7);
 }
 
-struct Sched {
-    long long total_tiles;   // T = units * tiles_per_unit
-    int tiles_per_unit;      // ceil(kv_len / 16)
-    int n_ctas;              // N
-};
+using Sched = SpSched;
 
-__host__ __device__ inline long long tile_begin(long long i, const Sched &s)
-{
-    return i * s.total_tiles / s.n_ctas;
-}
-// Index of the CTA whose range holds tile g.
-__host__ __device__ inline int cta_of_tile(long long g, const Sched &s)
-{
-    return (int)(((g + 1) * s.n_ctas + s.total_tiles - 1) / s.total_tiles) - 1;
-}
+__host__ __device__ inline long long tile_begin(long long i, const Sched &s) { return sp_tile_begin(i, s); }
+__host__ __device__ inline int cta_of_tile(long long g, const Sched &s) { return sp_cta_of_tile(g, s); }
 
 // ------------------------------------------------------------------ PTX --
 
@@ -823,6 +812,11 @@ int sp_attn_mma_launch(const SpAttnArgs &a_in, cudaStream_t s, cudaEvent_t ev_be
     if (ev_end) cudaEventRecord(ev_end, s);
     int rc = sp_check_cuda(cudaGetLastError(), "tensor-core attention launch");
     if (rc) return rc;
+    return sp_attn_seg_combine_launch(a, sc, s);
+}
+
+int sp_attn_seg_combine_launch(const SpAttnArgs &a, const SpSched &sc, cudaStream_t s)
+{
     const int per_block = 4;
     dim3 grid((a.n_q_heads + per_block - 1) / per_block, a.n_layers);
     k_attn_combine_seg<<<grid, per_block * 32, 0, s>>>(a, sc);

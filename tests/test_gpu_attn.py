@@ -41,7 +41,7 @@ def _oracle(cache, layer, q, kv_len, n, kb, vb, mobius, scale):
     return O.attn_decode(ks, vs, n, kb, vb, mobius, q, kv_len, scale)
 
 
-@pytest.mark.parametrize("impl", [1, 0])
+@pytest.mark.parametrize("impl", [1, 2, 3, 0])
 @pytest.mark.parametrize("kv_len", [1, 15, 16, 100, 1000, 4096])
 def test_decode_matches_oracle(cuda, impl, kv_len):
     import torch
@@ -62,11 +62,12 @@ def test_decode_matches_oracle(cuda, impl, kv_len):
         assert err <= RTOL_L2, (layer, err)
 
 
-@pytest.mark.parametrize("impl", [1, 0])
+@pytest.mark.parametrize("impl", [1, 2, 3, 0])
 def test_decode_layer_offset_scale_and_partial_bands(cuda, impl):
     import torch
     n, H, G = 128, 2, 4
-    cache = _build(torch, 3, H, 300, n, seed=3)
+    # 384 slots: whole 128-position tiles, so the tcgen05 kernel takes it
+    cache = _build(torch, 3, H, 300, n, seed=3, max_seq=384)
     q = synth.q_np(3, 1, H * G, n, 1.0)
     out = torch.empty(1, H * G, n, dtype=torch.float16, device="cuda")
     spb200.lib().sp_cuda_attn_force_impl(impl)
@@ -127,8 +128,9 @@ def test_kv_len_zero_and_errors(cuda):
     assert rc == spb200.SP_ERR_ARG                       # kv_len beyond the cache
 
 
+@pytest.mark.parametrize("impl", [2, 3])
 @pytest.mark.parametrize("G,kv_len", [(8, 2000), (8, 17), (3, 700), (1, 999)])
-def test_ship_decode_group_sizes(cuda, G, kv_len):
+def test_ship_decode_group_sizes(cuda, G, kv_len, impl):
     """The tensor-core kernel serves 1..8 query heads per KV head (8: two
     MMA column tiles, as config 3's 32 Q / 4 KV heads)."""
     import torch
@@ -136,7 +138,7 @@ def test_ship_decode_group_sizes(cuda, G, kv_len):
     cache = _build(torch, L, H, 2048, n, seed=12)
     q = synth.q_np(12, L, H * G, n, 1.0 / np.sqrt(128))
     out = torch.empty(L, H * G, n, dtype=torch.float16, device="cuda")
-    spb200.lib().sp_cuda_attn_force_impl(2)          # the tensor-core kernel must take it
+    spb200.lib().sp_cuda_attn_force_impl(impl)       # the tensor-core kernel must take it
     try:
         cache.attn_decode(0, L, torch.from_numpy(q).cuda(), kv_len, out, logit_scale=0.7)
         torch.cuda.synchronize()

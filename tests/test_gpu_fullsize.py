@@ -63,9 +63,12 @@ def test_config1_full_size(cuda):
     simt = _decode(torch, cache, q, T, 1)
     again = _decode(torch, cache, q, T, 2)
     assert torch.equal(mma, again)                      # deterministic
-    a, b = mma.float().cpu().numpy(), simt.float().cpu().numpy()
+    tc = _decode(torch, cache, q, T, 3)
+    assert torch.equal(tc, _decode(torch, cache, q, T, 3))
+    a, b, c = mma.float().cpu().numpy(), simt.float().cpu().numpy(), tc.float().cpu().numpy()
     for layer in range(L):
         assert _rel(a[layer], b[layer]) <= RTOL, layer
+        assert _rel(c[layer], b[layer]) <= RTOL, layer
     ks, vs = cache.slab(0), cache.slab(1)
     qn = q.cpu().numpy()
     for layer, h in ((0, 5), (31, 5), (17, 2)):
@@ -73,6 +76,7 @@ def test_config1_full_size(cuda):
         ref = O.attn_decode(ks[slot:slot + 1].cpu().numpy(), vs[slot:slot + 1].cpu().numpy(), n, KB, VB, True,
                             qn[layer, h * G:(h + 1) * G], T, 1.0)
         assert _rel(a[layer, h * G:(h + 1) * G], ref) <= RTOL, (layer, h)
+        assert _rel(c[layer, h * G:(h + 1) * G], ref) <= RTOL, (layer, h)
     for layer, (kx, vx) in sample_k.items():
         slot = layer * H + 5
         assert np.array_equal(ks[slot].cpu().numpy(), O.ship_write(kx, KB, True))
@@ -94,11 +98,14 @@ def test_config3_shape_one_layer(cuda):
     scale = 1.0 / n ** 0.5
     a = _decode(torch, cache, q, T, 2, scale).float().cpu().numpy()
     b = _decode(torch, cache, q, T, 1, scale).float().cpu().numpy()
+    c = _decode(torch, cache, q, T, 3, scale).float().cpu().numpy()
     assert _rel(a, b) <= RTOL
+    assert _rel(c, b) <= RTOL
     h = 3
     ref = O.attn_decode(cache.slab(0)[h:h + 1].cpu().numpy(), cache.slab(1)[h:h + 1].cpu().numpy(), n, KB, VB,
                         True, q.cpu().numpy()[0, h * G:(h + 1) * G], T, scale)
     assert _rel(a[0, h * G:(h + 1) * G], ref) <= RTOL
+    assert _rel(c[0, h * G:(h + 1) * G], ref) <= RTOL
 
 
 def test_config2_sqfree_full_length(cuda, monkeypatch):
