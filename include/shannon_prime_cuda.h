@@ -129,6 +129,18 @@ int  sp_cuda_read_batch_partial(const sp_cuda_cache_t *cc, int which,
                                 int layer, int head, int start_pos, int n_pos,
                                 float *d_out, int max_bands);
 
+/* New: token-major read of every KV head of a layer range in one launch
+ * (replaces the per-head loop of KvCache::read_gpu,
+ * src/engine/kv_cache.cpp:1100-1228): which 0 = K, 1 = V; positions
+ * [start_pos, start_pos + n_tok) of layers [layer0, layer0 + n_layers) go
+ * to d_out as fp32 [n_layers][n_tok][n_heads_kv][head_dim], rows equal to
+ * those of sp_cuda_read_batch_partial (same max_bands meaning).  The
+ * head_dim-128 ship layouts only (K 5/5/4/3 with the squarefree-first
+ * order, V 3-bit; d_out 16-byte aligned); other caches return
+ * SP_ERR_UNSUPPORTED.  Stream-ordered on cc->stream, allocates nothing. */
+int  sp_cuda_read_kv_tokens(const sp_cuda_cache_t *cc, int which, int layer0, int n_layers,
+                            int start_pos, int n_tok, float *d_out, int max_bands);
+
 /* -------------------------------------------------- fused decode attention -- */
 /* New (no reference GPU counterpart; replaces the CPU ggml op
  * llama_sp_kq_compute, src/engine/llama_sp_fused_kq.cpp:82-165, plus the
@@ -165,6 +177,18 @@ int  sp_cuda_attn_decode(const sp_cuda_cache_t *cc, int layer0, int n_layers,
 int  sp_cuda_kq_scores(const void *d_packed, int total_bytes_per_pos, int is_v, int head_dim,
                        int n_kv, const void *d_q, int q_dtype, long long q_row_stride,
                        int n_head_q, float *d_dst, long long dst_row_stride, void *stream);
+
+/* New: the same op over n_slots slots in one launch (slot i reads
+ * d_packed + i * packed_slot_stride, its query rows at d_q + i *
+ * q_slot_stride and writes dst rows at d_dst + i * dst_slot_stride, all in
+ * bytes), e.g. every (layer, KV head) of a cache with the slot stride
+ * max_seq_len * total_bytes_per_pos.  The reference calls its op once per
+ * head; one launch per step avoids a launch per slot.  At most 65535 slots. */
+int  sp_cuda_kq_scores_strided(const void *d_packed, long long packed_slot_stride, int n_slots,
+                               int total_bytes_per_pos, int is_v, int head_dim, int n_kv,
+                               const void *d_q, int q_dtype, long long q_row_stride,
+                               long long q_slot_stride, int n_head_q, float *d_dst,
+                               long long dst_row_stride, long long dst_slot_stride, void *stream);
 
 /* New; no counterpart in the reference.  The fused decode above for callers
  * that cannot allocate device memory (an engine that owns every device

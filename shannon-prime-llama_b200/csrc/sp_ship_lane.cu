@@ -34,6 +34,7 @@
 #include "sp_internal.cuh"
 #include "sp_bulk.cuh"
 
+#include <atomic>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <stdlib.h>
@@ -507,11 +508,17 @@ namespace {
 constexpr int kKqThreads = 128;       // positions per CTA
 constexpr int kKqMaxHeads = 64;
 
+// blockIdx.y selects the slot: packed, q and dst advance by their slot
+// strides (bytes), so one launch serves every (layer, KV head) of a call.
 template <bool KS>
 __global__ void __launch_bounds__(kKqThreads)
 k_kq_scores_lane(const uint8_t *packed, int n_kv, const void *q, int q_f16, long long q_stride, int n_head_q,
-                 float *dst, long long dst_stride, float inv_sqrt_n)
+                 float *dst, long long dst_stride, float inv_sqrt_n, long long packed_slot, long long q_slot,
+                 long long dst_slot)
 {
+    packed += (long long)blockIdx.y * packed_slot;
+    q = reinterpret_cast<const uint8_t *>(q) + (long long)blockIdx.y * q_slot;
+    dst = reinterpret_cast<float *>(reinterpret_cast<char *>(dst) + (long long)blockIdx.y * dst_slot);
     using L = LaneLayout<KS>;
     constexpr int TB = L::TB, TH = TB / 2;     // row bytes, halfwords
     constexpr LaneOrder ord = lane_order();
@@ -594,14 +601,17 @@ k_kq_scores_lane(const uint8_t *packed, int n_kv, const void *q, int q_f16, long
 
 }  // namespace
 
-extern "C" int sp_cuda_kq_scores(const void *d_packed, int total_bytes_per_pos, int is_v, int head_dim, int n_kv,
-                                 const void *d_q, int q_dtype, long long q_row_stride, int n_head_q,
-                                 float *d_dst, long long dst_row_stride, void *stream)
+extern "C" int sp_cuda_kq_scores_strided(const void *d_packed, long long packed_slot_stride, int n_slots,
+                                         int total_bytes_per_pos, int is_v, int head_dim, int n_kv, const void *d_q,
+                                         int q_dtype, long long q_row_stride, long long q_slot_stride, int n_head_q,
+                                         float *d_dst, long long dst_row_stride, long long dst_slot_stride,
+                                         void *stream)
 {
     sp_clear_error();
-    if (n_kv < 0 || n_head_q < 1 || !d_packed || !d_q || !d_dst)
+    if (n_kv < 0 || n_head_q < 1 || n_slots < 0 || !d_packed || !d_q || !d_dst)
         return sp_set_error(SP_ERR_ARG, "kq_scores: bad arguments");
-    if (n_kv == 0) return SP_OK;
+    if (n_kv == 0 || n_slots == 0) return SP_OK;
+    if (n_slots > 65535) return sp_set_error(SP_ERR_ARG, "kq_scores: at most 65535 slots per call");
     if (head_dim != kLN || n_head_q > kKqMaxHeads ||
         total_bytes_per_pos != (is_v ? LaneLayout<false>::TB : LaneLayout<true>::TB))
         return sp_set_error(SP_ERR_UNSUPPORTED,
@@ -611,20 +621,31 @@ extern "C" int sp_cuda_kq_scores(const void *d_packed, int total_bytes_per_pos, 
         return sp_set_error(SP_ERR_ARG, "kq_scores: q must be f32 or f16");
     const int es = q_dtype == SP_DTYPE_F32 ? 4 : 2;
     if (((uintptr_t)d_packed & 1) || ((uintptr_t)d_q % es) || (q_row_stride % es) || ((uintptr_t)d_dst & 3) ||
-        (dst_row_stride & 3) || q_row_stride < (long long)es * head_dim || dst_row_stride < 4LL * n_kv)
+        (dst_row_stride & 3) || q_row_stride < (long long)es * head_dim || dst_row_stride < 4LL * n_kv ||
+        (packed_slot_stride & 1) || (q_slot_stride % es) || (dst_slot_stride & 3))
         return sp_set_error(SP_ERR_ARG, "kq_scores: misaligned pointer or stride");
-    const unsigned blocks = (unsigned)((n_kv + kKqThreads - 1) / kKqThreads);
+    const dim3 grid((unsigned)((n_kv + kKqThreads - 1) / kKqThreads), (unsigned)n_slots);
     cudaStream_t s = (cudaStream_t)stream;
     const float isn = sp_inv_sqrt_n(kLN);
     if (is_v)
-        k_kq_scores_lane<false><<<blocks, kKqThreads, 0, s>>>((const uint8_t *)d_packed, n_kv, d_q,
-                                                              q_dtype == SP_DTYPE_F16, q_row_stride, n_head_q,
-                                                              d_dst, dst_row_stride, isn);
+        k_kq_scores_lane<false><<<grid, kKqThreads, 0, s>>>((const uint8_t *)d_packed, n_kv, d_q,
+                                                            q_dtype == SP_DTYPE_F16, q_row_stride, n_head_q, d_dst,
+                                                            dst_row_stride, isn, packed_slot_stride, q_slot_stride,
+                                                            dst_slot_stride);
     else
-        k_kq_scores_lane<true><<<blocks, kKqThreads, 0, s>>>((const uint8_t *)d_packed, n_kv, d_q,
-                                                             q_dtype == SP_DTYPE_F16, q_row_stride, n_head_q,
-                                                             d_dst, dst_row_stride, isn);
+        k_kq_scores_lane<true><<<grid, kKqThreads, 0, s>>>((const uint8_t *)d_packed, n_kv, d_q,
+                                                           q_dtype == SP_DTYPE_F16, q_row_stride, n_head_q, d_dst,
+                                                           dst_row_stride, isn, packed_slot_stride, q_slot_stride,
+                                                           dst_slot_stride);
     return sp_check_cuda(cudaGetLastError(), "kq_scores launch");
+}
+
+extern "C" int sp_cuda_kq_scores(const void *d_packed, int total_bytes_per_pos, int is_v, int head_dim, int n_kv,
+                                 const void *d_q, int q_dtype, long long q_row_stride, int n_head_q,
+                                 float *d_dst, long long dst_row_stride, void *stream)
+{
+    return sp_cuda_kq_scores_strided(d_packed, 0, 1, total_bytes_per_pos, is_v, head_dim, n_kv, d_q, q_dtype,
+                                     q_row_stride, 0, n_head_q, d_dst, dst_row_stride, 0, stream);
 }
 
 // ------------------------------------------------- lane-per-vector read --
@@ -648,9 +669,18 @@ struct ReadSmem {
     uint16_t rows[kLaneWarps][32 * LaneLayout<KS>::TB / 2];
 };
 
+// Slots a read covers: n_layers x n_heads slots, slot (l, h) at
+// packed + (slot0 + l * n_heads + h) * slot_stride + pos0 * row bytes; its
+// rows go to the output tensor at coordinates (h * 128, t, l).
+struct ReadGrid {
+    long long slot_stride;
+    long long slot0;
+    int n_heads, n_layers, pos0;
+};
+
 template <bool KS>
 __global__ void __launch_bounds__(kLaneWarps * 32, kLaneMinBlocks)
-k_decode_lane(const uint8_t *packed, int n_pos, int nb_use, float inv_sqrt_n, unsigned int *status,
+k_decode_lane(const uint8_t *packed, ReadGrid rg, int n_pos, int nb_use, float inv_sqrt_n, unsigned int *status,
               const __grid_constant__ ReadMap map)
 {
     using L = LaneLayout<KS>;
@@ -664,11 +694,15 @@ k_decode_lane(const uint8_t *packed, int n_pos, int nb_use, float inv_sqrt_n, un
         if (threadIdx.x == 0 && status) atomicOr(status, 4u);
         return;
     }
-    const int n_b = (n_pos + 31) >> 5;
-    for (int bt = blockIdx.x * kLaneWarps + warp; bt < n_b; bt += gridDim.x * kLaneWarps) {
-        const int t0 = bt * 32, live = min(32, n_pos - t0);
+    const int n_bs = (n_pos + 31) >> 5;                 // batches per slot
+    const long long n_b = (long long)n_bs * rg.n_heads * rg.n_layers;
+    for (long long bt = (long long)blockIdx.x * kLaneWarps + warp; bt < n_b; bt += (long long)gridDim.x * kLaneWarps) {
+        const int sl = (int)(bt / n_bs);
+        const int t0 = (int)(bt - (long long)sl * n_bs) * 32, live = min(32, n_pos - t0);
+        const int l = sl / rg.n_heads, hh = sl - l * rg.n_heads;
         uint16_t *rows = sm.rows[warp];
-        const uint16_t *src = reinterpret_cast<const uint16_t *>(packed + (long long)t0 * TB);
+        const uint16_t *src = reinterpret_cast<const uint16_t *>(
+            packed + (rg.slot0 + sl) * rg.slot_stride + (long long)(rg.pos0 + t0) * TB);
         for (int i = lane; i < live * TH; i += 32) rows[i] = src[i];
         __syncwarp();
         const uint16_t *r16 = rows + lane * TH;
@@ -720,9 +754,9 @@ k_decode_lane(const uint8_t *packed, int n_pos, int nb_use, float inv_sqrt_n, un
         if (lane == 0) {
 #pragma unroll
             for (int q = 0; q < 4; q++)
-                asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
                                  &map.m),
-                             "r"(q * 32), "r"(t0), "r"(out0 + q * 4096)
+                             "r"(hh * kLN + q * 32), "r"(t0), "r"(l), "r"(out0 + q * 4096)
                              : "memory");
             asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         }
@@ -731,42 +765,51 @@ k_decode_lane(const uint8_t *packed, int n_pos, int nb_use, float inv_sqrt_n, un
     if (lane == 0) bulk_wait_all();
 }
 
+// Output d_out: [n_layers][n_pos][n_heads][128] fp32 (one slot: [n_pos][128]).
 template <bool KS>
-int launch_read_lane(const uint8_t *packed, int n_pos, int nb_use, float *d_out, unsigned int *status,
-                     cudaStream_t s)
+int launch_read_lane(const uint8_t *packed, const ReadGrid &rg, int n_pos, int nb_use, float *d_out,
+                     unsigned int *status, cudaStream_t s)
 {
     auto fn = lane_encode_fn();
     if (!fn) return 1;
     ReadMap map;
     memset(&map, 0, sizeof(map));
-    const cuuint64_t dims[2] = {(cuuint64_t)kLN, (cuuint64_t)n_pos};
-    const cuuint64_t strides[1] = {(cuuint64_t)kLN * 4};
-    const cuuint32_t box[2] = {32, 32};
-    const cuuint32_t estr[2] = {1, 1};
-    if (fn(&map.m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, d_out, dims, strides, box, estr,
+    const cuuint64_t row = (cuuint64_t)kLN * rg.n_heads;
+    const cuuint64_t dims[3] = {row, (cuuint64_t)n_pos, (cuuint64_t)rg.n_layers};
+    const cuuint64_t strides[2] = {row * 4, row * 4 * (cuuint64_t)n_pos};
+    const cuuint32_t box[3] = {32, 32, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (fn(&map.m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, d_out, dims, strides, box, estr,
            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return 1;
     auto k = k_decode_lane<KS>;
     const size_t smem = sizeof(ReadSmem<KS>);
-    static int occ = 0, sms = 0, dev_done = -1;
+    // Per device: attribute set and occupancy looked up once (atomics, so
+    // host threads driving any devices race harmlessly).
+    constexpr int kMaxDev = 64;
+    static std::atomic<int> occ_tab[kMaxDev], sms_tab[kMaxDev];
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev != dev_done) {
+    if (dev < 0 || dev >= kMaxDev) return -1;
+    int occ = occ_tab[dev].load(std::memory_order_acquire);
+    if (occ == 0) {
         if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
             sp_check_cuda(cudaGetLastError(), "lane read smem attribute");
             return -1;
         }
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, kLaneWarps * 32, smem);
+        int o = 0, sms = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k, kLaneWarps * 32, smem);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (occ < 1) occ = 1;
-        if (sms < 1) sms = 148;
-        dev_done = dev;
+        sms_tab[dev].store(sms > 0 ? sms : 148, std::memory_order_relaxed);
+        occ = o > 0 ? o : 1;
+        occ_tab[dev].store(occ, std::memory_order_release);
     }
-    const long long n_b = (n_pos + 31) / 32;
+    const int sms = sms_tab[dev].load(std::memory_order_relaxed);
+    const long long n_b = (long long)((n_pos + 31) / 32) * rg.n_heads * rg.n_layers;
     long long blocks = (n_b + kLaneWarps - 1) / kLaneWarps;
     if (blocks > (long long)sms * occ) blocks = (long long)sms * occ;
-    k<<<(unsigned)blocks, kLaneWarps * 32, smem, s>>>(packed, n_pos, nb_use, sp_inv_sqrt_n(kLN), status, map);
+    k<<<(unsigned)blocks, kLaneWarps * 32, smem, s>>>(packed, rg, n_pos, nb_use, sp_inv_sqrt_n(kLN), status, map);
     return sp_check_cuda(cudaGetLastError(), "lane read launch") ? -1 : 0;
 }
 
@@ -782,9 +825,42 @@ int sp_decode_lane_try(const uint8_t *d_rows, int n_pos, float *d_out, const int
     const int hx = lane_half_of(bl, d_order, std_order);
     if (hx < 0 || ((uintptr_t)d_rows & 1) || ((uintptr_t)d_out & 15)) return 0;
     const int nb_use = (max_bands < 0 || max_bands >= bl.n_bands) ? bl.n_bands : max_bands;
-    const int r = hx == 0 ? launch_read_lane<true>(d_rows, n_pos, nb_use, d_out, d_status, s)
-                          : launch_read_lane<false>(d_rows, n_pos, nb_use, d_out, d_status, s);
+    const ReadGrid rg{0, 0, 1, 1, 0};
+    const int r = hx == 0 ? launch_read_lane<true>(d_rows, rg, n_pos, nb_use, d_out, d_status, s)
+                          : launch_read_lane<false>(d_rows, rg, n_pos, nb_use, d_out, d_status, s);
     if (r > 0) return 0;                        // no tensor-map encoder: the warp kernel reads
     *rc = r ? sp_set_error(SP_ERR_CUDA, "lane read failed") : SP_OK;
     return 1;
+}
+
+// Token-major read of every head of a layer range in one launch (the B200
+// form of the reference's KvCache::read_gpu, kv_cache.cpp:1100-1228, which
+// decompresses head by head into [kv_len][H][hd]): which 0 = K, 1 = V.
+extern "C" int sp_cuda_read_kv_tokens(const sp_cuda_cache_t *cc, int which, int layer0, int n_layers,
+                                      int start_pos, int n_tok, float *d_out, int max_bands)
+{
+    sp_clear_error();
+    if (!cc || !d_out || (which != 0 && which != 1)) return sp_set_error(SP_ERR_ARG, "read_kv_tokens: bad arguments");
+    const int H = cc->config.n_heads_kv;
+    if (layer0 < 0 || n_layers < 0 || layer0 + n_layers > cc->config.n_layers || start_pos < 0 || n_tok < 0 ||
+        (long long)start_pos + n_tok > cc->max_seq_len)
+        return sp_set_error(SP_ERR_ARG, "read_kv_tokens: range out of bounds");
+    if (n_layers == 0 || n_tok == 0) return SP_OK;
+    if (cudaSetDevice(cc->device) != cudaSuccess) return sp_set_error(SP_ERR_CUDA, "read_kv_tokens: cudaSetDevice");
+    const sp_band_config_t &bc = which ? cc->v_bands : cc->k_bands;
+    const SpBandLayout bl = sp_layout_from(bc);
+    const int *order = which ? nullptr : (cc->config.use_mobius_mask ? cc->d_mobius_order : nullptr);
+    const int hx = lane_half_of(bl, order, true);
+    const uint8_t *base = (const uint8_t *)(which ? cc->d_v_cache : cc->d_k_cache);
+    if (hx < 0 || hx != which || ((uintptr_t)base & 1) || ((uintptr_t)d_out & 15))
+        return sp_set_error(SP_ERR_UNSUPPORTED,
+                            "read_kv_tokens: head_dim 128 ship layouts (K 5/5/4/3 with the standard order, V 3-bit), "
+                            "16-byte aligned output");
+    const int nb_use = (max_bands < 0 || max_bands >= bl.n_bands) ? bl.n_bands : max_bands;
+    const ReadGrid rg{(long long)cc->max_seq_len * bc.total_bytes, (long long)layer0 * H, H, n_layers, start_pos};
+    cudaStream_t s = (cudaStream_t)cc->stream;
+    const int r = hx == 0 ? launch_read_lane<true>(base, rg, n_tok, nb_use, d_out, cc->d_status, s)
+                          : launch_read_lane<false>(base, rg, n_tok, nb_use, d_out, cc->d_status, s);
+    if (r > 0) return sp_set_error(SP_ERR_UNSUPPORTED, "read_kv_tokens: no tensor-map encoder in this driver");
+    return r ? sp_set_error(SP_ERR_CUDA, "read_kv_tokens: launch failed") : SP_OK;
 }

@@ -144,10 +144,13 @@ SIGNATURES = {
     "sp_cuda_read_k_batch": (_V, [_CC, _I, _I, _I, _I, _P]),
     "sp_cuda_read_v_batch": (_V, [_CC, _I, _I, _I, _I, _P]),
     "sp_cuda_read_batch_partial": (_I, [_CC, _I, _I, _I, _I, _I, _P, _I]),
+    "sp_cuda_read_kv_tokens": (_I, [_CC, _I, _I, _I, _I, _I, _P, _I]),
     "sp_cuda_attn_decode": (_I, [_CC, _I, _I, _P, _I, _I, _F, _P, _I, _P]),
     "sp_cuda_attn_decode_allgather": (_I, [_CC, _I, _I, _P, _I, _I, _F, _I, _P, _P, _P, _P, _I, C.c_longlong,
                                            C.c_longlong, _I, _I, C.c_uint, _P]),
     "sp_cuda_kq_scores": (_I, [_P, _I, _I, _I, _I, _P, _I, C.c_longlong, _I, _P, C.c_longlong, _P]),
+    "sp_cuda_kq_scores_strided": (_I, [_P, C.c_longlong, _I, _I, _I, _I, _I, _P, _I, C.c_longlong, C.c_longlong, _I,
+                                       _P, C.c_longlong, C.c_longlong, _P]),
     "sp_cuda_attn_decode_noalloc": (_I, [_P, _P, _I, C.POINTER(SpBandConfig),
                                          C.POINTER(SpBandConfig), _P, _I, _I, _I, _P, _I, _I,
                                          _F, _P, _I, _P]),

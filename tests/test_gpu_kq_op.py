@@ -42,6 +42,43 @@ def test_kq_scores_match_oracle(cuda, is_v, n_kv, n_q, qdt):
     assert np.all(got[:, n_kv:] == 7.0)                  # padding untouched
 
 
+@pytest.mark.parametrize("is_v", [0, 1])
+def test_kq_scores_strided_matches_per_slot_calls(cuda, is_v):
+    """One launch over several slots (padded slot strides for rows, queries
+    and scores) equals one call per slot, bit for bit, and the oracle."""
+    import torch
+    L = spb200.lib()
+    n, n_kv, n_q, n_slots = 128, 777, 4, 5
+    tb = 50 if is_v else 76
+    max_seq = 800
+    slab = torch.zeros(n_slots, max_seq * tb, dtype=torch.uint8)
+    recs = []
+    for sl in range(n_slots):
+        k, v = synth.kv_slot_np(6, 0, sl, n_kv, n, 1.0)
+        rows = O.ship_write(v if is_v else k, VB if is_v else KB, not is_v)
+        slab[sl, :n_kv * tb] = torch.from_numpy(rows.reshape(-1))
+        recs.append(O.ship_read(rows, n, VB if is_v else KB, not is_v).astype(np.float64))
+    slab = slab.cuda()
+    q = (torch.randn(n_slots, n_q + 1, n, generator=torch.Generator().manual_seed(3)) / 8).half().cuda()
+    dst = torch.full((n_slots, n_q, n_kv + 5), 7.0, dtype=torch.float32, device="cuda")
+    rc = L.sp_cuda_kq_scores_strided(slab.data_ptr(), max_seq * tb, n_slots, tb, is_v, n, n_kv, q.data_ptr(), 1,
+                                     n * 2, (n_q + 1) * n * 2, n_q, dst.data_ptr(), (n_kv + 5) * 4,
+                                     n_q * (n_kv + 5) * 4, None)
+    assert rc == 0, spb200.last_error()
+    one = torch.full_like(dst, 7.0)
+    for sl in range(n_slots):
+        assert L.sp_cuda_kq_scores(slab[sl].data_ptr(), tb, is_v, n, n_kv, q[sl].data_ptr(), 1, n * 2, n_q,
+                                   one[sl].data_ptr(), (n_kv + 5) * 4, None) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(dst, one)
+    got = dst.cpu().numpy()
+    for sl in range(n_slots):
+        ref = q[sl, :n_q].float().cpu().numpy().astype(np.float64) @ recs[sl].T
+        err = np.linalg.norm(got[sl, :, :n_kv] - ref) / np.linalg.norm(ref)
+        assert err <= 1e-5, (sl, err)
+    assert np.all(got[:, :, n_kv:] == 7.0)
+
+
 def test_kq_scores_rejects_other_shapes(cuda):
     import torch
     L = spb200.lib()

@@ -251,3 +251,33 @@ def test_ship_lane_read_matches_warp_read_and_oracle(cuda, monkeypatch, start, T
                 monkeypatch.delenv("SHANNON_PRIME_DECODE_WARP", raising=False)
             np.testing.assert_array_equal(outs[0], outs[1])
             np.testing.assert_array_equal(outs[0], O.ship_read(packed[1], n, bands, mob, max_bands=mb))
+
+
+@pytest.mark.parametrize("layer0,nl,start,T", [(0, 3, 0, 4096), (1, 2, 7, 333), (2, 1, 100, 1)])
+def test_read_kv_tokens_matches_per_slot_reads(cuda, layer0, nl, start, T):
+    """The token-major all-heads read (one launch over a layer range) puts
+    every slot's rows at [layer][token][head], bit-identical with the per-slot
+    reference read, for full and partial band reads."""
+    torch = _torch()
+    H, n, L = 3, 128, 3
+    cache = spb200.Cache(n, L, H, 4112)
+    for layer in range(L):
+        k, v = _layer_inputs(40 + layer, H, 4096, n, sigma=1.0)
+        cache.write_kv_tokens(layer, 0, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda())
+    torch.cuda.synchronize()
+    lib = spb200.lib()
+    for which in (0, 1):
+        for mb in (-1, 1):
+            got = torch.full((nl, T, H, n), 5.0, device="cuda")
+            rc = lib.sp_cuda_read_kv_tokens(C.byref(cache.cc), which, layer0, nl, start, T, got.data_ptr(), mb)
+            assert rc == 0, spb200.last_error()
+            ref = torch.full((nl, T, H, n), 6.0, device="cuda")
+            for l in range(nl):
+                for h in range(H):
+                    one = torch.empty(T, n, device="cuda")
+                    cache.read_batch(which, layer0 + l, h, start, one, max_bands=mb)
+                    ref[l, :, h] = one
+            torch.cuda.synchronize()
+            assert torch.equal(got, ref), (which, mb)
+    bad = torch.empty(1, 4, H, n, device="cuda")
+    assert lib.sp_cuda_read_kv_tokens(C.byref(cache.cc), 0, 2, 2, 0, 4, bad.data_ptr(), -1) == spb200.SP_ERR_ARG
