@@ -46,6 +46,7 @@
 #include <atomic>
 #include <utility>
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 
 namespace {
@@ -849,4 +850,310 @@ int sp_attn_tc_launch(const SpAttnArgs &a_in, cudaStream_t s, cudaEvent_t ev_beg
     int rc = sp_check_cuda(cudaGetLastError(), "tcgen05 attention launch");
     if (rc) return rc;
     return sp_attn_seg_combine_launch(a, sc, s);
+}
+
+// ------------------------------------------- fused-KQ scores op, tcgen05 --
+// The scores-only op (sp_cuda_kq_scores[_strided], the GPU body of the
+// reference's ggml op llama_sp_kq_compute, llama_sp_fused_kq.cpp:82-165)
+// for K rows of the head_dim-128 ship layout and up to 8 query rows: the K
+// side of the decode above without the softmax.  A CTA of 4 warps takes
+// 128-position tiles of one slot; thread t unpacks row t into tensor memory
+// (A operand, codes as fp16 subnormals), band b's warp issues band b's two
+// MMAs against the query operand B_q (q' = perm(H q) / sqrt(n) as fp16 hi
+// and lo parts), and thread t reads its score row back and writes its
+// position's score for every query row (coalesced along positions).
+namespace {
+
+constexpr int kKqTcThreads = 128;
+
+__host__ __device__ constexpr bool kq_squarefree(int n)
+{
+    for (int p = 2; p * p <= n; p++)
+        if (n % (p * p) == 0) return false;
+    return true;
+}
+// Squarefree-first order of 0..127 (the order of every ship cache's K rows).
+struct KqOrder { int v[kN]; };
+__host__ __device__ constexpr KqOrder kq_order()
+{
+    KqOrder o{};
+    int k = 0;
+    for (int i = 0; i < kN; i++)
+        if (kq_squarefree(i + 1)) o.v[k++] = i;
+    for (int i = 0; i < kN; i++)
+        if (!kq_squarefree(i + 1)) o.v[k++] = i;
+    return o;
+}
+__constant__ KqOrder c_kq_order = kq_order();
+
+struct alignas(128) KqSmem {
+    unsigned char rows[2][kKTileB];          // two tiles of K rows
+    unsigned char bq[16 * kN * 2];           // B_q, K-major: (n,k) at n/8*2048 + k/8*128 + n%8*16 + k%8*2
+    float qt[8][kN];
+    float q[8][kN];
+    float qsum[8][4];
+    float qmax[8];
+    float cin[4][8];
+    unsigned long long bar[2], bar_s;
+    uint32_t tmem;
+    int abort;
+};
+
+struct KqTcArgs {
+    const uint8_t *packed;
+    long long packed_slot;
+    const void *q;
+    long long q_stride, q_slot;
+    float *dst;
+    long long dst_stride, dst_slot;
+    int n_kv, n_head_q, q_f16;
+    float inv_sqrt_n;
+};
+
+template <int GT>
+__global__ void __launch_bounds__(kKqTcThreads, 3)
+k_kq_scores_tc(KqTcArgs a)
+{
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    KqSmem &sm = *reinterpret_cast<KqSmem *>(smem_raw);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, t = tid;
+    const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+    const uint8_t *packed = a.packed + (long long)blockIdx.y * a.packed_slot;
+    const uint8_t *qb = reinterpret_cast<const uint8_t *>(a.q) + (long long)blockIdx.y * a.q_slot;
+    float *dst = reinterpret_cast<float *>(reinterpret_cast<char *>(a.dst) + (long long)blockIdx.y * a.dst_slot);
+    const int n_tiles = (a.n_kv + kTM - 1) / kTM;
+    constexpr uint32_t kQColS = 0, kQColA = 64, kQCols = 128;
+
+    if (tid == 0) {
+        spb::mbar_init(spb::smem_u32(&sm.bar[0]), 1);
+        spb::mbar_init(spb::smem_u32(&sm.bar[1]), 1);
+        spb::mbar_init(spb::smem_u32(&sm.bar_s), 4);
+        spb::mbar_init_fence();
+        sm.abort = 0;
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(spb::smem_u32(&sm.tmem)), "r"(kQCols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    // ---- q' of every query row (warp g: rows g, g + 4) ----
+    for (int g = warp; g < GT; g += 4) {
+        if (g < a.n_head_q) {
+            const uint8_t *qr = qb + (long long)g * a.q_stride;
+            float x[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int i = lane * 4 + e;
+                x[e] = a.q_f16 ? __half2float(reinterpret_cast<const __half *>(qr)[i])
+                               : reinterpret_cast<const float *>(qr)[i];
+            }
+            sp_warp_wht<4>(x, lane);
+#pragma unroll
+            for (int e = 0; e < 4; e++) sm.qt[g][lane * 4 + e] = x[e] * a.inv_sqrt_n;
+            __syncwarp();
+            float mxv = 0.0f, bs = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int i = lane * 4 + e;
+                const float v = sm.qt[g][c_kq_order.v[i]];
+                sm.q[g][i] = v;
+                mxv = fmaxf(mxv, fabsf(v));
+                bs += v;
+            }
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) bs += __shfl_xor_sync(0xffffffffu, bs, o);
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) mxv = fmaxf(mxv, __shfl_xor_sync(0xffffffffu, mxv, o));
+            if ((lane & 7) == 0) sm.qsum[g][lane >> 3] = bs;
+            if (lane == 0) sm.qmax[g] = mxv;
+        } else {
+            for (int i = lane; i < kN; i += 32) sm.q[g][i] = 0.0f;
+            if (lane < 4) sm.qsum[g][lane] = 0.0f;
+            if (lane == 0) sm.qmax[g] = 0.0f;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sm.tmem;
+    // ---- B_q column k = t; score scales ----
+    float kc[GT];
+    {
+        const int b = t >> 5, r = (t & 31) >> 1, hf = t & 1;
+        const int code = c_tabs.k[b][r][hf], d = c_tabs.k[b][r][2 + hf];
+        unsigned char *colbase = sm.bq + (t >> 3) * 128 + (t & 7) * 2;
+#pragma unroll
+        for (int g = 0; g < GT; g++) {
+            const float qm = sm.qmax[g];
+            const int F = qm > 1e-30f ? 6 - ilogbf(qm) : 0;
+            const float v = ldexpf(sm.q[g][32 * b + code], F - d);
+            const __half hi = __float2half_rn(v);
+            const __half lo = __float2half_rn(v - __half2float(hi));
+            const int nh = g, nl = GT + g;
+            *reinterpret_cast<__half *>(colbase + (nh >> 3) * 2048 + (nh & 7) * 16) = hi;
+            *reinterpret_cast<__half *>(colbase + (nl >> 3) * 2048 + (nl & 7) * 16) = lo;
+            kc[g] = ldexpf(1.0f, 24 - F);
+            if (t < 4) {
+                const float m_b = (float)((1 << (kbits(t) - 1)) - 1);
+                sm.cin[t][g] = -ldexpf(m_b * sm.qsum[g][t], F - 24);
+            }
+        }
+        if (GT == 4) {
+#pragma unroll
+            for (int n = 8; n < 16; n++) *reinterpret_cast<__half *>(colbase + 2048 + (n & 7) * 16) = __float2half_rn(0.0f);
+        }
+    }
+    spb::fence_proxy_async();
+
+    // ---- tiles: full ones by bulk copy (thread 0, one tile ahead), a ragged
+    // last one by the threads ----
+    uint64_t policy = 0;
+    if (tid == 0) policy = spb::evict_first_policy();
+    auto full = [&](int tt) { return (tt + 1) * kTM <= a.n_kv; };
+    auto issue = [&](int tt, int buf) {
+        const uint32_t bar = spb::smem_u32(&sm.bar[buf]);
+        spb::fence_proxy_async();
+        spb::mbar_expect_tx(bar, kKTileB);
+        spb::bulk_g2s(spb::smem_u32(&sm.rows[buf][0]), packed + (long long)tt * kKTileB, kKTileB, bar, policy);
+    };
+    const int tt0 = blockIdx.x;
+    if (tid == 0 && tt0 < n_tiles && full(tt0)) issue(tt0, 0);
+    __syncthreads();
+    uint32_t phase[2] = {0u, 0u};
+    int j = 0;
+    for (int tt = tt0; tt < n_tiles; tt += gridDim.x, j++) {
+        const int buf = j & 1;
+        const int nxt = tt + gridDim.x;
+        if (tid == 0 && nxt < n_tiles && full(nxt)) issue(nxt, buf ^ 1);
+        const int live = min(kTM, a.n_kv - tt * kTM);
+        if (full(tt)) {
+            if (!*(volatile int *)&sm.abort &&
+                !spb::wait_stage(spb::smem_u32(&sm.bar[buf]), phase[buf], nullptr))
+                *(volatile int *)&sm.abort = 1;
+            phase[buf] ^= 1u;
+        } else {
+            const uint16_t *src = reinterpret_cast<const uint16_t *>(packed + (long long)tt * kKTileB);
+            uint16_t *d16 = reinterpret_cast<uint16_t *>(&sm.rows[buf][0]);
+            for (int i = tid; i < kTM * kKRow / 2; i += kKqTcThreads) d16[i] = i < live * kKRow / 2 ? src[i] : 0;
+            __syncthreads();
+        }
+        const uint32_t *kr = reinterpret_cast<const uint32_t *>(&sm.rows[buf][0] + kKRow * t);
+        uint32_t w[19];
+#pragma unroll
+        for (int i = 0; i < 19; i++) w[i] = kr[i];
+        float bsc[4];
+        bsc[0] = finite_or_zero_f((unsigned short)(w[0] & 0xffffu));
+        bsc[1] = finite_or_zero_f((unsigned short)(w[5] >> 16));
+        bsc[2] = finite_or_zero_f((unsigned short)(w[11] & 0xffffu));
+        bsc[3] = finite_or_zero_f((unsigned short)(w[15] >> 16));
+        static_for<4>([&](auto B) {
+            constexpr int b = decltype(B)::value;
+            uint32_t v[16];
+            static_for<16>([&](auto R) {
+                constexpr int r = decltype(R)::value;
+                constexpr int bits = kbits(b);
+                constexpr int W = kbit(b) + bits * kKPair[b][r][0] - kKPair[b][r][2];
+                constexpr uint32_t M = (((1u << bits) - 1u) << kKPair[b][r][2]) |
+                                       (((1u << bits) - 1u) << (16 + kKPair[b][r][3]));
+                v[r] = window<W>(w) & M;
+            });
+            tmem_st16(tmem + lane_base + kQColA + 16 * b, v);
+        });
+        tmem_wait_st();
+        tc_fence_before();
+        __syncthreads();                 // A rows written; this tile's row buffer read
+        if (elect_one()) {
+            tc_fence_after();
+            const uint32_t bq = spb::smem_u32(sm.bq);
+            const int b = warp;
+#pragma unroll
+            for (int jj = 0; jj < 2; jj++)
+                mma_ts(tmem + kQColS + 16u * b, tmem + kQColA + 16u * b + 8u * jj,
+                       sdesc(bq + (uint32_t)(4 * b + 2 * jj) * 128u, 128u, 2048u), (uint32_t)jj);
+            mma_commit(spb::smem_u32(&sm.bar_s));
+        }
+        __syncwarp();
+        if (!*(volatile int *)&sm.abort && !spb::wait_stage(spb::smem_u32(&sm.bar_s), (uint32_t)(j & 1), nullptr))
+            *(volatile int *)&sm.abort = 1;
+        tc_fence_after();
+        float su[GT];
+#pragma unroll
+        for (int h = 0; h < GT; h++) su[h] = 0.0f;
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            uint32_t d[16];
+            if constexpr (GT == 4) tmem_ld8(tmem + lane_base + kQColS + 16 * b, *reinterpret_cast<uint32_t (*)[8]>(&d[0]));
+            else tmem_ld16(tmem + lane_base + kQColS + 16 * b, d);
+            tmem_wait_ld();
+#pragma unroll
+            for (int h = 0; h < GT; h++)
+                su[h] = fmaf(bsc[b], __uint_as_float(d[h]) + __uint_as_float(d[GT + h]) + sm.cin[b][h], su[h]);
+        }
+        tc_fence_before();
+        if (t < live) {
+            const bool bad = *(volatile int *)&sm.abort != 0;
+            float *o = dst + (long long)tt * kTM + t;
+#pragma unroll
+            for (int h = 0; h < GT; h++)
+                if (h < a.n_head_q)
+                    *reinterpret_cast<float *>(reinterpret_cast<char *>(o) + (long long)h * a.dst_stride) =
+                        bad ? __int_as_float(0x7fc00000) : kc[h] * su[h];
+        }
+    }
+    // After a timed-out wait: let the copies and MMAs in flight land
+    // (bounded) before the memory is released.
+    __syncthreads();
+    if (sm.abort && tid == 0) {
+        spb::wait_stage(spb::smem_u32(&sm.bar[0]), phase[0], nullptr);
+        spb::wait_stage(spb::smem_u32(&sm.bar[1]), phase[1], nullptr);
+        if (j > 0) spb::wait_stage(spb::smem_u32(&sm.bar_s), (uint32_t)((j - 1) & 1), nullptr);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kQCols) : "memory");
+}
+
+}  // namespace
+
+// The tcgen05 scores op for K rows of the head_dim-128 ship layout with up
+// to 8 query rows: 1 and *rc set if it took the call.
+int sp_kq_scores_tc_try(const uint8_t *packed, long long packed_slot, int n_slots, int n_kv, const void *q,
+                        int q_f16, long long q_stride, long long q_slot, int n_head_q, float *dst,
+                        long long dst_stride, long long dst_slot, float inv_sqrt_n, cudaStream_t s, int *rc)
+{
+    if (n_head_q > 8 || ((uintptr_t)packed & 15) || (packed_slot & 15) || getenv("SHANNON_PRIME_KQ_SIMT"))
+        return 0;
+    KqTcArgs a{packed, packed_slot, q, q_stride, q_slot, dst, dst_stride, dst_slot, n_kv, n_head_q, q_f16,
+               inv_sqrt_n};
+    const bool wide = n_head_q > 4;
+    auto k = wide ? k_kq_scores_tc<8> : k_kq_scores_tc<4>;
+    const size_t smem = sizeof(KqSmem);
+    constexpr int kMaxDev = 64;
+    static std::atomic<int> ready[kMaxDev][2];
+    static std::atomic<int> sms_tab[kMaxDev];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= kMaxDev) return 0;
+    if (!ready[dev][wide].load(std::memory_order_acquire)) {
+        if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+            *rc = sp_check_cuda(cudaGetLastError(), "kq_scores tcgen05 smem attribute");
+            return 1;
+        }
+        int sms = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        sms_tab[dev].store(sms > 0 ? sms : 148, std::memory_order_relaxed);
+        ready[dev][wide].store(1, std::memory_order_release);
+    }
+    const int sms = sms_tab[dev].load(std::memory_order_relaxed);
+    const int n_tiles = (n_kv + kTM - 1) / kTM;
+    // three resident CTAs per SM in total, each walking its slot's tiles
+    // (four measured 1.18 against 1.11 us per slot)
+    int gx = (3 * sms + n_slots - 1) / n_slots;
+    if (gx > n_tiles) gx = n_tiles;
+    if (gx < 1) gx = 1;
+    k<<<dim3((unsigned)gx, (unsigned)n_slots), kKqTcThreads, smem, s>>>(a);
+    *rc = sp_check_cuda(cudaGetLastError(), "kq_scores tcgen05 launch");
+    return 1;
 }

@@ -601,6 +601,11 @@ k_kq_scores_lane(const uint8_t *packed, int n_kv, const void *q, int q_f16, long
 
 }  // namespace
 
+// tcgen05 form for K rows (sp_attn_tc.cu): 1 and *rc set if it took the call.
+int sp_kq_scores_tc_try(const uint8_t *packed, long long packed_slot, int n_slots, int n_kv, const void *q,
+                        int q_f16, long long q_stride, long long q_slot, int n_head_q, float *dst,
+                        long long dst_stride, long long dst_slot, float inv_sqrt_n, cudaStream_t s, int *rc);
+
 extern "C" int sp_cuda_kq_scores_strided(const void *d_packed, long long packed_slot_stride, int n_slots,
                                          int total_bytes_per_pos, int is_v, int head_dim, int n_kv, const void *d_q,
                                          int q_dtype, long long q_row_stride, long long q_slot_stride, int n_head_q,
@@ -624,9 +629,14 @@ extern "C" int sp_cuda_kq_scores_strided(const void *d_packed, long long packed_
         (dst_row_stride & 3) || q_row_stride < (long long)es * head_dim || dst_row_stride < 4LL * n_kv ||
         (packed_slot_stride & 1) || (q_slot_stride % es) || (dst_slot_stride & 3))
         return sp_set_error(SP_ERR_ARG, "kq_scores: misaligned pointer or stride");
-    const dim3 grid((unsigned)((n_kv + kKqThreads - 1) / kKqThreads), (unsigned)n_slots);
     cudaStream_t s = (cudaStream_t)stream;
     const float isn = sp_inv_sqrt_n(kLN);
+    int rc = SP_OK;
+    if (!is_v && sp_kq_scores_tc_try((const uint8_t *)d_packed, packed_slot_stride, n_slots, n_kv, d_q,
+                                     q_dtype == SP_DTYPE_F16, q_row_stride, q_slot_stride, n_head_q, d_dst,
+                                     dst_row_stride, dst_slot_stride, isn, s, &rc))
+        return rc;
+    const dim3 grid((unsigned)((n_kv + kKqThreads - 1) / kKqThreads), (unsigned)n_slots);
     if (is_v)
         k_kq_scores_lane<false><<<grid, kKqThreads, 0, s>>>((const uint8_t *)d_packed, n_kv, d_q,
                                                             q_dtype == SP_DTYPE_F16, q_row_stride, n_head_q, d_dst,
