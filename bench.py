@@ -838,6 +838,9 @@ def main():
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="layers in the cache (profiling aid: a smaller case for ncu; "
                          "the headline number is the default, all 32)")
+    ap.add_argument("--attn-impl", type=int, default=0, choices=[0, 1, 2, 3],
+                    help="fused-decode kernel family (profiling aid: 0 automatic = 2, 1 generic SIMT, "
+                         "2 mma.sync, 3 tcgen05); the headline number is the default")
     args = ap.parse_args()
     N_LAYERS = args.layers
     if args.warmup < 3:
@@ -845,6 +848,9 @@ def main():
     if args.impl == "reference":
         run_reference(args)
     else:
+        if args.attn_impl:
+            import spb200
+            spb200.lib().sp_cuda_attn_force_impl(args.attn_impl)
         run_ours(args)
 
 
