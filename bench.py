@@ -237,24 +237,38 @@ def measure_sqfree(torch, dev, stream, steps: int, warmup: int, peak: float, sca
     }
     res["compress"]["frac"] = res["compress"]["achieved_gbs"] / peak
     res["decode"]["frac"] = res["decode"]["achieved_gbs"] / peak
-    # the reference-named read of one (layer, head) slot, K and V, fp32 rows out
+    # the read of layer 0, K and V, fp32 rows out: every KV head token-major in
+    # one sp_cuda_sqfree_read_kv_tokens launch per half; the reference-named
+    # per-slot batch read timed beside it
+    rd_all = torch.empty(1, T_, H_, hd, dtype=torch.float32, device=dev)
     rd = torch.empty(T_, hd, dtype=torch.float32, device=dev)
+
     def read_all():
+        for which in (0, 1):
+            cache.read_kv_tokens(which, 0, 1, 0, rd_all)
+
+    def read_per_slot():
         for which in (0, 1):
             for h in range(H_):
                 cache.read_batch(which, 0, h, 0, rd)
-    read_all()
-    torch.cuda.synchronize()
-    e0.record(stream)
-    for _ in range(3):
-        read_all()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    r_ms = e0.elapsed_time(e1) / (3 * 2 * H_)
+
+    def time_read(fn):
+        fn()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(3):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / (3 * 2 * H_)
+    r_ms = time_read(read_all)
+    r_ms_one = time_read(read_per_slot)
     r_bytes = T_ * (cache.cc.bytes_per_pos_k + hd * 4)
     res["read"] = {"value": r_bytes / (r_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_slot": r_ms,
                    "frac": r_bytes / (r_ms * 1e-3) / 1e9 / peak,
-                   "workload": "layer 0, 8 KV heads x K and V, 16384 positions per call, fp32 [pos][128] out"}
+                   "per_slot_call_gbs": r_bytes / (r_ms_one * 1e-3) / 1e9,
+                   "workload": "layer 0, %d KV heads x K and V, %d positions, all heads per "
+                               "sp_cuda_sqfree_read_kv_tokens launch, fp32 [pos][head][128] out" % (H_, T_)}
     cache.free()
     return res
 

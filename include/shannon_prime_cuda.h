@@ -305,6 +305,16 @@ void sp_cuda_sqfree_read_k_batch(const sp_cuda_sqfree_cache_t *cc, int layer, in
                                  int start_pos, int n_pos, float *d_k_out);
 void sp_cuda_sqfree_read_v_batch(const sp_cuda_sqfree_cache_t *cc, int layer, int head,
                                  int start_pos, int n_pos, float *d_v_out);
+
+/* New: token-major read of every KV head of a layer range in one launch
+ * (which 0 = K, 1 = V): positions [start_pos, start_pos + n_tok) of layers
+ * [layer0, layer0 + n_layers) to d_out as fp32
+ * [n_layers][n_tok][n_heads_kv][head_dim], rows equal to those of the
+ * per-slot batch reads.  The head_dim-128 spinor layout with 3-bit
+ * residuals (pad 154, skeleton in 5 bands) and a 16-byte aligned d_out;
+ * other caches return SP_ERR_UNSUPPORTED.  Allocates nothing. */
+int  sp_cuda_sqfree_read_kv_tokens(const sp_cuda_sqfree_cache_t *cc, int which, int layer0,
+                                   int n_layers, int start_pos, int n_tok, float *d_out);
 /* New: token-major write of every head of layers [layer0, layer0+n_layers):
  * d_k / d_v are [n_layers][n_tokens][n_heads_kv][head_dim] (NULL skips). */
 int  sp_cuda_sqfree_write_kv_tokens(sp_cuda_sqfree_cache_t *cc, int layer0, int n_layers,

@@ -2081,8 +2081,16 @@ struct SlReadSmem {
     uint32_t rows[kSlWarps][32 * 25];               // 32 slots of 100 bytes
 };
 
+// Slots a lane read covers: n_layers x n_heads slots, slot (l, h) at
+// slab + (slot0 + l * n_heads + h) * slot_stride + pos0 * bytes_per_pos; its
+// rows go to the output tensor at coordinates (h * hd, t, l).
+struct SlGrid {
+    long long slot_stride, slot0;
+    int n_heads, n_layers, pos0;
+};
+
 __global__ void __launch_bounds__(kSlWarps * 32, 2)
-k_sq_decode_lane(const uint8_t *slab, int n_pos, unsigned int *status, const __grid_constant__ SlOutMap map)
+k_sq_decode_lane(const uint8_t *slab, SlGrid g, int n_pos, unsigned int *status, const __grid_constant__ SlOutMap map)
 {
     constexpr int NR = kSlNRes, TW = kSlBytes / 4;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -2093,11 +2101,15 @@ k_sq_decode_lane(const uint8_t *slab, int n_pos, unsigned int *status, const __g
         if (threadIdx.x == 0 && status) atomicOr(status, 4u);
         return;
     }
-    const int n_b = (n_pos + 31) >> 5;
-    for (int bt = blockIdx.x * kSlWarps + warp; bt < n_b; bt += gridDim.x * kSlWarps) {
-        const int t0 = bt * 32, live = min(32, n_pos - t0);
+    const int n_bs = (n_pos + 31) >> 5;                 // batches per slot
+    const long long n_b = (long long)n_bs * g.n_heads * g.n_layers;
+    for (long long bt = (long long)blockIdx.x * kSlWarps + warp; bt < n_b; bt += (long long)gridDim.x * kSlWarps) {
+        const int sl = (int)(bt / n_bs);
+        const int t0 = (int)(bt - (long long)sl * n_bs) * 32, live = min(32, n_pos - t0);
+        const int l = sl / g.n_heads, hh = sl - l * g.n_heads;
         uint32_t *rows = sm.rows[warp];
-        const uint32_t *src = reinterpret_cast<const uint32_t *>(slab + (long long)t0 * kSlBytes);
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(
+            slab + (g.slot0 + sl) * g.slot_stride + (long long)(g.pos0 + t0) * kSlBytes);
         for (int i = lane; i < live * TW; i += 32) rows[i] = src[i];
         __syncwarp();
         const uint32_t *rw = rows + lane * TW;
@@ -2155,9 +2167,9 @@ k_sq_decode_lane(const uint8_t *slab, int n_pos, unsigned int *status, const __g
         if (lane == 0) {
 #pragma unroll
             for (int q = 0; q < 4; q++)
-                asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
                                  &map.m),
-                             "r"(q * 32), "r"(t0), "r"(out0 + q * 4096)
+                             "r"(hh * kSlHD + q * 32), "r"(t0), "r"(l), "r"(out0 + q * 4096)
                              : "memory");
             asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         }
@@ -4189,6 +4201,56 @@ static int sq_write(sp_cuda_sqfree_cache_t *cc, int which, int layer0, int n_lay
     return sq_launch_encode(t, io, dtype, (cudaStream_t)cc->stream, sq_status(cc));
 }
 
+// The lane read of the config-2 slot over a grid of slots; d_out is
+// [n_layers][n_pos][n_heads][128] fp32 (one slot: [n_pos][128]).  Returns 1
+// when the driver has no tensor-map encoder (the caller takes another path),
+// -1 on a launch error, 0 when launched.
+static int sq_read_lane(const uint8_t *slab, const SlGrid &g, int n_pos, float *d_out, unsigned int *status,
+                        cudaStream_t s)
+{
+    auto fn = sq_encode_fn();
+    if (!fn) return 1;
+    SlOutMap map;
+    memset(&map, 0, sizeof(map));
+    const cuuint64_t row = (cuuint64_t)kSlHD * g.n_heads;
+    const cuuint64_t dims[3] = {row, (cuuint64_t)n_pos, (cuuint64_t)g.n_layers};
+    const cuuint64_t strides[2] = {row * 4, row * 4 * (cuuint64_t)n_pos};
+    const cuuint32_t box[3] = {32, 32, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (fn(&map.m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, d_out, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+        return 1;
+    const size_t smem = sizeof(SlReadSmem);
+    // Per device: attribute set and occupancy looked up once (atomics, so
+    // host threads driving any devices race harmlessly).
+    constexpr int kMaxDev = 64;
+    static std::atomic<int> occ_tab[kMaxDev], sms_tab[kMaxDev];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= kMaxDev) return -1;
+    int occ = occ_tab[dev].load(std::memory_order_acquire);
+    if (occ == 0) {
+        if (cudaFuncSetAttribute(k_sq_decode_lane, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess) {
+            sp_check_cuda(cudaGetLastError(), "sqfree lane read smem attribute");
+            return -1;
+        }
+        int o = 0, sms = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k_sq_decode_lane, kSlWarps * 32, smem);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        sms_tab[dev].store(sms > 0 ? sms : 148, std::memory_order_relaxed);
+        occ = o > 0 ? o : 1;
+        occ_tab[dev].store(occ, std::memory_order_release);
+    }
+    const int sms = sms_tab[dev].load(std::memory_order_relaxed);
+    const long long n_b = (long long)((n_pos + 31) / 32) * g.n_heads * g.n_layers;
+    long long blocks = (n_b + kSlWarps - 1) / kSlWarps;
+    if (blocks > (long long)sms * occ) blocks = (long long)sms * occ;
+    k_sq_decode_lane<<<(unsigned)blocks, kSlWarps * 32, smem, s>>>(slab, g, n_pos, status, map);
+    return sp_check_cuda(cudaGetLastError(), "sqfree lane read launch") ? -1 : 0;
+}
+
 static int sq_read(const sp_cuda_sqfree_cache_t *cc, int which, int layer, int head, int start_pos, int n_pos,
                    float *d_out)
 {
@@ -4209,37 +4271,10 @@ static int sq_read(const sp_cuda_sqfree_cache_t *cc, int which, int layer, int h
     io.single_slot = 1;
     if (sq_lane_fits(t, io) && !getenv("SHANNON_PRIME_SQFREE_DECODE_WARP") && !((uintptr_t)d_out & 15) &&
         !(((uintptr_t)io.cache + (uintptr_t)start_pos * t.bytes_per_pos) & 3)) {
-        auto fn = sq_encode_fn();
-        SlOutMap map;
-        memset(&map, 0, sizeof(map));
-        const cuuint64_t dims[2] = {(cuuint64_t)kSlHD, (cuuint64_t)n_pos};
-        const cuuint64_t strides[1] = {(cuuint64_t)kSlHD * 4};
-        const cuuint32_t box[2] = {32, 32};
-        const cuuint32_t estr[2] = {1, 1};
-        if (fn && fn(&map.m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, d_out, dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
-            const size_t smem = sizeof(SlReadSmem);
-            static int occ = 0, sms = 0, dev_done = -1;
-            int dev = 0;
-            cudaGetDevice(&dev);
-            if (dev != dev_done) {
-                if (cudaFuncSetAttribute(k_sq_decode_lane, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-                    cudaSuccess)
-                    return sp_check_cuda(cudaGetLastError(), "sqfree lane read smem attribute");
-                cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_sq_decode_lane, kSlWarps * 32, smem);
-                cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-                if (occ < 1) occ = 1;
-                if (sms < 1) sms = 148;
-                dev_done = dev;
-            }
-            const long long n_b = (n_pos + 31) / 32;
-            long long blocks = (n_b + kSlWarps - 1) / kSlWarps;
-            if (blocks > (long long)sms * occ) blocks = (long long)sms * occ;
-            k_sq_decode_lane<<<(unsigned)blocks, kSlWarps * 32, smem, (cudaStream_t)cc->stream>>>(
-                io.cache + (long long)start_pos * t.bytes_per_pos, n_pos, sq_status(cc), map);
-            return sp_check_cuda(cudaGetLastError(), "sqfree lane read launch");
-        }
+        const SlGrid g{0, 0, 1, 1, 0};
+        const int r = sq_read_lane(io.cache + (long long)start_pos * t.bytes_per_pos, g, n_pos, d_out, sq_status(cc),
+                                   (cudaStream_t)cc->stream);
+        if (r <= 0) return r ? sp_set_error(SP_ERR_CUDA, "sqfree lane read failed") : SP_OK;
     }
     return sq_launch_decode(t, io, (cudaStream_t)cc->stream);
 }
@@ -4688,3 +4723,32 @@ void sp_cuda_hier_read_v(const sp_cuda_hier_cache_t *hc, int layer, int head, in
 { hier_one((sp_cuda_hier_cache_t *)hc, 1, layer, head, pos, nullptr, d_v_out); }
 
 }  // extern "C"
+
+// Token-major read of every KV head of a layer range in one launch (the
+// per-head read loop of a cache's read_gpu), config-2 slot layout only:
+// which 0 = K, 1 = V; d_out [n_layers][n_tok][n_heads_kv][head_dim] fp32.
+int sp_cuda_sqfree_read_kv_tokens(const sp_cuda_sqfree_cache_t *cc, int which, int layer0, int n_layers,
+                                  int start_pos, int n_tok, float *d_out)
+{
+    sp_clear_error();
+    if (!cc || !d_out || (which != 0 && which != 1))
+        return sp_set_error(SP_ERR_ARG, "sqfree read_kv_tokens: bad arguments");
+    if (n_layers == 0 || n_tok == 0) return SP_OK;
+    int rc = sq_check(cc, layer0, n_layers, 0, start_pos, n_tok);
+    if (rc) return rc;
+    if (cudaSetDevice(cc->device) != cudaSuccess) return sp_set_error(SP_ERR_CUDA, "sqfree read_kv_tokens: cudaSetDevice");
+    const SpSqDev t = sq_desc(cc, which);
+    SqIo io;
+    memset(&io, 0, sizeof(io));
+    io.slot_stride = (long long)cc->max_seq_len * t.bytes_per_pos;
+    io.cache = (uint8_t *)(which ? cc->d_v_cache : cc->d_k_cache);
+    const int H = cc->config.n_heads_kv;
+    if (!sq_lane_fits(t, io) || ((uintptr_t)d_out & 15) || (((uintptr_t)start_pos * t.bytes_per_pos) & 3))
+        return sp_set_error(SP_ERR_UNSUPPORTED, "sqfree read_kv_tokens: the head_dim-128 spinor layout "
+                                                "(pad 154, 5 skeleton bands, 3-bit residuals) with a 16-byte "
+                                                "aligned output");
+    const SlGrid g{io.slot_stride, (long long)layer0 * H, H, n_layers, start_pos};
+    const int r = sq_read_lane(io.cache, g, n_tok, d_out, sq_status(cc), (cudaStream_t)cc->stream);
+    if (r > 0) return sp_set_error(SP_ERR_UNSUPPORTED, "sqfree read_kv_tokens: no tensor-map encoder in this driver");
+    return r ? sp_set_error(SP_ERR_CUDA, "sqfree read_kv_tokens: launch failed") : SP_OK;
+}

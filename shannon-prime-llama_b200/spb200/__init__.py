@@ -170,6 +170,7 @@ SIGNATURES = {
     "sp_cuda_sqfree_read_k": (_V, [C.POINTER(SpSqfreeCache), _I, _I, _I, _P]),
     "sp_cuda_sqfree_read_v": (_V, [C.POINTER(SpSqfreeCache), _I, _I, _I, _P]),
     "sp_cuda_sqfree_read_k_batch": (_V, [C.POINTER(SpSqfreeCache), _I, _I, _I, _I, _P]),
+    "sp_cuda_sqfree_read_kv_tokens": (_I, [C.POINTER(SpSqfreeCache), _I, _I, _I, _I, _I, _P]),
     "sp_cuda_sqfree_read_v_batch": (_V, [C.POINTER(SpSqfreeCache), _I, _I, _I, _I, _P]),
     "sp_cuda_sqfree_write_kv_tokens": (_I, [C.POINTER(SpSqfreeCache), _I, _I, _I, _I, _P, _P, _I]),
     "sp_cuda_sqfree_attn_decode": (_I, [C.POINTER(SpSqfreeCache), _I, _I, _P, _I, _I, _F, _P, _P]),

@@ -62,6 +62,12 @@ class SqfreeCache:
         f(C.byref(self.cc), layer, head, start_pos, out.shape[0], out.data_ptr())
         check(None, "sp_cuda_sqfree_read_batch")
 
+    def read_kv_tokens(self, which: int, layer0: int, n_layers: int, start_pos: int, out) -> None:
+        """out: fp32 CUDA tensor [n_layers][n_tok][n_heads_kv][head_dim]."""
+        rc = lib().sp_cuda_sqfree_read_kv_tokens(C.byref(self.cc), which, layer0, n_layers, start_pos,
+                                                 out.shape[1], out.data_ptr())
+        check(rc, "sp_cuda_sqfree_read_kv_tokens")
+
     def attn_decode(self, layer0: int, n_layers: int, q, kv_len: int, out,
                     logit_scale: float = 1.0, stream=None) -> None:
         rc = lib().sp_cuda_sqfree_attn_decode(C.byref(self.cc), layer0, n_layers, q.data_ptr(),

@@ -267,6 +267,30 @@ def test_sqfree_lane_read_matches_warp_read(cuda, monkeypatch, start, T):
         np.testing.assert_array_equal(outs[0], O.sqfree_read(slab, OL))
 
 
+@pytest.mark.parametrize("layer0,nl,start,T", [(0, 2, 0, 300), (1, 1, 5, 77)])
+def test_sqfree_read_kv_tokens_matches_per_slot_reads(cuda, layer0, nl, start, T):
+    """The token-major all-heads sqfree read (one launch over a layer range)
+    puts every slot's rows at [layer][token][head], bit-identical with the
+    per-slot batch read."""
+    import torch
+    L, H, hd = 2, 3, 128
+    k, v = _inputs(11, L, H, 320, hd, sigma=1.0)
+    cache = SqfreeCache(hd, L, H, 320, sk_frac=0.75)
+    cache.write_kv_tokens(0, 0, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda())
+    torch.cuda.synchronize()
+    for which in (0, 1):
+        got = torch.full((nl, T, H, hd), 5.0, device="cuda")
+        cache.read_kv_tokens(which, layer0, nl, start, got)
+        ref = torch.full((nl, T, H, hd), 6.0, device="cuda")
+        for l in range(nl):
+            for h in range(H):
+                one = torch.empty(T, hd, device="cuda")
+                cache.read_batch(which, layer0 + l, h, start, one)
+                ref[l, :, h] = one
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref), which
+
+
 @pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])
 @pytest.mark.parametrize("start,T", [(0, 300), (5, 77), (13, 1)])
 def test_hier_lane_and_warp_encoders_agree(cuda, dtype, start, T, monkeypatch):
