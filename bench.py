@@ -817,6 +817,15 @@ def run_ours(args):
     }
     if gather_check is not None:
         line["gather_check"] = gather_check
+    # Everything of a step after the main kernel: the segment combine with its
+    # inverse VHT2 and, at N > 1, the NVLink peer stores of the gathered rows
+    # and the flag wait (step time minus the main kernel's event-timed
+    # duration, max over ranks for both).
+    tail_us = max(0.0, ms - kernel_ms) * 1e3
+    line["gather_latency"] = {"per_step_us": tail_us, "per_layer_us": tail_us / N_LAYERS,
+                              "what": ("combine + peer-store all-gather + flag wait" if ws > 1 else
+                                       "combine (no gather at N = 1)") +
+                                      ": step time minus the main kernel's event-timed duration"}
     if cpu is not None:
         line["cpu_baseline"] = cpu
     if not args.no_extra:
