@@ -2225,16 +2225,69 @@ __host__ __device__ constexpr SaTerms sa_terms()
 }
 constexpr SaTerms kSaTerms = sa_terms();
 
-// Pad index of coefficient j of the slot order.
-__host__ __device__ constexpr int sa_pd_of(int j)
+// Row order of the lane decode's coefficient tile.  Skeleton slots that no
+// Möbius term names are dequantised two per instruction in fp16x2
+// arithmetic from a masked window of the row words (the fp32 path's value
+// rounded to fp16, exactly); they take the first row positions, in pairs of
+// one band whose codes fit the two halves of one 32-bit window.  The slots
+// the predictions need follow in slot order on the fp32 path, then the
+// residuals, then zero columns up to 160.
+constexpr int kSaMaxPairs = 64;
+struct SaPlan {
+    int n_pairs, n_f32;
+    int lo[kSaMaxPairs], hi[kSaMaxPairs];     // skeleton slot in the low / high half
+    int win[kSaMaxPairs];                     // row bit where the pair's window starts
+    int dlo[kSaMaxPairs], dhi[kSaMaxPairs];   // bit of each code inside its half
+    int f32[kSlSK];                           // skeleton slots on the fp32 path, ascending
+    int row[kSlPD];                           // row position of slot s (< kSlSK) or residual s - kSlSK
+    int pd[160];                              // pad index at a row position, -1 for zero columns
+};
+__host__ __device__ constexpr SaPlan sa_plan()
 {
-    return j < kSlSK ? kSlTab.skel[j] : kSlTab.res[j - kSlSK];
+    SaPlan p{};
+    bool named[kSlSK] = {}, used[kSlSK] = {};
+    for (int k = 0; k < kSlNT; k++) named[kSlTab.term[k] >> 1] = true;
+    constexpr int BS = kSlSK / 5;
+    for (int b = 0; b < 5; b++) {
+        const int bits = sl_bits(b), n_b = b == 4 ? kSlSK - 4 * BS : BS;
+        for (int i = 0; i < n_b; i++) {
+            const int s = b * BS + i;
+            if (named[s] || used[s]) continue;
+            for (int dl = 3; dl <= 5; dl++) {
+                const int t = s + dl, D = dl * bits;
+                if (i + dl >= n_b || named[t] || used[t]) continue;
+                const int d1 = D < 16 ? 16 - D : 0, d2 = d1 + D - 16;
+                if (d1 + bits > 10 || d2 + bits > 10) continue;
+                const int k = p.n_pairs++;
+                p.lo[k] = s;
+                p.hi[k] = t;
+                p.win[k] = 8 * (sl_band_byte(b) + 2) + i * bits - d1;
+                p.dlo[k] = d1;
+                p.dhi[k] = d2;
+                used[s] = used[t] = true;
+                break;
+            }
+        }
+    }
+    for (int s = 0; s < kSlSK; s++)
+        if (!used[s]) p.f32[p.n_f32++] = s;
+    for (int k = 0; k < p.n_pairs; k++) { p.row[p.lo[k]] = 2 * k; p.row[p.hi[k]] = 2 * k + 1; }
+    for (int k = 0; k < p.n_f32; k++) p.row[p.f32[k]] = 2 * p.n_pairs + k;
+    for (int r = 0; r < kSlNRes; r++) p.row[kSlSK + r] = 2 * p.n_pairs + p.n_f32 + r;
+    for (int j = 0; j < 160; j++) p.pd[j] = -1;
+    for (int s = 0; s < kSlPD; s++) p.pd[p.row[s]] = s < kSlSK ? kSlTab.skel[s] : kSlTab.res[s - kSlSK];
+    return p;
 }
+constexpr SaPlan kSaPlan = sa_plan();
+static_assert(kSaPlan.n_pairs <= kSaMaxPairs && 2 * kSaPlan.n_pairs + kSaPlan.n_f32 == kSlSK, "row plan");
+
+// Row position of pad index i.
 struct SaPdIdx { int v[kSlPD]; };
 __host__ __device__ constexpr SaPdIdx sa_pd_idx()
 {
     SaPdIdx x{};
-    for (int j = 0; j < kSlPD; j++) x.v[sa_pd_of(j)] = j;     // slot-order index of pad index i
+    for (int j = 0; j < 160; j++)
+        if (kSaPlan.pd[j] >= 0) x.v[kSaPlan.pd[j]] = j;
     return x;
 }
 __constant__ SaPdIdx c_sa_j_of = sa_pd_idx();
@@ -2286,36 +2339,6 @@ __device__ __forceinline__ uint32_t sa_h2(float lo, float hi)
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-template <int S>
-__device__ __forceinline__ float sa_skel_or0(const uint32_t (&w)[26], const float (&scl)[5])
-{
-    if constexpr (S < kSlSK) return sa_skel<S>(w, scl);
-    else return 0.0f;
-}
-template <int G, size_t... I>
-__device__ __forceinline__ void sa_group_vals(const uint32_t (&w)[26], const float (&scl)[5], float (&pr)[kSlNRes],
-                                              float (&v)[8], std::index_sequence<I...>)
-{
-    ((v[I] = sa_skel_or0<8 * G + (int)I>(w, scl)), ...);
-    (sa_terms_of<8 * G + (int)I, kSaTerms.grp[G], kSaTerms.grp[G + 1]>(pr, v[I]), ...);
-}
-// Skeleton group G (slots 8G..8G+7): values, their Möbius terms, and (for a
-// group of skeleton slots only) one 16-byte store of the fp16 row; the
-// values of the last, partial group are returned in v.
-template <int G>
-__device__ __forceinline__ void sa_group(const uint32_t (&w)[26], const float (&scl)[5], float (&pr)[kSlNRes],
-                                         uint32_t row, float (&v)[8])
-{
-    sa_group_vals<G>(w, scl, pr, v, std::make_index_sequence<8>{});
-    if constexpr (8 * G + 8 <= kSlSK)
-        sa_st4(row + 16 * G, sa_h2(v[0], v[1]), sa_h2(v[2], v[3]), sa_h2(v[4], v[5]), sa_h2(v[6], v[7]));
-}
-template <size_t... G>
-__device__ __forceinline__ void sa_groups(const uint32_t (&w)[26], const float (&scl)[5], float (&pr)[kSlNRes],
-                                          uint32_t row, float (&v)[8], std::index_sequence<G...>)
-{
-    (sa_group<(int)G>(w, scl, pr, row, v), ...);
-}
 template <int B>
 __device__ __forceinline__ float sa_scale(const uint32_t (&w)[26])
 {
@@ -2343,32 +2366,139 @@ __device__ __forceinline__ void sa_residuals(const uint32_t (&w)[26], const floa
     ((c[R] = sa_res<(int)R>(w, pr, step, nc)), ...);
 }
 
+// fp16 bits of a value fp16 holds exactly in its normal range (the
+// constants of the paired dequantisation).
+__host__ __device__ constexpr uint32_t sa_f16_bits(double x)
+{
+    const uint32_t sign = x < 0 ? 0x8000u : 0u;
+    double a = x < 0 ? -x : x;
+    int e = 0;
+    while (a >= 2.0) { a /= 2.0; e++; }
+    while (a < 1.0) { a *= 2.0; e--; }
+    return sign | ((uint32_t)(e + 15) << 10) | (uint32_t)((a - 1.0) * 1024.0);
+}
+__host__ __device__ constexpr double sa_pow2(int e)
+{
+    double x = 1.0;
+    for (; e > 0; e--) x *= 2.0;
+    for (; e < 0; e++) x *= 0.5;
+    return x;
+}
+// Band scale B as fp16x2 (both halves), zero if not finite.
+template <int B>
+__device__ __forceinline__ uint32_t sa_scale_h2(const uint32_t (&w)[26])
+{
+    const uint32_t h = sa_bits<8 * sl_band_byte(B), 16>(w);
+    const uint32_t f = (h & 0x7C00u) == 0x7C00u ? 0u : h;
+    return f | (f << 16);
+}
+// Pair K as one fp16x2 word: the window's two codes masked into halves
+// 1024 + u * 2^d, one fma to (u - m) * 2^-4 (exact), one multiply by the
+// band scale (the single rounding of the exact product, as the fp32 path's
+// conversion).
+template <int K>
+__device__ __forceinline__ uint32_t sa_pair(const uint32_t (&w)[26], const uint32_t (&sb)[5])
+{
+    constexpr int b = kSaPlan.lo[K] / (kSlSK / 5), bits = sl_bits(b), mv = (1 << (bits - 1)) - 1;
+    constexpr int W = kSaPlan.win[K], i = W >> 5, s = W & 31, d1 = kSaPlan.dlo[K], d2 = kSaPlan.dhi[K];
+    constexpr uint32_t m = (1u << bits) - 1u;
+    constexpr uint32_t mask = (m << d1) | (m << (16 + d2));
+    constexpr uint32_t kk = sa_f16_bits(sa_pow2(-4 - d1)) | (sa_f16_bits(sa_pow2(-4 - d2)) << 16);
+    constexpr uint32_t cc = sa_f16_bits(-(1024.0 + mv * sa_pow2(d1)) * sa_pow2(-4 - d1)) |
+                            (sa_f16_bits(-(1024.0 + mv * sa_pow2(d2)) * sa_pow2(-4 - d2)) << 16);
+    uint32_t win;
+    if constexpr (s == 0) win = w[i];
+    else win = __funnelshift_r(w[i], w[i + 1], s);
+    const uint32_t x = (win & mask) | 0x64006400u;
+    const __half2 v = __hfma2(*reinterpret_cast<const __half2 *>(&x), *reinterpret_cast<const __half2 *>(&kk),
+                              *reinterpret_cast<const __half2 *>(&cc));
+    const __half2 r = __hmul2_rn(v, *reinterpret_cast<const __half2 *>(&sb[b]));
+    return *reinterpret_cast<const uint32_t *>(&r);
+}
+
+// What row position J holds: 0 pair, 1 fp32 skeleton slot, 2 residual, 3 zero.
+__host__ __device__ constexpr int sa_kind(int j)
+{
+    return j < 2 * kSaPlan.n_pairs ? 0 : j < kSlSK ? 1 : j < kSlPD ? 2 : 3;
+}
+// Phase after which group G (row positions 8G..8G+7) is complete: 0 after
+// the pairs, 1 + k after fp32 slot k, 1 + n_f32 after the residuals.
+__host__ __device__ constexpr int sa_group_stage(int g)
+{
+    int st = 0;
+    for (int j = 8 * g; j < 8 * g + 8; j++) {
+        const int k = sa_kind(j);
+        const int sj = k == 1 ? 1 + (j - 2 * kSaPlan.n_pairs) : k == 2 ? 1 + kSaPlan.n_f32 : 0;
+        st = sj > st ? sj : st;
+    }
+    return st;
+}
+struct SaRowVals {
+    float fv[kSlSK];      // fp32 skeleton values, by fp32-path index
+    float rv[kSlNRes];    // residual coefficients
+};
+template <int J>
+__device__ __forceinline__ float sa_val(const SaRowVals &v)
+{
+    constexpr int k = sa_kind(J);
+    if constexpr (k == 1) return v.fv[J - 2 * kSaPlan.n_pairs];
+    else if constexpr (k == 2) return v.rv[J - kSlSK];
+    else return 0.0f;
+}
+template <int Wd>
+__device__ __forceinline__ uint32_t sa_word(const uint32_t (&w)[26], const uint32_t (&sb)[5], const SaRowVals &v)
+{
+    if constexpr (2 * Wd + 1 < 2 * kSaPlan.n_pairs) return sa_pair<Wd>(w, sb);
+    else return sa_h2(sa_val<2 * Wd>(v), sa_val<2 * Wd + 1>(v));
+}
+template <int ST, size_t... G>
+__device__ __forceinline__ void sa_store_stage(const uint32_t (&w)[26], const uint32_t (&sb)[5], const SaRowVals &v,
+                                               uint32_t row, std::index_sequence<G...>)
+{
+    ((sa_group_stage((int)G) == ST
+          ? sa_st4(row + 16 * (int)G, sa_word<4 * (int)G>(w, sb, v), sa_word<4 * (int)G + 1>(w, sb, v),
+                   sa_word<4 * (int)G + 2>(w, sb, v), sa_word<4 * (int)G + 3>(w, sb, v))
+          : (void)0),
+     ...);
+}
+template <int K>
+__device__ __forceinline__ void sa_f32_slot(const uint32_t (&w)[26], const float (&scl)[5], const uint32_t (&sb)[5],
+                                            float (&pr)[kSlNRes], SaRowVals &v, uint32_t row)
+{
+    constexpr int S = kSaPlan.f32[K];
+    v.fv[K] = sa_skel<S>(w, scl);
+    sa_terms_of<S, kSaTerms.grp[S >> 3], kSaTerms.grp[(S >> 3) + 1]>(pr, v.fv[K]);
+    sa_store_stage<1 + K>(w, sb, v, row, std::make_index_sequence<20>{});
+}
+template <size_t... K>
+__device__ __forceinline__ void sa_f32_slots(const uint32_t (&w)[26], const float (&scl)[5], const uint32_t (&sb)[5],
+                                             float (&pr)[kSlNRes], SaRowVals &v, uint32_t row, std::index_sequence<K...>)
+{
+    (sa_f32_slot<(int)K>(w, scl, sb, pr, v, row), ...);
+}
+
 // One slot (row words in w, w[25] zero) to its fp16 staging row (shared-
-// memory address row): 160 halves, coefficients times 2^-4 in slot order.
+// memory address row): 160 halves, coefficients times 2^-4 in row order
+// (kSaPlan).  Predictions accumulate term by term in slot order, as the
+// other decoders do.
 __device__ __forceinline__ void sa_slot_row(const uint32_t (&w)[26], uint32_t row)
 {
-    constexpr int NG = (kSlSK + 7) / 8;           // 15 groups; the last holds slots 112..114
-    constexpr int J0 = 8 * (NG - 1);
-    static_assert(kSlSK - J0 + kSlNRes <= 48 && J0 + 48 == 160, "tail of 48 halves");
+    uint32_t sb[5] = {sa_scale_h2<0>(w), sa_scale_h2<1>(w), sa_scale_h2<2>(w), sa_scale_h2<3>(w),
+                      sa_scale_h2<4>(w)};
+    SaRowVals v;
+    sa_store_stage<0>(w, sb, v, row, std::make_index_sequence<20>{});
     float scl[5];
     sa_scales(w, scl, std::make_index_sequence<5>{});
     float pr[kSlNRes];
 #pragma unroll
     for (int r = 0; r < kSlNRes; r++) pr[r] = 0.0f;
-    float v[8];
-    sa_groups(w, scl, pr, row, v, std::make_index_sequence<NG>{});
+    sa_f32_slots(w, scl, sb, pr, v, row, std::make_index_sequence<kSaPlan.n_f32>{});
     constexpr int L = 1 << kSlNR;
     const float mag = __uint_as_float(sa_bits<8 * kSlMagOff, 32>(w));
     const float step = __fmul_rn(__fdiv_rn(__fmul_rn(2.0f, __fmul_rn(mag, (float)kSlNR)), (float)(L - 1)), 0.0625f);
     const float nc = -0.5f * (float)(L - 1) * step;
-    float c[48];
-#pragma unroll
-    for (int j = 0; j < 48; j++) c[j] = j < kSlSK - J0 ? v[j < 8 ? j : 0] : 0.0f;
-    sa_residuals(w, pr, step, nc, c + (kSlSK - J0), std::make_index_sequence<kSlNRes>{});
-#pragma unroll
-    for (int g = 0; g < 6; g++)
-        sa_st4(row + 2 * J0 + 16 * g, sa_h2(c[8 * g], c[8 * g + 1]), sa_h2(c[8 * g + 2], c[8 * g + 3]),
-               sa_h2(c[8 * g + 4], c[8 * g + 5]), sa_h2(c[8 * g + 6], c[8 * g + 7]));
+    sa_residuals(w, pr, step, nc, v.rv, std::make_index_sequence<kSlNRes>{});
+    sa_store_stage<1 + kSaPlan.n_f32>(w, sb, v, row, std::make_index_sequence<20>{});
 }
 
 __device__ __forceinline__ void sa_ldsm4(uint32_t addr, uint32_t (&r)[4])
@@ -2418,7 +2548,7 @@ struct SaPdOf { int v[160]; };
 __host__ __device__ constexpr SaPdOf sa_pd_of_tab()
 {
     SaPdOf x{};
-    for (int j = 0; j < 160; j++) x.v[j] = j < kSlPD ? sa_pd_of(j) : -1;
+    for (int j = 0; j < 160; j++) x.v[j] = kSaPlan.pd[j];
     return x;
 }
 __constant__ SaPdOf c_sa_pd_of = sa_pd_of_tab();
