@@ -2359,12 +2359,6 @@ __device__ __forceinline__ float sa_res(const uint32_t (&w)[26], const float (&p
     const uint32_t sgn = sa_bits<8 * kSlSheetOff + R, 1>(w) << 31;
     return __fadd_rn(__uint_as_float(__float_as_uint(pr[R]) ^ sgn), dev);
 }
-template <size_t... R>
-__device__ __forceinline__ void sa_residuals(const uint32_t (&w)[26], const float (&pr)[kSlNRes], float step,
-                                             float nc, float *c, std::index_sequence<R...>)
-{
-    ((c[R] = sa_res<(int)R>(w, pr, step, nc)), ...);
-}
 
 // fp16 bits of a value fp16 holds exactly in its normal range (the
 // constants of the paired dequantisation).
@@ -2477,6 +2471,111 @@ __device__ __forceinline__ void sa_f32_slots(const uint32_t (&w)[26], const floa
     (sa_f32_slot<(int)K>(w, scl, sb, pr, v, row), ...);
 }
 
+// Residual levels in pairs (r, r + 3..7) whose 3-bit codes fit the two
+// halves of one 32-bit window: one fma turns both into lv - center exactly
+// (fp16x2), and each residual is then one fp32 fma with the step onto its
+// signed prediction.  An odd one left over takes sa_res.
+struct SaResPlan {
+    int n_pairs, n_left;
+    int lo[kSlNRes], hi[kSlNRes], win[kSlNRes], dlo[kSlNRes], dhi[kSlNRes];
+    int left[kSlNRes];
+};
+__host__ __device__ constexpr SaResPlan sa_res_plan()
+{
+    SaResPlan p{};
+    bool used[kSlNRes] = {};
+    for (int r = 0; r < kSlNRes; r++) {
+        if (used[r]) continue;
+        for (int dl = 5; dl <= 7; dl++) {
+            const int t = r + dl, D = dl * kSlNR;
+            if (t >= kSlNRes || used[t]) continue;
+            // d >= 1 keeps 1024 + center * 2^d an fp16 integer
+            const int d1 = D < 17 ? 17 - D : 1, d2 = d1 + D - 16;
+            if (d1 + kSlNR > 10 || d2 + kSlNR > 10) continue;
+            const int k = p.n_pairs++;
+            p.lo[k] = r;
+            p.hi[k] = t;
+            p.win[k] = 8 * kSlResOff + r * kSlNR - d1;
+            p.dlo[k] = d1;
+            p.dhi[k] = d2;
+            used[r] = used[t] = true;
+            break;
+        }
+    }
+    for (int r = 0; r < kSlNRes; r++)
+        if (!used[r]) p.left[p.n_left++] = r;
+    return p;
+}
+constexpr SaResPlan kSaResPlan = sa_res_plan();
+__host__ __device__ constexpr int sa_left_res(int k) { return kSaResPlan.left[k]; }
+
+// Every fp16x2 constant of both pair plans is exact in fp16 (checked at
+// compile time: the paired dequantisation relies on it).
+__host__ __device__ constexpr bool sa_f16_exact(double x)
+{
+    double a = x < 0 ? -x : x;
+    int e = 0;
+    while (a >= 2.0) { a /= 2.0; e++; }
+    while (a < 1.0) { a *= 2.0; e--; }
+    const double m = (a - 1.0) * 1024.0;
+    return e >= -14 && e <= 15 && m == (double)(long long)m;
+}
+__host__ __device__ constexpr bool sa_plans_exact()
+{
+    for (int k = 0; k < kSaPlan.n_pairs; k++) {
+        const int mv = (1 << (sl_bits(kSaPlan.lo[k] / (kSlSK / 5)) - 1)) - 1;
+        for (int d : {kSaPlan.dlo[k], kSaPlan.dhi[k]})
+            if (!sa_f16_exact(sa_pow2(-4 - d)) || !sa_f16_exact((1024.0 + mv * sa_pow2(d)) * sa_pow2(-4 - d)))
+                return false;
+    }
+    for (int k = 0; k < kSaResPlan.n_pairs; k++)
+        for (int d : {kSaResPlan.dlo[k], kSaResPlan.dhi[k]})
+            if (!sa_f16_exact(sa_pow2(-d)) || !sa_f16_exact((1024.0 + 0.5 * ((1 << kSlNR) - 1) * sa_pow2(d)) * sa_pow2(-d)))
+                return false;
+    return true;
+}
+static_assert(sa_plans_exact(), "fp16x2 pair constants must be exact");
+
+// Signed prediction of residual R: the sheet bit flips its sign.
+template <int R>
+__device__ __forceinline__ float sa_signed_pred(const uint32_t (&w)[26], const float (&pr)[kSlNRes])
+{
+    const uint32_t sgn = sa_bits<8 * kSlSheetOff + R, 1>(w) << 31;
+    return __uint_as_float(__float_as_uint(pr[R]) ^ sgn);
+}
+template <int K>
+__device__ __forceinline__ void sa_res_pair(const uint32_t (&w)[26], const float (&pr)[kSlNRes], float step,
+                                            float *c)
+{
+    constexpr int W = kSaResPlan.win[K], i = W >> 5, s = W & 31, d1 = kSaResPlan.dlo[K], d2 = kSaResPlan.dhi[K];
+    constexpr uint32_t m = (1u << kSlNR) - 1u, mask = (m << d1) | (m << (16 + d2));
+    constexpr double ctr = 0.5 * ((1 << kSlNR) - 1);
+    constexpr uint32_t kk = sa_f16_bits(sa_pow2(-d1)) | (sa_f16_bits(sa_pow2(-d2)) << 16);
+    constexpr uint32_t cc = sa_f16_bits(-(1024.0 + ctr * sa_pow2(d1)) * sa_pow2(-d1)) |
+                            (sa_f16_bits(-(1024.0 + ctr * sa_pow2(d2)) * sa_pow2(-d2)) << 16);
+    uint32_t win;
+    if constexpr (s == 0) win = w[i];
+    else win = __funnelshift_r(w[i], w[i + 1], s);
+    const uint32_t x = (win & mask) | 0x64006400u;
+    const __half2 v = __hfma2(*reinterpret_cast<const __half2 *>(&x), *reinterpret_cast<const __half2 *>(&kk),
+                              *reinterpret_cast<const __half2 *>(&cc));        // lv - center, both halves
+    constexpr int rl = kSaResPlan.lo[K], rh = kSaResPlan.hi[K];
+    c[rl] = __fmaf_rn(__low2float(v), step, sa_signed_pred<rl>(w, pr));
+    c[rh] = __fmaf_rn(__high2float(v), step, sa_signed_pred<rh>(w, pr));
+}
+template <size_t... K>
+__device__ __forceinline__ void sa_res_pairs(const uint32_t (&w)[26], const float (&pr)[kSlNRes], float step,
+                                             float *c, std::index_sequence<K...>)
+{
+    (sa_res_pair<(int)K>(w, pr, step, c), ...);
+}
+template <size_t... K>
+__device__ __forceinline__ void sa_res_left(const uint32_t (&w)[26], const float (&pr)[kSlNRes], float step,
+                                            float nc, float *c, std::index_sequence<K...>)
+{
+    ((c[sa_left_res((int)K)] = sa_res<sa_left_res((int)K)>(w, pr, step, nc)), ...);
+}
+
 // One slot (row words in w, w[25] zero) to its fp16 staging row (shared-
 // memory address row): 160 halves, coefficients times 2^-4 in row order
 // (kSaPlan).  Predictions accumulate term by term in slot order, as the
@@ -2495,9 +2594,12 @@ __device__ __forceinline__ void sa_slot_row(const uint32_t (&w)[26], uint32_t ro
     sa_f32_slots(w, scl, sb, pr, v, row, std::make_index_sequence<kSaPlan.n_f32>{});
     constexpr int L = 1 << kSlNR;
     const float mag = __uint_as_float(sa_bits<8 * kSlMagOff, 32>(w));
-    const float step = __fmul_rn(__fdiv_rn(__fmul_rn(2.0f, __fmul_rn(mag, (float)kSlNR)), (float)(L - 1)), 0.0625f);
+    // step = 2 mag bits / (L - 1), times 2^-4 (one multiply; the decode
+    // needs no bit-exact step)
+    const float step = __fmul_rn(mag, (float)(2.0 * kSlNR / (L - 1) * 0.0625));
     const float nc = -0.5f * (float)(L - 1) * step;
-    sa_residuals(w, pr, step, nc, v.rv, std::make_index_sequence<kSlNRes>{});
+    sa_res_pairs(w, pr, step, v.rv, std::make_index_sequence<kSaResPlan.n_pairs>{});
+    sa_res_left(w, pr, step, nc, v.rv, std::make_index_sequence<kSaResPlan.n_left>{});
     sa_store_stage<1 + kSaPlan.n_f32>(w, sb, v, row, std::make_index_sequence<20>{});
 }
 
