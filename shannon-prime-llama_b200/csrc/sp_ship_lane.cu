@@ -676,7 +676,8 @@ struct alignas(64) ReadMap { CUtensorMap m; };
 template <bool KS>
 struct ReadSmem {
     alignas(1024) unsigned char out[kLaneWarps][4][4096];      // 4 column slices x 32 rows x 128 B
-    uint16_t rows[kLaneWarps][32 * LaneLayout<KS>::TB / 2];
+    alignas(16) uint16_t rows[kLaneWarps][32 * LaneLayout<KS>::TB / 2];
+    unsigned long long bar[kLaneWarps];
 };
 
 // Slots a read covers: n_layers x n_heads slots, slot (l, h) at
@@ -706,15 +707,68 @@ k_decode_lane(const uint8_t *packed, ReadGrid rg, int n_pos, int nb_use, float i
     }
     const int n_bs = (n_pos + 31) >> 5;                 // batches per slot
     const long long n_b = (long long)n_bs * rg.n_heads * rg.n_layers;
-    for (long long bt = (long long)blockIdx.x * kLaneWarps + warp; bt < n_b; bt += (long long)gridDim.x * kLaneWarps) {
-        const int sl = (int)(bt / n_bs);
-        const int t0 = (int)(bt - (long long)sl * n_bs) * 32, live = min(32, n_pos - t0);
+    const long long b_step = (long long)gridDim.x * kLaneWarps;
+    // The 32 packed rows of a full batch are contiguous (32 x TB bytes, a
+    // multiple of 16): when their start is 16-byte aligned one bulk copy
+    // fetches them into the warp's row buffer, issued as soon as the
+    // previous batch's rows are in registers, so the load streams under that
+    // batch's butterfly and stores.  Ragged or unaligned batches are loaded
+    // by the lanes.
+    const uint32_t bar0 = spb::smem_u32(&sm.bar[warp]);
+    const uint32_t rows0 = spb::smem_u32(&sm.rows[warp][0]);
+    uint64_t policy = 0;
+    if (lane == 0) {
+        spb::mbar_init(bar0, 1);
+        spb::mbar_init_fence();
+        policy = spb::evict_first_policy();
+    }
+    __syncwarp();
+    auto batch_src = [&](long long bt, int &sl, int &t0, int &live) {
+        sl = (int)(bt / n_bs);
+        t0 = (int)(bt - (long long)sl * n_bs) * 32;
+        live = min(32, n_pos - t0);
+        return packed + (rg.slot0 + sl) * rg.slot_stride + (long long)(rg.pos0 + t0) * TB;
+    };
+    auto bulkable = [&](const uint8_t *src, int live) { return live == 32 && ((uintptr_t)src & 15) == 0; };
+    uint32_t par = 0u;                                  // parity of the next wait
+    bool pending = false;                               // a copy was issued into the buffer
+    // Next batch's source, or null when the lanes load it.
+    auto next_src = [&](long long bt) -> const uint8_t * {
+        if (bt >= n_b) return nullptr;
+        int sl, t0, live;
+        const uint8_t *src = batch_src(bt, sl, t0, live);
+        return bulkable(src, live) ? src : nullptr;
+    };
+    auto issue = [&](const uint8_t *src) {
+        if (!src) return;
+        pending = true;                                 // warp-uniform bookkeeping
+        if (lane == 0) {
+            spb::fence_proxy_async();
+            spb::mbar_expect_tx(bar0, 32 * TB);
+            spb::bulk_g2s(rows0, src, 32 * TB, bar0, policy);
+        }
+    };
+    long long bt = (long long)blockIdx.x * kLaneWarps + warp;
+    issue(next_src(bt));
+    bool failed = false;
+    for (; bt < n_b; bt += b_step) {
+        const uint8_t *nsrc = next_src(bt + b_step);
+        int sl, t0, live;
+        const uint8_t *srcb = batch_src(bt, sl, t0, live);
         const int l = sl / rg.n_heads, hh = sl - l * rg.n_heads;
         uint16_t *rows = sm.rows[warp];
-        const uint16_t *src = reinterpret_cast<const uint16_t *>(
-            packed + (rg.slot0 + sl) * rg.slot_stride + (long long)(rg.pos0 + t0) * TB);
-        for (int i = lane; i < live * TH; i += 32) rows[i] = src[i];
-        __syncwarp();
+        if (pending) {
+            if (!spb::wait_stage(bar0, par, status)) {
+                failed = true;                  // the copy may still land: waited for below
+                break;
+            }
+            pending = false;
+            par ^= 1u;
+        } else {
+            const uint16_t *src = reinterpret_cast<const uint16_t *>(srcb);
+            for (int i = lane; i < live * TH; i += 32) rows[i] = src[i];
+            __syncwarp();
+        }
         const uint16_t *r16 = rows + lane * TH;
         auto bits_at = [&](int p, int nb) -> uint32_t {
             const int h = p >> 4, sh = p & 15;
@@ -738,6 +792,8 @@ k_decode_lane(const uint8_t *packed, ReadGrid rg, int n_pos, int nb_use, float i
                 x[KS ? ord.v[j] : j] = v;                      // unreorder
             }
         }
+        __syncwarp();                           // every lane's row is in registers
+        issue(nsrc);
 #pragma unroll
         for (int len = 1; len < kLN; len <<= 1) {
 #pragma unroll
@@ -772,6 +828,9 @@ k_decode_lane(const uint8_t *packed, ReadGrid rg, int n_pos, int nb_use, float i
         }
         (void)live;
     }
+    // After a timed-out wait: bounded waits for the copies still in flight
+    // before the CTA's shared memory is released.
+    if (failed && pending) spb::wait_stage(bar0, par, nullptr);
     if (lane == 0) bulk_wait_all();
 }
 
