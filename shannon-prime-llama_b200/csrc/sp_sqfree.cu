@@ -2078,7 +2078,8 @@ struct alignas(64) SlOutMap { CUtensorMap m; };
 
 struct SlReadSmem {
     alignas(1024) unsigned char out[kSlWarps][4][4096];
-    uint32_t rows[kSlWarps][32 * 25];               // 32 slots of 100 bytes
+    alignas(16) uint32_t rows[kSlWarps][32 * 25];   // 32 slots of 100 bytes
+    unsigned long long bar[kSlWarps];
 };
 
 // Slots a lane read covers: n_layers x n_heads slots, slot (l, h) at
@@ -2103,15 +2104,63 @@ k_sq_decode_lane(const uint8_t *slab, SlGrid g, int n_pos, unsigned int *status,
     }
     const int n_bs = (n_pos + 31) >> 5;                 // batches per slot
     const long long n_b = (long long)n_bs * g.n_heads * g.n_layers;
-    for (long long bt = (long long)blockIdx.x * kSlWarps + warp; bt < n_b; bt += (long long)gridDim.x * kSlWarps) {
-        const int sl = (int)(bt / n_bs);
-        const int t0 = (int)(bt - (long long)sl * n_bs) * 32, live = min(32, n_pos - t0);
+    const long long b_step = (long long)gridDim.x * kSlWarps;
+    // A full batch's 32 slots (3200 contiguous bytes) arrive by one bulk
+    // copy when their start is 16-byte aligned, issued as soon as the
+    // previous batch's fields are in registers; the lanes load ragged or
+    // unaligned batches.
+    const uint32_t bar0 = spb::smem_u32(&sm.bar[warp]);
+    const uint32_t rows0 = spb::smem_u32(&sm.rows[warp][0]);
+    uint64_t policy = 0;
+    if (lane == 0) {
+        spb::mbar_init(bar0, 1);
+        spb::mbar_init_fence();
+        policy = spb::evict_first_policy();
+    }
+    __syncwarp();
+    auto batch_src = [&](long long bt, int &sl, int &t0, int &live) {
+        sl = (int)(bt / n_bs);
+        t0 = (int)(bt - (long long)sl * n_bs) * 32;
+        live = min(32, n_pos - t0);
+        return slab + (g.slot0 + sl) * g.slot_stride + (long long)(g.pos0 + t0) * kSlBytes;
+    };
+    auto next_src = [&](long long bt) -> const uint8_t * {
+        if (bt >= n_b) return nullptr;
+        int sl, t0, live;
+        const uint8_t *src = batch_src(bt, sl, t0, live);
+        return live == 32 && ((uintptr_t)src & 15) == 0 ? src : nullptr;
+    };
+    uint32_t par = 0u;
+    bool pending = false, failed = false;
+    auto issue = [&](const uint8_t *src) {
+        if (!src) return;
+        pending = true;
+        if (lane == 0) {
+            spb::fence_proxy_async();
+            spb::mbar_expect_tx(bar0, 32 * kSlBytes);
+            spb::bulk_g2s(rows0, src, 32 * kSlBytes, bar0, policy);
+        }
+    };
+    long long bt = (long long)blockIdx.x * kSlWarps + warp;
+    issue(next_src(bt));
+    for (; bt < n_b; bt += b_step) {
+        const uint8_t *nsrc = next_src(bt + b_step);
+        int sl, t0, live;
+        const uint8_t *srcb = batch_src(bt, sl, t0, live);
         const int l = sl / g.n_heads, hh = sl - l * g.n_heads;
         uint32_t *rows = sm.rows[warp];
-        const uint32_t *src = reinterpret_cast<const uint32_t *>(
-            slab + (g.slot0 + sl) * g.slot_stride + (long long)(g.pos0 + t0) * kSlBytes);
-        for (int i = lane; i < live * TW; i += 32) rows[i] = src[i];
-        __syncwarp();
+        if (pending) {
+            if (!spb::wait_stage(bar0, par, status)) {
+                failed = true;                  // the copy may still land: waited for below
+                break;
+            }
+            pending = false;
+            par ^= 1u;
+        } else {
+            const uint32_t *src = reinterpret_cast<const uint32_t *>(srcb);
+            for (int i = lane; i < live * TW; i += 32) rows[i] = src[i];
+            __syncwarp();
+        }
         const uint32_t *rw = rows + lane * TW;
         auto bits_at = [&](int p, int nb) -> uint32_t {
             const int w = p >> 5, sh = p & 31;
@@ -2149,6 +2198,8 @@ k_sq_decode_lane(const uint8_t *slab, SlGrid g, int n_pos, unsigned int *status,
             const float p = bits_at(8 * kSlSheetOff + r, 1) ? -pr[r] : pr[r];
             rs[r] = __fadd_rn(p, dev);
         }
+        __syncwarp();                           // every lane's fields are in registers
+        issue(nsrc);
         float x[kSlPD];
         sl_scatter(x, sk, rs, std::make_index_sequence<kSlSK>{}, std::make_index_sequence<NR>{});
         sl_stage<2, 1>(x);
@@ -2174,6 +2225,7 @@ k_sq_decode_lane(const uint8_t *slab, SlGrid g, int n_pos, unsigned int *status,
             asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         }
     }
+    if (failed && pending) spb::wait_stage(bar0, par, nullptr);
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
