@@ -410,28 +410,6 @@ extern "C" int sp_cuda_attn_decode(const sp_cuda_cache_t *cc, int layer0, int n_
 
 // ----------------------------------------------- fused decode + all-gather --
 
-// Bounded wait (2 s) until every rank's flag in this rank's buffer shows
-// `epoch` (wrap-safe); on timeout bit 1 of *status is set.
-__global__ void k_gather_wait(const unsigned int *flags, int world, unsigned int epoch, unsigned int *status)
-{
-    const int p = threadIdx.x;
-    if (p >= world) return;
-    unsigned long long t0;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-    for (;;) {
-        unsigned int v;
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + p) : "memory");
-        if ((int)(v - epoch) >= 0) return;
-        unsigned long long t;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        if (t - t0 > 2000000000ull) {
-            atomicOr(status, 2u);
-            return;
-        }
-        __nanosleep(200);
-    }
-}
-
 extern "C" int sp_cuda_attn_decode_allgather(const sp_cuda_cache_t *cc, int layer0, int n_layers,
                                              const void *d_q, int n_q_heads, int kv_len, float logit_scale,
                                              int max_bands, void *d_local_buf, void *const *d_peer_bufs,
@@ -464,12 +442,11 @@ extern "C" int sp_cuda_attn_decode_allgather(const sp_cuda_cache_t *cc, int laye
     a.g.epoch = epoch;
     a.g.block_count = cc->d_status + 1;          // zero between calls
     a.g.n_blocks = (unsigned)(((n_q_heads + 3) / 4) * n_layers);   // both combine grids: 4 rows per block
-    cudaStream_t s = (cudaStream_t)stream;
-    if ((rc = attn_launch(a, use_mma, s))) return rc;
-    k_gather_wait<<<1, 32, 0, s>>>(reinterpret_cast<const unsigned int *>(
-                                       reinterpret_cast<const unsigned char *>(d_local_buf) + flags_offset),
-                                   world, epoch, cc->d_status);
-    return sp_check_cuda(cudaGetLastError(), "attn_decode_allgather wait launch");
+    a.g.own_flags = reinterpret_cast<const unsigned int *>(static_cast<const unsigned char *>(d_local_buf) +
+                                                           flags_offset);
+    // The combine's last block waits for every rank's flag, so the call's
+    // kernels end only once the gathered rows are all in place.
+    return attn_launch(a, use_mma, (cudaStream_t)stream);
 }
 
 // ------------------------------------------------ allocation-free variant --

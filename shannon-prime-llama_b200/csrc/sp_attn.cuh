@@ -25,7 +25,15 @@ struct SpGather {
     unsigned int epoch;
     unsigned int *block_count;          // device counter, zero between calls
     unsigned int n_blocks;              // combine blocks in the call
+    const unsigned int *own_flags;      // [world] flags in this rank's own buffer
 };
+
+// Programmatic dependent launch: a main decode kernel lets its combine
+// kernel launch early (sp_pdl_trigger at its start); the combine waits for
+// the main grid's completion and memory (sp_pdl_wait) before it reads any
+// partial.
+__device__ __forceinline__ void sp_pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void sp_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 struct SpAttnArgs {
     const uint8_t *k_cache;
@@ -75,7 +83,10 @@ __device__ __forceinline__ void sp_attn_store_row(const SpAttnArgs &a, int li, i
 }
 
 // After a combine block's rows are stored: the last block of the call
-// raises this rank's flag in every rank's buffer.  Called by every thread.
+// raises this rank's flag in every rank's buffer, then waits (bounded at
+// 2 s by %globaltimer; bit 1 of *status on timeout) until every rank's flag
+// in this rank's own buffer shows the epoch (wrap-safe), so the kernel ends
+// only when the whole gathered output is in place.  Called by every thread.
 __device__ __forceinline__ void sp_attn_gather_signal(const SpAttnArgs &a)
 {
     if (a.g.world == 0) return;
@@ -90,6 +101,22 @@ __device__ __forceinline__ void sp_attn_gather_signal(const SpAttnArgs &a)
                 unsigned int *f = reinterpret_cast<unsigned int *>(
                     reinterpret_cast<unsigned char *>(a.g.peers[p]) + a.g.flags_offset) + a.g.rank;
                 asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(a.g.epoch) : "memory");
+            }
+            unsigned long long t0;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+            for (int p = 0; p < a.g.world; p++) {
+                for (;;) {
+                    unsigned int v;
+                    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a.g.own_flags + p) : "memory");
+                    if ((int)(v - a.g.epoch) >= 0) break;
+                    unsigned long long t;
+                    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+                    if (t - t0 > 2000000000ull) {
+                        atomicOr(a.status, 2u);
+                        return;
+                    }
+                    __nanosleep(64);
+                }
             }
         }
     }

@@ -167,46 +167,47 @@ __device__ __forceinline__ void combine_row(const SpAttnArgs &a, const Sched &sc
     const int i0 = cta_of_tile(u * sc.tiles_per_unit, sc);
     const int i1 = cta_of_tile((u + 1) * sc.tiles_per_unit - 1, sc);
     const int nseg = i1 - i0 + 1;
-    // Segment maxima and sums are loaded by the lanes in parallel (32
-    // segments per round), the weights broadcast, and the accumulator loads
-    // issued four segments at a time, so the merge costs a few L2 round
-    // trips rather than one per segment.
-    float M = kEmptyMax;
-    for (int s0 = 0; s0 < nseg; s0 += 32) {
-        const int s = s0 + lane;
-        if (s < nseg) M = fmaxf(M, __ldcg(sp_attn_partial(a, li, qh, s)));
+    // Lane s owns segments s, s + 32, s + 64, s + 96 (at most kAttnMaxSplits
+    // = 128): their maxima and sums arrive in one round of loads, the
+    // weights stay in the owning lanes, and the accumulator rows are loaded
+    // 16 segments at a time, all in flight together, so a row costs about
+    // 1 + nseg / 16 L2 round trips.
+    static_assert(kAttnMaxSplits <= 128, "four segments per lane");
+    float mv[4], lv[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int sg = lane + 32 * j;
+        mv[j] = kEmptyMax;
+        lv[j] = 0.0f;
+        if (sg < nseg) {
+            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(sp_attn_partial(a, li, qh, sg)));
+            mv[j] = ml.x;
+            lv[j] = ml.y;
+        }
     }
+    float M = fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float wv[4], L = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        wv[j] = lane + 32 * j < nseg ? exp2f(mv[j] - M) : 0.0f;
+        L += wv[j] * lv[j];
+    }
     float x[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    float L = 0.0f;
-    for (int s0 = 0; s0 < nseg; s0 += 32) {
-        const int s = s0 + lane;
-        float w = 0.0f;
-        if (s < nseg) {
-            const float *p = sp_attn_partial(a, li, qh, s);
-            w = exp2f(__ldcg(p) - M);
-            L += w * __ldcg(p + 1);
-        }
-        const int n_here = min(32, nseg - s0);
-        int j = 0;
-        for (; j + 4 <= n_here; j += 4) {
-            float4 v[4];
-            float wj[4];
+    for (int c0 = 0; c0 < nseg; c0 += 16) {
+        const int jw = c0 >> 5;                         // weights of this chunk live in wv[jw]
+        const float wsrc = jw == 0 ? wv[0] : jw == 1 ? wv[1] : jw == 2 ? wv[2] : wv[3];
+        float4 v[16];
 #pragma unroll
-            for (int t = 0; t < 4; t++) {
-                v[t] = __ldcg(reinterpret_cast<const float4 *>(sp_attn_partial(a, li, qh, s0 + j + t) + 4 + lane * 4));
-                wj[t] = __shfl_sync(0xffffffffu, w, j + t);
-            }
+        for (int t = 0; t < 16; t++)
+            v[t] = c0 + t < nseg
+                       ? __ldcg(reinterpret_cast<const float4 *>(sp_attn_partial(a, li, qh, c0 + t) + 4 + lane * 4))
+                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
-            for (int t = 0; t < 4; t++) {
-                x[0] += wj[t] * v[t].x; x[1] += wj[t] * v[t].y; x[2] += wj[t] * v[t].z; x[3] += wj[t] * v[t].w;
-            }
-        }
-        for (; j < n_here; j++) {
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(sp_attn_partial(a, li, qh, s0 + j) + 4 + lane * 4));
-            const float wj = __shfl_sync(0xffffffffu, w, j);
-            x[0] += wj * v.x; x[1] += wj * v.y; x[2] += wj * v.z; x[3] += wj * v.w;
+        for (int t = 0; t < 16; t++) {
+            const float wt = __shfl_sync(0xffffffffu, wsrc, (c0 + t) & 31);
+            x[0] += wt * v[t].x; x[1] += wt * v[t].y; x[2] += wt * v[t].z; x[3] += wt * v[t].w;
         }
     }
 #pragma unroll
@@ -226,6 +227,7 @@ __global__ void __launch_bounds__(kWarps * 32, kMinBlocks)
 k_attn_ship_mma(SpAttnArgs a, Sched sc)
 {
     static_assert(GT == 4 || GT == 8, "4 or 8 query heads per KV head");
+    sp_pdl_trigger();                   // the combine may launch and wait on this grid
     constexpr int NT = GT / 4;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     Smem<kWarps, kStages, GT> &sm = *reinterpret_cast<Smem<kWarps, kStages, GT> *>(smem_raw);
@@ -719,6 +721,7 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
 // (locally, or into every rank's gather buffer).
 __global__ void k_attn_combine_seg(SpAttnArgs a, Sched sc)
 {
+    sp_pdl_wait();                      // launched early: the main grid's partials first
     const int lane = threadIdx.x & 31;
     const int qh = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int li = blockIdx.y;
@@ -815,10 +818,22 @@ int sp_attn_mma_launch(const SpAttnArgs &a_in, cudaStream_t s, cudaEvent_t ev_be
     return sp_attn_seg_combine_launch(a, sc, s);
 }
 
+// The combine is launched as a programmatic dependent of the main kernel:
+// it may start as soon as every main block has begun (sp_pdl_trigger) and
+// waits in sp_pdl_wait for the main grid's completion, which takes the
+// kernel-to-kernel launch gap off the step.
 int sp_attn_seg_combine_launch(const SpAttnArgs &a, const SpSched &sc, cudaStream_t s)
 {
     const int per_block = 4;
-    dim3 grid((a.n_q_heads + per_block - 1) / per_block, a.n_layers);
-    k_attn_combine_seg<<<grid, per_block * 32, 0, s>>>(a, sc);
-    return sp_check_cuda(cudaGetLastError(), "tensor-core attention combine launch");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((a.n_q_heads + per_block - 1) / per_block, a.n_layers);
+    cfg.blockDim = dim3(per_block * 32);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return sp_check_cuda(cudaLaunchKernelEx(&cfg, k_attn_combine_seg, a, sc), "tensor-core attention combine launch");
 }
