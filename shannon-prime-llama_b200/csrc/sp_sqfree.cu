@@ -4705,16 +4705,23 @@ int sp_cuda_sqfree_attn_decode(const sp_cuda_sqfree_cache_t *cc, int layer0, int
             occ_dev = dev;
         }
         // Splits: the count (at most one tile per warp's worth of positions
-        // per split and kSqMaxSplits) whose CTAs fill the last wave best.
+        // per split and kSqMaxSplits) with the least modelled time: waves of
+        // resident CTAs times (32-position tiles of the busiest warp + a
+        // fixed cost per CTA of about two tiles: query fragments, the warp
+        // merge and the partial stores).  Long CTAs amortise that cost and
+        // keep a CTA's four warps balanced.
         const long long slots = (long long)occ_val.load() * occ_sms.load();
         const int max_s = std::max(1, std::min(kSqMaxSplits, (kv_len + 32 * kSaWarps - 1) / (32 * kSaWarps)));
+        constexpr double kCtaFixedTiles = 2.0;
         int best = 1;
-        double best_eff = -1.0;
+        double best_cost = 1e300;
         for (int sp = 1; sp <= max_s; sp++) {
             const long long ctas = (long long)units * sp;
             const long long waves = (ctas + slots - 1) / slots;
-            const double eff = (double)ctas / (double)(waves * slots);
-            if (eff > best_eff + 1e-9) { best_eff = eff; best = sp; }
+            const int chunk = ((kv_len + sp - 1) / sp + 31) / 32 * 32;
+            const int tiles = (chunk + 31) / 32;
+            const double cost = (double)waves * ((tiles + kSaWarps - 1) / kSaWarps + kCtaFixedTiles);
+            if (cost < best_cost - 1e-9) { best_cost = cost; best = sp; }
         }
         a.chunk = ((kv_len + best - 1) / best + 31) / 32 * 32;
         a.n_splits = (kv_len + a.chunk - 1) / a.chunk;
