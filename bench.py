@@ -794,7 +794,7 @@ def run_ours(args):
         "e2e": {"value": e2e_ms * 1e3, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "path": ("sp_cuda_attn_decode_allgather (pinned host q in, gathered output of all ranks back)"
-                         if gather is not None else "sp_llama_attn_decode (host q in, host out back)")},
+                         if gather is not None else "sp_llama_attn_decode (pinned host q in, host out back: the decode kernels read q and write the output rows over the host link in place)")},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
         "compress": {"metric": "ship-path compress throughput (K+V pairs)", "value": comp_mpairs,

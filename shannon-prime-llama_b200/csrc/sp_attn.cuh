@@ -62,6 +62,15 @@ __device__ __forceinline__ void sp_attn_store_row(const SpAttnArgs &a, int li, i
     const int n = 32 * E;
     if (a.g.world == 0) {
         __half *o = a.out + ((long long)li * a.n_q_heads + qh) * n + lane * E;
+        if constexpr (E == 4) {
+            if (((uintptr_t)o & 7) == 0) {      // one 8-byte store per lane (the output may be host memory)
+                uint2 w;
+                w.x = (uint32_t)__half_as_ushort(h[0]) | ((uint32_t)__half_as_ushort(h[1]) << 16);
+                w.y = (uint32_t)__half_as_ushort(h[2]) | ((uint32_t)__half_as_ushort(h[3]) << 16);
+                *reinterpret_cast<uint2 *>(o) = w;
+                return;
+            }
+        }
 #pragma unroll
         for (int e = 0; e < E; e++) o[e] = h[e];
         return;

@@ -99,7 +99,8 @@ def test_bridge_fused_decode_host_buffers(bridge):
     ref = O.attn_decode(kp, vp, n, KB, VB, True, q[0], T, 1.0)
     err = np.linalg.norm(out[0].astype(np.float64) - ref) / np.linalg.norm(ref)
     assert err <= 1e-3
-    # page-locked caller buffers take the direct-copy path: same result
+    # page-locked (mapped) caller buffers are read and written in place by
+    # the decode kernels: same result
     import torch
     qp = torch.from_numpy(q).pin_memory()
     op = torch.zeros(out.shape, dtype=torch.float16).pin_memory()
@@ -111,3 +112,8 @@ def test_bridge_fused_decode_host_buffers(bridge):
     rc = L.sp_llama_attn_decode(ctx, 0, 1, qp.data_ptr(), H * G, T, 1.0, out2.ctypes.data, -1)
     assert rc == 0
     np.testing.assert_array_equal(out2, out)
+    # pageable q with a page-locked output: same bytes
+    op2 = torch.zeros(out.shape, dtype=torch.float16).pin_memory()
+    rc = L.sp_llama_attn_decode(ctx, 0, 1, q.ctypes.data, H * G, T, 1.0, op2.data_ptr(), -1)
+    assert rc == 0
+    np.testing.assert_array_equal(op2.numpy(), out)
