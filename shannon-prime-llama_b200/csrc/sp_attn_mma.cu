@@ -134,6 +134,15 @@ __device__ __forceinline__ uint32_t split_hi_lo(float x)
     return (uint32_t)__half_as_ushort(h) | ((uint32_t)__half_as_ushort(l) << 16);
 }
 
+// x * 2^e by one multiply (e inside the normal exponent range, where that is
+// exactly ldexpf), else ldexpf.
+__device__ __forceinline__ float scale2(float x, int e)
+{
+    return (e >= -126 && e <= 127) ? x * __int_as_float((e + 127) << 23) : ldexpf(x, e);
+}
+// ilogbf of a normal, positive float.
+__device__ __forceinline__ int ilogb_normal(float x) { return ((__float_as_int(x) >> 23) & 0xff) - 127; }
+
 // Zero the non-finite halves of a half2 (the reference zeroes a band whose
 // stored scale is not finite, shannon_prime_cuda.cu:236-245).
 __device__ __forceinline__ __half2 finite_or_zero(__half2 h)
@@ -227,7 +236,11 @@ __global__ void __launch_bounds__(kWarps * 32, kMinBlocks)
 k_attn_ship_mma(SpAttnArgs a, Sched sc)
 {
     static_assert(GT == 4 || GT == 8, "4 or 8 query heads per KV head");
-    sp_pdl_trigger();                   // the combine may launch and wait on this grid
+    // Launched as a programmatic dependent of the stream's previous kernel:
+    // nothing global is touched before that kernel has completed.  Then the
+    // combine may launch and wait on this grid.
+    sp_pdl_wait();
+    sp_pdl_trigger();
     constexpr int NT = GT / 4;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     Smem<kWarps, kStages, GT> &sm = *reinterpret_cast<Smem<kWarps, kStages, GT> *>(smem_raw);
@@ -361,14 +374,14 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
         for (int nt = 0; nt < NT; nt++) {
             const int g = 4 * nt + (r >> 1);
             const float qm = sm.qmax[g];
-            const int F = qm > 1e-30f ? 6 - ilogbf(qm) : 0;
+            const int F = qm > 1e-30f ? 6 - ilogb_normal(qm) : 0;
 #pragma unroll
             for (int b = 0; b < 4; b++) {
 #pragma unroll
                 for (int p = 0; p < 4; p++) {
                     const int lo = 32 * b + 8 * c + p, hi = lo + 4;
-                    float vlo = ldexpf(sm.q[g][lo], F - pair_dlo(b, p));
-                    float vhi = ldexpf(sm.q[g][hi], F - pair_dhi(b, p));
+                    float vlo = scale2(sm.q[g][lo], F - pair_dlo(b, p));
+                    float vhi = scale2(sm.q[g][hi], F - pair_dhi(b, p));
                     if (b >= a.nb_k) vlo = vhi = 0.0f;
                     const uint32_t slo = split_hi_lo(vlo), shi = split_hi_lo(vhi);
                     const uint32_t w = (r & 1) ? ((slo >> 16) | (shi & 0xffff0000u))
@@ -384,12 +397,12 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
         for (int nt = 0; nt < NT; nt++) {
             const int g = 4 * nt + c;
             const float qm = sm.qmax[g];
-            const int F = qm > 1e-30f ? 6 - ilogbf(qm) : 0;
-            kc[nt] = ldexpf(1.0f, 24 - F);
+            const int F = qm > 1e-30f ? 6 - ilogb_normal(qm) : 0;
+            kc[nt] = scale2(1.0f, 24 - F);
 #pragma unroll
             for (int b = 0; b < 4; b++) {
                 const float m_b = (float)((1 << (kKBits(b) - 1)) - 1);
-                cinit[nt][b] = b < a.nb_k ? -ldexpf(m_b * sm.qsum[g][b], F - 24) : 0.0f;
+                cinit[nt][b] = b < a.nb_k ? -scale2(m_b * sm.qsum[g][b], F - 24) : 0.0f;
             }
         }
 
@@ -673,7 +686,7 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
 #pragma unroll
                 for (int rr = 0; rr < 2; rr++) {
                     const int j = 2 * mt + rr;
-                    const float v = ldexpf(oacc[nt][mt][2 * rr] + oacc[nt][mt][2 * rr + 1], 24 - vcode_d(j));
+                    const float v = (oacc[nt][mt][2 * rr] + oacc[nt][mt][2 * rr + 1]) * (float)(1 << (24 - vcode_d(j)));
                     mrow[4 + 16 * r + j] = v - mv * p_sum[nt];
                 }
             }
@@ -722,6 +735,7 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
 __global__ void k_attn_combine_seg(SpAttnArgs a, Sched sc)
 {
     sp_pdl_wait();                      // launched early: the main grid's partials first
+    sp_pdl_trigger();                   // the next call's main kernel may launch and wait on this grid
     const int lane = threadIdx.x & 31;
     const int qh = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int li = blockIdx.y;
@@ -811,9 +825,21 @@ int sp_attn_mma_launch(const SpAttnArgs &a_in, cudaStream_t s, cudaEvent_t ev_be
     sc.n_ctas = (int)n;
     a.n_splits = 0;
     if (ev_begin) cudaEventRecord(ev_begin, s);
-    kernel<<<sc.n_ctas, threads, smem, s>>>(a, sc);
+    // A programmatic dependent of the stream's previous kernel (the previous
+    // call's combine, in a decode loop): its blocks are placed while that
+    // kernel finishes and start at its completion.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sc.n_ctas);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int rc = sp_check_cuda(cudaLaunchKernelEx(&cfg, kernel, a, sc), "tensor-core attention launch");
     if (ev_end) cudaEventRecord(ev_end, s);
-    int rc = sp_check_cuda(cudaGetLastError(), "tensor-core attention launch");
     if (rc) return rc;
     return sp_attn_seg_combine_launch(a, sc, s);
 }
