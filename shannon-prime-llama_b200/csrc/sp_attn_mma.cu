@@ -51,9 +51,11 @@
 
 namespace {
 
-constexpr int kKTile = 16 * 76;       // 1216
+constexpr int kKTile = 16 * 76;       // 1216: one 16-position MMA tile of K rows
 constexpr int kVTile = 16 * 50;       // 800
-constexpr int kStageBytes = kKTile + kVTile;   // 2016
+constexpr int kSub = 2;               // MMA tiles per ring stage (32 positions per bulk-copied stage)
+constexpr int kKStage = kSub * kKTile;             // 2432
+constexpr int kStageBytes = kSub * (kKTile + kVTile);   // 4032
 constexpr int kN = 128;
 constexpr float kEmptyMax = -1.0e30f; // running max before the first valid token
 constexpr int kFlushTiles = 16;       // tiles between V-accumulator recentrings
@@ -162,7 +164,7 @@ struct Smem {
     float qsum[GT][4];       // per query, per band: sum of q'
     float qmax[GT];
     float merge[kWarps][GT][4 + kN];
-    float scl[kWarps][kStages][16][8];   // per stage: K band scales 0..3, V scale (fp32)
+    float scl[kWarps][kStages][16 * kSub][8];   // per stage position: K band scales 0..3, V scale (fp32)
 };
 
 // kWarps warps per CTA, a kStages-deep copy ring per warp, kMinBlocks CTAs
@@ -272,8 +274,8 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
     const uint8_t *ic_k = nullptr, *ic_v = nullptr;
     auto ic_point = [&]() {
         const long long slot = (long long)(a.layer0 + ic_li) * H + ic_h;
-        ic_k = a.k_cache + slot * a.k_slot_stride + (long long)ic_tile * kKTile;
-        ic_v = a.v_cache + slot * a.v_slot_stride + (long long)ic_tile * kVTile;
+        ic_k = a.k_cache + slot * a.k_slot_stride + (long long)ic_tile * kKStage;
+        ic_v = a.v_cache + slot * a.v_slot_stride + (long long)ic_tile * (kSub * kVTile);
     };
     if (lane == 0 && n_my > 0) {
         const long long u0 = my_first / n_t;
@@ -286,14 +288,18 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
         const int st = k % kStages;
         const uint32_t bar = bar0 + 8 * st;
         const uint32_t dst = ring0 + st * kStageBytes;
+        // the stage's 16-position tiles that start before kv_len (whole
+        // 16-row tiles lie inside the slot; the rows past kv_len are masked)
+        const int rem = a.kv_len - ic_tile * 16 * kSub;
+        const int nsub = rem >= 16 * kSub ? kSub : (rem + 15) / 16;
         spb::fence_proxy_async();
-        mbar_expect_tx(bar, kStageBytes);
-        bulk_g2s(dst, ic_k, kKTile, bar, policy);
-        bulk_g2s(dst + kKTile, ic_v, kVTile, bar, policy);
+        mbar_expect_tx(bar, (uint32_t)nsub * (kKTile + kVTile));
+        bulk_g2s(dst, ic_k, (uint32_t)nsub * kKTile, bar, policy);
+        bulk_g2s(dst + kKStage, ic_v, (uint32_t)nsub * kVTile, bar, policy);
         ic_tile += kWarps;
         if (ic_tile < n_t) {
-            ic_k += kWarps * kKTile;
-            ic_v += kWarps * kVTile;
+            ic_k += kWarps * kKStage;
+            ic_v += kWarps * (kSub * kVTile);
         } else {
             while (ic_tile >= n_t) {
                 ic_tile -= n_t;
@@ -450,25 +456,28 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
         // interleave in the schedule.  The running max is updated with the
         // scores of tile k+1 only after tile k's weights are formed.
         //
-        // K side of the tile in ring stage st (positions tok0..tok0+15):
-        // band scales to fp32 (scl[st]), code unpack, band MMAs, and the
-        // scores of positions r, r+8 for query 4nt+c in units of 1/kc.
-        auto k_scores = [&](int st, int tok0, float (&su)[NT][2]) {
+        // Band scales of ring stage st to fp32 (scl[st]): lane t converts
+        // the four K bands and the V scale of the stage's position t.
+        auto stage_scales = [&](int st) {
             const unsigned char *kt = sm.ring[warp][st];
+            const int sub = lane >> 4, t = lane & 15;
+            const uint32_t *row = reinterpret_cast<const uint32_t *>(kt + sub * kKTile) + 19 * t;
+            const uint32_t w0 = row[kKScaleWord(0)], w1 = row[kKScaleWord(1)];
+            const uint32_t w2 = row[kKScaleWord(2)], w3 = row[kKScaleWord(3)];
+            const uint32_t h01 = __byte_perm(w0, w1, 0x7610), h23 = __byte_perm(w2, w3, 0x7610);
+            const float2 f01 = __half22float2(finite_or_zero(*reinterpret_cast<const __half2 *>(&h01)));
+            const float2 f23 = __half22float2(finite_or_zero(*reinterpret_cast<const __half2 *>(&h23)));
+            *reinterpret_cast<float4 *>(&sm.scl[warp][st][lane][0]) = make_float4(f01.x, f01.y, f23.x, f23.y);
+            const unsigned short vb =
+                *reinterpret_cast<const unsigned short *>(kt + kKStage + sub * kVTile + 50 * t);
+            sm.scl[warp][st][lane][4] = __low2float(finite_or_zero(__half2half2(__ushort_as_half(vb))));
+        };
+        // K side of MMA tile `sub` of ring stage st (positions
+        // tok0..tok0+15): code unpack, band MMAs, and the scores of
+        // positions r, r+8 for query 4nt+c in units of 1/kc.
+        auto k_scores = [&](int st, int sub, int tok0, float (&su)[NT][2]) {
+            const unsigned char *kt = sm.ring[warp][st] + sub * kKTile;
             const uint32_t *K32 = reinterpret_cast<const uint32_t *>(kt);
-            // lane t<16 converts K bands 0,1 of position t, lane 16+t bands
-            // 2,3; every lane converts the V scale of position t&15.
-            {
-                const int t = lane & 15, hi = lane >> 4;
-                const uint32_t *row = K32 + 19 * t;
-                const uint32_t wa = row[hi ? kKScaleWord(2) : kKScaleWord(0)];
-                const uint32_t wb = row[hi ? kKScaleWord(3) : kKScaleWord(1)];
-                const uint32_t hw = __byte_perm(wa, wb, 0x7610);
-                const float2 f = __half22float2(finite_or_zero(*reinterpret_cast<const __half2 *>(&hw)));
-                *reinterpret_cast<float2 *>(&sm.scl[warp][st][t][2 * hi]) = f;
-                const unsigned short vb = *reinterpret_cast<const unsigned short *>(kt + kKTile + 50 * t);
-                sm.scl[warp][st][t][4] = __low2float(finite_or_zero(__half2half2(__ushort_as_half(vb))));
-            }
             // Band dot products; the accumulator starts at -m_b * sum(q') in
             // its hi column, so acc_hi + acc_lo = sum_i (u_i - m_b) q'_i / kc.
             // Each MMA's A quad is unpacked right before it, so the four
@@ -525,7 +534,8 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
             __syncwarp();
             float4 fs[2];
 #pragma unroll
-            for (int hh = 0; hh < 2; hh++) fs[hh] = *reinterpret_cast<const float4 *>(&sm.scl[warp][st][r + 8 * hh][0]);
+            for (int hh = 0; hh < 2; hh++)
+                fs[hh] = *reinterpret_cast<const float4 *>(&sm.scl[warp][st][16 * sub + r + 8 * hh][0]);
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
 #pragma unroll
@@ -540,10 +550,12 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
             }
         };
         // Online softmax max update (rescale only when the running max grows).
-        auto update_max = [&](const float (&su)[NT][2]) {
+        auto update_max = [&](const float (&su)[kSub][NT][2]) {
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
-                const float mx = fmaxf(su[nt][0], su[nt][1]);
+                float mx = fmaxf(su[0][nt][0], su[0][nt][1]);
+#pragma unroll
+                for (int sb = 1; sb < kSub; sb++) mx = fmaxf(mx, fmaxf(su[sb][nt][0], su[sb][nt][1]));
                 if (__any_sync(0xffffffffu, mx > m_run[nt])) {
                     float mt = mx;
                     mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
@@ -566,9 +578,9 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
         // Softmax weights of the tile in stage st and its V product: lane r
         // unpacks its 16-coefficient chunk of position pairs (2c, 2c+1) and
         // (2c+8, 2c+9).
-        auto v_step = [&](int st, const float (&su)[NT][2]) {
+        auto v_step = [&](int st, int sub, const float (&su)[NT][2]) {
             const unsigned char *kt = sm.ring[warp][st];
-            const uint32_t *V32 = reinterpret_cast<const uint32_t *>(kt + kKTile);
+            const uint32_t *V32 = reinterpret_cast<const uint32_t *>(kt + kKStage + sub * kVTile);
             // 16-bit windows of the two position rows, interleaved per half:
             // W[hh][wi] holds 5 codes of each row (the last one code).
             uint32_t W[2][4];
@@ -599,7 +611,7 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
             };
             float vscale[2];
 #pragma unroll
-            for (int hh = 0; hh < 2; hh++) vscale[hh] = sm.scl[warp][st][r + 8 * hh][4];
+            for (int hh = 0; hh < 2; hh++) vscale[hh] = sm.scl[warp][st][16 * sub + r + 8 * hh][4];
             uint32_t pb[NT][2];
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
@@ -640,11 +652,14 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
 
         int ctile = (int)(my_first + (long long)k_next * kWarps - u * n_t);
         if (k_next < n_my && ctile < n_t) {
-            float su[NT][2];
+            float su[kSub][NT][2];
             if (!wait_stage(bar0 + 8 * (k_next % kStages), (k_next / kStages) & 1, a.status)) {
                 failed = true;
             } else {
-                k_scores(k_next % kStages, ctile * 16, su);
+                stage_scales(k_next % kStages);
+                __syncwarp();
+#pragma unroll
+                for (int sb = 0; sb < kSub; sb++) k_scores(k_next % kStages, sb, ctile * 16 * kSub + 16 * sb, su[sb]);
                 update_max(su);
             }
             while (!failed) {
@@ -656,10 +671,15 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
                 }
                 // Without a next tile of this segment, the scores below are
                 // taken on whatever the next stage holds and discarded.
-                float sn[NT][2];
-                k_scores(kn % kStages, ctn * 16, sn);
-                v_step(k_next % kStages, su);
-                if (++n_since_flush == kFlushTiles) recenter();
+                float sn[kSub][NT][2];
+                stage_scales(kn % kStages);
+                __syncwarp();
+#pragma unroll
+                for (int sb = 0; sb < kSub; sb++) k_scores(kn % kStages, sb, ctn * 16 * kSub + 16 * sb, sn[sb]);
+#pragma unroll
+                for (int sb = 0; sb < kSub; sb++) v_step(k_next % kStages, sb, su[sb]);
+                n_since_flush += kSub;
+                if (n_since_flush >= kFlushTiles) recenter();
                 if (has_next) update_max(sn);
                 __syncwarp();
                 if (lane == 0 && k_next + kStages < n_my) issue(k_next + kStages);
@@ -667,7 +687,9 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
                 ctile = ctn;
                 if (!has_next) break;
 #pragma unroll
-                for (int nt = 0; nt < NT; nt++) { su[nt][0] = sn[nt][0]; su[nt][1] = sn[nt][1]; }
+                for (int sb = 0; sb < kSub; sb++)
+#pragma unroll
+                    for (int nt = 0; nt < NT; nt++) { su[sb][nt][0] = sn[sb][nt][0]; su[sb][nt][1] = sn[sb][nt][1]; }
             }
         }
 
@@ -773,7 +795,7 @@ int sp_attn_mma_supported(const SpAttnArgs &a)
 // deeper rings gain nothing (a ring of 4 already sustains the copy stream
 // at the HBM rate when the compute is removed).
 // Up to 8 query heads per KV head (two column tiles, more registers): 2 CTAs/SM.
-constexpr int kCtaWarps = 4, kRingStages = 4, kCtasPerSm = 3, kCtasPerSm8 = 2;
+constexpr int kCtaWarps = 4, kRingStages = 3, kCtasPerSm = 3, kCtasPerSm8 = 2;
 
 int sp_attn_mma_launch(const SpAttnArgs &a_in, cudaStream_t s, cudaEvent_t ev_begin, cudaEvent_t ev_end)
 {
@@ -816,7 +838,7 @@ int sp_attn_mma_launch(const SpAttnArgs &a_in, cudaStream_t s, cudaEvent_t ev_be
     const int sms_cached = sms_tab[dev].load(std::memory_order_relaxed);
     const int units = a.n_layers * a.n_kv_heads;
     Sched sc;
-    sc.tiles_per_unit = (a.kv_len + 15) / 16;
+    sc.tiles_per_unit = (a.kv_len + 16 * kSub - 1) / (16 * kSub);
     sc.total_tiles = (long long)units * sc.tiles_per_unit;
     long long n = (long long)sms_cached * occ_now;
     if (n > sc.total_tiles) n = sc.total_tiles;
