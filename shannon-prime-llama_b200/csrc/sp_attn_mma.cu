@@ -49,11 +49,18 @@
 #include <stdlib.h>
 #include <string.h>
 
+#ifndef SP_ATTN_SUB
+#define SP_ATTN_SUB 2
+#endif
+#ifndef SP_ATTN_STAGES
+#define SP_ATTN_STAGES 3
+#endif
+
 namespace {
 
 constexpr int kKTile = 16 * 76;       // 1216: one 16-position MMA tile of K rows
 constexpr int kVTile = 16 * 50;       // 800
-constexpr int kSub = 2;               // MMA tiles per ring stage (32 positions per bulk-copied stage)
+constexpr int kSub = SP_ATTN_SUB;     // MMA tiles per ring stage (16 kSub positions per bulk-copied stage)
 constexpr int kKStage = kSub * kKTile;             // 2432
 constexpr int kStageBytes = kSub * (kKTile + kVTile);   // 4032
 constexpr int kN = 128;
@@ -457,20 +464,24 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
         // scores of tile k+1 only after tile k's weights are formed.
         //
         // Band scales of ring stage st to fp32 (scl[st]): lane t converts
-        // the four K bands and the V scale of the stage's position t.
+        // the four K bands and the V scale of the stage's positions t,
+        // t + 32, ...
         auto stage_scales = [&](int st) {
             const unsigned char *kt = sm.ring[warp][st];
-            const int sub = lane >> 4, t = lane & 15;
-            const uint32_t *row = reinterpret_cast<const uint32_t *>(kt + sub * kKTile) + 19 * t;
-            const uint32_t w0 = row[kKScaleWord(0)], w1 = row[kKScaleWord(1)];
-            const uint32_t w2 = row[kKScaleWord(2)], w3 = row[kKScaleWord(3)];
-            const uint32_t h01 = __byte_perm(w0, w1, 0x7610), h23 = __byte_perm(w2, w3, 0x7610);
-            const float2 f01 = __half22float2(finite_or_zero(*reinterpret_cast<const __half2 *>(&h01)));
-            const float2 f23 = __half22float2(finite_or_zero(*reinterpret_cast<const __half2 *>(&h23)));
-            *reinterpret_cast<float4 *>(&sm.scl[warp][st][lane][0]) = make_float4(f01.x, f01.y, f23.x, f23.y);
-            const unsigned short vb =
-                *reinterpret_cast<const unsigned short *>(kt + kKStage + sub * kVTile + 50 * t);
-            sm.scl[warp][st][lane][4] = __low2float(finite_or_zero(__half2half2(__ushort_as_half(vb))));
+#pragma unroll
+            for (int p = lane; p < 16 * kSub; p += 32) {
+                const int sub = p >> 4, t = p & 15;
+                const uint32_t *row = reinterpret_cast<const uint32_t *>(kt + sub * kKTile) + 19 * t;
+                const uint32_t w0 = row[kKScaleWord(0)], w1 = row[kKScaleWord(1)];
+                const uint32_t w2 = row[kKScaleWord(2)], w3 = row[kKScaleWord(3)];
+                const uint32_t h01 = __byte_perm(w0, w1, 0x7610), h23 = __byte_perm(w2, w3, 0x7610);
+                const float2 f01 = __half22float2(finite_or_zero(*reinterpret_cast<const __half2 *>(&h01)));
+                const float2 f23 = __half22float2(finite_or_zero(*reinterpret_cast<const __half2 *>(&h23)));
+                *reinterpret_cast<float4 *>(&sm.scl[warp][st][p][0]) = make_float4(f01.x, f01.y, f23.x, f23.y);
+                const unsigned short vb =
+                    *reinterpret_cast<const unsigned short *>(kt + kKStage + sub * kVTile + 50 * t);
+                sm.scl[warp][st][p][4] = __low2float(finite_or_zero(__half2half2(__ushort_as_half(vb))));
+            }
         };
         // K side of MMA tile `sub` of ring stage st (positions
         // tok0..tok0+15): code unpack, band MMAs, and the scores of
@@ -795,7 +806,7 @@ int sp_attn_mma_supported(const SpAttnArgs &a)
 // deeper rings gain nothing (a ring of 4 already sustains the copy stream
 // at the HBM rate when the compute is removed).
 // Up to 8 query heads per KV head (two column tiles, more registers): 2 CTAs/SM.
-constexpr int kCtaWarps = 4, kRingStages = 3, kCtasPerSm = 3, kCtasPerSm8 = 2;
+constexpr int kCtaWarps = 4, kRingStages = SP_ATTN_STAGES, kCtasPerSm = 3, kCtasPerSm8 = 2;
 
 int sp_attn_mma_launch(const SpAttnArgs &a_in, cudaStream_t s, cudaEvent_t ev_begin, cudaEvent_t ev_end)
 {
