@@ -245,10 +245,13 @@ __global__ void __launch_bounds__(kWarps * 32, kMinBlocks)
 k_attn_ship_mma(SpAttnArgs a, Sched sc)
 {
     static_assert(GT == 4 || GT == 8, "4 or 8 query heads per KV head");
-    // Launched as a programmatic dependent of the stream's previous kernel:
-    // nothing global is touched before that kernel has completed.  Then the
-    // combine may launch and wait on this grid.
-    sp_pdl_wait();
+    // Launched as a programmatic dependent of the stream's previous kernel.
+    // The only kernel of this library that lets its dependents start early
+    // is the previous decode call's combine, which writes no cache byte; so
+    // the ring's first copies of the (unchanged) compressed cache and the
+    // Möbius order are fetched before the wait, and the queries, the
+    // partials and everything else only after it.  The combine of this call
+    // may then launch and wait on this grid.
     sp_pdl_trigger();
     constexpr int NT = GT / 4;
     extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -317,6 +320,10 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
     };
     if (lane == 0)
         for (int k = 0; k < kStages && k < n_my; k++) issue(k);
+    int ord[4];                         // Möbius order entries of this lane's four coefficients
+#pragma unroll
+    for (int e = 0; e < 4; e++) ord[e] = a.order ? __ldg(a.order + lane * 4 + e) : lane * 4 + e;
+    sp_pdl_wait();
 
     // ---- lane constants ---------------------------------------------------
     // K: window word and shift of lane c's chunk in each band.
@@ -360,7 +367,7 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
                     const int i = lane * 4 + e;
-                    const float v = sm.qt[g][a.order ? a.order[i] : i];
+                    const float v = sm.qt[g][ord[e]];
                     sm.q[g][i] = v;
                     mx = fmaxf(mx, fabsf(v));
                     bs += v;
