@@ -120,6 +120,18 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// The same with the accumulator input taken from separate registers (the
+// first MMA of a band starts from its constant offset without copies).
+__device__ __forceinline__ void mma16816_c(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1, float c0, float c1, float c2, float c3)
+{
+    asm(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%10,%11,%12,%13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(c2), "f"(c3));
+}
+
 // 2^x on the XU pipe (one MUFU op; rel. error ~2^-22, flushes subnormal
 // results, which are far below the softmax's resolution).
 __device__ __forceinline__ float fast_exp2(float x)
@@ -504,7 +516,7 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
 #pragma unroll
             for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-                for (int b = 0; b < 4; b++) {
+                for (int b = NBK; b < 4; b++) {
                     acc[nt][b][0] = cinit[nt][b]; acc[nt][b][1] = 0.0f; acc[nt][b][2] = cinit[nt][b]; acc[nt][b][3] = 0.0f;
                 }
 #pragma unroll
@@ -546,7 +558,11 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
                                    a3 = code(1, 2 * j + 1);
 #pragma unroll
                     for (int nt = 0; nt < NT; nt++)
-                        mma16816(acc[nt][b], a0, a1, a2, a3, bq[nt][2 * b + j][0], bq[nt][2 * b + j][1]);
+                        if (j == 0)
+                            mma16816_c(acc[nt][b], a0, a1, a2, a3, bq[nt][2 * b][0], bq[nt][2 * b][1], cinit[nt][b],
+                                       0.0f, cinit[nt][b], 0.0f);
+                        else
+                            mma16816(acc[nt][b], a0, a1, a2, a3, bq[nt][2 * b + j][0], bq[nt][2 * b + j][1]);
                 }
             }
             __syncwarp();
