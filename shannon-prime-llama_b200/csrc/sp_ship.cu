@@ -20,6 +20,8 @@
 // contraction), __float2half_rn for the scale, round-half-even for codes.
 #include "sp_internal.cuh"
 
+#include <atomic>
+
 #include <stdarg.h>
 #include <stdio.h>
 #include <string.h>
@@ -518,17 +520,21 @@ bool fast_bands(const SpBandLayout &bl, int E, FastBand &fb)
 template <int LPV, int E, typename Tin>
 int launch_encode_fast(const FastArgs &fa, bool wht, cudaStream_t s)
 {
-    static int blocks_per_sm[2] = {0, 0}, sms = 0;
+    // occupancy and SM count looked up once per kernel (atomics: host
+    // threads race harmlessly; every device here is the same B200 part)
+    static std::atomic<int> blocks_per_sm[2], sms_cached{0};
     auto k = wht ? k_encode_fast<LPV, E, Tin, true> : k_encode_fast<LPV, E, Tin, false>;
-    int &bps = blocks_per_sm[wht ? 1 : 0];
+    int bps = blocks_per_sm[wht ? 1 : 0].load(std::memory_order_acquire);
     if (!bps) {
-        int dev = 0;
+        int dev = 0, sm = 0, o = 0;
         cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, k, kFastWarps * 32, 0);
-        if (bps < 1) bps = 1;
-        if (sms < 1) sms = 148;
+        cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, dev);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k, kFastWarps * 32, 0);
+        sms_cached.store(sm > 0 ? sm : 148, std::memory_order_relaxed);
+        bps = o > 0 ? o : 1;
+        blocks_per_sm[wht ? 1 : 0].store(bps, std::memory_order_release);
     }
+    const int sms = sms_cached.load(std::memory_order_relaxed);
     const long long per_cta = (long long)kFastWarps * (32 / LPV);
     const long long n_vec = (long long)fa.e.n_tokens * fa.e.nh;
     long long blocks = (n_vec + per_cta - 1) / per_cta;

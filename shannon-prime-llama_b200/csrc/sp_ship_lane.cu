@@ -363,18 +363,25 @@ int launch_lane(const LaneArgs &a, const LaneMaps &maps, cudaStream_t s)
 {
     auto k = k_encode_lane<Tin>;
     const size_t smem = sizeof(LaneSmem<Tin>);
-    static int occ = 0, sms = 0, dev_done = -1;
+    // per device: attribute set and occupancy looked up once (atomics, so
+    // host threads driving any devices race harmlessly)
+    constexpr int kMaxDev = 64;
+    static std::atomic<int> occ_tab[kMaxDev], sms_tab[kMaxDev];
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev != dev_done) {
+    if (dev < 0 || dev >= kMaxDev) return sp_set_error(SP_ERR_CUDA, "lane encoder: device %d", dev);
+    int occ = occ_tab[dev].load(std::memory_order_acquire);
+    if (occ == 0) {
         if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return sp_check_cuda(cudaGetLastError(), "lane encoder smem attribute");
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, kLaneWarps * 32, smem);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (occ < 1) occ = 1;
-        if (sms < 1) sms = 148;
-        dev_done = dev;
+        int o = 0, sm = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k, kLaneWarps * 32, smem);
+        cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, dev);
+        sms_tab[dev].store(sm > 0 ? sm : 148, std::memory_order_relaxed);
+        occ = o > 0 ? o : 1;
+        occ_tab[dev].store(occ, std::memory_order_release);
     }
+    const int sms = sms_tab[dev].load(std::memory_order_relaxed);
     long long blocks = ((long long)a.nb * a.n_halves + kLaneWarps - 1) / kLaneWarps;
     if (blocks > (long long)sms * occ) blocks = (long long)sms * occ;
     k<<<(unsigned)blocks, kLaneWarps * 32, smem, s>>>(a, maps);
@@ -405,16 +412,15 @@ int lane_half_of(const SpBandLayout &bl, const int *d_order, bool std_order)
 // libcuda link); null if the driver does not provide it.
 PFN_cuTensorMapEncodeTiled_v12000 lane_encode_fn()
 {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
+    // looked up once, thread-safely (function-local static)
+    static const PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
         void *p = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    }
+            return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        return nullptr;
+    }();
     return fn;
 }
 

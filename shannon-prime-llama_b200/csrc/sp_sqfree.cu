@@ -3044,16 +3044,15 @@ int sq_plan_pd(const SpSqDev &t)
 // cuTensorMapEncodeTiled through the runtime's driver entry point.
 PFN_cuTensorMapEncodeTiled_v12000 sq_encode_fn()
 {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
+    // looked up once, thread-safely (function-local static)
+    static const PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
         void *p = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    }
+            return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        return nullptr;
+    }();
     return fn;
 }
 
@@ -3140,23 +3139,30 @@ int sq_lane_launch(const SpSqDev *t[2], const SqIo *io[2], int dtype, unsigned i
     a.status = status;
     auto k = k_sq_encode_lane<Tin, kSlSK>;
     const size_t smem = sizeof(SlSmem<Tin>);
-    static int occ[3] = {0, 0, 0}, sms = 0, dev_done[3] = {-1, -1, -1};
+    // per device and input type: attribute set and occupancy looked up once
+    // (atomics, so host threads driving any devices race harmlessly)
+    constexpr int kMaxDev = 64;
+    static std::atomic<int> occ_tab[kMaxDev][3], sms_tab[kMaxDev];
     const int ti = sizeof(Tin) == 4 ? 0 : (std::is_same<Tin, __half>::value ? 1 : 2);
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev != dev_done[ti]) {
+    if (dev < 0 || dev >= kMaxDev) return 0;
+    int occ = occ_tab[dev][ti].load(std::memory_order_acquire);
+    if (occ == 0) {
         if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
             *rc = sp_check_cuda(cudaGetLastError(), "sqfree lane encoder smem attribute");
             return 1;
         }
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ[ti], k, kSlWarps * 32, smem);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (occ[ti] < 1) occ[ti] = 1;
-        if (sms < 1) sms = 148;
-        dev_done[ti] = dev;
+        int o = 0, sm = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k, kSlWarps * 32, smem);
+        cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, dev);
+        sms_tab[dev].store(sm > 0 ? sm : 148, std::memory_order_relaxed);
+        occ = o > 0 ? o : 1;
+        occ_tab[dev][ti].store(occ, std::memory_order_release);
     }
+    const int sms = sms_tab[dev].load(std::memory_order_relaxed);
     long long blocks = (nb * a.n_halves + kSlWarps - 1) / kSlWarps;
-    if (blocks > (long long)sms * occ[ti]) blocks = (long long)sms * occ[ti];
+    if (blocks > (long long)sms * occ) blocks = (long long)sms * occ;
     k<<<(unsigned)blocks, kSlWarps * 32, smem, s>>>(a, map);
     *rc = sp_check_cuda(cudaGetLastError(), "sqfree lane encoder launch");
     return 1;
@@ -3565,10 +3571,10 @@ struct SqHost {
 // device; called from the cache constructors, outside any stream capture).
 int sq_upload_constants()
 {
-    static bool done[64] = {};
+    static std::atomic<bool> done[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && done[dev]) return SP_OK;
+    if (dev >= 0 && dev < 64 && done[dev].load(std::memory_order_acquire)) return SP_OK;
     float cas[208], isp[5];
     int off = 0, i = 0;
     for (int p : {2, 3, 5, 7, 11}) {
