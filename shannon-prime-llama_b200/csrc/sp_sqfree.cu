@@ -3285,7 +3285,7 @@ k_hier_encode_lane(HlArgs a)
 #pragma unroll
         for (int l = 0; l < 32; l++) part[l] = 0.0f;
         constexpr int EPV = 16 / (int)sizeof(Tin);          // elements per 16-byte load
-#pragma unroll 1
+#pragma unroll 2
         for (int k = 0; k < kHlHD / 32; k++) {
             float x[32];
 #pragma unroll
