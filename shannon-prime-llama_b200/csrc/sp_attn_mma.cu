@@ -476,11 +476,12 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
         };
 
         // ---- my tiles of this segment ------------------------------------
-        // Two-stage software pipeline: iteration k computes the K-side
-        // scores of tile k+1 and the softmax weights + V product of tile k
-        // in one straight-line block, so the two dependency chains
-        // interleave in the schedule.  The running max is updated with the
-        // scores of tile k+1 only after tile k's weights are formed.
+        // One ring stage per iteration: the scores of its two 16-position
+        // tiles, one running-max update, then the weights and V products of
+        // both tiles.  The two tiles are independent chains, which is the
+        // overlap the schedule needs (a cross-stage software pipeline that
+        // took the next stage's scores beside this stage's V products held
+        // more registers and ran 4% slower).
         //
         // Band scales of ring stage st to fp32 (scl[st]): lane t converts
         // the four K bands and the V scale of the stage's positions t,
@@ -685,46 +686,25 @@ k_attn_ship_mma(SpAttnArgs a, Sched sc)
         };
 
         int ctile = (int)(my_first + (long long)k_next * kWarps - u * n_t);
-        if (k_next < n_my && ctile < n_t) {
-            float su[kSub][NT][2];
+        while (k_next < n_my && ctile < n_t) {
             if (!wait_stage(bar0 + 8 * (k_next % kStages), (k_next / kStages) & 1, a.status)) {
                 failed = true;
-            } else {
-                stage_scales(k_next % kStages);
-                __syncwarp();
-#pragma unroll
-                for (int sb = 0; sb < kSub; sb++) k_scores(k_next % kStages, sb, ctile * 16 * kSub + 16 * sb, su[sb]);
-                update_max(su);
+                break;
             }
-            while (!failed) {
-                const int kn = k_next + 1, ctn = ctile + kWarps;
-                const bool has_next = kn < n_my && ctn < n_t;
-                if (has_next && !wait_stage(bar0 + 8 * (kn % kStages), (kn / kStages) & 1, a.status)) {
-                    failed = true;
-                    break;
-                }
-                // Without a next tile of this segment, the scores below are
-                // taken on whatever the next stage holds and discarded.
-                float sn[kSub][NT][2];
-                stage_scales(kn % kStages);
-                __syncwarp();
+            float su[kSub][NT][2];
+            stage_scales(k_next % kStages);
+            __syncwarp();
 #pragma unroll
-                for (int sb = 0; sb < kSub; sb++) k_scores(kn % kStages, sb, ctn * 16 * kSub + 16 * sb, sn[sb]);
+            for (int sb = 0; sb < kSub; sb++) k_scores(k_next % kStages, sb, ctile * 16 * kSub + 16 * sb, su[sb]);
+            update_max(su);
 #pragma unroll
-                for (int sb = 0; sb < kSub; sb++) v_step(k_next % kStages, sb, su[sb]);
-                n_since_flush += kSub;
-                if (n_since_flush >= kFlushTiles) recenter();
-                if (has_next) update_max(sn);
-                __syncwarp();
-                if (lane == 0 && k_next + kStages < n_my) issue(k_next + kStages);
-                k_next = kn;
-                ctile = ctn;
-                if (!has_next) break;
-#pragma unroll
-                for (int sb = 0; sb < kSub; sb++)
-#pragma unroll
-                    for (int nt = 0; nt < NT; nt++) { su[sb][nt][0] = sn[sb][nt][0]; su[sb][nt][1] = sn[sb][nt][1]; }
-            }
+            for (int sb = 0; sb < kSub; sb++) v_step(k_next % kStages, sb, su[sb]);
+            n_since_flush += kSub;
+            if (n_since_flush >= kFlushTiles) recenter();
+            __syncwarp();
+            if (lane == 0 && k_next + kStages < n_my) issue(k_next + kStages);
+            k_next++;
+            ctile += kWarps;
         }
 
         // ---- warp partial -> shared memory ---------------------------------
