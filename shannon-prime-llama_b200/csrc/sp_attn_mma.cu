@@ -49,20 +49,15 @@
 #include <stdlib.h>
 #include <string.h>
 
-#ifndef SP_ATTN_SUB
-#define SP_ATTN_SUB 2
-#endif
-#ifndef SP_ATTN_STAGES
-#define SP_ATTN_STAGES 3
-#endif
 
 namespace {
 
 constexpr int kKTile = 16 * 76;       // 1216: one 16-position MMA tile of K rows
 constexpr int kVTile = 16 * 50;       // 800
-constexpr int kSub = SP_ATTN_SUB;     // MMA tiles per ring stage (16 kSub positions per bulk-copied stage)
-constexpr int kKStage = kSub * kKTile;             // 2432
-constexpr int kStageBytes = kSub * (kKTile + kVTile);   // 4032
+// MMA tiles per ring stage (16 x this many positions per bulk-copied
+// stage): 3 for up to 4 query heads per KV head, 4 for 5..8 (measured best
+// for each; the stage work is paid once per stage).
+__host__ __device__ constexpr int stage_sub(int gt) { return gt == 8 ? 4 : 3; }
 constexpr int kN = 128;
 constexpr float kEmptyMax = -1.0e30f; // running max before the first valid token
 constexpr int kFlushTiles = 16;       // tiles between V-accumulator recentrings
@@ -175,6 +170,8 @@ __device__ __forceinline__ __half2 finite_or_zero(__half2 h)
 
 template <int kWarps, int kStages, int GT>
 struct Smem {
+    static constexpr int kSub = stage_sub(GT);
+    static constexpr int kStageBytes = kSub * (kKTile + kVTile);
     unsigned char ring[kWarps][kStages][kStageBytes];
     unsigned char pad[16];
     unsigned long long bar[kWarps][kStages];
@@ -257,6 +254,9 @@ __global__ void __launch_bounds__(kWarps * 32, kMinBlocks)
 k_attn_ship_mma(SpAttnArgs a, Sched sc)
 {
     static_assert(GT == 4 || GT == 8, "4 or 8 query heads per KV head");
+    constexpr int kSub = stage_sub(GT);
+    constexpr int kKStage = kSub * kKTile;
+    constexpr int kStageBytes = kSub * (kKTile + kVTile);
     // Launched as a programmatic dependent of the stream's previous kernel.
     // The only kernel of this library that lets its dependents start early
     // is the previous decode call's combine, which writes no cache byte; so
@@ -802,14 +802,14 @@ int sp_attn_mma_supported(const SpAttnArgs &a)
     return SP_OK;
 }
 
-// Launch configuration: 4 warps per CTA, a 4-deep ring per warp, and 3
-// CTAs per SM (12 warps, up to 168 registers per thread).  Measured on
-// config 1: 4/4/4 (16 warps, 127 registers) and 8/4/2 run within 1-2% of
-// it; configurations that force fewer registers spill and run slower, and
-// deeper rings gain nothing (a ring of 4 already sustains the copy stream
-// at the HBM rate when the compute is removed).
-// Up to 8 query heads per KV head (two column tiles, more registers): 2 CTAs/SM.
-constexpr int kCtaWarps = 4, kRingStages = SP_ATTN_STAGES, kCtasPerSm = 3, kCtasPerSm8 = 2;
+// Launch configuration: 4 warps per CTA, a ring of 2 stages per warp (48
+// positions per stage, 64 with 5..8 query heads per KV head), and 3 CTAs
+// per SM (12 warps, up to 168 registers per thread); 2 CTAs per SM with
+// 5..8 query heads (two column tiles, more registers).  Measured against
+// 16 x 4, 32 x 3, 32 x 2, 48 x 2 and 64 x 2 position stages for both query
+// group sizes; configurations that force fewer registers spill and run
+// slower.
+constexpr int kCtaWarps = 4, kRingStages = 2, kCtasPerSm = 3, kCtasPerSm8 = 2;
 
 int sp_attn_mma_launch(const SpAttnArgs &a_in, cudaStream_t s, cudaEvent_t ev_begin, cudaEvent_t ev_end)
 {
@@ -852,7 +852,8 @@ int sp_attn_mma_launch(const SpAttnArgs &a_in, cudaStream_t s, cudaEvent_t ev_be
     const int sms_cached = sms_tab[dev].load(std::memory_order_relaxed);
     const int units = a.n_layers * a.n_kv_heads;
     Sched sc;
-    sc.tiles_per_unit = (a.kv_len + 16 * kSub - 1) / (16 * kSub);
+    const int stage_pos = 16 * stage_sub(wide ? 8 : 4);
+    sc.tiles_per_unit = (a.kv_len + stage_pos - 1) / stage_pos;
     sc.total_tiles = (long long)units * sc.tiles_per_unit;
     long long n = (long long)sms_cached * occ_now;
     if (n > sc.total_tiles) n = sc.total_tiles;
