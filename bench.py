@@ -45,10 +45,10 @@ METRIC = ("fused decompress-KQ/V decode latency per token @32K ctx "
 UNIT = "us/token"
 # DRAM bytes (read + write) of one fused-decode launch per cached layer, from
 # an ncu capture of the 8-layer case of this workload
-# (dram__bytes_read.sum + dram__bytes_write.sum = 264.41 MB + 3.78 MB over 8
-# layers, 32-position stages); traffic grows in proportion to the layers
+# (dram__bytes_read.sum + dram__bytes_write.sum = 264.49 MB + 4.23 MB over 8
+# layers, 48-position stages); traffic grows in proportion to the layers
 # processed.
-NCU_TRAFFIC_PER_LAYER = 268.19e6 / 8
+NCU_TRAFFIC_PER_LAYER = 268.72e6 / 8
 
 
 def peaks():
