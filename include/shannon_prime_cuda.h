@@ -407,9 +407,9 @@ int  sp_cuda_hier_read_kv_tokens(const sp_cuda_hier_cache_t *hc, int layer0, int
  *     d_dst_layer[l] * n_q_heads_total + d_dst_qhead[h]   (rows of head_dim fp16)
  * for local layer l and local query head h, and its last block writes `epoch`
  * into uint32 slot `rank` of the flag array at byte flags_offset of every
- * buffer.  A final kernel waits (bounded, 2 s) until all `world` slots of this
- * rank's own flag array reach `epoch`; stream work after the call sees the
- * whole gathered output.
+ * buffer, then waits (bounded, 2 s) until all `world` slots of this rank's
+ * own flag array reach `epoch`; stream work after the call sees the whole
+ * gathered output.
  *   epoch_stride   bytes between two copies of the gathered rows in each
  *                  buffer: the rows of call `epoch` start at byte
  *                  (epoch & 1) * epoch_stride.  With two copies a rank may
