@@ -43,6 +43,9 @@ SEED = 1
 METRIC = ("fused decompress-KQ/V decode latency per token @32K ctx "
           "(Llama-3-8B shape: 32 layers, 32 Q / 8 KV heads, hd 128, ship K 5/5/4/3 + V 3-bit)")
 UNIT = "us/token"
+# The workload both arms (this one and --impl reference) report in config.
+WORKLOAD = ("config 1: fused decode, %d layers x 32 Q / 8 KV heads x hd 128, ctx 32768, batch 1, "
+            "ship K 5/5/4/3 + V 3-bit")
 # DRAM bytes (read + write) of one fused-decode launch per cached layer, from
 # an ncu capture of the 8-layer case of this workload
 # (dram__bytes_read.sum + dram__bytes_write.sum = 264.49 MB + 4.23 MB over 8
@@ -465,8 +468,7 @@ def run_reference(args):
         "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": us_tok / 1e3, "higher_is_better": False, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config-1 distributions)",
-        "config": {"workload": "config 1: 32L x 32Q/8KV x hd128, ctx 32768, batch 1, ship 5/5/4/3 + V3",
-                   "sample": "1 of 32 layers per step, scaled x32"},
+        "config": {"workload": WORKLOAD % N_LAYERS, "sample": "1 of 32 layers per step, scaled x32"},
         "cpu_baseline": {"value": us_tok, "unit": UNIT, "cores": cores, "kind": "port",
                          "min": min(times) * N_LAYERS * 1e6, "passes": len(times),
                          "sample": "one layer (8 KV heads x 32768 positions) per step, median over the "
@@ -779,8 +781,7 @@ def run_ours(args):
         "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
         "dtype": "u8 codes -> f32 accumulate (fp16 q/out)",
         "data": "synthetic (seeded; K = RoPE(N(0,1) x LogNormal(0,0.5) per dim), V = N(0,1), q = N(0,1/sqrt(128)) fp16)",
-        "config": {"workload": "config 1: fused decode, %d layers x 32 Q / 8 KV heads x hd 128, ctx 32768, batch 1, "
-                               "ship K 5/5/4/3 + V 3-bit" % N_LAYERS,
+        "config": {"workload": WORKLOAD % N_LAYERS,
                    "l2": "inputs larger than L2 (compressed cache %.2f GB per GPU)" % (cache_bytes / 1e9),
                    "parallelism": f"kv-head shards x{ws}" if ws > 1 else "single GPU",
                    "collective": collective,
